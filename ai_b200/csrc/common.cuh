@@ -1,0 +1,164 @@
+// Shared device/host helpers for the ai_b200 sm_100a kernels.
+//
+// * status word: kernels never trap; a failed bounded wait or a bad device-side argument records a code in
+//   `g_aib_status` (first writer wins) and the kernel returns. The host reads it with aib_status_read().
+// * PDL: kernels are launched with programmatic stream serialization when enabled; each kernel calls
+//   pdl_wait() before touching data produced or consumed by earlier kernels, and pdl_trigger() early so
+//   the next kernel's CTAs can start streaming their (independent) weights.
+// * mbarrier / TMA wrappers (inline PTX). Every wait is bounded.
+#pragma once
+#include <cstdint>
+#include <utility>
+#include <cuda_runtime.h>
+#include <cuda.h>
+#include "../../include/ai_b200.h"
+
+#define AIB_DEV __device__ __forceinline__
+
+namespace aib {
+
+// ------------------------------------------------------------------------------------------ status
+// The library is one translation unit (lib.cu), so the status word is defined here once.
+__device__ int g_aib_status = 0;
+
+AIB_DEV void set_status(int code) { atomicCAS(&g_aib_status, 0, code); }
+
+// spin limit for bounded waits: each try_wait may suspend for a hardware-defined window, so this bounds
+// a wait to well under a second while being ~1e6x longer than any legitimate wait in these kernels.
+constexpr uint32_t kSpinLimit = 1u << 22;
+
+// ------------------------------------------------------------------------------------------- PDL
+AIB_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+AIB_DEV void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+
+// ---------------------------------------------------------------------------------------- mbarrier
+AIB_DEV uint32_t smem_u32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
+
+AIB_DEV void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+AIB_DEV void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+AIB_DEV void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+AIB_DEV void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+AIB_DEV void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+AIB_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait: returns false (and records `code`) if the phase did not complete in time.
+AIB_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, int code) {
+  for (uint32_t i = 0; i < kSpinLimit; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  set_status(code);
+  return false;
+}
+
+// ------------------------------------------------------------------------------------------- TMA
+// 3-D tiled bulk tensor load (no multicast) into shared memory, completion on an mbarrier.
+AIB_DEV void tma_load_3d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cta.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], "
+      "[%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+AIB_DEV void prefetch_tensormap(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// named barrier among `threads` threads (multiple of 32)
+AIB_DEV void named_sync(int id, int threads) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory"); }
+
+// ------------------------------------------------------------------------------------ arithmetic
+AIB_DEV uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t r;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+  return r;
+}
+// d = a * b + c on two fp32 lanes (sm_100 packed FMA)
+AIB_DEV float2 ffma2(float2 a, float2 b, float2 c) {
+  uint64_t A, B, Cc, D;
+  asm("mov.b64 %0, {%1,%2};" : "=l"(A) : "f"(a.x), "f"(a.y));
+  asm("mov.b64 %0, {%1,%2};" : "=l"(B) : "f"(b.x), "f"(b.y));
+  asm("mov.b64 %0, {%1,%2};" : "=l"(Cc) : "f"(c.x), "f"(c.y));
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(D) : "l"(A), "l"(B), "l"(Cc));
+  float2 d;
+  asm("mov.b64 {%0,%1}, %2;" : "=f"(d.x), "=f"(d.y) : "l"(D));
+  return d;
+}
+AIB_DEV float bf16_to_f32(uint16_t b) { return __uint_as_float(static_cast<uint32_t>(b) << 16); }
+// round-to-nearest-even fp32 -> bf16 bits (NaN -> canonical 0x7FC0)
+AIB_DEV uint16_t f32_to_bf16_rne(float f) {
+  uint32_t u = __float_as_uint(f);
+  if ((u & 0x7F800000u) == 0x7F800000u && (u & 0x007FFFFFu)) return 0x7FC0;
+  u += 0x7FFFu + ((u >> 16) & 1u);
+  return static_cast<uint16_t>(u >> 16);
+}
+
+AIB_DEV float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+}  // namespace aib
+
+// --------------------------------------------------------------------------------------- host side
+namespace aib {
+int fail(int code, const char* fmt, ...);  // records the thread-local message, returns code
+bool pdl_enabled();
+int sm_count(int device = -1);
+int launch_check(const char* what);  // maps cudaGetLastError to AIB_ECUDA
+// Encodes a 3-D tiled tensor map (uint8 elements, no swizzle, no interleave).
+int make_map_3d_u8(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t s1_bytes,
+                   uint64_t s2_bytes, uint32_t b0, uint32_t b1, uint32_t b2);
+
+// Raise a kernel's dynamic shared-memory limit to the sm_100 maximum, once per (kernel, device).
+bool smem_raised(const void* kernel, int device);  // records the pair; true if it was already recorded
+template <typename K>
+int allow_smem(K kernel, size_t bytes) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (bytes > 227 * 1024) return fail(AIB_ENOTSUP, "kernel needs %zu bytes of shared memory", bytes);
+  if (smem_raised(reinterpret_cast<const void*>(kernel), dev)) return AIB_OK;
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+  if (e != cudaSuccess) return fail(AIB_ECUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+  return AIB_OK;
+}
+
+// Launch with the PDL attribute (when enabled) on `stream`.
+template <typename... KArgs, typename... Args>
+int launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, const char* what,
+           Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  int na = 0;
+  if (pdl_enabled()) {
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    na = 1;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+  if (e != cudaSuccess) return fail(AIB_ECUDA, "%s: launch failed: %s", what, cudaGetErrorString(e));
+  return AIB_OK;
+}
+}  // namespace aib

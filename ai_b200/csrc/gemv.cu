@@ -1,0 +1,556 @@
+// Codec GEMV: y (+)= W x with W in the 12-bit codec, decoded on the fly (sm_100a).
+//
+// Replaces the reference's gemvc1_k (T = 1, `ramvi/engine/ramvi_engine/kernels/wcomp.py:67-112`) and
+// gemvc_tc_k (1 < T <= 16, wcomp.py:155-219). Same modes: 0: y = Wx; 1: y += Wx; 2: input silu(x[:K]) *
+// x[K:2K], y += Wx; optional RMSNorm prologue for T = 1.
+//
+// Design (HBM-bound: 1.5 bytes/weight + exceptions):
+//  * Weight stream: a dedicated producer warp issues 3-D TMA tile loads of the m8 and e4 planes (viewed as
+//    [N][K/256][256] and [N][K/256][128]) into a ring of shared-memory stages, one mbarrier pair per stage.
+//    A stage is RT rows x CW 256-column chunks (RT*CW = 32): 8 KB of m8 + 4 KB of e4. The producer never
+//    waits on the previous kernel (PDL), so the ring fills with this kernel's weights while the previous
+//    kernel drains.
+//  * 256 consumer threads: thread t owns unit j = t%8 (columns 16j..16j+15 and 128+16j..128+16j+15 of a
+//    chunk: one 16-byte e4 vector carries both nibble halves), chunk slot cc and row slot r. Each unit is
+//    decoded with byte permutes into packed bf16 pairs (bf16 = sign<<15 | (code+base)<<7 | mantissa), split
+//    into fp32 and accumulated with packed fp32 FMA (fma.rn.f32x2): exact bf16 weights times fp32 x, fp32
+//    accumulation, like the reference.
+//  * x (after the RMS / SiLU prologue) lives in shared memory in a permuted order so every 16-byte read of a
+//    warp is bank-conflict free; for T > 1 the x columns of each stage are staged per stage.
+//  * Exceptions: a unit that contains a code-15 element (found from the CSR, never by scanning the data) is
+//    decoded by a slow path that zeroes those elements and adds their fp32 values times x in place.
+//  * Per row tile the partial sums are reduced in a fixed order (shuffles, then chunk slots), so the result
+//    is deterministic run to run.
+//  * Every wait is bounded. On a timeout each consumer keeps walking the same sequence of named barriers
+//    (skipping its work), so no thread is ever left at a barrier the others do not reach.
+#include <algorithm>
+#include <climits>
+#include "common.cuh"
+
+namespace aib {
+namespace gemv {
+
+constexpr int kConsumers = 256;            // 8 consumer warps
+constexpr int kThreads = kConsumers + 32;  // + 1 producer warp
+constexpr int kStageM8 = 32 * 256;         // bytes of m8 per stage (RT*CW*256)
+constexpr int kStageE4 = 32 * 128;
+constexpr int kStageBytes = kStageM8 + kStageE4;
+constexpr int kHeader = 1024;  // barriers, flags, reduction buffers
+
+struct Params {
+  const int32_t* rp;
+  const int32_t* ec;
+  const float* ev;
+  const float* x;
+  float* y;
+  const uint16_t* lnw;
+  float eps;
+  int base, N, K, nch;
+  int RT, CW, KS, tiles;
+  int NS;
+  int T, x_stride, y_stride;
+  int xs_floats;
+};
+
+// permuted index of column k in the shared x buffer (see file comment)
+AIB_DEV int xperm(int k) {
+  const int c = k >> 8, hf = (k >> 7) & 1, jj = (k >> 4) & 7, q = (k >> 2) & 3, e = k & 3;
+  return ((c * 2 + hf) * 4 + q) * 32 + jj * 4 + e;
+}
+
+AIB_DEV float silu_mul(float g, float u) { return g / (1.0f + expf(-g)) * u; }
+
+// Decode one 32-element unit (fast path: no code-15 element) and accumulate w * x.
+AIB_DEV void unit_fast(const uint4& ml, const uint4& mh, const uint4& ee, const float4* xl, const float4* xh,
+                       uint32_t base7, float2& acc) {
+  const uint32_t E[4] = {ee.x, ee.y, ee.z, ee.w};
+  const uint32_t L[4] = {ml.x, ml.y, ml.z, ml.w};
+  const uint32_t Hh[4] = {mh.x, mh.y, mh.z, mh.w};
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const uint32_t x01 = prmt(E[q], 0u, 0x4140u);  // [0, b1, 0, b0]
+    const uint32_t x23 = prmt(E[q], 0u, 0x4342u);  // [0, b3, 0, b2]
+    const uint32_t plo01 = ((x01 & 0x000F000Fu) << 7) + base7;
+    const uint32_t phi01 = ((x01 & 0x00F000F0u) << 3) + base7;
+    const uint32_t plo23 = ((x23 & 0x000F000Fu) << 7) + base7;
+    const uint32_t phi23 = ((x23 & 0x00F000F0u) << 3) + base7;
+    // [sign-rep(m1), m1, sign-rep(m0), m0] -> keep bit 15 and bits 0..6 of each half
+    const uint32_t zlo01 = (prmt(L[q], 0u, 0x9180u) & 0x807F807Fu) | plo01;
+    const uint32_t zlo23 = (prmt(L[q], 0u, 0xB3A2u) & 0x807F807Fu) | plo23;
+    const uint32_t zhi01 = (prmt(Hh[q], 0u, 0x9180u) & 0x807F807Fu) | phi01;
+    const uint32_t zhi23 = (prmt(Hh[q], 0u, 0xB3A2u) & 0x807F807Fu) | phi23;
+    acc = ffma2(make_float2(__uint_as_float(zlo01 << 16), __uint_as_float(zlo01 & 0xFFFF0000u)),
+                make_float2(xl[q].x, xl[q].y), acc);
+    acc = ffma2(make_float2(__uint_as_float(zlo23 << 16), __uint_as_float(zlo23 & 0xFFFF0000u)),
+                make_float2(xl[q].z, xl[q].w), acc);
+    acc = ffma2(make_float2(__uint_as_float(zhi01 << 16), __uint_as_float(zhi01 & 0xFFFF0000u)),
+                make_float2(xh[q].x, xh[q].y), acc);
+    acc = ffma2(make_float2(__uint_as_float(zhi23 << 16), __uint_as_float(zhi23 & 0xFFFF0000u)),
+                make_float2(xh[q].z, xh[q].w), acc);
+  }
+}
+
+// Element-wise decode with code 15 -> 0 (slow path for units holding exceptions).
+AIB_DEV float dec1(uint32_t m, uint32_t code, uint32_t base) {
+  if (code == 15u) return 0.0f;
+  return __uint_as_float(((m & 0x80u) << 24) | ((code + base) << 23) | ((m & 0x7Fu) << 16));
+}
+
+// Bounded consumer wait on a full-stage barrier; gives up early once another thread has aborted.
+AIB_DEV bool wait_full(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+  for (uint32_t i = 0; i < kSpinLimit; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+  }
+  set_status(AIB_DEV_TIMEOUT_FULL);
+  *abort_flag = 1;
+  return false;
+}
+
+// Does the 32-element unit (row's CSR slice, chunk starting at column c0) hold an exception?
+// ex_p / ex_col track the first exception of the row at or after the current chunk.
+AIB_DEV bool unit_has_exc(const int32_t* ec, int& ex_p, int ex_e, int& ex_col, int c0, uint32_t j) {
+  while (ex_col < c0) {
+    ++ex_p;
+    ex_col = ex_p < ex_e ? ec[ex_p] : INT_MAX;
+  }
+  for (int q = ex_p; q < ex_e; ++q) {
+    const int col = (q == ex_p) ? ex_col : ec[q];
+    if (col >= c0 + 256) break;
+    const uint32_t o = static_cast<uint32_t>(col - c0);
+    if (((o & 127u) >> 4) == j) return true;
+  }
+  return false;
+}
+
+// ------------------------------------------------------------------------------ shared producer
+// One elected thread streams the CTA's (tile, stage) sequence through the ring.
+AIB_DEV void produce(const CUtensorMap* tm8, const CUtensorMap* tme4, uint8_t* ring, uint64_t* full, uint64_t* empty,
+                     volatile int* abort_flag, int tb, int n_it, int KS, int RT, int CW, int NS) {
+  prefetch_tensormap(tm8);
+  prefetch_tensormap(tme4);
+  int issued = 0;
+  for (int it = 0; it < n_it; ++it) {
+    const int s = it % NS;
+    if (it >= NS) {
+      bool ok = false;
+      for (uint32_t i = 0; i < kSpinLimit && !ok; ++i) {
+        ok = mbar_try_wait(&empty[s], ((it / NS) - 1) & 1);
+        if (!ok && *abort_flag) break;
+      }
+      if (!ok) {
+        if (!*abort_flag) set_status(AIB_DEV_TIMEOUT_EMPTY);
+        *abort_flag = 1;
+        break;
+      }
+    }
+    const int tile = tb + it / KS, ks = it % KS;
+    uint8_t* st = ring + static_cast<size_t>(s) * kStageBytes;
+    mbar_arrive_expect_tx(&full[s], kStageBytes);
+    tma_load_3d(st, tm8, &full[s], 0, ks * CW, tile * RT);
+    tma_load_3d(st + kStageM8, tme4, &full[s], 0, ks * CW, tile * RT);
+    issued = it + 1;
+  }
+  // Never leave with copies in flight: on the abort path wait (bounded) for the stages this thread issued
+  // that the consumers may not have observed. In the normal path all of them were consumed.
+  if (*abort_flag) {
+    for (int it = (issued > NS ? issued - NS : 0); it < issued; ++it)
+      mbar_wait(&full[it % NS], (it / NS) & 1, AIB_DEV_TIMEOUT_FULL);
+  }
+}
+
+AIB_DEV void init_barriers(uint64_t* full, uint64_t* empty, volatile int* abort_flag, int NS) {
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kConsumers / 32);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+}
+
+// ------------------------------------------------------------------------------------ T = 1 kernel
+template <int MODE, bool RMS>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemv_t1_kernel(const __grid_constant__ CUtensorMap tm8, const __grid_constant__ CUtensorMap tme4, Params p) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* empty = full + 16;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + 256);
+  float* red = reinterpret_cast<float*>(smem + 512);  // [2][32] chunk-slot partials + [8] RMS partials
+  float* xs = reinterpret_cast<float*>(smem + kHeader);
+  uint8_t* ring = smem + kHeader + ((p.xs_floats * 4 + 1023) / 1024) * 1024;
+
+  const int tid = threadIdx.x;
+  const int tb = static_cast<int>((static_cast<long long>(blockIdx.x) * p.tiles) / gridDim.x);
+  const int te = static_cast<int>((static_cast<long long>(blockIdx.x + 1) * p.tiles) / gridDim.x);
+  const int n_it = (te - tb) * p.KS;
+
+  init_barriers(full, empty, abort_flag, p.NS);
+  pdl_trigger();
+
+  if (tid >= kConsumers) {  // producer warp
+    if (tid == kConsumers) produce(&tm8, &tme4, ring, full, empty, abort_flag, tb, n_it, p.KS, p.RT, p.CW, p.NS);
+    return;
+  }
+
+  // -------- consumers
+  pdl_wait();  // x / y are produced / consumed by neighbouring kernels
+  const int K = p.K;
+  float rs = 1.0f;
+  if (RMS) {
+    float ss = 0.0f;
+    for (int k = tid; k < K; k += kConsumers) {
+      const float v = p.x[k];
+      ss += v * v;
+    }
+    ss = warp_sum(ss);
+    if ((tid & 31) == 0) red[64 + (tid >> 5)] = ss;
+    named_sync(1, kConsumers);
+    float tot = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kConsumers / 32; ++w) tot += red[64 + w];
+    rs = rsqrtf(tot / static_cast<float>(K) + p.eps);
+  }
+  for (int k = tid; k < K; k += kConsumers) {
+    float v = (MODE == 2) ? silu_mul(p.x[k], p.x[K + k]) : p.x[k];
+    if (RMS) v = bf16_to_f32(p.lnw[k]) * (v * rs);
+    xs[xperm(k)] = v;
+  }
+  named_sync(1, kConsumers);
+
+  const int j = tid & 7, slot = tid >> 3;
+  const int CW = p.CW, cc = slot % CW, r = slot / CW;
+  const uint32_t base7 = (static_cast<uint32_t>(p.base) << 7) | (static_cast<uint32_t>(p.base) << 23);
+  float2 acc = make_float2(0.0f, 0.0f);
+  int row = 0, ex_p = 0, ex_e = 0, ex_col = INT_MAX, buf = 0;
+  bool aborted = false;
+
+  for (int it = 0; it < n_it; ++it) {
+    const int s = it % p.NS;
+    const int tile = tb + it / p.KS, ks = it % p.KS;
+    if (ks == 0) {
+      row = tile * p.RT + r;
+      acc = make_float2(0.0f, 0.0f);
+      ex_p = 0;
+      ex_e = 0;
+      if (row < p.N) {
+        ex_p = p.rp[row];
+        ex_e = p.rp[row + 1];
+      }
+      ex_col = ex_p < ex_e ? p.ec[ex_p] : INT_MAX;
+    }
+    const bool ok = !aborted && wait_full(&full[s], (it / p.NS) & 1, abort_flag);
+    if (!ok) aborted = true;
+    const int gc = ks * CW + cc;
+    if (ok && row < p.N && gc < p.nch) {
+      const uint8_t* st = ring + static_cast<size_t>(s) * kStageBytes;
+      const uint8_t* m8 = st + (r * CW + cc) * 256;
+      const uint8_t* e4 = st + kStageM8 + (r * CW + cc) * 128;
+      const uint4 ml = *reinterpret_cast<const uint4*>(m8 + 16 * j);
+      const uint4 mh = *reinterpret_cast<const uint4*>(m8 + 128 + 16 * j);
+      const uint4 ee = *reinterpret_cast<const uint4*>(e4 + 16 * j);
+      const float4* xb = reinterpret_cast<const float4*>(xs) + gc * 64;  // 256 floats per chunk
+      float4 xl[4], xh[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        xl[q] = xb[q * 8 + j];
+        xh[q] = xb[32 + q * 8 + j];
+      }
+      const int c0 = gc * 256;
+      if (!unit_has_exc(p.ec, ex_p, ex_e, ex_col, c0, j)) {
+        unit_fast(ml, mh, ee, xl, xh, base7, acc);
+      } else {
+        const uint32_t E[4] = {ee.x, ee.y, ee.z, ee.w}, L[4] = {ml.x, ml.y, ml.z, ml.w},
+                       Hh[4] = {mh.x, mh.y, mh.z, mh.w};
+        const float* xlf = reinterpret_cast<const float*>(xl);
+        const float* xhf = reinterpret_cast<const float*>(xh);
+        float sacc = 0.0f;
+        for (int q = 0; q < 4; ++q)
+          for (int b = 0; b < 4; ++b) {
+            const uint32_t eb = (E[q] >> (8 * b)) & 0xFFu;
+            sacc += dec1((L[q] >> (8 * b)) & 0xFFu, eb & 15u, p.base) * xlf[q * 4 + b];
+            sacc += dec1((Hh[q] >> (8 * b)) & 0xFFu, eb >> 4, p.base) * xhf[q * 4 + b];
+          }
+        for (int q = ex_p; q < ex_e; ++q) {
+          const int col = p.ec[q];
+          if (col >= c0 + 256) break;
+          const uint32_t o = static_cast<uint32_t>(col - c0);
+          if (((o & 127u) >> 4) == static_cast<uint32_t>(j)) sacc += p.ev[q] * xs[xperm(col)];
+        }
+        acc.x += sacc;
+      }
+    }
+    __syncwarp();
+    if ((tid & 31) == 0) mbar_arrive(&empty[s]);
+
+    if (ks == p.KS - 1) {  // row tile complete: fixed-order reduction
+      float v = acc.x + acc.y;
+      v += __shfl_xor_sync(0xffffffffu, v, 1);
+      v += __shfl_xor_sync(0xffffffffu, v, 2);
+      v += __shfl_xor_sync(0xffffffffu, v, 4);
+      if (j == 0) red[buf * 32 + slot] = v;
+      named_sync(1, kConsumers);
+      if (tid < p.RT && !aborted) {
+        const int orow = tile * p.RT + tid;
+        if (orow < p.N) {
+          float sum = 0.0f;
+          for (int c = 0; c < CW; ++c) sum += red[buf * 32 + tid * CW + c];
+          if (MODE == 0)
+            p.y[orow] = sum;
+          else
+            p.y[orow] += sum;
+        }
+      }
+      buf ^= 1;
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------- batched kernel
+// T <= TMAX tokens, RT = 32 rows x CW = 1 chunk per stage; the x columns of each stage (T x 256 floats,
+// SiLU-gated for mode 2) are staged in shared memory by the consumers.
+template <int MODE, int TMAX>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemv_tn_kernel(const __grid_constant__ CUtensorMap tm8, const __grid_constant__ CUtensorMap tme4, Params p) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* empty = full + 16;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + 256);
+  float* xs = reinterpret_cast<float*>(smem + kHeader);  // [TMAX][256] (permuted)
+  uint8_t* ring = smem + kHeader + ((TMAX * 256 * 4 + 1023) / 1024) * 1024;
+
+  const int tid = threadIdx.x;
+  const int tb = static_cast<int>((static_cast<long long>(blockIdx.x) * p.tiles) / gridDim.x);
+  const int te = static_cast<int>((static_cast<long long>(blockIdx.x + 1) * p.tiles) / gridDim.x);
+  const int n_it = (te - tb) * p.KS;
+  init_barriers(full, empty, abort_flag, p.NS);
+  pdl_trigger();
+  if (tid >= kConsumers) {
+    if (tid == kConsumers) produce(&tm8, &tme4, ring, full, empty, abort_flag, tb, n_it, p.KS, 32, 1, p.NS);
+    return;
+  }
+  pdl_wait();
+  const int K = p.K, T = p.T;
+  const int j = tid & 7, r = tid >> 3;
+  const uint32_t base7 = (static_cast<uint32_t>(p.base) << 7) | (static_cast<uint32_t>(p.base) << 23);
+  float2 acc[TMAX];
+  int row = 0, ex_p = 0, ex_e = 0, ex_col = INT_MAX;
+  bool aborted = false;
+  for (int it = 0; it < n_it; ++it) {
+    const int s = it % p.NS;
+    const int tile = tb + it / p.KS, ks = it % p.KS;
+    if (ks == 0) {
+      row = tile * 32 + r;
+#pragma unroll
+      for (int t = 0; t < TMAX; ++t) acc[t] = make_float2(0.0f, 0.0f);
+      ex_p = 0;
+      ex_e = 0;
+      if (row < p.N) {
+        ex_p = p.rp[row];
+        ex_e = p.rp[row + 1];
+      }
+      ex_col = ex_p < ex_e ? p.ec[ex_p] : INT_MAX;
+    }
+    // stage the x columns of chunk ks for all tokens
+    named_sync(1, kConsumers);  // previous chunk fully consumed
+    for (int i = tid; i < T * 256; i += kConsumers) {
+      const int t = i >> 8, k = ks * 256 + (i & 255);
+      const float* xr = p.x + static_cast<size_t>(t) * p.x_stride;
+      xs[t * 256 + xperm(i & 255)] = (MODE == 2) ? silu_mul(xr[k], xr[K + k]) : xr[k];
+    }
+    named_sync(1, kConsumers);
+    const bool ok = !aborted && wait_full(&full[s], (it / p.NS) & 1, abort_flag);
+    if (!ok) aborted = true;  // keep walking the barrier sequence, skip the work
+    if (ok && row < p.N) {
+      const uint8_t* st = ring + static_cast<size_t>(s) * kStageBytes;
+      const uint4 ml = *reinterpret_cast<const uint4*>(st + r * 256 + 16 * j);
+      const uint4 mh = *reinterpret_cast<const uint4*>(st + r * 256 + 128 + 16 * j);
+      const uint4 ee = *reinterpret_cast<const uint4*>(st + kStageM8 + r * 128 + 16 * j);
+      const int c0 = ks * 256;
+      if (!unit_has_exc(p.ec, ex_p, ex_e, ex_col, c0, j)) {
+#pragma unroll
+        for (int t = 0; t < TMAX; ++t) {
+          if (t < T) {
+            const float4* xb = reinterpret_cast<const float4*>(xs + t * 256);
+            float4 xl[4], xh[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              xl[q] = xb[q * 8 + j];
+              xh[q] = xb[32 + q * 8 + j];
+            }
+            unit_fast(ml, mh, ee, xl, xh, base7, acc[t]);
+          }
+        }
+      } else {
+        const uint32_t E[4] = {ee.x, ee.y, ee.z, ee.w}, L[4] = {ml.x, ml.y, ml.z, ml.w},
+                       Hh[4] = {mh.x, mh.y, mh.z, mh.w};
+        for (int t = 0; t < T; ++t) {
+          const float* xt = xs + t * 256;
+          float sacc = 0.0f;
+          for (int q = 0; q < 4; ++q)
+            for (int b = 0; b < 4; ++b) {
+              const uint32_t eb = (E[q] >> (8 * b)) & 0xFFu;
+              const int kl = 16 * j + 4 * q + b, kh = 128 + kl;
+              sacc += dec1((L[q] >> (8 * b)) & 0xFFu, eb & 15u, p.base) * xt[xperm(kl)];
+              sacc += dec1((Hh[q] >> (8 * b)) & 0xFFu, eb >> 4, p.base) * xt[xperm(kh)];
+            }
+          for (int q = ex_p; q < ex_e; ++q) {
+            const int col = p.ec[q];
+            if (col >= c0 + 256) break;
+            const uint32_t o = static_cast<uint32_t>(col - c0);
+            if (((o & 127u) >> 4) == static_cast<uint32_t>(j)) sacc += p.ev[q] * xt[xperm(col - c0)];
+          }
+#pragma unroll
+          for (int tt = 0; tt < TMAX; ++tt)
+            if (tt == t) acc[tt].x += sacc;
+        }
+      }
+    }
+    __syncwarp();
+    if ((tid & 31) == 0) mbar_arrive(&empty[s]);
+    if (ks == p.KS - 1) {
+#pragma unroll
+      for (int t = 0; t < TMAX; ++t) {
+        float v = acc[t].x + acc[t].y;
+        v += __shfl_xor_sync(0xffffffffu, v, 1);
+        v += __shfl_xor_sync(0xffffffffu, v, 2);
+        v += __shfl_xor_sync(0xffffffffu, v, 4);
+        if (j == 0 && t < T && row < p.N && !aborted) {
+          float* yr = p.y + static_cast<size_t>(t) * p.y_stride + row;
+          if (MODE == 0)
+            *yr = v;
+          else
+            *yr += v;
+        }
+      }
+    }
+  }
+}
+
+// ----------------------------------------------------------------------------------- host side
+struct Geometry {
+  int RT, CW, KS, tiles, grid;
+};
+
+// Row-tile shape that minimises the busiest CTA's work (rows x padded chunks).
+static Geometry pick_geometry(int N, int nch, int sms) {
+  Geometry best = {32, 1, nch, (N + 31) / 32, std::min((N + 31) / 32, sms)};
+  long long best_cost = LLONG_MAX;
+  for (int RT : {32, 16, 8, 4}) {
+    const int CW = 32 / RT;
+    if (CW > nch && RT != 32) continue;
+    const int tiles = (N + RT - 1) / RT;
+    const int grid = std::min(tiles, sms);
+    const int KS = (nch + CW - 1) / CW;
+    const long long cost = static_cast<long long>((tiles + grid - 1) / grid) * RT * KS * CW;
+    if (cost < best_cost) best_cost = cost, best = {RT, CW, KS, tiles, grid};
+  }
+  return best;
+}
+
+static int make_maps(const aib_c12* c, int RT, int CW, CUtensorMap* tm8, CUtensorMap* tme4) {
+  const uint64_t N = c->N, nch = c->K / 256;
+  int rc = make_map_3d_u8(tm8, c->m8, 256, nch, N, 256, static_cast<uint64_t>(c->K), 256, CW, RT);
+  if (rc) return rc;
+  return make_map_3d_u8(tme4, c->e4, 128, nch, N, 128, static_cast<uint64_t>(c->K) / 2, 128, CW, RT);
+}
+
+constexpr size_t kSmemTarget = 112 * 1024;  // leaves room for a neighbouring kernel's CTA (PDL overlap)
+constexpr size_t kSmemMax = 227 * 1024;
+
+static int run_t1(const aib_c12* c, const float* x, float* y, int mode, const uint16_t* lnw, float eps,
+                  cudaStream_t s) {
+  const int nch = c->K / 256;
+  const Geometry g = pick_geometry(c->N, nch, sm_count());
+  CUtensorMap tm8, tme4;
+  int rc = make_maps(c, g.RT, g.CW, &tm8, &tme4);
+  if (rc) return rc;
+  const size_t xs_bytes = ((static_cast<size_t>(c->K) * 4 + 1023) / 1024) * 1024;
+  const size_t budget = std::max(kSmemTarget, kHeader + xs_bytes + 2 * kStageBytes);
+  if (budget > kSmemMax) return fail(AIB_ENOTSUP, "aib_gemv_c12: K=%d too large for the shared x buffer", c->K);
+  int NS = static_cast<int>((budget - kHeader - xs_bytes) / kStageBytes);
+  NS = std::max(2, std::min(NS, 8));
+  const size_t smem = kHeader + xs_bytes + static_cast<size_t>(NS) * kStageBytes;
+  Params p{c->rp, c->ec, c->ev, x, y, lnw, eps, c->base, c->N, c->K, nch, g.RT, g.CW, g.KS, g.tiles, NS, 1, 0, 0,
+           c->K};
+  auto go = [&](auto kernel) -> int {
+    const int r2 = allow_smem(kernel, smem);
+    if (r2) return r2;
+    return launch(kernel, dim3(g.grid), dim3(kThreads), smem, s, "aib_gemv_c12(T=1)", tm8, tme4, p);
+  };
+  if (lnw) {
+    if (mode == 0) return go(gemv_t1_kernel<0, true>);
+    if (mode == 1) return go(gemv_t1_kernel<1, true>);
+    return go(gemv_t1_kernel<2, true>);
+  }
+  if (mode == 0) return go(gemv_t1_kernel<0, false>);
+  if (mode == 1) return go(gemv_t1_kernel<1, false>);
+  return go(gemv_t1_kernel<2, false>);
+}
+
+template <int MODE, int TMAX>
+static int run_tn_t(const aib_c12* c, const float* x, float* y, int T, int xs_, int ys_, cudaStream_t s) {
+  const int nch = c->K / 256;
+  const int tiles = (c->N + 31) / 32;
+  const int grid = std::min(tiles, sm_count());
+  CUtensorMap tm8, tme4;
+  int rc = make_maps(c, 32, 1, &tm8, &tme4);
+  if (rc) return rc;
+  const size_t xs_bytes = ((TMAX * 256 * 4 + 1023) / 1024) * 1024;
+  int NS = static_cast<int>((kSmemTarget - kHeader - xs_bytes) / kStageBytes);
+  NS = std::max(2, std::min(NS, 8));
+  const size_t smem = kHeader + xs_bytes + static_cast<size_t>(NS) * kStageBytes;
+  Params p{c->rp, c->ec, c->ev, x, y, nullptr, 0.0f, c->base, c->N, c->K, nch, 32, 1, nch, tiles, NS, T, xs_, ys_, 0};
+  rc = allow_smem(gemv_tn_kernel<MODE, TMAX>, smem);
+  if (rc) return rc;
+  return launch(gemv_tn_kernel<MODE, TMAX>, dim3(grid), dim3(kThreads), smem, s, "aib_gemv_c12(T>1)", tm8, tme4, p);
+}
+
+template <int TMAX>
+static int run_tn_mode(const aib_c12* c, const float* x, float* y, int T, int xs_, int ys_, int mode, cudaStream_t s) {
+  if (mode == 0) return run_tn_t<0, TMAX>(c, x, y, T, xs_, ys_, s);
+  if (mode == 1) return run_tn_t<1, TMAX>(c, x, y, T, xs_, ys_, s);
+  return run_tn_t<2, TMAX>(c, x, y, T, xs_, ys_, s);
+}
+
+}  // namespace gemv
+}  // namespace aib
+
+using namespace aib;
+
+extern "C" {
+
+size_t aib_gemv_c12_workspace(const aib_c12* c, int T) {
+  (void)c;
+  (void)T;
+  return 0;
+}
+
+int aib_gemv_c12(const aib_c12* c, const float* x, float* y, int T, int x_stride, int y_stride, int mode,
+                 const uint16_t* lnw, float eps, void* ws, size_t ws_bytes, void* stream) {
+  (void)ws;
+  (void)ws_bytes;
+  if (!c || !x || !y || !c->m8 || !c->e4 || !c->rp || (c->n_exc > 0 && (!c->ec || !c->ev)))
+    return fail(AIB_EINVAL, "aib_gemv_c12: null pointer");
+  if (c->N <= 0 || c->K <= 0 || c->K % 256 || c->CH != 256)
+    return fail(AIB_EINVAL, "aib_gemv_c12: K must be a positive multiple of 256 (N=%d K=%d CH=%d)", c->N, c->K, c->CH);
+  if (mode < 0 || mode > 2) return fail(AIB_EINVAL, "aib_gemv_c12: mode must be 0, 1 or 2");
+  if (c->base < 0 || c->base > 241) return fail(AIB_EINVAL, "aib_gemv_c12: base %d out of range", c->base);
+  if (T < 1 || T > 16) return fail(AIB_EINVAL, "aib_gemv_c12: T must be in 1..16");
+  if ((reinterpret_cast<uintptr_t>(c->m8) & 15) || (reinterpret_cast<uintptr_t>(c->e4) & 15))
+    return fail(AIB_EINVAL, "aib_gemv_c12: m8/e4 must be 16-byte aligned");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (T == 1) return gemv::run_t1(c, x, y, mode, lnw, eps, s);
+  if (lnw) return fail(AIB_EINVAL, "aib_gemv_c12: the RMS prologue is only available for T == 1");
+  const int xin = mode == 2 ? 2 * c->K : c->K;
+  if (x_stride < xin || y_stride < c->N) return fail(AIB_EINVAL, "aib_gemv_c12: row strides too small");
+  if (T <= 2) return gemv::run_tn_mode<2>(c, x, y, T, x_stride, y_stride, mode, s);
+  if (T <= 4) return gemv::run_tn_mode<4>(c, x, y, T, x_stride, y_stride, mode, s);
+  if (T <= 8) return gemv::run_tn_mode<8>(c, x, y, T, x_stride, y_stride, mode, s);
+  return gemv::run_tn_mode<16>(c, x, y, T, x_stride, y_stride, mode, s);
+}
+
+}  // extern "C"

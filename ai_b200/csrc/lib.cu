@@ -1,0 +1,8 @@
+// Single translation unit for libai_b200.so (device symbols such as the status word are shared by all
+// kernels without relocatable device code).
+#include "runtime.cu"
+#include "codec.cu"
+#include "gemv.cu"
+#include "norm.cu"
+#include "attn.cu"
+#include "sampler.cu"

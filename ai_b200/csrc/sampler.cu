@@ -1,0 +1,374 @@
+// Logits-in token sampler (sm_100a), one CTA per row.
+//
+// Reference semantics: GGUFEngine._pick (`ramvi/engine/ramvi_engine/core/gengine.py:452-469`) with the
+// bitmask of Constraint.apply (`generation/constrain.py:146-148`): greedy = first index among the maxima;
+// sampling = softmax(l.double()/T) -> descending order -> keep while the exclusive cumsum < top_p ->
+// renormalise -> numpy Generator.choice with a uniform u (index = #(cdf <= u)).
+// Extensions without a reference counterpart (the reference rejects them, server/validation.py:78-85):
+// repetition penalty (l<0 ? l*r : l/r over the set of prior ids), presence/frequency penalties
+// (l -= f*count + p*[count>0]) applied first, and top-k (keep z >= k-th largest) before top-p.
+//
+// Algorithm per row (no full sort of the vocabulary):
+//  1. penalties via a sorted prior-id table + a vocabulary bitmap in shared memory (O(1) test per token);
+//  2. greedy: block argmax;
+//  3. top-k threshold by 4-pass radix select on order-preserving 32-bit keys of the logits;
+//  4. top-p: a radix descent over per-bucket probability mass gives a key threshold whose upper set is a
+//     guaranteed superset of the nucleus (1e-9 relative margin on an atomically accumulated mass);
+//  5. the candidates (<= CMAX) are gathered, bitonic-sorted by (key desc, index asc), and the nucleus cut,
+//     renormalisation and inverse CDF are evaluated in float64 with a fixed-order block scan against the
+//     softmax denominator from a fixed-order reduction -- deterministic run to run.
+#include <climits>
+#include "common.cuh"
+
+namespace aib {
+namespace samp {
+
+constexpr int kThreads = 1024;
+constexpr int CMAX = 8192;
+constexpr int PMAX = 4096;
+
+AIB_DEV uint32_t fkey(float f) {
+  if (f != f) return 0u;  // NaN sorts last
+  const uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+AIB_DEV float key_value(uint32_t k) { return __uint_as_float((k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k); }
+
+struct Row {
+  const float* l;
+  const uint32_t* mask;  // may be null
+  const uint32_t* bitmap;
+  const int* pid;  // sorted prior ids (valid only), n_pid entries
+  int n_pid;
+  float rep, pres, freq;
+};
+
+// penalised + masked logit of token v
+AIB_DEV float value(const Row& r, int v) {
+  if (r.mask && !((r.mask[v >> 5] >> (v & 31)) & 1u)) return -INFINITY;
+  float x = __ldg(r.l + v);
+  if ((r.bitmap[v >> 5] >> (v & 31)) & 1u) {
+    int lo = 0, hi = r.n_pid;  // count = occurrences of v in the sorted prior list
+    while (lo < hi) {
+      const int mid = (lo + hi) >> 1;
+      if (r.pid[mid] < v) lo = mid + 1; else hi = mid;
+    }
+    const int a = lo;
+    hi = r.n_pid;
+    while (lo < hi) {
+      const int mid = (lo + hi) >> 1;
+      if (r.pid[mid] <= v) lo = mid + 1; else hi = mid;
+    }
+    const int cnt = lo - a;
+    if (r.rep != 1.0f) x = (x < 0.0f) ? __fmul_rn(x, r.rep) : __fdiv_rn(x, r.rep);
+    if (r.pres != 0.0f || r.freq != 0.0f)
+      x = __fsub_rn(x, __fadd_rn(__fmul_rn(static_cast<float>(cnt), r.freq), r.pres));
+  }
+  return x;
+}
+
+template <typename T>
+AIB_DEV T block_sum_fixed(T v, T* red) {  // deterministic: fixed lanes, fixed warp order
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  T s = 0;
+  for (int i = 0; i < kThreads / 32; ++i) s += red[i];
+  return s;
+}
+
+struct __align__(16) Shared {
+  double dred[32];
+  double hmass[256];
+  float fred[32];
+  int ired[32];
+  unsigned int hist[256];
+  int ncand;
+  uint32_t prefix;
+  double rem;
+};
+
+__global__ void __launch_bounds__(kThreads)
+    sample_kernel(const float* __restrict__ logits, int V, int ld, aib_sample_params prm,
+                  const int32_t* __restrict__ prior, int n_prior, const int32_t* __restrict__ bitmask,
+                  const double* __restrict__ us, int64_t* __restrict__ out) {
+  extern __shared__ __align__(16) uint8_t dsm[];
+  __shared__ Shared sh;
+  const int words = (V + 31) >> 5;
+  const int words_pad = (words + 3) & ~3;  // keeps every later array 16-byte aligned
+  uint32_t* bitmap = reinterpret_cast<uint32_t*>(dsm);
+  int* pid = reinterpret_cast<int*>(bitmap + words_pad);
+  uint32_t* ckey = reinterpret_cast<uint32_t*>(pid + PMAX);
+  int* cidx = reinterpret_cast<int*>(ckey + CMAX);
+  double* cp = reinterpret_cast<double*>(cidx + CMAX);
+  const int b = blockIdx.x, tid = threadIdx.x;
+  pdl_wait();
+
+  Row r;
+  r.l = logits + static_cast<size_t>(b) * ld;
+  r.mask = bitmask ? reinterpret_cast<const uint32_t*>(bitmask) + static_cast<size_t>(b) * words : nullptr;
+  r.bitmap = bitmap;
+  r.pid = pid;
+  r.rep = prm.repetition_penalty;
+  r.pres = prm.presence_penalty;
+  r.freq = prm.frequency_penalty;
+  // ---- 1. prior-id table (sorted) + bitmap
+  for (int i = tid; i < words; i += kThreads) bitmap[i] = 0u;
+  const bool penal = prior && n_prior > 0 &&
+                     (prm.repetition_penalty != 1.0f || prm.presence_penalty != 0.0f || prm.frequency_penalty != 0.0f);
+  int np2 = 1;
+  while (np2 < n_prior) np2 <<= 1;
+  if (!penal) np2 = 0;
+  for (int i = tid; i < np2; i += kThreads) {
+    int v = INT_MAX;
+    if (i < n_prior) {
+      const int x = prior[static_cast<size_t>(b) * n_prior + i];
+      if (x >= 0 && x < V) v = x;
+    }
+    pid[i] = v;
+  }
+  __syncthreads();
+  for (int k = 2; k <= np2; k <<= 1)
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      for (int i = tid; i < np2; i += kThreads) {
+        const int ixj = i ^ j;
+        if (ixj > i) {
+          const int a = pid[i], c = pid[ixj];
+          const bool up = (i & k) == 0;
+          if ((a > c) == up) pid[i] = c, pid[ixj] = a;
+        }
+      }
+      __syncthreads();
+    }
+  int nvalid = 0;
+  for (int i = tid; i < np2; i += kThreads) nvalid += pid[i] != INT_MAX;
+  nvalid = block_sum_fixed<int>(nvalid, sh.ired);
+  r.n_pid = nvalid;
+  for (int i = tid; i < nvalid; i += kThreads) atomicOr(&bitmap[pid[i] >> 5], 1u << (pid[i] & 31));
+  __syncthreads();
+
+  // ---- 2. max (and greedy argmax: first index among the maxima)
+  float best = -INFINITY;
+  int bi = INT_MAX;
+  for (int v = tid; v < V; v += kThreads) {
+    const float x = value(r, v);
+    if (x > best || (x == best && v < bi)) best = x, bi = v;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ob > best || (ob == best && oi < bi)) best = ob, bi = oi;
+  }
+  if ((tid & 31) == 0) sh.fred[tid >> 5] = best, sh.ired[tid >> 5] = bi;
+  __syncthreads();
+  best = -INFINITY;
+  bi = INT_MAX;
+  for (int i = 0; i < kThreads / 32; ++i)
+    if (sh.fred[i] > best || (sh.fred[i] == best && sh.ired[i] < bi)) best = sh.fred[i], bi = sh.ired[i];
+  if (bi == INT_MAX) bi = 0;  // every logit NaN / masked: first token
+  const float T = prm.temperature;
+  if (!(T > 0.0f) || best == -INFINITY) {
+    if (tid == 0) out[b] = bi;
+    pdl_trigger();
+    return;
+  }
+  const double Td = static_cast<double>(T);  // z = l.double() / T, as the reference
+  const double Mz = static_cast<double>(best) / Td;
+
+  // ---- 3. top-k threshold key (k-th largest, ties kept)
+  uint32_t thr = 0u;
+  const int topk = prm.top_k;
+  if (topk > 0 && topk < V) {
+    uint32_t prefix = 0u, pmask = 0u;
+    int remaining = topk;
+    for (int shift = 24; shift >= 0; shift -= 8) {
+      __syncthreads();
+      for (int i = tid; i < 256; i += kThreads) sh.hist[i] = 0u;
+      __syncthreads();
+      for (int v = tid; v < V; v += kThreads) {
+        const uint32_t k = fkey(value(r, v));
+        if ((k & pmask) == prefix) atomicAdd(&sh.hist[(k >> shift) & 0xFFu], 1u);
+      }
+      __syncthreads();
+      if (tid == 0) {
+        int cum = 0, d;
+        for (d = 255; d > 0; --d) {
+          if (cum + static_cast<int>(sh.hist[d]) >= remaining) break;
+          cum += sh.hist[d];
+        }
+        sh.prefix = prefix | (static_cast<uint32_t>(d) << shift);
+        sh.ired[0] = remaining - cum;
+      }
+      __syncthreads();
+      prefix = sh.prefix;
+      remaining = sh.ired[0];
+      pmask |= 0xFFu << shift;
+    }
+    thr = prefix;
+  }
+
+  // ---- softmax denominator over the kept set (fixed-order reduction)
+  double part = 0.0;
+  for (int v = tid; v < V; v += kThreads) {
+    const float x = value(r, v);
+    if (fkey(x) >= thr && x != -INFINITY) part += exp(static_cast<double>(x) / Td - Mz);
+  }
+  const double Z = block_sum_fixed<double>(part, sh.dred);
+
+  // ---- 4. top-p superset threshold by radix descent over probability mass
+  const double top_p = static_cast<double>(prm.top_p);
+  if (top_p < 1.0) {
+    uint32_t prefix = 0u, pmask = 0u;
+    double target = top_p * Z * (1.0 + 1e-9) + 1e-300;
+    for (int shift = 24; shift >= 0; shift -= 8) {
+      __syncthreads();
+      for (int i = tid; i < 256; i += kThreads) sh.hmass[i] = 0.0;
+      __syncthreads();
+      for (int v = tid; v < V; v += kThreads) {
+        const float x = value(r, v);
+        const uint32_t k = fkey(x);
+        if (k >= thr && x != -INFINITY && (k & pmask) == prefix)
+          atomicAdd(&sh.hmass[(k >> shift) & 0xFFu], exp(static_cast<double>(x) / Td - Mz));
+      }
+      __syncthreads();
+      if (tid == 0) {
+        double cum = 0.0;
+        int d;
+        for (d = 255; d > 0; --d) {
+          if (cum + sh.hmass[d] >= target) break;
+          cum += sh.hmass[d];
+        }
+        sh.prefix = prefix | (static_cast<uint32_t>(d) << shift);
+        sh.rem = target - cum;
+      }
+      __syncthreads();
+      prefix = sh.prefix;
+      target = sh.rem;
+      pmask |= 0xFFu << shift;
+    }
+    thr = max(thr, prefix);
+  }
+
+  // ---- 5. gather candidates (key >= thr, finite), sort, exact nucleus + inverse CDF
+  __syncthreads();
+  if (tid == 0) sh.ncand = 0;
+  __syncthreads();
+  for (int v = tid; v < V; v += kThreads) {
+    const float x = value(r, v);
+    const uint32_t k = fkey(x);
+    if (k >= thr && x != -INFINITY) {
+      const int slot = atomicAdd(&sh.ncand, 1);
+      if (slot < CMAX) ckey[slot] = k, cidx[slot] = v;
+    }
+  }
+  __syncthreads();
+  int nc = sh.ncand;
+  if (nc > CMAX) {
+    if (tid == 0) set_status(AIB_DEV_SAMPLER_CAP);
+    nc = CMAX;
+  }
+  int n2 = 1;
+  while (n2 < nc) n2 <<= 1;
+  for (int i = nc + tid; i < n2; i += kThreads) ckey[i] = 0u, cidx[i] = INT_MAX;
+  __syncthreads();
+  for (int k = 2; k <= n2; k <<= 1)  // bitonic sort: (key desc, idx asc)
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      for (int i = tid; i < n2; i += kThreads) {
+        const int ixj = i ^ j;
+        if (ixj > i) {
+          const uint32_t ka = ckey[i], kb = ckey[ixj];
+          const int ia = cidx[i], ib = cidx[ixj];
+          const bool a_first = (ka > kb) || (ka == kb && ia < ib);
+          const bool up = (i & k) == 0;
+          if (a_first != up) ckey[i] = kb, ckey[ixj] = ka, cidx[i] = ib, cidx[ixj] = ia;
+        }
+      }
+      __syncthreads();
+    }
+  for (int i = tid; i < nc; i += kThreads)  // probabilities in sorted order
+    cp[i] = exp(static_cast<double>(key_value(ckey[i])) / Td - Mz) / Z;
+  __syncthreads();
+  // exclusive scan in a fixed order: contiguous segment per thread, then lanes, then warps
+  const int per = (nc + kThreads - 1) / kThreads;
+  const int a0 = min(nc, tid * per), a1 = min(nc, a0 + per);
+  double seg = 0.0;
+  for (int i = a0; i < a1; ++i) seg += cp[i];
+  double incl = seg;
+  const int lane = tid & 31, warp = tid >> 5;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const double y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  __syncthreads();
+  if (lane == 31) sh.dred[warp] = incl;
+  __syncthreads();
+  double wbase = 0.0;
+  for (int w = 0; w < warp; ++w) wbase += sh.dred[w];
+  double run = wbase + incl - seg;
+  for (int i = a0; i < a1; ++i) {
+    const double pi = cp[i];
+    cp[i] = run;  // exclusive prefix
+    run += pi;
+  }
+  __syncthreads();
+  int keep = 0;  // keep while exclusive cumsum < top_p
+  for (int i = tid; i < nc; i += kThreads) keep += (top_p >= 1.0 || cp[i] < top_p) ? 1 : 0;
+  keep = block_sum_fixed<int>(keep, sh.ired);
+  keep = max(1, min(keep, nc));
+  const double pl = exp(static_cast<double>(key_value(ckey[keep - 1])) / Td - Mz) / Z;
+  const double S = cp[keep - 1] + pl;  // kept mass
+  const double u = us ? us[b] : 0.5;
+  int cntle = 0;  // index = #(cdf_i <= u), cdf_i = inclusive_i / S
+  for (int i = tid; i < keep; i += kThreads) {
+    const double incl_i = (i + 1 < keep) ? cp[i + 1] : S;
+    cntle += (incl_i / S <= u) ? 1 : 0;
+  }
+  cntle = block_sum_fixed<int>(cntle, sh.ired);
+  const int pick = min(cntle, keep - 1);
+  if (tid == 0) out[b] = cidx[pick];
+  pdl_trigger();
+}
+
+static size_t smem_bytes(int V) {
+  const size_t words = ((static_cast<size_t>(V) + 31) / 32 + 3) & ~static_cast<size_t>(3);
+  return words * 4 + PMAX * 4 + CMAX * 4 + CMAX * 4 + CMAX * 8;
+}
+
+}  // namespace samp
+}  // namespace aib
+
+using namespace aib;
+
+extern "C" {
+
+size_t aib_sample_workspace(int B, int V) {
+  (void)B;
+  (void)V;
+  return 0;
+}
+
+int aib_sample(const float* logits, int B, int V, int ld, const aib_sample_params* params, const int32_t* prior,
+               int n_prior, const int32_t* bitmask, const double* u, int64_t* out_ids, void* ws, size_t ws_bytes,
+               void* stream) {
+  (void)ws;
+  (void)ws_bytes;
+  if (!logits || !params || !out_ids || B <= 0 || V <= 0 || ld < V)
+    return fail(AIB_EINVAL, "aib_sample: bad arguments (B=%d V=%d ld=%d)", B, V, ld);
+  if (n_prior < 0 || n_prior > samp::PMAX) return fail(AIB_EINVAL, "aib_sample: n_prior must be in 0..%d", samp::PMAX);
+  const aib_sample_params& p = *params;
+  if (p.temperature > 0.0f && !u) return fail(AIB_EINVAL, "aib_sample: sampling needs the uniform draws u");
+  if (p.temperature > 0.0f && !(p.top_p > 0.0f)) return fail(AIB_EINVAL, "aib_sample: top_p must be > 0");
+  if (!(p.repetition_penalty > 0.0f)) return fail(AIB_EINVAL, "aib_sample: repetition_penalty must be > 0");
+  const size_t smem = samp::smem_bytes(V);
+  if (smem > 227 * 1024) return fail(AIB_ENOTSUP, "aib_sample: vocabulary of %d too large", V);
+  const int rc = allow_smem(samp::sample_kernel, smem);
+  if (rc) return rc;
+  return launch(samp::sample_kernel, dim3(B), dim3(samp::kThreads), smem, static_cast<cudaStream_t>(stream),
+                "aib_sample", logits, V, ld, p, prior, n_prior, bitmask, u, out_ids);
+}
+
+}  // extern "C"

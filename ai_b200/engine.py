@@ -1,0 +1,291 @@
+"""Qwen3 decode engine on the 12-bit codec -- the reference `Engine` surface (core/engine.py:195-803) on sm_100a.
+
+Load (`Engine.__init__`, core/engine.py:196-263): the reference encodes each fused matrix (qkv = [q;k;v],
+gu = [gate;up], formats/model.py:92-102) with `compress` on the GPU; here the device encoder of
+libai_b200.so does it. All layers stay resident (a B200 holds any dense model up to ~100B params in the
+12-bit codec), so the reference's gpu/stream/cpu placement, pinned arena and loader thread have no
+counterpart.
+
+Step (`_gpu_layer` :329-341 for T = 1, `_batch_layer` :344-356 for T <= 16), captured once per shape in a
+CUDA graph (`_capture` :415-444) and replayed with the position and the input ids in device memory:
+    embed(ids) -> per layer: gemv(qkv, RMS ln1) -> rope_attn -> gemv(o, +=) -> gemv(gu, RMS ln2) -> gemv(down,
+    silu*up, +=)  -> head gemv (RMS final norm fused) -> sampler -> advance(ids, pos)
+T > 1 uses rmsnorm + batched gemv + qk_rope_cache + cached attention. Unlike the reference (head on the
+GPU, exact logits and sampling on the CPU, head.py:59-88, with a D2H sync per token), the head is a 12-bit
+GEMV over the whole vocabulary and sampling runs on the device: one 8-byte read per generated token.
+
+`process(tokens, pos0, ...)` and `generate(prompt, ...)` keep the reference arguments and errors
+(core/engine.py:489-694), with top_k / penalties added; prompts longer than 16 tokens run in 16-token
+batched chunks (the reference's legacy prefill path, core/engine.py:471-480).
+"""
+import time
+
+import numpy as np
+import torch
+
+from . import _lib, wcomp, tkernels, sampler
+from ._lib import ptr, stream_ptr
+from .model import CONFIGS, Ckpt, RandomWeights, Qwen3Config
+
+MATS = ("qkv", "o", "gu", "down")
+MAXB = 16
+
+
+class Engine:
+    def __init__(self, name, maxt=2048, device="cuda", seed=0, log=print, norm_noise=0.0, weights=None,
+                 graphs=True):
+        """name: an HF Qwen3 folder, or a key of ai_b200.model.CONFIGS / a Qwen3Config for random-init
+        weights (N(0, 0.02) matrices, seed `seed`). weights: an explicit weight source (RandomWeights/Ckpt)."""
+        if not isinstance(maxt, int) or isinstance(maxt, bool) or maxt < 1:
+            raise ValueError("maxt must be a positive integer")
+        t0 = time.time()
+        self.device = torch.device(device)
+        torch.cuda.set_device(self.device)
+        if weights is not None:
+            src = weights
+            cfg = weights.cfg if hasattr(weights, "cfg") else weights.config
+        elif isinstance(name, Qwen3Config):
+            cfg, src = name, RandomWeights(name, seed=seed, norm_noise=norm_noise, device="cuda")
+        elif isinstance(name, str) and name in CONFIGS:
+            cfg = CONFIGS[name]
+            src = RandomWeights(cfg, seed=seed, norm_noise=norm_noise, device="cuda")
+        else:
+            src = Ckpt(name)
+            cfg = src.config
+        self.cfg = cfg
+        self.L, self.D, self.H, self.KV, self.HD, self.FF, self.V = cfg.L, cfg.D, cfg.H, cfg.KV, cfg.HD, cfg.FF, cfg.V
+        self.eps, self.maxt, self.log = cfg.eps, maxt, log
+        self.eos = set(cfg.eos)
+        dev = self.device
+        self.inv = (1.0 / (cfg.theta ** (torch.arange(0, self.HD, 2, dtype=torch.float32) / self.HD))).to(dev)
+        # ---- weights
+        self.W, self.small = [], []
+        for i in range(self.L):
+            lw = src.layer(i)
+            self.W.append({n: wcomp.compress(lw[n].to(dev)) for n in MATS})
+            self.small.append({k: lw[k].to(dev).contiguous() for k in ("ln1", "ln2", "qn", "kn")})
+            del lw
+        self.emb = src.embedding().to(dev).contiguous()
+        self.head = wcomp.compress(self.emb if cfg.tied else src.head().to(dev))
+        self.norm = src.final_norm().to(dev).contiguous()
+        torch.cuda.synchronize()
+        # ---- KV cache (bf16) and work buffers
+        self.kv = torch.zeros(self.L, 2, self.KV, maxt, self.HD, dtype=torch.bfloat16, device=dev)
+        f = lambda n: torch.zeros(MAXB, n, device=dev)  # noqa: E731
+        H, KV, HD = self.H, self.KV, self.HD
+        self.xb, self.hb = f(self.D), f(self.D)
+        self.qkvb, self.qb, self.attb, self.gub = f((H + 2 * KV) * HD), f(H * HD), f(H * HD), f(2 * self.FF)
+        self.logits = torch.zeros(MAXB, self.V, device=dev)
+        self.pos = torch.zeros(1, dtype=torch.int64, device=dev)
+        self.ids = torch.zeros(MAXB, dtype=torch.int64, device=dev)
+        self.out_ids = torch.zeros(MAXB, dtype=torch.int64, device=dev)
+        self.u = torch.zeros(MAXB, dtype=torch.float64, device=dev)
+        self.prior = torch.full((1, sampler.PMAX), -1, dtype=torch.int32, device=dev)
+        self.ws = torch.zeros(_lib.lib().aib_attn_workspace(H, KV, HD, maxt, MAXB), dtype=torch.uint8, device=dev)
+        self.use_graphs = graphs
+        self.graphs = {}
+        self.ctx = []
+        self.scale = HD ** -0.5
+        self.weight_bytes = sum(c.nbytes for w in self.W for c in w.values())
+        self.head_bytes = self.head.nbytes
+        self.load_s = time.time() - t0
+        if log:
+            log(f"loaded {cfg.name}: {self.weight_bytes / 2**30:.2f} GiB layers + {self.head_bytes / 2**30:.2f} GiB "
+                f"head (12-bit), KV {self.kv.numel() * 2 / 2**30:.2f} GiB, {self.load_s:.1f} s")
+
+    def close(self):
+        self.graphs.clear()
+
+    # ------------------------------------------------------------------------------------ step body
+    def _layers(self, T):
+        H, KV, HD = self.H, self.KV, self.HD
+        for l in range(self.L):
+            W, s = self.W[l], self.small[l]
+            kc, vc = self.kv[l, 0], self.kv[l, 1]
+            if T == 1:
+                x = self.xb[0]
+                wcomp.gemvc1(x, W["qkv"], self.qkvb[0], 0, lnw=s["ln1"], eps=self.eps)
+                tkernels.rope_attn(self.qkvb[0], s["qn"], s["kn"], self.inv, self.pos, kc, vc, self.attb[0], self.maxt,
+                                   self.eps, self.scale, H, KV, HD, ws=self.ws)
+                wcomp.gemvc1(self.attb[0], W["o"], x, 1)
+                wcomp.gemvc1(x, W["gu"], self.gub[0], 0, lnw=s["ln2"], eps=self.eps)
+                wcomp.gemvc1(self.gub[0], W["down"], x, 2)
+            else:
+                x, h = self.xb[:T], self.hb[:T]
+                tkernels.rmsg(x, s["ln1"], h, self.eps)
+                wcomp.gemvc_tc(h, W["qkv"], self.qkvb[:T], 0, T)
+                tkernels.qk_rope_cache(self.qkvb[:T], s["qn"], s["kn"], self.inv, self.pos, self.qb[:T], kc, vc,
+                                       self.maxt, self.eps, H, KV, HD, T)
+                tkernels.attn(self.qb[:T], kc, vc, self.pos, self.attb[:T], self.maxt, self.scale, H, KV, HD, T,
+                              ws=self.ws)
+                wcomp.gemvc_tc(self.attb[:T], W["o"], x, 1, T)
+                tkernels.rmsg(x, s["ln2"], h, self.eps)
+                wcomp.gemvc_tc(h, W["gu"], self.gub[:T], 0, T)
+                wcomp.gemvc_tc(self.gub[:T], W["down"], x, 2, T)
+
+    def _head(self, T):
+        if T == 1:
+            wcomp.gemvc1(self.xb[0], self.head, self.logits[0], 0, lnw=self.norm, eps=self.eps)
+        else:
+            tkernels.rmsg(self.xb[:T], self.norm, self.hb[:T], self.eps)
+            wcomp.gemvc_tc(self.hb[:T], self.head, self.logits[:T], 0, T)
+
+    def _step(self, T, prm, rows, penal):
+        """Everything that runs on the device for one pass of T tokens (graph body)."""
+        tkernels.embed(self.emb, self.ids[:T], self.xb[:T])
+        self._layers(T)
+        self._head(T)
+        r0 = T - rows
+        sampler.sample_into(self.logits[r0:T], self.out_ids[r0:T], prm, self.u[:rows] if prm.temperature > 0 else None,
+                            self.prior if penal else None, None, B=rows)
+        _lib.call("aib_step_advance", ptr(self.pos), ptr(self.ids), ptr(self.out_ids), T,
+                  ptr(self.prior) if penal else None, sampler.PMAX if penal else 0, stream_ptr())
+
+    def _run(self, T, prm, rows, penal):
+        key = (T, rows, penal, prm.temperature, prm.top_k, prm.top_p, prm.repetition_penalty, prm.presence_penalty,
+               prm.frequency_penalty)
+        if not self.use_graphs:
+            self._step(T, prm, rows, penal)
+            return
+        g = self.graphs.get(key)
+        if g is None:
+            # First use of this shape: run the step eagerly (it is the real step; one-time library setup such
+            # as shared-memory attributes happens outside capture), then capture it for later replays.
+            self._step(T, prm, rows, penal)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, capture_error_mode="thread_local"):
+                self._step(T, prm, rows, penal)
+            self.graphs[key] = g
+            return
+        g.replay()
+
+    # ----------------------------------------------------------------------------------------- API
+    def _validate_process(self, tokens, pos0):
+        if not isinstance(pos0, int) or isinstance(pos0, bool) or not 0 <= pos0 <= len(self.ctx):
+            raise ValueError("position does not extend a valid prefix")
+        if not tokens:
+            raise ValueError("an empty pass is not supported")
+        for t in tokens:
+            try:
+                i = t.__index__()
+            except (AttributeError, TypeError) as exc:
+                raise ValueError("token ids must be integers") from exc
+            if isinstance(t, bool) or i < 0 or i >= self.V:
+                raise ValueError("token id outside the vocabulary")
+
+    def _pass(self, tokens, pos0, prm, us, last_only, penal=False):
+        """Run tokens from pos0 in chunks of <= 16; returns the sampled ids (last chunk only if last_only)."""
+        out = []
+        n = len(tokens)
+        c = 0
+        while c < n:
+            T = min(MAXB, n - c)
+            final = c + T >= n
+            rows = (1 if last_only else T) if final else 0
+            self.ids[:T].copy_(torch.tensor(tokens[c:c + T], dtype=torch.int64))
+            self.pos.fill_(pos0 + c)
+            if rows:
+                if prm.temperature > 0:
+                    self.u[:rows].copy_(torch.tensor(us[:rows], dtype=torch.float64))
+                self._run(T, prm, rows, penal)
+                out = self.out_ids[T - rows:T].tolist()
+            else:
+                self._run(T, sampler.params(), 1, False)  # intermediate chunk: fills the KV cache
+            c += T
+        return out
+
+    def process(self, tokens, pos0, temperature=0.0, top_p=1.0, rng=None, last_only=False, top_k=0):
+        """Run `tokens` from position pos0 (KV before pos0 already cached). Returns the next-token pick after
+        each token (only after the last one for last_only or prompts longer than 16 tokens), like the
+        reference `Engine.process` (core/engine.py:505-526)."""
+        self._validate_process(tokens, pos0)
+        if pos0 + len(tokens) > self.maxt:
+            raise ValueError(f"text longer than {self.maxt} tokens")
+        previous = self.ctx[:pos0]
+        last_only = last_only or len(tokens) > MAXB
+        rows = 1 if last_only else len(tokens)
+        us = None
+        if temperature > 0:
+            rng = rng or np.random.default_rng()
+            us = [rng.random() for _ in range(rows)]
+        prm = sampler.params(temperature, top_k, top_p)
+        try:
+            result = self._pass(list(tokens), pos0, prm, us, last_only)
+        except Exception:
+            self.ctx = []
+            raise
+        self.ctx = previous + list(tokens)
+        return result
+
+    def common(self, seq):
+        n = 0
+        for a, b in zip(self.ctx, seq):
+            if a != b:
+                break
+            n += 1
+        return n
+
+    def generate(self, prompt, max_new=256, temperature=0.0, top_p=1.0, seed=None, top_k=0, repetition_penalty=1.0,
+                 presence_penalty=0.0, frequency_penalty=0.0, stats=None, draft=None, k=None, force=None, cons=None):
+        """Yield up to max_new tokens (reference generate, core/engine.py:538-694, without the draft engine).
+        Penalties count the prompt and the generated tokens (the most recent 4096 ids)."""
+        if draft is not None or cons is not None:
+            raise NotImplementedError("draft engines and grammar constraints are not part of this engine")
+        if not isinstance(max_new, int) or isinstance(max_new, bool) or max_new < 0:
+            raise ValueError("max_new must be a non-negative integer")
+        if max_new == 0:
+            if stats is not None:
+                stats.update(prompt_n=0, prompt_ms=0.0, gen_n=0, decode_n=0, gen_ms=0.0)
+            return
+        if not prompt:
+            raise ValueError("an empty prompt is not supported; pass BOS or text")
+        P = len(prompt)
+        if P > self.maxt:
+            raise ValueError(f"prompt longer than the context {self.maxt}")
+        rng = np.random.default_rng(seed)
+        max_new = min(max_new, self.maxt - P + 1)
+        c = min(self.common(prompt), P - 1)
+        prm = sampler.params(temperature, top_k, top_p, repetition_penalty, presence_penalty, frequency_penalty)
+        penal = repetition_penalty != 1.0 or presence_penalty != 0.0 or frequency_penalty != 0.0
+        if penal:
+            ring = np.full(sampler.PMAX, -1, np.int32)
+            for i, t in enumerate(prompt):
+                ring[i % sampler.PMAX] = t
+            self.prior.copy_(torch.from_numpy(ring)[None])
+        self._validate_process(list(prompt[c:]), c)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        us = [rng.random()] if temperature > 0 else None
+        try:
+            tok = self._pass(list(prompt[c:]), c, prm, us, True, penal)[-1]
+        except Exception:
+            self.ctx = []
+            raise
+        self.ctx = list(prompt)
+        t1 = time.perf_counter()
+        st = stats if stats is not None else {}
+        st.update(prompt_n=P - c, prompt_ms=(t1 - t0) * 1000, first_token_ms=(t1 - t0) * 1000, gen_n=1, decode_n=0,
+                  gen_ms=0.0, passes=0)
+        gen = [tok]
+        yield tok
+        # decode loop: the graph chains ids and pos on the device; the host supplies u and reads one id
+        while len(gen) < max_new and gen[-1] not in self.eos:
+            ts = time.perf_counter()
+            if temperature > 0:
+                self.u[0] = rng.random()
+            self._run(1, prm, 1, penal)
+            t = int(self.out_ids[0].item())
+            self.ctx.append(gen[-1])
+            st["gen_ms"] += (time.perf_counter() - ts) * 1000
+            st["passes"] += 1
+            gen.append(t)
+            st["gen_n"] = len(gen)
+            st["decode_n"] = len(gen) - 1
+            yield t
+
+    # ------------------------------------------------------------------------------ bench helpers
+    def bytes_per_token(self, ctx):
+        """Algorithmic HBM bytes of one T=1 decode step at context length ctx: 12-bit layer weights +
+        12-bit head + the bf16 K/V rows attended (ctx positions) + the current K/V written."""
+        kv = self.L * 2 * self.KV * (ctx + 1) * self.HD * 2
+        return self.weight_bytes + self.head_bytes + kv

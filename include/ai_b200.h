@@ -1,0 +1,156 @@
+/* ai_b200 -- C ABI of the B200-native (sm_100a) 12-bit-codec decode path.
+ *
+ * Every entry point replaces one Python launcher or kernel launch of the reference engine
+ * (karabilo214/AI, `ramvi/engine/ramvi_engine/...`; cited per function). The reference has no native FFI for
+ * this path -- its kernels are Triton launched from Python -- so this header is the boundary a binding
+ * (ctypes) calls instead of those launchers.
+ *
+ * Conventions (same contract as the reference launchers, made explicit for C):
+ *  - All device pointers are caller-owned; kernels write their outputs in place.
+ *  - Calls are stream-ordered on `stream` (a cudaStream_t passed as void*), never allocate device memory
+ *    and never synchronise, so they can be captured in CUDA graphs. Scratch memory, where a kernel needs
+ *    it, is a caller-provided workspace (`ws`, `ws_bytes`; size from the matching *_workspace query; it must
+ *    be zero-filled once before first use -- the kernels leave their counters at zero again).
+ *  - Return value: AIB_OK (0) or a negative AIB_E* code; aib_last_error() gives a message for the calling
+ *    thread. Shape errors map to the reference's ValueError (e.g. wcomp.py:122-123).
+ *  - Device-side failures (a bounded wait that ran out, an out-of-range index in data) never trap: they set
+ *    a device status word readable with aib_status_read().
+ */
+#ifndef AI_B200_H
+#define AI_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define AIB_ABI_VERSION 1
+
+#define AIB_OK 0
+#define AIB_EINVAL (-1)     /* bad argument / shape (reference: ValueError)           */
+#define AIB_ECUDA (-2)      /* CUDA runtime error at launch                            */
+#define AIB_EWORKSPACE (-3) /* workspace missing or too small                          */
+#define AIB_ENOTSUP (-4)    /* configuration not supported by this build               */
+#define AIB_ESPACE (-5)     /* output capacity too small (two-pass APIs report need)   */
+
+/* device status codes (aib_status_read) */
+#define AIB_DEV_TIMEOUT_FULL 101  /* GEMV consumer waited too long for a TMA stage          */
+#define AIB_DEV_TIMEOUT_EMPTY 102 /* GEMV producer waited too long for a free stage         */
+#define AIB_DEV_BAD_TOKEN 103     /* embedding id outside the vocabulary                     */
+#define AIB_DEV_BAD_POS 104       /* KV position outside [0, maxt)                            */
+#define AIB_DEV_SAMPLER_CAP 105   /* sampler candidate buffer overflow                        */
+#define AIB_DEV_OVERFLOW 106      /* an output list is shorter than its CSR row pointers say  */
+
+/* One 12-bit-encoded matrix W [N, K] (K % CH == 0, CH == 256), device pointers. Same planes as the
+ * reference `compress` dict (wcomp.py:13-32): m8 [N,K] = sign<<7|mantissa, e4 [N,K/2] exponent codes
+ * (byte i of each 256-chunk holds element i in the low nibble and 128+i in the high nibble), base,
+ * CSR exceptions rp [N+1], er/ec [n_exc] (row-major order), ev [n_exc] fp32 values. */
+typedef struct aib_c12 {
+  const uint8_t* m8;
+  const uint8_t* e4;
+  const int32_t* rp;
+  const int32_t* er;
+  const int32_t* ec;
+  const float* ev;
+  int32_t base;
+  int32_t N;
+  int32_t K;
+  int32_t CH;
+  int64_t n_exc;
+} aib_c12;
+
+/* ------------------------------------------------------------------------------------ library ---- */
+int aib_abi_version(void);
+const char* aib_last_error(void);
+/* Programmatic dependent launch between consecutive kernels (default on). */
+void aib_set_pdl(int enabled);
+/* Device status word of the current device: copies it to *out (synchronous) and, if clear != 0, resets it. */
+int aib_status_read(int* out, int clear);
+
+/* ---------------------------------------------------------------------------------- 12-bit codec ---- */
+/* Host encoder, bit-exact with `compress` (wcomp.py:13-32). w: bf16 bits [N,K]. Writes m8, e4, rp, *base,
+ * *n_exc; writes er/ec/ev when exc_cap >= *n_exc, else returns AIB_ESPACE (call again with room). */
+int aib_c12_encode_host(const uint16_t* w, int N, int K, uint8_t* m8, uint8_t* e4, int32_t* rp, int32_t* base,
+                        int64_t* n_exc, int32_t* er, int32_t* ec, float* ev, int64_t exc_cap);
+/* Device encoder, pass 1 (replaces `compress` run on the GPU at load, core/engine.py:223-224): histogram,
+ * base selection, m8/e4 planes and rp. base_out / rp are device pointers; rp[N] is the exception count.
+ * ws >= aib_c12_encode_workspace(N) bytes (no zero-fill needed). */
+size_t aib_c12_encode_workspace(int N);
+int aib_c12_encode_planes(const uint16_t* w, int N, int K, uint8_t* m8, uint8_t* e4, int32_t* rp, int32_t* base_out,
+                          void* ws, size_t ws_bytes, void* stream);
+/* Device encoder, pass 2: exception lists (row-major) given rp from pass 1. */
+int aib_c12_encode_exceptions(const uint16_t* w, int N, int K, int base, const int32_t* rp, int32_t* er,
+                              int32_t* ec, float* ev, void* stream);
+/* Exact decode of rows [first,last) (replaces `decompress` wcomp.py:35-45 and `decode_rows`
+ * prefill_kernels.py:221-231). out_dtype 0: fp32 [last-first, K]; 1: bf16 bits. */
+int aib_c12_decode(const aib_c12* c, int first, int last, void* out, int out_dtype, void* stream);
+
+/* --------------------------------------------------------------------------------- codec GEMV ---- */
+/* Y[t] (+)= W * xin(X[t]) for t < T (replaces `gemvc1` wcomp.py:118-126 for T == 1 and `gemvc_tc`
+ * wcomp.py:233-242 for 1 < T <= 16). mode 0: Y = Wx; 1: Y += Wx; 2: input silu(x[:K]) * x[K:2K], Y += Wx.
+ * lnw (bf16 bits [K], may be NULL): RMSNorm prologue of gemvc1_k (wcomp.py:75-86), T == 1 only.
+ * x_stride / y_stride: elements between rows of X / Y (ignored for T == 1). */
+size_t aib_gemv_c12_workspace(const aib_c12* c, int T);
+int aib_gemv_c12(const aib_c12* c, const float* x, float* y, int T, int x_stride, int y_stride, int mode,
+                 const uint16_t* lnw, float eps, void* ws, size_t ws_bytes, void* stream);
+
+/* ------------------------------------------------------------------------------- norm / embed ---- */
+/* out[t] = w * x[t] * rsqrt(mean(x[t]^2) + eps)   (replaces rmsg_k, tkernels.py:216-225) */
+int aib_rmsnorm(const float* x, const uint16_t* w, float* out, int T, int D, float eps, void* stream);
+/* out[t] = fp32(emb[ids[t]])   (replaces Engine._emb, core/engine.py:388-390, done on the device) */
+int aib_embed(const uint16_t* emb, const int64_t* ids, int T, int D, int V, float* out, void* stream);
+/* Decode-loop bookkeeping (the reference does this on the host, core/engine.py:393-413):
+ * next_ids[0] = out_ids[T-1]; *pos += T; if prior != NULL, prior[new_pos % n_prior] = that id (ring of
+ * recent ids for the sampler's penalties). Keeps a captured decode step free of host copies. */
+int aib_step_advance(int64_t* pos, int64_t* next_ids, const int64_t* out_ids, int T, int32_t* prior, int n_prior,
+                     void* stream);
+
+/* -------------------------------------------------------------------------------- attention ---- */
+/* T == 1 fused step (replaces rope_attn_k, tkernels.py:164-213): QK-RMSNorm + RoPE of q and k,
+ * bf16 round of the current k/v, write to the caches at *pos, GQA attention over 0..pos (flash-decoding
+ * split over the context, ordered merge). qkv fp32 [(H+2KV)*HD]; caches bf16 bits [KV, maxt, HD];
+ * out fp32 [H*HD]. ws >= aib_attn_workspace(...), zero-filled once. */
+size_t aib_attn_workspace(int H, int KV, int HD, int maxt, int T);
+int aib_rope_attn_decode(const float* qkv, const uint16_t* qn, const uint16_t* kn, const float* inv,
+                         const int64_t* pos, uint16_t* kc, uint16_t* vc, float* out, int H, int KV, int HD,
+                         int maxt, float eps, float scale, void* ws, size_t ws_bytes, void* stream);
+/* Batched prologue (replaces qk_rope_cache_k, tkernels.py:82-120): q of tokens t < T normed+rotated into
+ * q [T, H*HD]; k, v rows written at *pos + t. */
+int aib_qk_rope_cache(const float* qkv, const uint16_t* qn, const uint16_t* kn, const float* inv, const int64_t* pos,
+                      float* q, uint16_t* kc, uint16_t* vc, int T, int H, int KV, int HD, int maxt, float eps,
+                      void* stream);
+/* Batched causal attention over the cache (replaces attn_k, tkernels.py:123-150, and the prefill att_k,
+ * prefill_kernels.py:30-56): token t attends 0..*pos + t. q [T, H*HD] -> out [T, H*HD]. */
+int aib_attn_cached(const float* q, const uint16_t* kc, const uint16_t* vc, const int64_t* pos, float* out, int T,
+                    int H, int KV, int HD, int maxt, float scale, void* ws, size_t ws_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------------- sampler ---- */
+/* Logits-in sampler (replaces GGUFEngine._pick, core/gengine.py:452-469, with Constraint.apply,
+ * generation/constrain.py:146-148, and the sampling half of Head.pick, generation/head.py:59-88).
+ * Order: penalties (repetition over the set of prior ids: l<0 ? l*r : l/r; presence/frequency:
+ * l -= f*count + p*[count>0]) -> bitmask (bit j of word w = token 32w+j, 1 = allowed) -> temperature
+ * (<= 0: greedy, first index among maxima) -> top-k (keep z >= k-th largest; 0 = off) -> top-p over the
+ * descending order (keep while the exclusive cumsum < top_p) -> inverse CDF with the row's uniform u[b]
+ * (index = #(cdf <= u), numpy Generator.choice semantics). Top-k and penalties have no reference
+ * counterpart (the reference rejects them, server/validation.py:78-85).
+ * prior: int32 [B, n_prior] (ids outside [0,V) ignored); bitmask: int32 [B, ceil(V/32)] or NULL;
+ * u: float64 [B] or NULL (greedy only); out_ids: int64 [B]. */
+typedef struct aib_sample_params {
+  float temperature;
+  int32_t top_k;
+  float top_p;
+  float repetition_penalty;
+  float presence_penalty;
+  float frequency_penalty;
+} aib_sample_params;
+size_t aib_sample_workspace(int B, int V);
+int aib_sample(const float* logits, int B, int V, int ld, const aib_sample_params* params, const int32_t* prior,
+               int n_prior, const int32_t* bitmask, const double* u, int64_t* out_ids, void* ws, size_t ws_bytes,
+               void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* AI_B200_H */
