@@ -118,7 +118,7 @@ AIB_DEV bool unit_has_exc(const int32_t* ec, int& ex_p, int ex_e, int& ex_col, i
     const int col = (q == ex_p) ? ex_col : ec[q];
     if (col >= c0 + 256) break;
     const uint32_t o = static_cast<uint32_t>(col - c0);
-    if (((o & 127u) >> 4) == j) return true;
+    if (col >= c0 && ((o & 127u) >> 4) == j) return true;
   }
   return false;
 }
@@ -278,7 +278,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int col = p.ec[q];
           if (col >= c0 + 256) break;
           const uint32_t o = static_cast<uint32_t>(col - c0);
-          if (((o & 127u) >> 4) == static_cast<uint32_t>(j)) sacc += p.ev[q] * xs[xperm(col)];
+          if (col >= c0 && ((o & 127u) >> 4) == static_cast<uint32_t>(j)) sacc += p.ev[q] * xs[xperm(col)];
         }
         acc.x += sacc;
       }
@@ -401,7 +401,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int col = p.ec[q];
             if (col >= c0 + 256) break;
             const uint32_t o = static_cast<uint32_t>(col - c0);
-            if (((o & 127u) >> 4) == static_cast<uint32_t>(j)) sacc += p.ev[q] * xt[xperm(col - c0)];
+            if (col >= c0 && ((o & 127u) >> 4) == static_cast<uint32_t>(j)) sacc += p.ev[q] * xt[xperm(col - c0)];
           }
 #pragma unroll
           for (int tt = 0; tt < TMAX; ++tt)

@@ -81,7 +81,8 @@ class Engine:
         self.out_ids = torch.zeros(MAXB, dtype=torch.int64, device=dev)
         self.u = torch.zeros(MAXB, dtype=torch.float64, device=dev)
         self.prior = torch.full((1, sampler.PMAX), -1, dtype=torch.int32, device=dev)
-        self.ws = torch.zeros(_lib.lib().aib_attn_workspace(H, KV, HD, maxt, MAXB), dtype=torch.uint8, device=dev)
+        wsz = max(_lib.lib().aib_attn_workspace(H, KV, HD, maxt, t) for t in range(1, MAXB + 1))
+        self.ws = torch.zeros(wsz, dtype=torch.uint8, device=dev)
         self.use_graphs = graphs
         self.graphs = {}
         self.ctx = []

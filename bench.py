@@ -1,0 +1,286 @@
+"""Benchmark: Qwen3-8B 12-bit decode tokens/s at batch 1 (BASELINE.json `metric`, `configs[2]`).
+
+Workload (one "step" = one decode pass of one token): random-init Qwen3-8B (N(0,0.02) bf16 matrices encoded in
+the 12-bit codec), bf16 KV cache pre-filled to 4096 positions from N(0,1), sampling top-k 20 / top-p 0.8 /
+temperature 0.6, on one B200 per rank. The 10.4 GB of weights streamed per step exceed the 126 MB L2, so no
+explicit flush is needed between steps.
+
+  value  = tokens/s with inputs resident: K CUDA-graph replays timed with CUDA events (ids / position chained
+           on the device), max over ranks, summed over ranks (N > 1 runs independent replicas, one sequence
+           per GPU: "scaling": "weak").
+  e2e    = tokens/s through the public API, Engine.generate (host u draw in, host token id out every step).
+  roofline = the dominant kernel, the codec GEMV: algorithmic bytes (12-bit planes + CSR) per launch over its
+           CUDA-event duration, for the 5 matrices of a layer + the head, against MEASURED_PEAKS.json.
+  cpu_baseline = the oracle port (numpy restatement of the reference path) on a bounded sample: one layer's
+           four codec GEMVs + attention at ctx 4096 and 1/8 of the head, scaled to a whole token.
+
+`--impl reference` times that CPU path alone (the reference's path is Python/Triton/Numba and cannot run on
+the GPU box; its CPU restatement stands in) and prints its own JSON line.
+"""
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+CTX = 4096
+SAMPLING = dict(temperature=0.6, top_k=20, top_p=0.8)
+METRIC = "decode tok/s Qwen3-8B bs1 12-bit weights"
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class Clocks:
+    """nvidia-smi sampler run during a timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index, self.rows, self.proc = index, [], None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                          "-i", str(self.index), "-lms", "100"], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([c.strip() for c in line.split(",")])
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm = [float(r[1]) for r in self.rows if len(r) > 2 and r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if len(r) > 2 and r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows if len(r) >= 9 for i in range(4) if r[5 + i] == "Active"})
+        return {"sm_mhz": float(sorted(sm)[len(sm) // 2]) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------------- CPU baseline
+def cpu_baseline():
+    """Oracle port of one decode token on the host, from a bounded sample (seconds of CPU work)."""
+    import numpy as np
+    from ai_b200.model import CONFIGS
+    from oracle import codec, gemv, attn
+    cfg = CONFIGS["qwen3-8b"]
+    rng = np.random.default_rng(0)
+    P = cfg.layer_params()
+    mats = {n: codec.compress(codec.f32_to_bf16_bits((rng.standard_normal(P[n]) * 0.02).astype(np.float32)))
+            for n in ("qkv", "o", "gu", "down")}
+    ln = codec.f32_to_bf16_bits(np.ones(cfg.D, np.float32))
+    hn = codec.f32_to_bf16_bits(np.ones(cfg.HD, np.float32))
+    kc = codec.f32_to_bf16_bits(rng.standard_normal((cfg.KV, CTX + 1, cfg.HD)).astype(np.float32))
+    vc = codec.f32_to_bf16_bits(rng.standard_normal((cfg.KV, CTX + 1, cfg.HD)).astype(np.float32))
+    head_rows = cfg.V // 8
+    head = codec.compress(codec.f32_to_bf16_bits((rng.standard_normal((head_rows, cfg.D)) * 0.02).astype(np.float32)))
+    inv = attn.rope_inv(cfg.HD, cfg.theta)
+    x = rng.standard_normal(cfg.D).astype(np.float32)
+    t0 = time.perf_counter()
+    qkv = gemv.gemvc1(x, mats["qkv"], np.zeros(P["qkv"][0], np.float32), 0, ln, cfg.eps)
+    a = attn.rope_attn(qkv, hn, hn, inv, CTX, kc, vc, cfg.H, cfg.KV, cfg.HD, cfg.eps)
+    x = gemv.gemvc1(a, mats["o"], x, 1)
+    gu = gemv.gemvc1(x, mats["gu"], np.zeros(P["gu"][0], np.float32), 0, ln, cfg.eps)
+    x = gemv.gemvc1(gu, mats["down"], x, 2)
+    t1 = time.perf_counter()
+    gemv.gemvc1(x, head, np.zeros(head_rows, np.float32), 0, ln, cfg.eps)
+    t2 = time.perf_counter()
+    sec = (t1 - t0) * cfg.L + (t2 - t1) * 8
+    return {"value": 1.0 / sec, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"1 of {cfg.L} layers (4 codec GEMVs + attention at ctx {CTX}) and 1/8 of the head, numpy "
+                      f"oracle port (decode on the fly, float64 matvec), scaled to one token; "
+                      f"measured {t2 - t0:.1f} s"}
+
+
+# ------------------------------------------------------------------------------------ GPU arm
+def gemv_roofline(eng, peak, reps=20):
+    """Codec GEMV kernels timed alone (CUDA events on the launching stream), in decode order, on layer 0
+    and the head: achieved = algorithmic bytes / average launch duration."""
+    import torch
+    from ai_b200 import wcomp
+    W, s = eng.W[0], eng.small[0]
+    launches = [(W["qkv"], eng.xb[0], eng.qkvb[0], 0, s["ln1"]), (W["o"], eng.attb[0], eng.xb[1], 1, None),
+                (W["gu"], eng.xb[0], eng.gub[0], 0, s["ln2"]), (W["down"], eng.gub[0], eng.xb[1], 2, None),
+                (eng.head, eng.xb[0], eng.logits[0], 0, eng.norm)]
+    eng.xb[:2].normal_()
+    eng.attb[0].normal_()
+    eng.gub[0].normal_()
+    total_bytes = sum(c.nbytes for c, *_ in launches)
+    st = torch.cuda.current_stream()
+    for _ in range(3):
+        for c, x, y, m, lnw in launches:
+            wcomp.gemvc1(x, c, y, m, lnw=lnw, eps=eng.eps)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(reps):
+        for c, x, y, m, lnw in launches:
+            wcomp.gemvc1(x, c, y, m, lnw=lnw, eps=eng.eps)
+    e1.record(st)
+    torch.cuda.synchronize()
+    sec = e0.elapsed_time(e1) / 1e3 / reps
+    achieved = total_bytes / sec / 1e9
+    traffic = None
+    tp = os.path.join(ROOT, "profiles", "gemv_traffic.json")
+    if os.path.exists(tp):
+        t = json.load(open(tp))
+        traffic = t.get("bytes_per_launch_scaled")
+    return {"bound": "hbm", "kernel": "aib gemv_t1 (codec GEMV, T=1)", "achieved": round(achieved, 1),
+            "peak": peak[0], "peak_kind": peak[1], "unit": "GB/s", "frac": round(achieved / peak[0], 4),
+            "traffic": traffic, "algorithmic_bytes_per_launch": total_bytes // len(launches),
+            "avg_launch_us": round(sec / len(launches) * 1e6, 2)}
+
+
+def gpu_arm(args, rank, world):
+    import torch
+    import torch.distributed as dist
+    from ai_b200 import build
+    from ai_b200.engine import Engine
+    build.build()
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+    torch.cuda.set_device(dev)
+    maxt = CTX + 2 * (args.steps + args.warmup) + 64
+    eng = Engine("qwen3-8b", maxt=maxt, seed=rank, log=None)
+    g = torch.Generator(device=dev).manual_seed(1234 + rank)
+    eng.kv[:, :, :, :CTX].normal_(generator=g)
+    torch.cuda.synchronize()
+    from ai_b200 import sampler
+    import numpy as np
+    prm = sampler.params(**SAMPLING)
+    rng = np.random.default_rng(rank)
+    eng.u.copy_(torch.from_numpy(rng.random(16)))
+    eng.ids[0] = 1
+    eng.pos.fill_(CTX)
+    for _ in range(max(args.warmup, 1)):
+        eng._run(1, prm, 1, False)
+    torch.cuda.synchronize()
+    eng.pos.fill_(CTX)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(dev.index) as ck:
+        e0.record(st)
+        for _ in range(args.steps):
+            eng._run(1, prm, 1, False)
+        e1.record(st)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms = e0.elapsed_time(e1)
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    value = world * args.steps / (ms_max / 1e3)
+    # e2e through the public API: Engine.generate, host buffers every step
+    eng.ctx = [1] * CTX
+    prompt = eng.ctx + [1]
+    stats = {}
+    with Clocks(dev.index) as ck2:
+        n = 0
+        for _ in eng.generate(prompt, max_new=args.steps + 1, seed=rank, stats=stats, **SAMPLING):
+            n += 1
+    e2e_local = stats["decode_n"] / (stats["gen_ms"] / 1e3)
+    te = torch.tensor([stats["gen_ms"]], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e = world * stats["decode_n"] / (float(te.item()) / 1e3)
+    peak = peaks()
+    roof = gemv_roofline(eng, peak) if rank == 0 else None
+    step_bytes = eng.bytes_per_token(CTX + args.steps // 2)
+    from ai_b200._lib import status
+    dev_status = status()
+    if rank != 0:
+        return None
+    launches_per_step = 1 + 5 * eng.L + 1 + 1 + 1
+    out = {
+        "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp32 activations x exact bf16 weights (12-bit codec), "
+        "bf16 KV", "data": "synthetic (random-init N(0,0.02) weights, KV pre-filled N(0,1) to 4096)",
+        "config": {"workload": "Qwen3-8B decode bs1, 12-bit weights, ctx 4096->, top-k 20 / top-p 0.8 / T 0.6",
+                   "model": "qwen3-8b", "global_batch": world, "seq_len": CTX,
+                   "parallelism": "replicas" if world > 1 else "single", "l2": "weights (10.4 GB) > L2 every step"},
+        "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 8,
+                "per_rank": round(e2e_local, 2)},
+        "roofline": roof,
+        "step_roofline": {"bytes_per_token": step_bytes, "achieved_gbs": round(step_bytes * value / world / 1e9, 1),
+                          "frac": round(step_bytes * value / world / 1e9 / peak[0], 4)},
+        "gpu_launches": launches_per_step * args.steps,
+        "clocks": ck.summary(), "clocks_e2e": ck2.summary(), "device_status": dev_status,
+    }
+    if not args.no_cpu:
+        out["cpu_baseline"] = cpu_baseline()
+    return out
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=256)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        secs = []
+        for _ in range(max(1, min(args.steps, 1))):
+            t = time.perf_counter()
+            cb = cpu_baseline()
+            secs.append(time.perf_counter() - t)
+        v = cb["value"]
+        print(json.dumps({"impl": "reference", "metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": args.gpus,
+                          "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+                          "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
+                          "config": {"workload": "Qwen3-8B decode bs1, 12-bit weights, ctx 4096 (CPU port)",
+                                     "model": "qwen3-8b", "global_batch": 1, "seq_len": CTX},
+                          "cpu_baseline": cb, "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0,
+                                                      "d2h_bytes_per_step": 0}}))
+        return
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+    try:
+        out = gpu_arm(args, rank, world)
+        if out is not None:
+            print(json.dumps(out))
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,83 @@
+"""Whole-model parity: the engine's greedy tokens equal the CPU oracle's on random-init Qwen3 models."""
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def bits(t):
+    return t.contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
+
+
+def oracle_for(cfg, rw, maxt):
+    from oracle.model import DecodeOracle
+    layers = [{k: bits(v) for k, v in rw.layer(i).items()} for i in range(cfg.L)]
+    return DecodeOracle(cfg, layers, bits(rw.embedding()), bits(rw.head()), bits(rw.final_norm()), maxt)
+
+
+@pytest.fixture(scope="module", params=["tiny", "tiny-tied", "small"])
+def pair(request, cuda_dev):
+    from ai_b200 import build
+    from ai_b200.engine import Engine
+    from ai_b200.model import CONFIGS, RandomWeights
+    build.build()
+    cfg = CONFIGS[request.param]
+    rw = RandomWeights(cfg, seed=11, norm_noise=0.1, std=0.05)
+    eng = Engine(cfg, maxt=128, weights=rw, log=None)
+    return cfg, rw, eng
+
+
+def test_greedy_generate_matches_oracle(pair):
+    cfg, rw, eng = pair
+    prompt = [int(t) for t in np.random.default_rng(1).integers(0, cfg.V, 20)]
+    toks = list(eng.generate(prompt, max_new=24))
+    o = oracle_for(cfg, rw, 128)
+    ref, lg = o.greedy(prompt, 24)
+    assert toks == ref
+    from ai_b200._lib import status
+    assert status() == 0
+
+
+def test_process_rows_match_oracle_logit_argmax(pair):
+    cfg, rw, eng = pair
+    toks = [int(t) for t in np.random.default_rng(2).integers(0, cfg.V, 9)]
+    out = eng.process(toks, 0)
+    o = oracle_for(cfg, rw, 128)
+    ref = []
+    for p, t in enumerate(toks):
+        lg = o.step(t, p)
+        ref.append(int(np.flatnonzero(lg == lg.max()).min()))
+    assert out == ref
+    # continue with a single token at position 9 through the T=1 graph
+    assert eng.process([toks[-1]], 9) == [int(np.argmax(o.step(toks[-1], 9)))]
+
+
+def test_sampling_reproducible_and_graph_equals_eager(pair):
+    cfg, rw, eng = pair
+    prompt = [3, 1, 4, 1, 5]
+    a = list(eng.generate(prompt, max_new=12, temperature=0.8, top_p=0.9, top_k=20, seed=7))
+    b = list(eng.generate(prompt, max_new=12, temperature=0.8, top_p=0.9, top_k=20, seed=7))
+    assert a == b
+    eng.use_graphs = False
+    c = list(eng.generate(prompt, max_new=12, temperature=0.8, top_p=0.9, top_k=20, seed=7))
+    eng.use_graphs = True
+    assert a == c
+
+
+def test_penalties_change_greedy_path(pair):
+    cfg, rw, eng = pair
+    prompt = [7, 7, 7, 7]
+    plain = list(eng.generate(prompt, max_new=8))
+    pen = list(eng.generate(prompt, max_new=8, repetition_penalty=50.0, presence_penalty=5.0))
+    assert 7 not in pen[:1] or pen != plain
+
+
+def test_process_errors_like_reference(pair):
+    cfg, rw, eng = pair
+    with pytest.raises(ValueError):
+        eng.process([], 0)
+    with pytest.raises(ValueError):
+        eng.process([cfg.V], 0)
+    with pytest.raises(ValueError):
+        eng.process([1], 10 ** 6)

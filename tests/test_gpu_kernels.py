@@ -1,0 +1,344 @@
+"""Parity of every CUDA kernel of the decode path against the CPU oracle and the reference goldens.
+
+Tolerances: integer/byte work (codec encode/decode, K/V bf16 rounding, sampler ids) is bit-exact.
+Floating-point outputs are compared with the fp32-accumulation bound |y - ref| <= RTOL * (|W| |x|) + ATOL,
+RTOL = 2e-5 (far inside the rel-err 1e-2 that the path's spec allows for bf16 weights with fp32 accumulate).
+"""
+import numpy as np
+import pytest
+import torch
+
+from conftest import golden, cases, cdict
+from oracle import codec, gemv as ogemv, attn as oattn, sampler as osamp
+
+pytestmark = pytest.mark.gpu
+RTOL, ATOL = 2e-5, 1e-6
+
+
+@pytest.fixture(scope="module")
+def lib(cuda_dev):
+    from ai_b200 import build, _lib
+    build.build()
+    return _lib.lib()
+
+
+def bits(t):
+    return t.contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
+
+
+def from_bits(a, dev="cuda"):
+    return torch.from_numpy(np.ascontiguousarray(a).view(np.int16)).view(torch.bfloat16).to(dev)
+
+
+def close(y, ref, mag, rtol=RTOL, atol=ATOL):
+    y = np.asarray(y, np.float64)
+    ref = np.asarray(ref, np.float64)
+    bad = np.abs(y - ref) > rtol * np.asarray(mag, np.float64) + atol
+    assert not bad.any(), f"{bad.sum()} mismatches, max |d| {np.abs(y - ref).max():.3e}"
+
+
+def status_clear():
+    from ai_b200 import _lib
+    return _lib.status(clear=True)
+
+
+# ------------------------------------------------------------------------------------------- codec
+@pytest.mark.parametrize("name", cases(golden("codec")))
+def test_device_encoder_bit_exact(lib, name):
+    from ai_b200 import wcomp
+    z = golden("codec")
+    c = wcomp.compress(from_bits(z[f"{name}/w"]))
+    ref = cdict(z, f"{name}/")
+    assert c["base"] == ref["base"]
+    for k in ("m8", "e4", "rp", "er", "ec"):
+        np.testing.assert_array_equal(c[k].cpu().numpy(), ref[k], err_msg=k)
+    np.testing.assert_array_equal(c["ev"].cpu().numpy().view(np.uint32), ref["ev"].view(np.uint32))
+
+
+def test_device_encoder_large_matrix_matches_oracle(lib):
+    from ai_b200 import wcomp
+    g = torch.Generator(device="cuda").manual_seed(1)
+    w = (torch.randn(6144, 4096, generator=g, device="cuda") * 0.02).bfloat16()
+    w[17, 100] = 3e4
+    c = wcomp.compress(w)
+    o = codec.compress(bits(w))
+    assert c["base"] == o["base"] and c["ev"].numel() == len(o["ev"])
+    for k in ("m8", "e4", "rp", "er", "ec"):
+        assert np.array_equal(c[k].cpu().numpy(), o[k]), k
+    # decode round trip, bf16 and fp32 rows
+    assert torch.equal(wcomp.decompress(c).view(torch.int16), w.view(torch.int16))
+    assert torch.equal(wcomp.weight_rows(c, 10, 30), w[10:30].float())
+
+
+@pytest.mark.parametrize("name", cases(golden("codec")))
+def test_decode_roundtrip_golden(lib, name):
+    from ai_b200 import wcomp
+    z = golden("codec")
+    w = from_bits(z[f"{name}/w"])
+    c = wcomp.compress(w)
+    d = bits(wcomp.decompress(c))
+    f = codec.bf16_bits_to_f32(z[f"{name}/w"])
+    nan = np.isnan(f)
+    np.testing.assert_array_equal(d[~nan], z[f"{name}/w"][~nan])
+
+
+def test_weight_rows_matches_reference_decode_rows(lib):
+    from ai_b200 import wcomp
+    z = golden("prefill")
+    c = wcomp.compress(from_bits(z["rows/w"]))
+    out = wcomp.weight_rows(c, int(z["rows/first"]), int(z["rows/last"])).cpu().numpy()
+    np.testing.assert_array_equal(out.view(np.uint32), z["rows/out"].view(np.uint32))
+
+
+# -------------------------------------------------------------------------------------------- gemv
+@pytest.mark.parametrize("name", cases(golden("gemv")))
+def test_gemvc1_matches_reference_golden(lib, name):
+    from ai_b200 import wcomp
+    z = golden("gemv")
+    c = wcomp.compress(from_bits(z[f"{name}/w"]))
+    x = torch.from_numpy(z[f"{name}/x"]).cuda()
+    y = torch.from_numpy(z[f"{name}/y0"]).cuda()
+    lnw = from_bits(z[f"{name}/lnw"]) if f"{name}/lnw" in z.files else None
+    mode = int(z[f"{name}/mode"])
+    wcomp.gemvc1(x, c, y, mode, lnw=lnw, eps=1e-6)
+    W = np.abs(codec.bf16_bits_to_f32(z[f"{name}/w"])).astype(np.float64)
+    xe = np.abs(ogemv.xin(z[f"{name}/x"], c["K"], mode, z.get(f"{name}/lnw") if lnw is not None else None))
+    close(y.cpu().numpy(), z[f"{name}/y"], W @ xe + np.abs(z[f"{name}/y0"]) * (mode > 0), rtol=4e-5)
+    assert status_clear() == 0
+
+
+GEMV_SHAPES = [(6144, 4096, 0, True), (4096, 4096, 1, False), (24576, 4096, 0, True), (4096, 12288, 2, False),
+               (1024, 2048, 1, False), (4096, 1024, 0, True), (517, 768, 2, False), (40, 256, 0, True)]
+
+
+@pytest.mark.parametrize("N,K,mode,rms", GEMV_SHAPES)
+def test_gemvc1_shapes_vs_oracle(lib, N, K, mode, rms):
+    from ai_b200 import wcomp
+    g = torch.Generator(device="cuda").manual_seed(N + K + mode)
+    w = (torch.randn(N, K, generator=g, device="cuda") * 0.02).bfloat16()
+    idx = torch.randint(0, N * K, (37,), generator=g, device="cuda")
+    w.view(-1)[idx] = (torch.randn(37, generator=g, device="cuda") * 1e4).bfloat16()  # exceptions
+    c = wcomp.compress(w)
+    assert c["ev"].numel() >= 30
+    xin = 2 * K if mode == 2 else K
+    x = torch.randn(xin, generator=g, device="cuda") * (2.0 if rms else 1.0)
+    y0 = torch.randn(N, generator=g, device="cuda")
+    lnw = (1 + 0.1 * torch.randn(K, generator=g, device="cuda")).bfloat16() if rms else None
+    y = y0.clone()
+    wcomp.gemvc1(x, c, y, mode, lnw=lnw, eps=1e-6)
+    oc = codec.compress(bits(w))
+    ref = ogemv.gemvc1(x.cpu().numpy(), oc, y0.cpu().numpy(), mode, bits(lnw) if rms else None, 1e-6)
+    xe = ogemv.xin(x.cpu().numpy(), K, mode, bits(lnw) if rms else None, 1e-6)
+    mag = np.abs(codec.dense_f32(oc)).astype(np.float64) @ np.abs(xe) + np.abs(y0.cpu().numpy()) * (mode > 0)
+    close(y.cpu().numpy(), ref, mag)
+    assert status_clear() == 0
+
+
+@pytest.mark.parametrize("T", [2, 3, 8, 16])
+@pytest.mark.parametrize("mode", [0, 1, 2])
+def test_gemvc_tc_vs_oracle(lib, T, mode):
+    from ai_b200 import wcomp
+    N, K = 1000, 1536
+    g = torch.Generator(device="cuda").manual_seed(T * 10 + mode)
+    w = (torch.randn(N, K, generator=g, device="cuda") * 0.02).bfloat16()
+    w[5, 7] = 1e5
+    w[999, 1535] = -3e-20
+    c = wcomp.compress(w)
+    xs = 2 * K if mode == 2 else K
+    X = torch.randn(16, xs, generator=g, device="cuda")
+    Y0 = torch.randn(16, N, generator=g, device="cuda")
+    Y = Y0.clone()
+    wcomp.gemvc_tc(X, c, Y, mode, T)
+    oc = codec.compress(bits(w))
+    ref = ogemv.gemvc_tc(X.cpu().numpy(), oc, Y0.cpu().numpy(), mode, T)
+    xe = np.abs(ogemv.xin(X.cpu().numpy()[:T], K, mode))
+    mag = np.zeros((16, N))
+    mag[:T] = xe @ np.abs(codec.dense_f32(oc)).T.astype(np.float64) + np.abs(Y0.cpu().numpy()[:T]) * (mode > 0)
+    close(Y.cpu().numpy(), ref, mag)
+    assert torch.equal(Y[T:], Y0[T:])  # rows >= T untouched
+
+
+def test_gemv_deterministic(lib):
+    from ai_b200 import wcomp
+    g = torch.Generator(device="cuda").manual_seed(9)
+    c = wcomp.compress((torch.randn(4096, 4096, generator=g, device="cuda") * 0.02).bfloat16())
+    x = torch.randn(4096, generator=g, device="cuda")
+    outs = []
+    for _ in range(3):
+        y = torch.zeros(4096, device="cuda")
+        wcomp.gemvc1(x, c, y, 0)
+        outs.append(y)
+    assert torch.equal(outs[0], outs[1]) and torch.equal(outs[0], outs[2])
+
+
+# ----------------------------------------------------------------------------------- norm / embed
+def test_rmsnorm_vs_golden(lib):
+    from ai_b200 import tkernels
+    z = golden("attn")
+    x = torch.from_numpy(z["rms/x"]).cuda()
+    out = torch.zeros_like(x)
+    tkernels.rmsg(x, from_bits(z["rms/w"]), out, 1e-6)
+    np.testing.assert_allclose(out.cpu().numpy(), z["rms/out"], rtol=2e-6, atol=2e-6)
+
+
+def test_embed(lib):
+    from ai_b200 import tkernels
+    emb = torch.randn(300, 96, device="cuda").bfloat16()
+    ids = torch.tensor([0, 299, 17], device="cuda")
+    out = torch.zeros(3, 96, device="cuda")
+    tkernels.embed(emb, ids, out)
+    assert torch.equal(out, emb[ids].float())
+    bad = torch.tensor([300], device="cuda")
+    tkernels.embed(emb, bad, out[:1])
+    from ai_b200._lib import status
+    assert status(clear=True) == 103  # AIB_DEV_BAD_TOKEN, no fault
+
+
+# -------------------------------------------------------------------------------------- attention
+def _attn_case(H, KV, HD, maxt, pos, seed):
+    g = np.random.default_rng(seed)
+    qkv = (g.standard_normal((H + 2 * KV) * HD) * 2).astype(np.float32)
+    qn = codec.f32_to_bf16_bits((1 + 0.1 * g.standard_normal(HD)).astype(np.float32))
+    kn = codec.f32_to_bf16_bits((1 + 0.1 * g.standard_normal(HD)).astype(np.float32))
+    kc = codec.f32_to_bf16_bits(g.standard_normal((KV, maxt, HD)).astype(np.float32))
+    vc = codec.f32_to_bf16_bits(g.standard_normal((KV, maxt, HD)).astype(np.float32))
+    return qkv, qn, kn, kc, vc
+
+
+@pytest.mark.parametrize("H,KV,HD,pos", [(8, 2, 64, 0), (8, 2, 64, 77), (32, 8, 128, 1), (32, 8, 128, 4100),
+                                         (16, 8, 128, 300), (64, 8, 128, 2047)])
+def test_rope_attn_vs_oracle(lib, H, KV, HD, pos):
+    from ai_b200 import tkernels
+    maxt = max(128, pos + 1)
+    qkv, qn, kn, kc, vc = _attn_case(H, KV, HD, maxt, pos, pos + H)
+    inv = oattn.rope_inv(HD, 1e6)
+    kc_ref, vc_ref = kc.copy(), vc.copy()
+    ref = oattn.rope_attn(qkv, qn, kn, inv, pos, kc_ref, vc_ref, H, KV, HD, 1e-6)
+    KC, VC = from_bits(kc), from_bits(vc)
+    out = torch.zeros(H * HD, device="cuda")
+    P = torch.tensor([pos], dtype=torch.int64, device="cuda")
+    tkernels.rope_attn(torch.from_numpy(qkv).cuda(), from_bits(qn), from_bits(kn), torch.from_numpy(inv).cuda(), P,
+                       KC, VC, out, maxt, 1e-6, HD ** -0.5, H, KV, HD)
+    np.testing.assert_allclose(out.cpu().numpy(), ref, rtol=2e-4, atol=2e-5)
+    # cache rows: written row at pos matches RNE rounding (<= 1 bf16 ulp where fp32 sums differ), rest untouched
+    dk = np.abs(bits(KC).astype(np.int32) - kc_ref.astype(np.int32))
+    assert dk.max() <= 1 and (dk > 0).sum() <= 4
+    np.testing.assert_array_equal(bits(VC), vc_ref)
+    assert status_clear() == 0
+
+
+def test_rope_attn_matches_reference_golden_semantics(lib):
+    """Golden cases of rope_attn_k: same inputs; the GPU rounds K/V to nearest-even where the interpreter
+    truncated, so the check is against the oracle pinned to those goldens, in RNE mode."""
+    from ai_b200 import tkernels
+    z = golden("attn")
+    H, KV, HD, maxt = (int(v) for v in z["cfg"])
+    for name in cases(z):
+        pos = int(z[f"{name}/pos"])
+        kc_ref, vc_ref = z[f"{name}/kc0"].copy(), z[f"{name}/vc0"].copy()
+        ref = oattn.rope_attn(z[f"{name}/qkv"], z[f"{name}/qn"], z[f"{name}/kn"], z["inv"], pos, kc_ref, vc_ref, H, KV,
+                              HD, 1e-6)
+        KC, VC = from_bits(z[f"{name}/kc0"]), from_bits(z[f"{name}/vc0"])
+        out = torch.zeros(H * HD, device="cuda")
+        tkernels.rope_attn(torch.from_numpy(z[f"{name}/qkv"]).cuda(), from_bits(z[f"{name}/qn"]),
+                           from_bits(z[f"{name}/kn"]), torch.from_numpy(z["inv"]).cuda(),
+                           torch.tensor([pos], device="cuda"), KC, VC, out, maxt, 1e-6, HD ** -0.5, H, KV, HD)
+        np.testing.assert_allclose(out.cpu().numpy(), ref, rtol=2e-4, atol=2e-5)
+        # and within bf16-rounding distance of the reference's own output
+        np.testing.assert_allclose(out.cpu().numpy(), z[f"{name}/out"], rtol=2e-2, atol=2e-2)
+
+
+@pytest.mark.parametrize("T,pos", [(2, 0), (5, 40), (16, 1000)])
+def test_batched_attention_vs_oracle(lib, T, pos):
+    from ai_b200 import tkernels
+    H, KV, HD = 32, 8, 128
+    maxt = pos + T + 8
+    g = np.random.default_rng(T)
+    qkv = (g.standard_normal((T, (H + 2 * KV) * HD))).astype(np.float32)
+    _, qn, kn, kc, vc = _attn_case(H, KV, HD, maxt, pos, T + 5)
+    inv = oattn.rope_inv(HD, 1e6)
+    kc_ref, vc_ref = kc.copy(), vc.copy()
+    Qr = oattn.qk_rope_cache(qkv, qn, kn, inv, pos, kc_ref, vc_ref, H, KV, HD, 1e-6)
+    KC, VC = from_bits(kc), from_bits(vc)
+    q = torch.zeros(T, H * HD, device="cuda")
+    P = torch.tensor([pos], dtype=torch.int64, device="cuda")
+    tkernels.qk_rope_cache(torch.from_numpy(qkv).cuda(), from_bits(qn), from_bits(kn), torch.from_numpy(inv).cuda(),
+                           P, q, KC, VC, maxt, 1e-6, H, KV, HD, T)
+    np.testing.assert_allclose(q.cpu().numpy(), Qr, rtol=1e-5, atol=1e-5)
+    dk = np.abs(bits(KC).astype(np.int32) - kc_ref.astype(np.int32))
+    assert dk.max() <= 1
+    np.testing.assert_array_equal(bits(VC), vc_ref)
+    out = torch.zeros(T, H * HD, device="cuda")
+    tkernels.attn(q, KC, VC, P, out, maxt, HD ** -0.5, H, KV, HD, T)
+    ref = oattn.attn(q.cpu().numpy(), bits(KC), bits(VC), pos, H, KV, HD)
+    np.testing.assert_allclose(out.cpu().numpy(), ref, rtol=2e-4, atol=2e-5)
+    assert status_clear() == 0
+
+
+# ---------------------------------------------------------------------------------------- sampler
+@pytest.mark.parametrize("name", cases(golden("sampler")))
+def test_sampler_matches_reference_pick(lib, name):
+    from ai_b200 import sampler
+    z = golden("sampler")
+    lg = torch.from_numpy(z[f"{name}/logits"]).cuda()
+    mask = torch.from_numpy(z[f"{name}/mask"]).cuda() if f"{name}/mask" in z.files else None
+    ids = sampler.sample(lg, float(z[f"{name}/temp"]), float(z[f"{name}/top_p"]), 0, z[f"{name}/u"], mask=mask)
+    np.testing.assert_array_equal(ids, z[f"{name}/ids"])
+
+
+@pytest.mark.parametrize("name", cases(golden("sampler"), "head_names"))
+def test_sampler_matches_reference_head_pick(lib, name):
+    from ai_b200 import sampler
+    from oracle import head as ohead
+    z = golden("sampler")
+    ex = ohead.exact_logits(z[f"{name}/w"], z[f"{name}/h"])
+    ids = sampler.sample(torch.from_numpy(ex).cuda(), float(z[f"{name}/temp"]), float(z[f"{name}/top_p"]), 0,
+                         [float(z[f"{name}/u"])])
+    assert ids[0] == int(z[f"{name}/ids"][0])
+
+
+SAMPLER_CASES = [  # (V, T, top_k, top_p, rep, pres, freq, masked)
+    (151936, 0.7, 20, 0.8, 1.05, 0.0, 0.0, False),  # BASELINE config 1 sampler settings
+    (151936, 0.7, 50, 0.95, 1.1, 0.5, 0.3, True),   # config 4 sweep settings
+    (151936, 0.7, 1, 0.8, 1.1, 0.5, 0.3, False),
+    (151936, 0.6, 20, 0.8, 1.0, 0.0, 0.0, False),   # config 3 decode settings
+    (151936, 0.0, 0, 1.0, 1.3, 0.2, 0.1, True),
+    (151936, 0.7, 0, 0.8, 1.0, 0.0, 0.0, False),    # top-p over the whole vocabulary
+    (5000, 1.5, 0, 1.0, 1.0, 0.0, 0.0, False),
+    (5000, 0.9, 0, 0.9, 2.0, 1.0, 1.0, True),
+]
+
+
+@pytest.mark.parametrize("case", SAMPLER_CASES)
+def test_sampler_extended_vs_oracle(lib, case):
+    from ai_b200 import sampler
+    V, T, k, p, rep, pres, freq, masked = case
+    B = 4
+    rng = np.random.default_rng(V + k)
+    scale = 2.0 if V > 10000 else 3.0
+    lg = (rng.standard_normal((B, V)) * scale).astype(np.float32)
+    prior = rng.integers(0, V, (B, 1024)).astype(np.int32)
+    prior[:, :64] = prior[:, 64:128]  # repeated ids -> counts > 1
+    prior[0, 5] = -1
+    words = (V + 31) // 32
+    mask = None
+    if masked:
+        mask = (rng.random((B, words * 32)) < 0.1).reshape(B, words, 32)
+        mask = (mask * (1 << np.arange(32, dtype=np.uint64))).sum(-1).astype(np.uint32).view(np.int32)
+        mask[:, 0] |= 1  # token 0 always allowed
+    us = [np.random.default_rng(b).random() for b in range(B)]
+    ids = sampler.sample(torch.from_numpy(lg).cuda(), T, p, k, us, prior=torch.from_numpy(prior).cuda(),
+                         mask=torch.from_numpy(mask).cuda() if mask is not None else None, repetition_penalty=rep,
+                         presence_penalty=pres, frequency_penalty=freq)
+    ref = [osamp.sample_row(lg[b], T, k, p, rep, pres, freq, prior[b], mask[b] if mask is not None else None, us[b])
+           for b in range(B)]
+    assert ids == ref
+    assert status_clear() == 0
+
+
+def test_sampler_many_rows_and_greedy_ties(lib):
+    from ai_b200 import sampler
+    lg = torch.zeros(64, 1000, device="cuda")
+    lg[:, 17] = 1.0
+    lg[:, 400] = 1.0
+    assert sampler.sample(lg) == [17] * 64
