@@ -107,14 +107,13 @@ __global__ void hist_kernel(const uint16_t* __restrict__ w, size_t n, unsigned l
 // Pass 1b: base = first argmax of the 15-wide window sums.
 __global__ void base_kernel(const unsigned long long* __restrict__ gcnt, int32_t* base_out) {
   if (threadIdx.x != 0) return;
-  unsigned long long cs[257];
-  cs[0] = 0;
-  for (int i = 0; i < 256; ++i) cs[i + 1] = cs[i] + gcnt[i];
+  unsigned long long s = 0;  // sliding window sum over [b, b+14]
+  for (int i = 0; i < 15; ++i) s += gcnt[i];
   int base = 0;
-  unsigned long long best = 0;
-  for (int b = 0; b + 15 <= 256; ++b) {
-    const unsigned long long s = cs[b + 15] - cs[b];
-    if (b == 0 || s > best) best = s, base = b;
+  unsigned long long best = s;
+  for (int b = 1; b + 15 <= 256; ++b) {
+    s += gcnt[b + 14] - gcnt[b - 1];
+    if (s > best) best = s, base = b;
   }
   *base_out = base;
 }

@@ -126,16 +126,30 @@ int launch_check(const char* what);  // maps cudaGetLastError to AIB_ECUDA
 int make_map_3d_u8(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t s1_bytes,
                    uint64_t s2_bytes, uint32_t b0, uint32_t b1, uint32_t b2);
 
-// Raise a kernel's dynamic shared-memory limit to the sm_100 maximum, once per (kernel, device).
-bool smem_raised(const void* kernel, int device);  // records the pair; true if it was already recorded
+// Raise a kernel's dynamic shared-memory limit to the sm_100 per-block maximum (232448 bytes, static +
+// dynamic), once per (kernel, device). A failure is reported and clears the runtime's sticky error.
+bool smem_raised(const void* kernel, int device, bool record);  // true if already recorded
 template <typename K>
 int allow_smem(K kernel, size_t bytes) {
+  constexpr size_t kMaxBlock = 232448;
   int dev = 0;
   cudaGetDevice(&dev);
-  if (bytes > 227 * 1024) return fail(AIB_ENOTSUP, "kernel needs %zu bytes of shared memory", bytes);
-  if (smem_raised(reinterpret_cast<const void*>(kernel), dev)) return AIB_OK;
-  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-  if (e != cudaSuccess) return fail(AIB_ECUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+  cudaFuncAttributes fa;
+  cudaError_t e = cudaFuncGetAttributes(&fa, kernel);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return fail(AIB_ECUDA, "cudaFuncGetAttributes: %s", cudaGetErrorString(e));
+  }
+  if (bytes + fa.sharedSizeBytes > kMaxBlock)
+    return fail(AIB_ENOTSUP, "kernel needs %zu + %zu bytes of shared memory", bytes, (size_t)fa.sharedSizeBytes);
+  if (smem_raised(reinterpret_cast<const void*>(kernel), dev, false)) return AIB_OK;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(kMaxBlock - fa.sharedSizeBytes));
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return fail(AIB_ECUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+  }
+  smem_raised(reinterpret_cast<const void*>(kernel), dev, true);
   return AIB_OK;
 }
 

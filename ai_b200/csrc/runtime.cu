@@ -33,11 +33,12 @@ int sm_count(int device) {
   return cache[device];
 }
 
-bool smem_raised(const void* kernel, int device) {
+bool smem_raised(const void* kernel, int device, bool record) {
   static std::mutex mu;
   static std::set<std::pair<const void*, int>> seen;
   std::lock_guard<std::mutex> lock(mu);
-  return !seen.insert({kernel, device}).second;
+  if (record) seen.insert({kernel, device});
+  return seen.count({kernel, device}) != 0;
 }
 
 int launch_check(const char* what) {

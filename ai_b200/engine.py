@@ -39,8 +39,11 @@ class Engine:
         if not isinstance(maxt, int) or isinstance(maxt, bool) or maxt < 1:
             raise ValueError("maxt must be a positive integer")
         t0 = time.time()
-        self.device = torch.device(device)
-        torch.cuda.set_device(self.device)
+        dev = torch.device(device)
+        if dev.index is None:
+            dev = torch.device("cuda", torch.cuda.current_device())
+        self.device = dev
+        torch.cuda.set_device(dev)
         if weights is not None:
             src = weights
             cfg = weights.cfg if hasattr(weights, "cfg") else weights.config
