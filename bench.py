@@ -241,8 +241,40 @@ def gpu_arm(args, rank, world):
     return out
 
 
+def micro(args):
+    """One kernel alone on a small case (for ncu captures and quick A/B timing): the codec GEMV on a Qwen3-8B
+    gu-shaped matrix [24576, 4096] (151 MB of planes, > L2), T = 1 with the RMS prologue."""
+    import torch
+    from ai_b200 import build, wcomp
+    build.build()
+    torch.cuda.set_device(0)
+    g = torch.Generator(device="cuda").manual_seed(0)
+    N, K = (24576, 4096) if args.micro == "gemv" else (4096, 12288)
+    c = wcomp.compress((torch.randn(N, K, generator=g, device="cuda") * 0.02).bfloat16())
+    x = torch.randn(K * 2, generator=g, device="cuda")
+    y = torch.zeros(N, device="cuda")
+    lnw = torch.ones(K, dtype=torch.bfloat16, device="cuda")
+    mode = 0 if args.micro == "gemv" else 2
+    run = lambda: wcomp.gemvc1(x, c, y, mode, lnw=lnw if mode == 0 else None)  # noqa: E731
+    for _ in range(3):
+        run()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = max(args.steps, 1)
+    e0.record()
+    for _ in range(reps):
+        run()
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / reps
+    print(json.dumps({"micro": args.micro, "N": N, "K": K, "bytes": c.nbytes, "us_per_launch": round(us, 2),
+                      "GBps": round(c.nbytes / us / 1e3, 1)}))
+
+
 def main():
     ap = argparse.ArgumentParser()
+    ap.add_argument("--micro", choices=["gemv", "gemv_down"], default=None,
+                    help="time one kernel alone on a small case (for ncu) instead of the decode benchmark")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=256)
     ap.add_argument("--warmup", type=int, default=8)
@@ -251,6 +283,8 @@ def main():
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
+    if args.micro:
+        return micro(args)
     if args.impl == "reference":
         if rank != 0:
             return
