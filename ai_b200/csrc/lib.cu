@@ -5,4 +5,5 @@
 #include "gemv.cu"
 #include "norm.cu"
 #include "attn.cu"
+#include "attn_noalloc.cu"
 #include "sampler.cu"

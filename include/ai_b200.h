@@ -116,6 +116,15 @@ size_t aib_attn_workspace(int H, int KV, int HD, int maxt, int T);
 int aib_rope_attn_decode(const float* qkv, const uint16_t* qn, const uint16_t* kn, const float* inv,
                          const int64_t* pos, uint16_t* kc, uint16_t* vc, float* out, int H, int KV, int HD,
                          int maxt, float eps, float scale, void* ws, size_t ws_bytes, void* stream);
+/* Same step as aib_rope_attn_decode for callers that cannot allocate device memory once running (an
+ * embedding application that budgets all device memory itself, or a serving loop that must never enter
+ * cudaMalloc). No counterpart in the reference. Its scratch is a fixed 2 MiB array inside the library,
+ * held by every GPU that loads it; calls needing more are rejected with AIB_EINVAL. The first call on a
+ * device looks the array up (cudaGetSymbolAddress) and should come before any stream capture. All calls
+ * share the array: calls that overlap on the GPU race, so serialise them. */
+int aib_rope_attn_decode_noalloc(const float* qkv, const uint16_t* qn, const uint16_t* kn, const float* inv,
+                                 const int64_t* pos, uint16_t* kc, uint16_t* vc, float* out, int H, int KV, int HD,
+                                 int maxt, float eps, float scale, void* stream);
 /* Batched prologue (replaces qk_rope_cache_k, tkernels.py:82-120): q of tokens t < T normed+rotated into
  * q [T, H*HD]; k, v rows written at *pos + t. */
 int aib_qk_rope_cache(const float* qkv, const uint16_t* qn, const uint16_t* kn, const float* inv, const int64_t* pos,
