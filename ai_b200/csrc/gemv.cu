@@ -90,6 +90,32 @@ AIB_DEV void unit_fast(const uint4& ml, const uint4& mh, const uint4& ee, const 
   }
 }
 
+// Same decode, accumulated with scalar FMAs into four independent chains (shorter dependency chains and no
+// register-pair packing; the four partial sums are added at the end of the row).
+AIB_DEV void unit_fast4(const uint4& ml, const uint4& mh, const uint4& ee, const float4* xl, const float4* xh,
+                        uint32_t base7, float4& a) {
+  const uint32_t E[4] = {ee.x, ee.y, ee.z, ee.w};
+  const uint32_t L[4] = {ml.x, ml.y, ml.z, ml.w};
+  const uint32_t Hh[4] = {mh.x, mh.y, mh.z, mh.w};
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const uint32_t x01 = prmt(E[q], 0u, 0x4140u);
+    const uint32_t x23 = prmt(E[q], 0u, 0x4342u);
+    const uint32_t zlo01 = (prmt(L[q], 0u, 0x9180u) & 0x807F807Fu) | (((x01 & 0x000F000Fu) << 7) + base7);
+    const uint32_t zlo23 = (prmt(L[q], 0u, 0xB3A2u) & 0x807F807Fu) | (((x23 & 0x000F000Fu) << 7) + base7);
+    const uint32_t zhi01 = (prmt(Hh[q], 0u, 0x9180u) & 0x807F807Fu) | (((x01 & 0x00F000F0u) << 3) + base7);
+    const uint32_t zhi23 = (prmt(Hh[q], 0u, 0xB3A2u) & 0x807F807Fu) | (((x23 & 0x00F000F0u) << 3) + base7);
+    a.x = fmaf(__uint_as_float(zlo01 << 16), xl[q].x, a.x);
+    a.y = fmaf(__uint_as_float(zlo01 & 0xFFFF0000u), xl[q].y, a.y);
+    a.z = fmaf(__uint_as_float(zlo23 << 16), xl[q].z, a.z);
+    a.w = fmaf(__uint_as_float(zlo23 & 0xFFFF0000u), xl[q].w, a.w);
+    a.x = fmaf(__uint_as_float(zhi01 << 16), xh[q].x, a.x);
+    a.y = fmaf(__uint_as_float(zhi01 & 0xFFFF0000u), xh[q].y, a.y);
+    a.z = fmaf(__uint_as_float(zhi23 << 16), xh[q].z, a.z);
+    a.w = fmaf(__uint_as_float(zhi23 & 0xFFFF0000u), xh[q].w, a.w);
+  }
+}
+
 // Element-wise decode with code 15 -> 0 (slow path for units holding exceptions).
 AIB_DEV float dec1(uint32_t m, uint32_t code, uint32_t base) {
   if (code == 15u) return 0.0f;
@@ -172,139 +198,185 @@ AIB_DEV void init_barriers(uint64_t* full, uint64_t* empty, volatile int* abort_
 }
 
 // ------------------------------------------------------------------------------------ T = 1 kernel
+// 16 consumer warps in two groups of 8; group g consumes the CTA's tiles g, g+2, g+4, ... (the producer
+// interleaves the two groups' stages in the ring). Within a stage a warp owns whole row(s): lane = (row r,
+// chunk slot cc, unit j) with the CW chunk slots of a row in the same warp, so a row reduces with shuffles
+// and no CTA-wide barrier runs in the main loop.
+constexpr int kT1Consumers = 512;
+constexpr int kT1Threads = kT1Consumers + 32;
+
+AIB_DEV void produce_pairs(const CUtensorMap* tm8, const CUtensorMap* tme4, uint8_t* ring, uint64_t* full,
+                           uint64_t* empty, volatile int* abort_flag, int tb, int ntiles, int KS, int RT, int CW,
+                           int NS) {
+  prefetch_tensormap(tm8);
+  prefetch_tensormap(tme4);
+  const int n0 = (ntiles + 1) / 2;  // tiles of group 0 (group 1 has ntiles / 2)
+  const int n_it = 2 * n0 * KS;
+  int issued = 0;
+  for (int it = 0; it < n_it; ++it) {
+    const int g = it & 1, i = it >> 1;
+    const int lt = 2 * (i / KS) + g;  // local tile index
+    if (lt >= ntiles) continue;       // group 1 has no tile here (only at the very end)
+    const int s = it % NS;
+    if (it >= NS) {
+      bool ok = false;
+      for (uint32_t k = 0; k < kSpinLimit && !ok; ++k) {
+        ok = mbar_try_wait(&empty[s], ((it / NS) - 1) & 1);
+        if (!ok && *abort_flag) break;
+      }
+      if (!ok) {
+        if (!*abort_flag) set_status(AIB_DEV_TIMEOUT_EMPTY);
+        *abort_flag = 1;
+        break;
+      }
+    }
+    const int tile = tb + lt, ks = i % KS;
+    uint8_t* st = ring + static_cast<size_t>(s) * kStageBytes;
+    mbar_arrive_expect_tx(&full[s], kStageBytes);
+    tma_load_3d(st, tm8, &full[s], 0, ks * CW, tile * RT);
+    tma_load_3d(st + kStageM8, tme4, &full[s], 0, ks * CW, tile * RT);
+    issued = it + 1;
+  }
+  if (*abort_flag) {
+    for (int it = (issued > NS ? issued - NS : 0); it < issued; ++it) {
+      const int g = it & 1, i = it >> 1;
+      if (2 * (i / KS) + g < ntiles) mbar_wait(&full[it % NS], (it / NS) & 1, AIB_DEV_TIMEOUT_FULL);
+    }
+  }
+}
+
 template <int MODE, bool RMS>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kT1Threads, 1)
     gemv_t1_kernel(const __grid_constant__ CUtensorMap tm8, const __grid_constant__ CUtensorMap tme4, Params p) {
   extern __shared__ __align__(1024) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty = full + 16;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + 256);
-  float* red = reinterpret_cast<float*>(smem + 512);  // [2][32] chunk-slot partials + [8] RMS partials
+  float* red = reinterpret_cast<float*>(smem + 512);  // RMS partials
   float* xs = reinterpret_cast<float*>(smem + kHeader);
   uint8_t* ring = smem + kHeader + ((p.xs_floats * 4 + 1023) / 1024) * 1024;
 
   const int tid = threadIdx.x;
   const int tb = static_cast<int>((static_cast<long long>(blockIdx.x) * p.tiles) / gridDim.x);
   const int te = static_cast<int>((static_cast<long long>(blockIdx.x + 1) * p.tiles) / gridDim.x);
-  const int n_it = (te - tb) * p.KS;
+  const int ntiles = te - tb;
 
-  init_barriers(full, empty, abort_flag, p.NS);
+  if (tid == 0) {
+    for (int s = 0; s < p.NS; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 8);  // the 8 warps of the consuming group
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
   pdl_trigger();
 
-  if (tid >= kConsumers) {  // producer warp
-    if (tid == kConsumers) produce(&tm8, &tme4, ring, full, empty, abort_flag, tb, n_it, p.KS, p.RT, p.CW, p.NS);
+  if (tid >= kT1Consumers) {  // producer warp
+    if (tid == kT1Consumers)
+      produce_pairs(&tm8, &tme4, ring, full, empty, abort_flag, tb, ntiles, p.KS, p.RT, p.CW, p.NS);
     return;
   }
 
-  // -------- consumers
+  // -------- consumers: x prologue shared by both groups
   pdl_wait();  // x / y are produced / consumed by neighbouring kernels
   const int K = p.K;
   float rs = 1.0f;
   if (RMS) {
     float ss = 0.0f;
-    for (int k = tid; k < K; k += kConsumers) {
+    for (int k = tid; k < K; k += kT1Consumers) {
       const float v = p.x[k];
       ss += v * v;
     }
     ss = warp_sum(ss);
-    if ((tid & 31) == 0) red[64 + (tid >> 5)] = ss;
-    named_sync(1, kConsumers);
+    if ((tid & 31) == 0) red[tid >> 5] = ss;
+    named_sync(1, kT1Consumers);
     float tot = 0.0f;
 #pragma unroll
-    for (int w = 0; w < kConsumers / 32; ++w) tot += red[64 + w];
+    for (int w = 0; w < kT1Consumers / 32; ++w) tot += red[w];
     rs = rsqrtf(tot / static_cast<float>(K) + p.eps);
   }
-  for (int k = tid; k < K; k += kConsumers) {
+  for (int k = tid; k < K; k += kT1Consumers) {
     float v = (MODE == 2) ? silu_mul(p.x[k], p.x[K + k]) : p.x[k];
     if (RMS) v = bf16_to_f32(p.lnw[k]) * (v * rs);
     xs[xperm(k)] = v;
   }
-  named_sync(1, kConsumers);
+  named_sync(1, kT1Consumers);
 
-  const int j = tid & 7, slot = tid >> 3;
+  const int grp = tid >> 8, gt = tid & 255;  // group, thread within group
+  const int j = gt & 7, slot = gt >> 3;      // slot = r * CW + cc
   const int CW = p.CW, cc = slot % CW, r = slot / CW;
   const uint32_t base7 = (static_cast<uint32_t>(p.base) << 7) | (static_cast<uint32_t>(p.base) << 23);
-  float2 acc = make_float2(0.0f, 0.0f);
-  int row = 0, ex_p = 0, ex_e = 0, ex_col = INT_MAX, buf = 0;
+  const int my_tiles = grp == 0 ? (ntiles + 1) / 2 : ntiles / 2;
+  const int m8_off = slot * 256 + 16 * j, e4_off = kStageM8 + slot * 128 + 16 * j;
   bool aborted = false;
 
-  for (int it = 0; it < n_it; ++it) {
-    const int s = it % p.NS;
-    const int tile = tb + it / p.KS, ks = it % p.KS;
-    if (ks == 0) {
-      row = tile * p.RT + r;
-      acc = make_float2(0.0f, 0.0f);
-      ex_p = 0;
-      ex_e = 0;
-      if (row < p.N) {
-        ex_p = p.rp[row];
-        ex_e = p.rp[row + 1];
-      }
-      ex_col = ex_p < ex_e ? p.ec[ex_p] : INT_MAX;
+  for (int ti = 0; ti < my_tiles; ++ti) {
+    const int tile = tb + 2 * ti + grp;
+    const int row = tile * p.RT + r;
+    int ex_p = 0, ex_e = 0;
+    if (row < p.N) {
+      ex_p = p.rp[row];
+      ex_e = p.rp[row + 1];
     }
-    const bool ok = !aborted && wait_full(&full[s], (it / p.NS) & 1, abort_flag);
-    if (!ok) aborted = true;
-    const int gc = ks * CW + cc;
-    if (ok && row < p.N && gc < p.nch) {
-      const uint8_t* st = ring + static_cast<size_t>(s) * kStageBytes;
-      const uint8_t* m8 = st + (r * CW + cc) * 256;
-      const uint8_t* e4 = st + kStageM8 + (r * CW + cc) * 128;
-      const uint4 ml = *reinterpret_cast<const uint4*>(m8 + 16 * j);
-      const uint4 mh = *reinterpret_cast<const uint4*>(m8 + 128 + 16 * j);
-      const uint4 ee = *reinterpret_cast<const uint4*>(e4 + 16 * j);
-      const float4* xb = reinterpret_cast<const float4*>(xs) + gc * 64;  // 256 floats per chunk
-      float4 xl[4], xh[4];
+    int ex_col = ex_p < ex_e ? p.ec[ex_p] : INT_MAX;
+    float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    for (int ks = 0; ks < p.KS; ++ks) {
+      const int it = 2 * (ti * p.KS + ks) + grp;
+      const int s = it % p.NS;
+      const bool ok = !aborted && wait_full(&full[s], (it / p.NS) & 1, abort_flag);
+      if (!ok) aborted = true;
+      const int gc = ks * CW + cc;
+      if (ok && row < p.N && gc < p.nch) {
+        const uint8_t* st = ring + static_cast<size_t>(s) * kStageBytes;
+        const uint4 ml = *reinterpret_cast<const uint4*>(st + m8_off);
+        const uint4 mh = *reinterpret_cast<const uint4*>(st + m8_off + 128);
+        const uint4 ee = *reinterpret_cast<const uint4*>(st + e4_off);
+        const float4* xb = reinterpret_cast<const float4*>(xs) + gc * 64;
+        float4 xl[4], xh[4];
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        xl[q] = xb[q * 8 + j];
-        xh[q] = xb[32 + q * 8 + j];
-      }
-      const int c0 = gc * 256;
-      if (!unit_has_exc(p.ec, ex_p, ex_e, ex_col, c0, j)) {
-        unit_fast(ml, mh, ee, xl, xh, base7, acc);
-      } else {
-        const uint32_t E[4] = {ee.x, ee.y, ee.z, ee.w}, L[4] = {ml.x, ml.y, ml.z, ml.w},
-                       Hh[4] = {mh.x, mh.y, mh.z, mh.w};
-        const float* xlf = reinterpret_cast<const float*>(xl);
-        const float* xhf = reinterpret_cast<const float*>(xh);
-        float sacc = 0.0f;
-        for (int q = 0; q < 4; ++q)
-          for (int b = 0; b < 4; ++b) {
-            const uint32_t eb = (E[q] >> (8 * b)) & 0xFFu;
-            sacc += dec1((L[q] >> (8 * b)) & 0xFFu, eb & 15u, p.base) * xlf[q * 4 + b];
-            sacc += dec1((Hh[q] >> (8 * b)) & 0xFFu, eb >> 4, p.base) * xhf[q * 4 + b];
+        for (int q = 0; q < 4; ++q) {
+          xl[q] = xb[q * 8 + j];
+          xh[q] = xb[32 + q * 8 + j];
+        }
+        const int c0 = gc * 256;
+        if (!unit_has_exc(p.ec, ex_p, ex_e, ex_col, c0, j)) {
+          unit_fast4(ml, mh, ee, xl, xh, base7, acc);
+        } else {
+          const uint32_t E[4] = {ee.x, ee.y, ee.z, ee.w}, L[4] = {ml.x, ml.y, ml.z, ml.w},
+                         Hh[4] = {mh.x, mh.y, mh.z, mh.w};
+          const float* xlf = reinterpret_cast<const float*>(xl);
+          const float* xhf = reinterpret_cast<const float*>(xh);
+          float sacc = 0.0f;
+          for (int q = 0; q < 4; ++q)
+            for (int b = 0; b < 4; ++b) {
+              const uint32_t eb = (E[q] >> (8 * b)) & 0xFFu;
+              sacc += dec1((L[q] >> (8 * b)) & 0xFFu, eb & 15u, p.base) * xlf[q * 4 + b];
+              sacc += dec1((Hh[q] >> (8 * b)) & 0xFFu, eb >> 4, p.base) * xhf[q * 4 + b];
+            }
+          for (int q = ex_p; q < ex_e; ++q) {
+            const int col = p.ec[q];
+            if (col >= c0 + 256) break;
+            const uint32_t o = static_cast<uint32_t>(col - c0);
+            if (col >= c0 && ((o & 127u) >> 4) == static_cast<uint32_t>(j)) sacc += p.ev[q] * xs[xperm(col)];
           }
-        for (int q = ex_p; q < ex_e; ++q) {
-          const int col = p.ec[q];
-          if (col >= c0 + 256) break;
-          const uint32_t o = static_cast<uint32_t>(col - c0);
-          if (col >= c0 && ((o & 127u) >> 4) == static_cast<uint32_t>(j)) sacc += p.ev[q] * xs[xperm(col)];
+          acc.x += sacc;
         }
-        acc.x += sacc;
       }
+      __syncwarp();
+      if ((tid & 31) == 0) mbar_arrive(&empty[s]);
     }
-    __syncwarp();
-    if ((tid & 31) == 0) mbar_arrive(&empty[s]);
-
-    if (ks == p.KS - 1) {  // row tile complete: fixed-order reduction
-      float v = acc.x + acc.y;
-      v += __shfl_xor_sync(0xffffffffu, v, 1);
-      v += __shfl_xor_sync(0xffffffffu, v, 2);
-      v += __shfl_xor_sync(0xffffffffu, v, 4);
-      if (j == 0) red[buf * 32 + slot] = v;
-      named_sync(1, kConsumers);
-      if (tid < p.RT && !aborted) {
-        const int orow = tile * p.RT + tid;
-        if (orow < p.N) {
-          float sum = 0.0f;
-          for (int c = 0; c < CW; ++c) sum += red[buf * 32 + tid * CW + c];
-          if (MODE == 0)
-            p.y[orow] = sum;
-          else
-            p.y[orow] += sum;
-        }
-      }
-      buf ^= 1;
+    // row complete: fixed-order reduction inside the warp (units, then chunk slots)
+    float v = (acc.x + acc.y) + (acc.z + acc.w);
+    v += __shfl_xor_sync(0xffffffffu, v, 1);
+    v += __shfl_xor_sync(0xffffffffu, v, 2);
+    v += __shfl_xor_sync(0xffffffffu, v, 4);
+    for (int o = 8; o < 8 * CW; o <<= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (j == 0 && cc == 0 && row < p.N && !aborted) {
+      if (MODE == 0)
+        p.y[row] = v;
+      else
+        p.y[row] += v;
     }
   }
 }
@@ -435,20 +507,13 @@ struct Geometry {
   int RT, CW, KS, tiles, grid;
 };
 
-// Row-tile shape that minimises the busiest CTA's work (rows x padded chunks).
+// Row-tile shape for the T = 1 kernel: a warp holds 4 (row, chunk) pairs, so CW <= 4 keeps every row inside
+// one warp; the widest CW the row length allows gives the smallest tiles (RT = 32 / CW) and the best balance.
 static Geometry pick_geometry(int N, int nch, int sms) {
-  Geometry best = {32, 1, nch, (N + 31) / 32, std::min((N + 31) / 32, sms)};
-  long long best_cost = LLONG_MAX;
-  for (int RT : {32, 16, 8, 4}) {
-    const int CW = 32 / RT;
-    if (CW > nch && RT != 32) continue;
-    const int tiles = (N + RT - 1) / RT;
-    const int grid = std::min(tiles, sms);
-    const int KS = (nch + CW - 1) / CW;
-    const long long cost = static_cast<long long>((tiles + grid - 1) / grid) * RT * KS * CW;
-    if (cost < best_cost) best_cost = cost, best = {RT, CW, KS, tiles, grid};
-  }
-  return best;
+  const int CW = nch >= 4 ? 4 : (nch >= 2 ? 2 : 1);
+  const int RT = 32 / CW;
+  const int tiles = (N + RT - 1) / RT;
+  return {RT, CW, (nch + CW - 1) / CW, tiles, std::min(tiles, sms)};
 }
 
 static int make_maps(const aib_c12* c, int RT, int CW, CUtensorMap* tm8, CUtensorMap* tme4) {
@@ -472,14 +537,14 @@ static int run_t1(const aib_c12* c, const float* x, float* y, int mode, const ui
   const size_t budget = std::max(kSmemTarget, kHeader + xs_bytes + 2 * kStageBytes);
   if (budget > kSmemMax) return fail(AIB_ENOTSUP, "aib_gemv_c12: K=%d too large for the shared x buffer", c->K);
   int NS = static_cast<int>((budget - kHeader - xs_bytes) / kStageBytes);
-  NS = std::max(2, std::min(NS, 8));
+  NS = std::max(2, std::min(NS, 8)) & ~1;  // even: the two consumer groups own alternate ring slots
   const size_t smem = kHeader + xs_bytes + static_cast<size_t>(NS) * kStageBytes;
   Params p{c->rp, c->ec, c->ev, x, y, lnw, eps, c->base, c->N, c->K, nch, g.RT, g.CW, g.KS, g.tiles, NS, 1, 0, 0,
            c->K};
   auto go = [&](auto kernel) -> int {
     const int r2 = allow_smem(kernel, smem);
     if (r2) return r2;
-    return launch(kernel, dim3(g.grid), dim3(kThreads), smem, s, "aib_gemv_c12(T=1)", tm8, tme4, p);
+    return launch(kernel, dim3(g.grid), dim3(kT1Threads), smem, s, "aib_gemv_c12(T=1)", tm8, tme4, p);
   };
   if (lnw) {
     if (mode == 0) return go(gemv_t1_kernel<0, true>);
