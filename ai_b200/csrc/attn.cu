@@ -11,6 +11,9 @@
 // warp covers one bf16 row). Each CTA writes a partial (m, l, acc) to the workspace; the last CTA of a
 // group (atomic ticket, no waiting) merges the partials in split order -- starting, like the reference,
 // from the current token -- so results are deterministic. The ticket counters return to zero.
+// K/V rows of a CTA's range are staged into shared memory by bulk asynchronous copies (cp.async.bulk,
+// no multicast) through a ring of 32-position sub-chunks, so the whole range is in flight at once; the
+// merge loads every split's partial in parallel (weights exp(m_s - M) first, then the sums).
 #include <algorithm>
 #include "common.cuh"
 
@@ -21,6 +24,21 @@ constexpr int kWarps = 4;
 constexpr int kThreads = 32 * kWarps;
 constexpr int GMAX = 8;
 
+AIB_DEV void bulk_g2s(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(smem_dst)),
+               "l"(reinterpret_cast<uint64_t>(gsrc)), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
+constexpr int kSub = 32;   // positions per staged sub-chunk
+constexpr int kSlots = 4;  // ring depth
+
+template <int HD>
+constexpr size_t ring_bytes() {
+  return static_cast<size_t>(kSlots) * kSub * HD * 2 * 2;
+}
+
 template <int HD>
 struct Smem {
   float q[GMAX][HD];
@@ -30,7 +48,12 @@ struct Smem {
   float cs[HD / 2], sn[HD / 2];
   float wm[kWarps][GMAX], wl[kWarps][GMAX];
   float wacc[kWarps][GMAX][HD];
+  float mw[64][GMAX];  // merge weights exp(m_s - M) per split
+  float mM[GMAX], mL[GMAX], mc[GMAX];
+  uint64_t bar[kSlots];
   int last;
+  int abort;
+  int issued;
 };
 
 // RMSNorm (weight w) + RoPE of one head vector held by a warp: lane owns elements lane + 32*i.
@@ -73,12 +96,15 @@ AIB_DEV void load_row(const uint16_t* p, float* o) {
   }
 }
 
-// Attention of the G query heads in sm.q over cache rows [j0, j1) of one group. Writes the CTA partial
-// (acc[HD], m, l per head) to `part`.
+// Attention of the G query heads in sm.q over cache rows [j0, j1) of one group. The rows are streamed into
+// `ring` (dynamic shared memory) by bulk copies issued by thread 0, kSub positions per slot; every wait is
+// bounded and, on a timeout, all threads keep the same barrier sequence and skip the math. Writes the CTA
+// partial (acc[HD], m, l per head) to `part`.
 template <int HD>
-AIB_DEV void attend_range(Smem<HD>& sm, const uint16_t* kc, const uint16_t* vc, int G, int j0, int j1, float scale,
-                          float* part) {
+AIB_DEV void attend_range(Smem<HD>& sm, uint8_t* ring, const uint16_t* kc, const uint16_t* vc, int G, int j0, int j1,
+                          float scale, float* part) {
   constexpr int PER = HD / 32;  // dims per lane: 4 (HD=128) or 2 (HD=64)
+  constexpr uint32_t kRowBytes = HD * 2, kHalf = kSub * kRowBytes;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   float q[GMAX][PER], acc[GMAX][PER], m[GMAX], l[GMAX];
 #pragma unroll
@@ -91,35 +117,70 @@ AIB_DEV void attend_range(Smem<HD>& sm, const uint16_t* kc, const uint16_t* vc, 
       q[h][i] = (h < G) ? sm.q[h][lane * PER + i] * scale : 0.0f;
     }
   }
-  constexpr int U = 4;
-  for (int jb = j0 + warp * U; jb < j1; jb += kWarps * U) {
-    float kv[U][PER], vv[U][PER];
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      if (jb + u < j1) {
-        load_row<PER>(kc + static_cast<size_t>(jb + u) * HD + lane * PER, kv[u]);
-        load_row<PER>(vc + static_cast<size_t>(jb + u) * HD + lane * PER, vv[u]);
+  const int n = j1 - j0, nsub = (n + kSub - 1) / kSub;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kSlots; ++i) mbar_init(&sm.bar[i], 1);
+    sm.abort = 0;
+    sm.issued = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  volatile int* abort_flag = &sm.abort;
+  auto issue = [&](int i) {
+    sm.issued = i + 1;
+    const int p0 = j0 + i * kSub, cnt = min(kSub, j1 - p0);
+    uint8_t* slot = ring + static_cast<size_t>(i % kSlots) * 2 * kHalf;
+    mbar_arrive_expect_tx(&sm.bar[i % kSlots], 2 * cnt * kRowBytes);
+    bulk_g2s(slot, kc + static_cast<size_t>(p0) * HD, cnt * kRowBytes, &sm.bar[i % kSlots]);
+    bulk_g2s(slot + kHalf, vc + static_cast<size_t>(p0) * HD, cnt * kRowBytes, &sm.bar[i % kSlots]);
+  };
+  if (threadIdx.x == 0)
+    for (int i = 0; i < min(kSlots, nsub); ++i) issue(i);
+  for (int i = 0; i < nsub; ++i) {
+    bool ok = false;
+    if (!*abort_flag) {
+      for (uint32_t it = 0; it < kSpinLimit && !ok; ++it) {
+        ok = mbar_try_wait(&sm.bar[i % kSlots], (i / kSlots) & 1);
+        if (!ok && *abort_flag) break;
+      }
+      if (!ok && !*abort_flag) {
+        set_status(AIB_DEV_TIMEOUT_FULL);
+        *abort_flag = 1;
       }
     }
+    if (ok) {
+      const uint8_t* slot = ring + static_cast<size_t>(i % kSlots) * 2 * kHalf;
+      const int cnt = min(kSub, j1 - (j0 + i * kSub));
+      for (int pp = warp; pp < cnt; pp += kWarps) {
+        float kv[PER], vv[PER];
+        load_row<PER>(reinterpret_cast<const uint16_t*>(slot + pp * kRowBytes) + lane * PER, kv);
+        load_row<PER>(reinterpret_cast<const uint16_t*>(slot + kHalf + pp * kRowBytes) + lane * PER, vv);
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-      if (jb + u >= j1) break;
+        for (int h = 0; h < GMAX; ++h) {
+          if (h >= G) break;
+          float sc = 0.0f;
 #pragma unroll
-      for (int h = 0; h < GMAX; ++h) {
-        if (h >= G) break;
-        float sc = 0.0f;
+          for (int d = 0; d < PER; ++d) sc += q[h][d] * kv[d];
+          sc = warp_sum(sc);
+          const float mn = fmaxf(m[h], sc);
+          const float alpha = expf(m[h] - mn);
+          const float pr = expf(sc - mn);
+          l[h] = l[h] * alpha + pr;
 #pragma unroll
-        for (int i = 0; i < PER; ++i) sc += q[h][i] * kv[u][i];
-        sc = warp_sum(sc);
-        const float mn = fmaxf(m[h], sc);
-        const float alpha = expf(m[h] - mn);
-        const float pr = expf(sc - mn);
-        l[h] = l[h] * alpha + pr;
-#pragma unroll
-        for (int i = 0; i < PER; ++i) acc[h][i] = acc[h][i] * alpha + pr * vv[u][i];
-        m[h] = mn;
+          for (int d = 0; d < PER; ++d) acc[h][d] = acc[h][d] * alpha + pr * vv[d];
+          m[h] = mn;
+        }
       }
     }
+    __syncthreads();  // every warp is done with this slot
+    if (threadIdx.x == 0 && i + kSlots < nsub && !*abort_flag) {
+      fence_proxy_async();
+      issue(i + kSlots);
+    }
+  }
+  if (*abort_flag && threadIdx.x == 0) {  // never leave with copies in flight
+    const int last = sm.issued;
+    for (int i = max(0, last - kSlots); i < last; ++i) mbar_wait(&sm.bar[i % kSlots], (i / kSlots) & 1, AIB_DEV_TIMEOUT_FULL);
   }
   // combine the warps in order
 #pragma unroll
@@ -154,25 +215,39 @@ AIB_DEV void attend_range(Smem<HD>& sm, const uint16_t* kc, const uint16_t* vc, 
   }
 }
 
-// Merge S partials (in order) on top of an initial state (m0, l0, acc0[d]) and write out.
+// Merge S partials in split order on top of an initial state (m0, l0, acc0[d]; null = empty) and write out.
+// All partial maxima are loaded at once, the merge weights exp(m_s - M) computed in shared memory, then each
+// output is a fixed-order sum whose loads are independent of one another.
 template <int HD>
-AIB_DEV void merge_write(const float* parts, int S, int G, const float* m0, const float* l0, const float* acc0,
-                         float* out) {
+AIB_DEV void merge_write(Smem<HD>& sm, const float* parts, int S, int G, const float* m0, const float* l0,
+                         const float* acc0, float* out) {
+  for (int idx = threadIdx.x; idx < S * G; idx += kThreads) {
+    const int s = idx / G, h = idx % G;
+    sm.mw[s][h] = __ldcg(parts + (static_cast<size_t>(s) * G + h) * (HD + 2) + HD);
+  }
+  __syncthreads();
+  for (int h = threadIdx.x; h < G; h += kThreads) {
+    float M = m0 ? m0[h] : -INFINITY;
+    for (int s = 0; s < S; ++s) M = fmaxf(M, sm.mw[s][h]);
+    float L = (m0 && M != -INFINITY) ? l0[h] * expf(m0[h] - M) : 0.0f;
+    sm.mc[h] = (m0 && M != -INFINITY) ? expf(m0[h] - M) : 0.0f;
+    for (int s = 0; s < S; ++s) {
+      const float ms = sm.mw[s][h];
+      const float w = (ms == -INFINITY || M == -INFINITY) ? 0.0f : expf(ms - M);
+      sm.mw[s][h] = w;
+      L += w * __ldcg(parts + (static_cast<size_t>(s) * G + h) * (HD + 2) + HD + 1);
+    }
+    sm.mL[h] = L;
+  }
+  __syncthreads();
   for (int idx = threadIdx.x; idx < G * HD; idx += kThreads) {
     const int h = idx / HD, d = idx % HD;
-    float m = m0 ? m0[h] : -INFINITY, l = l0 ? l0[h] : 0.0f, a = acc0 ? acc0[d] : 0.0f;
-    for (int s = 0; s < S; ++s) {
-      const float* ph = parts + (static_cast<size_t>(s) * G + h) * (HD + 2);
-      const float ls = __ldcg(ph + HD + 1);
-      if (!(ls > 0.0f)) continue;
-      const float ms = __ldcg(ph + HD);
-      const float mn = fmaxf(m, ms);
-      const float fa = expf(m - mn), fb = expf(ms - mn);
-      a = a * fa + __ldcg(ph + d) * fb;
-      l = l * fa + ls * fb;
-      m = mn;
-    }
-    out[h * HD + d] = l > 0.0f ? a / l : 0.0f;
+    float a = acc0 ? sm.mc[h] * acc0[d] : 0.0f;
+    const float* ph = parts + static_cast<size_t>(h) * (HD + 2) + d;
+    const size_t stride = static_cast<size_t>(G) * (HD + 2);
+#pragma unroll 4
+    for (int s = 0; s < S; ++s) a += sm.mw[s][h] * __ldcg(ph + s * stride);
+    out[h * HD + d] = sm.mL[h] > 0.0f ? a / sm.mL[h] : 0.0f;
   }
 }
 
@@ -184,6 +259,7 @@ __global__ void __launch_bounds__(kThreads)
                      float* __restrict__ out, int H, int KV, int maxt, float eps, float scale, float* ws_part,
                      int* ws_cnt) {
   __shared__ Smem<HD> sm;
+  extern __shared__ __align__(128) uint8_t ring[];
   const int s = blockIdx.x, S = gridDim.x, g = blockIdx.y;
   const int G = H / KV;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -230,7 +306,7 @@ __global__ void __launch_bounds__(kThreads)
   const int chunk = (n + S - 1) / S;
   const int j0 = min(n, s * chunk), j1 = min(n, j0 + chunk);
   float* part = ws_part + (static_cast<size_t>(g) * S + s) * G * (HD + 2);
-  attend_range<HD>(sm, kg, vg, G, j0, j1, scale, part);
+  attend_range<HD>(sm, ring, kg, vg, G, j0, j1, scale, part);
   // ordered merge by the last CTA of the group
   __threadfence();
   __syncthreads();
@@ -244,7 +320,7 @@ __global__ void __launch_bounds__(kThreads)
     float l0[GMAX];
 #pragma unroll
     for (int h = 0; h < GMAX; ++h) l0[h] = 1.0f;
-    merge_write<HD>(ws_part + static_cast<size_t>(g) * S * G * (HD + 2), S, G, sm.cur_score, l0, sm.vcur,
+    merge_write<HD>(sm, ws_part + static_cast<size_t>(g) * S * G * (HD + 2), S, G, sm.cur_score, l0, sm.vcur,
                     out + static_cast<size_t>(g) * G * HD);
     if (threadIdx.x == 0) ws_cnt[g] = 0;
   }
@@ -295,6 +371,7 @@ __global__ void __launch_bounds__(kThreads)
                        const int64_t* __restrict__ pos_p, float* __restrict__ out, int H, int KV, int maxt,
                        float scale, float* ws_part, int* ws_cnt) {
   __shared__ Smem<HD> sm;
+  extern __shared__ __align__(128) uint8_t ring[];
   const int s = blockIdx.x, S = gridDim.x, g = blockIdx.y, t = blockIdx.z;
   const int G = H / KV;
   pdl_wait();
@@ -308,8 +385,8 @@ __global__ void __launch_bounds__(kThreads)
   const int j0 = min(n, s * chunk), j1 = min(n, j0 + chunk);
   const size_t slot = static_cast<size_t>(t) * KV + g;
   float* part = ws_part + (slot * S + s) * G * (HD + 2);
-  attend_range<HD>(sm, kc + static_cast<size_t>(g) * maxt * HD, vc + static_cast<size_t>(g) * maxt * HD, G, j0, j1,
-                   scale, part);
+  attend_range<HD>(sm, ring, kc + static_cast<size_t>(g) * maxt * HD, vc + static_cast<size_t>(g) * maxt * HD, G, j0,
+                   j1, scale, part);
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -319,7 +396,7 @@ __global__ void __launch_bounds__(kThreads)
   __syncthreads();
   if (sm.last) {
     __threadfence();
-    merge_write<HD>(ws_part + slot * S * G * (HD + 2), S, G, nullptr, nullptr, nullptr,
+    merge_write<HD>(sm, ws_part + slot * S * G * (HD + 2), S, G, nullptr, nullptr, nullptr,
                     out + (static_cast<size_t>(t) * H + g * G) * HD);
     if (threadIdx.x == 0) ws_cnt[slot] = 0;
   }
@@ -369,6 +446,8 @@ int aib_rope_attn_decode(const float* qkv, const uint16_t* qn, const uint16_t* k
   if (rc) return rc;
   if (!qkv || !qn || !kn || !inv || !pos || !kc || !vc || !out || maxt <= 0)
     return fail(AIB_EINVAL, "aib_rope_attn_decode: bad arguments");
+  if ((reinterpret_cast<uintptr_t>(kc) | reinterpret_cast<uintptr_t>(vc)) & 15)
+    return fail(AIB_EINVAL, "aib_rope_attn_decode: KV caches must be 16-byte aligned");
   const size_t need = attn::ws_bytes_for(H, KV, HD, 1);
   if (!ws || ws_bytes < need)
     return fail(AIB_EWORKSPACE, "aib_rope_attn_decode: workspace %zu < %zu bytes", ws_bytes, need);
@@ -376,11 +455,16 @@ int aib_rope_attn_decode(const float* qkv, const uint16_t* qn, const uint16_t* k
   int* cnt = static_cast<int*>(ws);
   float* part = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + attn::kCntBytes);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (HD == 128)
-    return launch(attn::rope_attn_kernel<128>, dim3(S, KV), dim3(attn::kThreads), 0, s, "aib_rope_attn_decode", qkv, qn,
-                  kn, inv, pos, kc, vc, out, H, KV, maxt, eps, scale, part, cnt);
-  return launch(attn::rope_attn_kernel<64>, dim3(S, KV), dim3(attn::kThreads), 0, s, "aib_rope_attn_decode", qkv, qn,
-                kn, inv, pos, kc, vc, out, H, KV, maxt, eps, scale, part, cnt);
+  if (HD == 128) {
+    rc = allow_smem(attn::rope_attn_kernel<128>, attn::ring_bytes<128>());
+    if (rc) return rc;
+    return launch(attn::rope_attn_kernel<128>, dim3(S, KV), dim3(attn::kThreads), attn::ring_bytes<128>(), s,
+                  "aib_rope_attn_decode", qkv, qn, kn, inv, pos, kc, vc, out, H, KV, maxt, eps, scale, part, cnt);
+  }
+  rc = allow_smem(attn::rope_attn_kernel<64>, attn::ring_bytes<64>());
+  if (rc) return rc;
+  return launch(attn::rope_attn_kernel<64>, dim3(S, KV), dim3(attn::kThreads), attn::ring_bytes<64>(), s,
+                "aib_rope_attn_decode", qkv, qn, kn, inv, pos, kc, vc, out, H, KV, maxt, eps, scale, part, cnt);
 }
 
 int aib_qk_rope_cache(const float* qkv, const uint16_t* qn, const uint16_t* kn, const float* inv, const int64_t* pos,
@@ -404,6 +488,8 @@ int aib_attn_cached(const float* q, const uint16_t* kc, const uint16_t* vc, cons
   if (rc) return rc;
   if (!q || !kc || !vc || !pos || !out || T <= 0 || T > 65535 || maxt <= 0)
     return fail(AIB_EINVAL, "aib_attn_cached: bad arguments");
+  if ((reinterpret_cast<uintptr_t>(kc) | reinterpret_cast<uintptr_t>(vc)) & 15)
+    return fail(AIB_EINVAL, "aib_attn_cached: KV caches must be 16-byte aligned");
   if (static_cast<long long>(T) * KV > attn::kMaxSlots)
     return fail(AIB_EINVAL, "aib_attn_cached: T * KV must be <= %d", attn::kMaxSlots);
   const size_t need = attn::ws_bytes_for(H, KV, HD, T);
@@ -412,11 +498,16 @@ int aib_attn_cached(const float* q, const uint16_t* kc, const uint16_t* vc, cons
   int* cnt = static_cast<int*>(ws);
   float* part = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + attn::kCntBytes);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (HD == 128)
-    return launch(attn::attn_cached_kernel<128>, dim3(S, KV, T), dim3(attn::kThreads), 0, s, "aib_attn_cached", q, kc,
-                  vc, pos, out, H, KV, maxt, scale, part, cnt);
-  return launch(attn::attn_cached_kernel<64>, dim3(S, KV, T), dim3(attn::kThreads), 0, s, "aib_attn_cached", q, kc, vc,
-                pos, out, H, KV, maxt, scale, part, cnt);
+  if (HD == 128) {
+    rc = allow_smem(attn::attn_cached_kernel<128>, attn::ring_bytes<128>());
+    if (rc) return rc;
+    return launch(attn::attn_cached_kernel<128>, dim3(S, KV, T), dim3(attn::kThreads), attn::ring_bytes<128>(), s,
+                  "aib_attn_cached", q, kc, vc, pos, out, H, KV, maxt, scale, part, cnt);
+  }
+  rc = allow_smem(attn::attn_cached_kernel<64>, attn::ring_bytes<64>());
+  if (rc) return rc;
+  return launch(attn::attn_cached_kernel<64>, dim3(S, KV, T), dim3(attn::kThreads), attn::ring_bytes<64>(), s,
+                "aib_attn_cached", q, kc, vc, pos, out, H, KV, maxt, scale, part, cnt);
 }
 
 }  // extern "C"

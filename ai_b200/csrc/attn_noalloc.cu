@@ -61,6 +61,8 @@ int aib_rope_attn_decode_noalloc(const float* qkv, const uint16_t* qn, const uin
   if (rc) return rc;
   if (!qkv || !qn || !kn || !inv || !pos || !kc || !vc || !out || maxt <= 0)
     return fail(AIB_EINVAL, "aib_rope_attn_decode_noalloc: bad arguments");
+  if ((reinterpret_cast<uintptr_t>(kc) | reinterpret_cast<uintptr_t>(vc)) & 15)
+    return fail(AIB_EINVAL, "aib_rope_attn_decode_noalloc: KV caches must be 16-byte aligned");
   const int S = attn::splits(KV, 1), G = H / KV;
   const size_t part_bytes = static_cast<size_t>(KV) * S * G * (HD + 2) * sizeof(float);
   if (static_cast<size_t>(KV) * sizeof(int) > attn_noalloc::kCounterBytes ||
@@ -79,12 +81,17 @@ int aib_rope_attn_decode_noalloc(const float* qkv, const uint16_t* qn, const uin
   cudaError_t e = cudaMemsetAsync(cnt, 0, static_cast<size_t>(KV) * sizeof(int), s);
   if (e != cudaSuccess)
     return fail(AIB_ECUDA, "aib_rope_attn_decode_noalloc: clearing counters: %s", cudaGetErrorString(e));
-  if (HD == 128)
-    return launch(attn::rope_attn_kernel<128>, dim3(S, KV), dim3(attn::kThreads), 0, s,
+  if (HD == 128) {
+    rc = allow_smem(attn::rope_attn_kernel<128>, attn::ring_bytes<128>());
+    if (rc) return rc;
+    return launch(attn::rope_attn_kernel<128>, dim3(S, KV), dim3(attn::kThreads), attn::ring_bytes<128>(), s,
                   "aib_rope_attn_decode_noalloc", qkv, qn, kn, inv, pos, kc, vc, out, H, KV, maxt, eps, scale, part,
                   cnt);
-  return launch(attn::rope_attn_kernel<64>, dim3(S, KV), dim3(attn::kThreads), 0, s, "aib_rope_attn_decode_noalloc",
-                qkv, qn, kn, inv, pos, kc, vc, out, H, KV, maxt, eps, scale, part, cnt);
+  }
+  rc = allow_smem(attn::rope_attn_kernel<64>, attn::ring_bytes<64>());
+  if (rc) return rc;
+  return launch(attn::rope_attn_kernel<64>, dim3(S, KV), dim3(attn::kThreads), attn::ring_bytes<64>(), s,
+                "aib_rope_attn_decode_noalloc", qkv, qn, kn, inv, pos, kc, vc, out, H, KV, maxt, eps, scale, part, cnt);
 }
 
 }  // extern "C"

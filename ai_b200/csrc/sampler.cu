@@ -12,11 +12,12 @@
 //  1. penalties via a sorted prior-id table + a vocabulary bitmap in shared memory (O(1) test per token);
 //  2. greedy: block argmax;
 //  3. top-k threshold by 4-pass radix select on order-preserving 32-bit keys of the logits;
-//  4. top-p: a radix descent over per-bucket probability mass gives a key threshold whose upper set is a
-//     guaranteed superset of the nucleus (1e-9 relative margin on an atomically accumulated mass);
-//  5. the candidates (<= CMAX) are gathered, bitonic-sorted by (key desc, index asc), and the nucleus cut,
+//  4. candidates = the top min(k, CMAX) keys (same radix select); histograms use warp-aggregated shared
+//     atomics (__match_any_sync), since logit keys crowd into a few buckets;
+//  5. the candidates are gathered, bitonic-sorted by (key desc, index asc), and the nucleus cut,
 //     renormalisation and inverse CDF are evaluated in float64 with a fixed-order block scan against the
-//     softmax denominator from a fixed-order reduction -- deterministic run to run.
+//     softmax denominator from a fixed-order reduction -- deterministic run to run. If the nucleus (or, at
+//     top_p = 1, the sampled point) lies beyond the CMAX largest logits the row sets AIB_DEV_SAMPLER_CAP.
 #include <climits>
 #include "common.cuh"
 
@@ -43,10 +44,9 @@ struct Row {
   float rep, pres, freq;
 };
 
-// penalised + masked logit of token v
-AIB_DEV float value(const Row& r, int v) {
+// penalised + masked logit of token v whose raw logit is x
+AIB_DEV float adjust(const Row& r, int v, float x) {
   if (r.mask && !((r.mask[v >> 5] >> (v & 31)) & 1u)) return -INFINITY;
-  float x = __ldg(r.l + v);
   if ((r.bitmap[v >> 5] >> (v & 31)) & 1u) {
     int lo = 0, hi = r.n_pid;  // count = occurrences of v in the sorted prior list
     while (lo < hi) {
@@ -67,6 +67,32 @@ AIB_DEV float value(const Row& r, int v) {
   return x;
 }
 
+// Eight consecutive raw logits from v0 (two 16-byte loads when the row is 16-byte aligned).
+AIB_DEV void load8(const Row& r, int V, int v0, float* x) {
+  if ((reinterpret_cast<uintptr_t>(r.l) & 15) == 0 && v0 + 8 <= V) {
+    const float4 a = __ldg(reinterpret_cast<const float4*>(r.l + v0));
+    const float4 b = __ldg(reinterpret_cast<const float4*>(r.l + v0 + 4));
+    x[0] = a.x, x[1] = a.y, x[2] = a.z, x[3] = a.w, x[4] = b.x, x[5] = b.y, x[6] = b.z, x[7] = b.w;
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) x[i] = (v0 + i < V) ? __ldg(r.l + v0 + i) : 0.0f;
+  }
+}
+
+// Visit every token of the row: f(v, adjusted logit). Each thread reads 8 consecutive logits per round,
+// so a pass keeps ~8K loads in flight in the block.
+template <typename F>
+AIB_DEV void for_each_value(const Row& r, int V, F&& f) {
+  for (int base = 0; base < V; base += kThreads * 8) {
+    const int v0 = base + threadIdx.x * 8;
+    float x[8];
+    load8(r, V, v0, x);
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if (v0 + i < V) f(v0 + i, adjust(r, v0 + i, x[i]));
+  }
+}
+
 template <typename T>
 AIB_DEV T block_sum_fixed(T v, T* red) {  // deterministic: fixed lanes, fixed warp order
 #pragma unroll
@@ -81,14 +107,58 @@ AIB_DEV T block_sum_fixed(T v, T* red) {  // deterministic: fixed lanes, fixed w
 
 struct __align__(16) Shared {
   double dred[32];
-  double hmass[256];
   float fred[32];
   int ired[32];
   unsigned int hist[256];
   int ncand;
+  int ncand_total;  // size of the kept set (V, or the top-k set)
   uint32_t prefix;
-  double rem;
 };
+
+// Key of the k-th largest value among tokens with key >= floor (ties at the boundary counted once each;
+// every token whose key is >= the result is kept). 4 radix passes of 8 bits; warp-aggregated histogram.
+AIB_DEV uint32_t select_kth(const Row& r, int V, int k, uint32_t floor, Shared& sh) {
+  const int tid = threadIdx.x, lane = tid & 31;
+  uint32_t prefix = 0u, pmask = 0u;
+  int remaining = k;
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    __syncthreads();
+    for (int i = tid; i < 256; i += kThreads) sh.hist[i] = 0u;
+    __syncthreads();
+    for (int base = 0; base < V; base += kThreads * 8) {  // uniform trip count: warp-wide match below
+      const int v0 = base + tid * 8;
+      float x[8];
+      load8(r, V, v0, x);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        int bucket = 256;  // "no bucket"
+        if (v0 + i < V) {
+          const uint32_t key = fkey(adjust(r, v0 + i, x[i]));
+          if (key >= floor && (key & pmask) == prefix) bucket = static_cast<int>((key >> shift) & 0xFFu);
+        }
+        const unsigned peers = __match_any_sync(0xffffffffu, bucket);
+        if (bucket != 256 && lane == __ffs(peers) - 1)
+          atomicAdd(&sh.hist[bucket], static_cast<unsigned>(__popc(peers)));
+      }
+    }
+    __syncthreads();
+    if (tid == 0) {
+      int cum = 0, d;
+      for (d = 255; d > 0; --d) {
+        if (cum + static_cast<int>(sh.hist[d]) >= remaining) break;
+        cum += sh.hist[d];
+      }
+      sh.prefix = prefix | (static_cast<uint32_t>(d) << shift);
+      sh.ired[0] = remaining - cum;
+    }
+    __syncthreads();
+    prefix = sh.prefix;
+    remaining = sh.ired[0];
+    pmask |= 0xFFu << shift;
+  }
+  __syncthreads();
+  return prefix;
+}
 
 __global__ void __launch_bounds__(kThreads)
     sample_kernel(const float* __restrict__ logits, int V, int ld, aib_sample_params prm,
@@ -152,10 +222,9 @@ __global__ void __launch_bounds__(kThreads)
   // ---- 2. max (and greedy argmax: first index among the maxima)
   float best = -INFINITY;
   int bi = INT_MAX;
-  for (int v = tid; v < V; v += kThreads) {
-    const float x = value(r, v);
+  for_each_value(r, V, [&](int v, float x) {
     if (x > best || (x == best && v < bi)) best = x, bi = v;
-  }
+  });
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     const float ob = __shfl_xor_sync(0xffffffffu, best, o);
@@ -179,97 +248,35 @@ __global__ void __launch_bounds__(kThreads)
   const double Mz = static_cast<double>(best) / Td;
 
   // ---- 3. top-k threshold key (k-th largest, ties kept)
-  uint32_t thr = 0u;
   const int topk = prm.top_k;
-  if (topk > 0 && topk < V) {
-    uint32_t prefix = 0u, pmask = 0u;
-    int remaining = topk;
-    for (int shift = 24; shift >= 0; shift -= 8) {
-      __syncthreads();
-      for (int i = tid; i < 256; i += kThreads) sh.hist[i] = 0u;
-      __syncthreads();
-      for (int v = tid; v < V; v += kThreads) {
-        const uint32_t k = fkey(value(r, v));
-        if ((k & pmask) == prefix) atomicAdd(&sh.hist[(k >> shift) & 0xFFu], 1u);
-      }
-      __syncthreads();
-      if (tid == 0) {
-        int cum = 0, d;
-        for (d = 255; d > 0; --d) {
-          if (cum + static_cast<int>(sh.hist[d]) >= remaining) break;
-          cum += sh.hist[d];
-        }
-        sh.prefix = prefix | (static_cast<uint32_t>(d) << shift);
-        sh.ired[0] = remaining - cum;
-      }
-      __syncthreads();
-      prefix = sh.prefix;
-      remaining = sh.ired[0];
-      pmask |= 0xFFu << shift;
-    }
-    thr = prefix;
-  }
+  const uint32_t thr_k = (topk > 0 && topk < V) ? select_kth(r, V, topk, 0u, sh) : 0u;
 
   // ---- softmax denominator over the kept set (fixed-order reduction)
   double part = 0.0;
-  for (int v = tid; v < V; v += kThreads) {
-    const float x = value(r, v);
-    if (fkey(x) >= thr && x != -INFINITY) part += exp(static_cast<double>(x) / Td - Mz);
-  }
+  for_each_value(r, V, [&](int, float x) {
+    if (fkey(x) >= thr_k && x != -INFINITY) part += exp(static_cast<double>(x) / Td - Mz);
+  });
   const double Z = block_sum_fixed<double>(part, sh.dred);
-
-  // ---- 4. top-p superset threshold by radix descent over probability mass
   const double top_p = static_cast<double>(prm.top_p);
-  if (top_p < 1.0) {
-    uint32_t prefix = 0u, pmask = 0u;
-    double target = top_p * Z * (1.0 + 1e-9) + 1e-300;
-    for (int shift = 24; shift >= 0; shift -= 8) {
-      __syncthreads();
-      for (int i = tid; i < 256; i += kThreads) sh.hmass[i] = 0.0;
-      __syncthreads();
-      for (int v = tid; v < V; v += kThreads) {
-        const float x = value(r, v);
-        const uint32_t k = fkey(x);
-        if (k >= thr && x != -INFINITY && (k & pmask) == prefix)
-          atomicAdd(&sh.hmass[(k >> shift) & 0xFFu], exp(static_cast<double>(x) / Td - Mz));
-      }
-      __syncthreads();
-      if (tid == 0) {
-        double cum = 0.0;
-        int d;
-        for (d = 255; d > 0; --d) {
-          if (cum + sh.hmass[d] >= target) break;
-          cum += sh.hmass[d];
-        }
-        sh.prefix = prefix | (static_cast<uint32_t>(d) << shift);
-        sh.rem = target - cum;
-      }
-      __syncthreads();
-      prefix = sh.prefix;
-      target = sh.rem;
-      pmask |= 0xFFu << shift;
-    }
-    thr = max(thr, prefix);
-  }
+
+  // ---- 4. candidates: the CMAX largest keys of the kept set (all of them if it is smaller)
+  uint32_t thr = thr_k;
+  const int kept_max = (topk > 0 && topk < V) ? topk : V;
+  if (kept_max > CMAX) thr = max(thr, select_kth(r, V, CMAX, thr_k, sh));
 
   // ---- 5. gather candidates (key >= thr, finite), sort, exact nucleus + inverse CDF
   __syncthreads();
-  if (tid == 0) sh.ncand = 0;
+  if (tid == 0) sh.ncand = 0, sh.ncand_total = kept_max;
   __syncthreads();
-  for (int v = tid; v < V; v += kThreads) {
-    const float x = value(r, v);
+  for_each_value(r, V, [&](int v, float x) {
     const uint32_t k = fkey(x);
     if (k >= thr && x != -INFINITY) {
       const int slot = atomicAdd(&sh.ncand, 1);
       if (slot < CMAX) ckey[slot] = k, cidx[slot] = v;
     }
-  }
+  });
   __syncthreads();
-  int nc = sh.ncand;
-  if (nc > CMAX) {
-    if (tid == 0) set_status(AIB_DEV_SAMPLER_CAP);
-    nc = CMAX;
-  }
+  int nc = min(sh.ncand, CMAX);  // ties at the CMAX-th key can add a few more; the extra ones are dropped
   int n2 = 1;
   while (n2 < nc) n2 <<= 1;
   for (int i = nc + tid; i < n2; i += kThreads) ckey[i] = 0u, cidx[i] = INT_MAX;
@@ -319,6 +326,9 @@ __global__ void __launch_bounds__(kThreads)
   for (int i = tid; i < nc; i += kThreads) keep += (top_p >= 1.0 || cp[i] < top_p) ? 1 : 0;
   keep = block_sum_fixed<int>(keep, sh.ired);
   keep = max(1, min(keep, nc));
+  // the candidates must contain the nucleus: their total mass reaches top_p, or they are the whole kept set
+  if (tid == 0 && nc < sh.ncand_total && (cp[nc - 1] + exp(static_cast<double>(key_value(ckey[nc - 1])) / Td - Mz) / Z) < min(top_p, 1.0 - 1e-12))
+    set_status(AIB_DEV_SAMPLER_CAP);
   const double pl = exp(static_cast<double>(key_value(ckey[keep - 1])) / Td - Mz) / Z;
   const double S = cp[keep - 1] + pl;  // kept mass
   const double u = us ? us[b] : 0.5;

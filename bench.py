@@ -241,13 +241,60 @@ def gpu_arm(args, rank, world):
     return out
 
 
+def micro_attn(args):
+    """Fused T=1 attention of one Qwen3-8B layer at position 4096 (bf16 KV, 8 groups x 4 heads)."""
+    import torch
+    from ai_b200 import tkernels
+    H, KV, HD, maxt, pos = 32, 8, 128, 4608, CTX
+    g = torch.Generator(device="cuda").manual_seed(0)
+    kc = torch.randn(KV, maxt, HD, generator=g, device="cuda").bfloat16()
+    vc = torch.randn(KV, maxt, HD, generator=g, device="cuda").bfloat16()
+    qkv = torch.randn((H + 2 * KV) * HD, generator=g, device="cuda")
+    qn = torch.ones(HD, dtype=torch.bfloat16, device="cuda")
+    inv = (1.0 / (1e6 ** (torch.arange(0, HD, 2, dtype=torch.float32) / HD))).cuda()
+    P = torch.tensor([pos], device="cuda")
+    out = torch.zeros(H * HD, device="cuda")
+    nbytes = 2 * KV * (pos + 1) * HD * 2
+    return (lambda: tkernels.rope_attn(qkv, qn, qn, inv, P, kc, vc, out, maxt, 1e-6, HD ** -0.5, H, KV, HD)), nbytes
+
+
+def micro_sample(args):
+    """Sampler on one [1, 151936] fp32 logits row, top-k 20 / top-p 0.8 / T 0.6."""
+    import torch
+    from ai_b200 import sampler
+    g = torch.Generator(device="cuda").manual_seed(0)
+    lg = torch.randn(1, 151936, generator=g, device="cuda") * 2
+    out = torch.zeros(1, dtype=torch.int64, device="cuda")
+    u = torch.full((1,), 0.37, dtype=torch.float64, device="cuda")
+    prm = sampler.params(**SAMPLING)
+    return (lambda: sampler.sample_into(lg, out, prm, u)), lg.numel() * 4
+
+
 def micro(args):
-    """One kernel alone on a small case (for ncu captures and quick A/B timing): the codec GEMV on a Qwen3-8B
-    gu-shaped matrix [24576, 4096] (151 MB of planes, > L2), T = 1 with the RMS prologue."""
+    """One kernel alone on a small case (for ncu captures and quick A/B timing). gemv: the codec GEMV on a
+    Qwen3-8B gu-shaped matrix [24576, 4096] (151 MB of planes, > L2), T = 1 with the RMS prologue;
+    gemv_down: [4096, 12288] with the SiLU-gated input; attn: one layer's decode attention at ctx 4096;
+    sample: the sampler on one vocabulary row."""
     import torch
     from ai_b200 import build, wcomp
     build.build()
     torch.cuda.set_device(0)
+    if args.micro in ("attn", "sample"):
+        run, nbytes = (micro_attn if args.micro == "attn" else micro_sample)(args)
+        for _ in range(3):
+            run()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = max(args.steps, 1)
+        e0.record()
+        for _ in range(reps):
+            run()
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / reps
+        print(json.dumps({"micro": args.micro, "bytes": nbytes, "us_per_launch": round(us, 2),
+                          "GBps": round(nbytes / us / 1e3, 1)}))
+        return
     g = torch.Generator(device="cuda").manual_seed(0)
     N, K = (24576, 4096) if args.micro == "gemv" else (4096, 12288)
     c = wcomp.compress((torch.randn(N, K, generator=g, device="cuda") * 0.02).bfloat16())
@@ -273,7 +320,7 @@ def micro(args):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--micro", choices=["gemv", "gemv_down"], default=None,
+    ap.add_argument("--micro", choices=["gemv", "gemv_down", "attn", "sample"], default=None,
                     help="time one kernel alone on a small case (for ncu) instead of the decode benchmark")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=256)
