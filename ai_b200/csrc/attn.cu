@@ -20,7 +20,7 @@
 namespace aib {
 namespace attn {
 
-constexpr int kWarps = 4;
+constexpr int kWarps = 8;
 constexpr int kThreads = 32 * kWarps;
 constexpr int GMAX = 8;
 
@@ -32,6 +32,7 @@ AIB_DEV void bulk_g2s(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t
 }
 
 constexpr int kSub = 32;   // positions per staged sub-chunk
+constexpr int kMaxSplits = 32;
 constexpr int kSlots = 4;  // ring depth
 
 template <int HD>
@@ -48,7 +49,7 @@ struct Smem {
   float cs[HD / 2], sn[HD / 2];
   float wm[kWarps][GMAX], wl[kWarps][GMAX];
   float wacc[kWarps][GMAX][HD];
-  float mw[64][GMAX];  // merge weights exp(m_s - M) per split
+  float mw[kMaxSplits][GMAX];  // merge weights exp(m_s - M) per split
   float mM[GMAX], mL[GMAX], mc[GMAX];
   uint64_t bar[kSlots];
   int last;
@@ -216,26 +217,32 @@ AIB_DEV void attend_range(Smem<HD>& sm, uint8_t* ring, const uint16_t* kc, const
 }
 
 // Merge S partials in split order on top of an initial state (m0, l0, acc0[d]; null = empty) and write out.
-// All partial maxima are loaded at once, the merge weights exp(m_s - M) computed in shared memory, then each
-// output is a fixed-order sum whose loads are independent of one another.
+// The group's partial block (S x G x (HD+2) floats, contiguous) is first copied into shared memory (`stage`,
+// the now idle K/V ring) with every thread issuing independent 16-byte loads, then merged from there:
+// weights exp(m_s - M) per split, fixed-order sums.
 template <int HD>
-AIB_DEV void merge_write(Smem<HD>& sm, const float* parts, int S, int G, const float* m0, const float* l0,
-                         const float* acc0, float* out) {
-  for (int idx = threadIdx.x; idx < S * G; idx += kThreads) {
-    const int s = idx / G, h = idx % G;
-    sm.mw[s][h] = __ldcg(parts + (static_cast<size_t>(s) * G + h) * (HD + 2) + HD);
+AIB_DEV void merge_write(Smem<HD>& sm, float* stage, const float* parts, int S, int G, const float* m0,
+                         const float* l0, const float* acc0, float* out) {
+  const int nf = S * G * (HD + 2);
+  const int n4 = nf / 4;
+  if ((nf & 3) == 0 && (reinterpret_cast<uintptr_t>(parts) & 15) == 0) {
+    const float4* src = reinterpret_cast<const float4*>(parts);
+    float4* dst = reinterpret_cast<float4*>(stage);
+    for (int i = threadIdx.x; i < n4; i += kThreads) dst[i] = __ldcg(src + i);
+  } else {
+    for (int i = threadIdx.x; i < nf; i += kThreads) stage[i] = __ldcg(parts + i);
   }
   __syncthreads();
   for (int h = threadIdx.x; h < G; h += kThreads) {
     float M = m0 ? m0[h] : -INFINITY;
-    for (int s = 0; s < S; ++s) M = fmaxf(M, sm.mw[s][h]);
+    for (int s = 0; s < S; ++s) M = fmaxf(M, stage[(s * G + h) * (HD + 2) + HD]);
     float L = (m0 && M != -INFINITY) ? l0[h] * expf(m0[h] - M) : 0.0f;
     sm.mc[h] = (m0 && M != -INFINITY) ? expf(m0[h] - M) : 0.0f;
     for (int s = 0; s < S; ++s) {
-      const float ms = sm.mw[s][h];
+      const float ms = stage[(s * G + h) * (HD + 2) + HD];
       const float w = (ms == -INFINITY || M == -INFINITY) ? 0.0f : expf(ms - M);
       sm.mw[s][h] = w;
-      L += w * __ldcg(parts + (static_cast<size_t>(s) * G + h) * (HD + 2) + HD + 1);
+      L += w * stage[(s * G + h) * (HD + 2) + HD + 1];
     }
     sm.mL[h] = L;
   }
@@ -243,10 +250,7 @@ AIB_DEV void merge_write(Smem<HD>& sm, const float* parts, int S, int G, const f
   for (int idx = threadIdx.x; idx < G * HD; idx += kThreads) {
     const int h = idx / HD, d = idx % HD;
     float a = acc0 ? sm.mc[h] * acc0[d] : 0.0f;
-    const float* ph = parts + static_cast<size_t>(h) * (HD + 2) + d;
-    const size_t stride = static_cast<size_t>(G) * (HD + 2);
-#pragma unroll 4
-    for (int s = 0; s < S; ++s) a += sm.mw[s][h] * __ldcg(ph + s * stride);
+    for (int s = 0; s < S; ++s) a += sm.mw[s][h] * stage[(s * G + h) * (HD + 2) + d];
     out[h * HD + d] = sm.mL[h] > 0.0f ? a / sm.mL[h] : 0.0f;
   }
 }
@@ -320,8 +324,8 @@ __global__ void __launch_bounds__(kThreads)
     float l0[GMAX];
 #pragma unroll
     for (int h = 0; h < GMAX; ++h) l0[h] = 1.0f;
-    merge_write<HD>(sm, ws_part + static_cast<size_t>(g) * S * G * (HD + 2), S, G, sm.cur_score, l0, sm.vcur,
-                    out + static_cast<size_t>(g) * G * HD);
+    merge_write<HD>(sm, reinterpret_cast<float*>(ring), ws_part + static_cast<size_t>(g) * S * G * (HD + 2), S, G,
+                    sm.cur_score, l0, sm.vcur, out + static_cast<size_t>(g) * G * HD);
     if (threadIdx.x == 0) ws_cnt[g] = 0;
   }
   pdl_trigger();
@@ -396,17 +400,22 @@ __global__ void __launch_bounds__(kThreads)
   __syncthreads();
   if (sm.last) {
     __threadfence();
-    merge_write<HD>(sm, ws_part + slot * S * G * (HD + 2), S, G, nullptr, nullptr, nullptr,
-                    out + (static_cast<size_t>(t) * H + g * G) * HD);
+    merge_write<HD>(sm, reinterpret_cast<float*>(ring), ws_part + slot * S * G * (HD + 2), S, G, nullptr, nullptr,
+                    nullptr, out + (static_cast<size_t>(t) * H + g * G) * HD);
     if (threadIdx.x == 0) ws_cnt[slot] = 0;
   }
   pdl_trigger();
 }
 
-static int splits(int KV, int T) {
+// Splits per (group, token): about one CTA per SM in total, capped so that a group's partials
+// (S x G x (HD+2) floats) fit the staging ring for the merge.
+static int splits(int KV, int T, int G, int HD) {
   const int sms = sm_count();
-  const int S = (2 * sms + KV * T - 1) / (KV * T);
-  return std::max(1, std::min(S, 64));
+  int S = std::max(1, sms / (KV * T));
+  S = std::min(S, kMaxSplits);
+  const size_t ring = HD == 128 ? ring_bytes<128>() : ring_bytes<64>();
+  const int fit = static_cast<int>(ring / (static_cast<size_t>(G) * (HD + 2) * sizeof(float)));
+  return std::max(1, std::min(S, fit));
 }
 
 // Workspace layout: [ticket counters: kMaxSlots ints][partials]. The counters sit at a fixed offset for every
@@ -415,7 +424,7 @@ constexpr int kMaxSlots = 65536;  // KV * T
 constexpr size_t kCntBytes = kMaxSlots * sizeof(int);
 
 static size_t ws_bytes_for(int H, int KV, int HD, int T) {
-  const int G = H / KV, S = splits(KV, T);
+  const int G = H / KV, S = splits(KV, T, G, HD);
   return kCntBytes + static_cast<size_t>(T) * KV * S * G * (HD + 2) * sizeof(float);
 }
 
@@ -451,7 +460,7 @@ int aib_rope_attn_decode(const float* qkv, const uint16_t* qn, const uint16_t* k
   const size_t need = attn::ws_bytes_for(H, KV, HD, 1);
   if (!ws || ws_bytes < need)
     return fail(AIB_EWORKSPACE, "aib_rope_attn_decode: workspace %zu < %zu bytes", ws_bytes, need);
-  const int S = attn::splits(KV, 1);
+  const int S = attn::splits(KV, 1, H / KV, HD);
   int* cnt = static_cast<int*>(ws);
   float* part = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + attn::kCntBytes);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -494,7 +503,7 @@ int aib_attn_cached(const float* q, const uint16_t* kc, const uint16_t* vc, cons
     return fail(AIB_EINVAL, "aib_attn_cached: T * KV must be <= %d", attn::kMaxSlots);
   const size_t need = attn::ws_bytes_for(H, KV, HD, T);
   if (!ws || ws_bytes < need) return fail(AIB_EWORKSPACE, "aib_attn_cached: workspace %zu < %zu bytes", ws_bytes, need);
-  const int S = attn::splits(KV, T);
+  const int S = attn::splits(KV, T, H / KV, HD);
   int* cnt = static_cast<int*>(ws);
   float* part = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + attn::kCntBytes);
   cudaStream_t s = static_cast<cudaStream_t>(stream);

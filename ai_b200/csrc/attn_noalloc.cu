@@ -63,7 +63,7 @@ int aib_rope_attn_decode_noalloc(const float* qkv, const uint16_t* qn, const uin
     return fail(AIB_EINVAL, "aib_rope_attn_decode_noalloc: bad arguments");
   if ((reinterpret_cast<uintptr_t>(kc) | reinterpret_cast<uintptr_t>(vc)) & 15)
     return fail(AIB_EINVAL, "aib_rope_attn_decode_noalloc: KV caches must be 16-byte aligned");
-  const int S = attn::splits(KV, 1), G = H / KV;
+  const int G = H / KV, S = attn::splits(KV, 1, G, HD);
   const size_t part_bytes = static_cast<size_t>(KV) * S * G * (HD + 2) * sizeof(float);
   if (static_cast<size_t>(KV) * sizeof(int) > attn_noalloc::kCounterBytes ||
       attn_noalloc::kCounterBytes + part_bytes > attn_noalloc::kNoallocScratchBytes)

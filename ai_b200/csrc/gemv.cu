@@ -207,7 +207,7 @@ constexpr int kT1Threads = kT1Consumers + 32;
 
 AIB_DEV void produce_pairs(const CUtensorMap* tm8, const CUtensorMap* tme4, uint8_t* ring, uint64_t* full,
                            uint64_t* empty, volatile int* abort_flag, int tb, int ntiles, int KS, int RT, int CW,
-                           int NS) {
+                           int NS, uint32_t stage_bytes, uint32_t e4_off) {
   prefetch_tensormap(tm8);
   prefetch_tensormap(tme4);
   const int n0 = (ntiles + 1) / 2;  // tiles of group 0 (group 1 has ntiles / 2)
@@ -231,10 +231,10 @@ AIB_DEV void produce_pairs(const CUtensorMap* tm8, const CUtensorMap* tme4, uint
       }
     }
     const int tile = tb + lt, ks = i % KS;
-    uint8_t* st = ring + static_cast<size_t>(s) * kStageBytes;
-    mbar_arrive_expect_tx(&full[s], kStageBytes);
+    uint8_t* st = ring + static_cast<size_t>(s) * stage_bytes;
+    mbar_arrive_expect_tx(&full[s], stage_bytes);
     tma_load_3d(st, tm8, &full[s], 0, ks * CW, tile * RT);
-    tma_load_3d(st + kStageM8, tme4, &full[s], 0, ks * CW, tile * RT);
+    tma_load_3d(st + e4_off, tme4, &full[s], 0, ks * CW, tile * RT);
     issued = it + 1;
   }
   if (*abort_flag) {
@@ -274,7 +274,8 @@ __global__ void __launch_bounds__(kT1Threads, 1)
 
   if (tid >= kT1Consumers) {  // producer warp
     if (tid == kT1Consumers)
-      produce_pairs(&tm8, &tme4, ring, full, empty, abort_flag, tb, ntiles, p.KS, p.RT, p.CW, p.NS);
+      produce_pairs(&tm8, &tme4, ring, full, empty, abort_flag, tb, ntiles, p.KS, p.RT, p.CW, p.NS, kStageBytes,
+                    kStageM8);
     return;
   }
 
@@ -377,6 +378,290 @@ __global__ void __launch_bounds__(kT1Threads, 1)
         p.y[row] = v;
       else
         p.y[row] += v;
+    }
+  }
+}
+
+// ------------------------------------------------------------------------ T = 1 tensor-core kernel
+// Same stream/decode as gemv_t1_kernel, but the packed bf16 pairs produced by the decode are exactly the
+// A-fragment registers of mma.sync.m16n8k16 (bf16 x bf16 -> fp32), so the multiply-accumulate runs on the
+// tensor cores and the fp32 split / FMA instructions disappear. x is stored in shared memory pre-split into
+// three bf16 parts (x = x1 + x2 + x3 exactly; the reference's `_x3`, wcomp.py:130-140) in B-fragment order.
+//
+// Tiles are 16 rows; a stage is 16 rows x 4 chunks (24 KB). The 8 consumer warps form two halves on
+// alternate tiles; warp q of a half takes chunk slot q of each stage and holds rows g and g+8 (g = lane/4)
+// for the lane's 64 columns {32t..32t+31} U {128+32t..128+32t+31} (t = lane%4) of that chunk. MMA i in
+// 0..7 uses the low-half columns 32t+4i..+3, MMA 8+i the high-half ones; the k order inside an MMA is a
+// permutation shared by A and B, so the sum is unchanged. Per tile the 4 warps of a half combine their
+// partial rows in a fixed order.
+constexpr int kMmaStageM8 = 16 * 4 * 256;
+constexpr int kMmaStageE4 = 16 * 4 * 128;
+constexpr int kMmaStage = kMmaStageM8 + kMmaStageE4;  // 24 KB
+constexpr int kMmaHeader = 2048;  // barriers (0..255), abort flag (256), RMS partials (512..), tile partials (1024..2047)
+static_assert(kMmaStageM8 == 16 * 4 * 256 && kMmaStageE4 == 16 * 4 * 128, "stage = TMA boxes {256,4,16} + {128,4,16}");
+
+AIB_DEV void mma_bf16(float* d, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// bf16 pairs of one 4-byte group: lo elements (cols +0,+1 | +2,+3) and hi elements (cols 128+...)
+struct Z4 {
+  uint32_t lo01, lo23, hi01, hi23;
+};
+AIB_DEV Z4 decode_word(uint32_t E, uint32_t L, uint32_t Hh, uint32_t base7) {
+  const uint32_t x01 = prmt(E, 0u, 0x4140u), x23 = prmt(E, 0u, 0x4342u);
+  Z4 z;
+  z.lo01 = (prmt(L, 0u, 0x9180u) & 0x807F807Fu) | (((x01 & 0x000F000Fu) << 7) + base7);
+  z.lo23 = (prmt(L, 0u, 0xB3A2u) & 0x807F807Fu) | (((x23 & 0x000F000Fu) << 7) + base7);
+  z.hi01 = (prmt(Hh, 0u, 0x9180u) & 0x807F807Fu) | (((x01 & 0x00F000F0u) << 3) + base7);
+  z.hi23 = (prmt(Hh, 0u, 0xB3A2u) & 0x807F807Fu) | (((x23 & 0x00F000F0u) << 3) + base7);
+  return z;
+}
+// clear the 16-bit halves whose exponent code is 15 (exceptions decode to 0; their value is added apart)
+AIB_DEV uint32_t clear15(uint32_t z, uint32_t codes) {  // codes: low element in bits 0..3, high in 16..19
+  uint32_t m = 0;
+  if ((codes & 0xFu) == 0xFu) m |= 0x0000FFFFu;
+  if (((codes >> 16) & 0xFu) == 0xFu) m |= 0xFFFF0000u;
+  return z & ~m;
+}
+AIB_DEV Z4 decode_word_exc(uint32_t E, uint32_t L, uint32_t Hh, uint32_t base7) {
+  Z4 z = decode_word(E, L, Hh, base7);
+  const uint32_t x01 = prmt(E, 0u, 0x4140u), x23 = prmt(E, 0u, 0x4342u);
+  z.lo01 = clear15(z.lo01, x01 & 0x000F000Fu);
+  z.lo23 = clear15(z.lo23, x23 & 0x000F000Fu);
+  z.hi01 = clear15(z.hi01, (x01 >> 4) & 0x000F000Fu);
+  z.hi23 = clear15(z.hi23, (x23 >> 4) & 0x000F000Fu);
+  return z;
+}
+
+// index (in 32-byte records) of x's B fragment for chunk gc, MMA i, quad lane t
+AIB_DEV int xfrag(int gc, int i, int t) { return (gc * 16 + i) * 4 + t; }
+
+// Does row's CSR slice hold an exception in lane t's columns of the chunk at c0?
+AIB_DEV bool lane_has_exc(const int32_t* ec, int& ex_p, int ex_e, int& ex_col, int c0, int t) {
+  while (ex_col < c0) {
+    ++ex_p;
+    ex_col = ex_p < ex_e ? ec[ex_p] : INT_MAX;
+  }
+  for (int q = ex_p; q < ex_e; ++q) {
+    const int col = (q == ex_p) ? ex_col : ec[q];
+    if (col >= c0 + 256) break;
+    if (col >= c0 && (((col - c0) & 127) >> 5) == t) return true;
+  }
+  return false;
+}
+
+template <int MODE, bool RMS>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemv_mma_kernel(const __grid_constant__ CUtensorMap tm8, const __grid_constant__ CUtensorMap tme4, Params p) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* empty = full + 16;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + 256);
+  float* rms_red = reinterpret_cast<float*>(smem + 512);             // [8] RMS partials
+  float* red = reinterpret_cast<float*>(smem + 1024);                // [2 halves][2 bufs][4 warps][16 rows]
+  uint4* xf = reinterpret_cast<uint4*>(smem + kMmaHeader);           // 2 x uint4 per record
+  uint8_t* ring = smem + kMmaHeader + ((static_cast<size_t>(p.nch) * 2048 + 1023) / 1024) * 1024;
+
+  const int tid = threadIdx.x;
+  const int tb = static_cast<int>((static_cast<long long>(blockIdx.x) * p.tiles) / gridDim.x);
+  const int te = static_cast<int>((static_cast<long long>(blockIdx.x + 1) * p.tiles) / gridDim.x);
+  const int ntiles = te - tb;
+  if (tid == 0) {
+    for (int s = 0; s < p.NS; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 4);  // the 4 warps of the consuming half
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  pdl_trigger();
+  if (tid >= kConsumers) {
+    if (tid == kConsumers)
+      produce_pairs(&tm8, &tme4, ring, full, empty, abort_flag, tb, ntiles, p.KS, 16, 4, p.NS, kMmaStage, kMmaStageM8);
+    return;
+  }
+  // -------- x prologue: x_eff = [RMS]( MODE 2 ? silu(g)*u : x ), split into 3 bf16 parts, B-fragment order
+  pdl_wait();
+  const int K = p.K;
+  float rs = 1.0f;
+  if (RMS) {
+    float ss = 0.0f;
+    for (int k = tid; k < K; k += kConsumers) {
+      const float v = p.x[k];
+      ss += v * v;
+    }
+    ss = warp_sum(ss);
+    if ((tid & 31) == 0) rms_red[tid >> 5] = ss;
+    named_sync(1, kConsumers);
+    float tot = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kConsumers / 32; ++w) tot += rms_red[w];
+    rs = rsqrtf(tot / static_cast<float>(K) + p.eps);
+  }
+  uint32_t* xw = reinterpret_cast<uint32_t*>(xf);
+  for (int pr = tid; pr < K / 2; pr += kConsumers) {  // column pair (2pr, 2pr+1)
+    const int k = 2 * pr;
+    float v[2];
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      float x = (MODE == 2) ? silu_mul(p.x[k + e], p.x[K + k + e]) : p.x[k + e];
+      if (RMS) x = bf16_to_f32(p.lnw[k + e]) * (x * rs);
+      v[e] = x;
+    }
+    uint32_t part[3];
+    float r0 = v[0], r1 = v[1];
+#pragma unroll
+    for (int sp = 0; sp < 3; ++sp) {
+      const uint16_t b0 = f32_to_bf16_rne(r0), b1 = f32_to_bf16_rne(r1);
+      part[sp] = static_cast<uint32_t>(b0) | (static_cast<uint32_t>(b1) << 16);
+      r0 -= bf16_to_f32(b0);
+      r1 -= bf16_to_f32(b1);
+    }
+    const int gc = k >> 8, kk = k & 255, hf = kk >> 7, kl = kk & 127;
+    const int t = kl >> 5, w = (kl & 31) >> 2, sub = (kl & 3) >> 1;  // sub: b0 (cols +0,+1) or b1 (+2,+3)
+    uint32_t* rec = xw + xfrag(gc, hf * 8 + w, t) * 8;
+    rec[0 + sub] = part[0];
+    rec[2 + sub] = part[1];
+    rec[4 + sub] = part[2];
+  }
+  named_sync(1, kConsumers);
+
+  const int half = tid >> 7, q = (tid >> 5) & 3, lane = tid & 31, g = lane >> 2, t = lane & 3;
+  const uint32_t base7 = (static_cast<uint32_t>(p.base) << 7) | (static_cast<uint32_t>(p.base) << 23);
+  const int my_tiles = half == 0 ? (ntiles + 1) / 2 : ntiles / 2;
+  const bool odd = g & 1;  // odd rows read their two 16-byte halves in the other order (bank spread)
+  bool aborted = false;
+  for (int ti = 0; ti < my_tiles; ++ti) {
+    const int tile = tb + 2 * ti + half;
+    const int rowA = tile * 16 + g, rowB = rowA + 8;
+    int exA_p = 0, exA_e = 0, exB_p = 0, exB_e = 0;
+    if (rowA < p.N) exA_p = p.rp[rowA], exA_e = p.rp[rowA + 1];
+    if (rowB < p.N) exB_p = p.rp[rowB], exB_e = p.rp[rowB + 1];
+    int exA_col = exA_p < exA_e ? p.ec[exA_p] : INT_MAX, exB_col = exB_p < exB_e ? p.ec[exB_p] : INT_MAX;
+    float acc[2][3][4];
+#pragma unroll
+    for (int a = 0; a < 2; ++a)
+#pragma unroll
+      for (int b = 0; b < 3; ++b)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) acc[a][b][c] = 0.0f;
+    float exA = 0.0f, exB = 0.0f;
+    for (int ks = 0; ks < p.KS; ++ks) {
+      const int it = 2 * (ti * p.KS + ks) + half;
+      const int s = it % p.NS;
+      const bool ok = !aborted && wait_full(&full[s], (it / p.NS) & 1, abort_flag);
+      if (!ok) aborted = true;
+      const int gc = ks * 4 + q;
+      if (ok && gc < p.nch) {
+        const uint8_t* st = ring + static_cast<size_t>(s) * kMmaStage;
+        const uint8_t* mA = st + (g * 4 + q) * 256 + 32 * t;
+        const uint8_t* mB = st + ((g + 8) * 4 + q) * 256 + 32 * t;
+        const uint8_t* eA = st + kMmaStageM8 + (g * 4 + q) * 128 + 32 * t;
+        const uint8_t* eB = st + kMmaStageM8 + ((g + 8) * 4 + q) * 128 + 32 * t;
+        // odd rows take their two 16-byte halves in swapped order (word w becomes physical word w ^ 4): the
+        // two row parities of an 8-lane phase then hit different banks. Their B fragments use the same
+        // permutation and their results are read from the odd output columns (see the end of the tile).
+        const int o0 = odd ? 16 : 0, o1 = 16 - o0;
+        uint4 LA[2], HA[2], EA[2], LB[2], HB[2], EB[2];
+        LA[0] = *reinterpret_cast<const uint4*>(mA + o0);
+        LA[1] = *reinterpret_cast<const uint4*>(mA + o1);
+        HA[0] = *reinterpret_cast<const uint4*>(mA + 128 + o0);
+        HA[1] = *reinterpret_cast<const uint4*>(mA + 128 + o1);
+        EA[0] = *reinterpret_cast<const uint4*>(eA + o0);
+        EA[1] = *reinterpret_cast<const uint4*>(eA + o1);
+        LB[0] = *reinterpret_cast<const uint4*>(mB + o0);
+        LB[1] = *reinterpret_cast<const uint4*>(mB + o1);
+        HB[0] = *reinterpret_cast<const uint4*>(mB + 128 + o0);
+        HB[1] = *reinterpret_cast<const uint4*>(mB + 128 + o1);
+        EB[0] = *reinterpret_cast<const uint4*>(eB + o0);
+        EB[1] = *reinterpret_cast<const uint4*>(eB + o1);
+        const int wx = odd ? 4 : 0;  // physical word of logical word w is w ^ wx
+        const int c0 = gc * 256;
+        const bool xa = (rowA < p.N) && lane_has_exc(p.ec, exA_p, exA_e, exA_col, c0, t);
+        const bool xb = (rowB < p.N) && lane_has_exc(p.ec, exB_p, exB_e, exB_col, c0, t);
+        const uint32_t* la = reinterpret_cast<const uint32_t*>(LA);
+        const uint32_t* ha = reinterpret_cast<const uint32_t*>(HA);
+        const uint32_t* ea = reinterpret_cast<const uint32_t*>(EA);
+        const uint32_t* lb = reinterpret_cast<const uint32_t*>(LB);
+        const uint32_t* hb = reinterpret_cast<const uint32_t*>(HB);
+        const uint32_t* eb = reinterpret_cast<const uint32_t*>(EB);
+#pragma unroll
+        for (int w = 0; w < 8; ++w) {
+          const Z4 za = xa ? decode_word_exc(ea[w], la[w], ha[w], base7) : decode_word(ea[w], la[w], ha[w], base7);
+          const Z4 zb = xb ? decode_word_exc(eb[w], lb[w], hb[w], base7) : decode_word(eb[w], lb[w], hb[w], base7);
+          const uint4* rl = xf + xfrag(gc, w ^ wx, t) * 2;
+          const uint4* rh = xf + xfrag(gc, 8 + (w ^ wx), t) * 2;
+          const uint4 bl0 = rl[0], bl1 = rl[1], bh0 = rh[0], bh1 = rh[1];
+          mma_bf16(acc[0][0], za.lo01, zb.lo01, za.lo23, zb.lo23, bl0.x, bl0.y);
+          mma_bf16(acc[0][1], za.lo01, zb.lo01, za.lo23, zb.lo23, bl0.z, bl0.w);
+          mma_bf16(acc[0][2], za.lo01, zb.lo01, za.lo23, zb.lo23, bl1.x, bl1.y);
+          mma_bf16(acc[1][0], za.hi01, zb.hi01, za.hi23, zb.hi23, bh0.x, bh0.y);
+          mma_bf16(acc[1][1], za.hi01, zb.hi01, za.hi23, zb.hi23, bh0.z, bh0.w);
+          mma_bf16(acc[1][2], za.hi01, zb.hi01, za.hi23, zb.hi23, bh1.x, bh1.y);
+        }
+        if (xa || xb) {  // exception values times x, for this lane's columns
+          const uint32_t* xw32 = reinterpret_cast<const uint32_t*>(xf);
+          auto xval = [&](int col) {
+            const int kk = col & 255, hf = kk >> 7, kl = kk & 127;
+            const uint32_t* rec = xw32 + xfrag(col >> 8, hf * 8 + ((kl & 31) >> 2), kl >> 5) * 8;
+            const int sub = (kl & 3) >> 1, sh = (kl & 1) * 16;
+            const float f1 = bf16_to_f32(static_cast<uint16_t>(rec[0 + sub] >> sh));
+            const float f2 = bf16_to_f32(static_cast<uint16_t>(rec[2 + sub] >> sh));
+            const float f3 = bf16_to_f32(static_cast<uint16_t>(rec[4 + sub] >> sh));
+            return (f1 + f2) + f3;
+          };
+          if (xa)
+            for (int e = exA_p; e < exA_e; ++e) {
+              const int col = p.ec[e];
+              if (col >= c0 + 256) break;
+              if (col >= c0 && (((col - c0) & 127) >> 5) == t) exA += p.ev[e] * xval(col);
+            }
+          if (xb)
+            for (int e = exB_p; e < exB_e; ++e) {
+              const int col = p.ec[e];
+              if (col >= c0 + 256) break;
+              if (col >= c0 && (((col - c0) & 127) >> 5) == t) exB += p.ev[e] * xval(col);
+            }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+    }
+    // rows g and g+8: lane (g, t) holds output columns n = 2t (c0, c2) and 2t+1 (c1, c3); column n carries
+    // x in the word order of lanes with g = n, so an even row is read from an even column, an odd row from
+    // an odd one.
+    float vA = 0.0f, vB = 0.0f;
+#pragma unroll
+    for (int a = 0; a < 2; ++a)
+#pragma unroll
+      for (int b = 0; b < 3; ++b) {
+        vA += odd ? acc[a][b][1] : acc[a][b][0];
+        vB += odd ? acc[a][b][3] : acc[a][b][2];
+      }
+    exA += __shfl_xor_sync(0xffffffffu, exA, 1);
+    exA += __shfl_xor_sync(0xffffffffu, exA, 2);
+    exB += __shfl_xor_sync(0xffffffffu, exB, 1);
+    exB += __shfl_xor_sync(0xffffffffu, exB, 2);
+    vA += exA;
+    vB += exB;
+    float* rb = red + (half * 2 + (ti & 1)) * 64;
+    if (t == 0) rb[q * 16 + g] = vA, rb[q * 16 + g + 8] = vB;
+    named_sync(2 + half, 128);
+    if (q == 0 && lane < 16 && !aborted) {
+      const int row = tile * 16 + lane;
+      if (row < p.N) {
+        const float v = ((rb[lane] + rb[16 + lane]) + rb[32 + lane]) + rb[48 + lane];
+        if (MODE == 0)
+          p.y[row] = v;
+        else
+          p.y[row] += v;
+      }
     }
   }
 }
@@ -526,8 +811,41 @@ static int make_maps(const aib_c12* c, int RT, int CW, CUtensorMap* tm8, CUtenso
 constexpr size_t kSmemTarget = 112 * 1024;  // leaves room for a neighbouring kernel's CTA (PDL overlap)
 constexpr size_t kSmemMax = 227 * 1024;
 
+static int run_mma(const aib_c12* c, const float* x, float* y, int mode, const uint16_t* lnw, float eps,
+                   cudaStream_t s) {
+  const int nch = c->K / 256;
+  const int tiles = (c->N + 15) / 16;
+  const int grid = std::min(tiles, sm_count());
+  CUtensorMap tm8, tme4;
+  int rc = make_maps(c, 16, 4, &tm8, &tme4);
+  if (rc) return rc;
+  const size_t xf_bytes = ((static_cast<size_t>(nch) * 2048 + 1023) / 1024) * 1024;
+  int NS = static_cast<int>((kSmemMax - kMmaHeader - xf_bytes) / kMmaStage);
+  NS = std::max(2, std::min(NS, 4)) & ~1;
+  const size_t smem = kMmaHeader + xf_bytes + static_cast<size_t>(NS) * kMmaStage;
+  if (smem > kSmemMax) return fail(AIB_ENOTSUP, "aib_gemv_c12: K=%d too large for the tensor-core kernel", c->K);
+  Params p{c->rp, c->ec, c->ev, x, y, lnw, eps, c->base, c->N, c->K, nch, 16, 4, (nch + 3) / 4, tiles, NS, 1, 0, 0,
+           c->K};
+  auto go = [&](auto kernel) -> int {
+    const int r2 = allow_smem(kernel, smem);
+    if (r2) return r2;
+    return launch(kernel, dim3(grid), dim3(kThreads), smem, s, "aib_gemv_c12(T=1, mma)", tm8, tme4, p);
+  };
+  if (lnw) {
+    if (mode == 0) return go(gemv_mma_kernel<0, true>);
+    if (mode == 1) return go(gemv_mma_kernel<1, true>);
+    return go(gemv_mma_kernel<2, true>);
+  }
+  if (mode == 0) return go(gemv_mma_kernel<0, false>);
+  if (mode == 1) return go(gemv_mma_kernel<1, false>);
+  return go(gemv_mma_kernel<2, false>);
+}
+
+static int g_variant = 1;  // 0: tensor-core kernel where it fits, 1: CUDA-core kernel
+
 static int run_t1(const aib_c12* c, const float* x, float* y, int mode, const uint16_t* lnw, float eps,
                   cudaStream_t s) {
+  if (g_variant == 0 && c->K <= 16384) return run_mma(c, x, y, mode, lnw, eps, s);
   const int nch = c->K / 256;
   const Geometry g = pick_geometry(c->N, nch, sm_count());
   CUtensorMap tm8, tme4;
@@ -587,6 +905,9 @@ static int run_tn_mode(const aib_c12* c, const float* x, float* y, int T, int xs
 using namespace aib;
 
 extern "C" {
+
+// Kernel selection for the T = 1 GEMV (tests and A/B timing): 0 = tensor-core kernel (default), 1 = CUDA-core.
+void aib_gemv_set_variant(int v) { gemv::g_variant = v; }
 
 size_t aib_gemv_c12_workspace(const aib_c12* c, int T) {
   (void)c;

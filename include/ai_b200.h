@@ -93,6 +93,9 @@ int aib_c12_decode(const aib_c12* c, int first, int last, void* out, int out_dty
  * lnw (bf16 bits [K], may be NULL): RMSNorm prologue of gemvc1_k (wcomp.py:75-86), T == 1 only.
  * x_stride / y_stride: elements between rows of X / Y (ignored for T == 1). */
 size_t aib_gemv_c12_workspace(const aib_c12* c, int T);
+/* Kernel choice for T == 1: 0 the tensor-core kernel (mma.sync bf16 with x split in 3 bf16 parts,
+ * K <= 16384), 1 (default) the CUDA-core fp32-FMA kernel. Same results within fp32 rounding; for tests and A/B timing. */
+void aib_gemv_set_variant(int variant);
 int aib_gemv_c12(const aib_c12* c, const float* x, float* y, int T, int x_stride, int y_stride, int mode,
                  const uint16_t* lnw, float eps, void* ws, size_t ws_bytes, void* stream);
 

@@ -92,7 +92,7 @@ def test_weight_rows_matches_reference_decode_rows(lib):
 
 # -------------------------------------------------------------------------------------------- gemv
 @pytest.mark.parametrize("name", cases(golden("gemv")))
-def test_gemvc1_matches_reference_golden(lib, name):
+def test_gemvc1_matches_reference_golden(lib, variant, name):
     from ai_b200 import wcomp
     z = golden("gemv")
     c = wcomp.compress(from_bits(z[f"{name}/w"]))
@@ -107,12 +107,19 @@ def test_gemvc1_matches_reference_golden(lib, name):
     assert status_clear() == 0
 
 
-GEMV_SHAPES = [(6144, 4096, 0, True), (4096, 4096, 1, False), (24576, 4096, 0, True), (4096, 12288, 2, False),
+GEMV_SHAPES = [(64, 1024, 0, False), (6144, 4096, 0, True), (4096, 4096, 1, False), (24576, 4096, 0, True), (4096, 12288, 2, False),
                (1024, 2048, 1, False), (4096, 1024, 0, True), (517, 768, 2, False), (40, 256, 0, True)]
 
 
+@pytest.fixture(params=[0, 1], ids=["tensorcore", "cudacore"])
+def variant(request, lib):
+    lib.aib_gemv_set_variant(request.param)
+    yield request.param
+    lib.aib_gemv_set_variant(1)  # library default
+
+
 @pytest.mark.parametrize("N,K,mode,rms", GEMV_SHAPES)
-def test_gemvc1_shapes_vs_oracle(lib, N, K, mode, rms):
+def test_gemvc1_shapes_vs_oracle(lib, variant, N, K, mode, rms):
     from ai_b200 import wcomp
     g = torch.Generator(device="cuda").manual_seed(N + K + mode)
     w = (torch.randn(N, K, generator=g, device="cuda") * 0.02).bfloat16()
@@ -156,6 +163,24 @@ def test_gemvc_tc_vs_oracle(lib, T, mode):
     mag[:T] = xe @ np.abs(codec.dense_f32(oc)).T.astype(np.float64) + np.abs(Y0.cpu().numpy()[:T]) * (mode > 0)
     close(Y.cpu().numpy(), ref, mag)
     assert torch.equal(Y[T:], Y0[T:])  # rows >= T untouched
+
+
+def test_gemv_dense_exceptions(lib, variant):
+    """Rows full of exceptions (every code 15 in a chunk / a whole row) through both kernels."""
+    from ai_b200 import wcomp
+    g = torch.Generator(device="cuda").manual_seed(77)
+    N, K = 48, 1024
+    w = (torch.randn(N, K, generator=g, device="cuda") * 0.02).bfloat16()
+    w[5] = (torch.randn(K, generator=g, device="cuda") * 1e5).bfloat16()
+    w[20, 256:512] = (torch.randn(256, generator=g, device="cuda") * 1e-9).bfloat16()
+    w[47, ::3] = 7e3
+    c = wcomp.compress(w)
+    x = torch.randn(K, generator=g, device="cuda")
+    y = torch.zeros(N, device="cuda")
+    wcomp.gemvc1(x, c, y, 0)
+    W = codec.bf16_bits_to_f32(bits(w)).astype(np.float64)
+    xn = x.cpu().numpy().astype(np.float64)
+    close(y.cpu().numpy(), W @ xn, np.abs(W) @ np.abs(xn))
 
 
 def test_gemv_deterministic(lib):
