@@ -50,6 +50,8 @@ struct Params {
   int NS;
   int T, x_stride, y_stride;
   int xs_floats;
+  int meta_rows;  // rows per CTA covered by the shared row-metadata arrays (tensor-core kernel)
+  int ring_off;   // byte offset of the stage ring in shared memory (tensor-core kernel)
 };
 
 // permuted index of column k in the shared x buffer (see file comment)
@@ -208,40 +210,41 @@ constexpr int kT1Threads = kT1Consumers + 32;
 AIB_DEV void produce_pairs(const CUtensorMap* tm8, const CUtensorMap* tme4, uint8_t* ring, uint64_t* full,
                            uint64_t* empty, volatile int* abort_flag, int tb, int ntiles, int KS, int RT, int CW,
                            int NS, uint32_t stage_bytes, uint32_t e4_off) {
+  // Half h owns ring slots h, h+2, h+4, ...; its j-th stage (tile 2*(j/KS)+h, chunk group j%KS) goes to slot
+  // h + 2*(j % (NS/2)), use j / (NS/2). The two halves are served in whatever order their slots free up, so
+  // a lagging half never starves the other.
   prefetch_tensormap(tm8);
   prefetch_tensormap(tme4);
-  const int n0 = (ntiles + 1) / 2;  // tiles of group 0 (group 1 has ntiles / 2)
-  const int n_it = 2 * n0 * KS;
-  int issued = 0;
-  for (int it = 0; it < n_it; ++it) {
-    const int g = it & 1, i = it >> 1;
-    const int lt = 2 * (i / KS) + g;  // local tile index
-    if (lt >= ntiles) continue;       // group 1 has no tile here (only at the very end)
-    const int s = it % NS;
-    if (it >= NS) {
-      bool ok = false;
-      for (uint32_t k = 0; k < kSpinLimit && !ok; ++k) {
-        ok = mbar_try_wait(&empty[s], ((it / NS) - 1) & 1);
-        if (!ok && *abort_flag) break;
-      }
-      if (!ok) {
-        if (!*abort_flag) set_status(AIB_DEV_TIMEOUT_EMPTY);
-        *abort_flag = 1;
-        break;
-      }
+  const int per = NS / 2;
+  int n[2] = {((ntiles + 1) / 2) * KS, (ntiles / 2) * KS};
+  int j[2] = {0, 0};
+  uint32_t idle = 0;
+  while ((j[0] < n[0] || j[1] < n[1]) && !*abort_flag) {
+    bool progressed = false;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      if (j[h] >= n[h]) continue;
+      const int s = h + 2 * (j[h] % per), use = j[h] / per;
+      if (use > 0 && !mbar_try_wait(&empty[s], (use - 1) & 1)) continue;
+      const int tile = tb + 2 * (j[h] / KS) + h, ks = j[h] % KS;
+      uint8_t* st = ring + static_cast<size_t>(s) * stage_bytes;
+      mbar_arrive_expect_tx(&full[s], stage_bytes);
+      tma_load_3d(st, tm8, &full[s], 0, ks * CW, tile * RT);
+      tma_load_3d(st + e4_off, tme4, &full[s], 0, ks * CW, tile * RT);
+      ++j[h];
+      progressed = true;
     }
-    const int tile = tb + lt, ks = i % KS;
-    uint8_t* st = ring + static_cast<size_t>(s) * stage_bytes;
-    mbar_arrive_expect_tx(&full[s], stage_bytes);
-    tma_load_3d(st, tm8, &full[s], 0, ks * CW, tile * RT);
-    tma_load_3d(st + e4_off, tme4, &full[s], 0, ks * CW, tile * RT);
-    issued = it + 1;
+    idle = progressed ? 0 : idle + 1;
+    if (idle > kSpinLimit) {
+      set_status(AIB_DEV_TIMEOUT_EMPTY);
+      *abort_flag = 1;
+    }
   }
+  // Never leave with copies in flight: on the abort path wait (bounded) for the last issued use of every slot.
   if (*abort_flag) {
-    for (int it = (issued > NS ? issued - NS : 0); it < issued; ++it) {
-      const int g = it & 1, i = it >> 1;
-      if (2 * (i / KS) + g < ntiles) mbar_wait(&full[it % NS], (it / NS) & 1, AIB_DEV_TIMEOUT_FULL);
-    }
+    for (int h = 0; h < 2; ++h)
+      for (int k = (j[h] > per ? j[h] - per : 0); k < j[h]; ++k)
+        mbar_wait(&full[h + 2 * (k % per)], (k / per) & 1, AIB_DEV_TIMEOUT_FULL);
   }
 }
 
@@ -250,7 +253,7 @@ __global__ void __launch_bounds__(kT1Threads, 1)
     gemv_t1_kernel(const __grid_constant__ CUtensorMap tm8, const __grid_constant__ CUtensorMap tme4, Params p) {
   extern __shared__ __align__(1024) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
-  uint64_t* empty = full + 16;
+  uint64_t* empty = full + 16;  // up to 16 ring slots
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + 256);
   float* red = reinterpret_cast<float*>(smem + 512);  // RMS partials
   float* xs = reinterpret_cast<float*>(smem + kHeader);
@@ -397,7 +400,9 @@ __global__ void __launch_bounds__(kT1Threads, 1)
 constexpr int kMmaStageM8 = 16 * 4 * 256;
 constexpr int kMmaStageE4 = 16 * 4 * 128;
 constexpr int kMmaStage = kMmaStageM8 + kMmaStageE4;  // 24 KB
-constexpr int kMmaHeader = 2048;  // barriers (0..255), abort flag (256), RMS partials (512..), tile partials (1024..2047)
+constexpr int kMmaHeader = 4096;  // barriers (0..255), abort flag (256), RMS partials (512..), tile partials (1024..3071)
+constexpr int kMmaConsumers = 512;  // 16 warps: 2 halves (alternate tiles) x 4 chunk slots x 2 column halves
+constexpr int kMmaThreads = kMmaConsumers + 32;
 static_assert(kMmaStageM8 == 16 * 4 * 256 && kMmaStageE4 == 16 * 4 * 128, "stage = TMA boxes {256,4,16} + {128,4,16}");
 
 AIB_DEV void mma_bf16(float* d, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1) {
@@ -408,19 +413,6 @@ AIB_DEV void mma_bf16(float* d, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t 
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// bf16 pairs of one 4-byte group: lo elements (cols +0,+1 | +2,+3) and hi elements (cols 128+...)
-struct Z4 {
-  uint32_t lo01, lo23, hi01, hi23;
-};
-AIB_DEV Z4 decode_word(uint32_t E, uint32_t L, uint32_t Hh, uint32_t base7) {
-  const uint32_t x01 = prmt(E, 0u, 0x4140u), x23 = prmt(E, 0u, 0x4342u);
-  Z4 z;
-  z.lo01 = (prmt(L, 0u, 0x9180u) & 0x807F807Fu) | (((x01 & 0x000F000Fu) << 7) + base7);
-  z.lo23 = (prmt(L, 0u, 0xB3A2u) & 0x807F807Fu) | (((x23 & 0x000F000Fu) << 7) + base7);
-  z.hi01 = (prmt(Hh, 0u, 0x9180u) & 0x807F807Fu) | (((x01 & 0x00F000F0u) << 3) + base7);
-  z.hi23 = (prmt(Hh, 0u, 0xB3A2u) & 0x807F807Fu) | (((x23 & 0x00F000F0u) << 3) + base7);
-  return z;
-}
 // clear the 16-bit halves whose exponent code is 15 (exceptions decode to 0; their value is added apart)
 AIB_DEV uint32_t clear15(uint32_t z, uint32_t codes) {  // codes: low element in bits 0..3, high in 16..19
   uint32_t m = 0;
@@ -428,44 +420,69 @@ AIB_DEV uint32_t clear15(uint32_t z, uint32_t codes) {  // codes: low element in
   if (((codes >> 16) & 0xFu) == 0xFu) m |= 0xFFFF0000u;
   return z & ~m;
 }
-AIB_DEV Z4 decode_word_exc(uint32_t E, uint32_t L, uint32_t Hh, uint32_t base7) {
-  Z4 z = decode_word(E, L, Hh, base7);
-  const uint32_t x01 = prmt(E, 0u, 0x4140u), x23 = prmt(E, 0u, 0x4342u);
-  z.lo01 = clear15(z.lo01, x01 & 0x000F000Fu);
-  z.lo23 = clear15(z.lo23, x23 & 0x000F000Fu);
-  z.hi01 = clear15(z.hi01, (x01 >> 4) & 0x000F000Fu);
-  z.hi23 = clear15(z.hi23, (x23 >> 4) & 0x000F000Fu);
-  return z;
+// Byte offset of x's B-fragment piece u (0: split0 b0,b1 + split1 b0,b1; 1: split2 b0,b1) for chunk gc,
+// MMA index i (0..15) and quad lane t. MMA i and i^4 are the two word orders used by even / odd rows, so
+// their records interleave: one 16-byte load of a warp touches 8 distinct 16-byte slots of one 128-byte
+// line -- no bank conflicts.
+AIB_DEV int xrec(int gc, int i, int t, int u) {
+  const int pi = (i & 3) | ((i >> 3) << 2), par = (i >> 2) & 1;
+  return gc * 2048 + pi * 256 + u * 128 + (t * 2 + par) * 16;
 }
 
-// index (in 32-byte records) of x's B fragment for chunk gc, MMA i, quad lane t
-AIB_DEV int xfrag(int gc, int i, int t) { return (gc * 16 + i) * 4 + t; }
-
-// Does row's CSR slice hold an exception in lane t's columns of the chunk at c0?
-AIB_DEV bool lane_has_exc(const int32_t* ec, int& ex_p, int ex_e, int& ex_col, int c0, int t) {
-  while (ex_col < c0) {
+// Does the row's CSR slice hold an exception in columns [lo, lo + 32)? (ex_p / ex_col advance monotonically)
+AIB_DEV bool lane_has_exc(const int32_t* ec, int& ex_p, int ex_e, int& ex_col, int lo) {
+  while (ex_col < lo - 256) {  // skip exceptions of earlier chunks (keep this chunk's, any column)
     ++ex_p;
     ex_col = ex_p < ex_e ? ec[ex_p] : INT_MAX;
   }
   for (int q = ex_p; q < ex_e; ++q) {
     const int col = (q == ex_p) ? ex_col : ec[q];
-    if (col >= c0 + 256) break;
-    if (col >= c0 && (((col - c0) & 127) >> 5) == t) return true;
+    if (col >= lo + 32) break;
+    if (col >= lo) return true;
   }
   return false;
 }
 
+// bf16 pairs of one 4-byte group of a column half (hs = 0: low nibbles / columns c..c+3, 1: high nibbles)
+struct Z2 {
+  uint32_t z01, z23;
+};
+AIB_DEV Z2 decode_half(uint32_t E, uint32_t M, uint32_t base7, int hs, bool exc) {
+  const uint32_t x01 = prmt(E, 0u, 0x4140u), x23 = prmt(E, 0u, 0x4342u);
+  const uint32_t c01 = hs ? (x01 >> 4) & 0x000F000Fu : x01 & 0x000F000Fu;
+  const uint32_t c23 = hs ? (x23 >> 4) & 0x000F000Fu : x23 & 0x000F000Fu;
+  Z2 z;
+  z.z01 = (prmt(M, 0u, 0x9180u) & 0x807F807Fu) | ((c01 << 7) + base7);
+  z.z23 = (prmt(M, 0u, 0xB3A2u) & 0x807F807Fu) | ((c23 << 7) + base7);
+  if (exc) {
+    z.z01 = clear15(z.z01, c01);
+    z.z23 = clear15(z.z23, c23);
+  }
+  return z;
+}
+
+// The CTA's row pointers rp[r0 .. r0+nr] and each row's first exception column, into shared memory.
+// They are weights (never written by an earlier kernel), so this runs before the grid-dependency wait.
+AIB_DEV void load_row_meta(const Params& p, int r0, int nr, int* rps, int* fcs, int nthreads) {
+  for (int i = threadIdx.x; i <= nr; i += nthreads) rps[i] = p.rp[min(r0 + i, p.N)];
+  named_sync(1, nthreads);
+  for (int i = threadIdx.x; i < nr; i += nthreads) fcs[i] = (rps[i] < rps[i + 1]) ? p.ec[rps[i]] : INT_MAX;
+  named_sync(1, nthreads);
+}
+
 template <int MODE, bool RMS>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kMmaThreads, 1)
     gemv_mma_kernel(const __grid_constant__ CUtensorMap tm8, const __grid_constant__ CUtensorMap tme4, Params p) {
   extern __shared__ __align__(1024) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
-  uint64_t* empty = full + 16;
+  uint64_t* empty = full + 16;  // up to 16 ring slots
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + 256);
-  float* rms_red = reinterpret_cast<float*>(smem + 512);             // [8] RMS partials
-  float* red = reinterpret_cast<float*>(smem + 1024);                // [2 halves][2 bufs][4 warps][16 rows]
-  uint4* xf = reinterpret_cast<uint4*>(smem + kMmaHeader);           // 2 x uint4 per record
-  uint8_t* ring = smem + kMmaHeader + ((static_cast<size_t>(p.nch) * 2048 + 1023) / 1024) * 1024;
+  float* rms_red = reinterpret_cast<float*>(smem + 512);                // [16] RMS partials
+  float* red = reinterpret_cast<float*>(smem + 1024);                   // [2 halves][2 bufs][8 warps][16 rows]
+  uint8_t* xf = smem + kMmaHeader;                                        // x fragments, 2048 B per chunk
+  int* rps = reinterpret_cast<int*>(xf + static_cast<size_t>(p.nch) * 2048);  // row pointers of the CTA's rows
+  int* fcs = rps + p.meta_rows + 1;                                       // first exception column per row
+  uint8_t* ring = smem + p.ring_off;
 
   const int tid = threadIdx.x;
   const int tb = static_cast<int>((static_cast<long long>(blockIdx.x) * p.tiles) / gridDim.x);
@@ -474,38 +491,40 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (tid == 0) {
     for (int s = 0; s < p.NS; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 4);  // the 4 warps of the consuming half
+      mbar_init(&empty[s], 8);  // the 8 warps of the consuming half
     }
     *abort_flag = 0;
     fence_mbar_init();
   }
   __syncthreads();
   pdl_trigger();
-  if (tid >= kConsumers) {
-    if (tid == kConsumers)
+  if (tid >= kMmaConsumers) {
+    if (tid == kMmaConsumers)
       produce_pairs(&tm8, &tme4, ring, full, empty, abort_flag, tb, ntiles, p.KS, 16, 4, p.NS, kMmaStage, kMmaStageM8);
     return;
   }
+  // row metadata (weights, independent of earlier kernels): load before waiting on them
+  const int r0 = tb * 16, nr = ntiles * 16;
+  load_row_meta(p, r0, nr, rps, fcs, kMmaConsumers);
   // -------- x prologue: x_eff = [RMS]( MODE 2 ? silu(g)*u : x ), split into 3 bf16 parts, B-fragment order
   pdl_wait();
   const int K = p.K;
   float rs = 1.0f;
   if (RMS) {
     float ss = 0.0f;
-    for (int k = tid; k < K; k += kConsumers) {
+    for (int k = tid; k < K; k += kMmaConsumers) {
       const float v = p.x[k];
       ss += v * v;
     }
     ss = warp_sum(ss);
     if ((tid & 31) == 0) rms_red[tid >> 5] = ss;
-    named_sync(1, kConsumers);
+    named_sync(1, kMmaConsumers);
     float tot = 0.0f;
 #pragma unroll
-    for (int w = 0; w < kConsumers / 32; ++w) tot += rms_red[w];
+    for (int w = 0; w < kMmaConsumers / 32; ++w) tot += rms_red[w];
     rs = rsqrtf(tot / static_cast<float>(K) + p.eps);
   }
-  uint32_t* xw = reinterpret_cast<uint32_t*>(xf);
-  for (int pr = tid; pr < K / 2; pr += kConsumers) {  // column pair (2pr, 2pr+1)
+  for (int pr = tid; pr < K / 2; pr += kMmaConsumers) {  // column pair (2pr, 2pr+1)
     const int k = 2 * pr;
     float v[2];
 #pragma unroll
@@ -515,35 +534,40 @@ __global__ void __launch_bounds__(kThreads, 1)
       v[e] = x;
     }
     uint32_t part[3];
-    float r0 = v[0], r1 = v[1];
+    float r0x = v[0], r1x = v[1];
 #pragma unroll
     for (int sp = 0; sp < 3; ++sp) {
-      const uint16_t b0 = f32_to_bf16_rne(r0), b1 = f32_to_bf16_rne(r1);
+      const uint16_t b0 = f32_to_bf16_rne(r0x), b1 = f32_to_bf16_rne(r1x);
       part[sp] = static_cast<uint32_t>(b0) | (static_cast<uint32_t>(b1) << 16);
-      r0 -= bf16_to_f32(b0);
-      r1 -= bf16_to_f32(b1);
+      r0x -= bf16_to_f32(b0);
+      r1x -= bf16_to_f32(b1);
     }
     const int gc = k >> 8, kk = k & 255, hf = kk >> 7, kl = kk & 127;
     const int t = kl >> 5, w = (kl & 31) >> 2, sub = (kl & 3) >> 1;  // sub: b0 (cols +0,+1) or b1 (+2,+3)
-    uint32_t* rec = xw + xfrag(gc, hf * 8 + w, t) * 8;
-    rec[0 + sub] = part[0];
-    rec[2 + sub] = part[1];
-    rec[4 + sub] = part[2];
+    const int i = hf * 8 + w;
+    uint32_t* u0 = reinterpret_cast<uint32_t*>(xf + xrec(gc, i, t, 0));
+    uint32_t* u1 = reinterpret_cast<uint32_t*>(xf + xrec(gc, i, t, 1));
+    u0[0 + sub] = part[0];  // uint4 0: split0 (b0, b1), split1 (b0, b1)
+    u0[2 + sub] = part[1];
+    u1[0 + sub] = part[2];  // uint4 1: split2 (b0, b1), unused
   }
-  named_sync(1, kConsumers);
+  named_sync(1, kMmaConsumers);
 
-  const int half = tid >> 7, q = (tid >> 5) & 3, lane = tid & 31, g = lane >> 2, t = lane & 3;
+  const int half = tid >> 8, wh = (tid >> 5) & 7, q = wh & 3, hs = wh >> 2;
+  const int lane = tid & 31, g = lane >> 2, t = lane & 3;
   const uint32_t base7 = (static_cast<uint32_t>(p.base) << 7) | (static_cast<uint32_t>(p.base) << 23);
   const int my_tiles = half == 0 ? (ntiles + 1) / 2 : ntiles / 2;
-  const bool odd = g & 1;  // odd rows read their two 16-byte halves in the other order (bank spread)
+  const bool odd = g & 1;
+  const int o0 = odd ? 16 : 0, o1 = 16 - o0;  // odd rows read their 16-byte halves swapped (bank spread)
+  const int wx = odd ? 4 : 0;                 // ... so their logical word w is physical word w ^ 4
+  const int colbase = hs * 128 + 32 * t;      // the lane's 32 columns inside a chunk
   bool aborted = false;
   for (int ti = 0; ti < my_tiles; ++ti) {
     const int tile = tb + 2 * ti + half;
-    const int rowA = tile * 16 + g, rowB = rowA + 8;
-    int exA_p = 0, exA_e = 0, exB_p = 0, exB_e = 0;
-    if (rowA < p.N) exA_p = p.rp[rowA], exA_e = p.rp[rowA + 1];
-    if (rowB < p.N) exB_p = p.rp[rowB], exB_e = p.rp[rowB + 1];
-    int exA_col = exA_p < exA_e ? p.ec[exA_p] : INT_MAX, exB_col = exB_p < exB_e ? p.ec[exB_p] : INT_MAX;
+    const int lrA = (2 * ti + half) * 16 + g, lrB = lrA + 8;  // rows relative to the CTA's first row
+    const int rowA = r0 + lrA, rowB = r0 + lrB;
+    int exA_p = rps[lrA], exA_e = rps[lrA + 1], exA_col = fcs[lrA];
+    int exB_p = rps[lrB], exB_e = rps[lrB + 1], exB_col = fcs[lrB];
     float acc[2][3][4];
 #pragma unroll
     for (int a = 0; a < 2; ++a)
@@ -560,73 +584,61 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int gc = ks * 4 + q;
       if (ok && gc < p.nch) {
         const uint8_t* st = ring + static_cast<size_t>(s) * kMmaStage;
-        const uint8_t* mA = st + (g * 4 + q) * 256 + 32 * t;
-        const uint8_t* mB = st + ((g + 8) * 4 + q) * 256 + 32 * t;
+        const uint8_t* mA = st + (g * 4 + q) * 256 + colbase;
+        const uint8_t* mB = st + ((g + 8) * 4 + q) * 256 + colbase;
         const uint8_t* eA = st + kMmaStageM8 + (g * 4 + q) * 128 + 32 * t;
         const uint8_t* eB = st + kMmaStageM8 + ((g + 8) * 4 + q) * 128 + 32 * t;
-        // odd rows take their two 16-byte halves in swapped order (word w becomes physical word w ^ 4): the
-        // two row parities of an 8-lane phase then hit different banks. Their B fragments use the same
-        // permutation and their results are read from the odd output columns (see the end of the tile).
-        const int o0 = odd ? 16 : 0, o1 = 16 - o0;
-        uint4 LA[2], HA[2], EA[2], LB[2], HB[2], EB[2];
-        LA[0] = *reinterpret_cast<const uint4*>(mA + o0);
-        LA[1] = *reinterpret_cast<const uint4*>(mA + o1);
-        HA[0] = *reinterpret_cast<const uint4*>(mA + 128 + o0);
-        HA[1] = *reinterpret_cast<const uint4*>(mA + 128 + o1);
+        uint4 MA[2], EA[2], MB[2], EB[2];
+        MA[0] = *reinterpret_cast<const uint4*>(mA + o0);
+        MA[1] = *reinterpret_cast<const uint4*>(mA + o1);
         EA[0] = *reinterpret_cast<const uint4*>(eA + o0);
         EA[1] = *reinterpret_cast<const uint4*>(eA + o1);
-        LB[0] = *reinterpret_cast<const uint4*>(mB + o0);
-        LB[1] = *reinterpret_cast<const uint4*>(mB + o1);
-        HB[0] = *reinterpret_cast<const uint4*>(mB + 128 + o0);
-        HB[1] = *reinterpret_cast<const uint4*>(mB + 128 + o1);
+        MB[0] = *reinterpret_cast<const uint4*>(mB + o0);
+        MB[1] = *reinterpret_cast<const uint4*>(mB + o1);
         EB[0] = *reinterpret_cast<const uint4*>(eB + o0);
         EB[1] = *reinterpret_cast<const uint4*>(eB + o1);
-        const int wx = odd ? 4 : 0;  // physical word of logical word w is w ^ wx
         const int c0 = gc * 256;
-        const bool xa = (rowA < p.N) && lane_has_exc(p.ec, exA_p, exA_e, exA_col, c0, t);
-        const bool xb = (rowB < p.N) && lane_has_exc(p.ec, exB_p, exB_e, exB_col, c0, t);
-        const uint32_t* la = reinterpret_cast<const uint32_t*>(LA);
-        const uint32_t* ha = reinterpret_cast<const uint32_t*>(HA);
+        const bool xa = (rowA < p.N) && lane_has_exc(p.ec, exA_p, exA_e, exA_col, c0 + colbase);
+        const bool xb = (rowB < p.N) && lane_has_exc(p.ec, exB_p, exB_e, exB_col, c0 + colbase);
+        const uint32_t* ma = reinterpret_cast<const uint32_t*>(MA);
         const uint32_t* ea = reinterpret_cast<const uint32_t*>(EA);
-        const uint32_t* lb = reinterpret_cast<const uint32_t*>(LB);
-        const uint32_t* hb = reinterpret_cast<const uint32_t*>(HB);
+        const uint32_t* mb = reinterpret_cast<const uint32_t*>(MB);
         const uint32_t* eb = reinterpret_cast<const uint32_t*>(EB);
 #pragma unroll
         for (int w = 0; w < 8; ++w) {
-          const Z4 za = xa ? decode_word_exc(ea[w], la[w], ha[w], base7) : decode_word(ea[w], la[w], ha[w], base7);
-          const Z4 zb = xb ? decode_word_exc(eb[w], lb[w], hb[w], base7) : decode_word(eb[w], lb[w], hb[w], base7);
-          const uint4* rl = xf + xfrag(gc, w ^ wx, t) * 2;
-          const uint4* rh = xf + xfrag(gc, 8 + (w ^ wx), t) * 2;
-          const uint4 bl0 = rl[0], bl1 = rl[1], bh0 = rh[0], bh1 = rh[1];
-          mma_bf16(acc[0][0], za.lo01, zb.lo01, za.lo23, zb.lo23, bl0.x, bl0.y);
-          mma_bf16(acc[0][1], za.lo01, zb.lo01, za.lo23, zb.lo23, bl0.z, bl0.w);
-          mma_bf16(acc[0][2], za.lo01, zb.lo01, za.lo23, zb.lo23, bl1.x, bl1.y);
-          mma_bf16(acc[1][0], za.hi01, zb.hi01, za.hi23, zb.hi23, bh0.x, bh0.y);
-          mma_bf16(acc[1][1], za.hi01, zb.hi01, za.hi23, zb.hi23, bh0.z, bh0.w);
-          mma_bf16(acc[1][2], za.hi01, zb.hi01, za.hi23, zb.hi23, bh1.x, bh1.y);
+          const Z2 za = decode_half(ea[w], ma[w], base7, hs, xa);
+          const Z2 zb = decode_half(eb[w], mb[w], base7, hs, xb);
+          const int i = hs * 8 + (w ^ wx);
+          const uint4 b0 = *reinterpret_cast<const uint4*>(xf + xrec(gc, i, t, 0));
+          const uint2 b1 = *reinterpret_cast<const uint2*>(xf + xrec(gc, i, t, 1));
+          float(*ac)[4] = acc[w & 1];
+          mma_bf16(ac[0], za.z01, zb.z01, za.z23, zb.z23, b0.x, b0.y);
+          mma_bf16(ac[1], za.z01, zb.z01, za.z23, zb.z23, b0.z, b0.w);
+          mma_bf16(ac[2], za.z01, zb.z01, za.z23, zb.z23, b1.x, b1.y);
         }
         if (xa || xb) {  // exception values times x, for this lane's columns
-          const uint32_t* xw32 = reinterpret_cast<const uint32_t*>(xf);
           auto xval = [&](int col) {
             const int kk = col & 255, hf = kk >> 7, kl = kk & 127;
-            const uint32_t* rec = xw32 + xfrag(col >> 8, hf * 8 + ((kl & 31) >> 2), kl >> 5) * 8;
-            const int sub = (kl & 3) >> 1, sh = (kl & 1) * 16;
-            const float f1 = bf16_to_f32(static_cast<uint16_t>(rec[0 + sub] >> sh));
-            const float f2 = bf16_to_f32(static_cast<uint16_t>(rec[2 + sub] >> sh));
-            const float f3 = bf16_to_f32(static_cast<uint16_t>(rec[4 + sub] >> sh));
+            const int i = hf * 8 + ((kl & 31) >> 2), sub = (kl & 3) >> 1, sh = (kl & 1) * 16;
+            const uint32_t* u0 = reinterpret_cast<const uint32_t*>(xf + xrec(col >> 8, i, kl >> 5, 0));
+            const uint32_t* u1 = reinterpret_cast<const uint32_t*>(xf + xrec(col >> 8, i, kl >> 5, 1));
+            const float f1 = bf16_to_f32(static_cast<uint16_t>(u0[0 + sub] >> sh));
+            const float f2 = bf16_to_f32(static_cast<uint16_t>(u0[2 + sub] >> sh));
+            const float f3 = bf16_to_f32(static_cast<uint16_t>(u1[0 + sub] >> sh));
             return (f1 + f2) + f3;
           };
+          const int lo = c0 + colbase, hi = lo + 32;
           if (xa)
             for (int e = exA_p; e < exA_e; ++e) {
               const int col = p.ec[e];
               if (col >= c0 + 256) break;
-              if (col >= c0 && (((col - c0) & 127) >> 5) == t) exA += p.ev[e] * xval(col);
+              if (col >= lo && col < hi) exA += p.ev[e] * xval(col);
             }
           if (xb)
             for (int e = exB_p; e < exB_e; ++e) {
               const int col = p.ec[e];
               if (col >= c0 + 256) break;
-              if (col >= c0 && (((col - c0) & 127) >> 5) == t) exB += p.ev[e] * xval(col);
+              if (col >= lo && col < hi) exB += p.ev[e] * xval(col);
             }
         }
       }
@@ -634,8 +646,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive(&empty[s]);
     }
     // rows g and g+8: lane (g, t) holds output columns n = 2t (c0, c2) and 2t+1 (c1, c3); column n carries
-    // x in the word order of lanes with g = n, so an even row is read from an even column, an odd row from
-    // an odd one.
+    // x in the word order of the lanes with g = n, so an even row is read from an even column, an odd row
+    // from an odd one (all B columns hold the same x).
     float vA = 0.0f, vB = 0.0f;
 #pragma unroll
     for (int a = 0; a < 2; ++a)
@@ -650,13 +662,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     exB += __shfl_xor_sync(0xffffffffu, exB, 2);
     vA += exA;
     vB += exB;
-    float* rb = red + (half * 2 + (ti & 1)) * 64;
-    if (t == 0) rb[q * 16 + g] = vA, rb[q * 16 + g + 8] = vB;
-    named_sync(2 + half, 128);
-    if (q == 0 && lane < 16 && !aborted) {
+    float* rb = red + (half * 2 + (ti & 1)) * 128;
+    if (t == 0) rb[wh * 16 + g] = vA, rb[wh * 16 + g + 8] = vB;
+    named_sync(2 + half, 256);
+    if (wh == 0 && lane < 16 && !aborted) {
       const int row = tile * 16 + lane;
       if (row < p.N) {
-        const float v = ((rb[lane] + rb[16 + lane]) + rb[32 + lane]) + rb[48 + lane];
+        float v = rb[lane];
+#pragma unroll
+        for (int w8 = 1; w8 < 8; ++w8) v += rb[w8 * 16 + lane];
         if (MODE == 0)
           p.y[row] = v;
         else
@@ -674,7 +688,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     gemv_tn_kernel(const __grid_constant__ CUtensorMap tm8, const __grid_constant__ CUtensorMap tme4, Params p) {
   extern __shared__ __align__(1024) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
-  uint64_t* empty = full + 16;
+  uint64_t* empty = full + 16;  // up to 16 ring slots
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + 256);
   float* xs = reinterpret_cast<float*>(smem + kHeader);  // [TMAX][256] (permuted)
   uint8_t* ring = smem + kHeader + ((TMAX * 256 * 4 + 1023) / 1024) * 1024;
@@ -816,20 +830,23 @@ static int run_mma(const aib_c12* c, const float* x, float* y, int mode, const u
   const int nch = c->K / 256;
   const int tiles = (c->N + 15) / 16;
   const int grid = std::min(tiles, sm_count());
+  const int meta_rows = ((tiles + grid - 1) / grid) * 16;
   CUtensorMap tm8, tme4;
   int rc = make_maps(c, 16, 4, &tm8, &tme4);
   if (rc) return rc;
-  const size_t xf_bytes = ((static_cast<size_t>(nch) * 2048 + 1023) / 1024) * 1024;
-  int NS = static_cast<int>((kSmemMax - kMmaHeader - xf_bytes) / kMmaStage);
-  NS = std::max(2, std::min(NS, 4)) & ~1;
-  const size_t smem = kMmaHeader + xf_bytes + static_cast<size_t>(NS) * kMmaStage;
-  if (smem > kSmemMax) return fail(AIB_ENOTSUP, "aib_gemv_c12: K=%d too large for the tensor-core kernel", c->K);
+  const size_t xf_bytes = static_cast<size_t>(nch) * 2048;
+  const size_t meta_bytes = (static_cast<size_t>(meta_rows) * 2 + 1) * 4;
+  const size_t ring_off = ((kMmaHeader + xf_bytes + meta_bytes + 1023) / 1024) * 1024;
+  int NS = static_cast<int>((kSmemMax - ring_off) / kMmaStage);
+  NS = std::min(NS, 8) & ~1;
+  if (NS < 2) return fail(AIB_ENOTSUP, "aib_gemv_c12: K=%d / N=%d too large for the tensor-core kernel", c->K, c->N);
+  const size_t smem = ring_off + static_cast<size_t>(NS) * kMmaStage;
   Params p{c->rp, c->ec, c->ev, x, y, lnw, eps, c->base, c->N, c->K, nch, 16, 4, (nch + 3) / 4, tiles, NS, 1, 0, 0,
-           c->K};
+           c->K, meta_rows, static_cast<int>(ring_off)};
   auto go = [&](auto kernel) -> int {
     const int r2 = allow_smem(kernel, smem);
     if (r2) return r2;
-    return launch(kernel, dim3(grid), dim3(kThreads), smem, s, "aib_gemv_c12(T=1, mma)", tm8, tme4, p);
+    return launch(kernel, dim3(grid), dim3(kMmaThreads), smem, s, "aib_gemv_c12(T=1, mma)", tm8, tme4, p);
   };
   if (lnw) {
     if (mode == 0) return go(gemv_mma_kernel<0, true>);
@@ -845,20 +862,23 @@ static int g_variant = 1;  // 0: tensor-core kernel where it fits, 1: CUDA-core 
 
 static int run_t1(const aib_c12* c, const float* x, float* y, int mode, const uint16_t* lnw, float eps,
                   cudaStream_t s) {
-  if (g_variant == 0 && c->K <= 16384) return run_mma(c, x, y, mode, lnw, eps, s);
+  if (g_variant == 0 && c->K <= 16384) {
+    const int rc = run_mma(c, x, y, mode, lnw, eps, s);
+    if (rc != AIB_ENOTSUP) return rc;  // shapes whose x / row metadata do not fit use the CUDA-core kernel
+  }
   const int nch = c->K / 256;
   const Geometry g = pick_geometry(c->N, nch, sm_count());
   CUtensorMap tm8, tme4;
   int rc = make_maps(c, g.RT, g.CW, &tm8, &tme4);
   if (rc) return rc;
   const size_t xs_bytes = ((static_cast<size_t>(c->K) * 4 + 1023) / 1024) * 1024;
-  const size_t budget = std::max(kSmemTarget, kHeader + xs_bytes + 2 * kStageBytes);
-  if (budget > kSmemMax) return fail(AIB_ENOTSUP, "aib_gemv_c12: K=%d too large for the shared x buffer", c->K);
-  int NS = static_cast<int>((budget - kHeader - xs_bytes) / kStageBytes);
-  NS = std::max(2, std::min(NS, 8)) & ~1;  // even: the two consumer groups own alternate ring slots
+  if (kHeader + xs_bytes + 2 * kStageBytes > kSmemMax)
+    return fail(AIB_ENOTSUP, "aib_gemv_c12: K=%d too large for the shared x buffer", c->K);
+  int NS = static_cast<int>((kSmemMax - kHeader - xs_bytes) / kStageBytes);
+  NS = std::max(2, std::min(NS, 16)) & ~1;  // even: the two consumer groups own alternate ring slots
   const size_t smem = kHeader + xs_bytes + static_cast<size_t>(NS) * kStageBytes;
   Params p{c->rp, c->ec, c->ev, x, y, lnw, eps, c->base, c->N, c->K, nch, g.RT, g.CW, g.KS, g.tiles, NS, 1, 0, 0,
-           c->K};
+           c->K, 0, 0};
   auto go = [&](auto kernel) -> int {
     const int r2 = allow_smem(kernel, smem);
     if (r2) return r2;
@@ -886,7 +906,8 @@ static int run_tn_t(const aib_c12* c, const float* x, float* y, int T, int xs_, 
   int NS = static_cast<int>((kSmemTarget - kHeader - xs_bytes) / kStageBytes);
   NS = std::max(2, std::min(NS, 8));
   const size_t smem = kHeader + xs_bytes + static_cast<size_t>(NS) * kStageBytes;
-  Params p{c->rp, c->ec, c->ev, x, y, nullptr, 0.0f, c->base, c->N, c->K, nch, 32, 1, nch, tiles, NS, T, xs_, ys_, 0};
+  Params p{c->rp, c->ec, c->ev, x, y, nullptr, 0.0f, c->base, c->N, c->K, nch, 32, 1, nch, tiles, NS, T, xs_, ys_, 0, 0,
+           0};
   rc = allow_smem(gemv_tn_kernel<MODE, TMAX>, smem);
   if (rc) return rc;
   return launch(gemv_tn_kernel<MODE, TMAX>, dim3(grid), dim3(kThreads), smem, s, "aib_gemv_c12(T>1)", tm8, tme4, p);
