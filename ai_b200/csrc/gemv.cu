@@ -225,7 +225,7 @@ AIB_DEV void produce_pairs(const CUtensorMap* tm8, const CUtensorMap* tme4, uint
     for (int h = 0; h < 2; ++h) {
       if (j[h] >= n[h]) continue;
       const int s = h + 2 * (j[h] % per), use = j[h] / per;
-      if (use > 0 && !mbar_try_wait(&empty[s], (use - 1) & 1)) continue;
+      if (use > 0 && !mbar_test_wait(&empty[s], (use - 1) & 1)) continue;
       const int tile = tb + 2 * (j[h] / KS) + h, ks = j[h] % KS;
       uint8_t* st = ring + static_cast<size_t>(s) * stage_bytes;
       mbar_arrive_expect_tx(&full[s], stage_bytes);
@@ -235,6 +235,7 @@ AIB_DEV void produce_pairs(const CUtensorMap* tm8, const CUtensorMap* tme4, uint
       progressed = true;
     }
     idle = progressed ? 0 : idle + 1;
+    if (!progressed) __nanosleep(64);  // both halves full: back off instead of taking issue slots from them
     if (idle > kSpinLimit) {
       set_status(AIB_DEV_TIMEOUT_EMPTY);
       *abort_flag = 1;
@@ -680,6 +681,305 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
   }
 }
 
+// --------------------------------------------------------------------- T = 1 wide-stage kernel
+// A TMA copy costs an SM a roughly fixed time whatever its size (measured on B200: 4 KB copies stream at
+// ~1.8 TB/s chip-wide, 16 KB copies at ~6.7 TB/s), so this kernel moves 48 KB per stage in two copies: R rows
+// x CW chunks of m8 (R*CW*256 bytes) and of e4 (half that), with R*CW = 128. Every consumer thread owns one
+// 32-element unit (chunk slot, 16-column group) of two rows of the stage -- rows `pair` and `pair + R/2` of
+// the tile -- so each x vector read from shared memory feeds two rows. The L = 8*CW threads of a row pair
+// cover the stage's row segment.
+//
+// The producer warp does the per-stage bookkeeping so the consumers' loop stays short:
+//  * before issuing a stage it marks, in a per-slot bitmask (one bit per row and unit), the units that hold
+//    an exception (from the CSR: row pointers and, when they fit, the CTA's exception columns, staged in
+//    shared memory before the grid-dependency wait) -- consumers test one bit instead of walking the CSR;
+//  * consumers reduce a finished tile inside each warp and leave one partial per (row, warp) in the slot;
+//    once the slot's empty barrier completes, the producer adds the W = L/32 partials of each row in a fixed
+//    order and writes y. No CTA-wide barrier runs in the main loop.
+constexpr int kRowsConsumers = 512;
+constexpr int kRowsThreads = kRowsConsumers + 32;
+constexpr int kRowsStage = 128 * 384;  // R * CW * (256 + 128) bytes
+constexpr int kRowsSlotMeta = 256;     // per slot: 32-word exception bitmask + 32 row/warp partials
+constexpr int kRowsHeader = 1024 + 8 * kRowsSlotMeta;  // barriers [0,256), abort 256, RMS partials [512,1024)
+
+struct RowsParams {
+  const int32_t* rp;
+  const int32_t* ec;
+  const float* ev;
+  const float* x;
+  float* y;
+  const uint16_t* lnw;
+  float eps;
+  int base, N, K, nch;
+  int R, CW, KS, tiles, NS;
+  int xs_off, rps_off, ecs_off, ecap, ring_off;
+};
+
+template <int MODE, bool RMS>
+__global__ void __launch_bounds__(kRowsThreads, 1)
+    gemv_rows_kernel(const __grid_constant__ CUtensorMap tm8, const __grid_constant__ CUtensorMap tme4, RowsParams p) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* empty = full + 16;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + 256);
+  float* rms_red = reinterpret_cast<float*>(smem + 512);
+  uint8_t* meta = smem + 1024;  // slot s: uint32 mask[32] at s*256, float part[32] at s*256 + 128
+  float* xs = reinterpret_cast<float*>(smem + p.xs_off);
+  int* rps = reinterpret_cast<int*>(smem + p.rps_off);
+  int* ecs = reinterpret_cast<int*>(smem + p.ecs_off);
+  uint8_t* ring = smem + p.ring_off;
+
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int tb = static_cast<int>((static_cast<long long>(blockIdx.x) * p.tiles) / gridDim.x);
+  const int te = static_cast<int>((static_cast<long long>(blockIdx.x + 1) * p.tiles) / gridDim.x);
+  const int R = p.R, CW = p.CW, KS = p.KS, NS = p.NS;
+  const int L = 8 * CW, W = L / 32;  // threads / warps per row pair (L = units per row per stage)
+  const int n_st = (te - tb) * KS;
+  const int row0 = tb * R;
+  const int nrows = min((te - tb) * R, p.N - row0);
+  if (tid == 0) {
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kRowsConsumers / 32);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  // row metadata (weights only, so before the grid-dependency wait), for producer and consumers
+  for (int i = tid; i <= nrows; i += kRowsThreads) rps[i] = p.rp[row0 + i];
+  __syncthreads();
+  const int e0 = rps[0], n_exc = rps[nrows] - e0;
+  const bool staged = n_exc <= p.ecap;
+  if (staged)
+    for (int i = tid; i < n_exc; i += kRowsThreads) ecs[i] = p.ec[e0 + i];
+  __syncthreads();
+  pdl_trigger();
+
+  if (tid >= kRowsConsumers) {  // ---------------- producer warp
+    if (lane == 0) {
+      prefetch_tensormap(&tm8);
+      prefetch_tensormap(&tme4);
+    }
+    const uint32_t m8_bytes = static_cast<uint32_t>(R * CW * 256);
+    const int wpr = L / 32;  // mask words per row
+    int cur = 0;             // lane r < R: cursor into its row's exceptions (advances over the tile's stages)
+    int s = 0, ph = 0, ks = 0, tile = tb;
+    int fs = 0, fph = 0, fks = 0, ftile = tb;  // stage being finalised (issued NS stages earlier)
+    for (int i = 0; i < n_st + NS; ++i) {
+      if (i >= NS) {  // finalise stage i - NS: its slot's consumers are done
+        bool ok = true;
+        if (lane == 0) {
+          ok = false;
+          for (uint32_t k = 0; k < kSpinLimit && !ok; ++k) {
+            ok = mbar_try_wait(&empty[fs], fph);
+            if (!ok && *abort_flag) break;
+          }
+          if (!ok) {
+            if (!*abort_flag) set_status(AIB_DEV_TIMEOUT_EMPTY);
+            *abort_flag = 1;
+          }
+        }
+        ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+        if (!ok) {
+          // drain: wait (bounded) for copies still in flight, then leave
+          if (lane == 0)
+            for (int k = i - NS; k < min(i, n_st); ++k) mbar_wait(&full[k % NS], (k / NS) & 1, AIB_DEV_TIMEOUT_FULL);
+          break;
+        }
+        if (fks == KS - 1 && lane < R && !*abort_flag) {
+          const int row = ftile * R + lane;
+          if (row < p.N) {
+            const float* part = reinterpret_cast<const float*>(meta + fs * kRowsSlotMeta + 128);
+            float v = part[lane * W];
+            for (int w = 1; w < W; ++w) v += part[lane * W + w];
+            if (MODE == 0)
+              p.y[row] = v;
+            else
+              p.y[row] += v;
+          }
+        }
+        if (++fks == KS) fks = 0, ++ftile;
+        if (++fs == NS) fs = 0, fph ^= 1;
+      }
+      if (i < n_st) {  // issue stage i into slot s, exception bitmask first
+        uint32_t* mask = reinterpret_cast<uint32_t*>(meta + s * kRowsSlotMeta);
+        mask[lane] = 0u;
+        __syncwarp();
+        if (ks == 0) cur = 0;
+        const int lr = (tile - tb) * R + lane;
+        if (lane < R && lr < nrows) {
+          const int a = rps[lr] - e0, b = rps[lr + 1] - e0;
+          const int lo = ks * CW * 256, hi = lo + CW * 256;
+          uint32_t* mw = mask + lane * wpr;
+          int q = a + cur;
+          for (; q < b; ++q) {
+            const int col = staged ? ecs[q] : p.ec[e0 + q];
+            if (col >= hi) break;
+            if (col >= lo) {
+              const int u = ((col - lo) >> 8) * 8 + ((col & 127) >> 4);
+              mw[u >> 5] |= 1u << (u & 31);
+            }
+          }
+          cur = q - a;
+        }
+        __syncwarp();
+        if (lane == 0) {
+          uint8_t* st = ring + static_cast<size_t>(s) * kRowsStage;
+          mbar_arrive_expect_tx(&full[s], kRowsStage);
+          tma_load_3d(st, &tm8, &full[s], 0, ks * CW, tile * R);
+          tma_load_3d(st + m8_bytes, &tme4, &full[s], 0, ks * CW, tile * R);
+        }
+        if (++ks == KS) ks = 0, ++tile;
+        if (++s == NS) s = 0, ph ^= 1;
+      }
+    }
+    return;
+  }
+
+  // ---------------- consumers: x prologue (after the grid-dependency wait: x is the previous kernel's output)
+  pdl_wait();
+  const int K = p.K, K4 = K / 4;
+  const float4* __restrict__ xg = reinterpret_cast<const float4*>(p.x);
+  float rs = 1.0f;
+  if (RMS) {
+    float ss = 0.0f;
+    for (int k = tid; k < K4; k += kRowsConsumers) {
+      const float4 v = xg[k];
+      ss += (v.x * v.x + v.y * v.y) + (v.z * v.z + v.w * v.w);
+    }
+    ss = warp_sum(ss);
+    if (lane == 0) rms_red[tid >> 5] = ss;
+    named_sync(1, kRowsConsumers);
+    float tot = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kRowsConsumers / 32; ++w) tot += rms_red[w];
+    rs = rsqrtf(tot / static_cast<float>(K) + p.eps);
+  }
+  for (int k0 = 0; k0 < K4; k0 += 4 * kRowsConsumers) {  // batches of 4 float4 per thread, loads first
+    float4 v[4], u[4];
+    uint2 wl[4];
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+      const int k = k0 + b * kRowsConsumers + tid;
+      if (k < K4) {
+        v[b] = xg[k];
+        if (MODE == 2) u[b] = xg[K4 + k];
+        if (RMS) wl[b] = reinterpret_cast<const uint2*>(p.lnw)[k];
+      }
+    }
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+      const int k = k0 + b * kRowsConsumers + tid;
+      if (k < K4) {
+        float4 o = v[b];
+        if (MODE == 2)
+          o = make_float4(silu_mul(o.x, u[b].x), silu_mul(o.y, u[b].y), silu_mul(o.z, u[b].z), silu_mul(o.w, u[b].w));
+        if (RMS)
+          o = make_float4(bf16_to_f32(static_cast<uint16_t>(wl[b].x)) * (o.x * rs),
+                          bf16_to_f32(static_cast<uint16_t>(wl[b].x >> 16)) * (o.y * rs),
+                          bf16_to_f32(static_cast<uint16_t>(wl[b].y)) * (o.z * rs),
+                          bf16_to_f32(static_cast<uint16_t>(wl[b].y >> 16)) * (o.w * rs));
+        *reinterpret_cast<float4*>(xs + xperm(4 * k)) = o;
+      }
+    }
+  }
+  named_sync(1, kRowsConsumers);
+
+  const int pair = tid / L, l = tid % L;  // rows pair and pair + R/2 of each tile
+  const int cc = l >> 3, j = l & 7;       // chunk slot and 16-column group of this thread's unit
+  const int wp = l >> 5;                  // warp index inside the pair
+  const uint32_t base7 = (static_cast<uint32_t>(p.base) << 7) | (static_cast<uint32_t>(p.base) << 23);
+  const int ra = pair, rb = pair + R / 2;
+  const uint32_t m8a = static_cast<uint32_t>((ra * CW + cc) * 256 + 16 * j);
+  const uint32_t m8b = static_cast<uint32_t>((rb * CW + cc) * 256 + 16 * j);
+  const uint32_t e4a = static_cast<uint32_t>(R * CW * 256 + (ra * CW + cc) * 128 + 16 * j);
+  const uint32_t e4b = static_cast<uint32_t>(R * CW * 256 + (rb * CW + cc) * 128 + 16 * j);
+  const int mwa = ra * W + (l >> 5), mwb = rb * W + (l >> 5);  // mask words of the two rows
+  const uint32_t mbit = 1u << (l & 31);
+  const float4* xs4 = reinterpret_cast<const float4*>(xs);
+
+  // slow path: code-15 elements decode to 0, then the exact values of the unit's exceptions are added
+  auto unit_slow = [&](int lr, int gc, const uint4& ml, const uint4& mh, const uint4& ee, const float4* xl,
+                       const float4* xh) -> float {
+    const uint32_t E[4] = {ee.x, ee.y, ee.z, ee.w}, Lw[4] = {ml.x, ml.y, ml.z, ml.w}, Hw[4] = {mh.x, mh.y, mh.z, mh.w};
+    const float* xlf = reinterpret_cast<const float*>(xl);
+    const float* xhf = reinterpret_cast<const float*>(xh);
+    float sacc = 0.0f;
+    for (int q = 0; q < 4; ++q)
+      for (int b = 0; b < 4; ++b) {
+        const uint32_t eb = (E[q] >> (8 * b)) & 0xFFu;
+        sacc += dec1((Lw[q] >> (8 * b)) & 0xFFu, eb & 15u, p.base) * xlf[q * 4 + b];
+        sacc += dec1((Hw[q] >> (8 * b)) & 0xFFu, eb >> 4, p.base) * xhf[q * 4 + b];
+      }
+    const int a = rps[lr] - e0, b = rps[lr + 1] - e0;
+    for (int q = a; q < b; ++q) {
+      const int col = staged ? ecs[q] : p.ec[e0 + q];
+      if ((col >> 8) > gc) break;
+      if ((col >> 8) == gc && ((col & 127) >> 4) == j) sacc += p.ev[e0 + q] * xs[xperm(col)];
+    }
+    return sacc;
+  };
+
+  bool aborted = false;
+  float4 accA = make_float4(0.0f, 0.0f, 0.0f, 0.0f), accB = accA;
+  float exA = 0.0f, exB = 0.0f;
+  int s = 0, ph = 0, ks = 0, tile = tb;
+  for (int i = 0; i < n_st; ++i) {
+    const bool ok = !aborted && wait_full(&full[s], ph, abort_flag);
+    if (!ok) aborted = true;
+    const int gc = ks * CW + cc;
+    const uint8_t* sm = meta + s * kRowsSlotMeta;
+    if (ok && gc < p.nch) {
+      const uint8_t* st = ring + static_cast<size_t>(s) * kRowsStage;
+      const uint32_t* mask = reinterpret_cast<const uint32_t*>(sm);
+      const bool xa = mask[mwa] & mbit, xb = mask[mwb] & mbit;
+      const float4* xb4 = xs4 + gc * 64;
+      float4 xl[4], xh[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        xl[q] = xb4[q * 8 + j];
+        xh[q] = xb4[32 + q * 8 + j];
+      }
+      const uint4 mlA = *reinterpret_cast<const uint4*>(st + m8a);
+      const uint4 mhA = *reinterpret_cast<const uint4*>(st + m8a + 128);
+      const uint4 eeA = *reinterpret_cast<const uint4*>(st + e4a);
+      const uint4 mlB = *reinterpret_cast<const uint4*>(st + m8b);
+      const uint4 mhB = *reinterpret_cast<const uint4*>(st + m8b + 128);
+      const uint4 eeB = *reinterpret_cast<const uint4*>(st + e4b);
+      const int lt = (tile - tb) * R;
+      if (!xa)
+        unit_fast4(mlA, mhA, eeA, xl, xh, base7, accA);
+      else
+        exA += unit_slow(lt + ra, gc, mlA, mhA, eeA, xl, xh);
+      if (!xb)
+        unit_fast4(mlB, mhB, eeB, xl, xh, base7, accB);
+      else
+        exB += unit_slow(lt + rb, gc, mlB, mhB, eeB, xl, xh);
+    }
+    if (ks == KS - 1) {  // tile complete: reduce inside the warp, leave one partial per (row, warp) in the slot
+      float vA = ((accA.x + accA.y) + (accA.z + accA.w)) + exA;
+      float vB = ((accB.x + accB.y) + (accB.z + accB.w)) + exB;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        vA += __shfl_xor_sync(0xffffffffu, vA, o);
+        vB += __shfl_xor_sync(0xffffffffu, vB, o);
+      }
+      if (lane == 0) {
+        float* part = reinterpret_cast<float*>(const_cast<uint8_t*>(sm) + 128);
+        part[ra * W + wp] = vA;
+        part[rb * W + wp] = vB;
+      }
+      accA = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      accB = accA;
+      exA = exB = 0.0f;
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+    if (++ks == KS) ks = 0, ++tile;
+    if (++s == NS) s = 0, ph ^= 1;
+  }
+}
+
 // ------------------------------------------------------------------------------- batched kernel
 // T <= TMAX tokens, RT = 32 rows x CW = 1 chunk per stage; the x columns of each stage (T x 256 floats,
 // SiLU-gated for mode 2) are staged in shared memory by the consumers.
@@ -858,10 +1158,58 @@ static int run_mma(const aib_c12* c, const float* x, float* y, int mode, const u
   return go(gemv_mma_kernel<2, false>);
 }
 
-static int g_variant = 1;  // 0: tensor-core kernel where it fits, 1: CUDA-core kernel
+// Wide-stage kernel (48 KB TMA stages); ENOTSUP when K is not a multiple of 1024 or x does not fit.
+static int run_rows(const aib_c12* c, const float* x, float* y, int mode, const uint16_t* lnw, float eps,
+                    cudaStream_t s) {
+  const int nch = c->K / 256;
+  if (nch % 4) return fail(AIB_ENOTSUP, "aib_gemv_c12: K=%d is not a multiple of 1024", c->K);
+  if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(lnw) & 7))
+    return fail(AIB_ENOTSUP, "aib_gemv_c12: x / lnw not aligned for vector loads");
+  const int CW = nch % 16 == 0 ? 16 : (nch % 8 == 0 ? 8 : 4);
+  const int R = 128 / CW;
+  const int tiles = (c->N + R - 1) / R;
+  const int grid = std::min(tiles, sm_count());
+  const int rows_max = ((tiles + grid - 1) / grid) * R;
+  const size_t xs_off = kRowsHeader;  // x (fp32, permuted), then row pointers, staged exception columns, ring
+  const size_t rps_off = xs_off + ((static_cast<size_t>(c->K) * 4 + 127) / 128) * 128;
+  const size_t ecs_off = rps_off + ((static_cast<size_t>(rows_max + 1) * 4 + 127) / 128) * 128;
+  const size_t min_ecs = 4096;  // room for at least 1024 staged exception columns
+  const size_t ring_need = ((ecs_off + min_ecs + 1023) / 1024) * 1024;
+  if (ring_need + 2 * static_cast<size_t>(kRowsStage) > kSmemMax)
+    return fail(AIB_ENOTSUP, "aib_gemv_c12: K=%d too large for the wide-stage kernel", c->K);
+  const int NS = std::min(8, static_cast<int>((kSmemMax - ring_need) / kRowsStage));
+  const size_t ring_off = ((kSmemMax - static_cast<size_t>(NS) * kRowsStage) / 1024) * 1024;
+  const int ecap = static_cast<int>((ring_off - ecs_off) / 4);
+  const size_t smem = ring_off + static_cast<size_t>(NS) * kRowsStage;
+  CUtensorMap tm8, tme4;
+  int rc = make_maps(c, R, CW, &tm8, &tme4);
+  if (rc) return rc;
+  RowsParams p{c->rp, c->ec, c->ev, x, y, lnw, eps, c->base, c->N, c->K, nch, R, CW, nch / CW, tiles, NS,
+               static_cast<int>(xs_off), static_cast<int>(rps_off), static_cast<int>(ecs_off), ecap,
+               static_cast<int>(ring_off)};
+  auto go = [&](auto kernel) -> int {
+    const int r2 = allow_smem(kernel, smem);
+    if (r2) return r2;
+    return launch(kernel, dim3(grid), dim3(kRowsThreads), smem, s, "aib_gemv_c12(T=1, wide)", tm8, tme4, p);
+  };
+  if (lnw) {
+    if (mode == 0) return go(gemv_rows_kernel<0, true>);
+    if (mode == 1) return go(gemv_rows_kernel<1, true>);
+    return go(gemv_rows_kernel<2, true>);
+  }
+  if (mode == 0) return go(gemv_rows_kernel<0, false>);
+  if (mode == 1) return go(gemv_rows_kernel<1, false>);
+  return go(gemv_rows_kernel<2, false>);
+}
+
+static int g_variant = 2;  // 0: tensor-core kernel, 1: CUDA-core 12 KB-stage kernel, 2: wide-stage kernel
 
 static int run_t1(const aib_c12* c, const float* x, float* y, int mode, const uint16_t* lnw, float eps,
                   cudaStream_t s) {
+  if (g_variant == 2) {
+    const int rc = run_rows(c, x, y, mode, lnw, eps, s);
+    if (rc != AIB_ENOTSUP) return rc;  // other shapes use the 12 KB-stage kernel
+  }
   if (g_variant == 0 && c->K <= 16384) {
     const int rc = run_mma(c, x, y, mode, lnw, eps, s);
     if (rc != AIB_ENOTSUP) return rc;  // shapes whose x / row metadata do not fit use the CUDA-core kernel
@@ -927,7 +1275,8 @@ using namespace aib;
 
 extern "C" {
 
-// Kernel selection for the T = 1 GEMV (tests and A/B timing): 0 = tensor-core kernel (default), 1 = CUDA-core.
+// Kernel selection for the T = 1 GEMV (tests and A/B timing): 0 = tensor-core kernel, 1 = CUDA-core kernel with
+// 12 KB stages, 2 = wide-stage kernel (default). Shapes a kernel cannot take fall back to kernel 1.
 void aib_gemv_set_variant(int v) { gemv::g_variant = v; }
 
 size_t aib_gemv_c12_workspace(const aib_c12* c, int T) {

@@ -276,9 +276,11 @@ def micro(args):
     gemv_down: [4096, 12288] with the SiLU-gated input; attn: one layer's decode attention at ctx 4096;
     sample: the sampler on one vocabulary row."""
     import torch
-    from ai_b200 import build, wcomp
+    from ai_b200 import build, wcomp, _lib
     build.build()
     torch.cuda.set_device(0)
+    if args.gemv_variant is not None:
+        _lib.lib().aib_gemv_set_variant(args.gemv_variant)
     if args.micro in ("attn", "sample"):
         run, nbytes = (micro_attn if args.micro == "attn" else micro_sample)(args)
         for _ in range(3):
@@ -314,7 +316,7 @@ def micro(args):
     e1.record()
     torch.cuda.synchronize()
     us = e0.elapsed_time(e1) * 1e3 / reps
-    print(json.dumps({"micro": args.micro, "N": N, "K": K, "bytes": c.nbytes, "us_per_launch": round(us, 2),
+    print(json.dumps({"micro": args.micro, "variant": args.gemv_variant, "N": N, "K": K, "bytes": c.nbytes, "us_per_launch": round(us, 2),
                       "GBps": round(c.nbytes / us / 1e3, 1)}))
 
 
@@ -322,6 +324,8 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--micro", choices=["gemv", "gemv_down", "attn", "sample"], default=None,
                     help="time one kernel alone on a small case (for ncu) instead of the decode benchmark")
+    ap.add_argument("--gemv-variant", type=int, default=None, choices=[0, 1, 2],
+                    help="codec GEMV kernel for --micro: 0 tensor-core (mma.sync), 1 CUDA-core 12 KB stages, 2 wide stages (default)")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=256)
     ap.add_argument("--warmup", type=int, default=8)

@@ -108,14 +108,15 @@ def test_gemvc1_matches_reference_golden(lib, variant, name):
 
 
 GEMV_SHAPES = [(64, 1024, 0, False), (6144, 4096, 0, True), (4096, 4096, 1, False), (24576, 4096, 0, True), (4096, 12288, 2, False),
-               (1024, 2048, 1, False), (4096, 1024, 0, True), (517, 768, 2, False), (40, 256, 0, True)]
+               (1024, 2048, 1, False), (4096, 1024, 0, True), (517, 768, 2, False), (40, 256, 0, True),
+               (100, 3072, 1, True), (33, 2048, 0, False), (1000, 5120, 2, False)]
 
 
-@pytest.fixture(params=[0, 1], ids=["tensorcore", "cudacore"])
+@pytest.fixture(params=[0, 1, 2], ids=["tensorcore", "cudacore", "wide"])
 def variant(request, lib):
     lib.aib_gemv_set_variant(request.param)
     yield request.param
-    lib.aib_gemv_set_variant(1)  # library default
+    lib.aib_gemv_set_variant(2)  # library default
 
 
 @pytest.mark.parametrize("N,K,mode,rms", GEMV_SHAPES)
@@ -181,6 +182,26 @@ def test_gemv_dense_exceptions(lib, variant):
     W = codec.bf16_bits_to_f32(bits(w)).astype(np.float64)
     xn = x.cpu().numpy().astype(np.float64)
     close(y.cpu().numpy(), W @ xn, np.abs(W) @ np.abs(xn))
+
+
+def test_gemv_exceptions_beyond_staged_capacity(lib, variant):
+    """One CTA holding more exceptions than the wide kernel stages in shared memory (read from global)."""
+    from ai_b200 import wcomp
+    g = torch.Generator(device="cuda").manual_seed(78)
+    N, K = 16, 4096
+    w = (torch.randn(N, K, generator=g, device="cuda") * 0.02).bfloat16()
+    w[3] = (torch.randn(K, generator=g, device="cuda") * 1e5).bfloat16()
+    w[9] = (torch.randn(K, generator=g, device="cuda") * 1e-12).bfloat16()
+    c = wcomp.compress(w)
+    assert c["ev"].numel() > 8000
+    x = torch.randn(K, generator=g, device="cuda")
+    y0 = torch.randn(N, generator=g, device="cuda")
+    y = y0.clone()
+    wcomp.gemvc1(x, c, y, 1)
+    W = codec.bf16_bits_to_f32(bits(w)).astype(np.float64)
+    xn = x.cpu().numpy().astype(np.float64)
+    close(y.cpu().numpy(), W @ xn + y0.cpu().numpy(), np.abs(W) @ np.abs(xn) + np.abs(y0.cpu().numpy()))
+    assert status_clear() == 0
 
 
 def test_gemv_deterministic(lib):
