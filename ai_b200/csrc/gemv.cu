@@ -118,6 +118,35 @@ AIB_DEV void unit_fast4(const uint4& ml, const uint4& mh, const uint4& ee, const
   }
 }
 
+// Same decode and the same four accumulation chains as unit_fast4, tuned for the integer pipe: the shifts
+// are multiplies by runtime constants (k128 = 128, k8 = 8, k65536 = 65536, passed in by the host so the
+// compiler cannot turn them back into shifts), which issue as IMAD on the FMA pipe instead of competing with
+// the byte permutes and logic ops for the ALU pipe, and the FMAs are packed (fma.rn.f32x2).
+AIB_DEV void unit_fast_imad(const uint4& ml, const uint4& mh, const uint4& ee, const float4* xl, const float4* xh,
+                            uint32_t base7, uint32_t k128, uint32_t k8, uint32_t k65536, float4& a) {
+  const uint32_t E[4] = {ee.x, ee.y, ee.z, ee.w};
+  const uint32_t L[4] = {ml.x, ml.y, ml.z, ml.w};
+  const uint32_t Hh[4] = {mh.x, mh.y, mh.z, mh.w};
+  float2 p0 = make_float2(a.x, a.y), p1 = make_float2(a.z, a.w);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const uint32_t x01 = prmt(E[q], 0u, 0x4140u), x23 = prmt(E[q], 0u, 0x4342u);
+    const uint32_t zlo01 = (prmt(L[q], 0u, 0x9180u) & 0x807F807Fu) | ((x01 & 0x000F000Fu) * k128 + base7);
+    const uint32_t zlo23 = (prmt(L[q], 0u, 0xB3A2u) & 0x807F807Fu) | ((x23 & 0x000F000Fu) * k128 + base7);
+    const uint32_t zhi01 = (prmt(Hh[q], 0u, 0x9180u) & 0x807F807Fu) | ((x01 & 0x00F000F0u) * k8 + base7);
+    const uint32_t zhi23 = (prmt(Hh[q], 0u, 0xB3A2u) & 0x807F807Fu) | ((x23 & 0x00F000F0u) * k8 + base7);
+    p0 = ffma2(make_float2(__uint_as_float(zlo01 * k65536), __uint_as_float(zlo01 & 0xFFFF0000u)),
+               make_float2(xl[q].x, xl[q].y), p0);
+    p1 = ffma2(make_float2(__uint_as_float(zlo23 * k65536), __uint_as_float(zlo23 & 0xFFFF0000u)),
+               make_float2(xl[q].z, xl[q].w), p1);
+    p0 = ffma2(make_float2(__uint_as_float(zhi01 * k65536), __uint_as_float(zhi01 & 0xFFFF0000u)),
+               make_float2(xh[q].x, xh[q].y), p0);
+    p1 = ffma2(make_float2(__uint_as_float(zhi23 * k65536), __uint_as_float(zhi23 & 0xFFFF0000u)),
+               make_float2(xh[q].z, xh[q].w), p1);
+  }
+  a = make_float4(p0.x, p0.y, p1.x, p1.y);
+}
+
 // Element-wise decode with code 15 -> 0 (slow path for units holding exceptions).
 AIB_DEV float dec1(uint32_t m, uint32_t code, uint32_t base) {
   if (code == 15u) return 0.0f;
@@ -580,7 +609,8 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
     for (int ks = 0; ks < p.KS; ++ks) {
       const int it = 2 * (ti * p.KS + ks) + half;
       const int s = it % p.NS;
-      const bool ok = !aborted && wait_full(&full[s], (it / p.NS) & 1, abort_flag);
+      // warp-uniform: the MMAs below must run with all 32 lanes converged
+      const bool ok = __all_sync(0xffffffffu, !aborted && wait_full(&full[s], (it / p.NS) & 1, abort_flag));
       if (!ok) aborted = true;
       const int gc = ks * 4 + q;
       if (ok && gc < p.nch) {
@@ -601,6 +631,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
         const int c0 = gc * 256;
         const bool xa = (rowA < p.N) && lane_has_exc(p.ec, exA_p, exA_e, exA_col, c0 + colbase);
         const bool xb = (rowB < p.N) && lane_has_exc(p.ec, exB_p, exB_e, exB_col, c0 + colbase);
+        __syncwarp();  // reconverge after the per-lane CSR walks: the MMAs below are warp-collective
         const uint32_t* ma = reinterpret_cast<const uint32_t*>(MA);
         const uint32_t* ea = reinterpret_cast<const uint32_t*>(EA);
         const uint32_t* mb = reinterpret_cast<const uint32_t*>(MB);
@@ -713,6 +744,7 @@ struct RowsParams {
   int base, N, K, nch;
   int R, CW, KS, tiles, NS;
   int xs_off, rps_off, ecs_off, ecap, ring_off;
+  uint32_t k128, k8, k65536;  // 128, 8, 65536 (see unit_fast_imad)
 };
 
 template <int MODE, bool RMS>
@@ -948,11 +980,11 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
       const uint4 eeB = *reinterpret_cast<const uint4*>(st + e4b);
       const int lt = (tile - tb) * R;
       if (!xa)
-        unit_fast4(mlA, mhA, eeA, xl, xh, base7, accA);
+        unit_fast_imad(mlA, mhA, eeA, xl, xh, base7, p.k128, p.k8, p.k65536, accA);
       else
         exA += unit_slow(lt + ra, gc, mlA, mhA, eeA, xl, xh);
       if (!xb)
-        unit_fast4(mlB, mhB, eeB, xl, xh, base7, accB);
+        unit_fast_imad(mlB, mhB, eeB, xl, xh, base7, p.k128, p.k8, p.k65536, accB);
       else
         exB += unit_slow(lt + rb, gc, mlB, mhB, eeB, xl, xh);
     }
@@ -971,6 +1003,343 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
       }
       accA = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
       accB = accA;
+      exA = exB = 0.0f;
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+    if (++ks == KS) ks = 0, ++tile;
+    if (++s == NS) s = 0, ph ^= 1;
+  }
+}
+
+// ----------------------------------------------------------- T = 1 wide-stage tensor-core kernel
+// Same 48 KB stages and producer bookkeeping as gemv_rows_kernel, but the decoded bf16 pairs are fed to
+// mma.sync.m16n8k16 (bf16 x bf16 -> fp32) as A fragments, so neither an fp32 split nor an FMA per weight is
+// needed. x is stored once in shared memory as three bf16 parts (x = x0 + x1 + x2 exactly, the reference's
+// `_x3` split, wcomp.py:130-140) placed in different B columns: one MMA per 8 weights and lane.
+//
+// Stage = R rows (RG = R/16 row groups of 16) x CW chunks; 16 warps = RG x CW x 2. Warp (rg, q, hh) handles
+// chunk q of row group rg: lane (g, t) holds rows g and g+8 and, for parity par = g & 1, the 16 low columns
+// blk*64 + 16t + [0, 16) with blk = hh ^ par, plus the 16 high columns 128 + those -- exactly one codec unit
+// (chunk q, 16-column group 4*blk + t) per row. MMA i (0..7) takes low columns 2i, 2i+1 and high columns
+// 128 + 2i, 129 + 2i of that range. Even and odd rows of the warp use different column blocks, which keeps
+// the 16-byte shared loads of a quarter-warp on distinct banks; B column n = 2*sp + par carries x part sp in
+// the column order of parity par, and a row reads its result from the columns of its own parity.
+constexpr int kTcConsumers = 512;
+constexpr int kTcThreads = kTcConsumers + 32;
+constexpr int kTcSlotMeta = 128 + 32 * 16 * 4;  // per slot: 32-word exception mask, partials [32 rows][16 warps]
+
+// Byte offset of the x record (8 bytes: low pair, high pair) for chunk gc, MMA i, lane quad t, column block
+// blk and part sp. Parts 0 and 1 of all (blk, t) form one 128-byte line per (gc, i) and part 2 a 64-byte line
+// in a second region (nch*8*128 bytes further), so each half-warp's 8-byte loads hit 16 distinct bank pairs.
+AIB_DEV int tc_xrec(int nch, int gc, int i, int blk, int t, int sp) {
+  const int gi = gc * 8 + i;
+  return sp < 2 ? gi * 128 + (blk * 2 + sp) * 32 + t * 8 : nch * 1024 + gi * 64 + blk * 32 + t * 8;
+}
+
+template <int MODE, bool RMS>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    gemv_tc_kernel(const __grid_constant__ CUtensorMap tm8, const __grid_constant__ CUtensorMap tme4, RowsParams p) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* empty = full + 16;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + 256);
+  float* rms_red = reinterpret_cast<float*>(smem + 512);
+  uint8_t* meta = smem + 1024;  // slot s: uint32 mask[32] at s*kTcSlotMeta, float part[32][16] at +128
+  uint8_t* xr = smem + p.xs_off;
+  int* rps = reinterpret_cast<int*>(smem + p.rps_off);
+  int* ecs = reinterpret_cast<int*>(smem + p.ecs_off);
+  uint8_t* ring = smem + p.ring_off;
+
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int tb = static_cast<int>((static_cast<long long>(blockIdx.x) * p.tiles) / gridDim.x);
+  const int te = static_cast<int>((static_cast<long long>(blockIdx.x + 1) * p.tiles) / gridDim.x);
+  const int R = p.R, CW = p.CW, KS = p.KS, NS = p.NS;
+  const int PW = 2 * CW;  // partials per row (warps per row group)
+  const int n_st = (te - tb) * KS;
+  const int row0 = tb * R;
+  const int nrows = min((te - tb) * R, p.N - row0);
+  if (tid == 0) {
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kTcConsumers / 32);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  for (int i = tid; i <= nrows; i += kTcThreads) rps[i] = p.rp[row0 + i];
+  __syncthreads();
+  const int e0 = rps[0], n_exc = rps[nrows] - e0;
+  const bool staged = n_exc <= p.ecap;
+  if (staged)
+    for (int i = tid; i < n_exc; i += kTcThreads) ecs[i] = p.ec[e0 + i];
+  __syncthreads();
+  pdl_trigger();
+
+  if (tid >= kTcConsumers) {  // ---------------- producer warp (same protocol as gemv_rows_kernel)
+    if (lane == 0) {
+      prefetch_tensormap(&tm8);
+      prefetch_tensormap(&tme4);
+    }
+    const uint32_t m8_bytes = static_cast<uint32_t>(R * CW * 256);
+    const int wpr = CW * 8 / 32;  // mask words per row (1 for CW = 4, 2 for CW = 8)
+    int cur = 0;
+    int s = 0, ks = 0, tile = tb;
+    int fs = 0, fph = 0, fks = 0, ftile = tb;
+    for (int i = 0; i < n_st + NS; ++i) {
+      if (i >= NS) {
+        bool ok = true;
+        if (lane == 0) {
+          ok = false;
+          for (uint32_t k = 0; k < kSpinLimit && !ok; ++k) {
+            ok = mbar_try_wait(&empty[fs], fph);
+            if (!ok && *abort_flag) break;
+          }
+          if (!ok) {
+            if (!*abort_flag) set_status(AIB_DEV_TIMEOUT_EMPTY);
+            *abort_flag = 1;
+          }
+        }
+        ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+        if (!ok) {
+          if (lane == 0)
+            for (int k = i - NS; k < min(i, n_st); ++k) mbar_wait(&full[k % NS], (k / NS) & 1, AIB_DEV_TIMEOUT_FULL);
+          break;
+        }
+        if (fks == KS - 1 && lane < R && !*abort_flag) {
+          const int row = ftile * R + lane;
+          if (row < p.N) {
+            const float* part = reinterpret_cast<const float*>(meta + fs * kTcSlotMeta + 128) + lane * 16;
+            float v = part[0];
+            for (int w = 1; w < PW; ++w) v += part[w];
+            if (MODE == 0)
+              p.y[row] = v;
+            else
+              p.y[row] += v;
+          }
+        }
+        if (++fks == KS) fks = 0, ++ftile;
+        if (++fs == NS) fs = 0, fph ^= 1;
+      }
+      if (i < n_st) {
+        uint32_t* mask = reinterpret_cast<uint32_t*>(meta + s * kTcSlotMeta);
+        mask[lane] = 0u;
+        __syncwarp();
+        if (ks == 0) cur = 0;
+        const int lr = (tile - tb) * R + lane;
+        if (lane < R && lr < nrows) {
+          const int a = rps[lr] - e0, b = rps[lr + 1] - e0;
+          const int lo = ks * CW * 256, hi = lo + CW * 256;
+          uint32_t* mw = mask + lane * wpr;
+          int q = a + cur;
+          for (; q < b; ++q) {
+            const int col = staged ? ecs[q] : p.ec[e0 + q];
+            if (col >= hi) break;
+            if (col >= lo) {
+              const int u = ((col - lo) >> 8) * 8 + ((col & 127) >> 4);
+              mw[u >> 5] |= 1u << (u & 31);
+            }
+          }
+          cur = q - a;
+        }
+        __syncwarp();
+        if (lane == 0) {
+          uint8_t* st = ring + static_cast<size_t>(s) * kRowsStage;
+          mbar_arrive_expect_tx(&full[s], kRowsStage);
+          tma_load_3d(st, &tm8, &full[s], 0, ks * CW, tile * R);
+          tma_load_3d(st + m8_bytes, &tme4, &full[s], 0, ks * CW, tile * R);
+        }
+        if (++ks == KS) ks = 0, ++tile;
+        if (++s == NS) s = 0;
+      }
+    }
+    return;
+  }
+
+  // ---------------- consumers: x prologue into the three-part B records
+  pdl_wait();
+  const int K = p.K;
+  float rs = 1.0f;
+  if (RMS) {
+    const float4* xg = reinterpret_cast<const float4*>(p.x);
+    float ss = 0.0f;
+    for (int k = tid; k < K / 4; k += kTcConsumers) {
+      const float4 v = xg[k];
+      ss += (v.x * v.x + v.y * v.y) + (v.z * v.z + v.w * v.w);
+    }
+    ss = warp_sum(ss);
+    if (lane == 0) rms_red[tid >> 5] = ss;
+    named_sync(1, kTcConsumers);
+    float tot = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kTcConsumers / 32; ++w) tot += rms_red[w];
+    rs = rsqrtf(tot / static_cast<float>(K) + p.eps);
+  }
+  for (int pr = tid; pr < K / 4; pr += kTcConsumers) {  // (low pair, high pair) of one record
+    const int gc = pr >> 6, c = (pr & 63) * 2;           // low column c, c+1 and high 128+c, 129+c of chunk gc
+    float v[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int k = gc * 256 + c + (e & 1) + (e >> 1) * 128;
+      float x = (MODE == 2) ? silu_mul(p.x[k], p.x[K + k]) : p.x[k];
+      if (RMS) x = bf16_to_f32(p.lnw[k]) * (x * rs);
+      v[e] = x;
+    }
+    uint32_t w[3][2];
+#pragma unroll
+    for (int sp = 0; sp < 3; ++sp) {
+      uint16_t b[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        b[e] = f32_to_bf16_rne(v[e]);
+        v[e] -= bf16_to_f32(b[e]);
+      }
+      w[sp][0] = static_cast<uint32_t>(b[0]) | (static_cast<uint32_t>(b[1]) << 16);
+      w[sp][1] = static_cast<uint32_t>(b[2]) | (static_cast<uint32_t>(b[3]) << 16);
+    }
+    const int blk = c >> 6, t = (c >> 4) & 3, i = (c & 15) >> 1;
+#pragma unroll
+    for (int sp = 0; sp < 3; ++sp)
+      *reinterpret_cast<uint2*>(xr + tc_xrec(p.nch, gc, i, blk, t, sp)) = make_uint2(w[sp][0], w[sp][1]);
+  }
+  named_sync(1, kTcConsumers);
+
+  const int warp = tid >> 5, g = lane >> 2, t = lane & 3;
+  const int hh = warp & 1, q = (warp >> 1) % CW, rg = (warp >> 1) / CW;
+  const int par = g & 1, blk = hh ^ par;
+  const int rA = rg * 16 + g, rB = rA + 8;
+  const uint32_t colo = static_cast<uint32_t>(q * 256 + blk * 64 + 16 * t);
+  const uint32_t m8A = static_cast<uint32_t>(rA * CW * 256) + colo, m8B = static_cast<uint32_t>(rB * CW * 256) + colo;
+  const uint32_t e4o = static_cast<uint32_t>(R * CW * 256 + q * 128 + blk * 64 + 16 * t);
+  const uint32_t e4A = e4o + static_cast<uint32_t>(rA * CW * 128), e4B = e4o + static_cast<uint32_t>(rB * CW * 128);
+  const int ubit = q * 8 + blk * 4 + t;  // the lane's unit inside the stage's row segment
+  const int mwA = rA * (CW / 4) + (ubit >> 5), mwB = rB * (CW / 4) + (ubit >> 5);
+  const uint32_t mbit = 1u << (ubit & 31);
+  const bool bl = g < 6;  // lanes supplying a B column (parts 0..2 x 2 parities); columns 6, 7 stay zero
+  const int sp = g >> 1;
+  const uint32_t base7 = (static_cast<uint32_t>(p.base) << 7) | (static_cast<uint32_t>(p.base) << 23);
+  const uint32_t k128 = p.k128, k8 = p.k8;
+
+  // exact value of x[col] from its three parts
+  auto xval = [&](int col) -> float {
+    const int gc = col >> 8, cc = col & 255, hf = cc >> 7, c = cc & 127;
+    const int b2 = c >> 6, t2 = (c >> 4) & 3, i2 = (c & 15) >> 1, sh = (c & 1) * 16;
+    float v = 0.0f;
+    float parts[3];
+#pragma unroll
+    for (int s2 = 0; s2 < 3; ++s2) {
+      const uint32_t wv = *reinterpret_cast<const uint32_t*>(xr + tc_xrec(p.nch, gc, i2, b2, t2, s2) + hf * 4);
+      parts[s2] = bf16_to_f32(static_cast<uint16_t>(wv >> sh));
+    }
+    v = (parts[0] + parts[1]) + parts[2];
+    return v;
+  };
+  // exceptions of local row lr that fall in this lane's unit (chunk gc), times x
+  auto exc_sum = [&](int lr, int gc) -> float {
+    const int a = rps[lr] - e0, b = rps[lr + 1] - e0;
+    const int j = blk * 4 + t;
+    float sacc = 0.0f;
+    for (int k = a; k < b; ++k) {
+      const int col = staged ? ecs[k] : p.ec[e0 + k];
+      if ((col >> 8) > gc) break;
+      if ((col >> 8) == gc && ((col & 127) >> 4) == j) sacc += p.ev[e0 + k] * xval(col);
+    }
+    return sacc;
+  };
+
+  bool aborted = false;
+  float acc[2][4] = {{0.0f, 0.0f, 0.0f, 0.0f}, {0.0f, 0.0f, 0.0f, 0.0f}};
+  float exA = 0.0f, exB = 0.0f;
+  int s = 0, ph = 0, ks = 0, tile = tb;
+  for (int it = 0; it < n_st; ++it) {
+    // warp-uniform: the MMAs below must run with all 32 lanes converged
+    const bool ok = __all_sync(0xffffffffu, !aborted && wait_full(&full[s], ph, abort_flag));
+    if (!ok) aborted = true;
+    const int gc = ks * CW + q;
+    const uint8_t* sm = meta + s * kTcSlotMeta;
+    if (ok && gc < p.nch) {
+      const uint8_t* st = ring + static_cast<size_t>(s) * kRowsStage;
+      const uint32_t* mask = reinterpret_cast<const uint32_t*>(sm);
+      const bool xa = mask[mwA] & mbit, xb = mask[mwB] & mbit;
+      const uint4 LA = *reinterpret_cast<const uint4*>(st + m8A);
+      const uint4 HA = *reinterpret_cast<const uint4*>(st + m8A + 128);
+      const uint4 EA = *reinterpret_cast<const uint4*>(st + e4A);
+      const uint4 LB = *reinterpret_cast<const uint4*>(st + m8B);
+      const uint4 HB = *reinterpret_cast<const uint4*>(st + m8B + 128);
+      const uint4 EB = *reinterpret_cast<const uint4*>(st + e4B);
+      const uint32_t la[4] = {LA.x, LA.y, LA.z, LA.w}, ha[4] = {HA.x, HA.y, HA.z, HA.w}, ea[4] = {EA.x, EA.y, EA.z, EA.w};
+      const uint32_t lb[4] = {LB.x, LB.y, LB.z, LB.w}, hb[4] = {HB.x, HB.y, HB.z, HB.w}, eb[4] = {EB.x, EB.y, EB.z, EB.w};
+      // this lane's B records for MMA i: xg + i * (128 or 64)
+      const uint8_t* xg = sp < 2 ? xr + (gc * 8) * 128 + (blk * 2 + sp) * 32 + t * 8
+                                 : xr + p.nch * 1024 + (gc * 8) * 64 + blk * 32 + t * 8;
+      const int xstep = sp < 2 ? 128 : 64;
+      // mma.sync.aligned needs the whole warp on the same instruction: the path choice is warp-uniform
+      if (!__any_sync(0xffffffffu, xa || xb)) {  // common case: no exception in any unit of the warp
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int wd = i >> 1;
+          const uint32_t sel = (i & 1) ? 0xB3A2u : 0x9180u, esel = (i & 1) ? 0x4342u : 0x4140u;
+          const uint32_t xa2 = prmt(ea[wd], 0u, esel), xb2 = prmt(eb[wd], 0u, esel);
+          const uint32_t a0 = (prmt(la[wd], 0u, sel) & 0x807F807Fu) | ((xa2 & 0x000F000Fu) * k128 + base7);
+          const uint32_t a1 = (prmt(lb[wd], 0u, sel) & 0x807F807Fu) | ((xb2 & 0x000F000Fu) * k128 + base7);
+          const uint32_t a2 = (prmt(ha[wd], 0u, sel) & 0x807F807Fu) | ((xa2 & 0x00F000F0u) * k8 + base7);
+          const uint32_t a3 = (prmt(hb[wd], 0u, sel) & 0x807F807Fu) | ((xb2 & 0x00F000F0u) * k8 + base7);
+          uint2 bb = make_uint2(0u, 0u);
+          if (bl) bb = *reinterpret_cast<const uint2*>(xg + i * xstep);
+          mma_bf16(acc[i & 1], a0, a1, a2, a3, bb.x, bb.y);
+        }
+      } else {  // code-15 elements of the lanes' flagged units decode to 0; their exact values are added below
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int wd = i >> 1;
+          const uint32_t sel = (i & 1) ? 0xB3A2u : 0x9180u, esel = (i & 1) ? 0x4342u : 0x4140u;
+          const uint32_t xa2 = prmt(ea[wd], 0u, esel), xb2 = prmt(eb[wd], 0u, esel);
+          const uint32_t cAl = xa2 & 0x000F000Fu, cAh = xa2 & 0x00F000F0u;
+          const uint32_t cBl = xb2 & 0x000F000Fu, cBh = xb2 & 0x00F000F0u;
+          uint32_t a0 = (prmt(la[wd], 0u, sel) & 0x807F807Fu) | (cAl * k128 + base7);
+          uint32_t a1 = (prmt(lb[wd], 0u, sel) & 0x807F807Fu) | (cBl * k128 + base7);
+          uint32_t a2 = (prmt(ha[wd], 0u, sel) & 0x807F807Fu) | (cAh * k8 + base7);
+          uint32_t a3 = (prmt(hb[wd], 0u, sel) & 0x807F807Fu) | (cBh * k8 + base7);
+          if (xa) {
+            a0 = clear15(a0, cAl);
+            a2 = clear15(a2, cAh >> 4);
+          }
+          if (xb) {
+            a1 = clear15(a1, cBl);
+            a3 = clear15(a3, cBh >> 4);
+          }
+          uint2 bb = make_uint2(0u, 0u);
+          if (bl) bb = *reinterpret_cast<const uint2*>(xg + i * xstep);
+          if (i & 1)
+            mma_bf16(acc[1], a0, a1, a2, a3, bb.x, bb.y);
+          else
+            mma_bf16(acc[0], a0, a1, a2, a3, bb.x, bb.y);
+        }
+        const int lt = (tile - tb) * R;
+        if (xa) exA += exc_sum(lt + rA, gc);
+        if (xb) exB += exc_sum(lt + rB, gc);
+      }
+    }
+    if (ks == KS - 1) {  // tile complete: row g takes the columns of its parity (parts 0..2 on quads t = 0..2)
+      float vA = par ? (acc[0][1] + acc[1][1]) : (acc[0][0] + acc[1][0]);
+      float vB = par ? (acc[0][3] + acc[1][3]) : (acc[0][2] + acc[1][2]);
+      if (t == 3) vA = vB = 0.0f;
+      vA += exA;
+      vB += exB;
+      vA += __shfl_xor_sync(0xffffffffu, vA, 1);
+      vB += __shfl_xor_sync(0xffffffffu, vB, 1);
+      vA += __shfl_xor_sync(0xffffffffu, vA, 2);
+      vB += __shfl_xor_sync(0xffffffffu, vB, 2);
+      if (t == 0) {
+        float* part = reinterpret_cast<float*>(const_cast<uint8_t*>(sm) + 128);
+        const int wi = q * 2 + hh;
+        part[rA * 16 + wi] = vA;
+        part[rB * 16 + wi] = vB;
+      }
+#pragma unroll
+      for (int a = 0; a < 2; ++a)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) acc[a][c] = 0.0f;
       exA = exB = 0.0f;
     }
     __syncwarp();
@@ -1186,7 +1555,7 @@ static int run_rows(const aib_c12* c, const float* x, float* y, int mode, const 
   if (rc) return rc;
   RowsParams p{c->rp, c->ec, c->ev, x, y, lnw, eps, c->base, c->N, c->K, nch, R, CW, nch / CW, tiles, NS,
                static_cast<int>(xs_off), static_cast<int>(rps_off), static_cast<int>(ecs_off), ecap,
-               static_cast<int>(ring_off)};
+               static_cast<int>(ring_off), 128u, 8u, 65536u};
   auto go = [&](auto kernel) -> int {
     const int r2 = allow_smem(kernel, smem);
     if (r2) return r2;
@@ -1202,11 +1571,66 @@ static int run_rows(const aib_c12* c, const float* x, float* y, int mode, const 
   return go(gemv_rows_kernel<2, false>);
 }
 
-static int g_variant = 2;  // 0: tensor-core kernel, 1: CUDA-core 12 KB-stage kernel, 2: wide-stage kernel
+// Wide-stage tensor-core kernel: R = 32 rows x 4 chunks (K a multiple of 1024) or 16 rows x 8 chunks (K a
+// multiple of 2048, finer row tiles); ENOTSUP when x's three-part records do not fit.
+static int run_tc(const aib_c12* c, const float* x, float* y, int mode, const uint16_t* lnw, float eps,
+                  cudaStream_t s) {
+  const int nch = c->K / 256;
+  if (nch % 4) return fail(AIB_ENOTSUP, "aib_gemv_c12: K=%d is not a multiple of 1024", c->K);
+  if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(lnw) & 7))
+    return fail(AIB_ENOTSUP, "aib_gemv_c12: x / lnw not aligned for vector loads");
+  const int CW = nch % 8 == 0 ? 8 : 4;
+  const int R = 128 / CW;
+  const int tiles = (c->N + R - 1) / R;
+  const int grid = std::min(tiles, sm_count());
+  const int rows_max = ((tiles + grid - 1) / grid) * R;
+  // layout: header + NS slot records, x records (6 bytes per column), row pointers, staged exception
+  // columns (at least 1024), ring; the deepest ring that fits
+  int NS = 8;
+  size_t xs_off = 0, rps_off = 0, ecs_off = 0;
+  for (; NS >= 2; --NS) {
+    xs_off = 1024 + static_cast<size_t>(NS) * kTcSlotMeta;
+    rps_off = xs_off + static_cast<size_t>(nch) * 1536;
+    ecs_off = rps_off + ((static_cast<size_t>(rows_max + 1) * 4 + 127) / 128) * 128;
+    const size_t ring_need = ((ecs_off + 4096 + 1023) / 1024) * 1024;
+    if (ring_need + static_cast<size_t>(NS) * kRowsStage <= kSmemMax) break;
+  }
+  if (NS < 2) return fail(AIB_ENOTSUP, "aib_gemv_c12: K=%d too large for the tensor-core kernel", c->K);
+  const size_t ring_off = ((kSmemMax - static_cast<size_t>(NS) * kRowsStage) / 1024) * 1024;
+  const int ecap = static_cast<int>((ring_off - ecs_off) / 4);
+  const size_t smem = ring_off + static_cast<size_t>(NS) * kRowsStage;
+  CUtensorMap tm8, tme4;
+  int rc = make_maps(c, R, CW, &tm8, &tme4);
+  if (rc) return rc;
+  RowsParams p{c->rp, c->ec, c->ev, x, y, lnw, eps, c->base, c->N, c->K, nch, R, CW, nch / CW, tiles, NS,
+               static_cast<int>(xs_off), static_cast<int>(rps_off), static_cast<int>(ecs_off), ecap,
+               static_cast<int>(ring_off), 128u, 8u, 65536u};
+  auto go = [&](auto kernel) -> int {
+    const int r2 = allow_smem(kernel, smem);
+    if (r2) return r2;
+    return launch(kernel, dim3(grid), dim3(kTcThreads), smem, s, "aib_gemv_c12(T=1, tensor)", tm8, tme4, p);
+  };
+  if (lnw) {
+    if (mode == 0) return go(gemv_tc_kernel<0, true>);
+    if (mode == 1) return go(gemv_tc_kernel<1, true>);
+    return go(gemv_tc_kernel<2, true>);
+  }
+  if (mode == 0) return go(gemv_tc_kernel<0, false>);
+  if (mode == 1) return go(gemv_tc_kernel<1, false>);
+  return go(gemv_tc_kernel<2, false>);
+}
+
+static int g_variant = 2;  // 0: tensor-core 24 KB-stage kernel, 1: CUDA-core 12 KB stages, 2: CUDA-core 48 KB
+                           // stages, 3: tensor-core 48 KB stages
+
 
 static int run_t1(const aib_c12* c, const float* x, float* y, int mode, const uint16_t* lnw, float eps,
                   cudaStream_t s) {
-  if (g_variant == 2) {
+  if (g_variant == 3) {
+    const int rc = run_tc(c, x, y, mode, lnw, eps, s);
+    if (rc != AIB_ENOTSUP) return rc;
+  }
+  if (g_variant == 2 || g_variant == 3) {
     const int rc = run_rows(c, x, y, mode, lnw, eps, s);
     if (rc != AIB_ENOTSUP) return rc;  // other shapes use the 12 KB-stage kernel
   }

@@ -316,7 +316,9 @@ def micro(args):
     e1.record()
     torch.cuda.synchronize()
     us = e0.elapsed_time(e1) * 1e3 / reps
-    print(json.dumps({"micro": args.micro, "variant": args.gemv_variant, "N": N, "K": K, "bytes": c.nbytes, "us_per_launch": round(us, 2),
+    torch.cuda.synchronize()
+    st = _lib.status()
+    print(json.dumps({"micro": args.micro, "variant": args.gemv_variant, "device_status": st, "N": N, "K": K, "bytes": c.nbytes, "us_per_launch": round(us, 2),
                       "GBps": round(c.nbytes / us / 1e3, 1)}))
 
 
@@ -324,7 +326,7 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--micro", choices=["gemv", "gemv_down", "attn", "sample"], default=None,
                     help="time one kernel alone on a small case (for ncu) instead of the decode benchmark")
-    ap.add_argument("--gemv-variant", type=int, default=None, choices=[0, 1, 2],
+    ap.add_argument("--gemv-variant", type=int, default=None, choices=[0, 1, 2, 3],
                     help="codec GEMV kernel for --micro: 0 tensor-core (mma.sync), 1 CUDA-core 12 KB stages, 2 wide stages (default)")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=256)

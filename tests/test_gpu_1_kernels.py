@@ -112,7 +112,7 @@ GEMV_SHAPES = [(64, 1024, 0, False), (6144, 4096, 0, True), (4096, 4096, 1, Fals
                (100, 3072, 1, True), (33, 2048, 0, False), (1000, 5120, 2, False)]
 
 
-@pytest.fixture(params=[0, 1, 2], ids=["tensorcore", "cudacore", "wide"])
+@pytest.fixture(params=[0, 1, 2, 3], ids=["tensorcore", "cudacore", "wide", "widetc"])
 def variant(request, lib):
     lib.aib_gemv_set_variant(request.param)
     yield request.param
