@@ -157,7 +157,7 @@ AIB_DEV float dec1(uint32_t m, uint32_t code, uint32_t base) {
 AIB_DEV bool wait_full(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
   for (uint32_t i = 0; i < kSpinLimit; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (*abort_flag) return false;
+    if ((i & 63) == 63 && *abort_flag) return false;
   }
   set_status(AIB_DEV_TIMEOUT_FULL);
   *abort_flag = 1;
@@ -443,6 +443,13 @@ AIB_DEV void mma_bf16(float* d, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t 
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// (a & 0x807F807F) | (b & 0x7F807F80) in one LOP3: sign and mantissa bits from a, exponent field from b
+AIB_DEV uint32_t merge_sm_e(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("lop3.b32 %0, %1, %2, %3, 0xE4;" : "=r"(r) : "r"(a), "r"(b), "r"(0x807F807Fu));
+  return r;
+}
+
 // clear the 16-bit halves whose exponent code is 15 (exceptions decode to 0; their value is added apart)
 AIB_DEV uint32_t clear15(uint32_t z, uint32_t codes) {  // codes: low element in bits 0..3, high in 16..19
   uint32_t m = 0;
@@ -712,6 +719,104 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
   }
 }
 
+constexpr int kRowsStage = 128 * 384;  // wide-stage kernels: R * CW * (256 + 128) bytes, R * CW = 128
+
+// ---------------------------------------------------------- producer warp of the wide-stage kernels
+// Streams the CTA's (tile, chunk group) stages through the NS-slot ring. A slot's full barrier completes on
+// two arrivals plus the copied bytes: the first arrival comes with the TMA copies, issued as soon as the slot
+// is free; the second once the slot's bookkeeping is done, which therefore overlaps the copy:
+//  * finalise the stage that last used the slot: when it ended a row tile, add the `pw` per-warp partials of
+//    each of the tile's R rows in a fixed order and write y;
+//  * mark the units of the new stage that hold an exception (one bit per row and unit) from the CSR: row
+//    pointers in shared memory, exception columns staged in shared memory when they fit.
+// Meta layout per slot (slot_meta bytes): uint32 mask[32], then float partials[R * pw].
+template <int MODE>
+AIB_DEV void produce_wide(const CUtensorMap* tm8, const CUtensorMap* tme4, uint8_t* ring, uint8_t* meta,
+                          int slot_meta, uint64_t* full, uint64_t* empty, volatile int* abort_flag, const int* rps,
+                          const int* ecs, bool staged, int e0, const int32_t* ec, float* y, int N, int tb, int n_st,
+                          int R, int CW, int KS, int NS, int nrows, int pw) {
+  const int lane = threadIdx.x & 31;
+  if (lane == 0) {
+    prefetch_tensormap(tm8);
+    prefetch_tensormap(tme4);
+  }
+  const uint32_t m8_bytes = static_cast<uint32_t>(R * CW * 256);
+  const int wpr = (CW * 8 + 31) / 32;  // mask words per row
+  int cur = 0;
+  int s = 0, round = 0, ks = 0, tile = tb;  // stage i: slot s, ring round i / NS
+  int fks = 0, ftile = tb;                  // stage i - NS (same slot)
+  for (int i = 0; i < n_st + NS; ++i) {
+    if (i >= NS) {  // the slot's previous stage must be consumed
+      bool ok = true;
+      if (lane == 0) {
+        ok = false;
+        for (uint32_t k = 0; k < kSpinLimit && !ok; ++k) {
+          ok = mbar_try_wait(&empty[s], (round - 1) & 1);
+          if (!ok && (k & 63) == 63 && *abort_flag) break;
+        }
+        if (!ok) {
+          if (!*abort_flag) set_status(AIB_DEV_TIMEOUT_EMPTY);
+          *abort_flag = 1;
+        }
+      }
+      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+      if (!ok) {  // never leave with copies in flight (both arrivals of every issued stage were made)
+        if (lane == 0)
+          for (int k = i - NS; k < min(i, n_st); ++k) mbar_wait(&full[k % NS], (k / NS) & 1, AIB_DEV_TIMEOUT_FULL);
+        return;
+      }
+    }
+    uint8_t* sm = meta + s * slot_meta;
+    if (i < n_st && lane == 0) {  // issue first: the copy is the long pole
+      uint8_t* st = ring + static_cast<size_t>(s) * kRowsStage;
+      mbar_arrive_expect_tx(&full[s], kRowsStage);
+      tma_load_3d(st, tm8, &full[s], 0, ks * CW, tile * R);
+      tma_load_3d(st + m8_bytes, tme4, &full[s], 0, ks * CW, tile * R);
+    }
+    if (i >= NS) {
+      if (fks == KS - 1 && lane < R && !*abort_flag) {
+        const int row = ftile * R + lane;
+        if (row < N) {
+          const float* part = reinterpret_cast<const float*>(sm + 128) + lane * pw;
+          float v = part[0];
+          for (int w = 1; w < pw; ++w) v += part[w];
+          if (MODE == 0)
+            y[row] = v;
+          else
+            y[row] += v;
+        }
+      }
+      if (++fks == KS) fks = 0, ++ftile;
+    }
+    if (i < n_st) {
+      uint32_t* mask = reinterpret_cast<uint32_t*>(sm);
+      mask[lane] = 0u;
+      __syncwarp();
+      if (ks == 0) cur = 0;
+      const int lr = (tile - tb) * R + lane;
+      if (lane < R && lr < nrows) {
+        const int a = rps[lr] - e0, b = rps[lr + 1] - e0;
+        const int lo = ks * CW * 256, hi = lo + CW * 256;
+        uint32_t* mw = mask + lane * wpr;
+        int q = a + cur;
+        for (; q < b; ++q) {
+          const int col = staged ? ecs[q] : ec[e0 + q];
+          if (col >= hi) break;
+          if (col >= lo) {
+            const int u = ((col - lo) >> 8) * 8 + ((col & 127) >> 4);
+            mw[u >> 5] |= 1u << (u & 31);
+          }
+        }
+        cur = q - a;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&full[s]);  // second arrival: bitmask written, old partials read
+      if (++ks == KS) ks = 0, ++tile;
+    }
+    if (++s == NS) s = 0, ++round;
+  }
+}
+
 // --------------------------------------------------------------------- T = 1 wide-stage kernel
 // A TMA copy costs an SM a roughly fixed time whatever its size (measured on B200: 4 KB copies stream at
 // ~1.8 TB/s chip-wide, 16 KB copies at ~6.7 TB/s), so this kernel moves 48 KB per stage in two copies: R rows
@@ -729,7 +834,6 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
 //    order and writes y. No CTA-wide barrier runs in the main loop.
 constexpr int kRowsConsumers = 512;
 constexpr int kRowsThreads = kRowsConsumers + 32;
-constexpr int kRowsStage = 128 * 384;  // R * CW * (256 + 128) bytes
 constexpr int kRowsSlotMeta = 256;     // per slot: 32-word exception bitmask + 32 row/warp partials
 constexpr int kRowsHeader = 1024 + 8 * kRowsSlotMeta;  // barriers [0,256), abort 256, RMS partials [512,1024)
 
@@ -771,7 +875,7 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
   const int nrows = min((te - tb) * R, p.N - row0);
   if (tid == 0) {
     for (int s = 0; s < NS; ++s) {
-      mbar_init(&full[s], 1);
+      mbar_init(&full[s], 2);  // TMA arrival + bookkeeping arrival
       mbar_init(&empty[s], kRowsConsumers / 32);
     }
     *abort_flag = 0;
@@ -788,83 +892,8 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
   pdl_trigger();
 
   if (tid >= kRowsConsumers) {  // ---------------- producer warp
-    if (lane == 0) {
-      prefetch_tensormap(&tm8);
-      prefetch_tensormap(&tme4);
-    }
-    const uint32_t m8_bytes = static_cast<uint32_t>(R * CW * 256);
-    const int wpr = L / 32;  // mask words per row
-    int cur = 0;             // lane r < R: cursor into its row's exceptions (advances over the tile's stages)
-    int s = 0, ph = 0, ks = 0, tile = tb;
-    int fs = 0, fph = 0, fks = 0, ftile = tb;  // stage being finalised (issued NS stages earlier)
-    for (int i = 0; i < n_st + NS; ++i) {
-      if (i >= NS) {  // finalise stage i - NS: its slot's consumers are done
-        bool ok = true;
-        if (lane == 0) {
-          ok = false;
-          for (uint32_t k = 0; k < kSpinLimit && !ok; ++k) {
-            ok = mbar_try_wait(&empty[fs], fph);
-            if (!ok && *abort_flag) break;
-          }
-          if (!ok) {
-            if (!*abort_flag) set_status(AIB_DEV_TIMEOUT_EMPTY);
-            *abort_flag = 1;
-          }
-        }
-        ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-        if (!ok) {
-          // drain: wait (bounded) for copies still in flight, then leave
-          if (lane == 0)
-            for (int k = i - NS; k < min(i, n_st); ++k) mbar_wait(&full[k % NS], (k / NS) & 1, AIB_DEV_TIMEOUT_FULL);
-          break;
-        }
-        if (fks == KS - 1 && lane < R && !*abort_flag) {
-          const int row = ftile * R + lane;
-          if (row < p.N) {
-            const float* part = reinterpret_cast<const float*>(meta + fs * kRowsSlotMeta + 128);
-            float v = part[lane * W];
-            for (int w = 1; w < W; ++w) v += part[lane * W + w];
-            if (MODE == 0)
-              p.y[row] = v;
-            else
-              p.y[row] += v;
-          }
-        }
-        if (++fks == KS) fks = 0, ++ftile;
-        if (++fs == NS) fs = 0, fph ^= 1;
-      }
-      if (i < n_st) {  // issue stage i into slot s, exception bitmask first
-        uint32_t* mask = reinterpret_cast<uint32_t*>(meta + s * kRowsSlotMeta);
-        mask[lane] = 0u;
-        __syncwarp();
-        if (ks == 0) cur = 0;
-        const int lr = (tile - tb) * R + lane;
-        if (lane < R && lr < nrows) {
-          const int a = rps[lr] - e0, b = rps[lr + 1] - e0;
-          const int lo = ks * CW * 256, hi = lo + CW * 256;
-          uint32_t* mw = mask + lane * wpr;
-          int q = a + cur;
-          for (; q < b; ++q) {
-            const int col = staged ? ecs[q] : p.ec[e0 + q];
-            if (col >= hi) break;
-            if (col >= lo) {
-              const int u = ((col - lo) >> 8) * 8 + ((col & 127) >> 4);
-              mw[u >> 5] |= 1u << (u & 31);
-            }
-          }
-          cur = q - a;
-        }
-        __syncwarp();
-        if (lane == 0) {
-          uint8_t* st = ring + static_cast<size_t>(s) * kRowsStage;
-          mbar_arrive_expect_tx(&full[s], kRowsStage);
-          tma_load_3d(st, &tm8, &full[s], 0, ks * CW, tile * R);
-          tma_load_3d(st + m8_bytes, &tme4, &full[s], 0, ks * CW, tile * R);
-        }
-        if (++ks == KS) ks = 0, ++tile;
-        if (++s == NS) s = 0, ph ^= 1;
-      }
-    }
+    produce_wide<MODE>(&tm8, &tme4, ring, meta, kRowsSlotMeta, full, empty, abort_flag, rps, ecs, staged, e0, p.ec,
+                       p.y, p.N, tb, n_st, R, CW, KS, NS, nrows, W);
     return;
   }
 
@@ -1027,7 +1056,7 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
 // the column order of parity par, and a row reads its result from the columns of its own parity.
 constexpr int kTcConsumers = 512;
 constexpr int kTcThreads = kTcConsumers + 32;
-constexpr int kTcSlotMeta = 128 + 32 * 16 * 4;  // per slot: 32-word exception mask, partials [32 rows][16 warps]
+constexpr int kTcSlotMeta = 128 + 256 * 4;  // per slot: 32-word exception mask, partials [R rows][2*CW warps]
 
 // Byte offset of the x record (8 bytes: low pair, high pair) for chunk gc, MMA i, lane quad t, column block
 // blk and part sp. Parts 0 and 1 of all (blk, t) form one 128-byte line per (gc, i) and part 2 a 64-byte line
@@ -1045,7 +1074,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint64_t* empty = full + 16;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + 256);
   float* rms_red = reinterpret_cast<float*>(smem + 512);
-  uint8_t* meta = smem + 1024;  // slot s: uint32 mask[32] at s*kTcSlotMeta, float part[32][16] at +128
+  uint8_t* meta = smem + 1024;  // slot s: uint32 mask[32] at s*kTcSlotMeta, float part[R][2*CW] at +128
   uint8_t* xr = smem + p.xs_off;
   int* rps = reinterpret_cast<int*>(smem + p.rps_off);
   int* ecs = reinterpret_cast<int*>(smem + p.ecs_off);
@@ -1061,7 +1090,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int nrows = min((te - tb) * R, p.N - row0);
   if (tid == 0) {
     for (int s = 0; s < NS; ++s) {
-      mbar_init(&full[s], 1);
+      mbar_init(&full[s], 2);  // TMA arrival + bookkeeping arrival
       mbar_init(&empty[s], kTcConsumers / 32);
     }
     *abort_flag = 0;
@@ -1076,83 +1105,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   __syncthreads();
   pdl_trigger();
 
-  if (tid >= kTcConsumers) {  // ---------------- producer warp (same protocol as gemv_rows_kernel)
-    if (lane == 0) {
-      prefetch_tensormap(&tm8);
-      prefetch_tensormap(&tme4);
-    }
-    const uint32_t m8_bytes = static_cast<uint32_t>(R * CW * 256);
-    const int wpr = CW * 8 / 32;  // mask words per row (1 for CW = 4, 2 for CW = 8)
-    int cur = 0;
-    int s = 0, ks = 0, tile = tb;
-    int fs = 0, fph = 0, fks = 0, ftile = tb;
-    for (int i = 0; i < n_st + NS; ++i) {
-      if (i >= NS) {
-        bool ok = true;
-        if (lane == 0) {
-          ok = false;
-          for (uint32_t k = 0; k < kSpinLimit && !ok; ++k) {
-            ok = mbar_try_wait(&empty[fs], fph);
-            if (!ok && *abort_flag) break;
-          }
-          if (!ok) {
-            if (!*abort_flag) set_status(AIB_DEV_TIMEOUT_EMPTY);
-            *abort_flag = 1;
-          }
-        }
-        ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-        if (!ok) {
-          if (lane == 0)
-            for (int k = i - NS; k < min(i, n_st); ++k) mbar_wait(&full[k % NS], (k / NS) & 1, AIB_DEV_TIMEOUT_FULL);
-          break;
-        }
-        if (fks == KS - 1 && lane < R && !*abort_flag) {
-          const int row = ftile * R + lane;
-          if (row < p.N) {
-            const float* part = reinterpret_cast<const float*>(meta + fs * kTcSlotMeta + 128) + lane * 16;
-            float v = part[0];
-            for (int w = 1; w < PW; ++w) v += part[w];
-            if (MODE == 0)
-              p.y[row] = v;
-            else
-              p.y[row] += v;
-          }
-        }
-        if (++fks == KS) fks = 0, ++ftile;
-        if (++fs == NS) fs = 0, fph ^= 1;
-      }
-      if (i < n_st) {
-        uint32_t* mask = reinterpret_cast<uint32_t*>(meta + s * kTcSlotMeta);
-        mask[lane] = 0u;
-        __syncwarp();
-        if (ks == 0) cur = 0;
-        const int lr = (tile - tb) * R + lane;
-        if (lane < R && lr < nrows) {
-          const int a = rps[lr] - e0, b = rps[lr + 1] - e0;
-          const int lo = ks * CW * 256, hi = lo + CW * 256;
-          uint32_t* mw = mask + lane * wpr;
-          int q = a + cur;
-          for (; q < b; ++q) {
-            const int col = staged ? ecs[q] : p.ec[e0 + q];
-            if (col >= hi) break;
-            if (col >= lo) {
-              const int u = ((col - lo) >> 8) * 8 + ((col & 127) >> 4);
-              mw[u >> 5] |= 1u << (u & 31);
-            }
-          }
-          cur = q - a;
-        }
-        __syncwarp();
-        if (lane == 0) {
-          uint8_t* st = ring + static_cast<size_t>(s) * kRowsStage;
-          mbar_arrive_expect_tx(&full[s], kRowsStage);
-          tma_load_3d(st, &tm8, &full[s], 0, ks * CW, tile * R);
-          tma_load_3d(st + m8_bytes, &tme4, &full[s], 0, ks * CW, tile * R);
-        }
-        if (++ks == KS) ks = 0, ++tile;
-        if (++s == NS) s = 0;
-      }
-    }
+  if (tid >= kTcConsumers) {  // ---------------- producer warp
+    produce_wide<MODE>(&tm8, &tme4, ring, meta, kTcSlotMeta, full, empty, abort_flag, rps, ecs, staged, e0, p.ec,
+                       p.y, p.N, tb, n_st, R, CW, KS, NS, nrows, PW);
     return;
   }
 
@@ -1277,13 +1232,19 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       if (!__any_sync(0xffffffffu, xa || xb)) {  // common case: no exception in any unit of the warp
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
+          // x2 = [0, e1, 0, e0] (two code bytes: low nibble = low-half column, high nibble = high-half column).
+          // High codes: x2*8 + base7 puts the high nibbles in the exponent fields and the low nibbles in
+          // mantissa bits that the merge discards (no carry reaches the exponent). Low codes: x2*128 + base7
+          // minus the high nibbles times 128 -- exact integer arithmetic, multiplies on the FMA pipe.
           const int wd = i >> 1;
           const uint32_t sel = (i & 1) ? 0xB3A2u : 0x9180u, esel = (i & 1) ? 0x4342u : 0x4140u;
           const uint32_t xa2 = prmt(ea[wd], 0u, esel), xb2 = prmt(eb[wd], 0u, esel);
-          const uint32_t a0 = (prmt(la[wd], 0u, sel) & 0x807F807Fu) | ((xa2 & 0x000F000Fu) * k128 + base7);
-          const uint32_t a1 = (prmt(lb[wd], 0u, sel) & 0x807F807Fu) | ((xb2 & 0x000F000Fu) * k128 + base7);
-          const uint32_t a2 = (prmt(ha[wd], 0u, sel) & 0x807F807Fu) | ((xa2 & 0x00F000F0u) * k8 + base7);
-          const uint32_t a3 = (prmt(hb[wd], 0u, sel) & 0x807F807Fu) | ((xb2 & 0x00F000F0u) * k8 + base7);
+          const uint32_t tA = xa2 * k128 + base7 - (xa2 & 0x00F000F0u) * k128;
+          const uint32_t tB = xb2 * k128 + base7 - (xb2 & 0x00F000F0u) * k128;
+          const uint32_t a0 = merge_sm_e(prmt(la[wd], 0u, sel), tA);
+          const uint32_t a1 = merge_sm_e(prmt(lb[wd], 0u, sel), tB);
+          const uint32_t a2 = merge_sm_e(prmt(ha[wd], 0u, sel), xa2 * k8 + base7);
+          const uint32_t a3 = merge_sm_e(prmt(hb[wd], 0u, sel), xb2 * k8 + base7);
           uint2 bb = make_uint2(0u, 0u);
           if (bl) bb = *reinterpret_cast<const uint2*>(xg + i * xstep);
           mma_bf16(acc[i & 1], a0, a1, a2, a3, bb.x, bb.y);
@@ -1333,8 +1294,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       if (t == 0) {
         float* part = reinterpret_cast<float*>(const_cast<uint8_t*>(sm) + 128);
         const int wi = q * 2 + hh;
-        part[rA * 16 + wi] = vA;
-        part[rB * 16 + wi] = vB;
+        part[rA * PW + wi] = vA;
+        part[rB * PW + wi] = vB;
       }
 #pragma unroll
       for (int a = 0; a < 2; ++a)
@@ -1592,7 +1553,7 @@ static int run_tc(const aib_c12* c, const float* x, float* y, int mode, const ui
     xs_off = 1024 + static_cast<size_t>(NS) * kTcSlotMeta;
     rps_off = xs_off + static_cast<size_t>(nch) * 1536;
     ecs_off = rps_off + ((static_cast<size_t>(rows_max + 1) * 4 + 127) / 128) * 128;
-    const size_t ring_need = ((ecs_off + 4096 + 1023) / 1024) * 1024;
+    const size_t ring_need = ((ecs_off + 1023) / 1024) * 1024;  // staged exception columns take what is left
     if (ring_need + static_cast<size_t>(NS) * kRowsStage <= kSmemMax) break;
   }
   if (NS < 2) return fail(AIB_ENOTSUP, "aib_gemv_c12: K=%d too large for the tensor-core kernel", c->K);
