@@ -1581,8 +1581,8 @@ static int run_tc(const aib_c12* c, const float* x, float* y, int mode, const ui
   return go(gemv_tc_kernel<2, false>);
 }
 
-static int g_variant = 2;  // 0: tensor-core 24 KB-stage kernel, 1: CUDA-core 12 KB stages, 2: CUDA-core 48 KB
-                           // stages, 3: tensor-core 48 KB stages
+static int g_variant = 3;  // 0: tensor-core 24 KB-stage kernel, 1: CUDA-core 12 KB stages, 2: CUDA-core 48 KB
+                           // stages, 3 (default): tensor-core 48 KB stages
 
 
 static int run_t1(const aib_c12* c, const float* x, float* y, int mode, const uint16_t* lnw, float eps,
@@ -1660,8 +1660,9 @@ using namespace aib;
 
 extern "C" {
 
-// Kernel selection for the T = 1 GEMV (tests and A/B timing): 0 = tensor-core kernel, 1 = CUDA-core kernel with
-// 12 KB stages, 2 = wide-stage kernel (default). Shapes a kernel cannot take fall back to kernel 1.
+// Kernel selection for the T = 1 GEMV (tests and A/B timing): 0 = tensor-core kernel with 24 KB stages,
+// 1 = CUDA-core kernel with 12 KB stages, 2 = CUDA-core wide-stage kernel, 3 = tensor-core wide-stage kernel
+// (default). Shapes a kernel cannot take fall back to kernel 2, then 1.
 void aib_gemv_set_variant(int v) { gemv::g_variant = v; }
 
 size_t aib_gemv_c12_workspace(const aib_c12* c, int T) {

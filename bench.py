@@ -327,7 +327,7 @@ def main():
     ap.add_argument("--micro", choices=["gemv", "gemv_down", "attn", "sample"], default=None,
                     help="time one kernel alone on a small case (for ncu) instead of the decode benchmark")
     ap.add_argument("--gemv-variant", type=int, default=None, choices=[0, 1, 2, 3],
-                    help="codec GEMV kernel for --micro: 0 tensor-core (mma.sync), 1 CUDA-core 12 KB stages, 2 wide stages (default)")
+                    help="codec GEMV kernel for --micro: 0 tensor-core 24 KB stages, 1 CUDA-core 12 KB stages, 2 CUDA-core 48 KB stages, 3 tensor-core 48 KB stages (default)")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=256)
     ap.add_argument("--warmup", type=int, default=8)

@@ -93,10 +93,11 @@ int aib_c12_decode(const aib_c12* c, int first, int last, void* out, int out_dty
  * lnw (bf16 bits [K], may be NULL): RMSNorm prologue of gemvc1_k (wcomp.py:75-86), T == 1 only.
  * x_stride / y_stride: elements between rows of X / Y (ignored for T == 1). */
 size_t aib_gemv_c12_workspace(const aib_c12* c, int T);
-/* Kernel choice for T == 1: 0 the tensor-core kernel (mma.sync bf16 with x split in 3 bf16 parts,
- * K <= 16384), 1 the CUDA-core fp32-FMA kernel with 12 KB stages, 2 (default) the CUDA-core kernel with 48 KB
- * stages (K a multiple of 1024). Shapes a kernel cannot take run on kernel 1. Same results within fp32 rounding;
- * for tests and A/B timing. No reference counterpart. */
+/* Kernel choice for T == 1: 0 the tensor-core kernel with 24 KB stages (mma.sync bf16, x split in 3 bf16 parts,
+ * K <= 16384), 1 the CUDA-core fp32-FMA kernel with 12 KB stages, 2 the CUDA-core kernel with 48 KB stages,
+ * 3 (default) the tensor-core kernel with 48 KB stages (2 and 3: K a multiple of 1024). Shapes a kernel cannot
+ * take fall back to 2, then 1. Same results within fp32 rounding; for tests and A/B timing. No reference
+ * counterpart. */
 void aib_gemv_set_variant(int variant);
 int aib_gemv_c12(const aib_c12* c, const float* x, float* y, int T, int x_stride, int y_stride, int mode,
                  const uint16_t* lnw, float eps, void* ws, size_t ws_bytes, void* stream);

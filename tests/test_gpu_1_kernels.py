@@ -116,7 +116,7 @@ GEMV_SHAPES = [(64, 1024, 0, False), (6144, 4096, 0, True), (4096, 4096, 1, Fals
 def variant(request, lib):
     lib.aib_gemv_set_variant(request.param)
     yield request.param
-    lib.aib_gemv_set_variant(2)  # library default
+    lib.aib_gemv_set_variant(3)  # library default
 
 
 @pytest.mark.parametrize("N,K,mode,rms", GEMV_SHAPES)
