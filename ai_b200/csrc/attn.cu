@@ -11,9 +11,12 @@
 // warp covers one bf16 row). Each CTA writes a partial (m, l, acc) to the workspace; the last CTA of a
 // group (atomic ticket, no waiting) merges the partials in split order -- starting, like the reference,
 // from the current token -- so results are deterministic. The ticket counters return to zero.
-// K/V rows of a CTA's range are staged into shared memory by bulk asynchronous copies (cp.async.bulk,
-// no multicast) through a ring of 32-position sub-chunks, so the whole range is in flight at once; the
-// merge loads every split's partial in parallel (weights exp(m_s - M) first, then the sums).
+// Inside a CTA every warp owns a contiguous slice of the range and walks it 32 positions at a time with
+// lane = position: each lane loads its K row and the block's V values straight from global memory (16-byte
+// loads, a whole block in flight per warp), scores the row against the G query heads with q broadcast from
+// shared memory (no reduction across lanes), and the block's softmax and P.V run warp-wide. The warps'
+// states are combined once, at the end. The merge loads every split's partial in parallel (weights
+// exp(m_s - M) first, then the sums).
 #include <algorithm>
 #include "common.cuh"
 
@@ -24,20 +27,14 @@ constexpr int kWarps = 8;
 constexpr int kThreads = 32 * kWarps;
 constexpr int GMAX = 8;
 
-AIB_DEV void bulk_g2s(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
-  asm volatile("cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                   smem_u32(smem_dst)),
-               "l"(reinterpret_cast<uint64_t>(gsrc)), "r"(bytes), "r"(smem_u32(bar))
-               : "memory");
-}
-
-constexpr int kSub = 32;   // positions per staged sub-chunk
+constexpr int kBlk = 32;  // positions per warp block (lane = position)
 constexpr int kMaxSplits = 32;
-constexpr int kSlots = 4;  // ring depth
 
+// Dynamic shared memory: the warps' final states [kWarps][GMAX][HD + 2], reused by the merge to stage the
+// splits' partials (at most kMaxSplits x GMAX x (HD + 2) floats).
 template <int HD>
 constexpr size_t ring_bytes() {
-  return static_cast<size_t>(kSlots) * kSub * HD * 2 * 2;
+  return static_cast<size_t>(kMaxSplits > kWarps ? kMaxSplits : kWarps) * GMAX * (HD + 2) * sizeof(float);
 }
 
 template <int HD>
@@ -47,14 +44,10 @@ struct Smem {
   float vcur[HD];
   float cur_score[GMAX];
   float cs[HD / 2], sn[HD / 2];
-  float wm[kWarps][GMAX], wl[kWarps][GMAX];
-  float wacc[kWarps][GMAX][HD];
-  float mw[kMaxSplits][GMAX];  // merge weights exp(m_s - M) per split
-  float mM[GMAX], mL[GMAX], mc[GMAX];
-  uint64_t bar[kSlots];
+  float pw[kWarps][GMAX][kBlk];  // each warp's block probabilities
+  float mw[kMaxSplits][GMAX];    // merge weights exp(m_s - M) per split
+  float mM[GMAX], mL[GMAX], mc[GMAX], ones[GMAX];
   int last;
-  int abort;
-  int issued;
 };
 
 // RMSNorm (weight w) + RoPE of one head vector held by a warp: lane owns elements lane + 32*i.
@@ -97,114 +90,160 @@ AIB_DEV void load_row(const uint16_t* p, float* o) {
   }
 }
 
-// Attention of the G query heads in sm.q over cache rows [j0, j1) of one group. The rows are streamed into
-// `ring` (dynamic shared memory) by bulk copies issued by thread 0, kSub positions per slot; every wait is
-// bounded and, on a timeout, all threads keep the same barrier sequence and skip the math. Writes the CTA
-// partial (acc[HD], m, l per head) to `part`.
-template <int HD>
-AIB_DEV void attend_range(Smem<HD>& sm, uint8_t* ring, const uint16_t* kc, const uint16_t* vc, int G, int j0, int j1,
+// Attention of the G query heads in sm.q over cache rows [j0, j1) of one group. Warp w takes a contiguous
+// slice of the range, 32 positions per block, lane = position:
+//  1. the lane loads its K row (HD bf16) and, for the block's positions, its HD/32 dimensions of each V row;
+//  2. scores against every head with q read from shared memory as broadcast float4s;
+//  3. per head: block max and sum over the lanes, p = exp(s - m'), rescale alpha = exp(m - m');
+//  4. P.V: the lane owns HD/32 dimensions of every head's accumulator, p comes from shared memory.
+// The warps' (m, l, acc) are combined in warp order at the end and written as the CTA partial to `part`.
+template <int HD, int G>
+AIB_DEV void attend_range(Smem<HD>& sm, uint8_t* ring, const uint16_t* kc, const uint16_t* vc, int j0, int j1,
                           float scale, float* part) {
-  constexpr int PER = HD / 32;  // dims per lane: 4 (HD=128) or 2 (HD=64)
-  constexpr uint32_t kRowBytes = HD * 2, kHalf = kSub * kRowBytes;
+  constexpr int PER = HD / 32;  // dims per lane in P.V
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  float q[GMAX][PER], acc[GMAX][PER], m[GMAX], l[GMAX];
+  const int n = j1 - j0, per_warp = (n + kWarps - 1) / kWarps;
+  const int w0 = j0 + min(n, warp * per_warp), w1 = j0 + min(n, (warp + 1) * per_warp);
+  float m[G], l[G], acc[G][PER];
 #pragma unroll
-  for (int h = 0; h < GMAX; ++h) {
+  for (int h = 0; h < G; ++h) {
     m[h] = -INFINITY;
     l[h] = 0.0f;
 #pragma unroll
-    for (int i = 0; i < PER; ++i) {
-      acc[h][i] = 0.0f;
-      q[h][i] = (h < G) ? sm.q[h][lane * PER + i] * scale : 0.0f;
-    }
+    for (int e = 0; e < PER; ++e) acc[h][e] = 0.0f;
   }
-  const int n = j1 - j0, nsub = (n + kSub - 1) / kSub;
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < kSlots; ++i) mbar_init(&sm.bar[i], 1);
-    sm.abort = 0;
-    sm.issued = 0;
-    fence_mbar_init();
-  }
-  __syncthreads();
-  volatile int* abort_flag = &sm.abort;
-  auto issue = [&](int i) {
-    sm.issued = i + 1;
-    const int p0 = j0 + i * kSub, cnt = min(kSub, j1 - p0);
-    uint8_t* slot = ring + static_cast<size_t>(i % kSlots) * 2 * kHalf;
-    mbar_arrive_expect_tx(&sm.bar[i % kSlots], 2 * cnt * kRowBytes);
-    bulk_g2s(slot, kc + static_cast<size_t>(p0) * HD, cnt * kRowBytes, &sm.bar[i % kSlots]);
-    bulk_g2s(slot + kHalf, vc + static_cast<size_t>(p0) * HD, cnt * kRowBytes, &sm.bar[i % kSlots]);
-  };
-  if (threadIdx.x == 0)
-    for (int i = 0; i < min(kSlots, nsub); ++i) issue(i);
-  for (int i = 0; i < nsub; ++i) {
-    bool ok = false;
-    if (!*abort_flag) {
-      for (uint32_t it = 0; it < kSpinLimit && !ok; ++it) {
-        ok = mbar_try_wait(&sm.bar[i % kSlots], (i / kSlots) & 1);
-        if (!ok && *abort_flag) break;
-      }
-      if (!ok && !*abort_flag) {
-        set_status(AIB_DEV_TIMEOUT_FULL);
-        *abort_flag = 1;
-      }
+  float* pw = &sm.pw[warp][0][0];
+  for (int b0 = w0; b0 < w1; b0 += kBlk) {
+    const int cnt = min(kBlk, w1 - b0);
+    const int pos = b0 + lane;
+    const bool valid = lane < cnt;
+    // 1. loads: K row of this lane's position, V slices of the block's positions
+    // All loads of the block are issued before any of them is used (volatile asm keeps them in program order
+    // ahead of the math), so the warp has its whole block (HD * 2 * 2 * 32 bytes) in flight at once.
+    uint4 kr[HD / 8];
+    const uint4* kp = reinterpret_cast<const uint4*>(kc + static_cast<size_t>(valid ? pos : b0) * HD);
+#pragma unroll
+    for (int c = 0; c < HD / 8; ++c)
+      asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                   : "=r"(kr[c].x), "=r"(kr[c].y), "=r"(kr[c].z), "=r"(kr[c].w)
+                   : "l"(kp + c));
+    uint32_t vr[kBlk][PER / 2];
+#pragma unroll
+    for (int pp = 0; pp < kBlk; ++pp) {
+      const int vp = b0 + min(pp, cnt - 1);
+      const uint32_t* vsrc = reinterpret_cast<const uint32_t*>(vc + static_cast<size_t>(vp) * HD + lane * PER);
+      if (PER == 4)
+        asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];"
+                     : "=r"(vr[pp][0]), "=r"(vr[pp][PER / 2 - 1])
+                     : "l"(vsrc));
+      else
+        asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(vr[pp][0]) : "l"(vsrc));
     }
-    if (ok) {
-      const uint8_t* slot = ring + static_cast<size_t>(i % kSlots) * 2 * kHalf;
-      const int cnt = min(kSub, j1 - (j0 + i * kSub));
-      for (int pp = warp; pp < cnt; pp += kWarps) {
-        float kv[PER], vv[PER];
-        load_row<PER>(reinterpret_cast<const uint16_t*>(slot + pp * kRowBytes) + lane * PER, kv);
-        load_row<PER>(reinterpret_cast<const uint16_t*>(slot + kHalf + pp * kRowBytes) + lane * PER, vv);
+    // 2. scores
+    float sc[G];
 #pragma unroll
-        for (int h = 0; h < GMAX; ++h) {
-          if (h >= G) break;
-          float sc = 0.0f;
+    for (int h = 0; h < G; ++h) sc[h] = 0.0f;
 #pragma unroll
-          for (int d = 0; d < PER; ++d) sc += q[h][d] * kv[d];
-          sc = warp_sum(sc);
-          const float mn = fmaxf(m[h], sc);
-          const float alpha = expf(m[h] - mn);
-          const float pr = expf(sc - mn);
-          l[h] = l[h] * alpha + pr;
+    for (int c = 0; c < HD / 8; ++c) {
+      const uint32_t w[4] = {kr[c].x, kr[c].y, kr[c].z, kr[c].w};
+      float kf[8];
 #pragma unroll
-          for (int d = 0; d < PER; ++d) acc[h][d] = acc[h][d] * alpha + pr * vv[d];
-          m[h] = mn;
+      for (int k = 0; k < 4; ++k) {
+        kf[2 * k] = __uint_as_float(w[k] << 16);
+        kf[2 * k + 1] = __uint_as_float(w[k] & 0xFFFF0000u);
+      }
+#pragma unroll
+      for (int h = 0; h < G; ++h) {
+        {
+          const float4 qa = *reinterpret_cast<const float4*>(&sm.q[h][c * 8]);
+          const float4 qb = *reinterpret_cast<const float4*>(&sm.q[h][c * 8 + 4]);
+          float a = sc[h];
+          a = fmaf(qa.x, kf[0], a);
+          a = fmaf(qa.y, kf[1], a);
+          a = fmaf(qa.z, kf[2], a);
+          a = fmaf(qa.w, kf[3], a);
+          a = fmaf(qb.x, kf[4], a);
+          a = fmaf(qb.y, kf[5], a);
+          a = fmaf(qb.z, kf[6], a);
+          a = fmaf(qb.w, kf[7], a);
+          sc[h] = a;
         }
       }
     }
-    __syncthreads();  // every warp is done with this slot
-    if (threadIdx.x == 0 && i + kSlots < nsub && !*abort_flag) {
-      fence_proxy_async();
-      issue(i + kSlots);
-    }
-  }
-  if (*abort_flag && threadIdx.x == 0) {  // never leave with copies in flight
-    const int last = sm.issued;
-    for (int i = max(0, last - kSlots); i < last; ++i) mbar_wait(&sm.bar[i % kSlots], (i / kSlots) & 1, AIB_DEV_TIMEOUT_FULL);
-  }
-  // combine the warps in order
+    // 3. block softmax per head
+    float alpha[G];
 #pragma unroll
-  for (int h = 0; h < GMAX; ++h) {
-    if (h >= G) break;
-    if (lane == 0) {
-      sm.wm[warp][h] = m[h];
-      sm.wl[warp][h] = l[h];
-    }
+    for (int h = 0; h < G; ++h) {
+      {
+        const float s = valid ? sc[h] * scale : -INFINITY;
+        float mb = s;
 #pragma unroll
-    for (int i = 0; i < PER; ++i) sm.wacc[warp][h][lane * PER + i] = acc[h][i];
+        for (int o = 16; o > 0; o >>= 1) mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, o));
+        const float mn = fmaxf(m[h], mb);
+        const float pr = valid ? expf(s - mn) : 0.0f;
+        float ps = pr;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
+        alpha[h] = (m[h] == -INFINITY) ? 0.0f : expf(m[h] - mn);
+        l[h] = l[h] * alpha[h] + ps;
+        m[h] = mn;
+        pw[h * kBlk + lane] = pr;
+      }
+    }
+    __syncwarp();
+    // 4. P.V
+#pragma unroll
+    for (int h = 0; h < G; ++h)
+#pragma unroll
+      for (int e = 0; e < PER; ++e) acc[h][e] *= alpha[h];
+#pragma unroll
+    for (int pp = 0; pp < kBlk; pp += 4) {
+#pragma unroll
+      for (int h = 0; h < G; ++h) {
+        {
+          const float4 p4 = *reinterpret_cast<const float4*>(&pw[h * kBlk + pp]);
+          const float pv[4] = {p4.x, p4.y, p4.z, p4.w};
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+#pragma unroll
+            for (int e2 = 0; e2 < PER / 2; ++e2) {
+              const uint32_t v = vr[pp + k][e2];
+              acc[h][2 * e2] = fmaf(pv[k], __uint_as_float(v << 16), acc[h][2 * e2]);
+              acc[h][2 * e2 + 1] = fmaf(pv[k], __uint_as_float(v & 0xFFFF0000u), acc[h][2 * e2 + 1]);
+            }
+          }
+        }
+      }
+    }
+    __syncwarp();  // pw is rewritten by the next block
+  }
+  // combine the warps in order through the dynamic buffer
+  float* wst = reinterpret_cast<float*>(ring);  // [kWarps][GMAX][HD + 2]
+#pragma unroll
+  for (int h = 0; h < G; ++h) {
+    {
+      float* dst = wst + (static_cast<size_t>(warp) * GMAX + h) * (HD + 2);
+#pragma unroll
+      for (int e = 0; e < PER; ++e) dst[lane * PER + e] = acc[h][e];
+      if (lane == 0) {
+        dst[HD] = m[h];
+        dst[HD + 1] = l[h];
+      }
+    }
   }
   __syncthreads();
   for (int idx = threadIdx.x; idx < G * HD; idx += kThreads) {
     const int h = idx / HD, d = idx % HD;
     float M = -INFINITY;
-    for (int w = 0; w < kWarps; ++w) M = fmaxf(M, sm.wm[w][h]);
+    for (int w = 0; w < kWarps; ++w) M = fmaxf(M, wst[(w * GMAX + h) * (HD + 2) + HD]);
     float L = 0.0f, A = 0.0f;
     if (M != -INFINITY) {
       for (int w = 0; w < kWarps; ++w) {
-        const float f = expf(sm.wm[w][h] - M);
-        L += sm.wl[w][h] * f;
-        A += sm.wacc[w][h][d] * f;
+        const float* src = wst + (w * GMAX + h) * (HD + 2);
+        if (src[HD] == -INFINITY) continue;
+        const float f = expf(src[HD] - M);
+        L += src[HD + 1] * f;
+        A += src[d] * f;
       }
     }
     float* ph = part + static_cast<size_t>(h) * (HD + 2);
@@ -214,6 +253,7 @@ AIB_DEV void attend_range(Smem<HD>& sm, uint8_t* ring, const uint16_t* kc, const
       ph[HD + 1] = L;
     }
   }
+  __syncthreads();  // the buffer is reused by the merge
 }
 
 // Merge S partials in split order on top of an initial state (m0, l0, acc0[d]; null = empty) and write out.
@@ -233,18 +273,26 @@ AIB_DEV void merge_write(Smem<HD>& sm, float* stage, const float* parts, int S, 
     for (int i = threadIdx.x; i < nf; i += kThreads) stage[i] = __ldcg(parts + i);
   }
   __syncthreads();
-  for (int h = threadIdx.x; h < G; h += kThreads) {
-    float M = m0 ? m0[h] : -INFINITY;
-    for (int s = 0; s < S; ++s) M = fmaxf(M, stage[(s * G + h) * (HD + 2) + HD]);
-    float L = (m0 && M != -INFINITY) ? l0[h] * expf(m0[h] - M) : 0.0f;
-    sm.mc[h] = (m0 && M != -INFINITY) ? expf(m0[h] - M) : 0.0f;
-    for (int s = 0; s < S; ++s) {
-      const float ms = stage[(s * G + h) * (HD + 2) + HD];
+  {  // statistics: warp h for head h, lane s for split s (S <= 32), fixed-order sums
+    const int lane = threadIdx.x & 31, h = threadIdx.x >> 5;
+    if (h < G) {
+      const float ms = lane < S ? stage[(lane * G + h) * (HD + 2) + HD] : -INFINITY;
+      float M = m0 ? m0[h] : -INFINITY;
+      float mm = ms;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) mm = fmaxf(mm, __shfl_xor_sync(0xffffffffu, mm, o));
+      M = fmaxf(M, mm);
       const float w = (ms == -INFINITY || M == -INFINITY) ? 0.0f : expf(ms - M);
-      sm.mw[s][h] = w;
-      L += w * stage[(s * G + h) * (HD + 2) + HD + 1];
+      if (lane < S) sm.mw[lane][h] = w;
+      float lw = lane < S ? w * stage[(lane * G + h) * (HD + 2) + HD + 1] : 0.0f;
+      // fixed-order sum over splits: gather to lane 0 in split order
+      float L = (m0 && M != -INFINITY) ? l0[h] * expf(m0[h] - M) : 0.0f;
+      for (int s2 = 0; s2 < S; ++s2) L += __shfl_sync(0xffffffffu, lw, s2);
+      if (lane == 0) {
+        sm.mL[h] = L;
+        sm.mc[h] = (m0 && M != -INFINITY) ? expf(m0[h] - M) : 0.0f;
+      }
     }
-    sm.mL[h] = L;
   }
   __syncthreads();
   for (int idx = threadIdx.x; idx < G * HD; idx += kThreads) {
@@ -256,7 +304,7 @@ AIB_DEV void merge_write(Smem<HD>& sm, float* stage, const float* parts, int S, 
 }
 
 // ------------------------------------------------------------------------------ fused T = 1 step
-template <int HD>
+template <int HD, int G>
 __global__ void __launch_bounds__(kThreads)
     rope_attn_kernel(const float* __restrict__ qkv, const uint16_t* __restrict__ qn, const uint16_t* __restrict__ kn,
                      const float* __restrict__ inv, const int64_t* __restrict__ pos_p, uint16_t* kc, uint16_t* vc,
@@ -265,7 +313,6 @@ __global__ void __launch_bounds__(kThreads)
   __shared__ Smem<HD> sm;
   extern __shared__ __align__(128) uint8_t ring[];
   const int s = blockIdx.x, S = gridDim.x, g = blockIdx.y;
-  const int G = H / KV;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   pdl_wait();
   const long long pos_ll = *pos_p;
@@ -310,7 +357,7 @@ __global__ void __launch_bounds__(kThreads)
   const int chunk = (n + S - 1) / S;
   const int j0 = min(n, s * chunk), j1 = min(n, j0 + chunk);
   float* part = ws_part + (static_cast<size_t>(g) * S + s) * G * (HD + 2);
-  attend_range<HD>(sm, ring, kg, vg, G, j0, j1, scale, part);
+  attend_range<HD, G>(sm, ring, kg, vg, j0, j1, scale, part);
   // ordered merge by the last CTA of the group
   __threadfence();
   __syncthreads();
@@ -321,11 +368,10 @@ __global__ void __launch_bounds__(kThreads)
   __syncthreads();
   if (sm.last) {
     __threadfence();
-    float l0[GMAX];
-#pragma unroll
-    for (int h = 0; h < GMAX; ++h) l0[h] = 1.0f;
+    if (threadIdx.x < GMAX) sm.ones[threadIdx.x] = 1.0f;  // the current token enters with weight 1
+    __syncthreads();
     merge_write<HD>(sm, reinterpret_cast<float*>(ring), ws_part + static_cast<size_t>(g) * S * G * (HD + 2), S, G,
-                    sm.cur_score, l0, sm.vcur, out + static_cast<size_t>(g) * G * HD);
+                    sm.cur_score, sm.ones, sm.vcur, out + static_cast<size_t>(g) * G * HD);
     if (threadIdx.x == 0) ws_cnt[g] = 0;
   }
   pdl_trigger();
@@ -369,7 +415,7 @@ __global__ void qk_rope_cache_kernel(const float* __restrict__ qkv, const uint16
   pdl_trigger();
 }
 
-template <int HD>
+template <int HD, int G>
 __global__ void __launch_bounds__(kThreads)
     attn_cached_kernel(const float* __restrict__ q, const uint16_t* kc, const uint16_t* vc,
                        const int64_t* __restrict__ pos_p, float* __restrict__ out, int H, int KV, int maxt,
@@ -377,7 +423,6 @@ __global__ void __launch_bounds__(kThreads)
   __shared__ Smem<HD> sm;
   extern __shared__ __align__(128) uint8_t ring[];
   const int s = blockIdx.x, S = gridDim.x, g = blockIdx.y, t = blockIdx.z;
-  const int G = H / KV;
   pdl_wait();
   const long long p = *pos_p + t;
   const bool ok = p >= 0 && p < maxt;
@@ -389,8 +434,8 @@ __global__ void __launch_bounds__(kThreads)
   const int j0 = min(n, s * chunk), j1 = min(n, j0 + chunk);
   const size_t slot = static_cast<size_t>(t) * KV + g;
   float* part = ws_part + (slot * S + s) * G * (HD + 2);
-  attend_range<HD>(sm, ring, kc + static_cast<size_t>(g) * maxt * HD, vc + static_cast<size_t>(g) * maxt * HD, G, j0,
-                   j1, scale, part);
+  attend_range<HD, G>(sm, ring, kc + static_cast<size_t>(g) * maxt * HD, vc + static_cast<size_t>(g) * maxt * HD, j0,
+                      j1, scale, part);
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -435,6 +480,36 @@ static int check_heads(int H, int KV, int HD) {
   return AIB_OK;
 }
 
+// Launch a kernel template instantiated for the group size G = H / KV (1..GMAX) and head dim HD.
+template <template <int, int> class KSel, typename... Args>
+static int launch_g(int HD, int G, dim3 grid, size_t smem, cudaStream_t s, const char* what, Args... args) {
+  auto go = [&](auto kernel) -> int {
+    const int rc = allow_smem(kernel, smem);
+    if (rc) return rc;
+    return launch(kernel, grid, dim3(kThreads), smem, s, what, args...);
+  };
+  switch (HD * 16 + G) {
+#define AIB_ATTN_CASE(hd, g) \
+  case hd * 16 + g:          \
+    return go(KSel<hd, g>::k);
+    AIB_ATTN_CASE(128, 1) AIB_ATTN_CASE(128, 2) AIB_ATTN_CASE(128, 3) AIB_ATTN_CASE(128, 4)
+    AIB_ATTN_CASE(128, 5) AIB_ATTN_CASE(128, 6) AIB_ATTN_CASE(128, 7) AIB_ATTN_CASE(128, 8)
+    AIB_ATTN_CASE(64, 1) AIB_ATTN_CASE(64, 2) AIB_ATTN_CASE(64, 3) AIB_ATTN_CASE(64, 4)
+    AIB_ATTN_CASE(64, 5) AIB_ATTN_CASE(64, 6) AIB_ATTN_CASE(64, 7) AIB_ATTN_CASE(64, 8)
+#undef AIB_ATTN_CASE
+    default:
+      return fail(AIB_ENOTSUP, "%s: HD=%d G=%d", what, HD, G);
+  }
+}
+template <int HD, int G>
+struct RopeAttnSel {
+  static constexpr auto k = rope_attn_kernel<HD, G>;
+};
+template <int HD, int G>
+struct AttnCachedSel {
+  static constexpr auto k = attn_cached_kernel<HD, G>;
+};
+
 }  // namespace attn
 }  // namespace aib
 
@@ -463,17 +538,10 @@ int aib_rope_attn_decode(const float* qkv, const uint16_t* qn, const uint16_t* k
   const int S = attn::splits(KV, 1, H / KV, HD);
   int* cnt = static_cast<int*>(ws);
   float* part = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + attn::kCntBytes);
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (HD == 128) {
-    rc = allow_smem(attn::rope_attn_kernel<128>, attn::ring_bytes<128>());
-    if (rc) return rc;
-    return launch(attn::rope_attn_kernel<128>, dim3(S, KV), dim3(attn::kThreads), attn::ring_bytes<128>(), s,
-                  "aib_rope_attn_decode", qkv, qn, kn, inv, pos, kc, vc, out, H, KV, maxt, eps, scale, part, cnt);
-  }
-  rc = allow_smem(attn::rope_attn_kernel<64>, attn::ring_bytes<64>());
-  if (rc) return rc;
-  return launch(attn::rope_attn_kernel<64>, dim3(S, KV), dim3(attn::kThreads), attn::ring_bytes<64>(), s,
-                "aib_rope_attn_decode", qkv, qn, kn, inv, pos, kc, vc, out, H, KV, maxt, eps, scale, part, cnt);
+  const size_t smem = HD == 128 ? attn::ring_bytes<128>() : attn::ring_bytes<64>();
+  return attn::launch_g<attn::RopeAttnSel>(HD, H / KV, dim3(S, KV), smem, static_cast<cudaStream_t>(stream),
+                                           "aib_rope_attn_decode", qkv, qn, kn, inv, pos, kc, vc, out, H, KV, maxt,
+                                           eps, scale, part, cnt);
 }
 
 int aib_qk_rope_cache(const float* qkv, const uint16_t* qn, const uint16_t* kn, const float* inv, const int64_t* pos,
@@ -506,17 +574,9 @@ int aib_attn_cached(const float* q, const uint16_t* kc, const uint16_t* vc, cons
   const int S = attn::splits(KV, T, H / KV, HD);
   int* cnt = static_cast<int*>(ws);
   float* part = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + attn::kCntBytes);
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (HD == 128) {
-    rc = allow_smem(attn::attn_cached_kernel<128>, attn::ring_bytes<128>());
-    if (rc) return rc;
-    return launch(attn::attn_cached_kernel<128>, dim3(S, KV, T), dim3(attn::kThreads), attn::ring_bytes<128>(), s,
-                  "aib_attn_cached", q, kc, vc, pos, out, H, KV, maxt, scale, part, cnt);
-  }
-  rc = allow_smem(attn::attn_cached_kernel<64>, attn::ring_bytes<64>());
-  if (rc) return rc;
-  return launch(attn::attn_cached_kernel<64>, dim3(S, KV, T), dim3(attn::kThreads), attn::ring_bytes<64>(), s,
-                "aib_attn_cached", q, kc, vc, pos, out, H, KV, maxt, scale, part, cnt);
+  const size_t smem = HD == 128 ? attn::ring_bytes<128>() : attn::ring_bytes<64>();
+  return attn::launch_g<attn::AttnCachedSel>(HD, H / KV, dim3(S, KV, T), smem, static_cast<cudaStream_t>(stream),
+                                             "aib_attn_cached", q, kc, vc, pos, out, H, KV, maxt, scale, part, cnt);
 }
 
 }  // extern "C"

@@ -81,17 +81,9 @@ int aib_rope_attn_decode_noalloc(const float* qkv, const uint16_t* qn, const uin
   cudaError_t e = cudaMemsetAsync(cnt, 0, static_cast<size_t>(KV) * sizeof(int), s);
   if (e != cudaSuccess)
     return fail(AIB_ECUDA, "aib_rope_attn_decode_noalloc: clearing counters: %s", cudaGetErrorString(e));
-  if (HD == 128) {
-    rc = allow_smem(attn::rope_attn_kernel<128>, attn::ring_bytes<128>());
-    if (rc) return rc;
-    return launch(attn::rope_attn_kernel<128>, dim3(S, KV), dim3(attn::kThreads), attn::ring_bytes<128>(), s,
-                  "aib_rope_attn_decode_noalloc", qkv, qn, kn, inv, pos, kc, vc, out, H, KV, maxt, eps, scale, part,
-                  cnt);
-  }
-  rc = allow_smem(attn::rope_attn_kernel<64>, attn::ring_bytes<64>());
-  if (rc) return rc;
-  return launch(attn::rope_attn_kernel<64>, dim3(S, KV), dim3(attn::kThreads), attn::ring_bytes<64>(), s,
-                "aib_rope_attn_decode_noalloc", qkv, qn, kn, inv, pos, kc, vc, out, H, KV, maxt, eps, scale, part, cnt);
+  const size_t smem = HD == 128 ? attn::ring_bytes<128>() : attn::ring_bytes<64>();
+  return attn::launch_g<attn::RopeAttnSel>(HD, H / KV, dim3(S, KV), smem, s, "aib_rope_attn_decode_noalloc", qkv, qn,
+                                           kn, inv, pos, kc, vc, out, H, KV, maxt, eps, scale, part, cnt);
 }
 
 }  // extern "C"

@@ -271,7 +271,8 @@ def micro_sample(args):
 
 
 def micro(args):
-    """One kernel alone on a small case (for ncu captures and quick A/B timing). gemv: the codec GEMV on a
+    """One kernel alone on a small case (for ncu captures and quick A/B timing), timed as `--steps` calls
+    captured in one CUDA graph and replayed (device time, no host launch overhead). gemv: the codec GEMV on a
     Qwen3-8B gu-shaped matrix [24576, 4096] (151 MB of planes, > L2), T = 1 with the RMS prologue;
     gemv_down: [4096, 12288] with the SiLU-gated input; attn: one layer's decode attention at ctx 4096;
     sample: the sampler on one vocabulary row."""
@@ -281,19 +282,31 @@ def micro(args):
     torch.cuda.set_device(0)
     if args.gemv_variant is not None:
         _lib.lib().aib_gemv_set_variant(args.gemv_variant)
-    if args.micro in ("attn", "sample"):
-        run, nbytes = (micro_attn if args.micro == "attn" else micro_sample)(args)
+    def timed(run, reps):
+        """Device time per call: `reps` calls captured in one CUDA graph (no host launch overhead), replayed."""
         for _ in range(3):
             run()
         torch.cuda.synchronize()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(graph, stream=s):
+                for _ in range(reps):
+                    run()
+        torch.cuda.current_stream().wait_stream(s)
+        graph.replay()
+        torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        reps = max(args.steps, 1)
         e0.record()
-        for _ in range(reps):
-            run()
+        graph.replay()
         e1.record()
         torch.cuda.synchronize()
-        us = e0.elapsed_time(e1) * 1e3 / reps
+        return e0.elapsed_time(e1) * 1e3 / reps
+
+    if args.micro in ("attn", "sample"):
+        run, nbytes = (micro_attn if args.micro == "attn" else micro_sample)(args)
+        us = timed(run, max(args.steps, 1))
         print(json.dumps({"micro": args.micro, "bytes": nbytes, "us_per_launch": round(us, 2),
                           "GBps": round(nbytes / us / 1e3, 1)}))
         return
@@ -305,17 +318,7 @@ def micro(args):
     lnw = torch.ones(K, dtype=torch.bfloat16, device="cuda")
     mode = 0 if args.micro == "gemv" else 2
     run = lambda: wcomp.gemvc1(x, c, y, mode, lnw=lnw if mode == 0 else None)  # noqa: E731
-    for _ in range(3):
-        run()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    reps = max(args.steps, 1)
-    e0.record()
-    for _ in range(reps):
-        run()
-    e1.record()
-    torch.cuda.synchronize()
-    us = e0.elapsed_time(e1) * 1e3 / reps
+    us = timed(run, max(args.steps, 1))
     torch.cuda.synchronize()
     st = _lib.status()
     print(json.dumps({"micro": args.micro, "variant": args.gemv_variant, "device_status": st, "N": N, "K": K, "bytes": c.nbytes, "us_per_launch": round(us, 2),
