@@ -18,6 +18,7 @@
 //     renormalisation and inverse CDF are evaluated in float64 with a fixed-order block scan against the
 //     softmax denominator from a fixed-order reduction -- deterministic run to run. If the nucleus (or, at
 //     top_p = 1, the sampled point) lies beyond the CMAX largest logits the row sets AIB_DEV_SAMPLER_CAP.
+#include <algorithm>
 #include <climits>
 #include "common.cuh"
 
@@ -160,12 +161,11 @@ AIB_DEV uint32_t select_kth(const Row& r, int V, int k, uint32_t floor, Shared& 
   return prefix;
 }
 
-__global__ void __launch_bounds__(kThreads)
-    sample_kernel(const float* __restrict__ logits, int V, int ld, aib_sample_params prm,
-                  const int32_t* __restrict__ prior, int n_prior, const int32_t* __restrict__ bitmask,
-                  const double* __restrict__ us, int64_t* __restrict__ out) {
-  extern __shared__ __align__(16) uint8_t dsm[];
-  __shared__ Shared sh;
+// The whole sampling of row b by one CTA of kThreads threads (dsm: smem_bytes(V) of dynamic shared memory).
+AIB_DEV void sample_row_full(uint8_t* dsm, Shared& sh, const float* __restrict__ logits, int V, int ld,
+                             const aib_sample_params& prm, const int32_t* __restrict__ prior, int n_prior,
+                             const int32_t* __restrict__ bitmask, const double* __restrict__ us,
+                             int64_t* __restrict__ out, int b) {
   const int words = (V + 31) >> 5;
   const int words_pad = (words + 3) & ~3;  // keeps every later array 16-byte aligned
   uint32_t* bitmap = reinterpret_cast<uint32_t*>(dsm);
@@ -173,8 +173,7 @@ __global__ void __launch_bounds__(kThreads)
   uint32_t* ckey = reinterpret_cast<uint32_t*>(pid + PMAX);
   int* cidx = reinterpret_cast<int*>(ckey + CMAX);
   double* cp = reinterpret_cast<double*>(cidx + CMAX);
-  const int b = blockIdx.x, tid = threadIdx.x;
-  pdl_wait();
+  const int tid = threadIdx.x;
 
   Row r;
   r.l = logits + static_cast<size_t>(b) * ld;
@@ -241,7 +240,6 @@ __global__ void __launch_bounds__(kThreads)
   const float T = prm.temperature;
   if (!(T > 0.0f) || best == -INFINITY) {
     if (tid == 0) out[b] = bi;
-    pdl_trigger();
     return;
   }
   const double Td = static_cast<double>(T);  // z = l.double() / T, as the reference
@@ -340,6 +338,351 @@ __global__ void __launch_bounds__(kThreads)
   cntle = block_sum_fixed<int>(cntle, sh.ired);
   const int pick = min(cntle, keep - 1);
   if (tid == 0) out[b] = cidx[pick];
+}
+
+__global__ void __launch_bounds__(kThreads)
+    sample_kernel(const float* __restrict__ logits, int V, int ld, aib_sample_params prm,
+                  const int32_t* __restrict__ prior, int n_prior, const int32_t* __restrict__ bitmask,
+                  const double* __restrict__ us, int64_t* __restrict__ out) {
+  extern __shared__ __align__(16) uint8_t dsm[];
+  __shared__ Shared sh;
+  pdl_wait();
+  sample_row_full(dsm, sh, logits, V, ld, prm, prior, n_prior, bitmask, us, out, blockIdx.x);
+  pdl_trigger();
+}
+
+// ------------------------------------------------------------------------------ two-phase fast path
+// Phase 1 (grid: slices x rows, kPartThreads threads): each CTA takes a slice of at most kSliceMax tokens of
+// one row, applies mask and penalties (prior ids of the slice counted in shared memory), and writes
+//   * its max logit and the first index holding it;
+//   * zmax_s = max/T and zsum_s = sum exp(l/T - zmax_s) in float64 over the slice (the softmax
+//     denominator when there is no top-k);
+//   * its candidates: every token whose key is >= the slice's C-th largest key (at most kCandCap; a slice
+//     with more ties than that flags overflow).
+// Phase 2 (one CTA of kThreads per row) merges the slices in slice order (deterministic): greedy from the
+// maxima; otherwise the N = top_k (or C) largest keys of the union are selected, sorted (key desc, index
+// asc) and the nucleus and inverse CDF are evaluated as in sample_row_full. Whenever the result could
+// depend on a token outside the union (top_k > C, an overflowing slice, or a nucleus that the N largest
+// tokens do not cover) the row falls back to sample_row_full: same tokens in every case.
+constexpr int kPartThreads = 256;
+constexpr int kSliceMax = 1280;   // 5 tokens per thread
+constexpr int kC = 64;            // candidates per slice (top_k <= kC uses the fast path)
+constexpr int kCandCap = 128;     // candidate slots per slice (ties at the C-th key)
+
+struct SlicePart {
+  double zmax, zsum;
+  float max;
+  int arg, ncand, overflow;
+};
+
+static int n_slices(int V) { return (V + kSliceMax - 1) / kSliceMax > 148 ? (V + kSliceMax - 1) / kSliceMax : std::min(148, (V + 255) / 256); }
+
+__global__ void __launch_bounds__(kPartThreads)
+    sample_part_kernel(const float* __restrict__ logits, int V, int ld, aib_sample_params prm,
+                       const int32_t* __restrict__ prior, int n_prior, const int32_t* __restrict__ bitmask,
+                       SlicePart* __restrict__ parts, uint32_t* __restrict__ ckeys, int* __restrict__ cids) {
+  __shared__ int cnt[kSliceMax];
+  __shared__ unsigned int hist[256];
+  __shared__ float fred[kPartThreads / 32];
+  __shared__ int ired[kPartThreads / 32];
+  __shared__ double dred[kPartThreads / 32];
+  __shared__ uint32_t s_prefix;
+  __shared__ int s_rem, s_nc;
+  const int sl = blockIdx.x, ns = gridDim.x, b = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int per = (V + ns - 1) / ns;
+  const int v0 = min(V, sl * per), v1 = min(V, v0 + per);
+  const float* l = logits + static_cast<size_t>(b) * ld;
+  const uint32_t* mask = bitmask ? reinterpret_cast<const uint32_t*>(bitmask) + static_cast<size_t>(b) * ((V + 31) >> 5) : nullptr;
+  for (int i = tid; i < kSliceMax; i += kPartThreads) cnt[i] = 0;
+  pdl_wait();
+  __syncthreads();
+  const bool penal = prior && n_prior > 0 &&
+                     (prm.repetition_penalty != 1.0f || prm.presence_penalty != 0.0f || prm.frequency_penalty != 0.0f);
+  if (penal)
+    for (int i = tid; i < n_prior; i += kPartThreads) {
+      const int x = prior[static_cast<size_t>(b) * n_prior + i];
+      if (x >= v0 && x < v1) atomicAdd(&cnt[x - v0], 1);
+    }
+  __syncthreads();
+  constexpr int E = kSliceMax / kPartThreads;
+  float x[E];
+  uint32_t key[E];
+  float best = -INFINITY;
+  int bi = INT_MAX;
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    const int v = v0 + e * kPartThreads + tid;
+    float xv = -INFINITY;
+    if (v < v1) {
+      xv = l[v];
+      if (mask && !((mask[v >> 5] >> (v & 31)) & 1u)) {
+        xv = -INFINITY;
+      } else {
+        const int c = cnt[v - v0];
+        if (c > 0) {
+          if (prm.repetition_penalty != 1.0f)
+            xv = (xv < 0.0f) ? __fmul_rn(xv, prm.repetition_penalty) : __fdiv_rn(xv, prm.repetition_penalty);
+          if (prm.presence_penalty != 0.0f || prm.frequency_penalty != 0.0f)
+            xv = __fsub_rn(xv, __fadd_rn(__fmul_rn(static_cast<float>(c), prm.frequency_penalty), prm.presence_penalty));
+        }
+      }
+      if (xv > best || (xv == best && v < bi)) best = xv, bi = v;
+    }
+    x[e] = xv;
+    key[e] = v < v1 ? fkey(xv) : 0u;
+  }
+  // max / first argmax of the slice
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ob > best || (ob == best && oi < bi)) best = ob, bi = oi;
+  }
+  if (lane == 0) fred[warp] = best, ired[warp] = bi;
+  __syncthreads();
+  best = -INFINITY;
+  bi = INT_MAX;
+  for (int w = 0; w < kPartThreads / 32; ++w)
+    if (fred[w] > best || (fred[w] == best && ired[w] < bi)) best = fred[w], bi = ired[w];
+  SlicePart* pp = parts + static_cast<size_t>(b) * ns + sl;
+  const float T = prm.temperature;
+  if (!(T > 0.0f)) {
+    if (tid == 0) pp->max = best, pp->arg = bi, pp->ncand = 0, pp->overflow = 0, pp->zmax = 0.0, pp->zsum = 0.0;
+    pdl_trigger();
+    return;
+  }
+  // float64 partial softmax denominator over the slice (fixed-order reduction)
+  const double Td = static_cast<double>(T);
+  const double zm = best == -INFINITY ? 0.0 : static_cast<double>(best) / Td;
+  double zs = 0.0;
+#pragma unroll
+  for (int e = 0; e < E; ++e)
+    if (x[e] != -INFINITY && e * kPartThreads + tid < v1 - v0) zs += exp(static_cast<double>(x[e]) / Td - zm);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) zs += __shfl_xor_sync(0xffffffffu, zs, o);
+  __syncthreads();
+  if (lane == 0) dred[warp] = zs;
+  __syncthreads();
+  zs = 0.0;
+  for (int w = 0; w < kPartThreads / 32; ++w) zs += dred[w];
+  // C-th largest key of the slice: 4 radix passes over the keys held in registers
+  const int kc = min(kC, v1 - v0);
+  uint32_t prefix = 0u, pmask = 0u;
+  int rem = kc;
+  for (int shift = 24; shift >= 0 && kc > 0; shift -= 8) {
+    __syncthreads();
+    hist[tid] = 0u;  // kPartThreads == 256 buckets
+    __syncthreads();
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      int bucket = 256;
+      if (e * kPartThreads + tid < v1 - v0 && (key[e] & pmask) == prefix) bucket = static_cast<int>((key[e] >> shift) & 0xFFu);
+      const unsigned peers = __match_any_sync(0xffffffffu, bucket);
+      if (bucket != 256 && lane == __ffs(peers) - 1) atomicAdd(&hist[bucket], static_cast<unsigned>(__popc(peers)));
+    }
+    __syncthreads();
+    if (tid == 0) {
+      int cum = 0, d;
+      for (d = 255; d > 0; --d) {
+        if (cum + static_cast<int>(hist[d]) >= rem) break;
+        cum += hist[d];
+      }
+      s_prefix = prefix | (static_cast<uint32_t>(d) << shift);
+      s_rem = rem - cum;
+    }
+    __syncthreads();
+    prefix = s_prefix;
+    rem = s_rem;
+    pmask |= 0xFFu << shift;
+  }
+  // candidates: keys >= the C-th key (finite logits)
+  if (tid == 0) s_nc = 0;
+  __syncthreads();
+  uint32_t* ck = ckeys + (static_cast<size_t>(b) * ns + sl) * kCandCap;
+  int* ci = cids + (static_cast<size_t>(b) * ns + sl) * kCandCap;
+  bool over = false;
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    const int v = v0 + e * kPartThreads + tid;
+    if (v < v1 && kc > 0 && key[e] >= prefix && x[e] != -INFINITY) {
+      const int slot = atomicAdd(&s_nc, 1);
+      if (slot < kCandCap) ck[slot] = key[e], ci[slot] = v; else over = true;
+    }
+  }
+  over = __syncthreads_or(over);
+  if (tid == 0) {
+    pp->max = best;
+    pp->arg = bi;
+    pp->zmax = zm;
+    pp->zsum = zs;
+    pp->ncand = min(s_nc, kCandCap);
+    pp->overflow = over ? 1 : 0;
+  }
+  pdl_trigger();
+}
+
+__global__ void __launch_bounds__(kThreads)
+    sample_merge_kernel(const float* __restrict__ logits, int V, int ld, aib_sample_params prm,
+                        const int32_t* __restrict__ prior, int n_prior, const int32_t* __restrict__ bitmask,
+                        const double* __restrict__ us, int64_t* __restrict__ out, int ns,
+                        const SlicePart* __restrict__ parts, const uint32_t* __restrict__ ckeys,
+                        const int* __restrict__ cids) {
+  extern __shared__ __align__(16) uint8_t dsm[];
+  __shared__ Shared sh;
+  const int b = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  pdl_wait();
+  const SlicePart* pp = parts + static_cast<size_t>(b) * ns;
+  // global max and first argmax, slices in order
+  float best = -INFINITY;
+  int bi = INT_MAX;
+  bool over = false;
+  int total = 0;
+  for (int s2 = 0; s2 < ns; ++s2) {
+    const SlicePart q = pp[s2];
+    if (q.max > best) best = q.max, bi = q.arg;
+    over |= q.overflow != 0;
+    total += q.ncand;
+  }
+  if (bi == INT_MAX) bi = 0;
+  const float T = prm.temperature;
+  if (!(T > 0.0f) || best == -INFINITY) {
+    if (tid == 0) out[b] = bi;
+    pdl_trigger();
+    return;
+  }
+  const int topk = prm.top_k;
+  const bool has_k = topk > 0 && topk < V;
+  if (over || (has_k && topk > kC)) {
+    sample_row_full(dsm, sh, logits, V, ld, prm, prior, n_prior, bitmask, us, out, b);
+    pdl_trigger();
+    return;
+  }
+  const double Td = static_cast<double>(T), Mz = static_cast<double>(best) / Td;
+  // N-th largest key of the union of the slices' candidates (radix select over the candidate lists)
+  const int N = has_k ? topk : kC;
+  const uint32_t* ckb = ckeys + static_cast<size_t>(b) * ns * kCandCap;
+  const int* cib = cids + static_cast<size_t>(b) * ns * kCandCap;
+  auto cand_at = [&](int i, uint32_t& k, int& id) -> bool {  // i-th slot of the concatenated lists
+    const int s2 = i / kCandCap, j = i % kCandCap;
+    if (j >= pp[s2].ncand) return false;
+    k = ckb[i];
+    id = cib[i];
+    return true;
+  };
+  uint32_t prefix = 0u, pmask = 0u;
+  int rem = min(N, total);
+  const int slots = ns * kCandCap;
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    __syncthreads();
+    for (int i = tid; i < 256; i += kThreads) sh.hist[i] = 0u;
+    __syncthreads();
+    for (int i0 = 0; i0 < slots; i0 += kThreads) {
+      const int i = i0 + tid;
+      int bucket = 256;
+      uint32_t k;
+      int id;
+      if (i < slots && cand_at(i, k, id) && (k & pmask) == prefix) bucket = static_cast<int>((k >> shift) & 0xFFu);
+      const unsigned peers = __match_any_sync(0xffffffffu, bucket);
+      if (bucket != 256 && lane == __ffs(peers) - 1) atomicAdd(&sh.hist[bucket], static_cast<unsigned>(__popc(peers)));
+    }
+    __syncthreads();
+    if (tid == 0) {
+      int cum = 0, d;
+      for (d = 255; d > 0; --d) {
+        if (cum + static_cast<int>(sh.hist[d]) >= rem) break;
+        cum += sh.hist[d];
+      }
+      sh.prefix = prefix | (static_cast<uint32_t>(d) << shift);
+      sh.ired[0] = rem - cum;
+    }
+    __syncthreads();
+    prefix = sh.prefix;
+    rem = sh.ired[0];
+    pmask |= 0xFFu << shift;
+  }
+  const uint32_t thr = prefix;
+  // gather the kept candidates (key >= thr) and sort them (key desc, index asc)
+  uint32_t* ckey = reinterpret_cast<uint32_t*>(dsm);
+  int* cidx = reinterpret_cast<int*>(ckey + CMAX);
+  double* cp = reinterpret_cast<double*>(cidx + CMAX);
+  __syncthreads();
+  if (tid == 0) sh.ncand = 0;
+  __syncthreads();
+  for (int i = tid; i < slots; i += kThreads) {
+    uint32_t k;
+    int id;
+    if (cand_at(i, k, id) && k >= thr) {
+      const int slot = atomicAdd(&sh.ncand, 1);
+      if (slot < CMAX) ckey[slot] = k, cidx[slot] = id;
+    }
+  }
+  __syncthreads();
+  const int nc = min(sh.ncand, CMAX);
+  int n2 = 1;
+  while (n2 < nc) n2 <<= 1;
+  for (int i = nc + tid; i < n2; i += kThreads) ckey[i] = 0u, cidx[i] = INT_MAX;
+  __syncthreads();
+  for (int k = 2; k <= n2; k <<= 1)
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      for (int i = tid; i < n2; i += kThreads) {
+        const int ixj = i ^ j;
+        if (ixj > i) {
+          const uint32_t ka = ckey[i], kb = ckey[ixj];
+          const int ia = cidx[i], ib = cidx[ixj];
+          const bool a_first = (ka > kb) || (ka == kb && ia < ib);
+          const bool up = (i & k) == 0;
+          if (a_first != up) ckey[i] = kb, ckey[ixj] = ka, cidx[i] = ib, cidx[ixj] = ia;
+        }
+      }
+      __syncthreads();
+    }
+  // softmax denominator: over the kept top-k set, or over the whole row from the slices (slice order)
+  double Z = 0.0;
+  if (has_k) {
+    double zpart = 0.0;
+    for (int i = tid; i < nc; i += kThreads) zpart += exp(static_cast<double>(key_value(ckey[i])) / Td - Mz);
+    Z = block_sum_fixed<double>(zpart, sh.dred);
+  } else {
+    for (int s2 = 0; s2 < ns; ++s2)
+      if (pp[s2].max != -INFINITY) Z += pp[s2].zsum * exp(pp[s2].zmax - Mz);
+  }
+  for (int i = tid; i < nc; i += kThreads) cp[i] = exp(static_cast<double>(key_value(ckey[i])) / Td - Mz) / Z;
+  __syncthreads();
+  if (tid == 0) {  // sequential exclusive scan of the (short) candidate list, fixed order
+    double run = 0.0;
+    for (int i = 0; i < nc; ++i) {
+      const double pi = cp[i];
+      cp[i] = run;
+      run += pi;
+    }
+    sh.dred[0] = run;  // mass of all candidates
+  }
+  __syncthreads();
+  const double top_p = static_cast<double>(prm.top_p), cand_mass = sh.dred[0];
+  // without top-k the candidates are the N largest logits of the row: fall back when the nucleus may extend
+  // past them (their mass does not reach top_p and the row has more tokens)
+  if (!has_k && nc < V && cand_mass < min(top_p, 1.0 - 1e-12)) {
+    __syncthreads();
+    sample_row_full(dsm, sh, logits, V, ld, prm, prior, n_prior, bitmask, us, out, b);
+    pdl_trigger();
+    return;
+  }
+  int keep = 0;
+  for (int i = tid; i < nc; i += kThreads) keep += (top_p >= 1.0 || cp[i] < top_p) ? 1 : 0;
+  keep = block_sum_fixed<int>(keep, sh.ired);
+  keep = max(1, min(keep, nc));
+  const double pl = exp(static_cast<double>(key_value(ckey[keep - 1])) / Td - Mz) / Z;
+  const double S = cp[keep - 1] + pl;
+  const double u = us ? us[b] : 0.5;
+  int cntle = 0;
+  for (int i = tid; i < keep; i += kThreads) {
+    const double incl_i = (i + 1 < keep) ? cp[i + 1] : S;
+    cntle += (incl_i / S <= u) ? 1 : 0;
+  }
+  cntle = block_sum_fixed<int>(cntle, sh.ired);
+  const int pick = min(cntle, keep - 1);
+  if (tid == 0) out[b] = cidx[pick];
+  (void)warp;
   pdl_trigger();
 }
 
@@ -356,16 +699,14 @@ using namespace aib;
 extern "C" {
 
 size_t aib_sample_workspace(int B, int V) {
-  (void)B;
-  (void)V;
-  return 0;
+  if (B <= 0 || V <= 0) return 0;
+  const size_t ns = static_cast<size_t>(samp::n_slices(V));
+  return static_cast<size_t>(B) * ns * (sizeof(samp::SlicePart) + samp::kCandCap * 8) + 256;
 }
 
 int aib_sample(const float* logits, int B, int V, int ld, const aib_sample_params* params, const int32_t* prior,
                int n_prior, const int32_t* bitmask, const double* u, int64_t* out_ids, void* ws, size_t ws_bytes,
                void* stream) {
-  (void)ws;
-  (void)ws_bytes;
   if (!logits || !params || !out_ids || B <= 0 || V <= 0 || ld < V)
     return fail(AIB_EINVAL, "aib_sample: bad arguments (B=%d V=%d ld=%d)", B, V, ld);
   if (n_prior < 0 || n_prior > samp::PMAX) return fail(AIB_EINVAL, "aib_sample: n_prior must be in 0..%d", samp::PMAX);
@@ -375,10 +716,26 @@ int aib_sample(const float* logits, int B, int V, int ld, const aib_sample_param
   if (!(p.repetition_penalty > 0.0f)) return fail(AIB_EINVAL, "aib_sample: repetition_penalty must be > 0");
   const size_t smem = samp::smem_bytes(V);
   if (smem > 227 * 1024) return fail(AIB_ENOTSUP, "aib_sample: vocabulary of %d too large", V);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (ws && ws_bytes >= aib_sample_workspace(B, V) && B <= 65535) {  // two-phase path
+    if (reinterpret_cast<uintptr_t>(ws) & 15) return fail(AIB_EINVAL, "aib_sample: workspace must be 16-byte aligned");
+    const int ns = samp::n_slices(V);
+    samp::SlicePart* parts = static_cast<samp::SlicePart*>(ws);
+    uint32_t* ck = reinterpret_cast<uint32_t*>(parts + static_cast<size_t>(B) * ns);
+    int* ci = reinterpret_cast<int*>(ck + static_cast<size_t>(B) * ns * samp::kCandCap);
+    int rc = launch(samp::sample_part_kernel, dim3(ns, B), dim3(samp::kPartThreads), 0, s, "aib_sample (slices)",
+                    logits, V, ld, p, prior, n_prior, bitmask, parts, ck, ci);
+    if (rc) return rc;
+    rc = allow_smem(samp::sample_merge_kernel, smem);
+    if (rc) return rc;
+    return launch(samp::sample_merge_kernel, dim3(B), dim3(samp::kThreads), smem, s, "aib_sample (merge)", logits, V,
+                  ld, p, prior, n_prior, bitmask, u, out_ids, ns, static_cast<const samp::SlicePart*>(parts),
+                  static_cast<const uint32_t*>(ck), static_cast<const int*>(ci));
+  }
   const int rc = allow_smem(samp::sample_kernel, smem);
   if (rc) return rc;
-  return launch(samp::sample_kernel, dim3(B), dim3(samp::kThreads), smem, static_cast<cudaStream_t>(stream),
-                "aib_sample", logits, V, ld, p, prior, n_prior, bitmask, u, out_ids);
+  return launch(samp::sample_kernel, dim3(B), dim3(samp::kThreads), smem, s, "aib_sample", logits, V, ld, p, prior,
+                n_prior, bitmask, u, out_ids);
 }
 
 }  // extern "C"

@@ -84,6 +84,7 @@ class Engine:
         self.out_ids = torch.zeros(MAXB, dtype=torch.int64, device=dev)
         self.u = torch.zeros(MAXB, dtype=torch.float64, device=dev)
         self.prior = torch.full((1, sampler.PMAX), -1, dtype=torch.int32, device=dev)
+        self.sample_ws = sampler.workspace(MAXB, self.cfg.V, dev)
         wsz = max(_lib.lib().aib_attn_workspace(H, KV, HD, maxt, t) for t in range(1, MAXB + 1))
         self.ws = torch.zeros(wsz, dtype=torch.uint8, device=dev)
         self.use_graphs = graphs
@@ -141,7 +142,7 @@ class Engine:
         self._head(T)
         r0 = T - rows
         sampler.sample_into(self.logits[r0:T], self.out_ids[r0:T], prm, self.u[:rows] if prm.temperature > 0 else None,
-                            self.prior if penal else None, None, B=rows)
+                            self.prior if penal else None, None, B=rows, ws=self.sample_ws)
         _lib.call("aib_step_advance", ptr(self.pos), ptr(self.ids), ptr(self.out_ids), T,
                   ptr(self.prior) if penal else None, sampler.PMAX if penal else 0, stream_ptr())
 

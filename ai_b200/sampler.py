@@ -20,9 +20,16 @@ def params(temperature=0.0, top_k=0, top_p=1.0, repetition_penalty=1.0, presence
                         float(presence_penalty), float(frequency_penalty))
 
 
-def sample_into(logits, out_ids, prm, u=None, prior=None, mask=None, B=None):
+def workspace(B, V, device):
+    """Scratch for the two-phase sampler path (slice partials + candidates); reuse it across calls."""
+    n = _lib.lib().aib_sample_workspace(B, V)
+    return torch.empty(max(n, 16), dtype=torch.uint8, device=device)
+
+
+def sample_into(logits, out_ids, prm, u=None, prior=None, mask=None, B=None, ws=None):
     """Launch the sampler on rows [0, B) of logits [>=B, V] (fp32, CUDA) writing int64 ids into out_ids.
-    u: float64 [B] CUDA tensor or None (greedy); prior: int32 [B, P] (-1 = empty); mask: int32 [B, ceil(V/32)]."""
+    u: float64 [B] CUDA tensor or None (greedy); prior: int32 [B, P] (-1 = empty); mask: int32 [B, ceil(V/32)];
+    ws: uint8 workspace from `workspace(B, V)` (selects the multi-CTA path; None = one CTA per row)."""
     B = logits.shape[0] if B is None else B
     V = logits.shape[-1]
     ld = logits.stride(0) if logits.dim() > 1 else V
@@ -31,12 +38,12 @@ def sample_into(logits, out_ids, prm, u=None, prior=None, mask=None, B=None):
         raise ValueError("prior ids must be int32")
     if mask is not None and (mask.dtype != torch.int32 or mask.shape[-1] != (V + 31) // 32):
         raise ValueError("mask must be int32 [B, ceil(V/32)]")
-    _lib.call("aib_sample", ptr(logits), B, V, ld, prm, ptr(prior), n_prior, ptr(mask), ptr(u), ptr(out_ids), None, 0,
-              stream_ptr())
+    _lib.call("aib_sample", ptr(logits), B, V, ld, prm, ptr(prior), n_prior, ptr(mask), ptr(u), ptr(out_ids),
+              ptr(ws), 0 if ws is None else ws.numel(), stream_ptr())
 
 
 def sample(logits, temperature=0.0, top_p=1.0, top_k=0, us=None, prior=None, mask=None, repetition_penalty=1.0,
-           presence_penalty=0.0, frequency_penalty=0.0):
+           presence_penalty=0.0, frequency_penalty=0.0, two_phase=True):
     """Convenience: returns a list of token ids. `us`: per-row uniform draws (sequence or tensor)."""
     if logits.dim() == 1:
         logits = logits[None]
@@ -49,7 +56,8 @@ def sample(logits, temperature=0.0, top_p=1.0, top_k=0, us=None, prior=None, mas
             raise ValueError("sampling needs uniform draws")
         u = torch.as_tensor(np.asarray(us, np.float64)).to(dev)
     prm = params(temperature, top_k, top_p, repetition_penalty, presence_penalty, frequency_penalty)
-    sample_into(logits.contiguous(), out, prm, u, prior, mask)
+    ws = workspace(B, logits.shape[-1], dev) if two_phase else None
+    sample_into(logits.contiguous(), out, prm, u, prior, mask, ws=ws)
     return out.tolist()
 
 

@@ -267,7 +267,8 @@ def micro_sample(args):
     out = torch.zeros(1, dtype=torch.int64, device="cuda")
     u = torch.full((1,), 0.37, dtype=torch.float64, device="cuda")
     prm = sampler.params(**SAMPLING)
-    return (lambda: sampler.sample_into(lg, out, prm, u)), lg.numel() * 4
+    ws = sampler.workspace(1, lg.shape[-1], lg.device)  # the engine's two-phase path
+    return (lambda: sampler.sample_into(lg, out, prm, u, ws=ws)), lg.numel() * 4
 
 
 def micro(args):

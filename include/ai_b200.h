@@ -160,6 +160,11 @@ typedef struct aib_sample_params {
   float presence_penalty;
   float frequency_penalty;
 } aib_sample_params;
+/* Workspace (bytes, 16-byte aligned) for the multi-CTA path: one CTA per vocabulary slice computes the
+ * slice's max, float64 softmax partial and 64 largest logits, one CTA per row merges them; rows whose
+ * result could depend on a token outside those candidates (top_k > 64, a nucleus the 64 largest logits do
+ * not cover) are completed by the single-CTA algorithm inside the merge, so the ids are the same either way.
+ * ws == NULL (or too small) runs the single-CTA algorithm directly. */
 size_t aib_sample_workspace(int B, int V);
 int aib_sample(const float* logits, int B, int V, int ld, const aib_sample_params* params, const int32_t* prior,
                int n_prior, const int32_t* bitmask, const double* u, int64_t* out_ids, void* ws, size_t ws_bytes,

@@ -322,13 +322,15 @@ def test_batched_attention_vs_oracle(lib, T, pos):
 
 
 # ---------------------------------------------------------------------------------------- sampler
+@pytest.mark.parametrize("two_phase", [True, False], ids=["slices", "onecta"])
 @pytest.mark.parametrize("name", cases(golden("sampler")))
-def test_sampler_matches_reference_pick(lib, name):
+def test_sampler_matches_reference_pick(lib, name, two_phase):
     from ai_b200 import sampler
     z = golden("sampler")
     lg = torch.from_numpy(z[f"{name}/logits"]).cuda()
     mask = torch.from_numpy(z[f"{name}/mask"]).cuda() if f"{name}/mask" in z.files else None
-    ids = sampler.sample(lg, float(z[f"{name}/temp"]), float(z[f"{name}/top_p"]), 0, z[f"{name}/u"], mask=mask)
+    ids = sampler.sample(lg, float(z[f"{name}/temp"]), float(z[f"{name}/top_p"]), 0, z[f"{name}/u"], mask=mask,
+                         two_phase=two_phase)
     np.testing.assert_array_equal(ids, z[f"{name}/ids"])
 
 
@@ -352,11 +354,14 @@ SAMPLER_CASES = [  # (V, T, top_k, top_p, rep, pres, freq, masked)
     (151936, 0.7, 0, 0.8, 1.0, 0.0, 0.0, False),    # top-p over the whole vocabulary
     (5000, 1.5, 0, 1.0, 1.0, 0.0, 0.0, False),
     (5000, 0.9, 0, 0.9, 2.0, 1.0, 1.0, True),
+    (151936, 0.8, 100, 0.9, 1.0, 0.0, 0.0, False),  # top_k above the per-slice candidates: merge falls back
+    (300, 0.5, 0, 0.99, 1.0, 0.0, 0.0, True),       # fewer tokens than slices x candidates
 ]
 
 
+@pytest.mark.parametrize("two_phase", [True, False], ids=["slices", "onecta"])
 @pytest.mark.parametrize("case", SAMPLER_CASES)
-def test_sampler_extended_vs_oracle(lib, case):
+def test_sampler_extended_vs_oracle(lib, case, two_phase):
     from ai_b200 import sampler
     V, T, k, p, rep, pres, freq, masked = case
     B = 4
@@ -375,16 +380,31 @@ def test_sampler_extended_vs_oracle(lib, case):
     us = [np.random.default_rng(b).random() for b in range(B)]
     ids = sampler.sample(torch.from_numpy(lg).cuda(), T, p, k, us, prior=torch.from_numpy(prior).cuda(),
                          mask=torch.from_numpy(mask).cuda() if mask is not None else None, repetition_penalty=rep,
-                         presence_penalty=pres, frequency_penalty=freq)
+                         presence_penalty=pres, frequency_penalty=freq, two_phase=two_phase)
     ref = [osamp.sample_row(lg[b], T, k, p, rep, pres, freq, prior[b], mask[b] if mask is not None else None, us[b])
            for b in range(B)]
     assert ids == ref
     assert status_clear() == 0
 
 
-def test_sampler_many_rows_and_greedy_ties(lib):
+@pytest.mark.parametrize("two_phase", [True, False], ids=["slices", "onecta"])
+def test_sampler_many_rows_and_greedy_ties(lib, two_phase):
     from ai_b200 import sampler
     lg = torch.zeros(64, 1000, device="cuda")
     lg[:, 17] = 1.0
     lg[:, 400] = 1.0
-    assert sampler.sample(lg) == [17] * 64
+    assert sampler.sample(lg, two_phase=two_phase) == [17] * 64
+
+
+def test_sampler_ties_across_slices(lib):
+    """Equal maxima in different vocabulary slices: the first index wins; sampling ties keep index order."""
+    from ai_b200 import sampler
+    lg = torch.full((2, 151936), -5.0, device="cuda")
+    lg[:, 150000] = 3.0
+    lg[:, 70000] = 3.0
+    lg[:, 5] = 2.0
+    assert sampler.sample(lg) == [70000, 70000]
+    ids = sampler.sample(lg, 1.0, 1.0, 2, [0.25, 0.75])  # top-2 = the tied pair, index order, p = 1/2 each
+    assert ids == [70000, 150000]
+    ids = sampler.sample(lg, 1.0, 0.5, 2, [0.25, 0.75])  # exclusive cumsum 0.5 is not < 0.5: one token kept
+    assert ids == [70000, 70000]
