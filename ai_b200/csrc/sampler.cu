@@ -106,6 +106,39 @@ AIB_DEV T block_sum_fixed(T v, T* red) {  // deterministic: fixed lanes, fixed w
   return s;
 }
 
+// Radix-select step on a 256-bucket histogram (buckets visited from 255 down): the digit d holding the
+// `rem`-th largest key and the count of keys in higher buckets. Run by one full warp (lane l owns buckets
+// 255-8l .. 248-8l); every lane returns the same result.
+AIB_DEV void pick_bucket(const unsigned int* hist, int rem, int& digit, int& above) {
+  const int lane = threadIdx.x & 31;
+  int c[8], tot = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) c[i] = static_cast<int>(hist[255 - 8 * lane - i]), tot += c[i];
+  int incl = tot;  // inclusive prefix over lanes (descending bucket order)
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  const int excl = incl - tot;
+  // first lane whose inclusive count reaches rem
+  const unsigned hit = __ballot_sync(0xffffffffu, incl >= rem);
+  const int src = hit ? __ffs(hit) - 1 : 31;
+  int d = 0, ab = 0;
+  if (lane == src) {
+    int cum = excl;
+    int i = 0;
+    for (; i < 7; ++i) {
+      if (cum + c[i] >= rem) break;
+      cum += c[i];
+    }
+    d = 255 - 8 * lane - i;
+    ab = cum;
+  }
+  digit = __shfl_sync(0xffffffffu, d, src);
+  above = __shfl_sync(0xffffffffu, ab, src);
+}
+
 struct __align__(16) Shared {
   double dred[32];
   float fred[32];
@@ -143,14 +176,13 @@ AIB_DEV uint32_t select_kth(const Row& r, int V, int k, uint32_t floor, Shared& 
       }
     }
     __syncthreads();
-    if (tid == 0) {
-      int cum = 0, d;
-      for (d = 255; d > 0; --d) {
-        if (cum + static_cast<int>(sh.hist[d]) >= remaining) break;
-        cum += sh.hist[d];
+    if (tid < 32) {
+      int d, cum;
+      pick_bucket(sh.hist, remaining, d, cum);
+      if (tid == 0) {
+        sh.prefix = prefix | (static_cast<uint32_t>(d) << shift);
+        sh.ired[0] = remaining - cum;
       }
-      sh.prefix = prefix | (static_cast<uint32_t>(d) << shift);
-      sh.ired[0] = remaining - cum;
     }
     __syncthreads();
     prefix = sh.prefix;
@@ -368,6 +400,7 @@ constexpr int kPartThreads = 256;
 constexpr int kSliceMax = 1280;   // 5 tokens per thread
 constexpr int kC = 64;            // candidates per slice (top_k <= kC uses the fast path)
 constexpr int kCandCap = 128;     // candidate slots per slice (ties at the C-th key)
+constexpr int kMaxSlices = 192;   // merge keeps ns * kCandCap keys in registers (24 per thread)
 
 struct SlicePart {
   double zmax, zsum;
@@ -451,22 +484,26 @@ __global__ void __launch_bounds__(kPartThreads)
     pdl_trigger();
     return;
   }
-  // float64 partial softmax denominator over the slice (fixed-order reduction)
+  // float64 partial softmax denominator over the slice (fixed-order reduction); only needed without top-k
+  const bool has_k = prm.top_k > 0 && prm.top_k < V;
   const double Td = static_cast<double>(T);
   const double zm = best == -INFINITY ? 0.0 : static_cast<double>(best) / Td;
   double zs = 0.0;
+  if (!has_k) {
 #pragma unroll
-  for (int e = 0; e < E; ++e)
-    if (x[e] != -INFINITY && e * kPartThreads + tid < v1 - v0) zs += exp(static_cast<double>(x[e]) / Td - zm);
+    for (int e = 0; e < E; ++e)
+      if (x[e] != -INFINITY && e * kPartThreads + tid < v1 - v0) zs += exp(static_cast<double>(x[e]) / Td - zm);
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) zs += __shfl_xor_sync(0xffffffffu, zs, o);
-  __syncthreads();
-  if (lane == 0) dred[warp] = zs;
-  __syncthreads();
-  zs = 0.0;
-  for (int w = 0; w < kPartThreads / 32; ++w) zs += dred[w];
-  // C-th largest key of the slice: 4 radix passes over the keys held in registers
-  const int kc = min(kC, v1 - v0);
+    for (int o = 16; o > 0; o >>= 1) zs += __shfl_xor_sync(0xffffffffu, zs, o);
+    __syncthreads();
+    if (lane == 0) dred[warp] = zs;
+    __syncthreads();
+    zs = 0.0;
+    for (int w = 0; w < kPartThreads / 32; ++w) zs += dred[w];
+  }
+  // kc-th largest key of the slice (kc = top_k when it is at most kC, else kC): 4 radix passes over the
+  // keys held in registers
+  const int kc = min(has_k ? min(prm.top_k, kC) : kC, v1 - v0);
   uint32_t prefix = 0u, pmask = 0u;
   int rem = kc;
   for (int shift = 24; shift >= 0 && kc > 0; shift -= 8) {
@@ -481,21 +518,20 @@ __global__ void __launch_bounds__(kPartThreads)
       if (bucket != 256 && lane == __ffs(peers) - 1) atomicAdd(&hist[bucket], static_cast<unsigned>(__popc(peers)));
     }
     __syncthreads();
-    if (tid == 0) {
-      int cum = 0, d;
-      for (d = 255; d > 0; --d) {
-        if (cum + static_cast<int>(hist[d]) >= rem) break;
-        cum += hist[d];
+    if (tid < 32) {
+      int d, cum;
+      pick_bucket(hist, rem, d, cum);
+      if (tid == 0) {
+        s_prefix = prefix | (static_cast<uint32_t>(d) << shift);
+        s_rem = rem - cum;
       }
-      s_prefix = prefix | (static_cast<uint32_t>(d) << shift);
-      s_rem = rem - cum;
     }
     __syncthreads();
     prefix = s_prefix;
     rem = s_rem;
     pmask |= 0xFFu << shift;
   }
-  // candidates: keys >= the C-th key (finite logits)
+  // candidates: keys >= the kc-th key (finite logits)
   if (tid == 0) s_nc = 0;
   __syncthreads();
   uint32_t* ck = ckeys + (static_cast<size_t>(b) * ns + sl) * kCandCap;
@@ -529,20 +565,46 @@ __global__ void __launch_bounds__(kThreads)
                         const int* __restrict__ cids) {
   extern __shared__ __align__(16) uint8_t dsm[];
   __shared__ Shared sh;
+  __shared__ SlicePart spart[kMaxSlices];
+  __shared__ int soff[kMaxSlices + 1];  // exclusive prefix of the slices' candidate counts
+  __shared__ float s_best;
+  __shared__ int s_bi, s_over;
   const int b = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   pdl_wait();
-  const SlicePart* pp = parts + static_cast<size_t>(b) * ns;
-  // global max and first argmax, slices in order
-  float best = -INFINITY;
-  int bi = INT_MAX;
-  bool over = false;
-  int total = 0;
-  for (int s2 = 0; s2 < ns; ++s2) {
-    const SlicePart q = pp[s2];
-    if (q.max > best) best = q.max, bi = q.arg;
-    over |= q.overflow != 0;
-    total += q.ncand;
+  for (int i = tid; i < ns; i += kThreads) spart[i] = parts[static_cast<size_t>(b) * ns + i];
+  __syncthreads();
+  // warp 0: global max / first argmax (slices in order), overflow flags, candidate offsets
+  if (warp == 0) {
+    float best = -INFINITY;
+    int bi = INT_MAX, over = 0, run = 0;
+    for (int i0 = 0; i0 < ns; i0 += 32) {
+      const int i = i0 + lane;
+      const bool ok = i < ns;
+      const float m = ok ? spart[i].max : -INFINITY;
+      const int a = ok ? spart[i].arg : INT_MAX;
+      if (ok) over |= spart[i].overflow;
+      if (m > best || (m == best && a < bi)) best = m, bi = a;
+      int c = ok ? spart[i].ncand : 0, incl = c;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+      }
+      if (ok) soff[i] = run + incl - c;
+      run += __shfl_sync(0xffffffffu, incl, 31);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ob > best || (ob == best && oi < bi)) best = ob, bi = oi;
+    }
+    over = __any_sync(0xffffffffu, over != 0);
+    if (lane == 0) s_best = best, s_bi = bi, s_over = over, soff[ns] = run;
   }
+  __syncthreads();
+  const float best = s_best;
+  int bi = s_bi;
   if (bi == INT_MAX) bi = 0;
   const float T = prm.temperature;
   if (!(T > 0.0f) || best == -INFINITY) {
@@ -552,48 +614,53 @@ __global__ void __launch_bounds__(kThreads)
   }
   const int topk = prm.top_k;
   const bool has_k = topk > 0 && topk < V;
-  if (over || (has_k && topk > kC)) {
+  const int total = soff[ns];
+  if (s_over || (has_k && topk > kC) || total > CMAX) {
     sample_row_full(dsm, sh, logits, V, ld, prm, prior, n_prior, bitmask, us, out, b);
     pdl_trigger();
     return;
   }
   const double Td = static_cast<double>(T), Mz = static_cast<double>(best) / Td;
-  // N-th largest key of the union of the slices' candidates (radix select over the candidate lists)
+  // compact the candidates into shared memory (warp per slice, lanes over the slice's list)
+  // dynamic shared memory (smem_bytes(V) >= 128 KB): [0, 64K) all candidates (keys, ids), then reused for
+  // the probabilities; [64K, 128K) the kept candidates (keys, ids)
+  uint32_t* ak = reinterpret_cast<uint32_t*>(dsm);
+  int* ai = reinterpret_cast<int*>(ak + CMAX);
+  uint32_t* ckey = reinterpret_cast<uint32_t*>(ai + CMAX);
+  int* cidx = reinterpret_cast<int*>(ckey + CMAX);
+  double* cp = reinterpret_cast<double*>(dsm);  // written only after the gather has consumed ak / ai
+  for (int sl = warp; sl < ns; sl += kThreads / 32) {
+    const int n = spart[sl].ncand, o = soff[sl];
+    const size_t src = (static_cast<size_t>(b) * ns + sl) * kCandCap;
+    for (int j = lane; j < n; j += 32) {
+      ak[o + j] = __ldcg(ckeys + src + j);
+      ai[o + j] = __ldcg(cids + src + j);
+    }
+  }
+  __syncthreads();
+  // N-th largest key of the union (radix select over the compact list)
   const int N = has_k ? topk : kC;
-  const uint32_t* ckb = ckeys + static_cast<size_t>(b) * ns * kCandCap;
-  const int* cib = cids + static_cast<size_t>(b) * ns * kCandCap;
-  auto cand_at = [&](int i, uint32_t& k, int& id) -> bool {  // i-th slot of the concatenated lists
-    const int s2 = i / kCandCap, j = i % kCandCap;
-    if (j >= pp[s2].ncand) return false;
-    k = ckb[i];
-    id = cib[i];
-    return true;
-  };
   uint32_t prefix = 0u, pmask = 0u;
   int rem = min(N, total);
-  const int slots = ns * kCandCap;
+  const int rounds = (total + kThreads - 1) / kThreads;
   for (int shift = 24; shift >= 0; shift -= 8) {
-    __syncthreads();
     for (int i = tid; i < 256; i += kThreads) sh.hist[i] = 0u;
     __syncthreads();
-    for (int i0 = 0; i0 < slots; i0 += kThreads) {
-      const int i = i0 + tid;
+    for (int r2 = 0; r2 < rounds; ++r2) {
+      const int i = r2 * kThreads + tid;
       int bucket = 256;
-      uint32_t k;
-      int id;
-      if (i < slots && cand_at(i, k, id) && (k & pmask) == prefix) bucket = static_cast<int>((k >> shift) & 0xFFu);
+      if (i < total && (ak[i] & pmask) == prefix) bucket = static_cast<int>((ak[i] >> shift) & 0xFFu);
       const unsigned peers = __match_any_sync(0xffffffffu, bucket);
       if (bucket != 256 && lane == __ffs(peers) - 1) atomicAdd(&sh.hist[bucket], static_cast<unsigned>(__popc(peers)));
     }
     __syncthreads();
-    if (tid == 0) {
-      int cum = 0, d;
-      for (d = 255; d > 0; --d) {
-        if (cum + static_cast<int>(sh.hist[d]) >= rem) break;
-        cum += sh.hist[d];
+    if (tid < 32) {
+      int d, cum;
+      pick_bucket(sh.hist, rem, d, cum);
+      if (tid == 0) {
+        sh.prefix = prefix | (static_cast<uint32_t>(d) << shift);
+        sh.ired[0] = rem - cum;
       }
-      sh.prefix = prefix | (static_cast<uint32_t>(d) << shift);
-      sh.ired[0] = rem - cum;
     }
     __syncthreads();
     prefix = sh.prefix;
@@ -601,64 +668,81 @@ __global__ void __launch_bounds__(kThreads)
     pmask |= 0xFFu << shift;
   }
   const uint32_t thr = prefix;
-  // gather the kept candidates (key >= thr) and sort them (key desc, index asc)
-  uint32_t* ckey = reinterpret_cast<uint32_t*>(dsm);
-  int* cidx = reinterpret_cast<int*>(ckey + CMAX);
-  double* cp = reinterpret_cast<double*>(cidx + CMAX);
-  __syncthreads();
   if (tid == 0) sh.ncand = 0;
   __syncthreads();
-  for (int i = tid; i < slots; i += kThreads) {
-    uint32_t k;
-    int id;
-    if (cand_at(i, k, id) && k >= thr) {
+  for (int i = tid; i < total; i += kThreads)
+    if (ak[i] >= thr) {
       const int slot = atomicAdd(&sh.ncand, 1);
-      if (slot < CMAX) ckey[slot] = k, cidx[slot] = id;
+      ckey[slot] = ak[i], cidx[slot] = ai[i];
     }
+  __syncthreads();
+  const int nc = sh.ncand;
+  if (nc > 256) {  // many ties at the boundary key: the parallel single-CTA algorithm handles them
+    sample_row_full(dsm, sh, logits, V, ld, prm, prior, n_prior, bitmask, us, out, b);
+    pdl_trigger();
+    return;
   }
-  __syncthreads();
-  const int nc = min(sh.ncand, CMAX);
-  int n2 = 1;
-  while (n2 < nc) n2 <<= 1;
-  for (int i = nc + tid; i < n2; i += kThreads) ckey[i] = 0u, cidx[i] = INT_MAX;
-  __syncthreads();
-  for (int k = 2; k <= n2; k <<= 1)
-    for (int j = k >> 1; j > 0; j >>= 1) {
-      for (int i = tid; i < n2; i += kThreads) {
-        const int ixj = i ^ j;
-        if (ixj > i) {
-          const uint32_t ka = ckey[i], kb = ckey[ixj];
-          const int ia = cidx[i], ib = cidx[ixj];
-          const bool a_first = (ka > kb) || (ka == kb && ia < ib);
-          const bool up = (i & k) == 0;
-          if (a_first != up) ckey[i] = kb, ckey[ixj] = ka, cidx[i] = ib, cidx[ixj] = ia;
+  // sort (key desc, index asc): one warp when it fits, else a block bitonic sort
+  if (nc <= 32) {
+    if (warp == 0) {
+      uint32_t k = lane < nc ? ckey[lane] : 0u;
+      int id = lane < nc ? cidx[lane] : INT_MAX;
+#pragma unroll
+      for (int kk = 2; kk <= 32; kk <<= 1)
+#pragma unroll
+        for (int j = kk >> 1; j > 0; j >>= 1) {
+          const uint32_t ok = __shfl_xor_sync(0xffffffffu, k, j);
+          const int oi = __shfl_xor_sync(0xffffffffu, id, j);
+          const bool lower = (lane & j) == 0;        // this lane holds the first of the pair
+          const bool up = (lane & kk) == 0;          // ascending block of the bitonic network ("first" = larger)
+          const bool mine_first = (k > ok) || (k == ok && id < oi);
+          const bool keep_mine = (lower == up) ? mine_first : !mine_first;
+          if (!keep_mine) k = ok, id = oi;
         }
-      }
-      __syncthreads();
+      if (lane < nc) ckey[lane] = k, cidx[lane] = id;
     }
-  // softmax denominator: over the kept top-k set, or over the whole row from the slices (slice order)
-  double Z = 0.0;
-  if (has_k) {
-    double zpart = 0.0;
-    for (int i = tid; i < nc; i += kThreads) zpart += exp(static_cast<double>(key_value(ckey[i])) / Td - Mz);
-    Z = block_sum_fixed<double>(zpart, sh.dred);
+    __syncthreads();
   } else {
-    for (int s2 = 0; s2 < ns; ++s2)
-      if (pp[s2].max != -INFINITY) Z += pp[s2].zsum * exp(pp[s2].zmax - Mz);
+    int n2 = 1;
+    while (n2 < nc) n2 <<= 1;
+    for (int i = nc + tid; i < n2; i += kThreads) ckey[i] = 0u, cidx[i] = INT_MAX;
+    __syncthreads();
+    for (int k = 2; k <= n2; k <<= 1)
+      for (int j = k >> 1; j > 0; j >>= 1) {
+        for (int i = tid; i < n2; i += kThreads) {
+          const int ixj = i ^ j;
+          if (ixj > i) {
+            const uint32_t ka = ckey[i], kb = ckey[ixj];
+            const int ia = cidx[i], ib = cidx[ixj];
+            const bool a_first = (ka > kb) || (ka == kb && ia < ib);
+            const bool up = (i & k) == 0;
+            if (a_first != up) ckey[i] = kb, ckey[ixj] = ka, cidx[i] = ib, cidx[ixj] = ia;
+          }
+        }
+        __syncthreads();
+      }
   }
-  for (int i = tid; i < nc; i += kThreads) cp[i] = exp(static_cast<double>(key_value(ckey[i])) / Td - Mz) / Z;
-  __syncthreads();
-  if (tid == 0) {  // sequential exclusive scan of the (short) candidate list, fixed order
+  // softmax denominator: over the kept top-k set (sorted order), or over the whole row from the slices
+  if (tid == 0) {
+    double Z = 0.0;
+    if (has_k) {
+      for (int i = 0; i < nc; ++i) Z += exp(static_cast<double>(key_value(ckey[i])) / Td - Mz);
+    } else {
+      for (int s2 = 0; s2 < ns; ++s2)
+        if (spart[s2].max != -INFINITY) Z += spart[s2].zsum * exp(spart[s2].zmax - Mz);
+    }
+    // probabilities and their exclusive prefix sums in sorted order (fixed order)
     double run = 0.0;
     for (int i = 0; i < nc; ++i) {
-      const double pi = cp[i];
+      const double pi = exp(static_cast<double>(key_value(ckey[i])) / Td - Mz) / Z;
       cp[i] = run;
       run += pi;
     }
     sh.dred[0] = run;  // mass of all candidates
+    sh.dred[1] = Z;
   }
   __syncthreads();
-  const double top_p = static_cast<double>(prm.top_p), cand_mass = sh.dred[0];
+  const double top_p = static_cast<double>(prm.top_p), cand_mass = sh.dred[0], Z = sh.dred[1];
   // without top-k the candidates are the N largest logits of the row: fall back when the nucleus may extend
   // past them (their mass does not reach top_p and the row has more tokens)
   if (!has_k && nc < V && cand_mass < min(top_p, 1.0 - 1e-12)) {
@@ -667,22 +751,20 @@ __global__ void __launch_bounds__(kThreads)
     pdl_trigger();
     return;
   }
-  int keep = 0;
-  for (int i = tid; i < nc; i += kThreads) keep += (top_p >= 1.0 || cp[i] < top_p) ? 1 : 0;
-  keep = block_sum_fixed<int>(keep, sh.ired);
-  keep = max(1, min(keep, nc));
-  const double pl = exp(static_cast<double>(key_value(ckey[keep - 1])) / Td - Mz) / Z;
-  const double S = cp[keep - 1] + pl;
-  const double u = us ? us[b] : 0.5;
-  int cntle = 0;
-  for (int i = tid; i < keep; i += kThreads) {
-    const double incl_i = (i + 1 < keep) ? cp[i + 1] : S;
-    cntle += (incl_i / S <= u) ? 1 : 0;
+  if (tid == 0) {
+    int keep = 0;  // keep while exclusive cumsum < top_p
+    for (int i = 0; i < nc; ++i) keep += (top_p >= 1.0 || cp[i] < top_p) ? 1 : 0;
+    keep = max(1, min(keep, nc));
+    const double pl = exp(static_cast<double>(key_value(ckey[keep - 1])) / Td - Mz) / Z;
+    const double S = cp[keep - 1] + pl;
+    const double u = us ? us[b] : 0.5;
+    int cntle = 0;  // index = #(cdf_i <= u)
+    for (int i = 0; i < keep; ++i) {
+      const double incl_i = (i + 1 < keep) ? cp[i + 1] : S;
+      cntle += (incl_i / S <= u) ? 1 : 0;
+    }
+    out[b] = cidx[min(cntle, keep - 1)];
   }
-  cntle = block_sum_fixed<int>(cntle, sh.ired);
-  const int pick = min(cntle, keep - 1);
-  if (tid == 0) out[b] = cidx[pick];
-  (void)warp;
   pdl_trigger();
 }
 
@@ -717,7 +799,7 @@ int aib_sample(const float* logits, int B, int V, int ld, const aib_sample_param
   const size_t smem = samp::smem_bytes(V);
   if (smem > 227 * 1024) return fail(AIB_ENOTSUP, "aib_sample: vocabulary of %d too large", V);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (ws && ws_bytes >= aib_sample_workspace(B, V) && B <= 65535) {  // two-phase path
+  if (ws && ws_bytes >= aib_sample_workspace(B, V) && B <= 65535 && samp::n_slices(V) <= samp::kMaxSlices) {
     if (reinterpret_cast<uintptr_t>(ws) & 15) return fail(AIB_EINVAL, "aib_sample: workspace must be 16-byte aligned");
     const int ns = samp::n_slices(V);
     samp::SlicePart* parts = static_cast<samp::SlicePart*>(ws);
