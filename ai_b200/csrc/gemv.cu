@@ -733,8 +733,9 @@ constexpr int kRowsStage = 128 * 384;  // wide-stage kernels: R * CW * (256 + 12
 template <int MODE>
 AIB_DEV void produce_wide(const CUtensorMap* tm8, const CUtensorMap* tme4, uint8_t* ring, uint8_t* meta,
                           int slot_meta, uint64_t* full, uint64_t* empty, volatile int* abort_flag, const int* rps,
-                          const int* ecs, bool staged, int e0, const int32_t* ec, float* y, int N, int tb, int n_st,
-                          int R, int CW, int KS, int NS, int nrows, int pw) {
+                          const int* ecs, bool staged, int e0, const int32_t* ec, float* y, int N, int tb, int ks0,
+                          int n_st, int R, int CW, int KS, int NS, int nrows, int pw, float* wsp, int* wsc, int maxp,
+                          int tiles) {
   const int lane = threadIdx.x & 31;
   if (lane == 0) {
     prefetch_tensormap(tm8);
@@ -743,8 +744,9 @@ AIB_DEV void produce_wide(const CUtensorMap* tm8, const CUtensorMap* tme4, uint8
   const uint32_t m8_bytes = static_cast<uint32_t>(R * CW * 256);
   const int wpr = (CW * 8 + 31) / 32;  // mask words per row
   int cur = 0;
-  int s = 0, round = 0, ks = 0, tile = tb;  // stage i: slot s, ring round i / NS
-  int fks = 0, ftile = tb;                  // stage i - NS (same slot)
+  int s = 0, round = 0, ks = ks0, tile = tb;  // stage i: slot s, ring round i / NS
+  int fks = ks0, ftile = tb;                  // stage i - NS (same slot)
+  const long long nall = static_cast<long long>(tiles) * KS, G = gridDim.x;
   for (int i = 0; i < n_st + NS; ++i) {
     if (i >= NS) {  // the slot's previous stage must be consumed
       bool ok = true;
@@ -774,16 +776,49 @@ AIB_DEV void produce_wide(const CUtensorMap* tm8, const CUtensorMap* tme4, uint8
       tma_load_3d(st + m8_bytes, tme4, &full[s], 0, ks * CW, tile * R);
     }
     if (i >= NS) {
-      if (fks == KS - 1 && lane < R && !*abort_flag) {
-        const int row = ftile * R + lane;
-        if (row < N) {
+      const bool seg_end = fks == KS - 1 || i - NS == n_st - 1;  // consumers left partials in the slot
+      if (seg_end && !*abort_flag) {
+        const bool whole = (ftile != tb || ks0 == 0) && fks == KS - 1;  // the tile lies inside this CTA
+        float v = 0.0f;
+        if (lane < R) {
           const float* part = reinterpret_cast<const float*>(sm + 128) + lane * pw;
-          float v = part[0];
+          v = part[0];
           for (int w = 1; w < pw; ++w) v += part[w];
-          if (MODE == 0)
-            y[row] = v;
-          else
-            y[row] += v;
+        }
+        const int row = ftile * R + lane;
+        if (whole) {
+          if (lane < R && row < N) {
+            if (MODE == 0)
+              y[row] = v;
+            else
+              y[row] += v;
+          }
+        } else {
+          // stream-K: this CTA holds part `pi` of the tile's stages; the last of its np parts to arrive adds
+          // them in part order (deterministic) and writes y, then clears the ticket
+          const long long st0 = static_cast<long long>(ftile) * KS;
+          const int bf = static_cast<int>(((st0 + 1) * G + nall - 1) / nall - 1);
+          const int bl = static_cast<int>(((st0 + KS) * G + nall - 1) / nall - 1);
+          const int pi = static_cast<int>(blockIdx.x) - bf, np = bl - bf + 1;
+          float* slot = wsp + (static_cast<size_t>(ftile) * maxp) * R;
+          if (lane < R) slot[pi * R + lane] = v;
+          __threadfence();
+          __syncwarp();
+          int last = 0;
+          if (lane == 0) last = atomicAdd(&wsc[ftile], 1) == np - 1;
+          last = __shfl_sync(0xffffffffu, last, 0);
+          if (last) {
+            __threadfence();
+            if (lane < R && row < N) {
+              float t = __ldcg(slot + lane);
+              for (int q = 1; q < np; ++q) t += __ldcg(slot + q * R + lane);
+              if (MODE == 0)
+                y[row] = t;
+              else
+                y[row] += t;
+            }
+            if (lane == 0) wsc[ftile] = 0;
+          }
         }
       }
       if (++fks == KS) fks = 0, ++ftile;
@@ -849,7 +884,40 @@ struct RowsParams {
   int R, CW, KS, tiles, NS;
   int xs_off, rps_off, ecs_off, ecap, ring_off;
   uint32_t k128, k8, k65536;  // 128, 8, 65536 (see unit_fast_imad)
+  float* wsp;                 // stream-K partials [tiles][maxp][R] (null: whole row tiles per CTA)
+  int* wsc;                   // stream-K tickets [tiles], zero between launches
+  int maxp;                   // partial slots per tile
 };
+
+// The CTA's share of the (tile, chunk group) stages. Without a workspace every CTA takes whole row tiles;
+// with one (stream-K) the tiles * KS stages are split evenly, so a tile may be shared by neighbouring CTAs.
+struct WideShare {
+  int g0, n_st, tb, ks0, row0, nrows;
+};
+AIB_DEV WideShare wide_share(const RowsParams& p) {
+  WideShare w;
+  const long long b = blockIdx.x, G = gridDim.x;
+  if (p.wsp) {
+    const long long n = static_cast<long long>(p.tiles) * p.KS;
+    const long long g0 = b * n / G, g1 = (b + 1) * n / G;
+    w.g0 = static_cast<int>(g0);
+    w.n_st = static_cast<int>(g1 - g0);
+    w.tb = static_cast<int>(g0 / p.KS);
+    w.ks0 = static_cast<int>(g0 % p.KS);
+    const int tl = w.n_st > 0 ? static_cast<int>((g1 - 1) / p.KS) : w.tb;
+    w.row0 = w.tb * p.R;
+    w.nrows = min((tl - w.tb + 1) * p.R, p.N - w.row0);
+  } else {
+    const int tb = static_cast<int>(b * p.tiles / G), te = static_cast<int>((b + 1) * p.tiles / G);
+    w.g0 = tb * p.KS;
+    w.n_st = (te - tb) * p.KS;
+    w.tb = tb;
+    w.ks0 = 0;
+    w.row0 = tb * p.R;
+    w.nrows = min((te - tb) * p.R, p.N - w.row0);
+  }
+  return w;
+}
 
 template <int MODE, bool RMS>
 __global__ void __launch_bounds__(kRowsThreads, 1)
@@ -866,13 +934,13 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
   uint8_t* ring = smem + p.ring_off;
 
   const int tid = threadIdx.x, lane = tid & 31;
-  const int tb = static_cast<int>((static_cast<long long>(blockIdx.x) * p.tiles) / gridDim.x);
-  const int te = static_cast<int>((static_cast<long long>(blockIdx.x + 1) * p.tiles) / gridDim.x);
+  const WideShare sh_ = wide_share(p);
+  const int tb = sh_.tb, ks0 = sh_.ks0;
   const int R = p.R, CW = p.CW, KS = p.KS, NS = p.NS;
   const int L = 8 * CW, W = L / 32;  // threads / warps per row pair (L = units per row per stage)
-  const int n_st = (te - tb) * KS;
-  const int row0 = tb * R;
-  const int nrows = min((te - tb) * R, p.N - row0);
+  const int n_st = sh_.n_st;
+  const int row0 = sh_.row0;
+  const int nrows = sh_.nrows;
   if (tid == 0) {
     for (int s = 0; s < NS; ++s) {
       mbar_init(&full[s], 2);  // TMA arrival + bookkeeping arrival
@@ -893,7 +961,7 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
 
   if (tid >= kRowsConsumers) {  // ---------------- producer warp
     produce_wide<MODE>(&tm8, &tme4, ring, meta, kRowsSlotMeta, full, empty, abort_flag, rps, ecs, staged, e0, p.ec,
-                       p.y, p.N, tb, n_st, R, CW, KS, NS, nrows, W);
+                       p.y, p.N, tb, ks0, n_st, R, CW, KS, NS, nrows, W, p.wsp, p.wsc, p.maxp, p.tiles);
     return;
   }
 
@@ -984,7 +1052,7 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
   bool aborted = false;
   float4 accA = make_float4(0.0f, 0.0f, 0.0f, 0.0f), accB = accA;
   float exA = 0.0f, exB = 0.0f;
-  int s = 0, ph = 0, ks = 0, tile = tb;
+  int s = 0, ph = 0, ks = ks0, tile = tb;
   for (int i = 0; i < n_st; ++i) {
     const bool ok = !aborted && wait_full(&full[s], ph, abort_flag);
     if (!ok) aborted = true;
@@ -1017,7 +1085,7 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
       else
         exB += unit_slow(lt + rb, gc, mlB, mhB, eeB, xl, xh);
     }
-    if (ks == KS - 1) {  // tile complete: reduce inside the warp, leave one partial per (row, warp) in the slot
+    if (ks == KS - 1 || i == n_st - 1) {  // segment end: reduce inside the warp, one partial per (row, warp)
       float vA = ((accA.x + accA.y) + (accA.z + accA.w)) + exA;
       float vB = ((accB.x + accB.y) + (accB.z + accB.w)) + exB;
 #pragma unroll
@@ -1081,13 +1149,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint8_t* ring = smem + p.ring_off;
 
   const int tid = threadIdx.x, lane = tid & 31;
-  const int tb = static_cast<int>((static_cast<long long>(blockIdx.x) * p.tiles) / gridDim.x);
-  const int te = static_cast<int>((static_cast<long long>(blockIdx.x + 1) * p.tiles) / gridDim.x);
+  const WideShare sh_ = wide_share(p);
+  const int tb = sh_.tb, ks0 = sh_.ks0;
   const int R = p.R, CW = p.CW, KS = p.KS, NS = p.NS;
   const int PW = 2 * CW;  // partials per row (warps per row group)
-  const int n_st = (te - tb) * KS;
-  const int row0 = tb * R;
-  const int nrows = min((te - tb) * R, p.N - row0);
+  const int n_st = sh_.n_st;
+  const int row0 = sh_.row0;
+  const int nrows = sh_.nrows;
   if (tid == 0) {
     for (int s = 0; s < NS; ++s) {
       mbar_init(&full[s], 2);  // TMA arrival + bookkeeping arrival
@@ -1107,7 +1175,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
   if (tid >= kTcConsumers) {  // ---------------- producer warp
     produce_wide<MODE>(&tm8, &tme4, ring, meta, kTcSlotMeta, full, empty, abort_flag, rps, ecs, staged, e0, p.ec,
-                       p.y, p.N, tb, n_st, R, CW, KS, NS, nrows, PW);
+                       p.y, p.N, tb, ks0, n_st, R, CW, KS, NS, nrows, PW, p.wsp, p.wsc, p.maxp, p.tiles);
     return;
   }
 
@@ -1205,7 +1273,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   bool aborted = false;
   float acc[2][4] = {{0.0f, 0.0f, 0.0f, 0.0f}, {0.0f, 0.0f, 0.0f, 0.0f}};
   float exA = 0.0f, exB = 0.0f;
-  int s = 0, ph = 0, ks = 0, tile = tb;
+  int s = 0, ph = 0, ks = ks0, tile = tb;
   for (int it = 0; it < n_st; ++it) {
     // warp-uniform: the MMAs below must run with all 32 lanes converged
     const bool ok = __all_sync(0xffffffffu, !aborted && wait_full(&full[s], ph, abort_flag));
@@ -1281,7 +1349,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         if (xb) exB += exc_sum(lt + rB, gc);
       }
     }
-    if (ks == KS - 1) {  // tile complete: row g takes the columns of its parity (parts 0..2 on quads t = 0..2)
+    if (ks == KS - 1 || it == n_st - 1) {  // segment end: row g takes the columns of its parity (quads t = 0..2)
       float vA = par ? (acc[0][1] + acc[1][1]) : (acc[0][0] + acc[1][0]);
       float vB = par ? (acc[0][3] + acc[1][3]) : (acc[0][2] + acc[1][2]);
       if (t == 3) vA = vB = 0.0f;
@@ -1488,18 +1556,46 @@ static int run_mma(const aib_c12* c, const float* x, float* y, int mode, const u
   return go(gemv_mma_kernel<2, false>);
 }
 
+// Stream-K split of `tiles * KS` stages over `grid` CTAs: the most CTAs that share one tile.
+static int streamk_max_parts(int tiles, int KS, int grid) {
+  const long long n = static_cast<long long>(tiles) * KS, G = grid;
+  int mp = 1;
+  for (int t = 0; t < tiles; ++t) {
+    const long long st0 = static_cast<long long>(t) * KS;
+    const long long bf = ((st0 + 1) * G + n - 1) / n - 1, bl = ((st0 + KS) * G + n - 1) / n - 1;
+    mp = std::max(mp, static_cast<int>(bl - bf + 1));
+  }
+  return mp;
+}
+// Workspace of a wide-stage launch: [tickets: tiles ints, 16-byte padded][partials: tiles x maxp x R floats].
+struct StreamK {
+  int grid, maxp;
+  size_t bytes;
+};
+static StreamK streamk_plan(int tiles, int KS, int R) {
+  StreamK k;
+  const long long n = static_cast<long long>(tiles) * KS;
+  k.grid = static_cast<int>(std::min<long long>(sm_count(), n));
+  k.maxp = streamk_max_parts(tiles, KS, k.grid);
+  k.bytes = ((static_cast<size_t>(tiles) * 4 + 15) / 16) * 16 + static_cast<size_t>(tiles) * k.maxp * R * 4;
+  return k;
+}
+
 // Wide-stage kernel (48 KB TMA stages); ENOTSUP when K is not a multiple of 1024 or x does not fit.
-static int run_rows(const aib_c12* c, const float* x, float* y, int mode, const uint16_t* lnw, float eps,
-                    cudaStream_t s) {
+static int run_rows(const aib_c12* c, const float* x, float* y, int mode, const uint16_t* lnw, float eps, void* ws,
+                    size_t ws_bytes, cudaStream_t s) {
   const int nch = c->K / 256;
   if (nch % 4) return fail(AIB_ENOTSUP, "aib_gemv_c12: K=%d is not a multiple of 1024", c->K);
   if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(lnw) & 7))
     return fail(AIB_ENOTSUP, "aib_gemv_c12: x / lnw not aligned for vector loads");
   const int CW = nch % 16 == 0 ? 16 : (nch % 8 == 0 ? 8 : 4);
-  const int R = 128 / CW;
+  const int R = 128 / CW, KS = nch / CW;
   const int tiles = (c->N + R - 1) / R;
-  const int grid = std::min(tiles, sm_count());
-  const int rows_max = ((tiles + grid - 1) / grid) * R;
+  const StreamK sk = streamk_plan(tiles, KS, R);
+  const bool use_sk = ws && ws_bytes >= sk.bytes && !(reinterpret_cast<uintptr_t>(ws) & 15);
+  const int grid = use_sk ? sk.grid : std::min(tiles, sm_count());
+  const int per = static_cast<int>((static_cast<long long>(tiles) * KS + grid - 1) / grid);
+  const int rows_max = use_sk ? ((per + KS - 1) / KS + 1) * R : ((tiles + grid - 1) / grid) * R;
   const size_t xs_off = kRowsHeader;  // x (fp32, permuted), then row pointers, staged exception columns, ring
   const size_t rps_off = xs_off + ((static_cast<size_t>(c->K) * 4 + 127) / 128) * 128;
   const size_t ecs_off = rps_off + ((static_cast<size_t>(rows_max + 1) * 4 + 127) / 128) * 128;
@@ -1514,9 +1610,12 @@ static int run_rows(const aib_c12* c, const float* x, float* y, int mode, const 
   CUtensorMap tm8, tme4;
   int rc = make_maps(c, R, CW, &tm8, &tme4);
   if (rc) return rc;
-  RowsParams p{c->rp, c->ec, c->ev, x, y, lnw, eps, c->base, c->N, c->K, nch, R, CW, nch / CW, tiles, NS,
+  const size_t cnt_bytes = ((static_cast<size_t>(tiles) * 4 + 15) / 16) * 16;
+  RowsParams p{c->rp, c->ec, c->ev, x, y, lnw, eps, c->base, c->N, c->K, nch, R, CW, KS, tiles, NS,
                static_cast<int>(xs_off), static_cast<int>(rps_off), static_cast<int>(ecs_off), ecap,
-               static_cast<int>(ring_off), 128u, 8u, 65536u};
+               static_cast<int>(ring_off), 128u, 8u, 65536u,
+               use_sk ? reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + cnt_bytes) : nullptr,
+               use_sk ? static_cast<int*>(ws) : nullptr, sk.maxp};
   auto go = [&](auto kernel) -> int {
     const int r2 = allow_smem(kernel, smem);
     if (r2) return r2;
@@ -1534,17 +1633,20 @@ static int run_rows(const aib_c12* c, const float* x, float* y, int mode, const 
 
 // Wide-stage tensor-core kernel: R = 32 rows x 4 chunks (K a multiple of 1024) or 16 rows x 8 chunks (K a
 // multiple of 2048, finer row tiles); ENOTSUP when x's three-part records do not fit.
-static int run_tc(const aib_c12* c, const float* x, float* y, int mode, const uint16_t* lnw, float eps,
-                  cudaStream_t s) {
+static int run_tc(const aib_c12* c, const float* x, float* y, int mode, const uint16_t* lnw, float eps, void* ws,
+                  size_t ws_bytes, cudaStream_t s) {
   const int nch = c->K / 256;
   if (nch % 4) return fail(AIB_ENOTSUP, "aib_gemv_c12: K=%d is not a multiple of 1024", c->K);
   if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(lnw) & 7))
     return fail(AIB_ENOTSUP, "aib_gemv_c12: x / lnw not aligned for vector loads");
   const int CW = nch % 8 == 0 ? 8 : 4;
-  const int R = 128 / CW;
+  const int R = 128 / CW, KS = nch / CW;
   const int tiles = (c->N + R - 1) / R;
-  const int grid = std::min(tiles, sm_count());
-  const int rows_max = ((tiles + grid - 1) / grid) * R;
+  const StreamK sk = streamk_plan(tiles, KS, R);
+  const bool use_sk = ws && ws_bytes >= sk.bytes && !(reinterpret_cast<uintptr_t>(ws) & 15);
+  const int grid = use_sk ? sk.grid : std::min(tiles, sm_count());
+  const int per = static_cast<int>((static_cast<long long>(tiles) * KS + grid - 1) / grid);
+  const int rows_max = use_sk ? ((per + KS - 1) / KS + 1) * R : ((tiles + grid - 1) / grid) * R;
   // layout: header + NS slot records, x records (6 bytes per column), row pointers, staged exception
   // columns (at least 1024), ring; the deepest ring that fits
   int NS = 8;
@@ -1563,9 +1665,12 @@ static int run_tc(const aib_c12* c, const float* x, float* y, int mode, const ui
   CUtensorMap tm8, tme4;
   int rc = make_maps(c, R, CW, &tm8, &tme4);
   if (rc) return rc;
-  RowsParams p{c->rp, c->ec, c->ev, x, y, lnw, eps, c->base, c->N, c->K, nch, R, CW, nch / CW, tiles, NS,
+  const size_t cnt_bytes = ((static_cast<size_t>(tiles) * 4 + 15) / 16) * 16;
+  RowsParams p{c->rp, c->ec, c->ev, x, y, lnw, eps, c->base, c->N, c->K, nch, R, CW, KS, tiles, NS,
                static_cast<int>(xs_off), static_cast<int>(rps_off), static_cast<int>(ecs_off), ecap,
-               static_cast<int>(ring_off), 128u, 8u, 65536u};
+               static_cast<int>(ring_off), 128u, 8u, 65536u,
+               use_sk ? reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + cnt_bytes) : nullptr,
+               use_sk ? static_cast<int*>(ws) : nullptr, sk.maxp};
   auto go = [&](auto kernel) -> int {
     const int r2 = allow_smem(kernel, smem);
     if (r2) return r2;
@@ -1585,14 +1690,14 @@ static int g_variant = 3;  // 0: tensor-core 24 KB-stage kernel, 1: CUDA-core 12
                            // stages, 3 (default): tensor-core 48 KB stages
 
 
-static int run_t1(const aib_c12* c, const float* x, float* y, int mode, const uint16_t* lnw, float eps,
-                  cudaStream_t s) {
+static int run_t1(const aib_c12* c, const float* x, float* y, int mode, const uint16_t* lnw, float eps, void* ws,
+                  size_t ws_bytes, cudaStream_t s) {
   if (g_variant == 3) {
-    const int rc = run_tc(c, x, y, mode, lnw, eps, s);
+    const int rc = run_tc(c, x, y, mode, lnw, eps, ws, ws_bytes, s);
     if (rc != AIB_ENOTSUP) return rc;
   }
   if (g_variant == 2 || g_variant == 3) {
-    const int rc = run_rows(c, x, y, mode, lnw, eps, s);
+    const int rc = run_rows(c, x, y, mode, lnw, eps, ws, ws_bytes, s);
     if (rc != AIB_ENOTSUP) return rc;  // other shapes use the 12 KB-stage kernel
   }
   if (g_variant == 0 && c->K <= 16384) {
@@ -1666,15 +1771,18 @@ extern "C" {
 void aib_gemv_set_variant(int v) { gemv::g_variant = v; }
 
 size_t aib_gemv_c12_workspace(const aib_c12* c, int T) {
-  (void)c;
-  (void)T;
-  return 0;
+  if (!c || T != 1 || c->N <= 0 || c->K <= 0 || c->K % 1024) return 0;
+  const int nch = c->K / 256;
+  size_t need = 0;
+  for (int CW : {nch % 8 == 0 ? 8 : 4, nch % 16 == 0 ? 16 : (nch % 8 == 0 ? 8 : 4)}) {  // both wide kernels
+    const int R = 128 / CW, tiles = (c->N + R - 1) / R;
+    need = std::max(need, gemv::streamk_plan(tiles, nch / CW, R).bytes);
+  }
+  return need;
 }
 
 int aib_gemv_c12(const aib_c12* c, const float* x, float* y, int T, int x_stride, int y_stride, int mode,
                  const uint16_t* lnw, float eps, void* ws, size_t ws_bytes, void* stream) {
-  (void)ws;
-  (void)ws_bytes;
   if (!c || !x || !y || !c->m8 || !c->e4 || !c->rp || (c->n_exc > 0 && (!c->ec || !c->ev)))
     return fail(AIB_EINVAL, "aib_gemv_c12: null pointer");
   if (c->N <= 0 || c->K <= 0 || c->K % 256 || c->CH != 256)
@@ -1685,7 +1793,7 @@ int aib_gemv_c12(const aib_c12* c, const float* x, float* y, int T, int x_stride
   if ((reinterpret_cast<uintptr_t>(c->m8) & 15) || (reinterpret_cast<uintptr_t>(c->e4) & 15))
     return fail(AIB_EINVAL, "aib_gemv_c12: m8/e4 must be 16-byte aligned");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (T == 1) return gemv::run_t1(c, x, y, mode, lnw, eps, s);
+  if (T == 1) return gemv::run_t1(c, x, y, mode, lnw, eps, ws, ws_bytes, s);
   if (lnw) return fail(AIB_EINVAL, "aib_gemv_c12: the RMS prologue is only available for T == 1");
   const int xin = mode == 2 ? 2 * c->K : c->K;
   if (x_stride < xin || y_stride < c->N) return fail(AIB_EINVAL, "aib_gemv_c12: row strides too small");

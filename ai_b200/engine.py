@@ -85,6 +85,7 @@ class Engine:
         self.u = torch.zeros(MAXB, dtype=torch.float64, device=dev)
         self.prior = torch.full((1, sampler.PMAX), -1, dtype=torch.int32, device=dev)
         self.sample_ws = sampler.workspace(MAXB, self.cfg.V, dev)
+        self.gemv_ws = wcomp.gemv_workspace(list(self.W[0].values()) + [self.head], dev)  # same shapes every layer
         wsz = max(_lib.lib().aib_attn_workspace(H, KV, HD, maxt, t) for t in range(1, MAXB + 1))
         self.ws = torch.zeros(wsz, dtype=torch.uint8, device=dev)
         self.use_graphs = graphs

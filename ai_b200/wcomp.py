@@ -122,8 +122,16 @@ def _chk(t, name):
         raise ValueError(f"{name} must be a contiguous fp32 CUDA tensor")
 
 
-def gemvc1(x, c, y, mode, BN=None, w=None, lnw=None, eps=1e-6):
-    """y (+)= W xin(x) for one token (reference gemvc1, wcomp.py:118-126)."""
+def gemv_workspace(cs, device):
+    """Zero-filled workspace for `gemvc1(..., ws=...)` covering every matrix in `cs` (reused across calls on one
+    stream: every call leaves it zeroed)."""
+    n = max([_lib.lib().aib_gemv_c12_workspace(C.byref(c.desc()), 1) for c in cs] + [16])
+    return torch.zeros(n, dtype=torch.uint8, device=device)
+
+
+def gemvc1(x, c, y, mode, BN=None, w=None, lnw=None, eps=1e-6, ws=None):
+    """y (+)= W xin(x) for one token (reference gemvc1, wcomp.py:118-126). ws: optional `gemv_workspace`
+    (even split of the matrix over the SMs)."""
     _chk(x, "x")
     _chk(y, "y")
     K = c["K"]
@@ -132,7 +140,8 @@ def gemvc1(x, c, y, mode, BN=None, w=None, lnw=None, eps=1e-6):
     if lnw is not None and lnw.dtype != torch.bfloat16:
         raise ValueError("lnw must be bf16")
     _lib.call("aib_gemv_c12", C.byref(c.desc()), ptr(x), ptr(y), 1, 0, 0, mode,
-              ptr(lnw.view(torch.int16)) if lnw is not None else None, float(eps), None, 0, stream_ptr())
+              ptr(lnw.view(torch.int16)) if lnw is not None else None, float(eps), ptr(ws),
+              0 if ws is None else ws.numel(), stream_ptr())
 
 
 def gemvc_tc(x, c, y, mode, T, BN=None, w=None, S=None):

@@ -119,8 +119,9 @@ def variant(request, lib):
     lib.aib_gemv_set_variant(3)  # library default
 
 
+@pytest.mark.parametrize("streamk", [False, True], ids=["tiles", "streamk"])
 @pytest.mark.parametrize("N,K,mode,rms", GEMV_SHAPES)
-def test_gemvc1_shapes_vs_oracle(lib, variant, N, K, mode, rms):
+def test_gemvc1_shapes_vs_oracle(lib, variant, N, K, mode, rms, streamk):
     from ai_b200 import wcomp
     g = torch.Generator(device="cuda").manual_seed(N + K + mode)
     w = (torch.randn(N, K, generator=g, device="cuda") * 0.02).bfloat16()
@@ -133,7 +134,10 @@ def test_gemvc1_shapes_vs_oracle(lib, variant, N, K, mode, rms):
     y0 = torch.randn(N, generator=g, device="cuda")
     lnw = (1 + 0.1 * torch.randn(K, generator=g, device="cuda")).bfloat16() if rms else None
     y = y0.clone()
-    wcomp.gemvc1(x, c, y, mode, lnw=lnw, eps=1e-6)
+    ws = wcomp.gemv_workspace([c], "cuda") if streamk else None
+    wcomp.gemvc1(x, c, y, mode, lnw=lnw, eps=1e-6, ws=ws)
+    if ws is not None:
+        assert int(ws.view(torch.int32)[: (c["N"] + 31) // 32].abs().sum()) == 0  # tickets (leading ints) back at zero
     oc = codec.compress(bits(w))
     ref = ogemv.gemvc1(x.cpu().numpy(), oc, y0.cpu().numpy(), mode, bits(lnw) if rms else None, 1e-6)
     xe = ogemv.xin(x.cpu().numpy(), K, mode, bits(lnw) if rms else None, 1e-6)
@@ -204,17 +208,22 @@ def test_gemv_exceptions_beyond_staged_capacity(lib, variant):
     assert status_clear() == 0
 
 
-def test_gemv_deterministic(lib):
+@pytest.mark.parametrize("K", [4096, 12288])
+def test_gemv_deterministic(lib, K):
+    """Repeated calls give identical bits, with and without the stream-K workspace (split tiles are added in
+    a fixed order whichever CTA finishes last)."""
     from ai_b200 import wcomp
     g = torch.Generator(device="cuda").manual_seed(9)
-    c = wcomp.compress((torch.randn(4096, 4096, generator=g, device="cuda") * 0.02).bfloat16())
-    x = torch.randn(4096, generator=g, device="cuda")
-    outs = []
-    for _ in range(3):
-        y = torch.zeros(4096, device="cuda")
-        wcomp.gemvc1(x, c, y, 0)
-        outs.append(y)
-    assert torch.equal(outs[0], outs[1]) and torch.equal(outs[0], outs[2])
+    c = wcomp.compress((torch.randn(4096, K, generator=g, device="cuda") * 0.02).bfloat16())
+    x = torch.randn(K, generator=g, device="cuda")
+    ws = wcomp.gemv_workspace([c], "cuda")
+    for w in (None, ws):
+        outs = []
+        for _ in range(4):
+            y = torch.zeros(4096, device="cuda")
+            wcomp.gemvc1(x, c, y, 0, ws=w)
+            outs.append(y)
+        assert all(torch.equal(outs[0], o) for o in outs[1:])
 
 
 # ----------------------------------------------------------------------------------- norm / embed
