@@ -62,6 +62,20 @@ AIB_DEV int xperm(int k) {
 
 AIB_DEV float silu_mul(float g, float u) { return g / (1.0f + expf(-g)) * u; }
 
+// What the wide kernels' decode makes of an exception (exponent code 15): sign and mantissa from its m8
+// byte, exponent field (base + 15) mod 256 (the select-merge below drops the carry). Finite for base < 240.
+AIB_DEV float exc_garbage(uint32_t m, int base) {
+  return __uint_as_float((((m & 0x80u) << 8) | (((static_cast<uint32_t>(base) + 15u) & 0xFFu) << 7) | (m & 0x7Fu)) << 16);
+}
+
+// (a & 0x807F807F) | (b & 0x7F807F80) in one LOP3: sign and mantissa bits from a, exponent field from b
+AIB_DEV uint32_t merge_sm_e(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("lop3.b32 %0, %1, %2, %3, 0xE4;" : "=r"(r) : "r"(a), "r"(b), "r"(0x807F807Fu));
+  return r;
+}
+
+
 // Decode one 32-element unit (fast path: no code-15 element) and accumulate w * x.
 AIB_DEV void unit_fast(const uint4& ml, const uint4& mh, const uint4& ee, const float4* xl, const float4* xh,
                        uint32_t base7, float2& acc) {
@@ -131,10 +145,10 @@ AIB_DEV void unit_fast_imad(const uint4& ml, const uint4& mh, const uint4& ee, c
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
     const uint32_t x01 = prmt(E[q], 0u, 0x4140u), x23 = prmt(E[q], 0u, 0x4342u);
-    const uint32_t zlo01 = (prmt(L[q], 0u, 0x9180u) & 0x807F807Fu) | ((x01 & 0x000F000Fu) * k128 + base7);
-    const uint32_t zlo23 = (prmt(L[q], 0u, 0xB3A2u) & 0x807F807Fu) | ((x23 & 0x000F000Fu) * k128 + base7);
-    const uint32_t zhi01 = (prmt(Hh[q], 0u, 0x9180u) & 0x807F807Fu) | ((x01 & 0x00F000F0u) * k8 + base7);
-    const uint32_t zhi23 = (prmt(Hh[q], 0u, 0xB3A2u) & 0x807F807Fu) | ((x23 & 0x00F000F0u) * k8 + base7);
+    const uint32_t zlo01 = merge_sm_e(prmt(L[q], 0u, 0x9180u), x01 * k128 + base7 - (x01 & 0x00F000F0u) * k128);
+    const uint32_t zlo23 = merge_sm_e(prmt(L[q], 0u, 0xB3A2u), x23 * k128 + base7 - (x23 & 0x00F000F0u) * k128);
+    const uint32_t zhi01 = merge_sm_e(prmt(Hh[q], 0u, 0x9180u), x01 * k8 + base7);
+    const uint32_t zhi23 = merge_sm_e(prmt(Hh[q], 0u, 0xB3A2u), x23 * k8 + base7);
     p0 = ffma2(make_float2(__uint_as_float(zlo01 * k65536), __uint_as_float(zlo01 & 0xFFFF0000u)),
                make_float2(xl[q].x, xl[q].y), p0);
     p1 = ffma2(make_float2(__uint_as_float(zlo23 * k65536), __uint_as_float(zlo23 & 0xFFFF0000u)),
@@ -443,13 +457,6 @@ AIB_DEV void mma_bf16(float* d, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t 
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// (a & 0x807F807F) | (b & 0x7F807F80) in one LOP3: sign and mantissa bits from a, exponent field from b
-AIB_DEV uint32_t merge_sm_e(uint32_t a, uint32_t b) {
-  uint32_t r;
-  asm("lop3.b32 %0, %1, %2, %3, 0xE4;" : "=r"(r) : "r"(a), "r"(b), "r"(0x807F807Fu));
-  return r;
-}
-
 // clear the 16-bit halves whose exponent code is 15 (exceptions decode to 0; their value is added apart)
 AIB_DEV uint32_t clear15(uint32_t z, uint32_t codes) {  // codes: low element in bits 0..3, high in 16..19
   uint32_t m = 0;
@@ -724,26 +731,34 @@ constexpr int kRowsStage = 128 * 384;  // wide-stage kernels: R * CW * (256 + 12
 // ---------------------------------------------------------- producer warp of the wide-stage kernels
 // Streams the CTA's (tile, chunk group) stages through the NS-slot ring. A slot's full barrier completes on
 // two arrivals plus the copied bytes: the first arrival comes with the TMA copies, issued as soon as the slot
-// is free; the second once the slot's bookkeeping is done, which therefore overlaps the copy:
-//  * finalise the stage that last used the slot: when it ended a row tile, add the `pw` per-warp partials of
-//    each of the tile's R rows in a fixed order and write y;
-//  * mark the units of the new stage that hold an exception (one bit per row and unit) from the CSR: row
-//    pointers in shared memory, exception columns staged in shared memory when they fit.
-// Meta layout per slot (slot_meta bytes): uint32 mask[32], then float partials[R * pw].
-template <int MODE>
+// is free; the second once the slot's bookkeeping is done, which therefore overlaps the copy: when the stage
+// that last used the slot ended a row segment (a whole row tile, or this CTA's share of one), the producer
+// adds the segment's per-warp partials of each of the R rows in a fixed order, adds the exception correction
+// sum_e (v_e - G_e) * x[c_e] over the segment's exceptions (the consumers decode every element, exceptions
+// included, as a finite stand-in G_e -- see exc_garbage) and writes y (stream-K: the tile's parts through
+// the workspace). Meta layout per slot (slot_meta bytes): 128 bytes unused, then float partials[R * pw].
+struct ExcTab {  // the CTA's exceptions: CSR slice in shared memory (columns + corrections) or in global memory
+  const int* rps;   // row pointers of the CTA's rows (shared)
+  const int* ecs;   // staged columns (shared), valid when staged
+  const float* evs; // staged corrections v - G (shared), valid when staged
+  bool staged;
+  int e0, row0;
+  const int32_t* ec;
+  const float* ev;
+  const uint8_t* m8;
+  int K, base;
+};
+template <int MODE, typename XF>
 AIB_DEV void produce_wide(const CUtensorMap* tm8, const CUtensorMap* tme4, uint8_t* ring, uint8_t* meta,
-                          int slot_meta, uint64_t* full, uint64_t* empty, volatile int* abort_flag, const int* rps,
-                          const int* ecs, bool staged, int e0, const int32_t* ec, float* y, int N, int tb, int ks0,
-                          int n_st, int R, int CW, int KS, int NS, int nrows, int pw, float* wsp, int* wsc, int maxp,
-                          int tiles) {
+                          int slot_meta, uint64_t* full, uint64_t* empty, volatile int* abort_flag, const ExcTab& et,
+                          XF xval, float* y, int N, int tb, int ks0, int n_st, int R, int CW, int KS, int NS,
+                          int nrows, int pw, float* wsp, int* wsc, int maxp, int tiles) {
   const int lane = threadIdx.x & 31;
   if (lane == 0) {
     prefetch_tensormap(tm8);
     prefetch_tensormap(tme4);
   }
   const uint32_t m8_bytes = static_cast<uint32_t>(R * CW * 256);
-  const int wpr = (CW * 8 + 31) / 32;  // mask words per row
-  int cur = 0;
   int s = 0, round = 0, ks = ks0, tile = tb;  // stage i: slot s, ring round i / NS
   int fks = ks0, ftile = tb;                  // stage i - NS (same slot)
   const long long nall = static_cast<long long>(tiles) * KS, G = gridDim.x;
@@ -778,16 +793,34 @@ AIB_DEV void produce_wide(const CUtensorMap* tm8, const CUtensorMap* tme4, uint8
     if (i >= NS) {
       const bool seg_end = fks == KS - 1 || i - NS == n_st - 1;  // consumers left partials in the slot
       if (seg_end && !*abort_flag) {
-        const bool whole = (ftile != tb || ks0 == 0) && fks == KS - 1;  // the tile lies inside this CTA
+        const int seg_lo = ftile == tb ? ks0 : 0;  // first chunk group of this CTA's share of the tile
+        const bool whole = seg_lo == 0 && fks == KS - 1;
         float v = 0.0f;
+        const int lr = (ftile - tb) * R + lane, row = ftile * R + lane;
         if (lane < R) {
           const float* part = reinterpret_cast<const float*>(sm + 128) + lane * pw;
           v = part[0];
           for (int w = 1; w < pw; ++w) v += part[w];
+          if (lr < nrows) {  // exception corrections of the segment's columns, in column order
+            const int lo = seg_lo * CW * 256, hi = (fks + 1) * CW * 256;
+            const int qa = et.rps[lr] - et.e0, qb = et.rps[lr + 1] - et.e0;
+            float corr = 0.0f;
+            for (int q = qa; q < qb; ++q) {
+              const int col = et.staged ? et.ecs[q] : et.ec[et.e0 + q];
+              if (col >= hi) break;
+              if (col < lo) continue;
+              const float d = et.staged ? et.evs[q]
+                                        : et.ev[et.e0 + q] - exc_garbage(et.m8[static_cast<size_t>(row) * et.K + col], et.base);
+              corr = fmaf(d, xval(col), corr);
+            }
+            v += corr;
+          }
         }
-        const int row = ftile * R + lane;
         if (whole) {
-          if (lane < R && row < N) {
+          if (MODE == 3) {  // rows (2i, 2i+1) = (gate_i, up_i): y[i] = silu(gate_i) * up_i
+            const float vu = __shfl_down_sync(0xffffffffu, v, 1);
+            if (lane < R && !(lane & 1) && row + 1 < N) y[row >> 1] = silu_mul(v, vu);
+          } else if (lane < R && row < N) {
             if (MODE == 0)
               y[row] = v;
             else
@@ -809,9 +842,15 @@ AIB_DEV void produce_wide(const CUtensorMap* tm8, const CUtensorMap* tme4, uint8
           last = __shfl_sync(0xffffffffu, last, 0);
           if (last) {
             __threadfence();
-            if (lane < R && row < N) {
-              float t = __ldcg(slot + lane);
+            float t = 0.0f;
+            if (lane < R) {
+              t = __ldcg(slot + lane);
               for (int q = 1; q < np; ++q) t += __ldcg(slot + q * R + lane);
+            }
+            if (MODE == 3) {
+              const float tu = __shfl_down_sync(0xffffffffu, t, 1);
+              if (lane < R && !(lane & 1) && row + 1 < N) y[row >> 1] = silu_mul(t, tu);
+            } else if (lane < R && row < N) {
               if (MODE == 0)
                 y[row] = t;
               else
@@ -823,32 +862,27 @@ AIB_DEV void produce_wide(const CUtensorMap* tm8, const CUtensorMap* tme4, uint8
       }
       if (++fks == KS) fks = 0, ++ftile;
     }
+    __syncwarp();
     if (i < n_st) {
-      uint32_t* mask = reinterpret_cast<uint32_t*>(sm);
-      mask[lane] = 0u;
-      __syncwarp();
-      if (ks == 0) cur = 0;
-      const int lr = (tile - tb) * R + lane;
-      if (lane < R && lr < nrows) {
-        const int a = rps[lr] - e0, b = rps[lr + 1] - e0;
-        const int lo = ks * CW * 256, hi = lo + CW * 256;
-        uint32_t* mw = mask + lane * wpr;
-        int q = a + cur;
-        for (; q < b; ++q) {
-          const int col = staged ? ecs[q] : ec[e0 + q];
-          if (col >= hi) break;
-          if (col >= lo) {
-            const int u = ((col - lo) >> 8) * 8 + ((col & 127) >> 4);
-            mw[u >> 5] |= 1u << (u & 31);
-          }
-        }
-        cur = q - a;
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&full[s]);  // second arrival: bitmask written, old partials read
+      if (lane == 0) mbar_arrive(&full[s]);  // second arrival: the slot's previous partials are read
       if (++ks == KS) ks = 0, ++tile;
     }
     if (++s == NS) s = 0, ++round;
+  }
+}
+
+// Stage the CTA's exceptions (weights only: before the grid-dependency wait): columns and the corrections
+// v - G they need (G: what the decode makes of the element, from its m8 byte). Threads take rows.
+AIB_DEV void stage_exceptions(int* ecs, float* evs, const int* rps, int nrows, int row0, int e0, const int32_t* ec,
+                              const float* ev, const uint8_t* m8, int K, int base, int nthreads) {
+  for (int lr = threadIdx.x; lr < nrows; lr += nthreads) {
+    const int qa = rps[lr] - e0, qb = rps[lr + 1] - e0;
+    const uint8_t* mrow = m8 + static_cast<size_t>(row0 + lr) * K;
+    for (int q = qa; q < qb; ++q) {
+      const int col = ec[e0 + q];
+      ecs[q] = col;
+      evs[q] = ev[e0 + q] - exc_garbage(mrow[col], base);
+    }
   }
 }
 
@@ -873,6 +907,7 @@ constexpr int kRowsSlotMeta = 256;     // per slot: 32-word exception bitmask + 
 constexpr int kRowsHeader = 1024 + 8 * kRowsSlotMeta;  // barriers [0,256), abort 256, RMS partials [512,1024)
 
 struct RowsParams {
+  const uint8_t* m8;  // the code planes (exception stand-ins are read from m8 when not staged)
   const int32_t* rp;
   const int32_t* ec;
   const float* ev;
@@ -954,14 +989,16 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
   __syncthreads();
   const int e0 = rps[0], n_exc = rps[nrows] - e0;
   const bool staged = n_exc <= p.ecap;
-  if (staged)
-    for (int i = tid; i < n_exc; i += kRowsThreads) ecs[i] = p.ec[e0 + i];
+  float* evs = reinterpret_cast<float*>(ecs + p.ecap);
+  if (staged) stage_exceptions(ecs, evs, rps, nrows, row0, e0, p.ec, p.ev, p.m8, p.K, p.base, kRowsThreads);
   __syncthreads();
+  const ExcTab et{rps, ecs, evs, staged, e0, row0, p.ec, p.ev, p.m8, p.K, p.base};
   pdl_trigger();
 
   if (tid >= kRowsConsumers) {  // ---------------- producer warp
-    produce_wide<MODE>(&tm8, &tme4, ring, meta, kRowsSlotMeta, full, empty, abort_flag, rps, ecs, staged, e0, p.ec,
-                       p.y, p.N, tb, ks0, n_st, R, CW, KS, NS, nrows, W, p.wsp, p.wsc, p.maxp, p.tiles);
+    auto xval = [&](int col) { return xs[xperm(col)]; };
+    produce_wide<MODE>(&tm8, &tme4, ring, meta, kRowsSlotMeta, full, empty, abort_flag, et, xval, p.y, p.N, tb, ks0,
+                       n_st, R, CW, KS, NS, nrows, W, p.wsp, p.wsc, p.maxp, p.tiles);
     return;
   }
 
@@ -1023,35 +1060,10 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
   const uint32_t m8b = static_cast<uint32_t>((rb * CW + cc) * 256 + 16 * j);
   const uint32_t e4a = static_cast<uint32_t>(R * CW * 256 + (ra * CW + cc) * 128 + 16 * j);
   const uint32_t e4b = static_cast<uint32_t>(R * CW * 256 + (rb * CW + cc) * 128 + 16 * j);
-  const int mwa = ra * W + (l >> 5), mwb = rb * W + (l >> 5);  // mask words of the two rows
-  const uint32_t mbit = 1u << (l & 31);
   const float4* xs4 = reinterpret_cast<const float4*>(xs);
-
-  // slow path: code-15 elements decode to 0, then the exact values of the unit's exceptions are added
-  auto unit_slow = [&](int lr, int gc, const uint4& ml, const uint4& mh, const uint4& ee, const float4* xl,
-                       const float4* xh) -> float {
-    const uint32_t E[4] = {ee.x, ee.y, ee.z, ee.w}, Lw[4] = {ml.x, ml.y, ml.z, ml.w}, Hw[4] = {mh.x, mh.y, mh.z, mh.w};
-    const float* xlf = reinterpret_cast<const float*>(xl);
-    const float* xhf = reinterpret_cast<const float*>(xh);
-    float sacc = 0.0f;
-    for (int q = 0; q < 4; ++q)
-      for (int b = 0; b < 4; ++b) {
-        const uint32_t eb = (E[q] >> (8 * b)) & 0xFFu;
-        sacc += dec1((Lw[q] >> (8 * b)) & 0xFFu, eb & 15u, p.base) * xlf[q * 4 + b];
-        sacc += dec1((Hw[q] >> (8 * b)) & 0xFFu, eb >> 4, p.base) * xhf[q * 4 + b];
-      }
-    const int a = rps[lr] - e0, b = rps[lr + 1] - e0;
-    for (int q = a; q < b; ++q) {
-      const int col = staged ? ecs[q] : p.ec[e0 + q];
-      if ((col >> 8) > gc) break;
-      if ((col >> 8) == gc && ((col & 127) >> 4) == j) sacc += p.ev[e0 + q] * xs[xperm(col)];
-    }
-    return sacc;
-  };
 
   bool aborted = false;
   float4 accA = make_float4(0.0f, 0.0f, 0.0f, 0.0f), accB = accA;
-  float exA = 0.0f, exB = 0.0f;
   int s = 0, ph = 0, ks = ks0, tile = tb;
   for (int i = 0; i < n_st; ++i) {
     const bool ok = !aborted && wait_full(&full[s], ph, abort_flag);
@@ -1060,8 +1072,6 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
     const uint8_t* sm = meta + s * kRowsSlotMeta;
     if (ok && gc < p.nch) {
       const uint8_t* st = ring + static_cast<size_t>(s) * kRowsStage;
-      const uint32_t* mask = reinterpret_cast<const uint32_t*>(sm);
-      const bool xa = mask[mwa] & mbit, xb = mask[mwb] & mbit;
       const float4* xb4 = xs4 + gc * 64;
       float4 xl[4], xh[4];
 #pragma unroll
@@ -1075,19 +1085,13 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
       const uint4 mlB = *reinterpret_cast<const uint4*>(st + m8b);
       const uint4 mhB = *reinterpret_cast<const uint4*>(st + m8b + 128);
       const uint4 eeB = *reinterpret_cast<const uint4*>(st + e4b);
-      const int lt = (tile - tb) * R;
-      if (!xa)
-        unit_fast_imad(mlA, mhA, eeA, xl, xh, base7, p.k128, p.k8, p.k65536, accA);
-      else
-        exA += unit_slow(lt + ra, gc, mlA, mhA, eeA, xl, xh);
-      if (!xb)
-        unit_fast_imad(mlB, mhB, eeB, xl, xh, base7, p.k128, p.k8, p.k65536, accB);
-      else
-        exB += unit_slow(lt + rb, gc, mlB, mhB, eeB, xl, xh);
+      // exceptions decode to their stand-ins; the producer adds the corrections
+      unit_fast_imad(mlA, mhA, eeA, xl, xh, base7, p.k128, p.k8, p.k65536, accA);
+      unit_fast_imad(mlB, mhB, eeB, xl, xh, base7, p.k128, p.k8, p.k65536, accB);
     }
     if (ks == KS - 1 || i == n_st - 1) {  // segment end: reduce inside the warp, one partial per (row, warp)
-      float vA = ((accA.x + accA.y) + (accA.z + accA.w)) + exA;
-      float vB = ((accB.x + accB.y) + (accB.z + accB.w)) + exB;
+      float vA = (accA.x + accA.y) + (accA.z + accA.w);
+      float vB = (accB.x + accB.y) + (accB.z + accB.w);
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) {
         vA += __shfl_xor_sync(0xffffffffu, vA, o);
@@ -1100,7 +1104,6 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
       }
       accA = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
       accB = accA;
-      exA = exB = 0.0f;
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
@@ -1132,6 +1135,18 @@ constexpr int kTcSlotMeta = 128 + 256 * 4;  // per slot: 32-word exception mask,
 AIB_DEV int tc_xrec(int nch, int gc, int i, int blk, int t, int sp) {
   const int gi = gc * 8 + i;
   return sp < 2 ? gi * 128 + (blk * 2 + sp) * 32 + t * 8 : nch * 1024 + gi * 64 + blk * 32 + t * 8;
+}
+// Exact value of x[col] from its three bf16 parts in the records.
+AIB_DEV float tc_xval(const uint8_t* xr, int nch, int col) {
+  const int gc = col >> 8, cc = col & 255, hf = cc >> 7, c = cc & 127;
+  const int b2 = c >> 6, t2 = (c >> 4) & 3, i2 = (c & 15) >> 1, sh = (c & 1) * 16;
+  float parts[3];
+#pragma unroll
+  for (int s2 = 0; s2 < 3; ++s2) {
+    const uint32_t wv = *reinterpret_cast<const uint32_t*>(xr + tc_xrec(nch, gc, i2, b2, t2, s2) + hf * 4);
+    parts[s2] = bf16_to_f32(static_cast<uint16_t>(wv >> sh));
+  }
+  return (parts[0] + parts[1]) + parts[2];
 }
 
 template <int MODE, bool RMS>
@@ -1168,14 +1183,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   __syncthreads();
   const int e0 = rps[0], n_exc = rps[nrows] - e0;
   const bool staged = n_exc <= p.ecap;
-  if (staged)
-    for (int i = tid; i < n_exc; i += kTcThreads) ecs[i] = p.ec[e0 + i];
+  float* evs = reinterpret_cast<float*>(ecs + p.ecap);
+  if (staged) stage_exceptions(ecs, evs, rps, nrows, row0, e0, p.ec, p.ev, p.m8, p.K, p.base, kTcThreads);
   __syncthreads();
+  const ExcTab et{rps, ecs, evs, staged, e0, row0, p.ec, p.ev, p.m8, p.K, p.base};
   pdl_trigger();
 
   if (tid >= kTcConsumers) {  // ---------------- producer warp
-    produce_wide<MODE>(&tm8, &tme4, ring, meta, kTcSlotMeta, full, empty, abort_flag, rps, ecs, staged, e0, p.ec,
-                       p.y, p.N, tb, ks0, n_st, R, CW, KS, NS, nrows, PW, p.wsp, p.wsc, p.maxp, p.tiles);
+    auto xval = [&](int col) { return tc_xval(xr, p.nch, col); };
+    produce_wide<MODE>(&tm8, &tme4, ring, meta, kTcSlotMeta, full, empty, abort_flag, et, xval, p.y, p.N, tb, ks0,
+                       n_st, R, CW, KS, NS, nrows, PW, p.wsp, p.wsc, p.maxp, p.tiles);
     return;
   }
 
@@ -1235,44 +1252,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const uint32_t m8A = static_cast<uint32_t>(rA * CW * 256) + colo, m8B = static_cast<uint32_t>(rB * CW * 256) + colo;
   const uint32_t e4o = static_cast<uint32_t>(R * CW * 256 + q * 128 + blk * 64 + 16 * t);
   const uint32_t e4A = e4o + static_cast<uint32_t>(rA * CW * 128), e4B = e4o + static_cast<uint32_t>(rB * CW * 128);
-  const int ubit = q * 8 + blk * 4 + t;  // the lane's unit inside the stage's row segment
-  const int mwA = rA * (CW / 4) + (ubit >> 5), mwB = rB * (CW / 4) + (ubit >> 5);
-  const uint32_t mbit = 1u << (ubit & 31);
   const bool bl = g < 6;  // lanes supplying a B column (parts 0..2 x 2 parities); columns 6, 7 stay zero
   const int sp = g >> 1;
   const uint32_t base7 = (static_cast<uint32_t>(p.base) << 7) | (static_cast<uint32_t>(p.base) << 23);
   const uint32_t k128 = p.k128, k8 = p.k8;
 
-  // exact value of x[col] from its three parts
-  auto xval = [&](int col) -> float {
-    const int gc = col >> 8, cc = col & 255, hf = cc >> 7, c = cc & 127;
-    const int b2 = c >> 6, t2 = (c >> 4) & 3, i2 = (c & 15) >> 1, sh = (c & 1) * 16;
-    float v = 0.0f;
-    float parts[3];
-#pragma unroll
-    for (int s2 = 0; s2 < 3; ++s2) {
-      const uint32_t wv = *reinterpret_cast<const uint32_t*>(xr + tc_xrec(p.nch, gc, i2, b2, t2, s2) + hf * 4);
-      parts[s2] = bf16_to_f32(static_cast<uint16_t>(wv >> sh));
-    }
-    v = (parts[0] + parts[1]) + parts[2];
-    return v;
-  };
-  // exceptions of local row lr that fall in this lane's unit (chunk gc), times x
-  auto exc_sum = [&](int lr, int gc) -> float {
-    const int a = rps[lr] - e0, b = rps[lr + 1] - e0;
-    const int j = blk * 4 + t;
-    float sacc = 0.0f;
-    for (int k = a; k < b; ++k) {
-      const int col = staged ? ecs[k] : p.ec[e0 + k];
-      if ((col >> 8) > gc) break;
-      if ((col >> 8) == gc && ((col & 127) >> 4) == j) sacc += p.ev[e0 + k] * xval(col);
-    }
-    return sacc;
-  };
-
   bool aborted = false;
   float acc[2][4] = {{0.0f, 0.0f, 0.0f, 0.0f}, {0.0f, 0.0f, 0.0f, 0.0f}};
-  float exA = 0.0f, exB = 0.0f;
   int s = 0, ph = 0, ks = ks0, tile = tb;
   for (int it = 0; it < n_st; ++it) {
     // warp-uniform: the MMAs below must run with all 32 lanes converged
@@ -1282,8 +1268,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const uint8_t* sm = meta + s * kTcSlotMeta;
     if (ok && gc < p.nch) {
       const uint8_t* st = ring + static_cast<size_t>(s) * kRowsStage;
-      const uint32_t* mask = reinterpret_cast<const uint32_t*>(sm);
-      const bool xa = mask[mwA] & mbit, xb = mask[mwB] & mbit;
       const uint4 LA = *reinterpret_cast<const uint4*>(st + m8A);
       const uint4 HA = *reinterpret_cast<const uint4*>(st + m8A + 128);
       const uint4 EA = *reinterpret_cast<const uint4*>(st + e4A);
@@ -1296,8 +1280,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const uint8_t* xg = sp < 2 ? xr + (gc * 8) * 128 + (blk * 2 + sp) * 32 + t * 8
                                  : xr + p.nch * 1024 + (gc * 8) * 64 + blk * 32 + t * 8;
       const int xstep = sp < 2 ? 128 : 64;
-      // mma.sync.aligned needs the whole warp on the same instruction: the path choice is warp-uniform
-      if (!__any_sync(0xffffffffu, xa || xb)) {  // common case: no exception in any unit of the warp
+      {  // exceptions decode to their stand-ins; the producer adds the corrections
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           // x2 = [0, e1, 0, e0] (two code bytes: low nibble = low-half column, high nibble = high-half column).
@@ -1317,44 +1300,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           if (bl) bb = *reinterpret_cast<const uint2*>(xg + i * xstep);
           mma_bf16(acc[i & 1], a0, a1, a2, a3, bb.x, bb.y);
         }
-      } else {  // code-15 elements of the lanes' flagged units decode to 0; their exact values are added below
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int wd = i >> 1;
-          const uint32_t sel = (i & 1) ? 0xB3A2u : 0x9180u, esel = (i & 1) ? 0x4342u : 0x4140u;
-          const uint32_t xa2 = prmt(ea[wd], 0u, esel), xb2 = prmt(eb[wd], 0u, esel);
-          const uint32_t cAl = xa2 & 0x000F000Fu, cAh = xa2 & 0x00F000F0u;
-          const uint32_t cBl = xb2 & 0x000F000Fu, cBh = xb2 & 0x00F000F0u;
-          uint32_t a0 = (prmt(la[wd], 0u, sel) & 0x807F807Fu) | (cAl * k128 + base7);
-          uint32_t a1 = (prmt(lb[wd], 0u, sel) & 0x807F807Fu) | (cBl * k128 + base7);
-          uint32_t a2 = (prmt(ha[wd], 0u, sel) & 0x807F807Fu) | (cAh * k8 + base7);
-          uint32_t a3 = (prmt(hb[wd], 0u, sel) & 0x807F807Fu) | (cBh * k8 + base7);
-          if (xa) {
-            a0 = clear15(a0, cAl);
-            a2 = clear15(a2, cAh >> 4);
-          }
-          if (xb) {
-            a1 = clear15(a1, cBl);
-            a3 = clear15(a3, cBh >> 4);
-          }
-          uint2 bb = make_uint2(0u, 0u);
-          if (bl) bb = *reinterpret_cast<const uint2*>(xg + i * xstep);
-          if (i & 1)
-            mma_bf16(acc[1], a0, a1, a2, a3, bb.x, bb.y);
-          else
-            mma_bf16(acc[0], a0, a1, a2, a3, bb.x, bb.y);
-        }
-        const int lt = (tile - tb) * R;
-        if (xa) exA += exc_sum(lt + rA, gc);
-        if (xb) exB += exc_sum(lt + rB, gc);
       }
     }
     if (ks == KS - 1 || it == n_st - 1) {  // segment end: row g takes the columns of its parity (quads t = 0..2)
       float vA = par ? (acc[0][1] + acc[1][1]) : (acc[0][0] + acc[1][0]);
       float vB = par ? (acc[0][3] + acc[1][3]) : (acc[0][2] + acc[1][2]);
       if (t == 3) vA = vB = 0.0f;
-      vA += exA;
-      vB += exB;
       vA += __shfl_xor_sync(0xffffffffu, vA, 1);
       vB += __shfl_xor_sync(0xffffffffu, vB, 1);
       vA += __shfl_xor_sync(0xffffffffu, vA, 2);
@@ -1369,7 +1320,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       for (int a = 0; a < 2; ++a)
 #pragma unroll
         for (int c = 0; c < 4; ++c) acc[a][c] = 0.0f;
-      exA = exB = 0.0f;
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
@@ -1487,7 +1437,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         v += __shfl_xor_sync(0xffffffffu, v, 1);
         v += __shfl_xor_sync(0xffffffffu, v, 2);
         v += __shfl_xor_sync(0xffffffffu, v, 4);
-        if (j == 0 && t < T && row < p.N && !aborted) {
+        if (MODE == 3) {  // rows r = tid/8: (2i, 2i+1) = (gate_i, up_i) are 8 lanes apart
+          const float vu = __shfl_down_sync(0xffffffffu, v, 8);
+          if (j == 0 && !(r & 1) && t < T && row + 1 < p.N && !aborted)
+            p.y[static_cast<size_t>(t) * p.y_stride + (row >> 1)] = silu_mul(v, vu);
+        } else if (j == 0 && t < T && row < p.N && !aborted) {
           float* yr = p.y + static_cast<size_t>(t) * p.y_stride + row;
           if (MODE == 0)
             *yr = v;
@@ -1586,6 +1540,8 @@ static int run_rows(const aib_c12* c, const float* x, float* y, int mode, const 
                     size_t ws_bytes, cudaStream_t s) {
   const int nch = c->K / 256;
   if (nch % 4) return fail(AIB_ENOTSUP, "aib_gemv_c12: K=%d is not a multiple of 1024", c->K);
+  if (c->base >= 240)  // the exception stand-in (exponent base + 15) would not be finite
+    return fail(AIB_ENOTSUP, "aib_gemv_c12: base %d: exceptions need the exact-path kernel", c->base);
   if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(lnw) & 7))
     return fail(AIB_ENOTSUP, "aib_gemv_c12: x / lnw not aligned for vector loads");
   const int CW = nch % 16 == 0 ? 16 : (nch % 8 == 0 ? 8 : 4);
@@ -1599,19 +1555,19 @@ static int run_rows(const aib_c12* c, const float* x, float* y, int mode, const 
   const size_t xs_off = kRowsHeader;  // x (fp32, permuted), then row pointers, staged exception columns, ring
   const size_t rps_off = xs_off + ((static_cast<size_t>(c->K) * 4 + 127) / 128) * 128;
   const size_t ecs_off = rps_off + ((static_cast<size_t>(rows_max + 1) * 4 + 127) / 128) * 128;
-  const size_t min_ecs = 4096;  // room for at least 1024 staged exception columns
+  const size_t min_ecs = 8192;  // room for at least 1024 staged exceptions (column + correction)
   const size_t ring_need = ((ecs_off + min_ecs + 1023) / 1024) * 1024;
   if (ring_need + 2 * static_cast<size_t>(kRowsStage) > kSmemMax)
     return fail(AIB_ENOTSUP, "aib_gemv_c12: K=%d too large for the wide-stage kernel", c->K);
   const int NS = std::min(8, static_cast<int>((kSmemMax - ring_need) / kRowsStage));
   const size_t ring_off = ((kSmemMax - static_cast<size_t>(NS) * kRowsStage) / 1024) * 1024;
-  const int ecap = static_cast<int>((ring_off - ecs_off) / 4);
+  const int ecap = static_cast<int>((ring_off - ecs_off) / 8);  // column + correction per staged exception
   const size_t smem = ring_off + static_cast<size_t>(NS) * kRowsStage;
   CUtensorMap tm8, tme4;
   int rc = make_maps(c, R, CW, &tm8, &tme4);
   if (rc) return rc;
   const size_t cnt_bytes = ((static_cast<size_t>(tiles) * 4 + 15) / 16) * 16;
-  RowsParams p{c->rp, c->ec, c->ev, x, y, lnw, eps, c->base, c->N, c->K, nch, R, CW, KS, tiles, NS,
+  RowsParams p{static_cast<const uint8_t*>(c->m8), c->rp, c->ec, c->ev, x, y, lnw, eps, c->base, c->N, c->K, nch, R, CW, KS, tiles, NS,
                static_cast<int>(xs_off), static_cast<int>(rps_off), static_cast<int>(ecs_off), ecap,
                static_cast<int>(ring_off), 128u, 8u, 65536u,
                use_sk ? reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + cnt_bytes) : nullptr,
@@ -1624,10 +1580,12 @@ static int run_rows(const aib_c12* c, const float* x, float* y, int mode, const 
   if (lnw) {
     if (mode == 0) return go(gemv_rows_kernel<0, true>);
     if (mode == 1) return go(gemv_rows_kernel<1, true>);
+    if (mode == 3) return go(gemv_rows_kernel<3, true>);
     return go(gemv_rows_kernel<2, true>);
   }
   if (mode == 0) return go(gemv_rows_kernel<0, false>);
   if (mode == 1) return go(gemv_rows_kernel<1, false>);
+  if (mode == 3) return go(gemv_rows_kernel<3, false>);
   return go(gemv_rows_kernel<2, false>);
 }
 
@@ -1637,6 +1595,8 @@ static int run_tc(const aib_c12* c, const float* x, float* y, int mode, const ui
                   size_t ws_bytes, cudaStream_t s) {
   const int nch = c->K / 256;
   if (nch % 4) return fail(AIB_ENOTSUP, "aib_gemv_c12: K=%d is not a multiple of 1024", c->K);
+  if (c->base >= 240)  // the exception stand-in (exponent base + 15) would not be finite
+    return fail(AIB_ENOTSUP, "aib_gemv_c12: base %d: exceptions need the exact-path kernel", c->base);
   if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(lnw) & 7))
     return fail(AIB_ENOTSUP, "aib_gemv_c12: x / lnw not aligned for vector loads");
   const int CW = nch % 8 == 0 ? 8 : 4;
@@ -1660,13 +1620,13 @@ static int run_tc(const aib_c12* c, const float* x, float* y, int mode, const ui
   }
   if (NS < 2) return fail(AIB_ENOTSUP, "aib_gemv_c12: K=%d too large for the tensor-core kernel", c->K);
   const size_t ring_off = ((kSmemMax - static_cast<size_t>(NS) * kRowsStage) / 1024) * 1024;
-  const int ecap = static_cast<int>((ring_off - ecs_off) / 4);
+  const int ecap = static_cast<int>((ring_off - ecs_off) / 8);  // column + correction per staged exception
   const size_t smem = ring_off + static_cast<size_t>(NS) * kRowsStage;
   CUtensorMap tm8, tme4;
   int rc = make_maps(c, R, CW, &tm8, &tme4);
   if (rc) return rc;
   const size_t cnt_bytes = ((static_cast<size_t>(tiles) * 4 + 15) / 16) * 16;
-  RowsParams p{c->rp, c->ec, c->ev, x, y, lnw, eps, c->base, c->N, c->K, nch, R, CW, KS, tiles, NS,
+  RowsParams p{static_cast<const uint8_t*>(c->m8), c->rp, c->ec, c->ev, x, y, lnw, eps, c->base, c->N, c->K, nch, R, CW, KS, tiles, NS,
                static_cast<int>(xs_off), static_cast<int>(rps_off), static_cast<int>(ecs_off), ecap,
                static_cast<int>(ring_off), 128u, 8u, 65536u,
                use_sk ? reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + cnt_bytes) : nullptr,
@@ -1679,10 +1639,12 @@ static int run_tc(const aib_c12* c, const float* x, float* y, int mode, const ui
   if (lnw) {
     if (mode == 0) return go(gemv_tc_kernel<0, true>);
     if (mode == 1) return go(gemv_tc_kernel<1, true>);
+    if (mode == 3) return go(gemv_tc_kernel<3, true>);
     return go(gemv_tc_kernel<2, true>);
   }
   if (mode == 0) return go(gemv_tc_kernel<0, false>);
   if (mode == 1) return go(gemv_tc_kernel<1, false>);
+  if (mode == 3) return go(gemv_tc_kernel<3, false>);
   return go(gemv_tc_kernel<2, false>);
 }
 
@@ -1692,6 +1654,13 @@ static int g_variant = 3;  // 0: tensor-core 24 KB-stage kernel, 1: CUDA-core 12
 
 static int run_t1(const aib_c12* c, const float* x, float* y, int mode, const uint16_t* lnw, float eps, void* ws,
                   size_t ws_bytes, cudaStream_t s) {
+  if (mode == 3) {  // gated output: wide kernels only (their producer pairs the rows)
+    const int rc = run_tc(c, x, y, mode, lnw, eps, ws, ws_bytes, s);
+    if (rc != AIB_ENOTSUP) return rc;
+    const int rc2 = run_rows(c, x, y, mode, lnw, eps, ws, ws_bytes, s);
+    if (rc2 != AIB_ENOTSUP) return rc2;
+    return fail(AIB_ENOTSUP, "aib_gemv_c12: mode 3 with T == 1 needs K a multiple of 1024 (K=%d)", c->K);
+  }
   if (g_variant == 3) {
     const int rc = run_tc(c, x, y, mode, lnw, eps, ws, ws_bytes, s);
     if (rc != AIB_ENOTSUP) return rc;
@@ -1755,6 +1724,7 @@ template <int TMAX>
 static int run_tn_mode(const aib_c12* c, const float* x, float* y, int T, int xs_, int ys_, int mode, cudaStream_t s) {
   if (mode == 0) return run_tn_t<0, TMAX>(c, x, y, T, xs_, ys_, s);
   if (mode == 1) return run_tn_t<1, TMAX>(c, x, y, T, xs_, ys_, s);
+  if (mode == 3) return run_tn_t<3, TMAX>(c, x, y, T, xs_, ys_, s);
   return run_tn_t<2, TMAX>(c, x, y, T, xs_, ys_, s);
 }
 
@@ -1787,7 +1757,8 @@ int aib_gemv_c12(const aib_c12* c, const float* x, float* y, int T, int x_stride
     return fail(AIB_EINVAL, "aib_gemv_c12: null pointer");
   if (c->N <= 0 || c->K <= 0 || c->K % 256 || c->CH != 256)
     return fail(AIB_EINVAL, "aib_gemv_c12: K must be a positive multiple of 256 (N=%d K=%d CH=%d)", c->N, c->K, c->CH);
-  if (mode < 0 || mode > 2) return fail(AIB_EINVAL, "aib_gemv_c12: mode must be 0, 1 or 2");
+  if (mode < 0 || mode > 3) return fail(AIB_EINVAL, "aib_gemv_c12: mode must be 0, 1, 2 or 3");
+  if (mode == 3 && (c->N & 1)) return fail(AIB_EINVAL, "aib_gemv_c12: mode 3 needs an even N (gate/up row pairs)");
   if (c->base < 0 || c->base > 241) return fail(AIB_EINVAL, "aib_gemv_c12: base %d out of range", c->base);
   if (T < 1 || T > 16) return fail(AIB_EINVAL, "aib_gemv_c12: T must be in 1..16");
   if ((reinterpret_cast<uintptr_t>(c->m8) & 15) || (reinterpret_cast<uintptr_t>(c->e4) & 15))
@@ -1796,7 +1767,8 @@ int aib_gemv_c12(const aib_c12* c, const float* x, float* y, int T, int x_stride
   if (T == 1) return gemv::run_t1(c, x, y, mode, lnw, eps, ws, ws_bytes, s);
   if (lnw) return fail(AIB_EINVAL, "aib_gemv_c12: the RMS prologue is only available for T == 1");
   const int xin = mode == 2 ? 2 * c->K : c->K;
-  if (x_stride < xin || y_stride < c->N) return fail(AIB_EINVAL, "aib_gemv_c12: row strides too small");
+  if (x_stride < xin || y_stride < (mode == 3 ? c->N / 2 : c->N))
+    return fail(AIB_EINVAL, "aib_gemv_c12: row strides too small");
   if (T <= 2) return gemv::run_tn_mode<2>(c, x, y, T, x_stride, y_stride, mode, s);
   if (T <= 4) return gemv::run_tn_mode<4>(c, x, y, T, x_stride, y_stride, mode, s);
   if (T <= 8) return gemv::run_tn_mode<8>(c, x, y, T, x_stride, y_stride, mode, s);

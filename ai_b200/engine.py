@@ -61,10 +61,15 @@ class Engine:
         self.eos = set(cfg.eos)
         dev = self.device
         self.inv = (1.0 / (cfg.theta ** (torch.arange(0, self.HD, 2, dtype=torch.float32) / self.HD))).to(dev)
-        # ---- weights
+        # ---- weights. When the hidden size allows the wide GEMV kernels (a multiple of 1024), gate and up rows
+        # are interleaved so the gate/up GEMV writes silu(gate) * up directly (mode 3) and down reads it as a
+        # plain input; otherwise [gate; up] and the SiLU-gated input of down (mode 2), as the reference.
+        self.gated = cfg.D % 1024 == 0
         self.W, self.small = [], []
         for i in range(self.L):
             lw = src.layer(i)
+            if self.gated:
+                lw["gu"] = wcomp.interleave_gate_up(lw["gu"])
             self.W.append({n: wcomp.compress(lw[n].to(dev)) for n in MATS})
             self.small.append({k: lw[k].to(dev).contiguous() for k in ("ln1", "ln2", "qn", "kn")})
             del lw
@@ -114,8 +119,12 @@ class Engine:
                 tkernels.rope_attn(self.qkvb[0], s["qn"], s["kn"], self.inv, self.pos, kc, vc, self.attb[0], self.maxt,
                                    self.eps, self.scale, H, KV, HD, ws=self.ws)
                 wcomp.gemvc1(self.attb[0], W["o"], x, 1)
-                wcomp.gemvc1(x, W["gu"], self.gub[0], 0, lnw=s["ln2"], eps=self.eps)
-                wcomp.gemvc1(self.gub[0], W["down"], x, 2)
+                if self.gated:
+                    wcomp.gemvc1(x, W["gu"], self.gub[0], 3, lnw=s["ln2"], eps=self.eps)
+                    wcomp.gemvc1(self.gub[0], W["down"], x, 1)
+                else:
+                    wcomp.gemvc1(x, W["gu"], self.gub[0], 0, lnw=s["ln2"], eps=self.eps)
+                    wcomp.gemvc1(self.gub[0], W["down"], x, 2)
             else:
                 x, h = self.xb[:T], self.hb[:T]
                 tkernels.rmsg(x, s["ln1"], h, self.eps)
@@ -126,8 +135,12 @@ class Engine:
                               ws=self.ws)
                 wcomp.gemvc_tc(self.attb[:T], W["o"], x, 1, T)
                 tkernels.rmsg(x, s["ln2"], h, self.eps)
-                wcomp.gemvc_tc(h, W["gu"], self.gub[:T], 0, T)
-                wcomp.gemvc_tc(self.gub[:T], W["down"], x, 2, T)
+                if self.gated:
+                    wcomp.gemvc_tc(h, W["gu"], self.gub[:T], 3, T)
+                    wcomp.gemvc_tc(self.gub[:T], W["down"], x, 1, T)
+                else:
+                    wcomp.gemvc_tc(h, W["gu"], self.gub[:T], 0, T)
+                    wcomp.gemvc_tc(self.gub[:T], W["down"], x, 2, T)
 
     def _head(self, T):
         if T == 1:

@@ -60,6 +60,8 @@ CONFIGS = {
     "tiny": Qwen3Config(L=2, D=256, H=4, KV=2, HD=64, FF=512, V=1000, tied=False, name="tiny"),
     "tiny-tied": Qwen3Config(L=2, D=256, H=4, KV=2, HD=64, FF=512, V=1000, tied=True, name="tiny-tied"),
     "small": Qwen3Config(L=4, D=512, H=8, KV=4, HD=128, FF=1536, V=4096, tied=False, name="small"),
+    # hidden size 1024: the engine takes the wide T = 1 GEMV kernels and the gated gate/up GEMV (mode 3)
+    "small-1k": Qwen3Config(L=2, D=1024, H=8, KV=4, HD=128, FF=2048, V=2048, tied=False, name="small-1k"),
 }
 
 

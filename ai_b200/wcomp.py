@@ -131,17 +131,25 @@ def gemv_workspace(cs, device):
 
 def gemvc1(x, c, y, mode, BN=None, w=None, lnw=None, eps=1e-6, ws=None):
     """y (+)= W xin(x) for one token (reference gemvc1, wcomp.py:118-126). ws: optional `gemv_workspace`
-    (even split of the matrix over the SMs)."""
+    (even split of the matrix over the SMs). mode 3 (no reference counterpart): W's rows are (gate, up) pairs
+    and y[i] = silu((Wx)[2i]) * (Wx)[2i+1] -- see `interleave_gate_up`."""
     _chk(x, "x")
     _chk(y, "y")
     K = c["K"]
-    if x.numel() < (2 * K if mode == 2 else K) or y.numel() < c["N"]:
+    if x.numel() < (2 * K if mode == 2 else K) or y.numel() < (c["N"] // 2 if mode == 3 else c["N"]):
         raise ValueError("gemvc1: x or y too small")
     if lnw is not None and lnw.dtype != torch.bfloat16:
         raise ValueError("lnw must be bf16")
     _lib.call("aib_gemv_c12", C.byref(c.desc()), ptr(x), ptr(y), 1, 0, 0, mode,
               ptr(lnw.view(torch.int16)) if lnw is not None else None, float(eps), ptr(ws),
               0 if ws is None else ws.numel(), stream_ptr())
+
+
+def interleave_gate_up(gu):
+    """[gate; up] ([2F, D], the reference's fused layout) -> rows (gate_0, up_0, gate_1, up_1, ...), the layout
+    mode 3 expects. The encoder's per-matrix exponent base is unchanged (same set of values)."""
+    F = gu.shape[0] // 2
+    return gu.view(2, F, gu.shape[1]).transpose(0, 1).reshape(2 * F, gu.shape[1]).contiguous()
 
 
 def gemvc_tc(x, c, y, mode, T, BN=None, w=None, S=None):

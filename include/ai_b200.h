@@ -89,7 +89,10 @@ int aib_c12_decode(const aib_c12* c, int first, int last, void* out, int out_dty
 
 /* --------------------------------------------------------------------------------- codec GEMV ---- */
 /* Y[t] (+)= W * xin(X[t]) for t < T (replaces `gemvc1` wcomp.py:118-126 for T == 1 and `gemvc_tc`
- * wcomp.py:233-242 for 1 < T <= 16). mode 0: Y = Wx; 1: Y += Wx; 2: input silu(x[:K]) * x[K:2K], Y += Wx.
+ * wcomp.py:233-242 for 1 < T <= 16). mode 0: Y = Wx; 1: Y += Wx; 2: input silu(x[:K]) * x[K:2K], Y += Wx;
+ * 3 (gated output, no reference counterpart): W's rows come in (gate_i, up_i) pairs -- rows 2i and 2i+1 --
+ *   and Y[i] = silu((Wx)[2i]) * (Wx)[2i+1] for i < N/2 (N even), the MLP's SiLU gate fused into the
+ *   gate/up GEMV; T == 1 needs K a multiple of 1024.
  * lnw (bf16 bits [K], may be NULL): RMSNorm prologue of gemvc1_k (wcomp.py:75-86), T == 1 only.
  * x_stride / y_stride: elements between rows of X / Y (ignored for T == 1).
  * ws (optional, T == 1): aib_gemv_c12_workspace(c, 1) bytes, 16-byte aligned and zero-filled once before the

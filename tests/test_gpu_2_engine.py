@@ -16,7 +16,7 @@ def oracle_for(cfg, rw, maxt):
     return DecodeOracle(cfg, layers, bits(rw.embedding()), bits(rw.head()), bits(rw.final_norm()), maxt)
 
 
-@pytest.fixture(scope="module", params=["tiny", "tiny-tied", "small"])
+@pytest.fixture(scope="module", params=["tiny", "tiny-tied", "small", "small-1k"])
 def pair(request, cuda_dev):
     from ai_b200 import build
     from ai_b200.engine import Engine
