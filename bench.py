@@ -124,8 +124,9 @@ def gemv_roofline(eng, peak, reps=20):
     import torch
     from ai_b200 import wcomp
     W, s = eng.W[0], eng.small[0]
+    gu_mode, down_mode = (3, 1) if eng.gated else (0, 2)  # the engine's own modes
     launches = [(W["qkv"], eng.xb[0], eng.qkvb[0], 0, s["ln1"]), (W["o"], eng.attb[0], eng.xb[1], 1, None),
-                (W["gu"], eng.xb[0], eng.gub[0], 0, s["ln2"]), (W["down"], eng.gub[0], eng.xb[1], 2, None),
+                (W["gu"], eng.xb[0], eng.gub[0], gu_mode, s["ln2"]), (W["down"], eng.gub[0], eng.xb[1], down_mode, None),
                 (eng.head, eng.xb[0], eng.logits[0], 0, eng.norm)]
     eng.xb[:2].normal_()
     eng.attb[0].normal_()
@@ -145,15 +146,21 @@ def gemv_roofline(eng, peak, reps=20):
     torch.cuda.synchronize()
     sec = e0.elapsed_time(e1) / 1e3 / reps
     achieved = total_bytes / sec / 1e9
-    traffic = None
-    tp = os.path.join(ROOT, "profiles", "gemv_traffic.json")
+    # DRAM traffic per launch: the ncu capture of one gate/up-shaped launch (profiles/gemv_tc_gu.md: read + write
+    # bytes over the launch's algorithmic bytes), scaled to this average launch by its algorithmic bytes
+    per_launch = total_bytes // len(launches)
+    traffic, ratio = None, None
+    tp = os.path.join(ROOT, "profiles", "gemv_tc_gu.md")
     if os.path.exists(tp):
-        t = json.load(open(tp))
-        traffic = t.get("bytes_per_launch_scaled")
-    return {"bound": "hbm", "kernel": "aib gemv_t1 (codec GEMV, T=1)", "achieved": round(achieved, 1),
+        for line in open(tp):
+            if line.startswith("| traffic / algorithmic bytes |"):
+                ratio = float(line.rsplit("=", 1)[1].strip(" |\n"))
+        if ratio:
+            traffic = int(per_launch * ratio)
+    return {"bound": "hbm", "kernel": "aib gemv_tc_kernel (codec GEMV, T=1)", "achieved": round(achieved, 1),
             "peak": peak[0], "peak_kind": peak[1], "unit": "GB/s", "frac": round(achieved / peak[0], 4),
-            "traffic": traffic, "algorithmic_bytes_per_launch": total_bytes // len(launches),
-            "avg_launch_us": round(sec / len(launches) * 1e6, 2)}
+            "traffic": traffic, "traffic_source": "ncu 24576x4096 launch, scaled by algorithmic bytes" if traffic else None,
+            "algorithmic_bytes_per_launch": per_launch, "avg_launch_us": round(sec / len(launches) * 1e6, 2)}
 
 
 def gpu_arm(args, rank, world):
