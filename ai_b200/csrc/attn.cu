@@ -7,16 +7,21 @@
 // aib_qk_rope_cache / aib_attn_cached replace the batched pair qk_rope_cache_k / attn_k (:82-150).
 //
 // B200 design: flash-decoding. The grid is (S splits, KV groups[, T tokens]); each CTA serves all G = H/KV
-// query heads of its group, so every K/V row is read from HBM once per group, with coalesced loads (a
-// warp covers one bf16 row). Each CTA writes a partial (m, l, acc) to the workspace; the last CTA of a
-// group (atomic ticket, no waiting) merges the partials in split order -- starting, like the reference,
-// from the current token -- so results are deterministic. The ticket counters return to zero.
-// Inside a CTA every warp owns a contiguous slice of the range and walks it 32 positions at a time with
-// lane = position: each lane loads its K row and the block's V values straight from global memory (16-byte
-// loads, a whole block in flight per warp), scores the row against the G query heads with q broadcast from
-// shared memory (no reduction across lanes), and the block's softmax and P.V run warp-wide. The warps'
-// states are combined once, at the end. The merge loads every split's partial in parallel (weights
-// exp(m_s - M) first, then the sums).
+// query heads of its group, so every K/V row is read from HBM once per group. Each CTA writes a partial
+// (m, l, acc) to the workspace; the last CTA of a group (atomic ticket, no waiting) merges the partials in
+// split order -- starting, like the reference, from the current token -- so results are deterministic. The
+// ticket counters return to zero.
+// Data movement: before the grid-dependency wait a CTA asks L2 to prefetch its K/V rows (bulk L2 prefetch
+// of two contiguous ranges, addressed from a possibly stale read of pos: a hint only, always in bounds).
+// After the wait every warp starts asynchronous 16-byte copies (cp.async, coalesced 512 bytes per warp
+// instruction) of its first block of 32 K rows and 32 V rows into its own shared-memory slot, and only then
+// runs the q/k norm + RoPE prologue, so the HBM latency overlaps the prologue. K rows land with a 16-byte
+// pad per row so that lane = position reads are bank-conflict free. Each warp pipelines K and V through
+// its one slot: scores on K(i) -> copy K(i+1) -> softmax -> P.V on V(i) -> copy V(i+1).
+// Compute: lane = position for the scores (q broadcast from shared memory, no reduction across lanes); the
+// block's softmax and P.V run warp-wide with the lane owning HD/32 dimensions. The warps' states are
+// combined once, at the end. The merge loads every split's partial in parallel (weights exp(m_s - M) first,
+// then the sums).
 #include <algorithm>
 #include "common.cuh"
 
@@ -30,11 +35,80 @@ constexpr int GMAX = 8;
 constexpr int kBlk = 32;  // positions per warp block (lane = position)
 constexpr int kMaxSplits = 32;
 
-// Dynamic shared memory: the warps' final states [kWarps][GMAX][HD + 2], reused by the merge to stage the
-// splits' partials (at most kMaxSplits x GMAX x (HD + 2) floats).
+// Per-warp K/V slot: kBlk K rows at a padded stride (HD + 8 bf16: consecutive rows start 16 bytes apart
+// modulo 128, so eight lanes reading the same 16-byte chunk of eight rows hit eight different bank groups)
+// followed by kBlk V rows at the plain stride (a V row is read by the whole warp at once).
+template <int HD>
+__host__ __device__ constexpr int k_stride() {
+  return (HD + 8) * 2;
+}
+template <int HD>
+__host__ __device__ constexpr size_t slot_bytes() {
+  return static_cast<size_t>(kBlk) * (k_stride<HD>() + HD * 2);
+}
+__host__ __device__ constexpr size_t cmax(size_t a, size_t b) { return a > b ? a : b; }
+// Dynamic shared memory: the warps' K/V slots; afterwards reused for the warps' final states
+// [kWarps][GMAX][HD + 2] and by the merge to stage the splits' partials (kMaxSplits x GMAX x (HD + 2) floats).
 template <int HD>
 constexpr size_t ring_bytes() {
-  return static_cast<size_t>(kMaxSplits > kWarps ? kMaxSplits : kWarps) * GMAX * (HD + 2) * sizeof(float);
+  return cmax(kWarps * slot_bytes<HD>(),
+              static_cast<size_t>(kMaxSplits > kWarps ? kMaxSplits : kWarps) * GMAX * (HD + 2) * sizeof(float));
+}
+
+// 16-byte asynchronous global -> shared copy (L2 only), and its group bookkeeping.
+AIB_DEV void cp16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+AIB_DEV void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+AIB_DEV void cp_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+// Hint L2 to fetch [p, p + bytes) (bytes a multiple of 16, p 16-byte aligned).
+AIB_DEV void prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// Warp-cooperative copy of `cnt` (<= kBlk) consecutive cache rows into a slot region with row stride STRIDE:
+// 16-byte chunk c of the source goes to row c / (HD/8), chunk c % (HD/8); consecutive lanes take
+// consecutive chunks (coalesced).
+template <int HD, int STRIDE>
+AIB_DEV void copy_rows(uint8_t* dst, const uint16_t* rows, int cnt) {
+  constexpr int CPR = HD / 8;
+  const int lane = threadIdx.x & 31;
+  const uint8_t* src = reinterpret_cast<const uint8_t*>(rows);
+  for (int c = lane; c < cnt * CPR; c += 32) cp16(dst + (c / CPR) * STRIDE + (c % CPR) * 16, src + c * 16);
+}
+
+// This warp's share [w0, w1) of the CTA range [j0, j1).
+AIB_DEV void warp_range(int j0, int j1, int* w0, int* w1) {
+  const int warp = threadIdx.x >> 5;
+  const int n = j1 - j0, per_warp = (n + kWarps - 1) / kWarps;
+  *w0 = j0 + min(n, warp * per_warp);
+  *w1 = j0 + min(n, (warp + 1) * per_warp);
+}
+
+// Start the copies of this warp's first block (two commit groups, K then V, possibly empty). Must be called
+// by every thread of the CTA exactly once before attend_range.
+template <int HD>
+AIB_DEV void attend_start(uint8_t* ring, const uint16_t* kc, const uint16_t* vc, int j0, int j1) {
+  int w0, w1;
+  warp_range(j0, j1, &w0, &w1);
+  uint8_t* kslot = ring + (threadIdx.x >> 5) * slot_bytes<HD>();
+  const int cnt = min(kBlk, w1 - w0);
+  if (cnt > 0) copy_rows<HD, k_stride<HD>()>(kslot, kc + static_cast<size_t>(w0) * HD, cnt);
+  cp_commit();
+  if (cnt > 0) copy_rows<HD, HD * 2>(kslot + kBlk * k_stride<HD>(), vc + static_cast<size_t>(w0) * HD, cnt);
+  cp_commit();
+}
+
+// L2 prefetch of the K and V rows [j0, j1) of one group (one thread).
+template <int HD>
+AIB_DEV void prefetch_range(const uint16_t* kc, const uint16_t* vc, int j0, int j1) {
+  if (j1 <= j0) return;
+  const uint32_t bytes = static_cast<uint32_t>(j1 - j0) * HD * 2;
+  prefetch_l2(kc + static_cast<size_t>(j0) * HD, bytes);
+  prefetch_l2(vc + static_cast<size_t>(j0) * HD, bytes);
 }
 
 template <int HD>
@@ -44,6 +118,8 @@ struct Smem {
   float vcur[HD];
   float cur_score[GMAX];
   float cs[HD / 2], sn[HD / 2];
+  float raw[GMAX + 2][HD];       // the group's q rows, its k row and its v row as produced by the qkv GEMV
+  uint16_t wq[HD], wk[HD];       // q / k norm weights (bf16 bits)
   float pw[kWarps][GMAX][kBlk];  // each warp's block probabilities
   float mw[kMaxSplits][GMAX];    // merge weights exp(m_s - M) per split
   float mM[GMAX], mL[GMAX], mc[GMAX], ones[GMAX];
@@ -74,36 +150,25 @@ AIB_DEV void norm_rope(const float* v, const uint16_t* w, const float* cs, const
   }
 }
 
-// PER consecutive bf16 values of a row (lane's slice) as fp32
-template <int PER>
-AIB_DEV void load_row(const uint16_t* p, float* o) {
-  if (PER == 4) {
-    const uint2 r = *reinterpret_cast<const uint2*>(p);
-    o[0] = __uint_as_float(r.x << 16);
-    o[1] = __uint_as_float(r.x & 0xFFFF0000u);
-    o[PER - 2] = __uint_as_float(r.y << 16);
-    o[PER - 1] = __uint_as_float(r.y & 0xFFFF0000u);
-  } else {
-    const uint32_t r = *reinterpret_cast<const uint32_t*>(p);
-    o[0] = __uint_as_float(r << 16);
-    o[PER - 1] = __uint_as_float(r & 0xFFFF0000u);
-  }
-}
-
 // Attention of the G query heads in sm.q over cache rows [j0, j1) of one group. Warp w takes a contiguous
-// slice of the range, 32 positions per block, lane = position:
-//  1. the lane loads its K row (HD bf16) and, for the block's positions, its HD/32 dimensions of each V row;
-//  2. scores against every head with q read from shared memory as broadcast float4s;
-//  3. per head: block max and sum over the lanes, p = exp(s - m'), rescale alpha = exp(m - m');
-//  4. P.V: the lane owns HD/32 dimensions of every head's accumulator, p comes from shared memory.
+// slice of the range, 32 positions per block, lane = position, with the block's rows in the warp's slot
+// (attend_start issued the first block's copies):
+//  1. wait for K(i); scores of the lane's row against every head, q read from shared memory as broadcast
+//     float4s; then start the copy of K(i+1) into the slot;
+//  2. per head: block max and sum over the lanes, p = exp(s - m'), rescale alpha = exp(m - m');
+//  3. wait for V(i); P.V with the lane owning HD/32 dimensions of every head's accumulator, p from shared
+//     memory; then start the copy of V(i+1).
 // The warps' (m, l, acc) are combined in warp order at the end and written as the CTA partial to `part`.
 template <int HD, int G>
 AIB_DEV void attend_range(Smem<HD>& sm, uint8_t* ring, const uint16_t* kc, const uint16_t* vc, int j0, int j1,
                           float scale, float* part) {
   constexpr int PER = HD / 32;  // dims per lane in P.V
+  constexpr int KS = k_stride<HD>();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int n = j1 - j0, per_warp = (n + kWarps - 1) / kWarps;
-  const int w0 = j0 + min(n, warp * per_warp), w1 = j0 + min(n, (warp + 1) * per_warp);
+  int w0, w1;
+  warp_range(j0, j1, &w0, &w1);
+  uint8_t* kslot = ring + warp * slot_bytes<HD>();
+  uint8_t* vslot = kslot + kBlk * KS;
   float m[G], l[G], acc[G][PER];
 #pragma unroll
   for (int h = 0; h < G; ++h) {
@@ -115,37 +180,19 @@ AIB_DEV void attend_range(Smem<HD>& sm, uint8_t* ring, const uint16_t* kc, const
   float* pw = &sm.pw[warp][0][0];
   for (int b0 = w0; b0 < w1; b0 += kBlk) {
     const int cnt = min(kBlk, w1 - b0);
-    const int pos = b0 + lane;
+    const int nb0 = b0 + kBlk, ncnt = max(0, min(kBlk, w1 - nb0));
     const bool valid = lane < cnt;
-    // 1. loads: K row of this lane's position, V slices of the block's positions
-    // All loads of the block are issued before any of them is used (volatile asm keeps them in program order
-    // ahead of the math), so the warp has its whole block (HD * 2 * 2 * 32 bytes) in flight at once.
-    uint4 kr[HD / 8];
-    const uint4* kp = reinterpret_cast<const uint4*>(kc + static_cast<size_t>(valid ? pos : b0) * HD);
-#pragma unroll
-    for (int c = 0; c < HD / 8; ++c)
-      asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-                   : "=r"(kr[c].x), "=r"(kr[c].y), "=r"(kr[c].z), "=r"(kr[c].w)
-                   : "l"(kp + c));
-    uint32_t vr[kBlk][PER / 2];
-#pragma unroll
-    for (int pp = 0; pp < kBlk; ++pp) {
-      const int vp = b0 + min(pp, cnt - 1);
-      const uint32_t* vsrc = reinterpret_cast<const uint32_t*>(vc + static_cast<size_t>(vp) * HD + lane * PER);
-      if (PER == 4)
-        asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];"
-                     : "=r"(vr[pp][0]), "=r"(vr[pp][PER / 2 - 1])
-                     : "l"(vsrc));
-      else
-        asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(vr[pp][0]) : "l"(vsrc));
-    }
-    // 2. scores
+    // 1. scores (K(i) is the older of the two pending groups)
+    cp_wait<1>();
+    __syncwarp();
     float sc[G];
 #pragma unroll
     for (int h = 0; h < G; ++h) sc[h] = 0.0f;
+    const uint8_t* krow = kslot + lane * KS;
 #pragma unroll
     for (int c = 0; c < HD / 8; ++c) {
-      const uint32_t w[4] = {kr[c].x, kr[c].y, kr[c].z, kr[c].w};
+      const uint4 kq = *reinterpret_cast<const uint4*>(krow + c * 16);
+      const uint32_t w[4] = {kq.x, kq.y, kq.z, kq.w};
       float kf[8];
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
@@ -154,69 +201,84 @@ AIB_DEV void attend_range(Smem<HD>& sm, uint8_t* ring, const uint16_t* kc, const
       }
 #pragma unroll
       for (int h = 0; h < G; ++h) {
-        {
-          const float4 qa = *reinterpret_cast<const float4*>(&sm.q[h][c * 8]);
-          const float4 qb = *reinterpret_cast<const float4*>(&sm.q[h][c * 8 + 4]);
-          float a = sc[h];
-          a = fmaf(qa.x, kf[0], a);
-          a = fmaf(qa.y, kf[1], a);
-          a = fmaf(qa.z, kf[2], a);
-          a = fmaf(qa.w, kf[3], a);
-          a = fmaf(qb.x, kf[4], a);
-          a = fmaf(qb.y, kf[5], a);
-          a = fmaf(qb.z, kf[6], a);
-          a = fmaf(qb.w, kf[7], a);
-          sc[h] = a;
-        }
+        const float4 qa = *reinterpret_cast<const float4*>(&sm.q[h][c * 8]);
+        const float4 qb = *reinterpret_cast<const float4*>(&sm.q[h][c * 8 + 4]);
+        float a = sc[h];
+        a = fmaf(qa.x, kf[0], a);
+        a = fmaf(qa.y, kf[1], a);
+        a = fmaf(qa.z, kf[2], a);
+        a = fmaf(qa.w, kf[3], a);
+        a = fmaf(qb.x, kf[4], a);
+        a = fmaf(qb.y, kf[5], a);
+        a = fmaf(qb.z, kf[6], a);
+        a = fmaf(qb.w, kf[7], a);
+        sc[h] = a;
       }
     }
-    // 3. block softmax per head
+    __syncwarp();  // every lane is done with the K rows
+    if (ncnt > 0) copy_rows<HD, KS>(kslot, kc + static_cast<size_t>(nb0) * HD, ncnt);
+    cp_commit();
+    // 2. block softmax per head
     float alpha[G];
 #pragma unroll
     for (int h = 0; h < G; ++h) {
-      {
-        const float s = valid ? sc[h] * scale : -INFINITY;
-        float mb = s;
+      const float s = valid ? sc[h] * scale : -INFINITY;
+      float mb = s;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, o));
-        const float mn = fmaxf(m[h], mb);
-        const float pr = valid ? expf(s - mn) : 0.0f;
-        float ps = pr;
+      for (int o = 16; o > 0; o >>= 1) mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, o));
+      const float mn = fmaxf(m[h], mb);
+      const float pr = valid ? expf(s - mn) : 0.0f;
+      float ps = pr;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
-        alpha[h] = (m[h] == -INFINITY) ? 0.0f : expf(m[h] - mn);
-        l[h] = l[h] * alpha[h] + ps;
-        m[h] = mn;
-        pw[h * kBlk + lane] = pr;
-      }
+      for (int o = 16; o > 0; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
+      alpha[h] = (m[h] == -INFINITY) ? 0.0f : expf(m[h] - mn);
+      l[h] = l[h] * alpha[h] + ps;
+      m[h] = mn;
+      pw[h * kBlk + lane] = pr;
     }
+    // 3. P.V (V(i) is now the older pending group)
+    cp_wait<1>();
     __syncwarp();
-    // 4. P.V
 #pragma unroll
     for (int h = 0; h < G; ++h)
 #pragma unroll
       for (int e = 0; e < PER; ++e) acc[h][e] *= alpha[h];
 #pragma unroll
     for (int pp = 0; pp < kBlk; pp += 4) {
+      uint32_t vr[4][PER / 2];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        // rows past cnt hold stale bytes: read a valid row instead (its p is 0)
+        const uint8_t* vrow = vslot + min(pp + k, cnt - 1) * (HD * 2) + lane * (PER * 2);
+        if (PER == 4) {
+          const uint2 v2 = *reinterpret_cast<const uint2*>(vrow);
+          vr[k][0] = v2.x;
+          vr[k][PER / 2 - 1] = v2.y;
+        } else {
+          vr[k][0] = *reinterpret_cast<const uint32_t*>(vrow);
+        }
+      }
 #pragma unroll
       for (int h = 0; h < G; ++h) {
-        {
-          const float4 p4 = *reinterpret_cast<const float4*>(&pw[h * kBlk + pp]);
-          const float pv[4] = {p4.x, p4.y, p4.z, p4.w};
+        const float4 p4 = *reinterpret_cast<const float4*>(&pw[h * kBlk + pp]);
+        const float pv[4] = {p4.x, p4.y, p4.z, p4.w};
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {
+        for (int k = 0; k < 4; ++k) {
 #pragma unroll
-            for (int e2 = 0; e2 < PER / 2; ++e2) {
-              const uint32_t v = vr[pp + k][e2];
-              acc[h][2 * e2] = fmaf(pv[k], __uint_as_float(v << 16), acc[h][2 * e2]);
-              acc[h][2 * e2 + 1] = fmaf(pv[k], __uint_as_float(v & 0xFFFF0000u), acc[h][2 * e2 + 1]);
-            }
+          for (int e2 = 0; e2 < PER / 2; ++e2) {
+            const uint32_t v = vr[k][e2];
+            acc[h][2 * e2] = fmaf(pv[k], __uint_as_float(v << 16), acc[h][2 * e2]);
+            acc[h][2 * e2 + 1] = fmaf(pv[k], __uint_as_float(v & 0xFFFF0000u), acc[h][2 * e2 + 1]);
           }
         }
       }
     }
-    __syncwarp();  // pw is rewritten by the next block
+    __syncwarp();  // pw and the V rows are rewritten next
+    if (ncnt > 0) copy_rows<HD, HD * 2>(vslot, vc + static_cast<size_t>(nb0) * HD, ncnt);
+    cp_commit();
   }
+  cp_wait<0>();     // nothing of this thread may land in the ring once it is reused below
+  __syncthreads();  // every warp is done with its slot
   // combine the warps in order through the dynamic buffer
   float* wst = reinterpret_cast<float*>(ring);  // [kWarps][GMAX][HD + 2]
 #pragma unroll
@@ -258,7 +320,7 @@ AIB_DEV void attend_range(Smem<HD>& sm, uint8_t* ring, const uint16_t* kc, const
 
 // Merge S partials in split order on top of an initial state (m0, l0, acc0[d]; null = empty) and write out.
 // The group's partial block (S x G x (HD+2) floats, contiguous) is first copied into shared memory (`stage`,
-// the now idle K/V ring) with every thread issuing independent 16-byte loads, then merged from there:
+// the now idle K/V ring) with asynchronous 16-byte copies all in flight at once, then merged from there:
 // weights exp(m_s - M) per split, fixed-order sums.
 template <int HD>
 AIB_DEV void merge_write(Smem<HD>& sm, float* stage, const float* parts, int S, int G, const float* m0,
@@ -266,9 +328,10 @@ AIB_DEV void merge_write(Smem<HD>& sm, float* stage, const float* parts, int S, 
   const int nf = S * G * (HD + 2);
   const int n4 = nf / 4;
   if ((nf & 3) == 0 && (reinterpret_cast<uintptr_t>(parts) & 15) == 0) {
-    const float4* src = reinterpret_cast<const float4*>(parts);
-    float4* dst = reinterpret_cast<float4*>(stage);
-    for (int i = threadIdx.x; i < n4; i += kThreads) dst[i] = __ldcg(src + i);
+    // asynchronous 16-byte copies from L2 (every copy in flight at once), then one wait
+    for (int i = threadIdx.x; i < n4; i += kThreads) cp16(stage + 4 * i, parts + 4 * i);
+    cp_commit();
+    cp_wait<0>();
   } else {
     for (int i = threadIdx.x; i < nf; i += kThreads) stage[i] = __ldcg(parts + i);
   }
@@ -314,35 +377,60 @@ __global__ void __launch_bounds__(kThreads)
   extern __shared__ __align__(128) uint8_t ring[];
   const int s = blockIdx.x, S = gridDim.x, g = blockIdx.y;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  uint16_t* kg = kc + static_cast<size_t>(g) * maxt * HD;
+  uint16_t* vg = vc + static_cast<size_t>(g) * maxt * HD;
+  // constant inputs before the grid dependency resolves: RoPE frequencies, q / k norm weights, and an L2
+  // hint for this split's K/V rows from a possibly stale pos (any value it reads gives in-bounds rows)
+  const float inv_r = threadIdx.x < HD / 2 ? inv[threadIdx.x] : 0.0f;
+  for (int d = threadIdx.x; d < HD; d += kThreads) {
+    sm.wq[d] = qn[d];
+    sm.wk[d] = kn[d];
+  }
+  if (threadIdx.x == 0) {
+    const long long ph = *reinterpret_cast<const volatile long long*>(pos_p);
+    const int n = (ph > 0 && ph < maxt) ? static_cast<int>(ph) : 0;
+    const int chunk = (n + S - 1) / S, a = min(n, s * chunk);
+    prefetch_range<HD>(kg, vg, a, min(n, a + chunk));
+  }
   pdl_wait();
+  // pos and the group's q, k and v rows in one round trip
   const long long pos_ll = *pos_p;
+  for (int i = threadIdx.x; i < (G + 2) * HD; i += kThreads) {
+    const int r = i / HD, d = i % HD;
+    const int row = r < G ? g * G + r : (r == G ? H + g : H + KV + g);
+    sm.raw[r][d] = qkv[static_cast<size_t>(row) * HD + d];
+  }
   const bool pos_ok = pos_ll >= 0 && pos_ll < maxt;
   if (!pos_ok && s == 0 && threadIdx.x == 0) set_status(AIB_DEV_BAD_POS);
   const int pos = pos_ok ? static_cast<int>(pos_ll) : 0;
-  for (int r = threadIdx.x; r < HD / 2; r += kThreads) {
-    const float ang = static_cast<float>(pos) * inv[r];
-    sm.cs[r] = cosf(ang);
-    sm.sn[r] = sinf(ang);
+  // this split's share of the past positions 0..pos-1; its first rows start streaming now
+  const int n = pos_ok ? pos : 0;
+  const int chunk = (n + S - 1) / S;
+  const int j0 = min(n, s * chunk), j1 = min(n, j0 + chunk);
+  attend_start<HD>(ring, kg, vg, j0, j1);
+  if (threadIdx.x < HD / 2) {
+    const float ang = static_cast<float>(pos) * inv_r;
+    sm.cs[threadIdx.x] = cosf(ang);
+    sm.sn[threadIdx.x] = sinf(ang);
   }
   __syncthreads();
-  // q heads of the group + the group's k (warp per head vector)
-  for (int t = warp; t <= G; t += kWarps) {
-    if (t < G)
-      norm_rope<HD>(qkv + static_cast<size_t>(g * G + t) * HD, qn, sm.cs, sm.sn, eps, sm.q[t]);
-    else
-      norm_rope<HD>(qkv + static_cast<size_t>(H + g) * HD, kn, sm.cs, sm.sn, eps, sm.kcur);
-  }
-  __syncthreads();
-  uint16_t* kg = kc + static_cast<size_t>(g) * maxt * HD;
-  uint16_t* vg = vc + static_cast<size_t>(g) * maxt * HD;
-  for (int d = threadIdx.x; d < HD; d += kThreads) {
-    const uint16_t kb = f32_to_bf16_rne(sm.kcur[d]);
-    const uint16_t vb = f32_to_bf16_rne(qkv[static_cast<size_t>(H + KV + g) * HD + d]);
-    sm.kcur[d] = bf16_to_f32(kb);
-    sm.vcur[d] = bf16_to_f32(vb);
-    if (s == 0 && pos_ok) {
-      kg[static_cast<size_t>(pos) * HD + d] = kb;
-      vg[static_cast<size_t>(pos) * HD + d] = vb;
+  // warp per vector: the q heads of the group, the group's k (norm, RoPE, bf16 rounding, cache write) and
+  // its v (bf16 rounding, cache write); lane owns elements lane + 32 i
+  for (int t = warp; t < G + 2; t += kWarps) {
+    if (t < G) {
+      norm_rope<HD>(sm.raw[t], sm.wq, sm.cs, sm.sn, eps, sm.q[t]);
+    } else {
+      float* cur = t == G ? sm.kcur : sm.vcur;
+      uint16_t* cache = t == G ? kg : vg;
+      if (t == G) norm_rope<HD>(sm.raw[G], sm.wk, sm.cs, sm.sn, eps, sm.kcur);
+      __syncwarp();
+#pragma unroll
+      for (int i = 0; i < HD / 32; ++i) {
+        const int d = lane + 32 * i;
+        const uint16_t b = f32_to_bf16_rne(t == G ? sm.kcur[d] : sm.raw[G + 1][d]);
+        cur[d] = bf16_to_f32(b);
+        if (s == 0 && pos_ok) cache[static_cast<size_t>(pos) * HD + d] = b;
+      }
     }
   }
   __syncthreads();
@@ -352,10 +440,6 @@ __global__ void __launch_bounds__(kThreads)
     sc = warp_sum(sc);
     if (lane == 0) sm.cur_score[h] = sc * scale;
   }
-  // this split's share of the past positions 0..pos-1
-  const int n = pos_ok ? pos : 0;
-  const int chunk = (n + S - 1) / S;
-  const int j0 = min(n, s * chunk), j1 = min(n, j0 + chunk);
   float* part = ws_part + (static_cast<size_t>(g) * S + s) * G * (HD + 2);
   attend_range<HD, G>(sm, ring, kg, vg, j0, j1, scale, part);
   // ordered merge by the last CTA of the group
@@ -423,19 +507,27 @@ __global__ void __launch_bounds__(kThreads)
   __shared__ Smem<HD> sm;
   extern __shared__ __align__(128) uint8_t ring[];
   const int s = blockIdx.x, S = gridDim.x, g = blockIdx.y, t = blockIdx.z;
+  const uint16_t* kg = kc + static_cast<size_t>(g) * maxt * HD;
+  const uint16_t* vg = vc + static_cast<size_t>(g) * maxt * HD;
+  if (threadIdx.x == 0) {  // L2 hint from a possibly stale pos: any value it reads gives in-bounds rows
+    const long long ph = *reinterpret_cast<const volatile long long*>(pos_p) + t;
+    const int n = (ph >= 0 && ph < maxt) ? static_cast<int>(ph) + 1 : 0;
+    const int chunk = (n + S - 1) / S, a = min(n, s * chunk);
+    prefetch_range<HD>(kg, vg, a, min(n, a + chunk));
+  }
   pdl_wait();
   const long long p = *pos_p + t;
   const bool ok = p >= 0 && p < maxt;
   const int n = ok ? static_cast<int>(p) + 1 : 0;
+  const int chunk = (n + S - 1) / S;
+  const int j0 = min(n, s * chunk), j1 = min(n, j0 + chunk);
+  attend_start<HD>(ring, kg, vg, j0, j1);
   for (int idx = threadIdx.x; idx < G * HD; idx += kThreads)
     sm.q[idx / HD][idx % HD] = q[(static_cast<size_t>(t) * H + g * G) * HD + idx];
   __syncthreads();
-  const int chunk = (n + S - 1) / S;
-  const int j0 = min(n, s * chunk), j1 = min(n, j0 + chunk);
   const size_t slot = static_cast<size_t>(t) * KV + g;
   float* part = ws_part + (slot * S + s) * G * (HD + 2);
-  attend_range<HD, G>(sm, ring, kc + static_cast<size_t>(g) * maxt * HD, vc + static_cast<size_t>(g) * maxt * HD, j0,
-                      j1, scale, part);
+  attend_range<HD, G>(sm, ring, kg, vg, j0, j1, scale, part);
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) {

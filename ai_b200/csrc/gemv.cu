@@ -1127,7 +1127,8 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
 // the column order of parity par, and a row reads its result from the columns of its own parity.
 constexpr int kTcConsumers = 512;
 constexpr int kTcThreads = kTcConsumers + 32;
-constexpr int kTcSlotMeta = 128 + 256 * 4;  // per slot: 32-word exception mask, partials [R rows][2*CW warps]
+constexpr int kTcSlotMeta = 128 + 256 * 4;
+constexpr int kTcPrologueRecords = 8;  // x records per consumer thread per prologue batch (K <= 16384: one batch)  // per slot: 32-word exception mask, partials [R rows][2*CW warps]
 
 // Byte offset of the x record (8 bytes: low pair, high pair) for chunk gc, MMA i, lane quad t, column block
 // blk and part sp. Parts 0 and 1 of all (blk, t) form one 128-byte line per (gc, i) and part 2 a 64-byte line
@@ -1197,10 +1198,25 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   }
 
   // ---------------- consumers: x prologue into the three-part B records
-  pdl_wait();
-  const int K = p.K;
-  float rs = 1.0f;
+  // Record pr holds columns (c, c+1) and (128+c, 129+c) of chunk gc = pr / 64 (c = 2 * (pr % 64)). Consumer
+  // thread tid owns records tid + 512 j. All of a batch's loads are issued before any is used (one memory
+  // round trip per batch; one batch up to K = 16384), the RMS sum reuses the loaded values, and the norm
+  // weights -- constant inputs -- are read before the grid dependency resolves.
+  const int K = p.K, npr = K / 4;
+  constexpr int kBatch = kTcPrologueRecords * kTcConsumers;
+  uint32_t lwa[kTcPrologueRecords], lwb[kTcPrologueRecords];
   if (RMS) {
+#pragma unroll
+    for (int j = 0; j < kTcPrologueRecords; ++j) {
+      const int pr = tid + j * kTcConsumers;
+      const int k0 = (pr >> 6) * 256 + (pr & 63) * 2;
+      lwa[j] = pr < npr ? *reinterpret_cast<const uint32_t*>(p.lnw + k0) : 0u;
+      lwb[j] = pr < npr ? *reinterpret_cast<const uint32_t*>(p.lnw + k0 + 128) : 0u;
+    }
+  }
+  pdl_wait();
+  float rs = 1.0f;
+  if (RMS && npr > kBatch) {  // several batches: the sum of squares first
     const float4* xg = reinterpret_cast<const float4*>(p.x);
     float ss = 0.0f;
     for (int k = tid; k < K / 4; k += kTcConsumers) {
@@ -1215,32 +1231,80 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     for (int w = 0; w < kTcConsumers / 32; ++w) tot += rms_red[w];
     rs = rsqrtf(tot / static_cast<float>(K) + p.eps);
   }
-  for (int pr = tid; pr < K / 4; pr += kTcConsumers) {  // (low pair, high pair) of one record
-    const int gc = pr >> 6, c = (pr & 63) * 2;           // low column c, c+1 and high 128+c, 129+c of chunk gc
-    float v[4];
+  for (int b0 = 0; b0 < npr; b0 += kBatch) {
+    float4 xv[kTcPrologueRecords];  // x at (c, c+1, 128+c, 129+c) of the record's chunk
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const int k = gc * 256 + c + (e & 1) + (e >> 1) * 128;
-      float x = (MODE == 2) ? silu_mul(p.x[k], p.x[K + k]) : p.x[k];
-      if (RMS) x = bf16_to_f32(p.lnw[k]) * (x * rs);
-      v[e] = x;
-    }
-    uint32_t w[3][2];
-#pragma unroll
-    for (int sp = 0; sp < 3; ++sp) {
-      uint16_t b[4];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        b[e] = f32_to_bf16_rne(v[e]);
-        v[e] -= bf16_to_f32(b[e]);
+    for (int j = 0; j < kTcPrologueRecords; ++j) {
+      const int pr = b0 + tid + j * kTcConsumers;
+      const int k0 = (pr >> 6) * 256 + (pr & 63) * 2;
+      float2 lo = make_float2(0.0f, 0.0f), hi = lo;
+      if (pr < npr) {
+        lo = *reinterpret_cast<const float2*>(p.x + k0);
+        hi = *reinterpret_cast<const float2*>(p.x + k0 + 128);
       }
-      w[sp][0] = static_cast<uint32_t>(b[0]) | (static_cast<uint32_t>(b[1]) << 16);
-      w[sp][1] = static_cast<uint32_t>(b[2]) | (static_cast<uint32_t>(b[3]) << 16);
+      xv[j] = make_float4(lo.x, lo.y, hi.x, hi.y);
     }
-    const int blk = c >> 6, t = (c >> 4) & 3, i = (c & 15) >> 1;
+    if (MODE == 2) {  // input silu(x[k]) * x[K + k]
 #pragma unroll
-    for (int sp = 0; sp < 3; ++sp)
-      *reinterpret_cast<uint2*>(xr + tc_xrec(p.nch, gc, i, blk, t, sp)) = make_uint2(w[sp][0], w[sp][1]);
+      for (int j = 0; j < kTcPrologueRecords; ++j) {
+        const int pr = b0 + tid + j * kTcConsumers;
+        const int k0 = (pr >> 6) * 256 + (pr & 63) * 2;
+        if (pr < npr) {
+          const float2 lo = *reinterpret_cast<const float2*>(p.x + K + k0);
+          const float2 hi = *reinterpret_cast<const float2*>(p.x + K + k0 + 128);
+          xv[j] = make_float4(silu_mul(xv[j].x, lo.x), silu_mul(xv[j].y, lo.y), silu_mul(xv[j].z, hi.x),
+                              silu_mul(xv[j].w, hi.y));
+        }
+      }
+    }
+    if (RMS && npr <= kBatch) {  // one batch: the sum of squares from the loaded values (zeros past K)
+      float ss = 0.0f;
+#pragma unroll
+      for (int j = 0; j < kTcPrologueRecords; ++j)
+        ss += (xv[j].x * xv[j].x + xv[j].y * xv[j].y) + (xv[j].z * xv[j].z + xv[j].w * xv[j].w);
+      ss = warp_sum(ss);
+      if (lane == 0) rms_red[tid >> 5] = ss;
+      named_sync(1, kTcConsumers);
+      float tot = 0.0f;
+#pragma unroll
+      for (int w = 0; w < kTcConsumers / 32; ++w) tot += rms_red[w];
+      rs = rsqrtf(tot / static_cast<float>(K) + p.eps);
+    }
+#pragma unroll
+    for (int j = 0; j < kTcPrologueRecords; ++j) {
+      const int pr = b0 + tid + j * kTcConsumers;
+      if (pr >= npr) continue;
+      const int gc = pr >> 6, c = (pr & 63) * 2;
+      float v[4] = {xv[j].x, xv[j].y, xv[j].z, xv[j].w};
+      if (RMS) {
+        uint32_t wa = lwa[j], wb = lwb[j];
+        if (b0 > 0) {  // later batches read their weights here
+          const int k0 = gc * 256 + c;
+          wa = *reinterpret_cast<const uint32_t*>(p.lnw + k0);
+          wb = *reinterpret_cast<const uint32_t*>(p.lnw + k0 + 128);
+        }
+        v[0] = __uint_as_float(wa << 16) * (v[0] * rs);
+        v[1] = __uint_as_float(wa & 0xFFFF0000u) * (v[1] * rs);
+        v[2] = __uint_as_float(wb << 16) * (v[2] * rs);
+        v[3] = __uint_as_float(wb & 0xFFFF0000u) * (v[3] * rs);
+      }
+      uint32_t w[3][2];
+#pragma unroll
+      for (int sp = 0; sp < 3; ++sp) {
+        uint16_t bq[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          bq[e] = f32_to_bf16_rne(v[e]);
+          v[e] -= bf16_to_f32(bq[e]);
+        }
+        w[sp][0] = static_cast<uint32_t>(bq[0]) | (static_cast<uint32_t>(bq[1]) << 16);
+        w[sp][1] = static_cast<uint32_t>(bq[2]) | (static_cast<uint32_t>(bq[3]) << 16);
+      }
+      const int blk = c >> 6, t = (c >> 4) & 3, i = (c & 15) >> 1;
+#pragma unroll
+      for (int sp = 0; sp < 3; ++sp)
+        *reinterpret_cast<uint2*>(xr + tc_xrec(p.nch, gc, i, blk, t, sp)) = make_uint2(w[sp][0], w[sp][1]);
+    }
   }
   named_sync(1, kTcConsumers);
 

@@ -249,20 +249,26 @@ def gpu_arm(args, rank, world):
 
 
 def micro_attn(args):
-    """Fused T=1 attention of one Qwen3-8B layer at position 4096 (bf16 KV, 8 groups x 4 heads)."""
+    """Fused T=1 attention of a Qwen3-8B layer at position 4096 (bf16 KV, 8 groups x 4 heads). Successive
+    calls walk the 36 layers' caches (680 MB), as the decode step does, so the K/V rows come from HBM."""
     import torch
     from ai_b200 import tkernels
-    H, KV, HD, maxt, pos = 32, 8, 128, 4608, CTX
+    H, KV, HD, maxt, pos, L = 32, 8, 128, 4608, CTX, 36
     g = torch.Generator(device="cuda").manual_seed(0)
-    kc = torch.randn(KV, maxt, HD, generator=g, device="cuda").bfloat16()
-    vc = torch.randn(KV, maxt, HD, generator=g, device="cuda").bfloat16()
+    kv = torch.randn(L, 2, KV, maxt, HD, generator=g, device="cuda").bfloat16()
     qkv = torch.randn((H + 2 * KV) * HD, generator=g, device="cuda")
     qn = torch.ones(HD, dtype=torch.bfloat16, device="cuda")
     inv = (1.0 / (1e6 ** (torch.arange(0, HD, 2, dtype=torch.float32) / HD))).cuda()
     P = torch.tensor([pos], device="cuda")
     out = torch.zeros(H * HD, device="cuda")
     nbytes = 2 * KV * (pos + 1) * HD * 2
-    return (lambda: tkernels.rope_attn(qkv, qn, qn, inv, P, kc, vc, out, maxt, 1e-6, HD ** -0.5, H, KV, HD)), nbytes
+    calls = [0]
+
+    def run():
+        layer = calls[0] % L
+        calls[0] += 1
+        tkernels.rope_attn(qkv, qn, qn, inv, P, kv[layer, 0], kv[layer, 1], out, maxt, 1e-6, HD ** -0.5, H, KV, HD)
+    return run, nbytes
 
 
 def micro_sample(args):
@@ -282,7 +288,8 @@ def micro(args):
     """One kernel alone on a small case (for ncu captures and quick A/B timing), timed as `--steps` calls
     captured in one CUDA graph and replayed (device time, no host launch overhead). gemv: the codec GEMV on a
     Qwen3-8B gu-shaped matrix [24576, 4096] (151 MB of planes, > L2), T = 1 with the RMS prologue;
-    gemv_down: [4096, 12288] with the SiLU-gated input; attn: one layer's decode attention at ctx 4096;
+    gemv_down: [4096, 12288] with the SiLU-gated input; gemv_qkv / gemv_o: the [6144, 4096] / [4096, 4096]
+    matrices; attn: a layer's decode attention at ctx 4096 (K/V from HBM);
     sample: the sampler on one vocabulary row."""
     import torch
     from ai_b200 import build, wcomp, _lib
@@ -319,26 +326,30 @@ def micro(args):
                           "GBps": round(nbytes / us / 1e3, 1)}))
         return
     g = torch.Generator(device="cuda").manual_seed(0)
-    N, K = (24576, 4096) if args.micro == "gemv" else (4096, 12288)
+    # Qwen3-8B layer shapes: (N, K, mode, RMS prologue)
+    N, K, mode, rms = {"gemv": (24576, 4096, 0, True), "gemv_down": (4096, 12288, 2, False),
+                       "gemv_qkv": (6144, 4096, 0, True), "gemv_o": (4096, 4096, 1, False)}[args.micro]
     c = wcomp.compress((torch.randn(N, K, generator=g, device="cuda") * 0.02).bfloat16())
     x = torch.randn(K * 2, generator=g, device="cuda")
     y = torch.zeros(N, device="cuda")
     lnw = torch.ones(K, dtype=torch.bfloat16, device="cuda")
-    mode = 0 if args.micro == "gemv" else 2
-    run = lambda: wcomp.gemvc1(x, c, y, mode, lnw=lnw if mode == 0 else None)  # noqa: E731
+    ws = wcomp.gemv_workspace([c], x.device) if args.streamk else None
+    run = lambda: wcomp.gemvc1(x, c, y, mode, lnw=lnw if rms else None, ws=ws)  # noqa: E731
     us = timed(run, max(args.steps, 1))
     torch.cuda.synchronize()
     st = _lib.status()
-    print(json.dumps({"micro": args.micro, "variant": args.gemv_variant, "device_status": st, "N": N, "K": K, "bytes": c.nbytes, "us_per_launch": round(us, 2),
+    print(json.dumps({"micro": args.micro, "variant": args.gemv_variant, "streamk": bool(args.streamk),
+                      "device_status": st, "N": N, "K": K, "bytes": c.nbytes, "us_per_launch": round(us, 2),
                       "GBps": round(c.nbytes / us / 1e3, 1)}))
 
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--micro", choices=["gemv", "gemv_down", "attn", "sample"], default=None,
+    ap.add_argument("--micro", choices=["gemv", "gemv_down", "gemv_qkv", "gemv_o", "attn", "sample"], default=None,
                     help="time one kernel alone on a small case (for ncu) instead of the decode benchmark")
     ap.add_argument("--gemv-variant", type=int, default=None, choices=[0, 1, 2, 3],
                     help="codec GEMV kernel for --micro: 0 tensor-core 24 KB stages, 1 CUDA-core 12 KB stages, 2 CUDA-core 48 KB stages, 3 tensor-core 48 KB stages (default)")
+    ap.add_argument("--streamk", action="store_true", help="--micro gemv*: pass the stream-K workspace")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=256)
     ap.add_argument("--warmup", type=int, default=8)
