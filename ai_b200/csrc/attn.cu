@@ -393,6 +393,9 @@ __global__ void __launch_bounds__(kThreads)
     prefetch_range<HD>(kg, vg, a, min(n, a + chunk));
   }
   pdl_wait();
+  // every CTA of this grid is resident by now: the next kernel may launch onto SMs as they free up (it waits
+  // for this grid to complete before it reads anything written here)
+  pdl_trigger();
   // pos and the group's q, k and v rows in one round trip
   const long long pos_ll = *pos_p;
   for (int i = threadIdx.x; i < (G + 2) * HD; i += kThreads) {
@@ -458,7 +461,6 @@ __global__ void __launch_bounds__(kThreads)
                     sm.cur_score, sm.ones, sm.vcur, out + static_cast<size_t>(g) * G * HD);
     if (threadIdx.x == 0) ws_cnt[g] = 0;
   }
-  pdl_trigger();
 }
 
 // ------------------------------------------------------------------------------------ batched
@@ -516,6 +518,7 @@ __global__ void __launch_bounds__(kThreads)
     prefetch_range<HD>(kg, vg, a, min(n, a + chunk));
   }
   pdl_wait();
+  pdl_trigger();  // as in rope_attn_kernel
   const long long p = *pos_p + t;
   const bool ok = p >= 0 && p < maxt;
   const int n = ok ? static_cast<int>(p) + 1 : 0;
@@ -541,7 +544,6 @@ __global__ void __launch_bounds__(kThreads)
                     nullptr, out + (static_cast<size_t>(t) * H + g * G) * HD);
     if (threadIdx.x == 0) ws_cnt[slot] = 0;
   }
-  pdl_trigger();
 }
 
 // Splits per (group, token): about one CTA per SM in total, capped so that a group's partials
