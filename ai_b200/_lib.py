@@ -41,6 +41,10 @@ SIGNATURES = {
     "aib_c12_decode": (I32, [C.POINTER(C12Desc), I32, I32, P, I32, P]),
     "aib_gemv_c12_workspace": (SZ, [C.POINTER(C12Desc), I32]),
     "aib_gemv_set_variant": (None, [I32]),
+    "aib_head8_tables": (I32, [P, I32, I32, P, P, P, P, P, P]),
+    "aib_head8_workspace": (SZ, [I32, I32, I32]),
+    "aib_head8_bounds": (I32, [P, I32, I32, P, P, P, P, P, I32, I32, P, I32, P, P, SZ, P]),
+    "aib_head8_greedy": (I32, [P, I32, I32, C.POINTER(C12Desc), P, I32, P, P, P, SZ, P]),
     "aib_gemv_c12": (I32, [C.POINTER(C12Desc), P, P, I32, I32, I32, I32, P, F32, P, SZ, P]),
     "aib_rmsnorm": (I32, [P, P, P, I32, I32, F32, P]),
     "aib_embed": (I32, [P, P, I32, I32, I32, P, P]),

@@ -7,3 +7,4 @@
 #include "attn.cu"
 #include "attn_noalloc.cu"
 #include "sampler.cu"
+#include "head8.cu"

@@ -1,0 +1,68 @@
+"""Int8 vocabulary head -- the reference's `generation/head.py` `Head` on sm_100a kernels.
+
+  Head(w, c12)          Head.__init__ (head.py:29-50): int8 copy Q [V, D] + S, C1, C2, AM [V] from the head's
+                        bf16 weights `w`; `c12` is the same head in the 12-bit codec (`wcomp.compress`),
+                        from which the exact candidate rows are decoded (lossless), so the bf16 head need
+                        not stay resident
+  .bounds(h, T)         Head.bounds / vocab_a_k (head.py:52-57, kernels/vocab8.py:19-44): HI [T, V], LO [T]
+  .pick(h, T)           Head.pick with temperature 0 (head.py:59-88): exact fp32 logits of the candidates
+                        HI >= LO, argmax with the smallest id on ties -> int64 ids [T] on the device
+
+Sampling (temperature > 0) is not offered here: the reference recomputes every exact logit on the CPU for
+it; the engine samples from the codec GEMV's logits with `ai_b200.sampler` instead.
+"""
+import ctypes as C
+
+import torch
+
+from . import _lib
+from ._lib import ptr, stream_ptr
+
+
+class Head:
+    def __init__(self, w, c12, TM=16):
+        if w.dtype != torch.bfloat16 or w.dim() != 2:
+            raise ValueError("Head: w must be a bf16 [V, D] tensor")
+        V, D = w.shape
+        if (c12["N"], c12["K"]) != (V, D):
+            raise ValueError("Head: the codec matrix must have the shape of w")
+        if D % 16:
+            raise ValueError("Head: D must be a multiple of 16")
+        dev = w.device
+        self.V, self.D, self.TM, self.c12 = V, D, TM, c12
+        self.Q = torch.empty(V, D, dtype=torch.int8, device=dev)
+        self.S, self.C1, self.C2, self.AM = (torch.empty(V, device=dev) for _ in range(4))
+        w = w.contiguous()
+        _lib.call("aib_head8_tables", ptr(w.view(torch.int16)), V, D, ptr(self.Q), ptr(self.S), ptr(self.C1),
+                  ptr(self.C2), ptr(self.AM), stream_ptr())
+        self.HI = torch.empty(TM, V, device=dev)
+        self.LO = torch.full((TM,), -float("inf"), device=dev)
+        self.out = torch.zeros(TM, dtype=torch.int64, device=dev)
+        self.ws = torch.zeros(_lib.lib().aib_head8_workspace(V, D, TM), dtype=torch.uint8, device=dev)
+        self._desc = c12.desc()
+
+    def _h(self, h, T):
+        if not (1 <= T <= self.TM) or h.dtype != torch.float32 or h.dim() != 2 or h.shape[1] != self.D:
+            raise ValueError("Head: h must be fp32 [>=T, D] with 1 <= T <= TM")
+        if h.stride(1) != 1:
+            raise ValueError("Head: h rows must be contiguous")
+        return h
+
+    def bounds(self, h, T):
+        """HI[:T], LO[:T] for rows h[:T] (on the device, graph-capturable)."""
+        h = self._h(h, T)
+        _lib.call("aib_head8_bounds", ptr(h), T, h.stride(0), ptr(self.Q), ptr(self.S), ptr(self.C1), ptr(self.C2),
+                  ptr(self.AM), self.V, self.D, ptr(self.HI), self.V, ptr(self.LO), ptr(self.ws), self.ws.numel(),
+                  stream_ptr())
+        return self.HI[:T], self.LO[:T]
+
+    def pick(self, h, T, temperature=0.0, run_bounds=True):
+        """Greedy ids for rows h[:T] (int64 device tensor view of length T)."""
+        if temperature > 0:
+            raise NotImplementedError("Head.pick samples only greedily; use ai_b200.sampler for temperature > 0")
+        h = self._h(h, T)
+        if run_bounds:
+            self.bounds(h, T)
+        _lib.call("aib_head8_greedy", ptr(h), T, h.stride(0), C.byref(self._desc), ptr(self.HI), self.V, ptr(self.LO),
+                  ptr(self.out), ptr(self.ws), self.ws.numel(), stream_ptr())
+        return self.out[:T]

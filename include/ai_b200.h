@@ -110,6 +110,28 @@ void aib_gemv_set_variant(int variant);
 int aib_gemv_c12(const aib_c12* c, const float* x, float* y, int T, int x_stride, int y_stride, int mode,
                  const uint16_t* lnw, float eps, void* ws, size_t ws_bytes, void* stream);
 
+/* --------------------------------------------------------------------------- int8 vocab head ---- */
+/* Quantised copy of a vocabulary head w (bf16 bits [V, D]) and its error bounds (replaces Head.__init__,
+ * generation/head.py:29-50): per row s = float(max|e|/127) (1 if 0), Q = round-half-even(e/s) clamped to
+ * +-127 (int8 [V, D]), C1 = max|e - sQ| (1 + 1e-6), C2 = ||e - sQ||_2 (1 + 1e-6), AM = max|e|, all computed in
+ * float64 and stored as fp32 [V]. */
+int aib_head8_tables(const uint16_t* w, int V, int D, int8_t* Q, float* S, float* C1, float* C2, float* AM,
+                     void* stream);
+/* Workspace bytes for aib_head8_bounds / aib_head8_greedy (zero-filled once; calls leave it zeroed). */
+size_t aib_head8_workspace(int V, int D, int T);
+/* Logit bounds for T <= 16 rows of h (fp32 [T, ldh]) (replaces vocab_a_k, kernels/vocab8.py:19-44):
+ * HI[t, v] = s_v Q_v.h_t + B (row stride ldhi), B = min(C2 ||h_t||_2, C1 ||h_t||_1) + 2e-4 AM ||h_t||_1,
+ * LO[t] = max_v (s_v Q_v.h_t - B). D a multiple of 16, Q 16-byte aligned. */
+int aib_head8_bounds(const float* h, int T, int ldh, const int8_t* Q, const float* S, const float* C1,
+                     const float* C2, const float* AM, int V, int D, float* HI, int ldhi, float* LO, void* ws,
+                     size_t ws_bytes, void* stream);
+/* Greedy token per row (replaces Head.pick with temperature 0, generation/head.py:59-88, and vocab_b_k /
+ * vocab_c_k, kernels/vocab8.py:46-77): among the rows v with HI[t, v] >= LO[t], the exact fp32 logit of
+ * the head row (decoded from the 12-bit codec W [V, D]; each product rounded to fp32, summed in column
+ * order, head.py:19-26); out[t] = the argmax, the smallest id on ties. */
+int aib_head8_greedy(const float* h, int T, int ldh, const aib_c12* W, const float* HI, int ldhi, const float* LO,
+                     int64_t* out, void* ws, size_t ws_bytes, void* stream);
+
 /* ------------------------------------------------------------------------------- norm / embed ---- */
 /* out[t] = w * x[t] * rsqrt(mean(x[t]^2) + eps)   (replaces rmsg_k, tkernels.py:216-225) */
 int aib_rmsnorm(const float* x, const uint16_t* w, float* out, int T, int D, float eps, void* stream);

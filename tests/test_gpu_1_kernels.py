@@ -458,3 +458,130 @@ def test_sampler_ties_across_slices(lib):
     assert ids == [70000, 150000]
     ids = sampler.sample(lg, 1.0, 0.5, 2, [0.25, 0.75])  # exclusive cumsum 0.5 is not < 0.5: one token kept
     assert ids == [70000, 70000]
+
+
+# ------------------------------------------------------------------------------------ int8 vocab head
+from oracle import head as ohead  # noqa: E402
+
+
+def _head_tables(w_bits):
+    from ai_b200 import _lib
+    V, D = w_bits.shape
+    w = from_bits(w_bits)
+    Q = torch.empty(V, D, dtype=torch.int8, device="cuda")
+    S, C1, C2, AM = (torch.empty(V, device="cuda") for _ in range(4))
+    from ai_b200._lib import ptr, stream_ptr
+    _lib.call("aib_head8_tables", ptr(w.view(torch.int16)), V, D, ptr(Q), ptr(S), ptr(C1), ptr(C2), ptr(AM),
+              stream_ptr())
+    torch.cuda.synchronize()
+    return Q, S, C1, C2, AM
+
+
+def _check_tables(got, ref):
+    Q, S, C1, C2, AM = (t.cpu().numpy() for t in got)
+    rq, rs, rc1, rc2, ram = ref
+    np.testing.assert_array_equal(Q, rq)
+    np.testing.assert_array_equal(S, rs)
+    np.testing.assert_array_equal(C1, rc1)
+    np.testing.assert_array_equal(AM, ram)
+    # C2 sums squares in float64 in another order: equal after rounding to fp32 up to one fp32 ulp
+    np.testing.assert_array_max_ulp(C2, rc2, maxulp=1)
+
+
+def test_head8_tables_golden(lib):
+    """Head.__init__ tables of the reference's own fixture (generation/head.py:29-50), bit for bit."""
+    z = golden("head")
+    _check_tables(_head_tables(z["w"]), (z["q"], z["s"], z["c1"], z["c2"], z["am"]))
+
+
+def test_head8_tables_vs_oracle(lib):
+    """Random head with the edge rows the quantiser meets: all zeros, one tiny row, exact .5 quotients, a row
+    whose max is negative."""
+    g = np.random.default_rng(5)
+    w = (g.standard_normal((2000, 1024)) * 0.02).astype(np.float32)
+    w[3] = 0.0
+    w[4] *= 1e-30
+    w[5, :8] = [127.0, 63.5, -63.5, 0.5, 1.5, -2.5, 31.75, 0.25]
+    w[5, 8:] = 0.0
+    w[6] = -np.abs(w[6]) * 3
+    wb = codec.f32_to_bf16_bits(w)
+    _check_tables(_head_tables(wb), ohead.tables(wb))
+
+
+def _head_case(seed, V, D, T, ties=False, exceptions=False):
+    from ai_b200 import wcomp
+    g = np.random.default_rng(seed)
+    w = (g.standard_normal((V, D)) * 0.02).astype(np.float32)
+    if ties:  # rows 17 and 9 identical and strongest: the smaller id must win
+        w[17] = w[9] = np.abs(w[9]) * 4
+    if exceptions:  # strongest row holds values far outside the exponent window (codec exceptions)
+        w[33] = np.abs(w[33]) * 4
+        w[33, ::97] = 1e-30
+        w[33, 5] = 3.0
+    wb = codec.f32_to_bf16_bits(w)
+    h = g.standard_normal((T, D)).astype(np.float32)
+    if ties or exceptions:
+        h = np.abs(h)
+    c = wcomp.compress(from_bits(wb))
+    return wb, h, c
+
+
+@pytest.mark.parametrize("T", [1, 3, 10])
+def test_head8_bounds_vs_oracle(lib, T):
+    """HI / LO of vocab_a_k against the float64 oracle, and the property the greedy pick relies on: every exact
+    logit lies at or below its HI, and the best exact logit at or above LO."""
+    from ai_b200.head import Head
+    wb, h, c = _head_case(100 + T, 4096, 512, T)
+    hd = Head(from_bits(wb), c)
+    H = torch.from_numpy(h).cuda()
+    HI, LO = hd.bounds(H, T)
+    torch.cuda.synchronize()
+    rhi, rlo = ohead.bounds(h, *ohead.tables(wb))
+    scale = (np.abs(ohead.tables(wb)[0]).astype(np.float64) @ np.abs(h).T.astype(np.float64)).T * \
+        ohead.tables(wb)[1][None].astype(np.float64)
+    np.testing.assert_allclose(HI.cpu().numpy(), rhi, rtol=0, atol=float(4e-6 * scale.max() + 1e-6))
+    np.testing.assert_allclose(LO.cpu().numpy(), rlo, rtol=0, atol=float(4e-6 * scale.max() + 1e-6))
+    ex = ohead.exact_logits(wb, h)
+    assert (ex <= HI.cpu().numpy()).all()
+    assert (ex.max(1) >= LO.cpu().numpy()).all()
+    assert status_clear() == 0
+
+
+def test_head8_bounds_golden(lib):
+    """HI / LO of the reference's fixture (3 rows of h, a 300 x 64 head), within fp32 accumulation order."""
+    from ai_b200._lib import ptr, stream_ptr
+    from ai_b200 import _lib
+    z = golden("head")
+    V, D = z["w"].shape
+    T = z["h"].shape[0]
+    Q, S, C1, C2, AM = _head_tables(z["w"])
+    h = torch.from_numpy(z["h"]).cuda()
+    HI = torch.empty(T, V, device="cuda")
+    LO = torch.empty(T, device="cuda")
+    ws = torch.zeros(lib.aib_head8_workspace(V, D, T), dtype=torch.uint8, device="cuda")
+    _lib.call("aib_head8_bounds", ptr(h), T, D, ptr(Q), ptr(S), ptr(C1), ptr(C2), ptr(AM), V, D, ptr(HI), V,
+              ptr(LO), ptr(ws), ws.numel(), stream_ptr())
+    torch.cuda.synchronize()
+    np.testing.assert_allclose(HI.cpu().numpy(), z["hi"], rtol=2e-6, atol=2e-5)
+    np.testing.assert_allclose(LO.cpu().numpy(), z["lo"], rtol=2e-6, atol=2e-5)
+
+
+@pytest.mark.parametrize("T,ties,exc", [(1, False, False), (3, False, False), (10, False, False), (2, True, False),
+                                        (1, False, True)])
+def test_head8_greedy_vs_oracle(lib, T, ties, exc):
+    """Greedy pick = argmax of the exact fp32 logits (head.py:19-26, sequential sum), smallest id on ties, with
+    the candidate rows decoded from the 12-bit codec (exceptions included); repeated calls agree."""
+    from ai_b200.head import Head
+    wb, h, c = _head_case(200 + T + 7 * ties + 11 * exc, 3000, 512, T, ties=ties, exceptions=exc)
+    hd = Head(from_bits(wb), c)
+    H = torch.from_numpy(h).cuda()
+    ex = ohead.exact_logits(wb, h)
+    want = [int(np.flatnonzero(ex[t] == ex[t].max()).min()) for t in range(T)]
+    for _ in range(2):
+        got = hd.pick(H, T).cpu().numpy().tolist()
+        assert got == want
+    if ties:
+        assert want[0] == 9 and want[1] == 9
+    if exc:
+        assert int(c["rp"][34] - c["rp"][33]) > 0 and want[0] == 33
+    assert status_clear() == 0
