@@ -100,8 +100,12 @@ struct BoundsArgs {
   int* ticket;
 };
 
-__global__ void __launch_bounds__(kThreads) bounds_kernel(BoundsArgs a) {
-  extern __shared__ __align__(16) float hs[];  // [T][nch * 512] permuted, then n1[T], n2[T]
+// TT: tokens handled per pass, rounded up to 1, 2, 4 or 8 (loops over t < a.T inside). Each warp walks its
+// rows as units of up to 8 chunks (one unit per row when D <= 4096) and keeps two units of loads in
+// flight: the next unit's loads are issued before the current unit's math.
+template <int TT>
+__global__ void __launch_bounds__(kThreads, 2) bounds_kernel(BoundsArgs a) {
+  extern __shared__ __align__(16) float hs[];  // [T][nch * 512] permuted, then n1[kTokPass], n2[kTokPass]
   __shared__ float wlo[kThreads / 32][kTokPass];
   __shared__ int last;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -129,61 +133,77 @@ __global__ void __launch_bounds__(kThreads) bounds_kernel(BoundsArgs a) {
   }
   __syncthreads();
   pdl_trigger();
-  float lo[kTokPass];
+  float lo[TT], acc[TT];
 #pragma unroll
-  for (int t = 0; t < kTokPass; ++t) lo[t] = -INFINITY;
+  for (int t = 0; t < TT; ++t) lo[t] = -INFINITY, acc[t] = 0.0f;
+  const int ngr = (nch + 7) >> 3;
   const long long nw = static_cast<long long>(gridDim.x) * (kThreads / 32);
-  for (long long v = static_cast<long long>(blockIdx.x) * (kThreads / 32) + warp; v < a.V; v += nw) {
-    const uint4* qrow = reinterpret_cast<const uint4*>(a.Q + v * D);
-    float acc[kTokPass];
+  long long v = static_cast<long long>(blockIdx.x) * (kThreads / 32) + warp;
+  int gi = 0;
+  auto load = [&](long long vv, int g, uint4 (&q)[8]) {
+    const uint4* qrow = reinterpret_cast<const uint4*>(a.Q + vv * D);
 #pragma unroll
-    for (int t = 0; t < kTokPass; ++t) acc[t] = 0.0f;
-    for (int c0 = 0; c0 < nch; c0 += 8) {
-      uint4 qv[8];
+    for (int k = 0; k < 8; ++k) {
+      const int c = g * 8 + k, col = c * kChunk + lane * 16;
+      q[k] = c < nch && col < D ? __ldg(qrow + (col >> 4)) : make_uint4(0u, 0u, 0u, 0u);  // zeros: q = 0
+    }
+  };
+  // math of unit (v, gi) from q, then the row epilogue after its last unit; false once the warp is done
+  auto step = [&](uint4 (&q)[8], uint4 (&qn)[8]) -> bool {
+    long long vn = v;
+    int gn = gi + 1;
+    if (gn == ngr) gn = 0, vn = v + nw;
+    if (vn < a.V) load(vn, gn, qn);
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {  // the whole group's loads in flight before any is used
-        const int col = (c0 + k) * kChunk + lane * 16;
-        qv[k] = c0 + k < nch && col < D ? __ldg(qrow + (col >> 4)) : make_uint4(0u, 0u, 0u, 0u);  // zeros: q = 0
-      }
+    for (int k = 0; k < 8; ++k) {
+      const int c = gi * 8 + k;
+      if (c < nch) {
+        const float* hb = hs + ((c * 4 * 32 + lane) << 2);
+        const uint32_t wd[4] = {q[k].x, q[k].y, q[k].z, q[k].w};
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        if (c0 + k >= nch) break;
-        float f[16];
-        i8x4(qv[k].x, f);
-        i8x4(qv[k].y, f + 4);
-        i8x4(qv[k].z, f + 8);
-        i8x4(qv[k].w, f + 12);
-        const float* hb = hs + (((c0 + k) * 4 * 32 + lane) << 2);
+        for (int j = 0; j < 4; ++j) {
+          float f[4];
+          i8x4(wd[j], f);
 #pragma unroll
-        for (int t = 0; t < kTokPass; ++t) {
-          if (t < T) {
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
+          for (int t = 0; t < TT; ++t) {
+            if (t < T) {
               const float4 x = *reinterpret_cast<const float4*>(hb + t * hstride + j * 128);
-              acc[t] = fmaf(f[4 * j], x.x, acc[t]);
-              acc[t] = fmaf(f[4 * j + 1], x.y, acc[t]);
-              acc[t] = fmaf(f[4 * j + 2], x.z, acc[t]);
-              acc[t] = fmaf(f[4 * j + 3], x.w, acc[t]);
+              acc[t] = fmaf(f[0], x.x, acc[t]);
+              acc[t] = fmaf(f[1], x.y, acc[t]);
+              acc[t] = fmaf(f[2], x.z, acc[t]);
+              acc[t] = fmaf(f[3], x.w, acc[t]);
             }
           }
         }
       }
     }
-    const float s = a.S[v], c1 = a.C1[v], c2 = a.C2[v], am = a.AM[v];
+    if (gi == ngr - 1) {  // row v complete
+      const float s = a.S[v], c1 = a.C1[v], c2 = a.C2[v], am = a.AM[v];
 #pragma unroll
-    for (int t = 0; t < kTokPass; ++t) {
-      if (t < T) {
-        const float dot = warp_sum(acc[t]);
-        const float av = s * dot;
-        const float b = fminf(c2 * n2s[t], c1 * n1s[t]) + kSlack * am * n1s[t];
-        if (lane == 0) a.HI[static_cast<size_t>(t) * a.ldhi + v] = av + b;
-        lo[t] = fmaxf(lo[t], av - b);
+      for (int t = 0; t < TT; ++t) {
+        if (t < T) {
+          const float dot = warp_sum(acc[t]);
+          const float av = s * dot;
+          const float b = fminf(c2 * n2s[t], c1 * n1s[t]) + kSlack * am * n1s[t];
+          if (lane == 0) a.HI[static_cast<size_t>(t) * a.ldhi + v] = av + b;
+          lo[t] = fmaxf(lo[t], av - b);
+        }
+        acc[t] = 0.0f;
       }
+    }
+    v = vn;
+    gi = gn;
+    return v < a.V;
+  };
+  uint4 qa[8], qb[8];
+  if (v < a.V) {
+    load(v, 0, qa);
+    while (step(qa, qb) && step(qb, qa)) {
     }
   }
   if (lane == 0)
 #pragma unroll
-    for (int t = 0; t < kTokPass; ++t) wlo[warp][t] = lo[t];
+    for (int t = 0; t < kTokPass; ++t) wlo[warp][t] = t < TT ? lo[t] : -INFINITY;
   __syncthreads();
   if (tid < T) {
     float m = -INFINITY;
@@ -216,51 +236,84 @@ AIB_DEV unsigned long long pick_key(float x, int v) {
   return (static_cast<unsigned long long>(u) << 32) | (0xFFFFFFFFu - static_cast<uint32_t>(v));
 }
 
+// Candidates (t, v) with HI[t, v] >= LO[t], appended as t << 24 | v.
+__global__ void __launch_bounds__(kThreads) cand_kernel(const float* __restrict__ HI, int ldhi,
+                                                        const float* __restrict__ LO, int T, int V, int* list,
+                                                        int* count) {
+  pdl_wait();
+  const long long i = static_cast<long long>(blockIdx.x) * kThreads + threadIdx.x;
+  if (i < static_cast<long long>(V) * T) {
+    const int t = static_cast<int>(i / V), v = static_cast<int>(i % V);
+    if (HI[static_cast<size_t>(t) * ldhi + v] >= LO[t]) list[atomicAdd(count, 1)] = (t << 24) | v;
+  }
+  pdl_trigger();
+}
+
+constexpr int kXWarps = 4;  // candidates in flight per CTA (each warp: the row's fp32 products in shared memory)
+
 struct GreedyArgs {
   const float* h;
-  int ldh, T;
+  int ldh;
   aib_c12 W;
-  const float* HI;
-  int ldhi;
-  const float* LO;
+  const int* list;
+  int* count;
+  int T;
   int64_t* out;
-  unsigned long long* best;  // [T], zero between calls
+  unsigned long long* best;  // [16], zero between calls
   int* ticket;
 };
 
-__global__ void __launch_bounds__(kThreads) greedy_kernel(GreedyArgs a) {
+// Exact logit of every listed candidate: the warp decodes row v from the codec planes (4 columns per lane
+// per step, exceptions patched from the CSR afterwards) into products w_d * h_d rounded to fp32, then lane 0
+// adds them in column order (head.py:19-26); atomicMax of the 64-bit key picks the winner. The last CTA
+// writes the ids and clears the keys and the candidate count.
+__global__ void __launch_bounds__(kXWarps * 32) exact_kernel(GreedyArgs a) {
+  extern __shared__ __align__(16) float prod[];  // [kXWarps][D]
   __shared__ int last;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, D = a.W.K;
   pdl_wait();
-  const int V = a.W.N, D = a.W.K;
-  const long long i = static_cast<long long>(blockIdx.x) * kThreads + threadIdx.x;
-  if (i < static_cast<long long>(V) * a.T) {
-    const int t = static_cast<int>(i / V), v = static_cast<int>(i % V);
-    if (a.HI[static_cast<size_t>(t) * a.ldhi + v] >= a.LO[t]) {
-      // exact logit: row v decoded (exceptions from the CSR in column order), products rounded to fp32,
-      // added in column order
-      const uint8_t* m8 = a.W.m8 + static_cast<size_t>(v) * D;
-      const uint8_t* e4 = a.W.e4 + static_cast<size_t>(v) * (D / 2);
-      const float* h = a.h + static_cast<size_t>(t) * a.ldh;
-      int ex = a.W.rp[v];
-      const int ex_end = a.W.rp[v + 1];
-      int ex_col = ex < ex_end ? a.W.ec[ex] : D;
-      const uint32_t base = static_cast<uint32_t>(a.W.base);
+  const int n = *a.count;
+  float* p = prod + warp * D;
+  const uint32_t base = static_cast<uint32_t>(a.W.base);
+  for (int i = blockIdx.x * kXWarps + warp; i < n; i += gridDim.x * kXWarps) {
+    const int e = a.list[i], t = e >> 24, v = e & 0xFFFFFF;
+    const uint8_t* m8 = a.W.m8 + static_cast<size_t>(v) * D;
+    const uint8_t* e4 = a.W.e4 + static_cast<size_t>(v) * (D / 2);
+    const float* h = a.h + static_cast<size_t>(t) * a.ldh;
+    for (int d0 = lane * 4; d0 < D; d0 += 128) {
+      const uint32_t mw = *reinterpret_cast<const uint32_t*>(m8 + d0);
+      const int i0 = d0 & 255;
+      const uint32_t ew = *reinterpret_cast<const uint32_t*>(e4 + (d0 >> 8) * 128 + (i0 & 127)) >> ((i0 & 128) ? 4 : 0);
+      const float4 x = *reinterpret_cast<const float4*>(h + d0);
+      const float xs[4] = {x.x, x.y, x.z, x.w};
+      float4 o;
+      float* op = &o.x;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const uint32_t m = (mw >> (8 * k)) & 0xFFu, code = (ew >> (8 * k)) & 15u;
+        const float w = __uint_as_float(((m & 0x80u) << 24) | (((code + base) & 0xFFu) << 23) | ((m & 0x7Fu) << 16));
+        op[k] = __fmul_rn(w, xs[k]);  // code-15 elements are replaced below
+      }
+      *reinterpret_cast<float4*>(p + d0) = o;
+    }
+    __syncwarp();
+    for (int q = a.W.rp[v] + lane; q < a.W.rp[v + 1]; q += 32) {
+      const int col = a.W.ec[q];
+      p[col] = __fmul_rn(a.W.ev[q], h[col]);
+    }
+    __syncwarp();
+    if (lane == 0) {
       float sum = 0.0f;
-      for (int d = 0; d < D; ++d) {
-        const uint32_t code = (e4[(d >> 8) * 128 + (d & 127)] >> ((d & 128) ? 4 : 0)) & 15u;
-        float w;
-        if (d == ex_col) {
-          w = a.W.ev[ex];
-          ++ex;
-          ex_col = ex < ex_end ? a.W.ec[ex] : D;
-        } else {
-          const uint32_t m = m8[d];
-          w = __uint_as_float(((m & 0x80u) << 24) | (((code + base) & 0xFFu) << 23) | ((m & 0x7Fu) << 16));
-        }
-        sum = __fadd_rn(sum, __fmul_rn(w, h[d]));
+      for (int d = 0; d < D; d += 4) {
+        const float4 y = *reinterpret_cast<const float4*>(p + d);
+        sum = __fadd_rn(sum, y.x);
+        sum = __fadd_rn(sum, y.y);
+        sum = __fadd_rn(sum, y.z);
+        sum = __fadd_rn(sum, y.w);
       }
       atomicMax(a.best + t, pick_key(sum, v));
     }
+    __syncwarp();  // the products are rewritten by the next candidate
   }
   __threadfence();
   __syncthreads();
@@ -268,22 +321,41 @@ __global__ void __launch_bounds__(kThreads) greedy_kernel(GreedyArgs a) {
   __syncthreads();
   if (last) {
     __threadfence();
-    for (int t = threadIdx.x; t < a.T; t += kThreads) {
+    for (int t = threadIdx.x; t < a.T; t += kXWarps * 32) {
       const unsigned long long k = atomicExch(a.best + t, 0ull);
       a.out[t] = k ? static_cast<int64_t>(0xFFFFFFFFu - static_cast<uint32_t>(k & 0xFFFFFFFFull)) : -1;
     }
-    if (threadIdx.x == 0) *a.ticket = 0;
+    if (threadIdx.x == 0) {
+      *a.count = 0;
+      *a.ticket = 0;
+    }
   }
   pdl_trigger();
 }
 
-static int bounds_grid(size_t smem) {
+template <typename K>
+static int resident_grid(K kernel, int threads, size_t smem, int cap) {
   int per = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, bounds_kernel, kThreads, smem) != cudaSuccess) {
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, kernel, threads, smem) != cudaSuccess) {
     cudaGetLastError();
     per = 1;
   }
-  return std::max(1, std::min(kMaxGrid, sm_count() * std::max(1, std::min(per, 4))));
+  return std::max(1, std::min(kMaxGrid, sm_count() * std::max(1, std::min(per, cap))));
+}
+
+// Workspace layout: [0, 256) bounds ticket; CTA maxima [kTokPass][kMaxGrid] floats; greedy block of 256
+// bytes (ticket, candidate count); keys [16] u64; candidate list [16][V] ints.
+constexpr size_t kPartOff = 256;
+constexpr size_t kGreedyOff = kPartOff + static_cast<size_t>(kTokPass) * kMaxGrid * sizeof(float);
+constexpr size_t kBestOff = kGreedyOff + 256;
+constexpr size_t kListOff = kBestOff + 16 * 8;
+
+template <int TT>
+static int launch_bounds_tt(const BoundsArgs& a, size_t smem, cudaStream_t s) {
+  const int rc = allow_smem(bounds_kernel<TT>, smem);
+  if (rc) return rc;
+  const int grid = resident_grid(bounds_kernel<TT>, kThreads, smem, 4);
+  return launch(bounds_kernel<TT>, dim3(grid), dim3(kThreads), smem, s, "aib_head8_bounds", a);
 }
 
 }  // namespace head8
@@ -304,18 +376,17 @@ int aib_head8_tables(const uint16_t* w, int V, int D, int8_t* Q, float* S, float
 }
 
 size_t aib_head8_workspace(int V, int D, int T) {
-  (void)V;
   (void)D;
   (void)T;
-  // bounds: ticket + CTA maxima [kTokPass][kMaxGrid]; greedy: ticket + keys [16]
-  return 256 + static_cast<size_t>(head8::kTokPass) * head8::kMaxGrid * sizeof(float) + 256 + 16 * 8;
+  if (V <= 0) return 0;
+  return head8::kListOff + static_cast<size_t>(16) * V * sizeof(int);
 }
 
 int aib_head8_bounds(const float* h, int T, int ldh, const int8_t* Q, const float* S, const float* C1,
                      const float* C2, const float* AM, int V, int D, float* HI, int ldhi, float* LO, void* ws,
                      size_t ws_bytes, void* stream) {
   if (!h || !Q || !S || !C1 || !C2 || !AM || !HI || !LO || V <= 0 || D <= 0 || T < 1 || T > 16 || ldh < D ||
-      ldhi < V)
+      ldhi < V || V >= (1 << 24))
     return fail(AIB_EINVAL, "aib_head8_bounds: bad arguments");
   if (D % 16 || (reinterpret_cast<uintptr_t>(Q) & 15))
     return fail(AIB_EINVAL, "aib_head8_bounds: D must be a multiple of 16 and Q 16-byte aligned (D=%d)", D);
@@ -327,13 +398,13 @@ int aib_head8_bounds(const float* h, int T, int ldh, const int8_t* Q, const floa
   for (int t0 = 0; t0 < T; t0 += head8::kTokPass) {
     const int tt = std::min(head8::kTokPass, T - t0);
     const size_t smem = (static_cast<size_t>(tt) * nch * head8::kChunk + 2 * head8::kTokPass) * sizeof(float);
-    int rc = allow_smem(head8::bounds_kernel, smem);
-    if (rc) return rc;
-    const int grid = head8::bounds_grid(smem);
     head8::BoundsArgs a{h + static_cast<size_t>(t0) * ldh, ldh, tt, Q, S, C1, C2, AM, V, D, nch,
                         HI + static_cast<size_t>(t0) * ldhi, ldhi, LO + t0,
-                        reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + 256), static_cast<int*>(ws)};
-    rc = launch(head8::bounds_kernel, dim3(grid), dim3(head8::kThreads), smem, s, "aib_head8_bounds", a);
+                        reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + head8::kPartOff), static_cast<int*>(ws)};
+    const int rc = tt == 1   ? head8::launch_bounds_tt<1>(a, smem, s)
+                   : tt == 2 ? head8::launch_bounds_tt<2>(a, smem, s)
+                   : tt <= 4 ? head8::launch_bounds_tt<4>(a, smem, s)
+                             : head8::launch_bounds_tt<8>(a, smem, s);
     if (rc) return rc;
   }
   return AIB_OK;
@@ -342,18 +413,30 @@ int aib_head8_bounds(const float* h, int T, int ldh, const int8_t* Q, const floa
 int aib_head8_greedy(const float* h, int T, int ldh, const aib_c12* W, const float* HI, int ldhi, const float* LO,
                      int64_t* out, void* ws, size_t ws_bytes, void* stream) {
   if (!h || !W || !W->m8 || !W->e4 || !W->rp || (W->n_exc > 0 && (!W->ec || !W->ev)) || !HI || !LO || !out ||
-      T < 1 || T > 16 || W->N <= 0 || W->K <= 0 || W->K % 256 || ldh < W->K || ldhi < W->N)
+      T < 1 || T > 16 || W->N <= 0 || W->K <= 0 || W->K % 256 || ldh < W->K || ldhi < W->N || W->N >= (1 << 24))
     return fail(AIB_EINVAL, "aib_head8_greedy: bad arguments");
+  if ((ldh & 3) || (reinterpret_cast<uintptr_t>(h) & 15) || (reinterpret_cast<uintptr_t>(W->m8) & 15) ||
+      (reinterpret_cast<uintptr_t>(W->e4) & 15))
+    return fail(AIB_EINVAL, "aib_head8_greedy: h rows, m8 and e4 must be 16-byte aligned");
   if (!ws || ws_bytes < aib_head8_workspace(W->N, W->K, T) || (reinterpret_cast<uintptr_t>(ws) & 15))
     return fail(AIB_EWORKSPACE, "aib_head8_greedy: workspace %zu < %zu bytes", ws_bytes,
                 aib_head8_workspace(W->N, W->K, T));
-  uint8_t* g = static_cast<uint8_t*>(ws) + 256 + static_cast<size_t>(head8::kTokPass) * head8::kMaxGrid * sizeof(float);
-  head8::GreedyArgs a{h, ldh, T, *W, HI, ldhi, LO, out, reinterpret_cast<unsigned long long*>(g + 256),
-                      reinterpret_cast<int*>(g)};
+  const size_t smem = static_cast<size_t>(head8::kXWarps) * W->K * sizeof(float);
+  int rc = allow_smem(head8::exact_kernel, smem);
+  if (rc) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint8_t* w8 = static_cast<uint8_t*>(ws);
+  int* ticket = reinterpret_cast<int*>(w8 + head8::kGreedyOff);
+  int* count = ticket + 1;
+  int* list = reinterpret_cast<int*>(w8 + head8::kListOff);
   const long long n = static_cast<long long>(W->N) * T;
-  const int grid = static_cast<int>((n + head8::kThreads - 1) / head8::kThreads);
-  return launch(head8::greedy_kernel, dim3(grid), dim3(head8::kThreads), 0, static_cast<cudaStream_t>(stream),
-                "aib_head8_greedy", a);
+  rc = launch(head8::cand_kernel, dim3(static_cast<int>((n + head8::kThreads - 1) / head8::kThreads)),
+              dim3(head8::kThreads), 0, s, "aib_head8_greedy (candidates)", HI, ldhi, LO, T, W->N, list, count);
+  if (rc) return rc;
+  head8::GreedyArgs a{h, ldh, *W, list, count, T, out,
+                      reinterpret_cast<unsigned long long*>(w8 + head8::kBestOff), ticket};
+  const int grid = head8::resident_grid(head8::exact_kernel, head8::kXWarps * 32, smem, 4);
+  return launch(head8::exact_kernel, dim3(grid), dim3(head8::kXWarps * 32), smem, s, "aib_head8_greedy", a);
 }
 
 }  // extern "C"

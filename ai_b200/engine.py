@@ -23,6 +23,7 @@ import time
 import numpy as np
 import torch
 
+from .head import Head as Head8
 from . import _lib, wcomp, tkernels, sampler
 from ._lib import ptr, stream_ptr
 from .model import CONFIGS, Ckpt, RandomWeights, Qwen3Config
@@ -33,9 +34,11 @@ MAXB = 16
 
 class Engine:
     def __init__(self, name, maxt=2048, device="cuda", seed=0, log=print, norm_noise=0.0, weights=None,
-                 graphs=True):
+                 graphs=True, head8=True):
         """name: an HF Qwen3 folder, or a key of ai_b200.model.CONFIGS / a Qwen3Config for random-init
-        weights (N(0, 0.02) matrices, seed `seed`). weights: an explicit weight source (RandomWeights/Ckpt)."""
+        weights (N(0, 0.02) matrices, seed `seed`). weights: an explicit weight source (RandomWeights/Ckpt).
+        head8: greedy steps without penalties pick through the int8 head (the reference's Head: bounds over an
+        int8 copy, exact fp32 logits of the candidates) instead of the full 12-bit head GEMV + sampler."""
         if not isinstance(maxt, int) or isinstance(maxt, bool) or maxt < 1:
             raise ValueError("maxt must be a positive integer")
         t0 = time.time()
@@ -74,7 +77,10 @@ class Engine:
             self.small.append({k: lw[k].to(dev).contiguous() for k in ("ln1", "ln2", "qn", "kn")})
             del lw
         self.emb = src.embedding().to(dev).contiguous()
-        self.head = wcomp.compress(self.emb if cfg.tied else src.head().to(dev))
+        hw = self.emb if cfg.tied else src.head().to(dev)
+        self.head = wcomp.compress(hw)
+        self.head8 = Head8(hw, self.head, TM=MAXB) if head8 else None
+        del hw
         self.norm = src.final_norm().to(dev).contiguous()
         torch.cuda.synchronize()
         # ---- KV cache (bf16) and work buffers
@@ -153,10 +159,16 @@ class Engine:
         """Everything that runs on the device for one pass of T tokens (graph body)."""
         tkernels.embed(self.emb, self.ids[:T], self.xb[:T])
         self._layers(T)
-        self._head(T)
         r0 = T - rows
-        sampler.sample_into(self.logits[r0:T], self.out_ids[r0:T], prm, self.u[:rows] if prm.temperature > 0 else None,
-                            self.prior if penal else None, None, B=rows, ws=self.sample_ws)
+        if self.head8 is not None and prm.temperature <= 0 and not penal:
+            # greedy: final norm, int8 bounds, exact logits of the candidate rows (Head.pick, head.py:59-88)
+            tkernels.rmsg(self.xb[r0:T], self.norm, self.hb[r0:T], self.eps)
+            self.head8.pick(self.hb[r0:T], rows, out=self.out_ids[r0:T])
+        else:
+            self._head(T)
+            sampler.sample_into(self.logits[r0:T], self.out_ids[r0:T], prm,
+                                self.u[:rows] if prm.temperature > 0 else None, self.prior if penal else None, None,
+                                B=rows, ws=self.sample_ws)
         _lib.call("aib_step_advance", ptr(self.pos), ptr(self.ids), ptr(self.out_ids), T,
                   ptr(self.prior) if penal else None, sampler.PMAX if penal else 0, stream_ptr())
 

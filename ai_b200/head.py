@@ -56,13 +56,17 @@ class Head:
                   stream_ptr())
         return self.HI[:T], self.LO[:T]
 
-    def pick(self, h, T, temperature=0.0, run_bounds=True):
-        """Greedy ids for rows h[:T] (int64 device tensor view of length T)."""
+    def pick(self, h, T, temperature=0.0, run_bounds=True, out=None):
+        """Greedy ids for rows h[:T]: an int64 device tensor of length T (`out` if given, else a view of an
+        internal buffer)."""
         if temperature > 0:
             raise NotImplementedError("Head.pick samples only greedily; use ai_b200.sampler for temperature > 0")
         h = self._h(h, T)
         if run_bounds:
             self.bounds(h, T)
+        if out is not None and (out.dtype != torch.int64 or out.numel() < T or not out.is_contiguous()):
+            raise ValueError("Head.pick: out must be a contiguous int64 tensor of >= T elements")
+        dst = self.out if out is None else out
         _lib.call("aib_head8_greedy", ptr(h), T, h.stride(0), C.byref(self._desc), ptr(self.HI), self.V, ptr(self.LO),
-                  ptr(self.out), ptr(self.ws), self.ws.numel(), stream_ptr())
-        return self.out[:T]
+                  ptr(dst), ptr(self.ws), self.ws.numel(), stream_ptr())
+        return dst[:T]

@@ -271,6 +271,22 @@ def micro_attn(args):
     return run, nbytes
 
 
+def micro_head8(args):
+    """Greedy pick through the int8 head at the Qwen3-8B vocabulary size (151936 x 4096): int8 bounds over the
+    622 MB copy, then exact logits of the candidate rows from the 12-bit head. Returns (bounds-only, full pick)
+    callables and the int8 bytes of one bounds pass."""
+    import torch
+    from ai_b200 import wcomp
+    from ai_b200.head import Head
+    g = torch.Generator(device="cuda").manual_seed(0)
+    V, D = 151936, 4096
+    w = (torch.randn(V, D, generator=g, device="cuda") * 0.02).bfloat16()
+    hd = Head(w, wcomp.compress(w), TM=1)
+    del w
+    h = torch.randn(1, D, generator=g, device="cuda")
+    return (lambda: hd.bounds(h, 1)), (lambda: hd.pick(h, 1)), V * D + 16 * V
+
+
 def micro_sample(args):
     """Sampler on one [1, 151936] fp32 logits row, top-k 20 / top-p 0.8 / T 0.6."""
     import torch
@@ -319,6 +335,14 @@ def micro(args):
         torch.cuda.synchronize()
         return e0.elapsed_time(e1) * 1e3 / reps
 
+    if args.micro == "head8":
+        bnd, pick, nbytes = micro_head8(args)
+        ub = timed(bnd, max(args.steps, 1))
+        up = timed(pick, max(args.steps, 1))
+        print(json.dumps({"micro": "head8", "bytes": nbytes, "bounds_us": round(ub, 2),
+                          "bounds_GBps": round(nbytes / ub / 1e3, 1), "pick_us": round(up, 2),
+                          "device_status": _lib.status()}))
+        return
     if args.micro in ("attn", "sample"):
         run, nbytes = (micro_attn if args.micro == "attn" else micro_sample)(args)
         us = timed(run, max(args.steps, 1))
@@ -345,7 +369,8 @@ def micro(args):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--micro", choices=["gemv", "gemv_down", "gemv_qkv", "gemv_o", "attn", "sample"], default=None,
+    ap.add_argument("--micro", choices=["gemv", "gemv_down", "gemv_qkv", "gemv_o", "attn", "sample", "head8"],
+                    default=None,
                     help="time one kernel alone on a small case (for ncu) instead of the decode benchmark")
     ap.add_argument("--gemv-variant", type=int, default=None, choices=[0, 1, 2, 3],
                     help="codec GEMV kernel for --micro: 0 tensor-core 24 KB stages, 1 CUDA-core 12 KB stages, 2 CUDA-core 48 KB stages, 3 tensor-core 48 KB stages (default)")
