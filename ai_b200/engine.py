@@ -26,7 +26,7 @@ import torch
 from .head import Head as Head8
 from . import _lib, wcomp, tkernels, sampler
 from ._lib import ptr, stream_ptr
-from .model import CONFIGS, Ckpt, RandomWeights, Qwen3Config
+from .model import CONFIGS, Ckpt, RandomWeights, Qwen3Config, check_tp, shard_layer
 
 MATS = ("qkv", "o", "gu", "down")
 MAXB = 16
@@ -34,11 +34,16 @@ MAXB = 16
 
 class Engine:
     def __init__(self, name, maxt=2048, device="cuda", seed=0, log=print, norm_noise=0.0, weights=None,
-                 graphs=True, head8=True):
+                 graphs=True, head8=True, tp=1):
         """name: an HF Qwen3 folder, or a key of ai_b200.model.CONFIGS / a Qwen3Config for random-init
         weights (N(0, 0.02) matrices, seed `seed`). weights: an explicit weight source (RandomWeights/Ckpt).
         head8: greedy steps without penalties pick through the int8 head (the reference's Head: bounds over an
-        int8 copy, exact fp32 logits of the candidates) instead of the full 12-bit head GEMV + sampler."""
+        int8 copy, exact fp32 logits of the candidates) instead of the full 12-bit head GEMV + sampler.
+        tp: tensor-parallel ranks (> 1 needs an initialised torch.distributed group of that size, one rank per
+        GPU, every rank making the same calls): each rank holds its KV groups' share of every layer
+        (`model.shard_layer`), and one all-reduce after o_proj and after down_proj sums the ranks' partial
+        residual updates. Embedding, final norm, head and sampler are replicated: every rank picks the same
+        token from the same all-reduced state."""
         if not isinstance(maxt, int) or isinstance(maxt, bool) or maxt < 1:
             raise ValueError("maxt must be a positive integer")
         t0 = time.time()
@@ -59,7 +64,16 @@ class Engine:
             src = Ckpt(name)
             cfg = src.config
         self.cfg = cfg
-        self.L, self.D, self.H, self.KV, self.HD, self.FF, self.V = cfg.L, cfg.D, cfg.H, cfg.KV, cfg.HD, cfg.FF, cfg.V
+        self.tp, self.tp_rank = int(tp), 0
+        if self.tp > 1:
+            import torch.distributed as dist
+            if not dist.is_initialized() or dist.get_world_size() != self.tp:
+                raise ValueError("tp > 1 needs an initialised torch.distributed group of that size")
+            check_tp(cfg, self.tp)
+            self.tp_rank = dist.get_rank()
+        # per-rank shapes (the whole model when tp == 1)
+        self.L, self.D, self.HD, self.V = cfg.L, cfg.D, cfg.HD, cfg.V
+        self.H, self.KV, self.FF = cfg.H // self.tp, cfg.KV // self.tp, cfg.FF // self.tp
         self.eps, self.maxt, self.log = cfg.eps, maxt, log
         self.eos = set(cfg.eos)
         dev = self.device
@@ -71,6 +85,8 @@ class Engine:
         self.W, self.small = [], []
         for i in range(self.L):
             lw = src.layer(i)
+            if self.tp > 1:
+                lw = shard_layer(lw, cfg, self.tp_rank, self.tp)
             if self.gated:
                 lw["gu"] = wcomp.interleave_gate_up(lw["gu"])
             self.W.append({n: wcomp.compress(lw[n].to(dev)) for n in MATS})
@@ -114,6 +130,17 @@ class Engine:
         self.graphs.clear()
 
     # ------------------------------------------------------------------------------------ step body
+    @property
+    def _add(self):
+        """GEMV mode of the residual updates: add into x (1) on rank 0 (and without tensor parallelism); the
+        other ranks write their partial (0) and the all-reduce sums x + every rank's partial."""
+        return 1 if self.tp_rank == 0 else 0
+
+    def _reduce(self, x):
+        if self.tp > 1:
+            import torch.distributed as dist
+            dist.all_reduce(x)
+
     def _layers(self, T):
         H, KV, HD = self.H, self.KV, self.HD
         for l in range(self.L):
@@ -124,13 +151,17 @@ class Engine:
                 wcomp.gemvc1(x, W["qkv"], self.qkvb[0], 0, lnw=s["ln1"], eps=self.eps)
                 tkernels.rope_attn(self.qkvb[0], s["qn"], s["kn"], self.inv, self.pos, kc, vc, self.attb[0], self.maxt,
                                    self.eps, self.scale, H, KV, HD, ws=self.ws)
-                wcomp.gemvc1(self.attb[0], W["o"], x, 1)
+                wcomp.gemvc1(self.attb[0], W["o"], x, self._add)
+                self._reduce(self.xb[:1])
                 if self.gated:
                     wcomp.gemvc1(x, W["gu"], self.gub[0], 3, lnw=s["ln2"], eps=self.eps)
-                    wcomp.gemvc1(self.gub[0], W["down"], x, 1)
+                    wcomp.gemvc1(self.gub[0], W["down"], x, self._add)
                 else:
                     wcomp.gemvc1(x, W["gu"], self.gub[0], 0, lnw=s["ln2"], eps=self.eps)
+                    if not self._add:
+                        x.zero_()
                     wcomp.gemvc1(self.gub[0], W["down"], x, 2)
+                self._reduce(self.xb[:1])
             else:
                 x, h = self.xb[:T], self.hb[:T]
                 tkernels.rmsg(x, s["ln1"], h, self.eps)
@@ -139,14 +170,18 @@ class Engine:
                                        self.maxt, self.eps, H, KV, HD, T)
                 tkernels.attn(self.qb[:T], kc, vc, self.pos, self.attb[:T], self.maxt, self.scale, H, KV, HD, T,
                               ws=self.ws)
-                wcomp.gemvc_tc(self.attb[:T], W["o"], x, 1, T)
+                wcomp.gemvc_tc(self.attb[:T], W["o"], x, self._add, T)
+                self._reduce(x)
                 tkernels.rmsg(x, s["ln2"], h, self.eps)
                 if self.gated:
                     wcomp.gemvc_tc(h, W["gu"], self.gub[:T], 3, T)
-                    wcomp.gemvc_tc(self.gub[:T], W["down"], x, 1, T)
+                    wcomp.gemvc_tc(self.gub[:T], W["down"], x, self._add, T)
                 else:
                     wcomp.gemvc_tc(h, W["gu"], self.gub[:T], 0, T)
+                    if not self._add:
+                        x.zero_()
                     wcomp.gemvc_tc(self.gub[:T], W["down"], x, 2, T)
+                self._reduce(x)
 
     def _head(self, T):
         if T == 1:

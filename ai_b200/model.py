@@ -205,6 +205,32 @@ class Ckpt:
         return self.t("model.norm.weight")
 
 
+def check_tp(cfg: Qwen3Config, n):
+    """Raise ValueError unless the layer matrices split into n tensor-parallel shards: whole KV groups (and
+    their query heads) per rank and an MLP slice that the codec can encode (a multiple of 256 columns)."""
+    if n < 1 or cfg.KV % n or cfg.H % n or cfg.FF % n or (cfg.FF // n) % 256:
+        raise ValueError(f"{cfg.name}: cannot split H={cfg.H}, KV={cfg.KV}, FF={cfg.FF} over {n} ranks")
+
+
+def shard_layer(lw, cfg: Qwen3Config, rank, n):
+    """Rank `rank` of n tensor-parallel shards of one layer's fused matrices (the split of the Megatron-style
+    decode layer: qkv by KV group, o by the matching input columns, gate/up by MLP rows, down by the matching
+    input columns). qkv keeps the [q; k; v] order with the rank's heads only; gu keeps [gate; up] with the
+    rank's MLP rows. The small tensors (norm weights) are shared. Concatenating the shards along the split
+    dimensions gives back the full matrices."""
+    check_tp(cfg, n)
+    H, KV, HD, FF = cfg.H, cfg.KV, cfg.HD, cfg.FF
+    hq, hk, fr = H // n * HD, KV // n * HD, FF // n
+    q, k, v = torch.split(lw["qkv"], [H * HD, KV * HD, KV * HD])
+    g, u = torch.split(lw["gu"], [FF, FF])
+    out = dict(lw)
+    out["qkv"] = torch.cat([q[rank * hq:(rank + 1) * hq], k[rank * hk:(rank + 1) * hk], v[rank * hk:(rank + 1) * hk]])
+    out["o"] = lw["o"][:, rank * hq:(rank + 1) * hq].contiguous()
+    out["gu"] = torch.cat([g[rank * fr:(rank + 1) * fr], u[rank * fr:(rank + 1) * fr]])
+    out["down"] = lw["down"][:, rank * fr:(rank + 1) * fr].contiguous()
+    return out
+
+
 def save_checkpoint(path, cfg: Qwen3Config, weights: RandomWeights):
     """Write a random-init model as an HF folder (config.json + model.safetensors), unfused tensors."""
     os.makedirs(path, exist_ok=True)

@@ -172,14 +172,17 @@ def gpu_arm(args, rank, world):
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
     torch.cuda.set_device(dev)
     maxt = CTX + 2 * (args.steps + args.warmup) + 64
-    eng = Engine("qwen3-8b", maxt=maxt, seed=rank, log=None)
+    tp = world if args.tp else 1
+    # replicas: one sequence per GPU (own weights seed); tensor parallel: one sequence over all ranks
+    seq = 0 if tp > 1 else rank
+    eng = Engine("qwen3-8b", maxt=maxt, seed=seq, log=None, tp=tp)
     g = torch.Generator(device=dev).manual_seed(1234 + rank)
     eng.kv[:, :, :, :CTX].normal_(generator=g)
     torch.cuda.synchronize()
     from ai_b200 import sampler
     import numpy as np
     prm = sampler.params(**SAMPLING)
-    rng = np.random.default_rng(rank)
+    rng = np.random.default_rng(seq)
     eng.u.copy_(torch.from_numpy(rng.random(16)))
     eng.ids[0] = 1
     eng.pos.fill_(CTX)
@@ -205,41 +208,46 @@ def gpu_arm(args, rank, world):
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_max = float(t.item())
-    value = world * args.steps / (ms_max / 1e3)
+    nseq = 1 if tp > 1 else world  # sequences decoded by the whole job
+    value = nseq * args.steps / (ms_max / 1e3)
     # e2e through the public API: Engine.generate, host buffers every step
     eng.ctx = [1] * CTX
     prompt = eng.ctx + [1]
     stats = {}
     with Clocks(dev.index) as ck2:
         n = 0
-        for _ in eng.generate(prompt, max_new=args.steps + 1, seed=rank, stats=stats, **SAMPLING):
+        for _ in eng.generate(prompt, max_new=args.steps + 1, seed=seq, stats=stats, **SAMPLING):
             n += 1
     e2e_local = stats["decode_n"] / (stats["gen_ms"] / 1e3)
     te = torch.tensor([stats["gen_ms"]], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    e2e = world * stats["decode_n"] / (float(te.item()) / 1e3)
+    e2e = nseq * stats["decode_n"] / (float(te.item()) / 1e3)
     peak = peaks()
     roof = gemv_roofline(eng, peak) if rank == 0 else None
     step_bytes = eng.bytes_per_token(CTX + args.steps // 2)
     from ai_b200._lib import status
     dev_status = status()
+    if tp > 1:
+        eng.close()  # its graphs hold NCCL calls: release them before the process group goes
     if rank != 0:
         return None
     launches_per_step = 1 + 5 * eng.L + 1 + 1 + 1
     out = {
         "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "fp32 activations x exact bf16 weights (12-bit codec), "
+        "scaling": "strong" if tp > 1 else "weak", "vs_baseline": None, "dtype": "fp32 activations x exact bf16 weights (12-bit codec), "
         "bf16 KV", "data": "synthetic (random-init N(0,0.02) weights, KV pre-filled N(0,1) to 4096)",
         "config": {"workload": "Qwen3-8B decode bs1, 12-bit weights, ctx 4096->, top-k 20 / top-p 0.8 / T 0.6",
-                   "model": "qwen3-8b", "global_batch": world, "seq_len": CTX,
-                   "parallelism": "replicas" if world > 1 else "single", "l2": "weights (10.4 GB) > L2 every step"},
+                   "model": "qwen3-8b", "global_batch": nseq, "seq_len": CTX,
+                   "parallelism": f"tp{tp}" if tp > 1 else ("replicas" if world > 1 else "single"),
+                   "l2": "weights (10.4 GB) > L2 every step"},
         "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 8,
                 "per_rank": round(e2e_local, 2)},
         "roofline": roof,
-        "step_roofline": {"bytes_per_token": step_bytes, "achieved_gbs": round(step_bytes * value / world / 1e9, 1),
-                          "frac": round(step_bytes * value / world / 1e9 / peak[0], 4)},
+        "step_roofline": {"bytes_per_token": step_bytes, "per": "rank",
+                          "achieved_gbs": round(step_bytes * value / nseq / 1e9, 1),
+                          "frac": round(step_bytes * value / nseq / 1e9 / peak[0], 4)},
         "gpu_launches": launches_per_step * args.steps,
         "clocks": ck.summary(), "clocks_e2e": ck2.summary(), "device_status": dev_status,
     }
@@ -375,6 +383,8 @@ def main():
     ap.add_argument("--gemv-variant", type=int, default=None, choices=[0, 1, 2, 3],
                     help="codec GEMV kernel for --micro: 0 tensor-core 24 KB stages, 1 CUDA-core 12 KB stages, 2 CUDA-core 48 KB stages, 3 tensor-core 48 KB stages (default)")
     ap.add_argument("--streamk", action="store_true", help="--micro gemv*: pass the stream-K workspace")
+    ap.add_argument("--tp", action="store_true",
+                    help="with --gpus N under torchrun: one sequence, tensor parallel over the N ranks (default: N replicas)")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=256)
     ap.add_argument("--warmup", type=int, default=8)
