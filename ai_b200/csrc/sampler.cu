@@ -722,19 +722,28 @@ __global__ void __launch_bounds__(kThreads)
         __syncthreads();
       }
   }
-  // softmax denominator: over the kept top-k set (sorted order), or over the whole row from the slices
+  // softmax denominator: over the kept top-k set (sorted order), or over the whole row from the slices.
+  // The exponentials are evaluated in parallel (ep: candidates in sorted order, zt: slice terms); one thread
+  // then adds them in a fixed order.
+  double* ep = cp + 256;  // nc <= 256
+  double* zt = cp + 512;  // ns <= kMaxSlices
+  for (int i = tid; i < nc; i += kThreads) ep[i] = exp(static_cast<double>(key_value(ckey[i])) / Td - Mz);
+  if (!has_k)
+    for (int s2 = tid; s2 < ns; s2 += kThreads)
+      zt[s2] = spart[s2].max != -INFINITY ? spart[s2].zsum * exp(spart[s2].zmax - Mz) : 0.0;
+  __syncthreads();
   if (tid == 0) {
     double Z = 0.0;
     if (has_k) {
-      for (int i = 0; i < nc; ++i) Z += exp(static_cast<double>(key_value(ckey[i])) / Td - Mz);
+      for (int i = 0; i < nc; ++i) Z += ep[i];
     } else {
       for (int s2 = 0; s2 < ns; ++s2)
-        if (spart[s2].max != -INFINITY) Z += spart[s2].zsum * exp(spart[s2].zmax - Mz);
+        if (spart[s2].max != -INFINITY) Z += zt[s2];
     }
     // probabilities and their exclusive prefix sums in sorted order (fixed order)
     double run = 0.0;
     for (int i = 0; i < nc; ++i) {
-      const double pi = exp(static_cast<double>(key_value(ckey[i])) / Td - Mz) / Z;
+      const double pi = ep[i] / Z;
       cp[i] = run;
       run += pi;
     }
@@ -755,7 +764,7 @@ __global__ void __launch_bounds__(kThreads)
     int keep = 0;  // keep while exclusive cumsum < top_p
     for (int i = 0; i < nc; ++i) keep += (top_p >= 1.0 || cp[i] < top_p) ? 1 : 0;
     keep = max(1, min(keep, nc));
-    const double pl = exp(static_cast<double>(key_value(ckey[keep - 1])) / Td - Mz) / Z;
+    const double pl = ep[keep - 1] / Z;
     const double S = cp[keep - 1] + pl;
     const double u = us ? us[b] : 0.5;
     int cntle = 0;  // index = #(cdf_i <= u)
