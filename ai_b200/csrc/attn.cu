@@ -35,16 +35,15 @@ constexpr int GMAX = 8;
 constexpr int kBlk = 32;  // positions per warp block (lane = position)
 constexpr int kMaxSplits = 32;
 
-// Per-warp K/V slot: kBlk K rows at a padded stride (HD + 8 bf16: consecutive rows start 16 bytes apart
-// modulo 128, so eight lanes reading the same 16-byte chunk of eight rows hit eight different bank groups)
-// followed by kBlk V rows at the plain stride (a V row is read by the whole warp at once).
+// Per-warp K/V slot: kBlk K rows then kBlk V rows, each at a padded stride (HD + 8 bf16: consecutive rows
+// start 16 bytes apart modulo 128, so the 8 row addresses of an ldmatrix hit 8 different bank groups).
 template <int HD>
 __host__ __device__ constexpr int k_stride() {
   return (HD + 8) * 2;
 }
 template <int HD>
 __host__ __device__ constexpr size_t slot_bytes() {
-  return static_cast<size_t>(kBlk) * (k_stride<HD>() + HD * 2);
+  return static_cast<size_t>(kBlk) * 2 * k_stride<HD>();  // K rows, then V rows, both padded
 }
 __host__ __device__ constexpr size_t cmax(size_t a, size_t b) { return a > b ? a : b; }
 // Dynamic shared memory: the warps' K/V slots; afterwards reused for the warps' final states
@@ -98,7 +97,7 @@ AIB_DEV void attend_start(uint8_t* ring, const uint16_t* kc, const uint16_t* vc,
   const int cnt = min(kBlk, w1 - w0);
   if (cnt > 0) copy_rows<HD, k_stride<HD>()>(kslot, kc + static_cast<size_t>(w0) * HD, cnt);
   cp_commit();
-  if (cnt > 0) copy_rows<HD, HD * 2>(kslot + kBlk * k_stride<HD>(), vc + static_cast<size_t>(w0) * HD, cnt);
+  if (cnt > 0) copy_rows<HD, k_stride<HD>()>(kslot + kBlk * k_stride<HD>(), vc + static_cast<size_t>(w0) * HD, cnt);
   cp_commit();
 }
 
@@ -150,150 +149,201 @@ AIB_DEV void norm_rope(const float* v, const uint16_t* w, const float* cs, const
   }
 }
 
-// Attention of the G query heads in sm.q over cache rows [j0, j1) of one group. Warp w takes a contiguous
-// slice of the range, 32 positions per block, lane = position, with the block's rows in the warp's slot
-// (attend_start issued the first block's copies):
-//  1. wait for K(i); scores of the lane's row against every head, q read from shared memory as broadcast
-//     float4s; then start the copy of K(i+1) into the slot;
-//  2. per head: block max and sum over the lanes, p = exp(s - m'), rescale alpha = exp(m - m');
-//  3. wait for V(i); P.V with the lane owning HD/32 dimensions of every head's accumulator, p from shared
-//     memory; then start the copy of V(i+1).
-// The warps' (m, l, acc) are combined in warp order at the end and written as the CTA partial to `part`.
+// ldmatrix: four 8x8 b16 matrices, lane L gives the row address of matrix L / 8, row L % 8; with .trans each
+// matrix arrives transposed.
+AIB_DEV void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+AIB_DEV void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+// x = p0 + p1 + p2 in bf16 parts (round to nearest even at each step): fp32-faithful products on bf16 MMAs
+AIB_DEV void split3(float x, uint16_t* p) {
+  p[0] = f32_to_bf16_rne(x);
+  x -= bf16_to_f32(p[0]);
+  p[1] = f32_to_bf16_rne(x);
+  x -= bf16_to_f32(p[1]);
+  p[2] = f32_to_bf16_rne(x);
+}
+AIB_DEV void split3_pair(float lo, float hi, uint32_t* w) {  // w[part] = (hi part << 16) | lo part
+  uint16_t a[3], b[3];
+  split3(lo, a);
+  split3(hi, b);
+#pragma unroll
+  for (int k = 0; k < 3; ++k) w[k] = static_cast<uint32_t>(a[k]) | (static_cast<uint32_t>(b[k]) << 16);
+}
+
+// Attention of the G query heads in sm.q over cache rows [j0, j1) of one group, on the tensor cores. Warp w
+// takes a contiguous slice of the range in blocks of 32 positions, the block's K and V rows in the warp's
+// slot (attend_start issued the first block's copies). mma.sync m16n8k16 with bf16 operands: the K and V
+// rows are exact bf16, q and the probabilities enter as three bf16 parts each, so products and fp32
+// accumulation are as accurate as fp32 FMAs.
+//  1. wait for K(i); S = K q^T: A = K rows (ldmatrix), B = q (heads as the 8 columns), 2 position tiles x
+//     HD/16 dimension steps x 3 parts; then start the copy of K(i+1) into the slot;
+//  2. per head: block max and sum over the 32 positions (lanes holding the same head), p = exp(s - m'),
+//     rescale alpha = exp(m - m'); p goes to shared memory to be re-read in the B layout;
+//  3. wait for V(i); O^T += V^T P: A = V rows transposed (ldmatrix.trans), B = p (3 parts), HD/16 dimension
+//     tiles x 2 position steps; then start the copy of V(i+1).
+// Lane (g, t) accumulates O^T rows (dims) g and g + 8 of every 16-dim tile for heads 2t and 2t + 1. The
+// warps' (m, l, acc) are combined in warp order at the end and written as the CTA partial to `part`.
 template <int HD, int G>
 AIB_DEV void attend_range(Smem<HD>& sm, uint8_t* ring, const uint16_t* kc, const uint16_t* vc, int j0, int j1,
                           float scale, float* part) {
-  constexpr int PER = HD / 32;  // dims per lane in P.V
-  constexpr int KS = k_stride<HD>();
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  constexpr int KS = k_stride<HD>(), NT = HD / 16;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g = lane >> 2, t = lane & 3;
   int w0, w1;
   warp_range(j0, j1, &w0, &w1);
   uint8_t* kslot = ring + warp * slot_bytes<HD>();
   uint8_t* vslot = kslot + kBlk * KS;
-  float m[G], l[G], acc[G][PER];
+  const uint32_t ks32 = smem_u32(kslot), vs32 = smem_u32(vslot);
+  // B fragments of q (head g, dims 16 s + 2t, +1, +8, +9), three parts, for every dimension step
+  uint32_t bq[NT][3][2];
 #pragma unroll
-  for (int h = 0; h < G; ++h) {
-    m[h] = -INFINITY;
-    l[h] = 0.0f;
+  for (int st = 0; st < NT; ++st) {
+    const float* q = sm.q[g];
+    const bool hv = g < G;
+    const int d = st * 16 + 2 * t;
+    uint32_t w[3];
+    split3_pair(hv ? q[d] : 0.0f, hv ? q[d + 1] : 0.0f, w);
+    uint32_t w2[3];
+    split3_pair(hv ? q[d + 8] : 0.0f, hv ? q[d + 9] : 0.0f, w2);
 #pragma unroll
-    for (int e = 0; e < PER; ++e) acc[h][e] = 0.0f;
+    for (int k = 0; k < 3; ++k) bq[st][k][0] = w[k], bq[st][k][1] = w2[k];
   }
-  float* pw = &sm.pw[warp][0][0];
+  const int h0 = 2 * t, h1 = 2 * t + 1;  // this lane's heads in the accumulators
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
+  float acc[NT][4];
+#pragma unroll
+  for (int dt = 0; dt < NT; ++dt) acc[dt][0] = acc[dt][1] = acc[dt][2] = acc[dt][3] = 0.0f;
+  float* pw = &sm.pw[warp][0][0];  // [GMAX][kBlk] probabilities of the block
+  // ldmatrix row addresses: lane L -> matrix L / 8, row L % 8
+  const int mr = (lane & 7) + ((lane >> 3) & 1) * 8, mc = (lane >> 4) * 8;  // A (non-transposed) tile
+  const int vr = (lane & 7) + (lane >> 4) * 8, vcol = ((lane >> 3) & 1) * 8;  // V tile, transposed load
   for (int b0 = w0; b0 < w1; b0 += kBlk) {
     const int cnt = min(kBlk, w1 - b0);
     const int nb0 = b0 + kBlk, ncnt = max(0, min(kBlk, w1 - nb0));
-    const bool valid = lane < cnt;
     // 1. scores (K(i) is the older of the two pending groups)
     cp_wait<1>();
     __syncwarp();
-    float sc[G];
+    float sc[2][4];
 #pragma unroll
-    for (int h = 0; h < G; ++h) sc[h] = 0.0f;
-    const uint8_t* krow = kslot + lane * KS;
+    for (int mt = 0; mt < 2; ++mt) {
+      sc[mt][0] = sc[mt][1] = sc[mt][2] = sc[mt][3] = 0.0f;
 #pragma unroll
-    for (int c = 0; c < HD / 8; ++c) {
-      const uint4 kq = *reinterpret_cast<const uint4*>(krow + c * 16);
-      const uint32_t w[4] = {kq.x, kq.y, kq.z, kq.w};
-      float kf[8];
+      for (int st = 0; st < NT; ++st) {
+        uint32_t a0, a1, a2, a3;
+        ldsm_x4(ks32 + (mt * 16 + mr) * KS + (st * 16 + mc) * 2, a0, a1, a2, a3);
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        kf[2 * k] = __uint_as_float(w[k] << 16);
-        kf[2 * k + 1] = __uint_as_float(w[k] & 0xFFFF0000u);
-      }
-#pragma unroll
-      for (int h = 0; h < G; ++h) {
-        const float4 qa = *reinterpret_cast<const float4*>(&sm.q[h][c * 8]);
-        const float4 qb = *reinterpret_cast<const float4*>(&sm.q[h][c * 8 + 4]);
-        float a = sc[h];
-        a = fmaf(qa.x, kf[0], a);
-        a = fmaf(qa.y, kf[1], a);
-        a = fmaf(qa.z, kf[2], a);
-        a = fmaf(qa.w, kf[3], a);
-        a = fmaf(qb.x, kf[4], a);
-        a = fmaf(qb.y, kf[5], a);
-        a = fmaf(qb.z, kf[6], a);
-        a = fmaf(qb.w, kf[7], a);
-        sc[h] = a;
+        for (int k = 0; k < 3; ++k) mma_bf16(sc[mt], a0, a1, a2, a3, bq[st][k][0], bq[st][k][1]);
       }
     }
     __syncwarp();  // every lane is done with the K rows
     if (ncnt > 0) copy_rows<HD, KS>(kslot, kc + static_cast<size_t>(nb0) * HD, ncnt);
     cp_commit();
-    // 2. block softmax per head
-    float alpha[G];
+    // 2. block softmax: sc[mt][0/1] position mt*16+g heads h0/h1, sc[mt][2/3] position mt*16+g+8
+    float s0[4], s1[4];
 #pragma unroll
-    for (int h = 0; h < G; ++h) {
-      const float s = valid ? sc[h] * scale : -INFINITY;
-      float mb = s;
+    for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, o));
-      const float mn = fmaxf(m[h], mb);
-      const float pr = valid ? expf(s - mn) : 0.0f;
-      float ps = pr;
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
-      alpha[h] = (m[h] == -INFINITY) ? 0.0f : expf(m[h] - mn);
-      l[h] = l[h] * alpha[h] + ps;
-      m[h] = mn;
-      pw[h * kBlk + lane] = pr;
-    }
-    // 3. P.V (V(i) is now the older pending group)
-    cp_wait<1>();
-    __syncwarp();
-#pragma unroll
-    for (int h = 0; h < G; ++h)
-#pragma unroll
-      for (int e = 0; e < PER; ++e) acc[h][e] *= alpha[h];
-#pragma unroll
-    for (int pp = 0; pp < kBlk; pp += 4) {
-      uint32_t vr[4][PER / 2];
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        // rows past cnt hold stale bytes: read a valid row instead (its p is 0)
-        const uint8_t* vrow = vslot + min(pp + k, cnt - 1) * (HD * 2) + lane * (PER * 2);
-        if (PER == 4) {
-          const uint2 v2 = *reinterpret_cast<const uint2*>(vrow);
-          vr[k][0] = v2.x;
-          vr[k][PER / 2 - 1] = v2.y;
-        } else {
-          vr[k][0] = *reinterpret_cast<const uint32_t*>(vrow);
-        }
+      for (int hi = 0; hi < 2; ++hi) {
+        const int pos = mt * 16 + g + hi * 8;
+        const bool ok = pos < cnt;
+        s0[mt * 2 + hi] = ok ? sc[mt][hi * 2] * scale : -INFINITY;
+        s1[mt * 2 + hi] = ok ? sc[mt][hi * 2 + 1] * scale : -INFINITY;
       }
+    float mb0 = fmaxf(fmaxf(s0[0], s0[1]), fmaxf(s0[2], s0[3]));
+    float mb1 = fmaxf(fmaxf(s1[0], s1[1]), fmaxf(s1[2], s1[3]));
 #pragma unroll
-      for (int h = 0; h < G; ++h) {
-        const float4 p4 = *reinterpret_cast<const float4*>(&pw[h * kBlk + pp]);
-        const float pv[4] = {p4.x, p4.y, p4.z, p4.w};
+    for (int o = 4; o < 32; o <<= 1) {
+      mb0 = fmaxf(mb0, __shfl_xor_sync(0xffffffffu, mb0, o));
+      mb1 = fmaxf(mb1, __shfl_xor_sync(0xffffffffu, mb1, o));
+    }
+    const float mn0 = fmaxf(m0, mb0), mn1 = fmaxf(m1, mb1);
+    float ps0 = 0.0f, ps1 = 0.0f;
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
+    for (int i = 0; i < 4; ++i) {
+      const int pos = (i >> 1) * 16 + g + (i & 1) * 8;
+      const float p0 = s0[i] == -INFINITY ? 0.0f : expf(s0[i] - mn0);
+      const float p1 = s1[i] == -INFINITY ? 0.0f : expf(s1[i] - mn1);
+      ps0 += p0;
+      ps1 += p1;
+      pw[h0 * kBlk + pos] = p0;  // h0, h1 < GMAX always; heads >= G carry zeros (q = 0) and are ignored
+      pw[h1 * kBlk + pos] = p1;
+    }
 #pragma unroll
-          for (int e2 = 0; e2 < PER / 2; ++e2) {
-            const uint32_t v = vr[k][e2];
-            acc[h][2 * e2] = fmaf(pv[k], __uint_as_float(v << 16), acc[h][2 * e2]);
-            acc[h][2 * e2 + 1] = fmaf(pv[k], __uint_as_float(v & 0xFFFF0000u), acc[h][2 * e2 + 1]);
-          }
-        }
+    for (int o = 4; o < 32; o <<= 1) {
+      ps0 += __shfl_xor_sync(0xffffffffu, ps0, o);
+      ps1 += __shfl_xor_sync(0xffffffffu, ps1, o);
+    }
+    const float al0 = m0 == -INFINITY ? 0.0f : expf(m0 - mn0), al1 = m1 == -INFINITY ? 0.0f : expf(m1 - mn1);
+    l0 = l0 * al0 + ps0;
+    l1 = l1 * al1 + ps1;
+    m0 = mn0;
+    m1 = mn1;
+    // 3. P.V (V(i) is now the older pending group); rows past cnt hold stale bytes: zero them first
+    cp_wait<1>();
+    if (cnt < kBlk)
+      for (int i = lane; i < (kBlk - cnt) * (HD / 8); i += 32)
+        *reinterpret_cast<uint4*>(vslot + (cnt + i / (HD / 8)) * KS + (i % (HD / 8)) * 16) = make_uint4(0, 0, 0, 0);
+    __syncwarp();
+    // B fragments of p (positions 16 s + 2t, +1, +8, +9 for head g), three parts
+    uint32_t bp[2][3][2];
+#pragma unroll
+    for (int ps = 0; ps < 2; ++ps) {
+      const float* pr = pw + (g < GMAX ? g : 0) * kBlk + ps * 16 + 2 * t;
+      const float2 lo = *reinterpret_cast<const float2*>(pr);
+      const float2 hi = *reinterpret_cast<const float2*>(pr + 8);
+      const bool hv = g < G;
+      uint32_t w[3], w2[3];
+      split3_pair(hv ? lo.x : 0.0f, hv ? lo.y : 0.0f, w);
+      split3_pair(hv ? hi.x : 0.0f, hv ? hi.y : 0.0f, w2);
+#pragma unroll
+      for (int k = 0; k < 3; ++k) bp[ps][k][0] = w[k], bp[ps][k][1] = w2[k];
+    }
+#pragma unroll
+    for (int dt = 0; dt < NT; ++dt) {
+      acc[dt][0] *= al0;
+      acc[dt][1] *= al1;
+      acc[dt][2] *= al0;
+      acc[dt][3] *= al1;
+#pragma unroll
+      for (int ps = 0; ps < 2; ++ps) {
+        uint32_t a0, a1, a2, a3;
+        ldsm_x4_t(vs32 + (ps * 16 + vr) * KS + (dt * 16 + vcol) * 2, a0, a1, a2, a3);
+#pragma unroll
+        for (int k = 0; k < 3; ++k) mma_bf16(acc[dt], a0, a1, a2, a3, bp[ps][k][0], bp[ps][k][1]);
       }
     }
     __syncwarp();  // pw and the V rows are rewritten next
-    if (ncnt > 0) copy_rows<HD, HD * 2>(vslot, vc + static_cast<size_t>(nb0) * HD, ncnt);
+    if (ncnt > 0) copy_rows<HD, KS>(vslot, vc + static_cast<size_t>(nb0) * HD, ncnt);
     cp_commit();
   }
   cp_wait<0>();     // nothing of this thread may land in the ring once it is reused below
   __syncthreads();  // every warp is done with its slot
-  // combine the warps in order through the dynamic buffer
+  // this warp's state for its heads: m, l and O rows (dims dt*16 + g, + 8)
   float* wst = reinterpret_cast<float*>(ring);  // [kWarps][GMAX][HD + 2]
 #pragma unroll
-  for (int h = 0; h < G; ++h) {
-    {
+  for (int hh = 0; hh < 2; ++hh) {
+    const int h = 2 * t + hh;
+    if (h < G) {
       float* dst = wst + (static_cast<size_t>(warp) * GMAX + h) * (HD + 2);
 #pragma unroll
-      for (int e = 0; e < PER; ++e) dst[lane * PER + e] = acc[h][e];
-      if (lane == 0) {
-        dst[HD] = m[h];
-        dst[HD + 1] = l[h];
+      for (int dt = 0; dt < NT; ++dt) {
+        dst[dt * 16 + g] = acc[dt][hh];
+        dst[dt * 16 + g + 8] = acc[dt][2 + hh];
+      }
+      if (g == 0) {
+        dst[HD] = hh ? m1 : m0;
+        dst[HD + 1] = hh ? l1 : l0;
       }
     }
   }
   __syncthreads();
+  // combine the warps in order
   for (int idx = threadIdx.x; idx < G * HD; idx += kThreads) {
     const int h = idx / HD, d = idx % HD;
     float M = -INFINITY;

@@ -449,13 +449,6 @@ constexpr int kMmaConsumers = 512;  // 16 warps: 2 halves (alternate tiles) x 4 
 constexpr int kMmaThreads = kMmaConsumers + 32;
 static_assert(kMmaStageM8 == 16 * 4 * 256 && kMmaStageE4 == 16 * 4 * 128, "stage = TMA boxes {256,4,16} + {128,4,16}");
 
-AIB_DEV void mma_bf16(float* d, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
 
 // clear the 16-bit halves whose exponent code is 15 (exceptions decode to 0; their value is added apart)
 AIB_DEV uint32_t clear15(uint32_t z, uint32_t codes) {  // codes: low element in bits 0..3, high in 16..19
