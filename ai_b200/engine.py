@@ -18,13 +18,14 @@ GEMV over the whole vocabulary and sampling runs on the device: one 8-byte read 
 (core/engine.py:489-694), with top_k / penalties added; prompts longer than 16 tokens run in 16-token
 batched chunks (the reference's legacy prefill path, core/engine.py:471-480).
 """
+import os
 import time
 
 import numpy as np
 import torch
 
 from .head import Head as Head8
-from . import _lib, wcomp, tkernels, sampler
+from . import _lib, wcomp, tkernels, sampler, codecfile
 from ._lib import ptr, stream_ptr
 from .model import CONFIGS, Ckpt, RandomWeights, Qwen3Config, check_tp, shard_layer
 
@@ -34,7 +35,7 @@ MAXB = 16
 
 class Engine:
     def __init__(self, name, maxt=2048, device="cuda", seed=0, log=print, norm_noise=0.0, weights=None,
-                 graphs=True, head8=True, tp=1):
+                 graphs=True, head8=True, tp=1, codec_cache=None):
         """name: an HF Qwen3 folder, or a key of ai_b200.model.CONFIGS / a Qwen3Config for random-init
         weights (N(0, 0.02) matrices, seed `seed`). weights: an explicit weight source (RandomWeights/Ckpt).
         head8: greedy steps without penalties pick through the int8 head (the reference's Head: bounds over an
@@ -43,7 +44,10 @@ class Engine:
         GPU, every rank making the same calls): each rank holds its KV groups' share of every layer
         (`model.shard_layer`), and one all-reduce after o_proj and after down_proj sums the ranks' partial
         residual updates. Embedding, final norm, head and sampler are replicated: every rank picks the same
-        token from the same all-reduced state."""
+        token from the same all-reduced state.
+        codec_cache: path of a `codecfile` with this model's encoded matrices (per tensor-parallel rank: the
+        path gets a `.tp{N}r{rank}` suffix). Loaded when present and made for this model and layout,
+        written after encoding otherwise."""
         if not isinstance(maxt, int) or isinstance(maxt, bool) or maxt < 1:
             raise ValueError("maxt must be a positive integer")
         t0 = time.time()
@@ -83,18 +87,40 @@ class Engine:
         # plain input; otherwise [gate; up] and the SiLU-gated input of down (mode 2), as the reference.
         self.gated = cfg.D % 1024 == 0
         self.W, self.small = [], []
-        for i in range(self.L):
-            lw = src.layer(i)
-            if self.tp > 1:
-                lw = shard_layer(lw, cfg, self.tp_rank, self.tp)
-            if self.gated:
-                lw["gu"] = wcomp.interleave_gate_up(lw["gu"])
-            self.W.append({n: wcomp.compress(lw[n].to(dev)) for n in MATS})
-            self.small.append({k: lw[k].to(dev).contiguous() for k in ("ln1", "ln2", "qn", "kn")})
-            del lw
+        cache = None
+        if codec_cache:
+            cache = codec_cache if self.tp == 1 else f"{codec_cache}.tp{self.tp}r{self.tp_rank}"
+        cmeta = {"model": cfg.name, "L": cfg.L, "D": cfg.D, "H": cfg.H, "KV": cfg.KV, "HD": cfg.HD, "FF": cfg.FF,
+                 "V": cfg.V, "tied": cfg.tied, "gu_layout": "interleaved" if self.gated else "fused",
+                 "tp": f"{self.tp}:{self.tp_rank}",
+                 "source": f"random:{src.seed}:{src.std}" if isinstance(src, RandomWeights) else
+                 os.path.abspath(getattr(src, "dir", ""))}
+        mats = codecfile.load(cache, dev, expect=cmeta) if cache and os.path.exists(cache) else None
         self.emb = src.embedding().to(dev).contiguous()
-        hw = self.emb if cfg.tied else src.head().to(dev)
-        self.head = wcomp.compress(hw)
+        if mats is not None:  # encoded planes from disk: only the norm weights come from the source
+            for i in range(self.L):
+                self.W.append({n: mats[f"layers.{i}.{n}"] for n in MATS})
+                lw = src.layer_small(i)
+                self.small.append({k: lw[k].to(dev).contiguous() for k in ("ln1", "ln2", "qn", "kn")})
+            self.head = mats["head"]
+            hw = wcomp.decompress(self.head) if head8 else None  # lossless: the head's bf16 weights
+        else:
+            for i in range(self.L):
+                lw = src.layer(i)
+                if self.tp > 1:
+                    lw = shard_layer(lw, cfg, self.tp_rank, self.tp)
+                if self.gated:
+                    lw["gu"] = wcomp.interleave_gate_up(lw["gu"])
+                self.W.append({n: wcomp.compress(lw[n].to(dev)) for n in MATS})
+                self.small.append({k: lw[k].to(dev).contiguous() for k in ("ln1", "ln2", "qn", "kn")})
+                del lw
+            hw = self.emb if cfg.tied else src.head().to(dev)
+            self.head = wcomp.compress(hw)
+            if cache:
+                torch.cuda.synchronize()
+                out = {f"layers.{i}.{n}": self.W[i][n] for i in range(self.L) for n in MATS}
+                out["head"] = self.head
+                codecfile.save(cache, out, cmeta)
         self.head8 = Head8(hw, self.head, TM=MAXB) if head8 else None
         del hw
         self.norm = src.final_norm().to(dev).contiguous()

@@ -115,6 +115,13 @@ class RandomWeights:
                 "ln1": self._norm(b + 7, c.D), "ln2": self._norm(b + 8, c.D),
                 "qn": self._norm(b + 9, c.HD), "kn": self._norm(b + 10, c.HD)}
 
+    def layer_small(self, i):
+        """The layer's norm weights only (ln1, ln2, qn, kn), without producing its matrices."""
+        c = self.cfg
+        b = 100 + 16 * i
+        return {"ln1": self._norm(b + 7, c.D), "ln2": self._norm(b + 8, c.D), "qn": self._norm(b + 9, c.HD),
+                "kn": self._norm(b + 10, c.HD)}
+
     def embedding(self):
         return self._mat(1, self.cfg.V, self.cfg.D)
 
@@ -194,6 +201,11 @@ class Ckpt:
         return {"qkv": torch.cat([t(n["q"]), t(n["k"]), t(n["v"])]), "o": t(n["o"]),
                 "gu": torch.cat([t(n["gate"]), t(n["up"])]), "down": t(n["down"]),
                 "ln1": t(n["ln1"]), "ln2": t(n["ln2"]), "qn": t(n["qn"]), "kn": t(n["kn"])}
+
+    def layer_small(self, i):
+        """The layer's norm weights only (ln1, ln2, qn, kn), without reading its matrices."""
+        n = layer_tensor_names(i)
+        return {k: self.t(n[k]) for k in ("ln1", "ln2", "qn", "kn")}
 
     def embedding(self):
         return self.t("model.embed_tokens.weight")

@@ -81,3 +81,24 @@ def test_process_errors_like_reference(pair):
         eng.process([cfg.V], 0)
     with pytest.raises(ValueError):
         eng.process([1], 10 ** 6)
+
+
+def test_codec_cache_reload(tmp_path):
+    """An engine loaded from the on-disk codec file (written by a first load) holds the same planes and
+    decodes the same greedy tokens; a file made for other weights is refused."""
+    from ai_b200.engine import Engine
+    from ai_b200.model import CONFIGS, RandomWeights
+    cfg = CONFIGS["small-1k"]
+    rw = RandomWeights(cfg, seed=11, norm_noise=0.1, std=0.05)
+    path = str(tmp_path / "small-1k.codec")
+    a = Engine(cfg, maxt=64, weights=rw, log=None, codec_cache=path)
+    b = Engine(cfg, maxt=64, weights=rw, log=None, codec_cache=path)
+    for la, lb in zip(a.W, b.W):
+        for n in la:
+            for k in ("m8", "e4", "rp", "ec", "ev"):
+                assert torch.equal(la[n][k], lb[n][k])
+    prompt = [5, 4, 3, 2, 1]
+    assert list(a.generate(prompt, max_new=8)) == list(b.generate(prompt, max_new=8))
+    with pytest.raises(ValueError):
+        Engine(cfg, maxt=64, weights=RandomWeights(cfg, seed=12, norm_noise=0.1, std=0.05), log=None,
+               codec_cache=path)
