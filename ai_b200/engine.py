@@ -309,6 +309,17 @@ class Engine:
         self.ctx = previous + list(tokens)
         return result
 
+    def draft(self, seq, k):
+        """This engine as the drafter (reference Engine.draft, core/engine.py:787-803): up to k greedy tokens
+        after seq, reusing the cached prefix it shares with seq."""
+        if k <= 0:
+            return []
+        c = min(self.common(seq), len(seq) - 1)
+        out = [self.process(list(seq[c:]), c, last_only=True)[-1]]
+        for i in range(k - 1):
+            out.append(self.process([out[-1]], len(seq) + i)[0])
+        return out
+
     def common(self, seq):
         n = 0
         for a, b in zip(self.ctx, seq):
@@ -319,10 +330,18 @@ class Engine:
 
     def generate(self, prompt, max_new=256, temperature=0.0, top_p=1.0, seed=None, top_k=0, repetition_penalty=1.0,
                  presence_penalty=0.0, frequency_penalty=0.0, stats=None, draft=None, k=None, force=None, cons=None):
-        """Yield up to max_new tokens (reference generate, core/engine.py:538-694, without the draft engine).
-        Penalties count the prompt and the generated tokens (the most recent 4096 ids)."""
-        if draft is not None or cons is not None:
-            raise NotImplementedError("draft engines and grammar constraints are not part of this engine")
+        """Yield up to max_new tokens (reference generate, core/engine.py:538-694). Penalties count the prompt and
+        the generated tokens (the most recent 4096 ids).
+        draft: another Engine that proposes up to k (default 15) greedy tokens per pass; this engine verifies
+        the last token plus the proposal in one batched pass (the weights are read once for all of them) and
+        keeps the proposal's longest prefix that matches its own picks, plus its own next token (the
+        reference's speculative loop, engine.py:589-694, without its cost-model gating). Greedy only, as in
+        the reference; stats gain drafted / accepted counts."""
+        if cons is not None:
+            raise NotImplementedError("grammar constraints are not part of this engine")
+        if draft is not None and (temperature > 0 or repetition_penalty != 1.0 or presence_penalty != 0.0 or
+                                  frequency_penalty != 0.0):
+            raise NotImplementedError("the draft path verifies greedy decoding without penalties, as the reference")
         if not isinstance(max_new, int) or isinstance(max_new, bool) or max_new < 0:
             raise ValueError("max_new must be a non-negative integer")
         if max_new == 0:
@@ -360,6 +379,30 @@ class Engine:
                   gen_ms=0.0, passes=0)
         gen = [tok]
         yield tok
+        if draft is not None:
+            st.update(drafted=0, accepted=0)
+            while len(gen) < max_new and gen[-1] not in self.eos:
+                ts = time.perf_counter()
+                seq = list(prompt) + gen
+                kmax = min(k or 15, MAXB - 1, max_new - len(gen) - 1, self.maxt - len(seq),
+                           max(0, draft.maxt - len(seq)))
+                d = draft.draft(seq, kmax) if kmax > 0 else []
+                res = self.process([gen[-1]] + d, len(seq) - 1)  # the KV holds seq[:-1]
+                n = 0
+                while n < len(d) and d[n] == res[n]:
+                    n += 1
+                st["drafted"] += len(d)
+                st["accepted"] += n
+                st["gen_ms"] += (time.perf_counter() - ts) * 1000
+                st["passes"] += 1
+                for t in d[:n] + [res[n]]:
+                    if len(gen) >= max_new or gen[-1] in self.eos:
+                        break
+                    gen.append(t)
+                    st["gen_n"] = len(gen)
+                    st["decode_n"] = len(gen) - 1
+                    yield t
+            return
         # decode loop: the graph chains ids and pos on the device; the host supplies u and reads one id
         while len(gen) < max_new and gen[-1] not in self.eos:
             ts = time.perf_counter()

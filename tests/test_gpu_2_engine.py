@@ -102,3 +102,23 @@ def test_codec_cache_reload(tmp_path):
     with pytest.raises(ValueError):
         Engine(cfg, maxt=64, weights=RandomWeights(cfg, seed=12, norm_noise=0.1, std=0.05), log=None,
                codec_cache=path)
+
+
+def test_speculative_greedy_equals_plain():
+    """Greedy decoding verified against a draft engine gives the plain greedy tokens: with the same model as
+    drafter every proposal is accepted, with another model most are rejected and corrected."""
+    from ai_b200.engine import Engine
+    from ai_b200.model import CONFIGS, RandomWeights
+    cfg = CONFIGS["small"]
+    tgt = Engine(cfg, maxt=128, weights=RandomWeights(cfg, seed=11, norm_noise=0.1, std=0.05), log=None)
+    same = Engine(cfg, maxt=128, weights=RandomWeights(cfg, seed=11, norm_noise=0.1, std=0.05), log=None)
+    other = Engine(cfg, maxt=128, weights=RandomWeights(cfg, seed=29, norm_noise=0.1, std=0.05), log=None)
+    prompt = [int(t) for t in np.random.default_rng(4).integers(0, cfg.V, 12)]
+    plain = list(tgt.generate(prompt, max_new=40))
+    st1, st2 = {}, {}
+    assert list(tgt.generate(prompt, max_new=40, draft=same, k=7, stats=st1)) == plain
+    assert st1["accepted"] == st1["drafted"] and st1["passes"] < 39
+    assert list(tgt.generate(prompt, max_new=40, draft=other, stats=st2)) == plain
+    assert st2["accepted"] < st2["drafted"]
+    with pytest.raises(NotImplementedError):
+        list(tgt.generate(prompt, max_new=4, draft=same, temperature=0.7))
