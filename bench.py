@@ -181,7 +181,8 @@ def gpu_arm(args, rank, world):
     torch.cuda.synchronize()
     from ai_b200 import sampler
     import numpy as np
-    prm = sampler.params(**SAMPLING)
+    samp = dict(temperature=0.0, top_k=0, top_p=1.0) if args.greedy else SAMPLING
+    prm = sampler.params(**samp)
     rng = np.random.default_rng(seq)
     eng.u.copy_(torch.from_numpy(rng.random(16)))
     eng.ids[0] = 1
@@ -216,7 +217,7 @@ def gpu_arm(args, rank, world):
     stats = {}
     with Clocks(dev.index) as ck2:
         n = 0
-        for _ in eng.generate(prompt, max_new=args.steps + 1, seed=seq, stats=stats, **SAMPLING):
+        for _ in eng.generate(prompt, max_new=args.steps + 1, seed=seq, stats=stats, **samp):
             n += 1
     e2e_local = stats["decode_n"] / (stats["gen_ms"] / 1e3)
     te = torch.tensor([stats["gen_ms"]], dtype=torch.float64, device=dev)
@@ -238,7 +239,8 @@ def gpu_arm(args, rank, world):
         "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4), "higher_is_better": True,
         "scaling": "strong" if tp > 1 else "weak", "vs_baseline": None, "dtype": "fp32 activations x exact bf16 weights (12-bit codec), "
         "bf16 KV", "data": "synthetic (random-init N(0,0.02) weights, KV pre-filled N(0,1) to 4096)",
-        "config": {"workload": "Qwen3-8B decode bs1, 12-bit weights, ctx 4096->, top-k 20 / top-p 0.8 / T 0.6",
+        "config": {"workload": "Qwen3-8B decode bs1, 12-bit weights, ctx 4096->, " +
+                   ("greedy (int8 head + exact candidates)" if args.greedy else "top-k 20 / top-p 0.8 / T 0.6"),
                    "model": "qwen3-8b", "global_batch": nseq, "seq_len": CTX,
                    "parallelism": f"tp{tp}" if tp > 1 else ("replicas" if world > 1 else "single"),
                    "l2": "weights (10.4 GB) > L2 every step"},
@@ -383,6 +385,8 @@ def main():
     ap.add_argument("--gemv-variant", type=int, default=None, choices=[0, 1, 2, 3],
                     help="codec GEMV kernel for --micro: 0 tensor-core 24 KB stages, 1 CUDA-core 12 KB stages, 2 CUDA-core 48 KB stages, 3 tensor-core 48 KB stages (default)")
     ap.add_argument("--streamk", action="store_true", help="--micro gemv*: pass the stream-K workspace")
+    ap.add_argument("--greedy", action="store_true",
+                    help="greedy decoding (the int8 head's exact-candidate pick) instead of the default sampling")
     ap.add_argument("--tp", action="store_true",
                     help="with --gpus N under torchrun: one sequence, tensor parallel over the N ranks (default: N replicas)")
     ap.add_argument("--gpus", type=int, default=1)
