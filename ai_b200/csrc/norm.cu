@@ -12,7 +12,16 @@ __global__ void rms_kernel(const float* __restrict__ x, const uint16_t* __restri
   const int t = blockIdx.x;
   const float* xr = x + static_cast<size_t>(t) * D;
   float ss = 0.0f;
-  for (int i = threadIdx.x; i < D; i += blockDim.x) ss += xr[i] * xr[i];
+  const bool vec = (D & 3) == 0 && !(reinterpret_cast<uintptr_t>(xr) & 15);
+  if (vec) {  // 16-byte loads, several in flight per thread
+#pragma unroll 4
+    for (int i = threadIdx.x; i < D / 4; i += blockDim.x) {
+      const float4 v = reinterpret_cast<const float4*>(xr)[i];
+      ss += (v.x * v.x + v.y * v.y) + (v.z * v.z + v.w * v.w);
+    }
+  } else {
+    for (int i = threadIdx.x; i < D; i += blockDim.x) ss += xr[i] * xr[i];
+  }
   __shared__ float red[32];
   ss = warp_sum(ss);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
@@ -36,7 +45,20 @@ __global__ void embed_kernel(const uint16_t* __restrict__ emb, const int64_t* __
   }
   const uint16_t* row = emb + static_cast<size_t>(id) * D;
   float* o = out + static_cast<size_t>(t) * D;
-  for (int i = threadIdx.x; i < D; i += blockDim.x) o[i] = bf16_to_f32(row[i]);
+  if ((D & 7) == 0 && !(reinterpret_cast<uintptr_t>(row) & 15) && !(reinterpret_cast<uintptr_t>(o) & 15)) {
+    // 8 values per 16-byte load, all of a thread's loads in flight together (one HBM round trip)
+#pragma unroll 4
+    for (int i = threadIdx.x; i < D / 8; i += blockDim.x) {
+      const uint4 v = __ldg(reinterpret_cast<const uint4*>(row) + i);
+      float4* o4 = reinterpret_cast<float4*>(o) + 2 * i;
+      o4[0] = make_float4(__uint_as_float(v.x << 16), __uint_as_float(v.x & 0xFFFF0000u), __uint_as_float(v.y << 16),
+                          __uint_as_float(v.y & 0xFFFF0000u));
+      o4[1] = make_float4(__uint_as_float(v.z << 16), __uint_as_float(v.z & 0xFFFF0000u), __uint_as_float(v.w << 16),
+                          __uint_as_float(v.w & 0xFFFF0000u));
+    }
+  } else {
+    for (int i = threadIdx.x; i < D; i += blockDim.x) o[i] = bf16_to_f32(row[i]);
+  }
   pdl_trigger();
 }
 
