@@ -233,7 +233,9 @@ def gpu_arm(args, rank, world):
         eng.close()  # its graphs hold NCCL calls: release them before the process group goes
     if rank != 0:
         return None
-    launches_per_step = 1 + 5 * eng.L + 1 + 1 + 1
+    # embed, 5 per layer (qkv GEMV, attention, o, gate/up, down), head GEMV, sampler (2 phases), advance;
+    # greedy: final norm, bounds, candidates, exact pick in place of head + sampler
+    launches_per_step = 1 + 5 * eng.L + (4 if args.greedy else 1 + 2) + 1
     out = {
         "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4), "higher_is_better": True,
