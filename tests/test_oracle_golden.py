@@ -225,3 +225,26 @@ def test_tiny_model_oracle_matches_reference_step_sequence():
     toks, lg = o.greedy(list(z["prompt"]), len(z["tokens"]))
     assert toks == list(z["tokens"])
     np.testing.assert_allclose(lg, z["logits"], rtol=1e-4, atol=1e-4)
+
+
+@pytest.mark.parametrize("seed", [0, 1, 2])
+def test_head_bounds_contain_exact_logits(seed):
+    """The property the greedy pick rests on (vocab8.py:1-12): every exact logit lies in [a - B, a + B], so the
+    argmax row always has HI >= LO -- on random heads with rows of very different scales, an all-zero row,
+    and tokens whose h has large and tiny entries."""
+    g = np.random.default_rng(seed)
+    V, D, T = 400, 128, 4
+    w = (g.standard_normal((V, D)) * 0.02).astype(np.float32)
+    w[::7] *= 300.0
+    w[5] = 0.0
+    wb = codec.f32_to_bf16_bits(w)
+    h = g.standard_normal((T, D)).astype(np.float32)
+    h[1, :8] *= 1e4
+    h[2] *= 1e-3
+    Q, S, C1, C2, AM = head.tables(wb)
+    hi, lo = head.bounds(h, Q, S, C1, C2, AM)
+    ex = head.exact_logits(wb, h)
+    assert (ex <= hi).all()
+    assert (ex.max(1) >= lo).all()
+    for t in range(T):  # the argmax is always a candidate
+        assert hi[t, int(np.argmax(ex[t]))] >= lo[t]
