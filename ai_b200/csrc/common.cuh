@@ -146,6 +146,9 @@ int launch_check(const char* what);  // maps cudaGetLastError to AIB_ECUDA
 // Encodes a 3-D tiled tensor map (uint8 elements, no swizzle, no interleave).
 int make_map_3d_u8(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t s1_bytes,
                    uint64_t s2_bytes, uint32_t b0, uint32_t b1, uint32_t b2);
+// General tiled tensor map: `rank` dims (innermost first), rank-1 byte strides, box, swizzle mode.
+int make_map(CUtensorMap* map, CUtensorMapDataType dtype, int elem_bytes, int rank, const void* base,
+             const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle swizzle);
 
 // Raise a kernel's dynamic shared-memory limit to the sm_100 per-block maximum (232448 bytes, static +
 // dynamic), once per (kernel, device). A failure is reported and clears the runtime's sticky error.

@@ -229,9 +229,10 @@ __global__ void __launch_bounds__(kThreads, 2) bounds_kernel(BoundsArgs a) {
 
 // ------------------------------------------------------------------------------------------ greedy
 // 64-bit key: the fp32 logit in an order-preserving unsigned form, then 0xFFFFFFFF - v (a larger key is a
-// larger logit, or the same logit at a smaller id). 0 is below every key.
+// larger logit, or the same logit at a smaller id). 0 is below every key. -0.0 and +0.0 compare equal, as in
+// the reference's `l == l.max()`, so both map to the key of +0.0.
 AIB_DEV unsigned long long pick_key(float x, int v) {
-  const uint32_t b = __float_as_uint(x);
+  const uint32_t b = x == 0.0f ? 0u : __float_as_uint(x);
   const uint32_t u = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
   return (static_cast<unsigned long long>(u) << 32) | (0xFFFFFFFFu - static_cast<uint32_t>(v));
 }

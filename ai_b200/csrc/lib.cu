@@ -3,8 +3,10 @@
 #include "runtime.cu"
 #include "codec.cu"
 #include "gemv.cu"
+#include "gemm.cu"
 #include "norm.cu"
 #include "attn.cu"
 #include "attn_noalloc.cu"
 #include "sampler.cu"
 #include "head8.cu"
+#include "exact.cu"

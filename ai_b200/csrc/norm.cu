@@ -12,16 +12,16 @@ __global__ void rms_kernel(const float* __restrict__ x, const uint16_t* __restri
   const int t = blockIdx.x;
   const float* xr = x + static_cast<size_t>(t) * D;
   float ss = 0.0f;
-  const bool vec = (D & 3) == 0 && !(reinterpret_cast<uintptr_t>(xr) & 15);
-  if (vec) {  // 16-byte loads, several in flight per thread
+  // One summation order whatever the row's alignment: groups of four columns per thread, the tail after.
+  // Aligned rows load each group with one 16-byte load; others load the same four values one by one.
+  const bool vec = !(reinterpret_cast<uintptr_t>(xr) & 15);
 #pragma unroll 4
-    for (int i = threadIdx.x; i < D / 4; i += blockDim.x) {
-      const float4 v = reinterpret_cast<const float4*>(xr)[i];
-      ss += (v.x * v.x + v.y * v.y) + (v.z * v.z + v.w * v.w);
-    }
-  } else {
-    for (int i = threadIdx.x; i < D; i += blockDim.x) ss += xr[i] * xr[i];
+  for (int i = threadIdx.x; i < D / 4; i += blockDim.x) {
+    const float4 v = vec ? reinterpret_cast<const float4*>(xr)[i]
+                         : make_float4(xr[4 * i], xr[4 * i + 1], xr[4 * i + 2], xr[4 * i + 3]);
+    ss += (v.x * v.x + v.y * v.y) + (v.z * v.z + v.w * v.w);
   }
+  for (int i = (D & ~3) + threadIdx.x; i < D; i += blockDim.x) ss += xr[i] * xr[i];
   __shared__ float red[32];
   ss = warp_sum(ss);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;

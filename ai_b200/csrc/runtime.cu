@@ -82,6 +82,31 @@ int make_map_3d_u8(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1,
   return AIB_OK;
 }
 
+int make_map(CUtensorMap* map, CUtensorMapDataType dtype, int elem_bytes, int rank, const void* base,
+             const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle swizzle) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(AIB_ECUDA, "cuTensorMapEncodeTiled is not available");
+  if (rank < 1 || rank > 5) return fail(AIB_EINVAL, "tensor map: rank %d", rank);
+  if (reinterpret_cast<uintptr_t>(base) & 15) return fail(AIB_EINVAL, "tensor map: base must be 16-byte aligned");
+  for (int i = 0; i + 1 < rank; ++i)
+    if (strides_bytes[i] & 15) return fail(AIB_EINVAL, "tensor map: strides must be multiples of 16 bytes");
+  if ((box[0] * static_cast<uint32_t>(elem_bytes)) & 15)
+    return fail(AIB_EINVAL, "tensor map: the inner box must be a multiple of 16 bytes");
+  cuuint64_t d[5], s[4];
+  cuuint32_t b[5], es[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    b[i] = box[i];
+    es[i] = 1;
+    if (i + 1 < rank) s[i] = strides_bytes[i];
+  }
+  CUresult r = fn(map, dtype, static_cast<cuuint32_t>(rank), const_cast<void*>(base), d, s, b, es,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(AIB_ECUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return AIB_OK;
+}
+
 }  // namespace aib
 
 extern "C" {

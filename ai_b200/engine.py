@@ -9,10 +9,11 @@ counterpart.
 Step (`_gpu_layer` :329-341 for T = 1, `_batch_layer` :344-356 for T <= 16), captured once per shape in a
 CUDA graph (`_capture` :415-444) and replayed with the position and the input ids in device memory:
     embed(ids) -> per layer: gemv(qkv, RMS ln1) -> rope_attn -> gemv(o, +=) -> gemv(gu, RMS ln2) -> gemv(down,
-    silu*up, +=)  -> head gemv (RMS final norm fused) -> sampler -> advance(ids, pos)
-T > 1 uses rmsnorm + batched gemv + qk_rope_cache + cached attention. Unlike the reference (head on the
-GPU, exact logits and sampling on the CPU, head.py:59-88, with a D2H sync per token), the head is a 12-bit
-GEMV over the whole vocabulary and sampling runs on the device: one 8-byte read per generated token.
+    silu*up, +=)  -> final RMSNorm -> head -> advance(ids, pos)
+T > 1 uses rmsnorm + batched gemv + qk_rope_cache + cached attention. The head is the reference's `Head.pick`
+(generation/head.py:59-88) on the device: greedy steps take the int8 bounds + exact candidate logits, sampling
+steps the exact logits of the whole vocabulary (the reference computes those on the CPU after a D2H copy), then
+the device sampler: one 8-byte read per generated token.
 
 `process(tokens, pos0, ...)` and `generate(prompt, ...)` keep the reference arguments and errors
 (core/engine.py:489-694), with top_k / penalties added; prompts longer than 16 tokens run in 16-token
@@ -24,7 +25,7 @@ import time
 import numpy as np
 import torch
 
-from .head import Head as Head8
+from .head import Head as Head8, exact_logits
 from . import _lib, wcomp, tkernels, sampler, codecfile
 from ._lib import ptr, stream_ptr
 from .model import CONFIGS, Ckpt, RandomWeights, Qwen3Config, check_tp, shard_layer
@@ -209,24 +210,19 @@ class Engine:
                     wcomp.gemvc_tc(self.gub[:T], W["down"], x, 2, T)
                 self._reduce(x)
 
-    def _head(self, T):
-        if T == 1:
-            wcomp.gemvc1(self.xb[0], self.head, self.logits[0], 0, lnw=self.norm, eps=self.eps)
-        else:
-            tkernels.rmsg(self.xb[:T], self.norm, self.hb[:T], self.eps)
-            wcomp.gemvc_tc(self.hb[:T], self.head, self.logits[:T], 0, T)
-
     def _step(self, T, prm, rows, penal):
         """Everything that runs on the device for one pass of T tokens (graph body)."""
         tkernels.embed(self.emb, self.ids[:T], self.xb[:T])
         self._layers(T)
         r0 = T - rows
+        tkernels.rmsg(self.xb[r0:T], self.norm, self.hb[r0:T], self.eps)
         if self.head8 is not None and prm.temperature <= 0 and not penal:
-            # greedy: final norm, int8 bounds, exact logits of the candidate rows (Head.pick, head.py:59-88)
-            tkernels.rmsg(self.xb[r0:T], self.norm, self.hb[r0:T], self.eps)
+            # greedy: int8 bounds, exact logits of the candidate rows (Head.pick, head.py:59-88)
             self.head8.pick(self.hb[r0:T], rows, out=self.out_ids[r0:T])
         else:
-            self._head(T)
+            # sampling (or penalties): exact logits of the whole vocabulary, as Head.pick computes them for
+            # sampling (head.py:62-71), then the device sampler
+            exact_logits(self.hb[r0:T], self.head, rows, self.logits[r0:T])
             sampler.sample_into(self.logits[r0:T], self.out_ids[r0:T], prm,
                                 self.u[:rows] if prm.temperature > 0 else None, self.prior if penal else None, None,
                                 B=rows, ws=self.sample_ws)

@@ -8,8 +8,10 @@
   .pick(h, T)           Head.pick with temperature 0 (head.py:59-88): exact fp32 logits of the candidates
                         HI >= LO, argmax with the smallest id on ties -> int64 ids [T] on the device
 
-Sampling (temperature > 0) is not offered here: the reference recomputes every exact logit on the CPU for
-it; the engine samples from the codec GEMV's logits with `ai_b200.sampler` instead.
+  exact_logits(h, c12, T, out)
+                        the exact_rows arithmetic (head.py:19-26) for EVERY vocabulary row, as Head.pick does
+                        for sampling (head.py:62-71): fp32 products, sequential fp32 sum in column order, on the
+                        device from the 12-bit head; the sampler (`ai_b200.sampler`) then draws from them
 """
 import ctypes as C
 
@@ -70,3 +72,15 @@ class Head:
         _lib.call("aib_head8_greedy", ptr(h), T, h.stride(0), C.byref(self._desc), ptr(self.HI), self.V, ptr(self.LO),
                   ptr(dst), ptr(self.ws), self.ws.numel(), stream_ptr())
         return dst[:T]
+
+
+def exact_logits(h, c12, T, out):
+    """out[:T, :V] = exact fp32 logits of every row of the 12-bit head `c12` for h[:T] (fp32 [>=T, D], rows
+    contiguous): the reference's exact_rows arithmetic (head.py:19-26) over the whole vocabulary."""
+    if not (1 <= T <= 16) or h.dtype != torch.float32 or h.dim() != 2 or h.shape[1] != c12["K"] or h.stride(1) != 1:
+        raise ValueError("exact_logits: h must be fp32 [>=T, D] with contiguous rows and 1 <= T <= 16")
+    if out.dtype != torch.float32 or out.dim() != 2 or out.shape[0] < T or out.shape[1] < c12["N"] or out.stride(1) != 1:
+        raise ValueError("exact_logits: out must be fp32 [>=T, >=V] with contiguous rows")
+    _lib.call("aib_head_exact_logits", ptr(h), T, h.stride(0), C.byref(c12.desc()), ptr(out), out.stride(0),
+              stream_ptr())
+    return out[:T]

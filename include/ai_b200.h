@@ -3,7 +3,7 @@
  * Every entry point replaces one Python launcher or kernel launch of the reference engine
  * (karabilo214/AI, `ramvi/engine/ramvi_engine/...`; cited per function). The reference has no native FFI for
  * this path -- its kernels are Triton launched from Python -- so this header is the boundary a binding
- * (ctypes) calls instead of those launchers.
+ * (for example through Python ctypes) calls instead of those launchers.
  *
  * Conventions (same contract as the reference launchers, made explicit for C):
  *  - All device pointers are caller-owned; kernels write their outputs in place.
@@ -110,6 +110,19 @@ void aib_gemv_set_variant(int variant);
 int aib_gemv_c12(const aib_c12* c, const float* x, float* y, int T, int x_stride, int y_stride, int mode,
                  const uint16_t* lnw, float eps, void* ws, size_t ws_bytes, void* stream);
 
+/* ------------------------------------------------------------------------------- prefill GEMM ---- */
+/* Y[m] (+)= W * xin(X[m]) for all M prompt rows at once on the tcgen05 tensor cores, W decoded on the fly
+ * (replaces prefill.matrix, kernels/prefill.py:66-78, with mm_k, prefill_kernels.py:8-27, and the fp32 weight
+ * blocks of dequant_k + exceptions_k, prefill_kernels.py:59-110). X fp32 [M, ldx]; Y fp32 [M, ldy].
+ * xmode 0: xin = X[:, :K]; 2: xin = silu(X[:, :K]) * X[:, K:2K]. lnw (bf16 [K] or NULL): RMSNorm of the rows
+ * first, as the gemvc1 prologue. ymode 0: Y = ...; 1: Y += ...; 3: W's rows come in (gate, up) pairs and
+ * Y[m, i] = silu(row 2i) * row 2i+1 (N even). precision 1: products of bf16(xin) and the exact bf16 weights;
+ * 3: xin split into three bf16 parts (products exact in fp32, fp32 accumulation -- the accuracy of the
+ * reference's fp32 mm_k). ws: aib_gemm_c12_workspace(M, K, precision) bytes, 16-byte aligned (no zero-fill). */
+size_t aib_gemm_c12_workspace(int M, int K, int precision);
+int aib_gemm_c12(const aib_c12* W, const float* X, int M, int ldx, int xmode, const uint16_t* lnw, float eps, float* Y,
+                 int ldy, int ymode, int precision, void* ws, size_t ws_bytes, void* stream);
+
 /* --------------------------------------------------------------------------- int8 vocab head ---- */
 /* Quantised copy of a vocabulary head w (bf16 bits [V, D]) and its error bounds (replaces Head.__init__,
  * generation/head.py:29-50): per row s = float(max|e|/127) (1 if 0), Q = round-half-even(e/s) clamped to
@@ -131,6 +144,11 @@ int aib_head8_bounds(const float* h, int T, int ldh, const int8_t* Q, const floa
  * order, head.py:19-26); out[t] = the argmax, the smallest id on ties. */
 int aib_head8_greedy(const float* h, int T, int ldh, const aib_c12* W, const float* HI, int ldhi, const float* LO,
                      int64_t* out, void* ws, size_t ws_bytes, void* stream);
+/* Exact logits of every vocabulary row for T <= 16 rows of h (fp32 [T, ldh]) from the 12-bit head W [V, D]
+ * (replaces the full-vocabulary exact_rows call of Head.pick when sampling, generation/head.py:19-26 and
+ * :62-71): out[t, v] (row stride ldo) = sum over d in column order of fp32(w[v,d] * h[t,d]), each product
+ * rounded to fp32 and each addition in fp32 -- bit-identical to the reference's Numba loop. */
+int aib_head_exact_logits(const float* h, int T, int ldh, const aib_c12* W, float* out, int ldo, void* stream);
 
 /* ------------------------------------------------------------------------------- norm / embed ---- */
 /* out[t] = w * x[t] * rsqrt(mean(x[t]^2) + eps)   (replaces rmsg_k, tkernels.py:216-225) */

@@ -585,3 +585,50 @@ def test_head8_greedy_vs_oracle(lib, T, ties, exc):
     if exc:
         assert int(c["rp"][34] - c["rp"][33]) > 0 and want[0] == 33
     assert status_clear() == 0
+
+
+# ------------------------------------------------------------------------------ exact vocabulary logits
+def _exact(c, h, T):
+    from ai_b200.head import exact_logits
+    H = torch.from_numpy(np.ascontiguousarray(h, np.float32)).cuda()
+    out = torch.full((T, int(c["N"])), float("nan"), device="cuda")
+    exact_logits(H, c, T, out)
+    torch.cuda.synchronize()
+    return out.cpu().numpy()
+
+
+def test_exact_logits_reference_golden(lib):
+    """Full-vocabulary exact logits are bit-identical to the reference's exact_rows (head.py:19-26) output in
+    the golden file. D = 64 there, so rows and h are zero-padded to the codec's 256-column chunk: the padding
+    adds exact zeros after the 64 real terms and cannot change a nonzero sequential sum."""
+    from ai_b200 import wcomp
+    z = golden("head")
+    w, h, want = z["w"], z["h"], z["exact"]
+    V, D = w.shape
+    T = h.shape[0]
+    wp = np.zeros((V, 256), np.uint16)
+    wp[:, :D] = w
+    hp = np.zeros((T, 256), np.float32)
+    hp[:, :D] = h
+    c = wcomp.compress(from_bits(wp))
+    got = _exact(c, hp, T)
+    nz = want != 0  # the all-zero row 7 sums to +0 either way
+    assert np.array_equal(got[nz].view(np.uint32), want[nz].view(np.uint32))
+    assert (got[~nz] == 0).all()
+    assert status_clear() == 0
+
+
+@pytest.mark.parametrize("V,D,T,exc", [(3000, 512, 1, True), (3001, 768, 3, True), (1000, 256, 8, False),
+                                       (777, 1024, 11, True), (151936, 1024, 1, False)])
+def test_exact_logits_vs_oracle(lib, V, D, T, exc):
+    """Bit-exact against the oracle's exact_rows restatement (fp32 products, sequential fp32 sum), with codec
+    exceptions (tiny and huge values outside the exponent window) on some rows, ragged V and T > 8 (two
+    token passes); the full Qwen3 vocabulary at D = 1024."""
+    wb, h, c = _head_case(300 + V + T, V, D, T, exceptions=exc)
+    if exc:
+        assert int(c["rp"][34] - c["rp"][33]) > 0
+    got = _exact(c, h, T)
+    want = ohead.exact_logits(wb, h)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), \
+        f"{(got != want).sum()} of {got.size} logits differ"
+    assert status_clear() == 0

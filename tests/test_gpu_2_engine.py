@@ -11,9 +11,11 @@ def bits(t):
 
 
 def oracle_for(cfg, rw, maxt):
+    """The oracle decode with the reference head's arithmetic (exact_rows: fp32 products, sequential sum)."""
     from oracle.model import DecodeOracle
     layers = [{k: bits(v) for k, v in rw.layer(i).items()} for i in range(cfg.L)]
-    return DecodeOracle(cfg, layers, bits(rw.embedding()), bits(rw.head()), bits(rw.final_norm()), maxt)
+    return DecodeOracle(cfg, layers, bits(rw.embedding()), bits(rw.head()), bits(rw.final_norm()), maxt,
+                        exact_head=True)
 
 
 @pytest.fixture(scope="module", params=["tiny", "tiny-tied", "small", "small-1k"])
@@ -63,6 +65,30 @@ def test_sampling_reproducible_and_graph_equals_eager(pair):
     c = list(eng.generate(prompt, max_new=12, temperature=0.8, top_p=0.9, top_k=20, seed=7))
     eng.use_graphs = True
     assert a == c
+
+
+def test_sampled_steps_match_head_pick(pair):
+    """Sampling at temperature > 0 picks, at every decode step, the token the reference's Head.pick draws for the
+    same hidden state and the same uniform: exact fp32 logits of the whole vocabulary (exact_rows, head.py:19-26 --
+    here recomputed by the oracle from the engine's own final-norm output) and the sampler's steps with the
+    step's draw from np.random.default_rng(seed). (Whole trajectories are compared with greedy decoding: a sampled
+    trajectory depends on hidden-state rounding wherever a draw lands within ~1e-7 of a CDF boundary.)"""
+    from oracle import head as ohead, sampler as osamp
+    cfg, rw, eng = pair
+    head_bits = bits(rw.head())
+    prompt = [int(t) for t in np.random.default_rng(5).integers(0, cfg.V, 7)]
+    for seed, (temp, k, p) in [(3, (0.6, 20, 0.8)), (4, (1.0, 0, 0.95)), (5, (0.7, 1, 1.0))]:
+        rng = np.random.default_rng(seed)
+        gen = eng.generate(prompt, max_new=16, temperature=temp, top_k=k, top_p=p, seed=seed)
+        next(gen)
+        rng.random()  # the prompt pass's draw
+        n = 0
+        for tok in gen:
+            h = eng.hb[0].cpu().numpy()[None]
+            lg = ohead.exact_logits(head_bits, h)[0]
+            assert tok == osamp.sample_row(lg, temp, k, p, u=rng.random()), (seed, n)
+            n += 1
+        assert n == 15
 
 
 def test_penalties_change_greedy_path(pair):

@@ -1,0 +1,125 @@
+"""Whole-prompt prefill on the GPU: the tcgen05 codec GEMM and the causal prefill attention against the reference
+goldens (`tests/golden/prefill.npz`: mm_k and att_k run by the reference) and the oracle.
+
+Tolerances: precision 3 (three bf16 parts of the activations, exact products, fp32 accumulation) is held to the
+fp32-accumulation bound |y - ref| <= 2e-5 * sum|w||x| + 1e-6, as the GEMV tests; precision 1 (bf16 activations)
+to 8e-3 * sum|w||x| (the activation rounding, 2^-9 relative per product, plus accumulation).
+"""
+import numpy as np
+import pytest
+import torch
+
+from conftest import golden
+from oracle import codec, gemv as ogemv
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def lib(cuda_dev):
+    from ai_b200 import build, _lib
+    build.build()
+    return _lib.lib()
+
+
+def from_bits(a):
+    return torch.from_numpy(np.ascontiguousarray(a).view(np.int16)).view(torch.bfloat16).cuda()
+
+
+def status_clear():
+    from ai_b200 import _lib
+    return _lib.status(clear=True)
+
+
+def check(got, want, mag, precision):
+    rtol = 2e-5 if precision == 3 else 8e-3
+    d = np.abs(np.asarray(got, np.float64) - np.asarray(want, np.float64))
+    bad = d > rtol * mag + 1e-6
+    assert not bad.any(), f"{bad.sum()} of {bad.size} off, max |d| {d.max():.3e}"
+
+
+@pytest.mark.parametrize("precision", [3, 1])
+def test_gemm_matches_reference_mm_golden(lib, precision):
+    """Y = X W^T of the reference's fp32 mm_k on its golden inputs: W [40, 512] with a 1e-30 and a 1e20
+    exception, X [37, 512]; both M and N are ragged (partial tiles)."""
+    from ai_b200 import wcomp, prefill
+    z = golden("prefill")
+    w, x, want = z["rows/w"], z["mm/x"], z["mm/y"]
+    c = wcomp.compress(from_bits(w))
+    assert int(c["ev"].numel()) >= 2
+    X = torch.from_numpy(x).cuda()
+    Y = torch.full((x.shape[0], w.shape[0]), float("nan"), device="cuda")
+    prefill.matrix(X, c, Y, precision=precision)
+    torch.cuda.synchronize()
+    W = codec.bf16_bits_to_f32(w).astype(np.float64)
+    mag = np.abs(x.astype(np.float64)) @ np.abs(W).T
+    check(Y.cpu().numpy(), want, mag, precision)
+    assert status_clear() == 0
+
+
+CASES = [  # (M, N, K, xmode, ymode, rms)
+    (128, 256, 512, 0, 0, False), (37, 300, 1024, 0, 1, False), (300, 384, 256, 0, 0, True),
+    (200, 256, 1024, 2, 1, False), (64, 512, 768, 0, 3, True), (17, 128, 4096, 0, 0, True),
+    (513, 640, 2048, 0, 1, False),
+]
+
+
+@pytest.mark.parametrize("precision", [3, 1])
+@pytest.mark.parametrize("M,N,K,xmode,ymode,rms", CASES)
+def test_gemm_vs_oracle(lib, M, N, K, xmode, ymode, rms, precision):
+    """Ragged M and N tiles, several K blocks, the SiLU-gated input (xmode 2), accumulate (ymode 1), gated output
+    (ymode 3), the RMSNorm prologue, and exceptions on a few rows -- against the float64 oracle."""
+    from ai_b200 import wcomp, prefill
+    g = np.random.default_rng(M * 7 + N + K + ymode + precision)
+    wf = (g.standard_normal((N, K)) * 0.02).astype(np.float32)
+    wf[5, ::131] = 1e-30
+    wf[N - 1, 7] = 5.0
+    wb = codec.f32_to_bf16_bits(wf)
+    xin_cols = 2 * K if xmode == 2 else K
+    x = g.standard_normal((M, xin_cols)).astype(np.float32)
+    lnw = codec.f32_to_bf16_bits((1 + 0.1 * g.standard_normal(K)).astype(np.float32)) if rms else None
+    y0 = g.standard_normal((M, N // 2 if ymode == 3 else N)).astype(np.float32)
+    c = wcomp.compress(from_bits(wb))
+    assert int(c["ev"].numel()) > 0
+    X = torch.from_numpy(x).cuda()
+    Y = torch.from_numpy(y0.copy()).cuda()
+    prefill.matrix(X, c, Y, add=ymode == 1, precision=precision, lnw=from_bits(lnw) if rms else None,
+                   silu_input=xmode == 2, gated=ymode == 3)
+    torch.cuda.synchronize()
+    xe = ogemv.xin(x, K, xmode, lnw, 1e-6).astype(np.float64)
+    W = codec.bf16_bits_to_f32(wb).astype(np.float64)
+    acc = xe @ W.T
+    mag = np.abs(xe) @ np.abs(W).T
+    if ymode == 3:
+        g_, u_ = acc[:, 0::2].astype(np.float32), acc[:, 1::2].astype(np.float32)
+        want = ogemv.silu_mul(g_, u_)
+        check(Y.cpu().numpy(), want, 1.2 * (np.abs(u_) * mag[:, 0::2] + np.abs(g_) * mag[:, 1::2]), precision)
+    else:
+        want = acc + (y0 if ymode == 1 else 0)
+        check(Y.cpu().numpy(), want, mag, precision)
+    assert status_clear() == 0
+
+
+def test_gemm_deterministic_and_large(lib):
+    """A Qwen3-8B-shaped gate/up matrix (24576 x 4096) over 512 prompt rows: repeated launches give identical
+    bits, and sampled rows match the oracle."""
+    from ai_b200 import wcomp, prefill
+    gen = torch.Generator(device="cuda").manual_seed(3)
+    N, K, M = 24576, 4096, 512
+    Wt = (torch.randn(N, K, generator=gen, device="cuda") * 0.02).bfloat16()
+    c = wcomp.compress(Wt)
+    X = torch.randn(M, K, generator=gen, device="cuda")
+    Y1 = torch.empty(M, N, device="cuda")
+    Y2 = torch.empty(M, N, device="cuda")
+    ws = prefill.workspace(M, K, 3)
+    prefill.matrix(X, c, Y1, ws=ws)
+    prefill.matrix(X, c, Y2, ws=ws)
+    torch.cuda.synchronize()
+    assert torch.equal(Y1, Y2)
+    rows = torch.tensor([0, 1, 255, 511], device="cuda")
+    cols = torch.arange(0, N, 97, device="cuda")
+    W64 = Wt[cols].double()
+    want = (X[rows].double() @ W64.T).cpu().numpy()
+    mag = (X[rows].double().abs() @ W64.abs().T).cpu().numpy()
+    check(Y1[rows][:, cols].cpu().numpy(), want, mag, 3)
+    assert status_clear() == 0
