@@ -57,6 +57,7 @@ SIGNATURES = {
     "aib_rope_attn_decode_noalloc": (I32, [P, P, P, P, P, P, P, P, I32, I32, I32, I32, F32, F32, P]),
     "aib_qk_rope_cache": (I32, [P, P, P, P, P, P, P, P, I32, I32, I32, I32, I32, F32, P]),
     "aib_attn_cached": (I32, [P, P, P, P, P, I32, I32, I32, I32, I32, F32, P, SZ, P]),
+    "aib_attn_prefill": (I32, [P, P, P, P, I32, I32, I32, I32, I32, I32, F32, P]),
     "aib_sample_workspace": (SZ, [I32, I32]),
     "aib_sample": (I32, [P, I32, I32, I32, C.POINTER(SampleParams), P, I32, P, P, P, P, SZ, P]),
 }

@@ -745,7 +745,8 @@ template <int MODE, typename XF>
 AIB_DEV void produce_wide(const CUtensorMap* tm8, const CUtensorMap* tme4, uint8_t* ring, uint8_t* meta,
                           int slot_meta, uint64_t* full, uint64_t* empty, volatile int* abort_flag, const ExcTab& et,
                           XF xval, float* y, int N, int tb, int ks0, int n_st, int R, int CW, int KS, int NS,
-                          int nrows, int pw, float* wsp, int* wsc, int maxp, int tiles) {
+                          int nrows, int pw, float* wsp, int* wsc, int maxp, int tiles,
+                          uint32_t stage_bytes = kRowsStage) {
   const int lane = threadIdx.x & 31;
   if (lane == 0) {
     prefetch_tensormap(tm8);
@@ -778,8 +779,8 @@ AIB_DEV void produce_wide(const CUtensorMap* tm8, const CUtensorMap* tme4, uint8
     }
     uint8_t* sm = meta + s * slot_meta;
     if (i < n_st && lane == 0) {  // issue first: the copy is the long pole
-      uint8_t* st = ring + static_cast<size_t>(s) * kRowsStage;
-      mbar_arrive_expect_tx(&full[s], kRowsStage);
+      uint8_t* st = ring + static_cast<size_t>(s) * stage_bytes;
+      mbar_arrive_expect_tx(&full[s], stage_bytes);
       tma_load_3d(st, tm8, &full[s], 0, ks * CW, tile * R);
       tma_load_3d(st + m8_bytes, tme4, &full[s], 0, ks * CW, tile * R);
     }
@@ -1118,8 +1119,6 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
 // 128 + 2i, 129 + 2i of that range. Even and odd rows of the warp use different column blocks, which keeps
 // the 16-byte shared loads of a quarter-warp on distinct banks; B column n = 2*sp + par carries x part sp in
 // the column order of parity par, and a row reads its result from the columns of its own parity.
-constexpr int kTcConsumers = 512;
-constexpr int kTcThreads = kTcConsumers + 32;
 constexpr int kTcSlotMeta = 128 + 256 * 4;
 constexpr int kTcPrologueRecords = 8;  // x records per consumer thread per prologue batch (K <= 16384: one batch)  // per slot: 32-word exception mask, partials [R rows][2*CW warps]
 
@@ -1143,9 +1142,15 @@ AIB_DEV float tc_xval(const uint8_t* xr, int nch, int col) {
   return (parts[0] + parts[1]) + parts[2];
 }
 
-template <int MODE, bool RMS>
-__global__ void __launch_bounds__(kTcThreads, 1)
+// NCW consumer warps: 16 with 48 KB stages (R * CW = 128, one CTA per SM), or 8 with 24 KB stages (R * CW = 64,
+// <= 113 KB of shared memory and 288 threads, so two CTAs share an SM: two of the same launch, or the tail of one
+// launch and the head of the next, whose producer then streams its weights while the previous CTA drains).
+template <int MODE, bool RMS, int NCW>
+__global__ void __launch_bounds__(NCW * 32 + 32, NCW == 16 ? 1 : 2)
     gemv_tc_kernel(const __grid_constant__ CUtensorMap tm8, const __grid_constant__ CUtensorMap tme4, RowsParams p) {
+  constexpr int kTcConsumers = NCW * 32;
+  constexpr int kTcThreads = kTcConsumers + 32;
+  constexpr int kStage = NCW * 2048 * 3 / 2;  // bytes per ring slot: 2048 weights per consumer warp
   extern __shared__ __align__(1024) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty = full + 16;
@@ -1186,7 +1191,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   if (tid >= kTcConsumers) {  // ---------------- producer warp
     auto xval = [&](int col) { return tc_xval(xr, p.nch, col); };
     produce_wide<MODE>(&tm8, &tme4, ring, meta, kTcSlotMeta, full, empty, abort_flag, et, xval, p.y, p.N, tb, ks0,
-                       n_st, R, CW, KS, NS, nrows, PW, p.wsp, p.wsc, p.maxp, p.tiles);
+                       n_st, R, CW, KS, NS, nrows, PW, p.wsp, p.wsc, p.maxp, p.tiles, kStage);
     return;
   }
 
@@ -1324,7 +1329,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int gc = ks * CW + q;
     const uint8_t* sm = meta + s * kTcSlotMeta;
     if (ok && gc < p.nch) {
-      const uint8_t* st = ring + static_cast<size_t>(s) * kRowsStage;
+      const uint8_t* st = ring + static_cast<size_t>(s) * kStage;
       const uint4 LA = *reinterpret_cast<const uint4*>(st + m8A);
       const uint4 HA = *reinterpret_cast<const uint4*>(st + m8A + 128);
       const uint4 EA = *reinterpret_cast<const uint4*>(st + e4A);
@@ -1648,20 +1653,25 @@ static int run_rows(const aib_c12* c, const float* x, float* y, int mode, const 
 
 // Wide-stage tensor-core kernel: R = 32 rows x 4 chunks (K a multiple of 1024) or 16 rows x 8 chunks (K a
 // multiple of 2048, finer row tiles); ENOTSUP when x's three-part records do not fit.
-static int run_tc(const aib_c12* c, const float* x, float* y, int mode, const uint16_t* lnw, float eps, void* ws,
-                  size_t ws_bytes, cudaStream_t s) {
+static int g_variant = 3;  // 0: tensor-core 24 KB-stage kernel, 1: CUDA-core 12 KB stages, 2: CUDA-core 48 KB
+                           // stages, 3 (default): tensor-core wide stages, two CTAs per SM where the shape fits,
+                           // 4: tensor-core 48 KB stages, one CTA per SM
+constexpr size_t kSmemPair = 113 * 1024;  // two CTAs per SM (228 KB per SM, 1 KB reserved per CTA)
+
+template <int NCW>
+static int run_tc_var(const aib_c12* c, const float* x, float* y, int mode, const uint16_t* lnw, float eps, void* ws,
+                      size_t ws_bytes, cudaStream_t s) {
+  constexpr int kThreadsV = NCW * 32 + 32;
+  constexpr size_t kStage = static_cast<size_t>(NCW) * 2048 * 3 / 2;
+  const size_t smem_max = NCW == 16 ? kSmemMax : kSmemPair;
   const int nch = c->K / 256;
-  if (nch % 4) return fail(AIB_ENOTSUP, "aib_gemv_c12: K=%d is not a multiple of 1024", c->K);
-  if (c->base >= 240)  // the exception stand-in (exponent base + 15) would not be finite
-    return fail(AIB_ENOTSUP, "aib_gemv_c12: base %d: exceptions need the exact-path kernel", c->base);
-  if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(lnw) & 7))
-    return fail(AIB_ENOTSUP, "aib_gemv_c12: x / lnw not aligned for vector loads");
-  const int CW = nch % 8 == 0 ? 8 : 4;
-  const int R = 128 / CW, KS = nch / CW;
+  const int CW = NCW == 16 ? (nch % 8 == 0 ? 8 : 4) : 4;
+  const int R = static_cast<int>(kStage / 384) / CW, KS = nch / CW;
   const int tiles = (c->N + R - 1) / R;
+  const int max_grid = NCW == 16 ? sm_count() : 2 * sm_count();
   const StreamK sk = streamk_plan(tiles, KS, R);
-  const bool use_sk = ws && ws_bytes >= sk.bytes && !(reinterpret_cast<uintptr_t>(ws) & 15);
-  const int grid = use_sk ? sk.grid : std::min(tiles, sm_count());
+  const bool use_sk = NCW == 16 && ws && ws_bytes >= sk.bytes && !(reinterpret_cast<uintptr_t>(ws) & 15);
+  const int grid = use_sk ? sk.grid : std::min(tiles, max_grid);
   const int per = static_cast<int>((static_cast<long long>(tiles) * KS + grid - 1) / grid);
   const int rows_max = use_sk ? ((per + KS - 1) / KS + 1) * R : ((tiles + grid - 1) / grid) * R;
   // layout: header + NS slot records, x records (6 bytes per column), row pointers, staged exception
@@ -1673,12 +1683,12 @@ static int run_tc(const aib_c12* c, const float* x, float* y, int mode, const ui
     rps_off = xs_off + static_cast<size_t>(nch) * 1536;
     ecs_off = rps_off + ((static_cast<size_t>(rows_max + 1) * 4 + 127) / 128) * 128;
     const size_t ring_need = ((ecs_off + 1023) / 1024) * 1024;  // staged exception columns take what is left
-    if (ring_need + static_cast<size_t>(NS) * kRowsStage <= kSmemMax) break;
+    if (ring_need + static_cast<size_t>(NS) * kStage <= smem_max) break;
   }
   if (NS < 2) return fail(AIB_ENOTSUP, "aib_gemv_c12: K=%d too large for the tensor-core kernel", c->K);
-  const size_t ring_off = ((kSmemMax - static_cast<size_t>(NS) * kRowsStage) / 1024) * 1024;
+  const size_t ring_off = ((smem_max - static_cast<size_t>(NS) * kStage) / 1024) * 1024;
   const int ecap = static_cast<int>((ring_off - ecs_off) / 8);  // column + correction per staged exception
-  const size_t smem = ring_off + static_cast<size_t>(NS) * kRowsStage;
+  const size_t smem = ring_off + static_cast<size_t>(NS) * kStage;
   CUtensorMap tm8, tme4;
   int rc = make_maps(c, R, CW, &tm8, &tme4);
   if (rc) return rc;
@@ -1691,23 +1701,35 @@ static int run_tc(const aib_c12* c, const float* x, float* y, int mode, const ui
   auto go = [&](auto kernel) -> int {
     const int r2 = allow_smem(kernel, smem);
     if (r2) return r2;
-    return launch(kernel, dim3(grid), dim3(kTcThreads), smem, s, "aib_gemv_c12(T=1, tensor)", tm8, tme4, p);
+    return launch(kernel, dim3(grid), dim3(kThreadsV), smem, s, "aib_gemv_c12(T=1, tensor)", tm8, tme4, p);
   };
   if (lnw) {
-    if (mode == 0) return go(gemv_tc_kernel<0, true>);
-    if (mode == 1) return go(gemv_tc_kernel<1, true>);
-    if (mode == 3) return go(gemv_tc_kernel<3, true>);
-    return go(gemv_tc_kernel<2, true>);
+    if (mode == 0) return go(gemv_tc_kernel<0, true, NCW>);
+    if (mode == 1) return go(gemv_tc_kernel<1, true, NCW>);
+    if (mode == 3) return go(gemv_tc_kernel<3, true, NCW>);
+    return go(gemv_tc_kernel<2, true, NCW>);
   }
-  if (mode == 0) return go(gemv_tc_kernel<0, false>);
-  if (mode == 1) return go(gemv_tc_kernel<1, false>);
-  if (mode == 3) return go(gemv_tc_kernel<3, false>);
-  return go(gemv_tc_kernel<2, false>);
+  if (mode == 0) return go(gemv_tc_kernel<0, false, NCW>);
+  if (mode == 1) return go(gemv_tc_kernel<1, false, NCW>);
+  if (mode == 3) return go(gemv_tc_kernel<3, false, NCW>);
+  return go(gemv_tc_kernel<2, false, NCW>);
 }
 
-static int g_variant = 3;  // 0: tensor-core 24 KB-stage kernel, 1: CUDA-core 12 KB stages, 2: CUDA-core 48 KB
-                           // stages, 3 (default): tensor-core 48 KB stages
-
+// Wide-stage tensor-core kernel: K a multiple of 1024; ENOTSUP when x's three-part records do not fit.
+static int run_tc(const aib_c12* c, const float* x, float* y, int mode, const uint16_t* lnw, float eps, void* ws,
+                  size_t ws_bytes, cudaStream_t s) {
+  const int nch = c->K / 256;
+  if (nch % 4) return fail(AIB_ENOTSUP, "aib_gemv_c12: K=%d is not a multiple of 1024", c->K);
+  if (c->base >= 240)  // the exception stand-in (exponent base + 15) would not be finite
+    return fail(AIB_ENOTSUP, "aib_gemv_c12: base %d: exceptions need the exact-path kernel", c->base);
+  if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(lnw) & 7))
+    return fail(AIB_ENOTSUP, "aib_gemv_c12: x / lnw not aligned for vector loads");
+  if (g_variant == 3 && !ws) {
+    const int rc = run_tc_var<8>(c, x, y, mode, lnw, eps, ws, ws_bytes, s);
+    if (rc != AIB_ENOTSUP) return rc;
+  }
+  return run_tc_var<16>(c, x, y, mode, lnw, eps, ws, ws_bytes, s);
+}
 
 static int run_t1(const aib_c12* c, const float* x, float* y, int mode, const uint16_t* lnw, float eps, void* ws,
                   size_t ws_bytes, cudaStream_t s) {
@@ -1718,11 +1740,11 @@ static int run_t1(const aib_c12* c, const float* x, float* y, int mode, const ui
     if (rc2 != AIB_ENOTSUP) return rc2;
     return fail(AIB_ENOTSUP, "aib_gemv_c12: mode 3 with T == 1 needs K a multiple of 1024 (K=%d)", c->K);
   }
-  if (g_variant == 3) {
+  if (g_variant == 3 || g_variant == 4) {
     const int rc = run_tc(c, x, y, mode, lnw, eps, ws, ws_bytes, s);
     if (rc != AIB_ENOTSUP) return rc;
   }
-  if (g_variant == 2 || g_variant == 3) {
+  if (g_variant == 2 || g_variant == 3 || g_variant == 4) {
     const int rc = run_rows(c, x, y, mode, lnw, eps, ws, ws_bytes, s);
     if (rc != AIB_ENOTSUP) return rc;  // other shapes use the 12 KB-stage kernel
   }

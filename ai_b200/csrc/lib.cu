@@ -7,6 +7,7 @@
 #include "norm.cu"
 #include "attn.cu"
 #include "attn_noalloc.cu"
+#include "pattn.cu"
 #include "sampler.cu"
 #include "head8.cu"
 #include "exact.cu"

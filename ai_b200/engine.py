@@ -16,8 +16,10 @@ steps the exact logits of the whole vocabulary (the reference computes those on 
 the device sampler: one 8-byte read per generated token.
 
 `process(tokens, pos0, ...)` and `generate(prompt, ...)` keep the reference arguments and errors
-(core/engine.py:489-694), with top_k / penalties added; prompts longer than 16 tokens run in 16-token
-batched chunks (the reference's legacy prefill path, core/engine.py:471-480).
+(core/engine.py:489-694), with top_k / penalties added. Prompts longer than 16 tokens that need only the last
+pick run through the whole-prompt prefill (`ai_b200.prefill`: tcgen05 codec GEMMs + causal flash attention,
+the reference's blocked path, core/engine.py:446-487); others run in 16-token batched chunks (the reference's
+legacy path, core/engine.py:471-480).
 """
 import os
 import time
@@ -26,7 +28,7 @@ import numpy as np
 import torch
 
 from .head import Head as Head8, exact_logits
-from . import _lib, wcomp, tkernels, sampler, codecfile
+from . import _lib, wcomp, tkernels, sampler, codecfile, prefill
 from ._lib import ptr, stream_ptr
 from .model import CONFIGS, Ckpt, RandomWeights, Qwen3Config, check_tp, shard_layer
 
@@ -36,7 +38,7 @@ MAXB = 16
 
 class Engine:
     def __init__(self, name, maxt=2048, device="cuda", seed=0, log=print, norm_noise=0.0, weights=None,
-                 graphs=True, head8=True, tp=1, codec_cache=None):
+                 graphs=True, head8=True, tp=1, codec_cache=None, prefill_precision=3):
         """name: an HF Qwen3 folder, or a key of ai_b200.model.CONFIGS / a Qwen3Config for random-init
         weights (N(0, 0.02) matrices, seed `seed`). weights: an explicit weight source (RandomWeights/Ckpt).
         head8: greedy steps without penalties pick through the int8 head (the reference's Head: bounds over an
@@ -48,7 +50,9 @@ class Engine:
         token from the same all-reduced state.
         codec_cache: path of a `codecfile` with this model's encoded matrices (per tensor-parallel rank: the
         path gets a `.tp{N}r{rank}` suffix). Loaded when present and made for this model and layout,
-        written after encoding otherwise."""
+        written after encoding otherwise.
+        prefill_precision: activations of the whole-prompt prefill GEMMs as three bf16 parts (3, fp32-accurate
+        products, the reference's fp32 mm_k) or one (1, bf16, three times the tensor throughput)."""
         if not isinstance(maxt, int) or isinstance(maxt, bool) or maxt < 1:
             raise ValueError("maxt must be a positive integer")
         t0 = time.time()
@@ -69,6 +73,9 @@ class Engine:
             src = Ckpt(name)
             cfg = src.config
         self.cfg = cfg
+        if prefill_precision not in (1, 3):
+            raise ValueError("prefill_precision must be 1 or 3")
+        self.prefill_precision = prefill_precision
         self.tp, self.tp_rank = int(tp), 0
         if self.tp > 1:
             import torch.distributed as dist
@@ -214,6 +221,10 @@ class Engine:
         """Everything that runs on the device for one pass of T tokens (graph body)."""
         tkernels.embed(self.emb, self.ids[:T], self.xb[:T])
         self._layers(T)
+        self._pick(T, prm, rows, penal)
+
+    def _pick(self, T, prm, rows, penal):
+        """Final norm of the last `rows` rows of xb[:T], the head's pick into out_ids, then advance(ids, pos)."""
         r0 = T - rows
         tkernels.rmsg(self.xb[r0:T], self.norm, self.hb[r0:T], self.eps)
         if self.head8 is not None and prm.temperature <= 0 and not penal:
@@ -228,6 +239,24 @@ class Engine:
                                 B=rows, ws=self.sample_ws)
         _lib.call("aib_step_advance", ptr(self.pos), ptr(self.ids), ptr(self.out_ids), T,
                   ptr(self.prior) if penal else None, sampler.PMAX if penal else 0, stream_ptr())
+
+    def _prefill(self, tokens, pos0, prm, us, penal):
+        """Whole-prompt prefill (the reference's blocked path, core/engine.py:446-487 with kernels/prefill.py):
+        every layer runs over all n prompt rows at once -- tcgen05 GEMMs that read each weight matrix once per
+        token tile, causal flash attention -- then the head picks after the last row. Returns [token]."""
+        n = len(tokens)
+        ids = torch.tensor(tokens, dtype=torch.int64).to(self.device)
+        x = torch.empty(n, self.D, device=self.device)
+        tkernels.embed(self.emb, ids, x)
+        bufs = prefill.Buffers(self, n)
+        for l in range(self.L):
+            prefill.layer(self, l, x, pos0, bufs)
+        self.xb[0].copy_(x[n - 1])
+        self.pos.fill_(pos0 + n - 1)  # the head step advances it to pos0 + n
+        if prm.temperature > 0:
+            self.u[0] = us[0]
+        self._pick(1, prm, 1, penal)
+        return self.out_ids[:1].tolist()
 
     def _run(self, T, prm, rows, penal):
         key = (T, rows, penal, prm.temperature, prm.top_k, prm.top_p, prm.repetition_penalty, prm.presence_penalty,
@@ -262,9 +291,12 @@ class Engine:
                 raise ValueError("token id outside the vocabulary")
 
     def _pass(self, tokens, pos0, prm, us, last_only, penal=False):
-        """Run tokens from pos0 in chunks of <= 16; returns the sampled ids (last chunk only if last_only)."""
+        """Run tokens from pos0: whole-prompt prefill for long prompts that need only the last pick, else chunks of
+        <= 16; returns the sampled ids (last chunk only if last_only)."""
         out = []
         n = len(tokens)
+        if last_only and prefill.enabled(n):
+            return self._prefill(tokens, pos0, prm, us, penal)
         c = 0
         while c < n:
             T = min(MAXB, n - c)

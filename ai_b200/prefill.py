@@ -54,3 +54,50 @@ def matrix(x, w, y, add=False, precision=3, lnw=None, eps=1e-6, silu_input=False
               ptr(lnw.view(torch.int16)) if lnw is not None else None, float(eps), ptr(y), y.stride(0), ymode,
               precision, ptr(ws), ws.numel(), stream_ptr())
     return y
+
+
+def attention(q, kc, vc, out, start, h, kv, hd):
+    """Causal attention of the prompt rows q [n, h*hd] (normed + rotated) over the cache kc/vc [kv, maxt, hd] (bf16):
+    row i sees positions 0 .. start + i (prefill_kernels.py:30-56, `attention`)."""
+    n, maxt = q.shape[0], kc.shape[-2]
+    _lib.call("aib_attn_prefill", ptr(q), ptr(kc.view(torch.int16)), ptr(vc.view(torch.int16)), ptr(out), n, int(start),
+              h, kv, hd, maxt, float(hd ** -0.5), stream_ptr())
+    return out
+
+
+class Buffers:
+    """Per-prompt work buffers of `layer` (allocated once per prefill call, reused by every layer)."""
+
+    def __init__(self, eng, n):
+        dev, H, KV, HD = eng.device, eng.H, eng.KV, eng.HD
+        f = lambda c: torch.empty(n, c, device=dev)  # noqa: E731
+        self.qkv, self.q, self.att = f((H + 2 * KV) * HD), f(H * HD), f(H * HD)
+        self.mid = f(eng.FF if eng.gated else 2 * eng.FF)
+        kmax = max(int(c["K"]) for c in eng.W[0].values())
+        self.ws = workspace(n, kmax, eng.prefill_precision, dev)
+
+
+def layer(eng, l, x, start, bufs=None):
+    """One decoder layer over the whole prompt (prefill.py:81-121): x [n, D] fp32 residual rows, updated in place;
+    the layer's K/V rows are written to the cache at positions start .. start + n - 1. Tensor parallel: rank 0
+    adds its partial residual update, the other ranks write theirs, and the engine's all-reduce sums them."""
+    n = x.shape[0]
+    b = bufs or Buffers(eng, n)
+    W, s = eng.W[l], eng.small[l]
+    kc, vc = eng.kv[l, 0], eng.kv[l, 1]
+    H, KV, HD, pr = eng.H, eng.KV, eng.HD, eng.prefill_precision
+    add = eng._add == 1
+    matrix(x, W["qkv"], b.qkv, precision=pr, lnw=s["ln1"], eps=eng.eps, ws=b.ws)
+    eng.pos.fill_(start)
+    tkernels.qk_rope_cache(b.qkv, s["qn"], s["kn"], eng.inv, eng.pos, b.q, kc, vc, eng.maxt, eng.eps, H, KV, HD, n)
+    attention(b.q, kc, vc, b.att, start, H, KV, HD)
+    matrix(b.att, W["o"], x, add=add, precision=pr, ws=b.ws)
+    eng._reduce(x)
+    if eng.gated:  # rows interleaved (gate_i, up_i): the GEMM writes silu(gate) * up directly
+        matrix(x, W["gu"], b.mid, precision=pr, lnw=s["ln2"], eps=eng.eps, gated=True, ws=b.ws)
+        matrix(b.mid, W["down"], x, add=add, precision=pr, ws=b.ws)
+    else:
+        matrix(x, W["gu"], b.mid, precision=pr, lnw=s["ln2"], eps=eng.eps, ws=b.ws)
+        matrix(b.mid, W["down"], x, add=add, precision=pr, silu_input=True, ws=b.ws)
+    eng._reduce(x)
+    return x

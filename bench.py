@@ -11,11 +11,11 @@ explicit flush is needed between steps.
   e2e    = tokens/s through the public API, Engine.generate (host u draw in, host token id out every step).
   roofline = the dominant kernel, the codec GEMV: algorithmic bytes (12-bit planes + CSR) per launch over its
            CUDA-event duration, for the 5 matrices of a layer + the head, against MEASURED_PEAKS.json.
-  cpu_baseline = the oracle port (numpy restatement of the reference path) on a bounded sample: one layer's
-           four codec GEMVs + attention at ctx 4096 and 1/8 of the head, scaled to a whole token.
+  cpu_baseline = the reference's CPU decode path (its Numba CpuLayer kernels + exact_rows head, restated
+           bit-identically in oracle/cpu_ref.py) on the host cores, a bounded sample scaled to one token.
 
-`--impl reference` times that CPU path alone (the reference's path is Python/Triton/Numba and cannot run on
-the GPU box; its CPU restatement stands in) and prints its own JSON line.
+`--impl reference` times that CPU path alone (the reference package itself does not travel to the GPU box; its
+Numba kernels, restated, stand in) and prints its own JSON line.
 """
 import argparse
 import json
@@ -83,38 +83,73 @@ class Clocks:
 
 
 # ---------------------------------------------------------------------------------- CPU baseline
-def cpu_baseline():
-    """Oracle port of one decode token on the host, from a bounded sample (seconds of CPU work)."""
+def cpu_baseline(layer_reps=36, head_frac=4):
+    """The reference's CPU decode path on the host cores: its Numba CpuLayer kernels and exact_rows head
+    (`ramvi_engine/cpu/cpu_layer.py`, `generation/head.py:19-26`, restated bit-identically in oracle/cpu_ref.py --
+    oracle/check_cpu_ref.py compares both in the build container), all host threads. Bounded sample: one Qwen3-8B
+    layer (bf16 weights, fp32 KV cache at ctx 4096) run `layer_reps` times and 1/head_frac of the vocabulary's
+    exact logits, scaled to one token (36 layers + the whole head). Also times BASELINE configs[0], the
+    Qwen3-0.6B MLP block (RMSNorm, gate/up, SiLU*up, down)."""
+    import numba
     import numpy as np
     from ai_b200.model import CONFIGS
-    from oracle import codec, gemv, attn
+    from oracle import codec, cpu_ref, attn
+    numba.set_num_threads(numba.config.NUMBA_NUM_THREADS)
     cfg = CONFIGS["qwen3-8b"]
     rng = np.random.default_rng(0)
     P = cfg.layer_params()
-    mats = {n: codec.compress(codec.f32_to_bf16_bits((rng.standard_normal(P[n]) * 0.02).astype(np.float32)))
-            for n in ("qkv", "o", "gu", "down")}
-    ln = codec.f32_to_bf16_bits(np.ones(cfg.D, np.float32))
-    hn = codec.f32_to_bf16_bits(np.ones(cfg.HD, np.float32))
-    kc = codec.f32_to_bf16_bits(rng.standard_normal((cfg.KV, CTX + 1, cfg.HD)).astype(np.float32))
-    vc = codec.f32_to_bf16_bits(rng.standard_normal((cfg.KV, CTX + 1, cfg.HD)).astype(np.float32))
-    head_rows = cfg.V // 8
-    head = codec.compress(codec.f32_to_bf16_bits((rng.standard_normal((head_rows, cfg.D)) * 0.02).astype(np.float32)))
+    W = {n: codec.f32_to_bf16_bits((rng.standard_normal(P[n], dtype=np.float32) * 0.02)) for n in P}
+    one_d, one_h = np.ones(cfg.D, np.float32), np.ones(cfg.HD, np.float32)
+    lay = cpu_ref.CpuLayer(W["qkv"], W["o"], W["gu"], W["down"], one_d, one_d, one_h, one_h, cfg, CTX + 8)
+    lay.K[:, :CTX] = rng.standard_normal((cfg.KV, CTX, cfg.HD), dtype=np.float32)
+    lay.V[:, :CTX] = rng.standard_normal((cfg.KV, CTX, cfg.HD), dtype=np.float32)
     inv = attn.rope_inv(cfg.HD, cfg.theta)
-    x = rng.standard_normal(cfg.D).astype(np.float32)
+    x = rng.standard_normal((1, cfg.D), dtype=np.float32)
+    rows = cfg.V // head_frac
+    hw = codec.f32_to_bf16_bits(rng.standard_normal((rows, cfg.D), dtype=np.float32) * 0.02)
+    toks, trow, lg = np.arange(rows), np.zeros(rows, np.int64), np.empty(rows, np.float32)
+    h = rng.standard_normal((1, cfg.D), dtype=np.float32)
+    lay(x.copy(), CTX, inv)  # JIT compile outside the timed region
+    cpu_ref.exact_rows(hw, toks, trow, h, lg)
     t0 = time.perf_counter()
-    qkv = gemv.gemvc1(x, mats["qkv"], np.zeros(P["qkv"][0], np.float32), 0, ln, cfg.eps)
-    a = attn.rope_attn(qkv, hn, hn, inv, CTX, kc, vc, cfg.H, cfg.KV, cfg.HD, cfg.eps)
-    x = gemv.gemvc1(a, mats["o"], x, 1)
-    gu = gemv.gemvc1(x, mats["gu"], np.zeros(P["gu"][0], np.float32), 0, ln, cfg.eps)
-    x = gemv.gemvc1(gu, mats["down"], x, 2)
+    for _ in range(layer_reps):
+        lay(x, CTX, inv)
     t1 = time.perf_counter()
-    gemv.gemvc1(x, head, np.zeros(head_rows, np.float32), 0, ln, cfg.eps)
+    cpu_ref.exact_rows(hw, toks, trow, h, lg)
     t2 = time.perf_counter()
-    sec = (t1 - t0) * cfg.L + (t2 - t1) * 8
-    return {"value": 1.0 / sec, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
-            "sample": f"1 of {cfg.L} layers (4 codec GEMVs + attention at ctx {CTX}) and 1/8 of the head, numpy "
-                      f"oracle port (decode on the fly, float64 matvec), scaled to one token; "
-                      f"measured {t2 - t0:.1f} s"}
+    sec = (t1 - t0) / layer_reps * cfg.L + (t2 - t1) * head_frac
+    # configs[0]: Qwen3-0.6B MLP block (gu fused [6144, 1024], down [1024, 3072]), x bf16 N(0, 1)
+    c6 = CONFIGS["qwen3-0.6b"]
+    g0 = np.random.default_rng(0)
+    gate = codec.f32_to_bf16_bits((g0.standard_normal((c6.FF, c6.D)) * 0.02).astype(np.float32))
+    up = codec.f32_to_bf16_bits((g0.standard_normal((c6.FF, c6.D)) * 0.02).astype(np.float32))
+    down = codec.f32_to_bf16_bits((g0.standard_normal((c6.D, c6.FF)) * 0.02).astype(np.float32))
+    gu = np.concatenate([gate, up])
+    xb = codec.bf16_bits_to_f32(codec.f32_to_bf16_bits(g0.standard_normal((1, c6.D)).astype(np.float32)))
+
+    def block():
+        hh = np.empty_like(xb)
+        cpu_ref.rms_rows(xb, np.ones(c6.D, np.float32), hh, np.float32(1e-6))
+        g2 = np.empty((1, 2 * c6.FF), np.float32)
+        cpu_ref.matmat16(gu, hh, g2, False)
+        m = np.empty((1, c6.FF), np.float32)
+        cpu_ref.silu_mul(g2, m, c6.FF)
+        y = np.zeros((1, c6.D), np.float32)
+        cpu_ref.matmat16(down, m, y, False)
+    block()
+    bt = min(_timed(block) for _ in range(20))
+    return {"value": 1.0 / sec, "unit": "tok/s", "cores": numba.get_num_threads(), "kind": "port",
+            "sample": f"{layer_reps} runs of one Qwen3-8B layer (bf16 weights, fp32 KV at ctx {CTX}) and 1/{head_frac} "
+                      f"of the exact-logit head, scaled to one token; the reference's Numba CpuLayer/exact_rows "
+                      f"kernels restated bit-identically in oracle/cpu_ref.py; measured {t2 - t0:.2f} s",
+            "config0_mlp_block_us": round(bt * 1e6, 1),
+            "config0_mlp_block_gbs": round((gu.size + down.size) * 2 / bt / 1e9, 1)}
+
+
+def _timed(fn):
+    t = time.perf_counter()
+    fn()
+    return time.perf_counter() - t
 
 
 # ------------------------------------------------------------------------------------ GPU arm
@@ -384,8 +419,8 @@ def main():
     ap.add_argument("--micro", choices=["gemv", "gemv_down", "gemv_qkv", "gemv_o", "attn", "sample", "head8"],
                     default=None,
                     help="time one kernel alone on a small case (for ncu) instead of the decode benchmark")
-    ap.add_argument("--gemv-variant", type=int, default=None, choices=[0, 1, 2, 3],
-                    help="codec GEMV kernel for --micro: 0 tensor-core 24 KB stages, 1 CUDA-core 12 KB stages, 2 CUDA-core 48 KB stages, 3 tensor-core 48 KB stages (default)")
+    ap.add_argument("--gemv-variant", type=int, default=None, choices=[0, 1, 2, 3, 4],
+                    help="codec GEMV kernel for --micro: 0 tensor-core 24 KB stages, 1 CUDA-core 12 KB stages, 2 CUDA-core 48 KB stages, 3 tensor-core wide stages with two CTAs per SM where they fit (default), 4 tensor-core 48 KB stages, one CTA per SM")
     ap.add_argument("--streamk", action="store_true", help="--micro gemv*: pass the stream-K workspace")
     ap.add_argument("--greedy", action="store_true",
                     help="greedy decoding (the int8 head's exact-candidate pick) instead of the default sampling")
@@ -404,16 +439,13 @@ def main():
     if args.impl == "reference":
         if rank != 0:
             return
-        secs = []
-        for _ in range(max(1, min(args.steps, 1))):
-            t = time.perf_counter()
-            cb = cpu_baseline()
-            secs.append(time.perf_counter() - t)
+        cb = cpu_baseline(layer_reps=max(36, min(args.steps, 72)))
         v = cb["value"]
         print(json.dumps({"impl": "reference", "metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": args.gpus,
                           "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
                           "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
-                          "config": {"workload": "Qwen3-8B decode bs1, 12-bit weights, ctx 4096 (CPU port)",
+                          "config": {"workload": "Qwen3-8B decode bs1, ctx 4096 (the reference's Numba CPU path, "
+                                                 "bf16 weights)",
                                      "model": "qwen3-8b", "global_batch": 1, "seq_len": CTX},
                           "cpu_baseline": cb, "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0,
                                                       "d2h_bytes_per_step": 0}}))

@@ -188,6 +188,12 @@ int aib_qk_rope_cache(const float* qkv, const uint16_t* qn, const uint16_t* kn, 
  * prefill_kernels.py:30-56): token t attends 0..*pos + t. q [T, H*HD] -> out [T, H*HD]. */
 int aib_attn_cached(const float* q, const uint16_t* kc, const uint16_t* vc, const int64_t* pos, float* out, int T,
                     int H, int KV, int HD, int maxt, float scale, void* ws, size_t ws_bytes, void* stream);
+/* Causal attention of a whole prompt (replaces att_k / attention, prefill_kernels.py:30-56): row i of q
+ * [n, H*HD] (position start + i, already normed and rotated) attends cache positions 0 .. start + i of its
+ * group; out [n, H*HD]. Tensor-core flash attention (q and probabilities as three bf16 parts). H / KV in
+ * {1, 2, 4, 8}; HD 64 or 128; start + n <= maxt. */
+int aib_attn_prefill(const float* q, const uint16_t* kc, const uint16_t* vc, float* out, int n, int start, int H, int KV,
+                     int HD, int maxt, float scale, void* stream);
 
 /* ---------------------------------------------------------------------------------- sampler ---- */
 /* Logits-in sampler (replaces GGUFEngine._pick, core/gengine.py:452-469, with Constraint.apply,

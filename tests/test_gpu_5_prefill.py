@@ -123,3 +123,63 @@ def test_gemm_deterministic_and_large(lib):
     mag = (X[rows].double().abs() @ W64.abs().T).cpu().numpy()
     check(Y1[rows][:, cols].cpu().numpy(), want, mag, 3)
     assert status_clear() == 0
+
+
+# --------------------------------------------------------------------------------- prefill attention
+def bits(t):
+    return t.contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
+
+
+def test_prefill_attention_matches_reference_golden(lib):
+    """att_k's own output on its golden inputs (H 4, KV 2, HD 64, 37 prompt rows after 20 cached positions)."""
+    from ai_b200 import prefill
+    z = golden("prefill")
+    H, KV, HD, maxt, n, start = (int(v) for v in z["att/cfg"])
+    q = torch.from_numpy(z["att/q"]).cuda()
+    out = torch.full((n, H * HD), float("nan"), device="cuda")
+    prefill.attention(q, from_bits(z["att/kc"]), from_bits(z["att/vc"]), out, start, H, KV, HD)
+    torch.cuda.synchronize()
+    np.testing.assert_allclose(out.cpu().numpy(), z["att/out"], rtol=2e-4, atol=2e-5)
+    assert status_clear() == 0
+
+
+@pytest.mark.parametrize("H,KV,HD,n,start", [(32, 8, 128, 300, 0), (16, 8, 128, 129, 17), (8, 1, 128, 70, 5),
+                                             (4, 4, 64, 33, 2), (64, 8, 128, 517, 1000)])
+def test_prefill_attention_vs_oracle(lib, H, KV, HD, n, start):
+    """Causal attention of n prompt rows after `start` cached positions, GQA ratios 1..8, ragged query tiles,
+    against the oracle's exact softmax."""
+    from ai_b200 import prefill
+    from oracle import attn as oattn
+    g = np.random.default_rng(n + H + start)
+    maxt = start + n + 3
+    q = g.standard_normal((n, H * HD)).astype(np.float32)
+    kc = codec.f32_to_bf16_bits(g.standard_normal((KV, maxt, HD)).astype(np.float32))
+    vc = codec.f32_to_bf16_bits(g.standard_normal((KV, maxt, HD)).astype(np.float32))
+    out = torch.full((n, H * HD), float("nan"), device="cuda")
+    prefill.attention(torch.from_numpy(q).cuda(), from_bits(kc), from_bits(vc), out, start, H, KV, HD)
+    torch.cuda.synchronize()
+    rows = np.unique(np.r_[0, 1, n // 2, n - 1, g.integers(0, n, 12)])
+    ref = np.stack([oattn.prefill_attention(q[r:r + 1], kc, vc, start + int(r), H, KV, HD)[0] for r in rows])
+    np.testing.assert_allclose(out.cpu().numpy()[rows], ref, rtol=2e-4, atol=2e-5)
+    assert status_clear() == 0
+
+
+# ------------------------------------------------------------------------------------ engine prefill
+@pytest.mark.parametrize("name", ["small", "small-1k"])
+def test_engine_prefill_matches_chunked_path(lib, name, monkeypatch):
+    """A 53-token prompt through the whole-prompt prefill gives the same next token as the 16-token chunk path
+    (the reference's legacy path), a KV cache within one bf16 ulp of it, and the same greedy continuation."""
+    from ai_b200.engine import Engine
+    from ai_b200.model import CONFIGS, RandomWeights
+    cfg = CONFIGS[name]
+    rw = RandomWeights(cfg, seed=11, norm_noise=0.1, std=0.05)
+    prompt = [int(t) for t in np.random.default_rng(9).integers(0, cfg.V, 53)]
+    a = Engine(cfg, maxt=128, weights=rw, log=None)
+    b = Engine(cfg, maxt=128, weights=rw, log=None)
+    ta = list(a.generate(prompt, max_new=12))
+    monkeypatch.setenv("AIB_PREFILL", "legacy")
+    tb = list(b.generate(prompt, max_new=12))
+    assert ta == tb
+    ka, kb = bits(a.kv[:, :, :, :53]).astype(np.int32), bits(b.kv[:, :, :, :53]).astype(np.int32)
+    assert np.abs(ka - kb).max() <= 1
+    assert status_clear() == 0
