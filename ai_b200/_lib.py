@@ -52,9 +52,13 @@ SIGNATURES = {
     "aib_rmsnorm": (I32, [P, P, P, I32, I32, F32, P]),
     "aib_embed": (I32, [P, P, I32, I32, I32, P, P]),
     "aib_step_advance": (I32, [P, P, P, I32, P, I32, P]),
+    "aib_batch_advance": (I32, [P, P, P, I32, P]),
     "aib_attn_workspace": (SZ, [I32, I32, I32, I32, I32]),
     "aib_rope_attn_decode": (I32, [P, P, P, P, P, P, P, P, I32, I32, I32, I32, F32, F32, P, SZ, P]),
     "aib_rope_attn_decode_noalloc": (I32, [P, P, P, P, P, P, P, P, I32, I32, I32, I32, F32, F32, P]),
+    "aib_attn_batch_workspace": (SZ, [I32, I32, I32, I32, I32]),
+    "aib_rope_attn_decode_batch": (I32, [P, I32, P, P, P, P, P, P, I64, P, I32, I32, I32, I32, I32, I32, F32, F32, P,
+                                         SZ, P]),
     "aib_qk_rope_cache": (I32, [P, P, P, P, P, P, P, P, I32, I32, I32, I32, I32, F32, P]),
     "aib_attn_cached": (I32, [P, P, P, P, P, I32, I32, I32, I32, I32, F32, P, SZ, P]),
     "aib_attn_prefill": (I32, [P, P, P, P, I32, I32, I32, I32, I32, I32, F32, P]),

@@ -417,16 +417,25 @@ AIB_DEV void merge_write(Smem<HD>& sm, float* stage, const float* parts, int S, 
 }
 
 // ------------------------------------------------------------------------------ fused T = 1 step
+// blockIdx.z = b selects one of B independent sequences (batched decode): its qkv row (qkv + b * qkv_ld), its
+// position pos_p[b], its caches (kc / vc + b * kv_bstride elements) and its output row (out + b * out_ld); the
+// split partials and tickets of (b, group) use slot b * KV + g of the workspace.
 template <int HD, int G>
 __global__ void __launch_bounds__(kThreads)
     rope_attn_kernel(const float* __restrict__ qkv, const uint16_t* __restrict__ qn, const uint16_t* __restrict__ kn,
                      const float* __restrict__ inv, const int64_t* __restrict__ pos_p, uint16_t* kc, uint16_t* vc,
                      float* __restrict__ out, int H, int KV, int maxt, float eps, float scale, float* ws_part,
-                     int* ws_cnt) {
+                     int* ws_cnt, int qkv_ld, long long kv_bstride, int out_ld) {
   __shared__ Smem<HD> sm;
   extern __shared__ __align__(128) uint8_t ring[];
-  const int s = blockIdx.x, S = gridDim.x, g = blockIdx.y;
+  const int s = blockIdx.x, S = gridDim.x, g = blockIdx.y, b = blockIdx.z;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int slot = b * KV + g;
+  qkv += static_cast<size_t>(b) * qkv_ld;
+  pos_p += b;
+  kc += static_cast<size_t>(b) * kv_bstride;
+  vc += static_cast<size_t>(b) * kv_bstride;
+  out += static_cast<size_t>(b) * out_ld;
   uint16_t* kg = kc + static_cast<size_t>(g) * maxt * HD;
   uint16_t* vg = vc + static_cast<size_t>(g) * maxt * HD;
   // constant inputs before the grid dependency resolves: RoPE frequencies, q / k norm weights, and an L2
@@ -493,13 +502,13 @@ __global__ void __launch_bounds__(kThreads)
     sc = warp_sum(sc);
     if (lane == 0) sm.cur_score[h] = sc * scale;
   }
-  float* part = ws_part + (static_cast<size_t>(g) * S + s) * G * (HD + 2);
+  float* part = ws_part + (static_cast<size_t>(slot) * S + s) * G * (HD + 2);
   attend_range<HD, G>(sm, ring, kg, vg, j0, j1, scale, part);
   // ordered merge by the last CTA of the group
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) {
-    const int old = atomicAdd(&ws_cnt[g], 1);
+    const int old = atomicAdd(&ws_cnt[slot], 1);
     sm.last = (old == S - 1);
   }
   __syncthreads();
@@ -507,9 +516,9 @@ __global__ void __launch_bounds__(kThreads)
     __threadfence();
     if (threadIdx.x < GMAX) sm.ones[threadIdx.x] = 1.0f;  // the current token enters with weight 1
     __syncthreads();
-    merge_write<HD>(sm, reinterpret_cast<float*>(ring), ws_part + static_cast<size_t>(g) * S * G * (HD + 2), S, G,
+    merge_write<HD>(sm, reinterpret_cast<float*>(ring), ws_part + static_cast<size_t>(slot) * S * G * (HD + 2), S, G,
                     sm.cur_score, sm.ones, sm.vcur, out + static_cast<size_t>(g) * G * HD);
-    if (threadIdx.x == 0) ws_cnt[g] = 0;
+    if (threadIdx.x == 0) ws_cnt[slot] = 0;
   }
 }
 
@@ -685,7 +694,37 @@ int aib_rope_attn_decode(const float* qkv, const uint16_t* qn, const uint16_t* k
   const size_t smem = HD == 128 ? attn::ring_bytes<128>() : attn::ring_bytes<64>();
   return attn::launch_g<attn::RopeAttnSel>(HD, H / KV, dim3(S, KV), smem, static_cast<cudaStream_t>(stream),
                                            "aib_rope_attn_decode", qkv, qn, kn, inv, pos, kc, vc, out, H, KV, maxt,
-                                           eps, scale, part, cnt);
+                                           eps, scale, part, cnt, (H + 2 * KV) * HD, 0LL, H * HD);
+}
+
+size_t aib_attn_batch_workspace(int H, int KV, int HD, int maxt, int B) {
+  (void)maxt;
+  if (H <= 0 || KV <= 0 || B <= 0) return 0;
+  return attn::ws_bytes_for(H, KV, HD, B);
+}
+
+int aib_rope_attn_decode_batch(const float* qkv, int qkv_ld, const uint16_t* qn, const uint16_t* kn, const float* inv,
+                               const int64_t* pos, uint16_t* kc, uint16_t* vc, long long kv_bstride, float* out,
+                               int out_ld, int B, int H, int KV, int HD, int maxt, float eps, float scale, void* ws,
+                               size_t ws_bytes, void* stream) {
+  int rc = attn::check_heads(H, KV, HD);
+  if (rc) return rc;
+  if (!qkv || !qn || !kn || !inv || !pos || !kc || !vc || !out || maxt <= 0 || B < 1 ||
+      static_cast<long long>(B) * KV > attn::kMaxSlots || qkv_ld < (H + 2 * KV) * HD || out_ld < H * HD ||
+      (B > 1 && kv_bstride < static_cast<long long>(KV) * maxt * HD) || kv_bstride < 0)
+    return fail(AIB_EINVAL, "aib_rope_attn_decode_batch: bad arguments");
+  if (((reinterpret_cast<uintptr_t>(kc) | reinterpret_cast<uintptr_t>(vc)) & 15) || (kv_bstride * 2) % 16)
+    return fail(AIB_EINVAL, "aib_rope_attn_decode_batch: KV caches must be 16-byte aligned");
+  const size_t need = attn::ws_bytes_for(H, KV, HD, B);
+  if (!ws || ws_bytes < need)
+    return fail(AIB_EWORKSPACE, "aib_rope_attn_decode_batch: workspace %zu < %zu bytes", ws_bytes, need);
+  const int S = attn::splits(KV, B, H / KV, HD);
+  int* cnt = static_cast<int*>(ws);
+  float* part = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + attn::kCntBytes);
+  const size_t smem = HD == 128 ? attn::ring_bytes<128>() : attn::ring_bytes<64>();
+  return attn::launch_g<attn::RopeAttnSel>(HD, H / KV, dim3(S, KV, B), smem, static_cast<cudaStream_t>(stream),
+                                           "aib_rope_attn_decode_batch", qkv, qn, kn, inv, pos, kc, vc, out, H, KV,
+                                           maxt, eps, scale, part, cnt, qkv_ld, kv_bstride, out_ld);
 }
 
 int aib_qk_rope_cache(const float* qkv, const uint16_t* qn, const uint16_t* kn, const float* inv, const int64_t* pos,

@@ -76,6 +76,16 @@ __global__ void advance_kernel(int64_t* pos, int64_t* next_ids, const int64_t* o
   pdl_trigger();
 }
 
+// Batched decode: sequence b's sampled id becomes its next input and its position advances by one.
+__global__ void batch_advance_kernel(int64_t* pos, int64_t* next_ids, const int64_t* out_ids, int B) {
+  pdl_wait();
+  for (int b = threadIdx.x; b < B; b += blockDim.x) {
+    next_ids[b] = out_ids[b];
+    pos[b] += 1;
+  }
+  pdl_trigger();
+}
+
 }  // namespace norm
 }  // namespace aib
 
@@ -100,6 +110,12 @@ int aib_step_advance(int64_t* pos, int64_t* next_ids, const int64_t* out_ids, in
   if (!pos || !next_ids || !out_ids || T <= 0 || n_prior < 0) return fail(AIB_EINVAL, "aib_step_advance: bad arguments");
   return launch(norm::advance_kernel, dim3(1), dim3(32), 0, static_cast<cudaStream_t>(stream), "aib_step_advance", pos,
                 next_ids, out_ids, T, prior, n_prior);
+}
+
+int aib_batch_advance(int64_t* pos, int64_t* next_ids, const int64_t* out_ids, int B, void* stream) {
+  if (!pos || !next_ids || !out_ids || B <= 0) return fail(AIB_EINVAL, "aib_batch_advance: bad arguments");
+  return launch(norm::batch_advance_kernel, dim3(1), dim3(32), 0, static_cast<cudaStream_t>(stream),
+                "aib_batch_advance", pos, next_ids, out_ids, B);
 }
 
 }  // extern "C"

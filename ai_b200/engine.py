@@ -83,8 +83,11 @@ class Engine:
                 raise ValueError("tp > 1 needs an initialised torch.distributed group of that size")
             check_tp(cfg, self.tp)
             self.tp_rank = dist.get_rank()
-        # per-rank shapes (the whole model when tp == 1)
+        # per-rank shapes (the whole model when tp == 1); Vs: the rank's share of the vocabulary head
         self.L, self.D, self.HD, self.V = cfg.L, cfg.D, cfg.HD, cfg.V
+        if self.tp > 1 and cfg.V % self.tp:
+            raise ValueError(f"vocabulary {cfg.V} does not split over {self.tp} ranks")
+        self.Vs = cfg.V // self.tp
         self.H, self.KV, self.FF = cfg.H // self.tp, cfg.KV // self.tp, cfg.FF // self.tp
         self.eps, self.maxt, self.log = cfg.eps, maxt, log
         self.eos = set(cfg.eos)
@@ -111,7 +114,7 @@ class Engine:
                 lw = src.layer_small(i)
                 self.small.append({k: lw[k].to(dev).contiguous() for k in ("ln1", "ln2", "qn", "kn")})
             self.head = mats["head"]
-            hw = wcomp.decompress(self.head) if head8 else None  # lossless: the head's bf16 weights
+            hw = wcomp.decompress(self.head) if head8 and self.tp == 1 else None  # lossless: the bf16 head
         else:
             for i in range(self.L):
                 lw = src.layer(i)
@@ -123,13 +126,16 @@ class Engine:
                 self.small.append({k: lw[k].to(dev).contiguous() for k in ("ln1", "ln2", "qn", "kn")})
                 del lw
             hw = self.emb if cfg.tied else src.head().to(dev)
+            if self.tp > 1:  # vocabulary-sharded head: this rank's rows only
+                hw = hw[self.tp_rank * self.Vs:(self.tp_rank + 1) * self.Vs].contiguous()
             self.head = wcomp.compress(hw)
             if cache:
                 torch.cuda.synchronize()
                 out = {f"layers.{i}.{n}": self.W[i][n] for i in range(self.L) for n in MATS}
                 out["head"] = self.head
                 codecfile.save(cache, out, cmeta)
-        self.head8 = Head8(hw, self.head, TM=MAXB) if head8 else None
+        # the int8 greedy head needs the whole vocabulary on one GPU; tensor-parallel ranks pick from gathered logits
+        self.head8 = Head8(hw, self.head, TM=MAXB) if head8 and self.tp == 1 else None
         del hw
         self.norm = src.final_norm().to(dev).contiguous()
         torch.cuda.synchronize()
@@ -140,6 +146,9 @@ class Engine:
         self.xb, self.hb = f(self.D), f(self.D)
         self.qkvb, self.qb, self.attb, self.gub = f((H + 2 * KV) * HD), f(H * HD), f(H * HD), f(2 * self.FF)
         self.logits = torch.zeros(MAXB, self.V, device=dev)
+        if self.tp > 1:  # this rank's logit columns, and every rank's gathered ([tp, rows, Vs] per call)
+            self.logits_part = torch.zeros(MAXB, self.Vs, device=dev)
+            self.logits_all = torch.zeros(self.tp * MAXB * self.Vs, device=dev)
         self.pos = torch.zeros(1, dtype=torch.int64, device=dev)
         self.ids = torch.zeros(MAXB, dtype=torch.int64, device=dev)
         self.out_ids = torch.zeros(MAXB, dtype=torch.int64, device=dev)
@@ -233,12 +242,25 @@ class Engine:
         else:
             # sampling (or penalties): exact logits of the whole vocabulary, as Head.pick computes them for
             # sampling (head.py:62-71), then the device sampler
-            exact_logits(self.hb[r0:T], self.head, rows, self.logits[r0:T])
+            self._exact(r0, T, rows)
             sampler.sample_into(self.logits[r0:T], self.out_ids[r0:T], prm,
                                 self.u[:rows] if prm.temperature > 0 else None, self.prior if penal else None, None,
                                 B=rows, ws=self.sample_ws)
         _lib.call("aib_step_advance", ptr(self.pos), ptr(self.ids), ptr(self.out_ids), T,
                   ptr(self.prior) if penal else None, sampler.PMAX if penal else 0, stream_ptr())
+
+    def _exact(self, r0, T, rows):
+        """Exact logits of rows hb[r0:T] into logits[r0:T]. Tensor parallel: each rank computes its vocabulary slice
+        and one all-gather gives every rank the whole row, so all ranks sample the same token."""
+        if self.tp == 1:
+            exact_logits(self.hb[r0:T], self.head, rows, self.logits[r0:T])
+            return
+        import torch.distributed as dist
+        exact_logits(self.hb[r0:T], self.head, rows, self.logits_part[:rows])
+        n = self.tp * rows * self.Vs
+        dist.all_gather_into_tensor(self.logits_all[:n], self.logits_part[:rows].reshape(-1))
+        self.logits[r0:T].view(rows, self.tp, self.Vs).copy_(
+            self.logits_all[:n].view(self.tp, rows, self.Vs).transpose(0, 1))
 
     def _prefill(self, tokens, pos0, prm, us, penal):
         """Whole-prompt prefill (the reference's blocked path, core/engine.py:446-487 with kernels/prefill.py):
@@ -452,3 +474,138 @@ class Engine:
         12-bit head + the bf16 K/V rows attended (ctx positions) + the current K/V written."""
         kv = self.L * 2 * self.KV * (ctx + 1) * self.HD * 2
         return self.weight_bytes + self.head_bytes + kv
+
+    # ------------------------------------------------------------------------------ batched decode
+    def generate_batch(self, prompts, max_new=256, temperature=0.0, top_p=1.0, top_k=0, seed=None):
+        """Decode B <= 16 independent sequences together (no reference counterpart: the reference engine decodes
+        one sequence). Each prompt is prefilled into its own KV cache; then every step reads each weight matrix
+        once for all B tokens. Returns B token lists of max_new tokens each (no early stop at EOS, so the batch
+        stays aligned). Uniform draws come from np.random.default_rng(seed), B per step in sequence order."""
+        B = len(prompts)
+        if not 1 <= B <= MAXB:
+            raise ValueError(f"generate_batch takes 1..{MAXB} prompts")
+        for p in prompts:
+            if not p:
+                raise ValueError("an empty prompt is not supported; pass BOS or text")
+            self._validate_process(list(p), 0)
+            if len(p) + max_new > self.maxt:
+                raise ValueError(f"prompt + max_new longer than the context {self.maxt}")
+        bt = self._batch(B)
+        prm = sampler.params(temperature, top_k, top_p)
+        rng = np.random.default_rng(seed)
+        out = [[] for _ in range(B)]
+        for b, p in enumerate(prompts):
+            us = [rng.random()] if temperature > 0 else None
+            out[b].append(bt.prefill(b, list(p), prm, us))
+        for _ in range(max_new - 1):
+            if temperature > 0:
+                bt.u.copy_(torch.from_numpy(rng.random(B)))
+            bt.run(prm)
+            for b, t in enumerate(bt.out_ids.tolist()):
+                out[b].append(t)
+        return out
+
+    def _batch(self, B):
+        bt = getattr(self, "_bt", None)
+        if bt is None or bt.B != B:
+            self._bt = bt = Batch(self, B)
+        return bt
+
+
+class Batch:
+    """Device state of B sequences decoded together by one engine: per-sequence KV caches [B, L, 2, KV, maxt, HD]
+    (bf16), positions and input ids, and [B, n] work rows. A step is one CUDA graph: the batched codec GEMVs (rows =
+    sequences, each weight read once), the batched fused attention (each sequence at its own position over its own
+    cache), the head's pick for B rows and a per-sequence advance."""
+
+    def __init__(self, eng, B):
+        self.eng, self.B = eng, B
+        dev, H, KV, HD = eng.device, eng.H, eng.KV, eng.HD
+        self.kv = torch.zeros(B, eng.L, 2, KV, eng.maxt, HD, dtype=torch.bfloat16, device=dev)
+        self.pos = torch.zeros(B, dtype=torch.int64, device=dev)
+        self.ids = torch.zeros(B, dtype=torch.int64, device=dev)
+        self.out_ids = torch.zeros(B, dtype=torch.int64, device=dev)
+        self.u = torch.zeros(B, dtype=torch.float64, device=dev)
+        f = lambda n: torch.zeros(B, n, device=dev)  # noqa: E731
+        self.xb, self.hb = f(eng.D), f(eng.D)
+        self.qkvb, self.attb, self.gub = f((H + 2 * KV) * HD), f(H * HD), f(2 * eng.FF)
+        self.logits = torch.zeros(B, eng.V, device=dev)
+        self.ws = torch.zeros(_lib.lib().aib_attn_batch_workspace(H, KV, HD, eng.maxt, B), dtype=torch.uint8,
+                              device=dev)
+        self.sample_ws = sampler.workspace(B, eng.V, dev)
+        self.seq_stride = eng.L * 2 * KV * eng.maxt * HD  # elements between two sequences' caches
+        self.graphs = {}
+
+    def prefill(self, b, tokens, prm, us):
+        """Prompt of sequence b into its cache (whole-prompt prefill); returns its first token."""
+        eng = self.eng
+        own = eng.kv
+        eng.kv = self.kv[b]
+        try:
+            tok = eng._prefill(tokens, 0, prm, us, False)[0]
+        finally:
+            eng.kv = own
+        self.pos[b] = len(tokens)
+        self.ids[b] = tok
+        return tok
+
+    def _attn(self, l):
+        eng, s = self.eng, self.eng.small[l]
+        H, KV, HD = eng.H, eng.KV, eng.HD
+        _lib.call("aib_rope_attn_decode_batch", ptr(self.qkvb), self.qkvb.stride(0), ptr(s["qn"].view(torch.int16)),
+                  ptr(s["kn"].view(torch.int16)), ptr(eng.inv), ptr(self.pos), ptr(self.kv[0, l, 0].view(torch.int16)),
+                  ptr(self.kv[0, l, 1].view(torch.int16)), self.seq_stride, ptr(self.attb), self.attb.stride(0), self.B,
+                  H, KV, HD, eng.maxt, float(eng.eps), float(eng.scale), ptr(self.ws), self.ws.numel(), stream_ptr())
+
+    def _step(self, prm):
+        eng, B = self.eng, self.B
+        x, h = self.xb, self.hb
+        tkernels.embed(eng.emb, self.ids, x)
+        for l in range(eng.L):
+            W, s = eng.W[l], eng.small[l]
+            tkernels.rmsg(x, s["ln1"], h, eng.eps)
+            wcomp.gemvc_tc(h, W["qkv"], self.qkvb, 0, B)
+            self._attn(l)
+            wcomp.gemvc_tc(self.attb, W["o"], x, eng._add, B)
+            eng._reduce(x)
+            tkernels.rmsg(x, s["ln2"], h, eng.eps)
+            if eng.gated:
+                wcomp.gemvc_tc(h, W["gu"], self.gub, 3, B)
+                wcomp.gemvc_tc(self.gub, W["down"], x, eng._add, B)
+            else:
+                wcomp.gemvc_tc(h, W["gu"], self.gub, 0, B)
+                if not eng._add:
+                    x.zero_()
+                wcomp.gemvc_tc(self.gub, W["down"], x, 2, B)
+            eng._reduce(x)
+        tkernels.rmsg(x, eng.norm, h, eng.eps)
+        if eng.head8 is not None and prm.temperature <= 0:
+            eng.head8.pick(h, B, out=self.out_ids)
+        else:
+            if eng.tp > 1:
+                raise NotImplementedError("batched decode runs on one GPU (or as replicas)")
+            exact_logits(h, eng.head, B, self.logits)
+            sampler.sample_into(self.logits, self.out_ids, prm, self.u if prm.temperature > 0 else None, None, None,
+                                B=B, ws=self.sample_ws)
+        _lib.call("aib_batch_advance", ptr(self.pos), ptr(self.ids), ptr(self.out_ids), B, stream_ptr())
+
+    def run(self, prm):
+        key = (prm.temperature, prm.top_k, prm.top_p)
+        if not self.eng.use_graphs:
+            self._step(prm)
+            return
+        g = self.graphs.get(key)
+        if g is None:
+            self._step(prm)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, capture_error_mode="thread_local"):
+                self._step(prm)
+            self.graphs[key] = g
+            return
+        g.replay()
+
+    def bytes_per_step(self, ctx):
+        """Algorithmic HBM bytes of one batched step at context ctx: weights once, each sequence's K/V."""
+        eng = self.eng
+        kv = self.B * eng.L * 2 * eng.KV * (ctx + 1) * eng.HD * 2
+        return eng.weight_bytes + eng.head_bytes + kv

@@ -6,8 +6,8 @@ temperature 0.6, on one B200 per rank. The 10.4 GB of weights streamed per step 
 explicit flush is needed between steps.
 
   value  = tokens/s with inputs resident: K CUDA-graph replays timed with CUDA events (ids / position chained
-           on the device), max over ranks, summed over ranks (N > 1 runs independent replicas, one sequence
-           per GPU: "scaling": "weak").
+           on the device), max over ranks. N > 1 runs one sequence tensor-parallel over the N ranks (BASELINE
+           configs[2], "scaling": "strong"); --replicas runs N independent sequences instead ("weak").
   e2e    = tokens/s through the public API, Engine.generate (host u draw in, host token id out every step).
   roofline = the dominant kernel, the codec GEMV: algorithmic bytes (12-bit planes + CSR) per launch over its
            CUDA-event duration, for the 5 matrices of a layer + the head, against MEASURED_PEAKS.json.
@@ -198,6 +198,74 @@ def gemv_roofline(eng, peak, reps=20):
             "algorithmic_bytes_per_launch": per_launch, "avg_launch_us": round(sec / len(launches) * 1e6, 2)}
 
 
+def bench_prefill(eng, n=2048, reps=3):
+    """Whole-prompt prefill of an n-token random prompt (BASELINE configs[4] runs 2048 tokens): tokens/s, and the
+    tensor-pipe fraction of the linear layers' algorithmic FLOPs (2 * n * params, counted once -- the default
+    precision-3 GEMMs execute three bf16 MMAs per product) against the measured bf16 peak."""
+    import numpy as np
+    import torch
+    from ai_b200 import sampler
+    toks = [int(t) for t in np.random.default_rng(5).integers(0, eng.V, n)]
+    prm = sampler.params()
+    eng._prefill(toks, 0, prm, None, False)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        eng._prefill(toks, 0, prm, None, False)
+    e1.record()
+    torch.cuda.synchronize()
+    sec = e0.elapsed_time(e1) / 1e3 / reps
+    params = sum(int(c["N"]) * int(c["K"]) for c in eng.W[0].values()) * eng.L
+    lin = 2.0 * n * params
+    att = 2.0 * 2 * eng.L * eng.H * eng.HD * n * (n + 1) / 2
+    tf = bf16_peak()
+    return {"tokens": n, "ms": round(sec * 1e3, 2), "tok_s": round(n / sec, 1), "precision": eng.prefill_precision,
+            "linear_tflops": round(lin / sec / 1e12, 1), "attention_tflops": round(att / sec / 1e12, 2),
+            "tensor_frac_algorithmic": round(lin / sec / 1e12 / tf[0], 4),
+            "tensor_frac_executed": round(eng.prefill_precision * lin / sec / 1e12 / tf[0], 4),
+            "peak_tflops": tf[0], "peak_kind": tf[1]}
+
+
+def bench_batch(eng, B=8, steps=16, warmup=3):
+    """BASELINE configs[2] at batch 8: B sequences, each with its own KV cache pre-filled N(0, 1) to 4096
+    positions, decoded together (one weight read per step), top-k 20 / top-p 0.8 / T 0.6."""
+    import torch
+    from ai_b200 import sampler
+    bt = eng._batch(B)
+    g = torch.Generator(device=eng.device).manual_seed(77)
+    bt.kv[:, :, :, :, :CTX].normal_(generator=g)
+    bt.ids.random_(0, eng.V, generator=g)
+    bt.u.uniform_(generator=g)
+    prm = sampler.params(**SAMPLING)
+    bt.pos.fill_(CTX)
+    for _ in range(warmup):
+        bt.run(prm)
+    bt.pos.fill_(CTX)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        bt.run(prm)
+    e1.record()
+    torch.cuda.synchronize()
+    sec = e0.elapsed_time(e1) / 1e3 / steps
+    nb = bt.bytes_per_step(CTX + steps // 2)
+    hbm = peaks()
+    out = {"batch": B, "ms_per_step": round(sec * 1e3, 3), "tok_s": round(B / sec, 1), "bytes_per_step": nb,
+           "achieved_gbs": round(nb / sec / 1e9, 1), "frac": round(nb / sec / 1e9 / hbm[0], 4)}
+    del eng._bt
+    return out
+
+
+def bf16_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["bf16_tflops"]), "measured"
+    return 1590.0, "fallback"
+
+
 def gpu_arm(args, rank, world):
     import torch
     import torch.distributed as dist
@@ -207,7 +275,7 @@ def gpu_arm(args, rank, world):
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
     torch.cuda.set_device(dev)
     maxt = CTX + 2 * (args.steps + args.warmup) + 64
-    tp = world if args.tp else 1
+    tp = 1 if args.replicas else world
     # replicas: one sequence per GPU (own weights seed); tensor parallel: one sequence over all ranks
     seq = 0 if tp > 1 else rank
     eng = Engine("qwen3-8b", maxt=maxt, seed=seq, log=None, tp=tp)
@@ -264,13 +332,17 @@ def gpu_arm(args, rank, world):
     step_bytes = eng.bytes_per_token(CTX + args.steps // 2)
     from ai_b200._lib import status
     dev_status = status()
+    extra = {}
+    if rank == 0 and tp == 1 and not args.no_extra:
+        extra["prefill"] = bench_prefill(eng)
+        extra["batch"] = bench_batch(eng)
     if tp > 1:
         eng.close()  # its graphs hold NCCL calls: release them before the process group goes
     if rank != 0:
         return None
-    # embed, 5 per layer (qkv GEMV, attention, o, gate/up, down), head GEMV, sampler (2 phases), advance;
-    # greedy: final norm, bounds, candidates, exact pick in place of head + sampler
-    launches_per_step = 1 + 5 * eng.L + (4 if args.greedy else 1 + 2) + 1
+    # embed, 5 per layer (qkv GEMV, attention, o, gate/up, down), final norm, then sampling: exact logits +
+    # sampler (2 phases), or greedy: bounds, candidates, exact pick; advance
+    launches_per_step = 1 + 5 * eng.L + 1 + 3 + 1
     out = {
         "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4), "higher_is_better": True,
@@ -289,6 +361,7 @@ def gpu_arm(args, rank, world):
                           "frac": round(step_bytes * value / nseq / 1e9 / peak[0], 4)},
         "gpu_launches": launches_per_step * args.steps,
         "clocks": ck.summary(), "clocks_e2e": ck2.summary(), "device_status": dev_status,
+        **extra,
     }
     if not args.no_cpu:
         out["cpu_baseline"] = cpu_baseline()
@@ -390,6 +463,30 @@ def micro(args):
                           "bounds_GBps": round(nbytes / ub / 1e3, 1), "pick_us": round(up, 2),
                           "device_status": _lib.status()}))
         return
+    if args.micro in ("gemm", "gemm1"):  # prefill GEMM, gate/up-shaped [24576, 4096] over 2048 prompt rows
+        from ai_b200 import prefill
+        g = torch.Generator(device="cuda").manual_seed(0)
+        c = wcomp.compress((torch.randn(24576, 4096, generator=g, device="cuda") * 0.02).bfloat16())
+        M, prec = 2048, (3 if args.micro == "gemm" else 1)
+        X = torch.randn(M, 4096, generator=g, device="cuda")
+        Y = torch.empty(M, 24576, device="cuda")
+        ws = prefill.workspace(M, 4096, prec)
+        us = timed(lambda: prefill.matrix(X, c, Y, precision=prec, ws=ws), max(args.steps, 1))
+        fl = 2.0 * M * 24576 * 4096
+        print(json.dumps({"micro": args.micro, "M": M, "N": 24576, "K": 4096, "precision": prec,
+                          "us_per_launch": round(us, 1), "tflops_algorithmic": round(fl / us / 1e6, 1),
+                          "tflops_executed": round(prec * fl / us / 1e6, 1), "device_status": _lib.status()}))
+        return
+    if args.micro == "exact":  # exact logits of the whole Qwen3-8B vocabulary for one row
+        from ai_b200.head import exact_logits
+        g = torch.Generator(device="cuda").manual_seed(0)
+        c = wcomp.compress((torch.randn(151936, 4096, generator=g, device="cuda") * 0.02).bfloat16())
+        h = torch.randn(1, 4096, generator=g, device="cuda")
+        out = torch.empty(1, 151936, device="cuda")
+        us = timed(lambda: exact_logits(h, c, 1, out), max(args.steps, 1))
+        print(json.dumps({"micro": "exact", "bytes": c.nbytes, "us_per_launch": round(us, 1),
+                          "GBps": round(c.nbytes / us / 1e3, 1), "device_status": _lib.status()}))
+        return
     if args.micro in ("attn", "sample"):
         run, nbytes = (micro_attn if args.micro == "attn" else micro_sample)(args)
         us = timed(run, max(args.steps, 1))
@@ -416,7 +513,8 @@ def micro(args):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--micro", choices=["gemv", "gemv_down", "gemv_qkv", "gemv_o", "attn", "sample", "head8"],
+    ap.add_argument("--micro", choices=["gemv", "gemv_down", "gemv_qkv", "gemv_o", "attn", "sample", "head8", "gemm",
+                                        "gemm1", "exact"],
                     default=None,
                     help="time one kernel alone on a small case (for ncu) instead of the decode benchmark")
     ap.add_argument("--gemv-variant", type=int, default=None, choices=[0, 1, 2, 3, 4],
@@ -424,13 +522,17 @@ def main():
     ap.add_argument("--streamk", action="store_true", help="--micro gemv*: pass the stream-K workspace")
     ap.add_argument("--greedy", action="store_true",
                     help="greedy decoding (the int8 head's exact-candidate pick) instead of the default sampling")
-    ap.add_argument("--tp", action="store_true",
-                    help="with --gpus N under torchrun: one sequence, tensor parallel over the N ranks (default: N replicas)")
+    ap.add_argument("--tp", action="store_true", help="tensor parallel over the N ranks (the default for N > 1)")
+    ap.add_argument("--replicas", action="store_true",
+                    help="with --gpus N under torchrun: N independent sequences, one per GPU, instead of one sequence "
+                         "tensor-parallel over the N ranks")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=256)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="skip the prefill (2048-token prompt) and batch-8 decode measurements of the default run")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

@@ -160,6 +160,8 @@ int aib_embed(const uint16_t* emb, const int64_t* ids, int T, int D, int V, floa
  * recent ids for the sampler's penalties). Keeps a captured decode step free of host copies. */
 int aib_step_advance(int64_t* pos, int64_t* next_ids, const int64_t* out_ids, int T, int32_t* prior, int n_prior,
                      void* stream);
+/* Batched decode bookkeeping: next_ids[b] = out_ids[b]; pos[b] += 1 for b < B. */
+int aib_batch_advance(int64_t* pos, int64_t* next_ids, const int64_t* out_ids, int B, void* stream);
 
 /* -------------------------------------------------------------------------------- attention ---- */
 /* T == 1 fused step (replaces rope_attn_k, tkernels.py:164-213): QK-RMSNorm + RoPE of q and k,
@@ -179,6 +181,15 @@ int aib_rope_attn_decode(const float* qkv, const uint16_t* qn, const uint16_t* k
 int aib_rope_attn_decode_noalloc(const float* qkv, const uint16_t* qn, const uint16_t* kn, const float* inv,
                                  const int64_t* pos, uint16_t* kc, uint16_t* vc, float* out, int H, int KV, int HD,
                                  int maxt, float eps, float scale, void* stream);
+/* Batched decode of B independent sequences (one token each; no reference counterpart -- the reference decodes one
+ * sequence, core/engine.py:538-694 -- it is the rope_attn_k step of each): sequence b's qkv row at qkv + b * qkv_ld,
+ * its position pos[b], its caches at kc / vc + b * kv_bstride elements, its output row at out + b * out_ld.
+ * ws >= aib_attn_batch_workspace(...), zero-filled once. */
+size_t aib_attn_batch_workspace(int H, int KV, int HD, int maxt, int B);
+int aib_rope_attn_decode_batch(const float* qkv, int qkv_ld, const uint16_t* qn, const uint16_t* kn, const float* inv,
+                               const int64_t* pos, uint16_t* kc, uint16_t* vc, long long kv_bstride, float* out,
+                               int out_ld, int B, int H, int KV, int HD, int maxt, float eps, float scale, void* ws,
+                               size_t ws_bytes, void* stream);
 /* Batched prologue (replaces qk_rope_cache_k, tkernels.py:82-120): q of tokens t < T normed+rotated into
  * q [T, H*HD]; k, v rows written at *pos + t. */
 int aib_qk_rope_cache(const float* qkv, const uint16_t* qn, const uint16_t* kn, const float* inv, const int64_t* pos,

@@ -148,3 +148,15 @@ def test_speculative_greedy_equals_plain():
     assert st2["accepted"] < st2["drafted"]
     with pytest.raises(NotImplementedError):
         list(tgt.generate(prompt, max_new=4, draft=same, temperature=0.7))
+
+
+def test_batch_decode_equals_single_sequences(pair):
+    """Sequences decoded together (one weight read per step for all of them, each attending its own cache at its
+    own position) give each sequence's own greedy tokens."""
+    cfg, rw, eng = pair
+    g = np.random.default_rng(12)
+    prompts = [[int(t) for t in g.integers(0, cfg.V, n)] for n in (5, 20, 33)]
+    alone = [list(eng.generate(p, max_new=10)) for p in prompts]
+    assert eng.generate_batch(prompts, max_new=10) == alone
+    from ai_b200._lib import status
+    assert status() == 0
