@@ -34,6 +34,7 @@ SIGNATURES = {
     "aib_last_error": (C.c_char_p, []),
     "aib_set_pdl": (None, [I32]),
     "aib_status_read": (I32, [C.POINTER(I32), I32]),
+    "aib_debug_knob": (I32, [I32, I32]),
     "aib_c12_encode_host": (I32, [P, I32, I32, P, P, P, P, P, P, P, P, I64]),
     "aib_c12_encode_workspace": (SZ, [I32]),
     "aib_c12_encode_planes": (I32, [P, I32, I32, P, P, P, P, P, SZ, P]),
@@ -53,6 +54,7 @@ SIGNATURES = {
     "aib_embed": (I32, [P, P, I32, I32, I32, P, P]),
     "aib_step_advance": (I32, [P, P, P, I32, P, I32, P]),
     "aib_batch_advance": (I32, [P, P, P, I32, P]),
+    "aib_allreduce_oneshot": (I32, [P, I32, I32, P, P, I32, I32, P, P]),
     "aib_attn_workspace": (SZ, [I32, I32, I32, I32, I32]),
     "aib_rope_attn_decode": (I32, [P, P, P, P, P, P, P, P, I32, I32, I32, I32, F32, F32, P, SZ, P]),
     "aib_rope_attn_decode_noalloc": (I32, [P, P, P, P, P, P, P, P, I32, I32, I32, I32, F32, F32, P]),

@@ -26,6 +26,14 @@ AIB_DEV void set_status(int code) { atomicCAS(&g_aib_status, 0, code); }
 // spin limit for bounded waits: each try_wait may suspend for a hardware-defined window, so this bounds
 // a wait to well under a second while being ~1e6x longer than any legitimate wait in these kernels.
 constexpr uint32_t kSpinLimit = 1u << 22;
+// Test knobs (aib_debug_knob): a smaller spin limit, so a test can make a wait run out in milliseconds, and a
+// switch under which the wide GEMV's producer issues no copies (its stages never fill). Zero = off.
+__device__ uint32_t g_aib_spin_override = 0;
+__device__ int g_aib_withhold_copies = 0;
+AIB_DEV uint32_t spin_limit() {
+  const uint32_t o = g_aib_spin_override;  // written by the host between launches only
+  return o ? o : kSpinLimit;
+}
 
 // ------------------------------------------------------------------------------------------- PDL
 AIB_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
@@ -72,7 +80,9 @@ AIB_DEV bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
 }
 
 AIB_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, int code) {
-  for (uint32_t i = 0; i < kSpinLimit; ++i)
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint32_t lim = spin_limit();
+  for (uint32_t i = 0; i < lim; ++i)
     if (mbar_try_wait(bar, parity)) return true;
   set_status(code);
   return false;

@@ -114,7 +114,8 @@ AIB_DEV uint32_t merge_sm_e(uint32_t a, uint32_t b) {  // (a & 0x807F807F) | (b 
 
 // Bounded wait on a barrier phase; gives up early once another thread has aborted.
 AIB_DEV bool wait_b(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int code) {
-  for (uint32_t i = 0; i < kSpinLimit; ++i) {
+  if (mbar_try_wait(bar, parity)) return true;  // the common case reads no limit
+  for (uint32_t i = 0, lim = spin_limit(); i < lim; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 63) == 63 && *abort_flag) return false;
   }

@@ -169,7 +169,8 @@ AIB_DEV float dec1(uint32_t m, uint32_t code, uint32_t base) {
 
 // Bounded consumer wait on a full-stage barrier; gives up early once another thread has aborted.
 AIB_DEV bool wait_full(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
-  for (uint32_t i = 0; i < kSpinLimit; ++i) {
+  if (mbar_try_wait(bar, parity)) return true;  // the common case reads no limit
+  for (uint32_t i = 0, lim = spin_limit(); i < lim; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 63) == 63 && *abort_flag) return false;
   }
@@ -205,7 +206,7 @@ AIB_DEV void produce(const CUtensorMap* tm8, const CUtensorMap* tme4, uint8_t* r
     const int s = it % NS;
     if (it >= NS) {
       bool ok = false;
-      for (uint32_t i = 0; i < kSpinLimit && !ok; ++i) {
+      for (uint32_t i = 0, lim = spin_limit(); i < lim && !ok; ++i) {
         ok = mbar_try_wait(&empty[s], ((it / NS) - 1) & 1);
         if (!ok && *abort_flag) break;
       }
@@ -279,7 +280,7 @@ AIB_DEV void produce_pairs(const CUtensorMap* tm8, const CUtensorMap* tme4, uint
     }
     idle = progressed ? 0 : idle + 1;
     if (!progressed) __nanosleep(64);  // both halves full: back off instead of taking issue slots from them
-    if (idle > kSpinLimit) {
+    if (idle > spin_limit()) {
       set_status(AIB_DEV_TIMEOUT_EMPTY);
       *abort_flag = 1;
     }
@@ -761,7 +762,7 @@ AIB_DEV void produce_wide(const CUtensorMap* tm8, const CUtensorMap* tme4, uint8
       bool ok = true;
       if (lane == 0) {
         ok = false;
-        for (uint32_t k = 0; k < kSpinLimit && !ok; ++k) {
+        for (uint32_t k = 0, lim = spin_limit(); k < lim && !ok; ++k) {
           ok = mbar_try_wait(&empty[s], (round - 1) & 1);
           if (!ok && (k & 63) == 63 && *abort_flag) break;
         }
@@ -778,7 +779,7 @@ AIB_DEV void produce_wide(const CUtensorMap* tm8, const CUtensorMap* tme4, uint8
       }
     }
     uint8_t* sm = meta + s * slot_meta;
-    if (i < n_st && lane == 0) {  // issue first: the copy is the long pole
+    if (i < n_st && lane == 0 && !g_aib_withhold_copies) {  // issue first: the copy is the long pole
       uint8_t* st = ring + static_cast<size_t>(s) * stage_bytes;
       mbar_arrive_expect_tx(&full[s], stage_bytes);
       tma_load_3d(st, tm8, &full[s], 0, ks * CW, tile * R);

@@ -11,3 +11,4 @@
 #include "sampler.cu"
 #include "head8.cu"
 #include "exact.cu"
+#include "allreduce.cu"

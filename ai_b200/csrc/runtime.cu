@@ -117,6 +117,21 @@ const char* aib_last_error(void) { return aib::t_err; }
 
 void aib_set_pdl(int enabled) { aib::g_pdl = enabled ? 1 : 0; }
 
+int aib_debug_knob(int knob, int value) {
+  cudaError_t e = cudaSuccess;
+  if (knob == 1) {
+    const uint32_t v = value > 0 ? static_cast<uint32_t>(value) : 0u;
+    e = cudaMemcpyToSymbol(aib::g_aib_spin_override, &v, sizeof(v));
+  } else if (knob == 2) {
+    const int v = value ? 1 : 0;
+    e = cudaMemcpyToSymbol(aib::g_aib_withhold_copies, &v, sizeof(v));
+  } else {
+    return aib::fail(AIB_EINVAL, "aib_debug_knob: unknown knob %d", knob);
+  }
+  if (e != cudaSuccess) return aib::fail(AIB_ECUDA, "aib_debug_knob: %s", cudaGetErrorString(e));
+  return AIB_OK;
+}
+
 int aib_status_read(int* out, int clear) {
   if (!out) return aib::fail(AIB_EINVAL, "aib_status_read: out is NULL");
   cudaError_t e = cudaMemcpyFromSymbol(out, aib::g_aib_status, sizeof(int));

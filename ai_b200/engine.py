@@ -155,11 +155,12 @@ class Engine:
         self.u = torch.zeros(MAXB, dtype=torch.float64, device=dev)
         self.prior = torch.full((1, sampler.PMAX), -1, dtype=torch.int32, device=dev)
         self.sample_ws = sampler.workspace(MAXB, self.cfg.V, dev)
-        self.gemv_ws = wcomp.gemv_workspace(list(self.W[0].values()) + [self.head], dev)  # same shapes every layer
+        self.tws = prefill.workspace(MAXB, max(int(c["K"]) for c in self.W[0].values()), 3, dev)  # T <= 16 passes
         wsz = max(_lib.lib().aib_attn_workspace(H, KV, HD, maxt, t) for t in range(1, MAXB + 1))
         self.ws = torch.zeros(wsz, dtype=torch.uint8, device=dev)
         self.use_graphs = graphs
         self.graphs = {}
+        self._setup_allreduce()
         self.ctx = []
         self.scale = HD ** -0.5
         self.weight_bytes = sum(c.nbytes for w in self.W for c in w.values())
@@ -180,9 +181,43 @@ class Engine:
         return 1 if self.tp_rank == 0 else 0
 
     def _reduce(self, x):
+        """Sum x over the tensor-parallel ranks: the one-shot peer-memory all-reduce for decode-sized blocks,
+        NCCL for larger ones (whole-prompt prefill) or when symmetric memory is unavailable."""
         if self.tp > 1:
+            a = self.ar
+            if a is not None and x.numel() <= a["nmax"]:
+                _lib.call("aib_allreduce_oneshot", ptr(x), x.numel(), a["nmax"], a["bufs"], a["flags"], self.tp_rank,
+                          self.tp, ptr(a["epoch"]), stream_ptr())
+                return
             import torch.distributed as dist
             dist.all_reduce(x)
+
+    def _setup_allreduce(self):
+        """Symmetric buffers (two slots of MAXB * D floats) and flag words mapped on every rank, for the one-shot
+        all-reduce (AIB_ALLREDUCE=nccl keeps NCCL for every exchange)."""
+        self.ar = None
+        if self.tp == 1 or os.environ.get("AIB_ALLREDUCE", "oneshot") != "oneshot":
+            return
+        import ctypes as C
+        import torch.distributed as dist
+        try:
+            import torch.distributed._symmetric_memory as symm_mem
+            nmax = MAXB * self.D
+            buf = symm_mem.empty(2 * nmax, dtype=torch.float32, device=self.device)
+            hb = symm_mem.rendezvous(buf, dist.group.WORLD)
+            flg = symm_mem.empty(self.tp, dtype=torch.int32, device=self.device)
+            flg.zero_()
+            hf = symm_mem.rendezvous(flg, dist.group.WORLD)
+            bufs = (C.c_int64 * self.tp)(*[int(v) for v in hb.buffer_ptrs])
+            flags = (C.c_int64 * self.tp)(*[int(v) for v in hf.buffer_ptrs])
+        except Exception as exc:  # no symmetric memory on this system: NCCL for every exchange
+            if self.log:
+                self.log(f"one-shot all-reduce unavailable ({exc}); using NCCL")
+            return
+        torch.cuda.synchronize()
+        dist.barrier()
+        self.ar = {"buf": buf, "flg": flg, "hb": hb, "hf": hf, "nmax": nmax, "bufs": bufs, "flags": flags,
+                   "epoch": torch.zeros(1, dtype=torch.int32, device=self.device)}
 
     def _layers(self, T):
         H, KV, HD = self.H, self.KV, self.HD
@@ -206,24 +241,23 @@ class Engine:
                     wcomp.gemvc1(self.gub[0], W["down"], x, 2)
                 self._reduce(self.xb[:1])
             else:
-                x, h = self.xb[:T], self.hb[:T]
-                tkernels.rmsg(x, s["ln1"], h, self.eps)
-                wcomp.gemvc_tc(h, W["qkv"], self.qkvb[:T], 0, T)
+                # T <= 16 rows: the tcgen05 codec GEMM (RMSNorm and SiLU gate fused, three bf16 parts of the
+                # activations so the products are fp32-exact): each weight matrix is read once for all rows
+                x, pr, ws, add = self.xb[:T], 3, self.tws, self._add == 1
+                prefill.matrix(x, W["qkv"], self.qkvb[:T], precision=pr, lnw=s["ln1"], eps=self.eps, ws=ws)
                 tkernels.qk_rope_cache(self.qkvb[:T], s["qn"], s["kn"], self.inv, self.pos, self.qb[:T], kc, vc,
                                        self.maxt, self.eps, H, KV, HD, T)
                 tkernels.attn(self.qb[:T], kc, vc, self.pos, self.attb[:T], self.maxt, self.scale, H, KV, HD, T,
                               ws=self.ws)
-                wcomp.gemvc_tc(self.attb[:T], W["o"], x, self._add, T)
+                prefill.matrix(self.attb[:T], W["o"], x, add=add, precision=pr, ws=ws)
                 self._reduce(x)
-                tkernels.rmsg(x, s["ln2"], h, self.eps)
                 if self.gated:
-                    wcomp.gemvc_tc(h, W["gu"], self.gub[:T], 3, T)
-                    wcomp.gemvc_tc(self.gub[:T], W["down"], x, self._add, T)
+                    prefill.matrix(x, W["gu"], self.gub[:T], precision=pr, lnw=s["ln2"], eps=self.eps, gated=True,
+                                   ws=ws)
+                    prefill.matrix(self.gub[:T], W["down"], x, add=add, precision=pr, ws=ws)
                 else:
-                    wcomp.gemvc_tc(h, W["gu"], self.gub[:T], 0, T)
-                    if not self._add:
-                        x.zero_()
-                    wcomp.gemvc_tc(self.gub[:T], W["down"], x, 2, T)
+                    prefill.matrix(x, W["gu"], self.gub[:T], precision=pr, lnw=s["ln2"], eps=self.eps, ws=ws)
+                    prefill.matrix(self.gub[:T], W["down"], x, add=add, precision=pr, silu_input=True, ws=ws)
                 self._reduce(x)
 
     def _step(self, T, prm, rows, penal):
@@ -561,22 +595,19 @@ class Batch:
         eng, B = self.eng, self.B
         x, h = self.xb, self.hb
         tkernels.embed(eng.emb, self.ids, x)
+        ws, add = eng.tws, eng._add == 1
         for l in range(eng.L):
             W, s = eng.W[l], eng.small[l]
-            tkernels.rmsg(x, s["ln1"], h, eng.eps)
-            wcomp.gemvc_tc(h, W["qkv"], self.qkvb, 0, B)
+            prefill.matrix(x, W["qkv"], self.qkvb, precision=3, lnw=s["ln1"], eps=eng.eps, ws=ws)
             self._attn(l)
-            wcomp.gemvc_tc(self.attb, W["o"], x, eng._add, B)
+            prefill.matrix(self.attb, W["o"], x, add=add, precision=3, ws=ws)
             eng._reduce(x)
-            tkernels.rmsg(x, s["ln2"], h, eng.eps)
             if eng.gated:
-                wcomp.gemvc_tc(h, W["gu"], self.gub, 3, B)
-                wcomp.gemvc_tc(self.gub, W["down"], x, eng._add, B)
+                prefill.matrix(x, W["gu"], self.gub, precision=3, lnw=s["ln2"], eps=eng.eps, gated=True, ws=ws)
+                prefill.matrix(self.gub, W["down"], x, add=add, precision=3, ws=ws)
             else:
-                wcomp.gemvc_tc(h, W["gu"], self.gub, 0, B)
-                if not eng._add:
-                    x.zero_()
-                wcomp.gemvc_tc(self.gub, W["down"], x, 2, B)
+                prefill.matrix(x, W["gu"], self.gub, precision=3, lnw=s["ln2"], eps=eng.eps, ws=ws)
+                prefill.matrix(self.gub, W["down"], x, add=add, precision=3, silu_input=True, ws=ws)
             eng._reduce(x)
         tkernels.rmsg(x, eng.norm, h, eng.eps)
         if eng.head8 is not None and prm.temperature <= 0:

@@ -487,6 +487,29 @@ def micro(args):
         print(json.dumps({"micro": "exact", "bytes": c.nbytes, "us_per_launch": round(us, 1),
                           "GBps": round(c.nbytes / us / 1e3, 1), "device_status": _lib.status()}))
         return
+    if args.micro == "sampler_sweep":
+        import numpy as np
+        from ai_b200 import sampler
+        V, res = 151936, []
+        for B in (1, 16, 64, 256):
+            g = torch.Generator(device="cuda").manual_seed(B)
+            lg = torch.randn(B, V, generator=g, device="cuda") * 3.0
+            prior = torch.randint(0, V, (B, 1024), generator=g, device="cuda", dtype=torch.int32)
+            bits = np.random.default_rng(B).random((B, (V + 31) // 32 * 32)) < 0.1  # 10 % of tokens allowed
+            packed = np.packbits(bits, axis=1, bitorder="little").view(np.int32).copy()  # bit j of word w: 32w + j
+            packed[:, 0] |= 1
+            mask = torch.from_numpy(packed).cuda()
+            u = torch.from_numpy(np.array([np.random.default_rng(r).random() for r in range(B)])).cuda()
+            out = torch.zeros(B, dtype=torch.int64, device="cuda")
+            ws = sampler.workspace(B, V, lg.device)
+            for k in (1, 20, 50):
+                for p in (0.8, 0.95):
+                    prm = sampler.params(0.7, k, p, 1.1, 0.5, 0.3)
+                    us = timed(lambda: sampler.sample_into(lg, out, prm, u, prior, mask, ws=ws), max(args.steps, 1))
+                    nb = B * V * 4 + mask.numel() * 4 + prior.numel() * 4
+                    res.append({"B": B, "top_k": k, "top_p": p, "us": round(us, 2), "GBps": round(nb / us / 1e3, 1)})
+        print(json.dumps({"micro": "sampler_sweep", "rows": res, "device_status": _lib.status()}))
+        return
     if args.micro in ("attn", "sample"):
         run, nbytes = (micro_attn if args.micro == "attn" else micro_sample)(args)
         us = timed(run, max(args.steps, 1))
@@ -514,7 +537,7 @@ def micro(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--micro", choices=["gemv", "gemv_down", "gemv_qkv", "gemv_o", "attn", "sample", "head8", "gemm",
-                                        "gemm1", "exact"],
+                                        "gemm1", "exact", "sampler_sweep"],
                     default=None,
                     help="time one kernel alone on a small case (for ncu) instead of the decode benchmark")
     ap.add_argument("--gemv-variant", type=int, default=None, choices=[0, 1, 2, 3, 4],

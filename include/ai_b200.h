@@ -68,6 +68,11 @@ const char* aib_last_error(void);
 void aib_set_pdl(int enabled);
 /* Device status word of the current device: copies it to *out (synchronous) and, if clear != 0, resets it. */
 int aib_status_read(int* out, int clear);
+/* Test knobs of the current device (synchronous; no reference counterpart), so that tests can make a bounded wait
+ * run out without any fault: knob 1 = spin limit of every bounded wait (polls; 0 restores the default, ~1e6 times
+ * longer than any legitimate wait), knob 2 = 1 makes the wide T = 1 GEMV's producer withhold its copies (its stages
+ * never fill, its consumers give up after the spin limit and record AIB_DEV_TIMEOUT_FULL). Not for production. */
+int aib_debug_knob(int knob, int value);
 
 /* ---------------------------------------------------------------------------------- 12-bit codec ---- */
 /* Host encoder, bit-exact with `compress` (wcomp.py:13-32). w: bf16 bits [N,K]. Writes m8, e4, rp, *base,
@@ -205,6 +210,17 @@ int aib_attn_cached(const float* q, const uint16_t* kc, const uint16_t* vc, cons
  * {1, 2, 4, 8}; HD 64 or 128; start + n <= maxt. */
 int aib_attn_prefill(const float* q, const uint16_t* kc, const uint16_t* vc, float* out, int n, int start, int H, int KV,
                      int HD, int maxt, float scale, void* stream);
+
+/* ------------------------------------------------------------------------- tensor parallelism ---- */
+/* In-place sum of x (fp32 [n], n <= nmax) over the `world` tensor-parallel ranks of one node (replaces, for the
+ * decode step's small blocks, the NCCL all-reduce after o_proj and down_proj; the reference has no tensor
+ * parallelism, planning/multigpu.py:48-95 splits layers instead). buf_ptrs / flag_ptrs: host arrays of every
+ * rank's symmetric buffer (2 * nmax floats, 16-byte aligned) and flag words (world ints, zero before the first
+ * call), mapped into this process; epoch: this rank's device counter (int, zero before the first call). Every
+ * rank makes the same calls in the same order. The sum runs in rank order, so every rank gets the same bits. A
+ * peer that does not arrive within the bounded wait sets AIB_DEV_TIMEOUT_FULL and leaves x unchanged. */
+int aib_allreduce_oneshot(float* x, int n, int nmax, const int64_t* buf_ptrs, const int64_t* flag_ptrs, int rank,
+                          int world, int* epoch, void* stream);
 
 /* ---------------------------------------------------------------------------------- sampler ---- */
 /* Logits-in sampler (replaces GGUFEngine._pick, core/gengine.py:452-469, with Constraint.apply,

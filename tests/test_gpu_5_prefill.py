@@ -168,7 +168,7 @@ def test_prefill_attention_vs_oracle(lib, H, KV, HD, n, start):
 @pytest.mark.parametrize("name", ["small", "small-1k"])
 def test_engine_prefill_matches_chunked_path(lib, name, monkeypatch):
     """A 53-token prompt through the whole-prompt prefill gives the same next token as the 16-token chunk path
-    (the reference's legacy path), a KV cache within one bf16 rounding of it, and the same greedy continuation."""
+    (the reference's legacy path), a KV cache within bf16 rounding of it, and the same greedy continuation."""
     from ai_b200.engine import Engine
     from ai_b200.model import CONFIGS, RandomWeights
     cfg = CONFIGS[name]
@@ -181,6 +181,9 @@ def test_engine_prefill_matches_chunked_path(lib, name, monkeypatch):
     tb = list(b.generate(prompt, max_new=12))
     assert ta == tb
     ka, kb = a.kv[:, :, :, :53].float().cpu().numpy(), b.kv[:, :, :, :53].float().cpu().numpy()
-    # one bf16 rounding step apart at most (fp32 sums in another order can round the other way)
-    assert (np.abs(ka - kb) <= 2.0 ** -7 * np.maximum(np.abs(ka), np.abs(kb)) + 1e-6).all()
+    # a bf16 rounding step apart (fp32 sums in another order can round the other way), with an absolute floor at
+    # 1e-3 of the cache's scale for entries near zero, where the two paths' fp32 rounding differences dominate
+    d = np.abs(ka - kb)
+    bad = d > 2.0 ** -7 * np.maximum(np.abs(ka), np.abs(kb)) + 1e-3 * np.abs(kb).max()
+    assert not bad.any(), f"{bad.sum()} of {bad.size} cache entries differ; max |d| {d.max():.3e}"
     assert status_clear() == 0

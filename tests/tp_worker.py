@@ -12,6 +12,26 @@ import torch.distributed as dist
 sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 
 
+def ar_check(eng, rank, world):
+    """The one-shot all-reduce gives bitwise the rank-order sum of every rank's block, call after call (the
+    epochs alternate the two buffer slots)."""
+    if eng.ar is None:
+        return None
+    ok = True
+    for i, n in enumerate((4096, 1000, eng.ar["nmax"], 4096)):
+        g = torch.Generator(device="cuda").manual_seed(100 * i + rank)
+        x = torch.randn(n, generator=g, device="cuda")
+        parts = [torch.empty_like(x) for _ in range(world)]
+        dist.all_gather(parts, x)
+        want = torch.zeros_like(x)
+        for p in parts:
+            want += p
+        eng._reduce(x)
+        torch.cuda.synchronize()
+        ok = ok and torch.equal(x, want)
+    return ok
+
+
 def main():
     rank, world, lr = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"]), int(os.environ["LOCAL_RANK"])
     torch.cuda.set_device(lr)
@@ -24,7 +44,8 @@ def main():
     rw = RandomWeights(cfg, seed=11, norm_noise=0.1, std=0.05)
     prompt = [3, 1, 4, 1, 5, 9, 2, 6, 5, 3, 5, 8, 9, 7, 9, 3, 2, 3, 8, 4]  # > 16 tokens: the batched path too
     eng = Engine(cfg, maxt=128, weights=rw, log=None, tp=world)
-    res = {"greedy": list(eng.generate(prompt, max_new=16)),
+    res = {"oneshot": eng.ar is not None, "ar_exact": ar_check(eng, rank, world),
+           "greedy": list(eng.generate(prompt, max_new=16)),
            "sample": list(eng.generate(prompt, max_new=12, temperature=0.8, top_p=0.9, top_k=20, seed=7))}
     eng.use_graphs = False
     res["eager"] = list(eng.generate(prompt, max_new=16))
