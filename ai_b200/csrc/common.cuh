@@ -23,9 +23,9 @@ __device__ int g_aib_status = 0;
 
 AIB_DEV void set_status(int code) { atomicCAS(&g_aib_status, 0, code); }
 
-// spin limit for bounded waits: each try_wait may suspend for a hardware-defined window, so this bounds
-// a wait to well under a second while being ~1e6x longer than any legitimate wait in these kernels.
-constexpr uint32_t kSpinLimit = 1u << 22;
+// spin limit for bounded waits: each try_wait suspends for at most kSuspendNs (1 us), so this bounds a wait to
+// about a second while being ~1e5x longer than any legitimate wait in these kernels.
+constexpr uint32_t kSpinLimit = 1u << 20;
 // Test knobs (aib_debug_knob): a smaller spin limit, so a test can make a wait run out in milliseconds, and a
 // switch under which the wide GEMV's producer issues no copies (its stages never fill). Zero = off.
 __device__ uint32_t g_aib_spin_override = 0;
@@ -56,14 +56,29 @@ AIB_DEV void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
 AIB_DEV void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
+// A waiting thread is suspended (it takes no issue slots) until the phase completes or kSuspendNs elapses; a
+// spin-loop of these therefore sleeps instead of competing with the working warps for issue.
+#ifndef AIB_SUSPEND_NS
+#define AIB_SUSPEND_NS 1000
+#endif
+constexpr uint32_t kSuspendNs = AIB_SUSPEND_NS;
 AIB_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n"
-      " selp.u32 %0, 1, 0, p;\n}\n"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
+  if (kSuspendNs) {
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n"
+        " selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendNs)
+        : "memory");
+  } else {
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+  }
   return ok != 0;
 }
 // Bounded wait: returns false (and records `code`) if the phase did not complete in time.

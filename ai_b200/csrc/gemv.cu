@@ -27,6 +27,16 @@
 #include <climits>
 #include "common.cuh"
 
+#ifndef AIB_GEMV_EARLY
+#define AIB_GEMV_EARLY 1  // issue the ring's first stages before the CTA's shared prologue
+#endif
+#ifndef AIB_GEMV_LOWNIB2
+#define AIB_GEMV_LOWNIB2 0  // low-nibble codes with one mask and one multiply-add (instead of two multiply-adds)
+#endif
+#ifndef AIB_GEMV_ACC
+#define AIB_GEMV_ACC 2  // accumulator chains per consumer warp in the tensor-core T = 1 kernel (2 or 4)
+#endif
+
 namespace aib {
 namespace gemv {
 
@@ -747,7 +757,7 @@ AIB_DEV void produce_wide(const CUtensorMap* tm8, const CUtensorMap* tme4, uint8
                           int slot_meta, uint64_t* full, uint64_t* empty, volatile int* abort_flag, const ExcTab& et,
                           XF xval, float* y, int N, int tb, int ks0, int n_st, int R, int CW, int KS, int NS,
                           int nrows, int pw, float* wsp, int* wsc, int maxp, int tiles,
-                          uint32_t stage_bytes = kRowsStage) {
+                          uint32_t stage_bytes = kRowsStage, int first = 0) {
   const int lane = threadIdx.x & 31;
   if (lane == 0) {
     prefetch_tensormap(tm8);
@@ -779,7 +789,7 @@ AIB_DEV void produce_wide(const CUtensorMap* tm8, const CUtensorMap* tme4, uint8
       }
     }
     uint8_t* sm = meta + s * slot_meta;
-    if (i < n_st && lane == 0 && !g_aib_withhold_copies) {  // issue first: the copy is the long pole
+    if (i >= first && i < n_st && lane == 0 && !g_aib_withhold_copies) {  // issue first: the copy is the long pole
       uint8_t* st = ring + static_cast<size_t>(s) * stage_bytes;
       mbar_arrive_expect_tx(&full[s], stage_bytes);
       tma_load_3d(st, tm8, &full[s], 0, ks * CW, tile * R);
@@ -859,7 +869,7 @@ AIB_DEV void produce_wide(const CUtensorMap* tm8, const CUtensorMap* tme4, uint8
     }
     __syncwarp();
     if (i < n_st) {
-      if (lane == 0) mbar_arrive(&full[s]);  // second arrival: the slot's previous partials are read
+      if (lane == 0 && i >= first) mbar_arrive(&full[s]);  // second arrival: the slot's previous partials are read
       if (++ks == KS) ks = 0, ++tile;
     }
     if (++s == NS) s = 0, ++round;
@@ -1146,12 +1156,15 @@ AIB_DEV float tc_xval(const uint8_t* xr, int nch, int col) {
 // NCW consumer warps: 16 with 48 KB stages (R * CW = 128, one CTA per SM), or 8 with 24 KB stages (R * CW = 64,
 // <= 113 KB of shared memory and 288 threads, so two CTAs share an SM: two of the same launch, or the tail of one
 // launch and the head of the next, whose producer then streams its weights while the previous CTA drains).
-template <int MODE, bool RMS, int NCW>
-__global__ void __launch_bounds__(NCW * 32 + 32, NCW == 16 ? 1 : 2)
+// SPL = 2 splits each (row group, chunk slot, half) unit's eight MMA steps between two warps (four each), so 16
+// consumer warps share a 24 KB stage and two 544-thread CTAs fit an SM: 32 consumer warps per SM to hide the
+// decode's dependency chains.
+template <int MODE, bool RMS, int NCW, int SPL = 1>
+__global__ void __launch_bounds__(NCW * 32 + 32, (NCW == 16 && SPL == 1) ? 1 : 2)
     gemv_tc_kernel(const __grid_constant__ CUtensorMap tm8, const __grid_constant__ CUtensorMap tme4, RowsParams p) {
   constexpr int kTcConsumers = NCW * 32;
   constexpr int kTcThreads = kTcConsumers + 32;
-  constexpr int kStage = NCW * 2048 * 3 / 2;  // bytes per ring slot: 2048 weights per consumer warp
+  constexpr int kStage = NCW * 2048 * 3 / 2 / SPL;  // bytes per ring slot: 2048 / SPL weights per consumer warp
   extern __shared__ __align__(1024) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty = full + 16;
@@ -1167,17 +1180,35 @@ __global__ void __launch_bounds__(NCW * 32 + 32, NCW == 16 ? 1 : 2)
   const WideShare sh_ = wide_share(p);
   const int tb = sh_.tb, ks0 = sh_.ks0;
   const int R = p.R, CW = p.CW, KS = p.KS, NS = p.NS;
-  const int PW = 2 * CW;  // partials per row (warps per row group)
+  const int PW = 2 * CW * SPL;  // partials per row (warps per row group)
   const int n_st = sh_.n_st;
   const int row0 = sh_.row0;
   const int nrows = sh_.nrows;
-  if (tid == 0) {
+  // The producer thread initialises the barriers and, before the shared prologue below (row pointers and
+  // exception staging: global round trips), issues the ring's first stages, so the weights start streaming at
+  // once; the slots have no previous partials, so both of each stage's arrivals are made here.
+  const int first = AIB_GEMV_EARLY ? min(NS, n_st) : 0;
+  if (tid == kTcConsumers) {
     for (int s = 0; s < NS; ++s) {
       mbar_init(&full[s], 2);  // TMA arrival + bookkeeping arrival
       mbar_init(&empty[s], kTcConsumers / 32);
     }
     *abort_flag = 0;
     fence_mbar_init();
+    if (!g_aib_withhold_copies) {
+      prefetch_tensormap(&tm8);
+      prefetch_tensormap(&tme4);
+      const uint32_t m8_bytes = static_cast<uint32_t>(R * CW * 256);
+      int ks = ks0, tile = tb;
+      for (int i = 0; i < first; ++i) {
+        uint8_t* st = ring + static_cast<size_t>(i) * kStage;
+        mbar_arrive_expect_tx(&full[i], kStage);
+        tma_load_3d(st, &tm8, &full[i], 0, ks * CW, tile * R);
+        tma_load_3d(st + m8_bytes, &tme4, &full[i], 0, ks * CW, tile * R);
+        mbar_arrive(&full[i]);
+        if (++ks == KS) ks = 0, ++tile;
+      }
+    }
   }
   for (int i = tid; i <= nrows; i += kTcThreads) rps[i] = p.rp[row0 + i];
   __syncthreads();
@@ -1192,7 +1223,8 @@ __global__ void __launch_bounds__(NCW * 32 + 32, NCW == 16 ? 1 : 2)
   if (tid >= kTcConsumers) {  // ---------------- producer warp
     auto xval = [&](int col) { return tc_xval(xr, p.nch, col); };
     produce_wide<MODE>(&tm8, &tme4, ring, meta, kTcSlotMeta, full, empty, abort_flag, et, xval, p.y, p.N, tb, ks0,
-                       n_st, R, CW, KS, NS, nrows, PW, p.wsp, p.wsc, p.maxp, p.tiles, kStage);
+                       n_st, R, CW, KS, NS, nrows, PW, p.wsp, p.wsc, p.maxp, p.tiles, kStage,
+                       g_aib_withhold_copies ? 0 : first);
     return;
   }
 
@@ -1308,7 +1340,8 @@ __global__ void __launch_bounds__(NCW * 32 + 32, NCW == 16 ? 1 : 2)
   named_sync(1, kTcConsumers);
 
   const int warp = tid >> 5, g = lane >> 2, t = lane & 3;
-  const int hh = warp & 1, q = (warp >> 1) % CW, rg = (warp >> 1) / CW;
+  const int half = SPL == 2 ? (warp & 1) : 0, wu = SPL == 2 ? (warp >> 1) : warp;  // wu: the warp's unit
+  const int hh = wu & 1, q = (wu >> 1) % CW, rg = (wu >> 1) / CW;
   const int par = g & 1, blk = hh ^ par;
   const int rA = rg * 16 + g, rB = rA + 8;
   const uint32_t colo = static_cast<uint32_t>(q * 256 + blk * 64 + 16 * t);
@@ -1321,7 +1354,10 @@ __global__ void __launch_bounds__(NCW * 32 + 32, NCW == 16 ? 1 : 2)
   const uint32_t k128 = p.k128, k8 = p.k8;
 
   bool aborted = false;
-  float acc[2][4] = {{0.0f, 0.0f, 0.0f, 0.0f}, {0.0f, 0.0f, 0.0f, 0.0f}};
+  constexpr int NACC = AIB_GEMV_ACC;  // independent accumulator chains (MMA i feeds chain i % NACC)
+  float acc[NACC][4];
+#pragma unroll
+  for (int a = 0; a < NACC; ++a) acc[a][0] = acc[a][1] = acc[a][2] = acc[a][3] = 0.0f;
   int s = 0, ph = 0, ks = ks0, tile = tb;
   for (int it = 0; it < n_st; ++it) {
     // warp-uniform: the MMAs below must run with all 32 lanes converged
@@ -1331,43 +1367,71 @@ __global__ void __launch_bounds__(NCW * 32 + 32, NCW == 16 ? 1 : 2)
     const uint8_t* sm = meta + s * kTcSlotMeta;
     if (ok && gc < p.nch) {
       const uint8_t* st = ring + static_cast<size_t>(s) * kStage;
-      const uint4 LA = *reinterpret_cast<const uint4*>(st + m8A);
-      const uint4 HA = *reinterpret_cast<const uint4*>(st + m8A + 128);
-      const uint4 EA = *reinterpret_cast<const uint4*>(st + e4A);
-      const uint4 LB = *reinterpret_cast<const uint4*>(st + m8B);
-      const uint4 HB = *reinterpret_cast<const uint4*>(st + m8B + 128);
-      const uint4 EB = *reinterpret_cast<const uint4*>(st + e4B);
-      const uint32_t la[4] = {LA.x, LA.y, LA.z, LA.w}, ha[4] = {HA.x, HA.y, HA.z, HA.w}, ea[4] = {EA.x, EA.y, EA.z, EA.w};
-      const uint32_t lb[4] = {LB.x, LB.y, LB.z, LB.w}, hb[4] = {HB.x, HB.y, HB.z, HB.w}, eb[4] = {EB.x, EB.y, EB.z, EB.w};
+      uint32_t la[4], ha[4], ea[4], lb[4], hb[4], eb[4];  // the lane's 16 columns (SPL 2: its half, words 0-1)
+      if (SPL == 1) {
+        const uint4 LA = *reinterpret_cast<const uint4*>(st + m8A);
+        const uint4 HA = *reinterpret_cast<const uint4*>(st + m8A + 128);
+        const uint4 EA = *reinterpret_cast<const uint4*>(st + e4A);
+        const uint4 LB = *reinterpret_cast<const uint4*>(st + m8B);
+        const uint4 HB = *reinterpret_cast<const uint4*>(st + m8B + 128);
+        const uint4 EB = *reinterpret_cast<const uint4*>(st + e4B);
+        la[0] = LA.x, la[1] = LA.y, la[2] = LA.z, la[3] = LA.w;
+        ha[0] = HA.x, ha[1] = HA.y, ha[2] = HA.z, ha[3] = HA.w;
+        ea[0] = EA.x, ea[1] = EA.y, ea[2] = EA.z, ea[3] = EA.w;
+        lb[0] = LB.x, lb[1] = LB.y, lb[2] = LB.z, lb[3] = LB.w;
+        hb[0] = HB.x, hb[1] = HB.y, hb[2] = HB.z, hb[3] = HB.w;
+        eb[0] = EB.x, eb[1] = EB.y, eb[2] = EB.z, eb[3] = EB.w;
+      } else {
+        const uint32_t ho = static_cast<uint32_t>(half * 8);
+        const uint2 LA = *reinterpret_cast<const uint2*>(st + m8A + ho);
+        const uint2 HA = *reinterpret_cast<const uint2*>(st + m8A + 128 + ho);
+        const uint2 EA = *reinterpret_cast<const uint2*>(st + e4A + ho);
+        const uint2 LB = *reinterpret_cast<const uint2*>(st + m8B + ho);
+        const uint2 HB = *reinterpret_cast<const uint2*>(st + m8B + 128 + ho);
+        const uint2 EB = *reinterpret_cast<const uint2*>(st + e4B + ho);
+        la[0] = LA.x, la[1] = LA.y, ha[0] = HA.x, ha[1] = HA.y, ea[0] = EA.x, ea[1] = EA.y;
+        lb[0] = LB.x, lb[1] = LB.y, hb[0] = HB.x, hb[1] = HB.y, eb[0] = EB.x, eb[1] = EB.y;
+        la[2] = la[3] = ha[2] = ha[3] = ea[2] = ea[3] = lb[2] = lb[3] = hb[2] = hb[3] = eb[2] = eb[3] = 0u;
+      }
       // this lane's B records for MMA i: xg + i * (128 or 64)
       const uint8_t* xg = sp < 2 ? xr + (gc * 8) * 128 + (blk * 2 + sp) * 32 + t * 8
                                  : xr + p.nch * 1024 + (gc * 8) * 64 + blk * 32 + t * 8;
       const int xstep = sp < 2 ? 128 : 64;
       {  // exceptions decode to their stand-ins; the producer adds the corrections
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
+        for (int ii = 0; ii < 8 / SPL; ++ii) {
+          const int i = ii + half * (8 / SPL);  // MMA step within the unit (its K slice)
           // x2 = [0, e1, 0, e0] (two code bytes: low nibble = low-half column, high nibble = high-half column).
           // High codes: x2*8 + base7 puts the high nibbles in the exponent fields and the low nibbles in
           // mantissa bits that the merge discards (no carry reaches the exponent). Low codes: x2*128 + base7
           // minus the high nibbles times 128 -- exact integer arithmetic, multiplies on the FMA pipe.
-          const int wd = i >> 1;
+          const int wd = ii >> 1;
           const uint32_t sel = (i & 1) ? 0xB3A2u : 0x9180u, esel = (i & 1) ? 0x4342u : 0x4140u;
           const uint32_t xa2 = prmt(ea[wd], 0u, esel), xb2 = prmt(eb[wd], 0u, esel);
+#if AIB_GEMV_LOWNIB2
+          const uint32_t tA = (xa2 & 0x000F000Fu) * k128 + base7;
+          const uint32_t tB = (xb2 & 0x000F000Fu) * k128 + base7;
+#else
           const uint32_t tA = xa2 * k128 + base7 - (xa2 & 0x00F000F0u) * k128;
           const uint32_t tB = xb2 * k128 + base7 - (xb2 & 0x00F000F0u) * k128;
+#endif
           const uint32_t a0 = merge_sm_e(prmt(la[wd], 0u, sel), tA);
           const uint32_t a1 = merge_sm_e(prmt(lb[wd], 0u, sel), tB);
           const uint32_t a2 = merge_sm_e(prmt(ha[wd], 0u, sel), xa2 * k8 + base7);
           const uint32_t a3 = merge_sm_e(prmt(hb[wd], 0u, sel), xb2 * k8 + base7);
           uint2 bb = make_uint2(0u, 0u);
           if (bl) bb = *reinterpret_cast<const uint2*>(xg + i * xstep);
-          mma_bf16(acc[i & 1], a0, a1, a2, a3, bb.x, bb.y);
+          mma_bf16(acc[i % NACC], a0, a1, a2, a3, bb.x, bb.y);
         }
       }
     }
     if (ks == KS - 1 || it == n_st - 1) {  // segment end: row g takes the columns of its parity (quads t = 0..2)
       float vA = par ? (acc[0][1] + acc[1][1]) : (acc[0][0] + acc[1][0]);
       float vB = par ? (acc[0][3] + acc[1][3]) : (acc[0][2] + acc[1][2]);
+      if (NACC == 4) {
+        vA += par ? (acc[2][1] + acc[3][1]) : (acc[2][0] + acc[3][0]);
+        vB += par ? (acc[2][3] + acc[3][3]) : (acc[2][2] + acc[3][2]);
+      }
       if (t == 3) vA = vB = 0.0f;
       vA += __shfl_xor_sync(0xffffffffu, vA, 1);
       vB += __shfl_xor_sync(0xffffffffu, vB, 1);
@@ -1375,12 +1439,12 @@ __global__ void __launch_bounds__(NCW * 32 + 32, NCW == 16 ? 1 : 2)
       vB += __shfl_xor_sync(0xffffffffu, vB, 2);
       if (t == 0) {
         float* part = reinterpret_cast<float*>(const_cast<uint8_t*>(sm) + 128);
-        const int wi = q * 2 + hh;
+        const int wi = (q * 2 + hh) * SPL + half;
         part[rA * PW + wi] = vA;
         part[rB * PW + wi] = vB;
       }
 #pragma unroll
-      for (int a = 0; a < 2; ++a)
+      for (int a = 0; a < NACC; ++a)
 #pragma unroll
         for (int c = 0; c < 4; ++c) acc[a][c] = 0.0f;
     }
@@ -1659,19 +1723,20 @@ static int g_variant = 3;  // 0: tensor-core 24 KB-stage kernel, 1: CUDA-core 12
                            // 4: tensor-core 48 KB stages, one CTA per SM
 constexpr size_t kSmemPair = 113 * 1024;  // two CTAs per SM (228 KB per SM, 1 KB reserved per CTA)
 
-template <int NCW>
+template <int NCW, int SPL = 1>
 static int run_tc_var(const aib_c12* c, const float* x, float* y, int mode, const uint16_t* lnw, float eps, void* ws,
                       size_t ws_bytes, cudaStream_t s) {
   constexpr int kThreadsV = NCW * 32 + 32;
-  constexpr size_t kStage = static_cast<size_t>(NCW) * 2048 * 3 / 2;
-  const size_t smem_max = NCW == 16 ? kSmemMax : kSmemPair;
+  constexpr size_t kStage = static_cast<size_t>(NCW) * 2048 * 3 / 2 / SPL;
+  constexpr bool kPair = !(NCW == 16 && SPL == 1);  // two CTAs per SM
+  const size_t smem_max = kPair ? kSmemPair : kSmemMax;
   const int nch = c->K / 256;
-  const int CW = NCW == 16 ? (nch % 8 == 0 ? 8 : 4) : 4;
+  const int CW = kStage == 49152 ? (nch % 8 == 0 ? 8 : 4) : 4;
   const int R = static_cast<int>(kStage / 384) / CW, KS = nch / CW;
   const int tiles = (c->N + R - 1) / R;
-  const int max_grid = NCW == 16 ? sm_count() : 2 * sm_count();
+  const int max_grid = kPair ? 2 * sm_count() : sm_count();
   const StreamK sk = streamk_plan(tiles, KS, R);
-  const bool use_sk = NCW == 16 && ws && ws_bytes >= sk.bytes && !(reinterpret_cast<uintptr_t>(ws) & 15);
+  const bool use_sk = !kPair && ws && ws_bytes >= sk.bytes && !(reinterpret_cast<uintptr_t>(ws) & 15);
   const int grid = use_sk ? sk.grid : std::min(tiles, max_grid);
   const int per = static_cast<int>((static_cast<long long>(tiles) * KS + grid - 1) / grid);
   const int rows_max = use_sk ? ((per + KS - 1) / KS + 1) * R : ((tiles + grid - 1) / grid) * R;
@@ -1705,15 +1770,15 @@ static int run_tc_var(const aib_c12* c, const float* x, float* y, int mode, cons
     return launch(kernel, dim3(grid), dim3(kThreadsV), smem, s, "aib_gemv_c12(T=1, tensor)", tm8, tme4, p);
   };
   if (lnw) {
-    if (mode == 0) return go(gemv_tc_kernel<0, true, NCW>);
-    if (mode == 1) return go(gemv_tc_kernel<1, true, NCW>);
-    if (mode == 3) return go(gemv_tc_kernel<3, true, NCW>);
-    return go(gemv_tc_kernel<2, true, NCW>);
+    if (mode == 0) return go(gemv_tc_kernel<0, true, NCW, SPL>);
+    if (mode == 1) return go(gemv_tc_kernel<1, true, NCW, SPL>);
+    if (mode == 3) return go(gemv_tc_kernel<3, true, NCW, SPL>);
+    return go(gemv_tc_kernel<2, true, NCW, SPL>);
   }
-  if (mode == 0) return go(gemv_tc_kernel<0, false, NCW>);
-  if (mode == 1) return go(gemv_tc_kernel<1, false, NCW>);
-  if (mode == 3) return go(gemv_tc_kernel<3, false, NCW>);
-  return go(gemv_tc_kernel<2, false, NCW>);
+  if (mode == 0) return go(gemv_tc_kernel<0, false, NCW, SPL>);
+  if (mode == 1) return go(gemv_tc_kernel<1, false, NCW, SPL>);
+  if (mode == 3) return go(gemv_tc_kernel<3, false, NCW, SPL>);
+  return go(gemv_tc_kernel<2, false, NCW, SPL>);
 }
 
 // Wide-stage tensor-core kernel: K a multiple of 1024; ENOTSUP when x's three-part records do not fit.
@@ -1725,6 +1790,10 @@ static int run_tc(const aib_c12* c, const float* x, float* y, int mode, const ui
     return fail(AIB_ENOTSUP, "aib_gemv_c12: base %d: exceptions need the exact-path kernel", c->base);
   if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(lnw) & 7))
     return fail(AIB_ENOTSUP, "aib_gemv_c12: x / lnw not aligned for vector loads");
+  if (g_variant == 5 && !ws) {
+    const int rc = run_tc_var<16, 2>(c, x, y, mode, lnw, eps, ws, ws_bytes, s);
+    if (rc != AIB_ENOTSUP) return rc;
+  }
   if (g_variant == 3 && !ws) {
     const int rc = run_tc_var<8>(c, x, y, mode, lnw, eps, ws, ws_bytes, s);
     if (rc != AIB_ENOTSUP) return rc;
@@ -1741,11 +1810,11 @@ static int run_t1(const aib_c12* c, const float* x, float* y, int mode, const ui
     if (rc2 != AIB_ENOTSUP) return rc2;
     return fail(AIB_ENOTSUP, "aib_gemv_c12: mode 3 with T == 1 needs K a multiple of 1024 (K=%d)", c->K);
   }
-  if (g_variant == 3 || g_variant == 4) {
+  if (g_variant >= 3) {
     const int rc = run_tc(c, x, y, mode, lnw, eps, ws, ws_bytes, s);
     if (rc != AIB_ENOTSUP) return rc;
   }
-  if (g_variant == 2 || g_variant == 3 || g_variant == 4) {
+  if (g_variant >= 2) {
     const int rc = run_rows(c, x, y, mode, lnw, eps, ws, ws_bytes, s);
     if (rc != AIB_ENOTSUP) return rc;  // other shapes use the 12 KB-stage kernel
   }

@@ -154,33 +154,42 @@ def _timed(fn):
 
 # ------------------------------------------------------------------------------------ GPU arm
 def gemv_roofline(eng, peak, reps=20):
-    """Codec GEMV kernels timed alone (CUDA events on the launching stream), in decode order, on layer 0
-    and the head: achieved = algorithmic bytes / average launch duration."""
+    """The dominant kernel of the decode step, the codec GEMV, timed alone (CUDA events on the launching stream)
+    as the engine runs it: one layer's four matrices in the engine's modes (qkv with the RMS prologue, o +=,
+    gate/up gated, down +=), back to back. achieved = their algorithmic bytes (12-bit planes + CSR) / time. The
+    vocabulary head -- the exact-logit kernel the sampling step runs -- is reported beside it."""
     import torch
     from ai_b200 import wcomp
+    from ai_b200.head import exact_logits
     W, s = eng.W[0], eng.small[0]
     gu_mode, down_mode = (3, 1) if eng.gated else (0, 2)  # the engine's own modes
     launches = [(W["qkv"], eng.xb[0], eng.qkvb[0], 0, s["ln1"]), (W["o"], eng.attb[0], eng.xb[1], 1, None),
-                (W["gu"], eng.xb[0], eng.gub[0], gu_mode, s["ln2"]), (W["down"], eng.gub[0], eng.xb[1], down_mode, None),
-                (eng.head, eng.xb[0], eng.logits[0], 0, eng.norm)]
+                (W["gu"], eng.xb[0], eng.gub[0], gu_mode, s["ln2"]), (W["down"], eng.gub[0], eng.xb[1], down_mode, None)]
     eng.xb[:2].normal_()
     eng.attb[0].normal_()
     eng.gub[0].normal_()
     total_bytes = sum(c.nbytes for c, *_ in launches)
     st = torch.cuda.current_stream()
-    for _ in range(3):
+
+    def run_layer():
         for c, x, y, m, lnw in launches:
             wcomp.gemvc1(x, c, y, m, lnw=lnw, eps=eng.eps)
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(st)
-    for _ in range(reps):
-        for c, x, y, m, lnw in launches:
-            wcomp.gemvc1(x, c, y, m, lnw=lnw, eps=eng.eps)
-    e1.record(st)
-    torch.cuda.synchronize()
-    sec = e0.elapsed_time(e1) / 1e3 / reps
+
+    def timed(fn):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for _ in range(reps):
+            fn()
+        e1.record(st)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / 1e3 / reps
+
+    sec = timed(run_layer)
     achieved = total_bytes / sec / 1e9
+    hsec = timed(lambda: exact_logits(eng.hb[:1], eng.head, 1, eng.logits[:1]))
     # DRAM traffic per launch: the ncu capture of one gate/up-shaped launch (profiles/gemv_tc_gu.md: read + write
     # bytes over the launch's algorithmic bytes), scaled to this average launch by its algorithmic bytes
     per_launch = total_bytes // len(launches)
@@ -192,10 +201,14 @@ def gemv_roofline(eng, peak, reps=20):
                 ratio = float(line.rsplit("=", 1)[1].strip(" |\n"))
         if ratio:
             traffic = int(per_launch * ratio)
-    return {"bound": "hbm", "kernel": "aib gemv_tc_kernel (codec GEMV, T=1)", "achieved": round(achieved, 1),
-            "peak": peak[0], "peak_kind": peak[1], "unit": "GB/s", "frac": round(achieved / peak[0], 4),
-            "traffic": traffic, "traffic_source": "ncu 24576x4096 launch, scaled by algorithmic bytes" if traffic else None,
-            "algorithmic_bytes_per_launch": per_launch, "avg_launch_us": round(sec / len(launches) * 1e6, 2)}
+    return {"bound": "hbm", "kernel": "aib gemv_tc_kernel (codec GEMV, T=1): one layer's qkv, o, gate/up, down",
+            "achieved": round(achieved, 1), "peak": peak[0], "peak_kind": peak[1], "unit": "GB/s",
+            "frac": round(achieved / peak[0], 4), "traffic": traffic,
+            "traffic_source": "ncu 24576x4096 launch, scaled by algorithmic bytes" if traffic else None,
+            "algorithmic_bytes_per_launch": per_launch, "avg_launch_us": round(sec / len(launches) * 1e6, 2),
+            "head": {"kernel": "aib exact_logits_kernel (full-vocabulary exact logits)", "bytes": eng.head.nbytes,
+                     "us": round(hsec * 1e6, 1), "GBps": round(eng.head.nbytes / hsec / 1e9, 1),
+                     "frac": round(eng.head.nbytes / hsec / 1e9 / peak[0], 4)}}
 
 
 def bench_prefill(eng, n=2048, reps=3):

@@ -8,7 +8,7 @@ import torch
 from oracle import codec, gemv as ogemv
 
 pytestmark = pytest.mark.gpu
-AIB_DEV_TIMEOUT_FULL = 101
+AIB_DEV_TIMEOUT_FULL, AIB_DEV_TIMEOUT_EMPTY = 101, 102
 
 
 @pytest.fixture(scope="module")
@@ -35,7 +35,9 @@ def test_gemv_wait_runs_out_reports_status_and_recovers(lib):
     finally:
         _lib.call("aib_debug_knob", 2, 0)
         _lib.call("aib_debug_knob", 1, 0)
-    assert st == AIB_DEV_TIMEOUT_FULL
+    # whichever side gives up first records its code: the consumers (stage never filled) or the producer (slot
+    # never released by consumers still waiting)
+    assert st in (AIB_DEV_TIMEOUT_FULL, AIB_DEV_TIMEOUT_EMPTY)
     # the context is intact: the same call now returns the right product and no status
     wcomp.gemvc1(x, c, y, 0)
     torch.cuda.synchronize()
