@@ -752,6 +752,78 @@ struct ExcTab {  // the CTA's exceptions: CSR slice in shared memory (columns + 
   const uint8_t* m8;
   int K, base;
 };
+// Finishes one row segment of a wide-stage kernel (tile ftile, chunk groups seg_lo..fks, where seg_lo is ks0
+// for the CTA's first tile and 0 otherwise). Lane r < R holds v = the segment's partial sum of row r of the
+// tile; the lanes add the exception corrections sum_e (v_e - G_e) * x[c_e] over the segment's exceptions (the
+// consumers decode every element, exceptions included, as a finite stand-in G_e -- see exc_garbage) in column
+// order and write y; a segment that is only part of its tile goes through the stream-K workspace. Warp-wide.
+template <int MODE, typename XF>
+AIB_DEV void finish_segment(float v, int ftile, int fks, const ExcTab& et, XF xval, float* y, int N, int tb, int ks0,
+                            int R, int CW, int KS, int nrows, float* wsp, int* wsc, int maxp, int tiles) {
+  const int lane = threadIdx.x & 31;
+  const int seg_lo = ftile == tb ? ks0 : 0;
+  const bool whole = seg_lo == 0 && fks == KS - 1;
+  const int lr = (ftile - tb) * R + lane, row = ftile * R + lane;
+  if (lane < R && lr < nrows) {  // exception corrections of the segment's columns, in column order
+    const int lo = seg_lo * CW * 256, hi = (fks + 1) * CW * 256;
+    const int qa = et.rps[lr] - et.e0, qb = et.rps[lr + 1] - et.e0;
+    float corr = 0.0f;
+    for (int q = qa; q < qb; ++q) {
+      const int col = et.staged ? et.ecs[q] : et.ec[et.e0 + q];
+      if (col >= hi) break;
+      if (col < lo) continue;
+      const float d = et.staged ? et.evs[q]
+                                : et.ev[et.e0 + q] - exc_garbage(et.m8[static_cast<size_t>(row) * et.K + col], et.base);
+      corr = fmaf(d, xval(col), corr);
+    }
+    v += corr;
+  }
+  if (whole) {
+    if (MODE == 3) {  // rows (2i, 2i+1) = (gate_i, up_i): y[i] = silu(gate_i) * up_i
+      const float vu = __shfl_down_sync(0xffffffffu, v, 1);
+      if (lane < R && !(lane & 1) && row + 1 < N) y[row >> 1] = silu_mul(v, vu);
+    } else if (lane < R && row < N) {
+      if (MODE == 0)
+        y[row] = v;
+      else
+        y[row] += v;
+    }
+    return;
+  }
+  // stream-K: this CTA holds part `pi` of the tile's stages; the last of its np parts to arrive adds them in
+  // part order (deterministic) and writes y, then clears the ticket
+  const long long nall = static_cast<long long>(tiles) * KS, G = gridDim.x;
+  const long long st0 = static_cast<long long>(ftile) * KS;
+  const int bf = static_cast<int>(((st0 + 1) * G + nall - 1) / nall - 1);
+  const int bl = static_cast<int>(((st0 + KS) * G + nall - 1) / nall - 1);
+  const int pi = static_cast<int>(blockIdx.x) - bf, np = bl - bf + 1;
+  float* slot = wsp + (static_cast<size_t>(ftile) * maxp) * R;
+  if (lane < R) slot[pi * R + lane] = v;
+  __threadfence();
+  __syncwarp();
+  int last = 0;
+  if (lane == 0) last = atomicAdd(&wsc[ftile], 1) == np - 1;
+  last = __shfl_sync(0xffffffffu, last, 0);
+  if (last) {
+    __threadfence();
+    float t = 0.0f;
+    if (lane < R) {
+      t = __ldcg(slot + lane);
+      for (int q = 1; q < np; ++q) t += __ldcg(slot + q * R + lane);
+    }
+    if (MODE == 3) {
+      const float tu = __shfl_down_sync(0xffffffffu, t, 1);
+      if (lane < R && !(lane & 1) && row + 1 < N) y[row >> 1] = silu_mul(t, tu);
+    } else if (lane < R && row < N) {
+      if (MODE == 0)
+        y[row] = t;
+      else
+        y[row] += t;
+    }
+    if (lane == 0) wsc[ftile] = 0;
+  }
+}
+
 template <int MODE, typename XF>
 AIB_DEV void produce_wide(const CUtensorMap* tm8, const CUtensorMap* tme4, uint8_t* ring, uint8_t* meta,
                           int slot_meta, uint64_t* full, uint64_t* empty, volatile int* abort_flag, const ExcTab& et,
@@ -766,7 +838,6 @@ AIB_DEV void produce_wide(const CUtensorMap* tm8, const CUtensorMap* tme4, uint8
   const uint32_t m8_bytes = static_cast<uint32_t>(R * CW * 256);
   int s = 0, round = 0, ks = ks0, tile = tb;  // stage i: slot s, ring round i / NS
   int fks = ks0, ftile = tb;                  // stage i - NS (same slot)
-  const long long nall = static_cast<long long>(tiles) * KS, G = gridDim.x;
   for (int i = 0; i < n_st + NS; ++i) {
     if (i >= NS) {  // the slot's previous stage must be consumed
       bool ok = true;
@@ -798,72 +869,13 @@ AIB_DEV void produce_wide(const CUtensorMap* tm8, const CUtensorMap* tme4, uint8
     if (i >= NS) {
       const bool seg_end = fks == KS - 1 || i - NS == n_st - 1;  // consumers left partials in the slot
       if (seg_end && !*abort_flag) {
-        const int seg_lo = ftile == tb ? ks0 : 0;  // first chunk group of this CTA's share of the tile
-        const bool whole = seg_lo == 0 && fks == KS - 1;
         float v = 0.0f;
-        const int lr = (ftile - tb) * R + lane, row = ftile * R + lane;
         if (lane < R) {
           const float* part = reinterpret_cast<const float*>(sm + 128) + lane * pw;
           v = part[0];
           for (int w = 1; w < pw; ++w) v += part[w];
-          if (lr < nrows) {  // exception corrections of the segment's columns, in column order
-            const int lo = seg_lo * CW * 256, hi = (fks + 1) * CW * 256;
-            const int qa = et.rps[lr] - et.e0, qb = et.rps[lr + 1] - et.e0;
-            float corr = 0.0f;
-            for (int q = qa; q < qb; ++q) {
-              const int col = et.staged ? et.ecs[q] : et.ec[et.e0 + q];
-              if (col >= hi) break;
-              if (col < lo) continue;
-              const float d = et.staged ? et.evs[q]
-                                        : et.ev[et.e0 + q] - exc_garbage(et.m8[static_cast<size_t>(row) * et.K + col], et.base);
-              corr = fmaf(d, xval(col), corr);
-            }
-            v += corr;
-          }
         }
-        if (whole) {
-          if (MODE == 3) {  // rows (2i, 2i+1) = (gate_i, up_i): y[i] = silu(gate_i) * up_i
-            const float vu = __shfl_down_sync(0xffffffffu, v, 1);
-            if (lane < R && !(lane & 1) && row + 1 < N) y[row >> 1] = silu_mul(v, vu);
-          } else if (lane < R && row < N) {
-            if (MODE == 0)
-              y[row] = v;
-            else
-              y[row] += v;
-          }
-        } else {
-          // stream-K: this CTA holds part `pi` of the tile's stages; the last of its np parts to arrive adds
-          // them in part order (deterministic) and writes y, then clears the ticket
-          const long long st0 = static_cast<long long>(ftile) * KS;
-          const int bf = static_cast<int>(((st0 + 1) * G + nall - 1) / nall - 1);
-          const int bl = static_cast<int>(((st0 + KS) * G + nall - 1) / nall - 1);
-          const int pi = static_cast<int>(blockIdx.x) - bf, np = bl - bf + 1;
-          float* slot = wsp + (static_cast<size_t>(ftile) * maxp) * R;
-          if (lane < R) slot[pi * R + lane] = v;
-          __threadfence();
-          __syncwarp();
-          int last = 0;
-          if (lane == 0) last = atomicAdd(&wsc[ftile], 1) == np - 1;
-          last = __shfl_sync(0xffffffffu, last, 0);
-          if (last) {
-            __threadfence();
-            float t = 0.0f;
-            if (lane < R) {
-              t = __ldcg(slot + lane);
-              for (int q = 1; q < np; ++q) t += __ldcg(slot + q * R + lane);
-            }
-            if (MODE == 3) {
-              const float tu = __shfl_down_sync(0xffffffffu, t, 1);
-              if (lane < R && !(lane & 1) && row + 1 < N) y[row >> 1] = silu_mul(t, tu);
-            } else if (lane < R && row < N) {
-              if (MODE == 0)
-                y[row] = t;
-              else
-                y[row] += t;
-            }
-            if (lane == 0) wsc[ftile] = 0;
-          }
-        }
+        finish_segment<MODE>(v, ftile, fks, et, xval, y, N, tb, ks0, R, CW, KS, nrows, wsp, wsc, maxp, tiles);
       }
       if (++fks == KS) fks = 0, ++ftile;
     }
@@ -873,6 +885,88 @@ AIB_DEV void produce_wide(const CUtensorMap* tm8, const CUtensorMap* tme4, uint8
       if (++ks == KS) ks = 0, ++tile;
     }
     if (++s == NS) s = 0, ++round;
+  }
+}
+
+// ------------------------------------------- producer and finisher warps of the tensor-core wide-stage kernel
+// The producer only streams: one thread issues stage i (two 3-D TMA copies, m8 and e4, no multicast) as soon as
+// its slot's previous stage has been consumed; a slot's full barrier completes on that one arrival plus the
+// copied bytes. Stages below `first` were issued before the CTA's prologue. A wait that runs out raises the
+// abort flag and, before returning, waits (bounded) for the copies still in flight.
+AIB_DEV void issue_stages(const CUtensorMap* tm8, const CUtensorMap* tme4, uint8_t* ring, uint64_t* full,
+                          uint64_t* empty, volatile int* abort_flag, int tb, int ks0, int n_st, int first, int R,
+                          int CW, int KS, int NS, uint32_t stage_bytes) {
+  if (g_aib_withhold_copies) return;
+  const uint32_t m8_bytes = static_cast<uint32_t>(R * CW * 256);
+  int ks = ks0 + first, tile = tb;
+  tile += ks / KS;
+  ks %= KS;
+  for (int i = first; i < n_st; ++i) {
+    const int s = i % NS;
+    if (i >= NS) {
+      const uint32_t par = ((i / NS) - 1) & 1;
+      bool ok = mbar_try_wait(&empty[s], par);
+      for (uint32_t k = 0, lim = ok ? 0u : spin_limit(); k < lim && !ok; ++k) {
+        ok = mbar_try_wait(&empty[s], par);
+        if (!ok && (k & 63) == 63 && *abort_flag) break;
+      }
+      if (!ok) {
+        if (!*abort_flag) set_status(AIB_DEV_TIMEOUT_EMPTY);
+        *abort_flag = 1;
+        for (int k = i - NS; k < i; ++k) mbar_wait(&full[k % NS], (k / NS) & 1, AIB_DEV_TIMEOUT_FULL);
+        return;
+      }
+    }
+    uint8_t* st = ring + static_cast<size_t>(s) * stage_bytes;
+    mbar_arrive_expect_tx(&full[s], stage_bytes);
+    tma_load_3d(st, tm8, &full[s], 0, ks * CW, tile * R);
+    tma_load_3d(st + m8_bytes, tme4, &full[s], 0, ks * CW, tile * R);
+    if (++ks == KS) ks = 0, ++tile;
+  }
+}
+
+// The finisher warp walks the same stage sequence as the consumers. At the j-th segment end the consumer warps
+// have left one partial per (row, warp) in buffer j & 1 (float [R][pw]) and arrived on ready[j & 1]; the
+// finisher adds each row's pw partials in warp order, releases the buffer (free[j & 1]: the consumers reuse it
+// at segment end j + 2) and then finishes the segment -- exception corrections, y -- off the copy and MMA
+// paths. Two buffers: the consumers wait only when the finisher is two segments behind.
+template <int MODE, typename XF>
+AIB_DEV void finish_segments(const float* pbuf, int pstride, uint64_t* ready, uint64_t* free_, volatile int* abort_flag,
+                             const ExcTab& et, XF xval, float* y, int N, int tb, int ks0, int n_st, int R, int CW,
+                             int KS, int nrows, int pw, float* wsp, int* wsc, int maxp, int tiles) {
+  const int lane = threadIdx.x & 31;
+  pdl_wait();  // y is read (mode 1) and written after the previous kernel's
+  int ks = ks0, tile = tb, j = 0;
+  for (int i = 0; i < n_st; ++i) {
+    if (ks == KS - 1 || i == n_st - 1) {
+      const int b = j & 1;
+      const uint32_t par = (j >> 1) & 1;
+      int ok = 1;
+      if (lane == 0) {
+        ok = mbar_try_wait(&ready[b], par);
+        for (uint32_t k = 0, lim = ok ? 0u : spin_limit(); k < lim && !ok; ++k) {
+          ok = mbar_try_wait(&ready[b], par);
+          if (!ok && (k & 63) == 63 && *abort_flag) break;
+        }
+        if (!ok) {
+          if (!*abort_flag) set_status(AIB_DEV_TIMEOUT_FULL);
+          *abort_flag = 1;
+        }
+        if (*abort_flag) ok = 0;
+      }
+      if (!__shfl_sync(0xffffffffu, ok, 0)) return;
+      float v = 0.0f;
+      if (lane < R) {
+        const float* part = pbuf + b * pstride + lane * pw;
+        v = part[0];
+        for (int w = 1; w < pw; ++w) v += part[w];
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&free_[b]);
+      finish_segment<MODE>(v, tile, ks, et, xval, y, N, tb, ks0, R, CW, KS, nrows, wsp, wsc, maxp, tiles);
+      ++j;
+    }
+    if (++ks == KS) ks = 0, ++tile;
   }
 }
 
@@ -1130,8 +1224,7 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
 // 128 + 2i, 129 + 2i of that range. Even and odd rows of the warp use different column blocks, which keeps
 // the 16-byte shared loads of a quarter-warp on distinct banks; B column n = 2*sp + par carries x part sp in
 // the column order of parity par, and a row reads its result from the columns of its own parity.
-constexpr int kTcSlotMeta = 128 + 256 * 4;
-constexpr int kTcPrologueRecords = 8;  // x records per consumer thread per prologue batch (K <= 16384: one batch)  // per slot: 32-word exception mask, partials [R rows][2*CW warps]
+constexpr int kTcPrologueRecords = 8;  // x records per consumer thread per prologue batch (K <= 16384: one batch)
 
 // Byte offset of the x record (8 bytes: low pair, high pair) for chunk gc, MMA i, lane quad t, column block
 // blk and part sp. Parts 0 and 1 of all (blk, t) form one 128-byte line per (gc, i) and part 2 a 64-byte line
@@ -1160,17 +1253,19 @@ AIB_DEV float tc_xval(const uint8_t* xr, int nch, int col) {
 // consumer warps share a 24 KB stage and two 544-thread CTAs fit an SM: 32 consumer warps per SM to hide the
 // decode's dependency chains.
 template <int MODE, bool RMS, int NCW, int SPL = 1>
-__global__ void __launch_bounds__(NCW * 32 + 32, (NCW == 16 && SPL == 1) ? 1 : 2)
+__global__ void __launch_bounds__(NCW * 32 + 64, (NCW == 16 && SPL == 1) ? 1 : 2)
     gemv_tc_kernel(const __grid_constant__ CUtensorMap tm8, const __grid_constant__ CUtensorMap tme4, RowsParams p) {
   constexpr int kTcConsumers = NCW * 32;
-  constexpr int kTcThreads = kTcConsumers + 32;
+  constexpr int kTcThreads = kTcConsumers + 64;  // + producer warp + finisher warp
   constexpr int kStage = NCW * 2048 * 3 / 2 / SPL;  // bytes per ring slot: 2048 / SPL weights per consumer warp
   extern __shared__ __align__(1024) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty = full + 16;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + 256);
+  uint64_t* pready = reinterpret_cast<uint64_t*>(smem + 384);  // partial buffers: consumers -> finisher
+  uint64_t* pfree = pready + 2;                                // finisher -> consumers
   float* rms_red = reinterpret_cast<float*>(smem + 512);
-  uint8_t* meta = smem + 1024;  // slot s: uint32 mask[32] at s*kTcSlotMeta, float part[R][2*CW] at +128
+  float* pbuf = reinterpret_cast<float*>(smem + 1024);  // two partial buffers, float [R][PW] each (<= 1 KB)
   uint8_t* xr = smem + p.xs_off;
   int* rps = reinterpret_cast<int*>(smem + p.rps_off);
   int* ecs = reinterpret_cast<int*>(smem + p.ecs_off);
@@ -1190,8 +1285,12 @@ __global__ void __launch_bounds__(NCW * 32 + 32, (NCW == 16 && SPL == 1) ? 1 : 2
   const int first = AIB_GEMV_EARLY ? min(NS, n_st) : 0;
   if (tid == kTcConsumers) {
     for (int s = 0; s < NS; ++s) {
-      mbar_init(&full[s], 2);  // TMA arrival + bookkeeping arrival
+      mbar_init(&full[s], 1);  // the TMA arrival (with the stage's bytes)
       mbar_init(&empty[s], kTcConsumers / 32);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&pready[b], kTcConsumers / 32);
+      mbar_init(&pfree[b], 1);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -1205,7 +1304,6 @@ __global__ void __launch_bounds__(NCW * 32 + 32, (NCW == 16 && SPL == 1) ? 1 : 2
         mbar_arrive_expect_tx(&full[i], kStage);
         tma_load_3d(st, &tm8, &full[i], 0, ks * CW, tile * R);
         tma_load_3d(st + m8_bytes, &tme4, &full[i], 0, ks * CW, tile * R);
-        mbar_arrive(&full[i]);
         if (++ks == KS) ks = 0, ++tile;
       }
     }
@@ -1220,11 +1318,15 @@ __global__ void __launch_bounds__(NCW * 32 + 32, (NCW == 16 && SPL == 1) ? 1 : 2
   const ExcTab et{rps, ecs, evs, staged, e0, row0, p.ec, p.ev, p.m8, p.K, p.base};
   pdl_trigger();
 
-  if (tid >= kTcConsumers) {  // ---------------- producer warp
+  if (tid >= kTcConsumers + 32) {  // ---------------- finisher warp
     auto xval = [&](int col) { return tc_xval(xr, p.nch, col); };
-    produce_wide<MODE>(&tm8, &tme4, ring, meta, kTcSlotMeta, full, empty, abort_flag, et, xval, p.y, p.N, tb, ks0,
-                       n_st, R, CW, KS, NS, nrows, PW, p.wsp, p.wsc, p.maxp, p.tiles, kStage,
-                       g_aib_withhold_copies ? 0 : first);
+    finish_segments<MODE>(pbuf, 256, pready, pfree, abort_flag, et, xval, p.y, p.N, tb, ks0, n_st, R, CW, KS, nrows,
+                          PW, p.wsp, p.wsc, p.maxp, p.tiles);
+    return;
+  }
+  if (tid >= kTcConsumers) {  // ---------------- producer warp: one thread streams the stages
+    if (tid == kTcConsumers)
+      issue_stages(&tm8, &tme4, ring, full, empty, abort_flag, tb, ks0, n_st, first, R, CW, KS, NS, kStage);
     return;
   }
 
@@ -1358,13 +1460,12 @@ __global__ void __launch_bounds__(NCW * 32 + 32, (NCW == 16 && SPL == 1) ? 1 : 2
   float acc[NACC][4];
 #pragma unroll
   for (int a = 0; a < NACC; ++a) acc[a][0] = acc[a][1] = acc[a][2] = acc[a][3] = 0.0f;
-  int s = 0, ph = 0, ks = ks0, tile = tb;
+  int s = 0, ph = 0, ks = ks0, tile = tb, jc = 0;  // jc: segment ends passed
   for (int it = 0; it < n_st; ++it) {
     // warp-uniform: the MMAs below must run with all 32 lanes converged
     const bool ok = __all_sync(0xffffffffu, !aborted && wait_full(&full[s], ph, abort_flag));
     if (!ok) aborted = true;
     const int gc = ks * CW + q;
-    const uint8_t* sm = meta + s * kTcSlotMeta;
     if (ok && gc < p.nch) {
       const uint8_t* st = ring + static_cast<size_t>(s) * kStage;
       uint32_t la[4], ha[4], ea[4], lb[4], hb[4], eb[4];  // the lane's 16 columns (SPL 2: its half, words 0-1)
@@ -1425,6 +1526,8 @@ __global__ void __launch_bounds__(NCW * 32 + 32, (NCW == 16 && SPL == 1) ? 1 : 2
         }
       }
     }
+    __syncwarp();  // the stage's shared loads are done (their values fed the MMAs): release the slot
+    if (lane == 0) mbar_arrive(&empty[s]);
     if (ks == KS - 1 || it == n_st - 1) {  // segment end: row g takes the columns of its parity (quads t = 0..2)
       float vA = par ? (acc[0][1] + acc[1][1]) : (acc[0][0] + acc[1][0]);
       float vB = par ? (acc[0][3] + acc[1][3]) : (acc[0][2] + acc[1][2]);
@@ -1437,19 +1540,38 @@ __global__ void __launch_bounds__(NCW * 32 + 32, (NCW == 16 && SPL == 1) ? 1 : 2
       vB += __shfl_xor_sync(0xffffffffu, vB, 1);
       vA += __shfl_xor_sync(0xffffffffu, vA, 2);
       vB += __shfl_xor_sync(0xffffffffu, vB, 2);
-      if (t == 0) {
-        float* part = reinterpret_cast<float*>(const_cast<uint8_t*>(sm) + 128);
+      // partial buffer jc & 1: wait until the finisher has read its previous contents (segment end jc - 2)
+      const int b = jc & 1;
+      if (jc >= 2 && !aborted) {
+        int fr = 1;
+        if (lane == 0) {
+          const uint32_t fpar = ((jc >> 1) - 1) & 1;
+          fr = mbar_try_wait(&pfree[b], fpar);
+          for (uint32_t k = 0, lim = fr ? 0u : spin_limit(); k < lim && !fr; ++k) {
+            fr = mbar_try_wait(&pfree[b], fpar);
+            if (!fr && (k & 63) == 63 && *abort_flag) break;
+          }
+          if (!fr) {
+            if (!*abort_flag) set_status(AIB_DEV_TIMEOUT_EMPTY);
+            *abort_flag = 1;
+          }
+        }
+        if (!__shfl_sync(0xffffffffu, fr, 0)) aborted = true;
+      }
+      if (t == 0 && !aborted) {
+        float* part = pbuf + b * 256;
         const int wi = (q * 2 + hh) * SPL + half;
         part[rA * PW + wi] = vA;
         part[rB * PW + wi] = vB;
       }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&pready[b]);
+      ++jc;
 #pragma unroll
       for (int a = 0; a < NACC; ++a)
 #pragma unroll
         for (int c = 0; c < 4; ++c) acc[a][c] = 0.0f;
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[s]);
     if (++ks == KS) ks = 0, ++tile;
     if (++s == NS) s = 0, ph ^= 1;
   }
@@ -1726,13 +1848,14 @@ constexpr size_t kSmemPair = 113 * 1024;  // two CTAs per SM (228 KB per SM, 1 K
 template <int NCW, int SPL = 1>
 static int run_tc_var(const aib_c12* c, const float* x, float* y, int mode, const uint16_t* lnw, float eps, void* ws,
                       size_t ws_bytes, cudaStream_t s) {
-  constexpr int kThreadsV = NCW * 32 + 32;
+  constexpr int kThreadsV = NCW * 32 + 64;
   constexpr size_t kStage = static_cast<size_t>(NCW) * 2048 * 3 / 2 / SPL;
   constexpr bool kPair = !(NCW == 16 && SPL == 1);  // two CTAs per SM
   const size_t smem_max = kPair ? kSmemPair : kSmemMax;
   const int nch = c->K / 256;
   const int CW = kStage == 49152 ? (nch % 8 == 0 ? 8 : 4) : 4;
   const int R = static_cast<int>(kStage / 384) / CW, KS = nch / CW;
+  if (R * 2 * CW * SPL > 256) return fail(AIB_ENOTSUP, "aib_gemv_c12: partial buffer too small");
   const int tiles = (c->N + R - 1) / R;
   const int max_grid = kPair ? 2 * sm_count() : sm_count();
   const StreamK sk = streamk_plan(tiles, KS, R);
@@ -1740,12 +1863,12 @@ static int run_tc_var(const aib_c12* c, const float* x, float* y, int mode, cons
   const int grid = use_sk ? sk.grid : std::min(tiles, max_grid);
   const int per = static_cast<int>((static_cast<long long>(tiles) * KS + grid - 1) / grid);
   const int rows_max = use_sk ? ((per + KS - 1) / KS + 1) * R : ((tiles + grid - 1) / grid) * R;
-  // layout: header + NS slot records, x records (6 bytes per column), row pointers, staged exception
-  // columns (at least 1024), ring; the deepest ring that fits
+  // layout: header, two partial buffers, x records (6 bytes per column), row pointers, staged exception
+  // columns, ring; the deepest ring that fits
   int NS = 8;
   size_t xs_off = 0, rps_off = 0, ecs_off = 0;
   for (; NS >= 2; --NS) {
-    xs_off = 1024 + static_cast<size_t>(NS) * kTcSlotMeta;
+    xs_off = 1024 + 2 * 1024;
     rps_off = xs_off + static_cast<size_t>(nch) * 1536;
     ecs_off = rps_off + ((static_cast<size_t>(rows_max + 1) * 4 + 127) / 128) * 128;
     const size_t ring_need = ((ecs_off + 1023) / 1024) * 1024;  // staged exception columns take what is left
