@@ -33,6 +33,9 @@
 #ifndef AIB_GEMV_LOWNIB2
 #define AIB_GEMV_LOWNIB2 0  // low-nibble codes with one mask and one multiply-add (instead of two multiply-adds)
 #endif
+#ifndef AIB_GEMV_EVICT_FIRST
+#define AIB_GEMV_EVICT_FIRST 1  // weight copies with an L2 evict-first policy
+#endif
 #ifndef AIB_GEMV_ACC
 #define AIB_GEMV_ACC 2  // accumulator chains per consumer warp in the tensor-core T = 1 kernel (2 or 4)
 #endif
@@ -757,9 +760,11 @@ struct ExcTab {  // the CTA's exceptions: CSR slice in shared memory (columns + 
 // tile; the lanes add the exception corrections sum_e (v_e - G_e) * x[c_e] over the segment's exceptions (the
 // consumers decode every element, exceptions included, as a finite stand-in G_e -- see exc_garbage) in column
 // order and write y; a segment that is only part of its tile goes through the stream-K workspace. Warp-wide.
+// yold: (modes 1, 2, whole segments) y[row] read ahead of time, used when use_yold.
 template <int MODE, typename XF>
 AIB_DEV void finish_segment(float v, int ftile, int fks, const ExcTab& et, XF xval, float* y, int N, int tb, int ks0,
-                            int R, int CW, int KS, int nrows, float* wsp, int* wsc, int maxp, int tiles) {
+                            int R, int CW, int KS, int nrows, float* wsp, int* wsc, int maxp, int tiles,
+                            float yold = 0.0f, bool use_yold = false) {
   const int lane = threadIdx.x & 31;
   const int seg_lo = ftile == tb ? ks0 : 0;
   const bool whole = seg_lo == 0 && fks == KS - 1;
@@ -786,7 +791,7 @@ AIB_DEV void finish_segment(float v, int ftile, int fks, const ExcTab& et, XF xv
       if (MODE == 0)
         y[row] = v;
       else
-        y[row] += v;
+        y[row] = (use_yold ? yold : y[row]) + v;
     }
     return;
   }
@@ -898,6 +903,7 @@ AIB_DEV void issue_stages(const CUtensorMap* tm8, const CUtensorMap* tme4, uint8
                           int CW, int KS, int NS, uint32_t stage_bytes) {
   if (g_aib_withhold_copies) return;
   const uint32_t m8_bytes = static_cast<uint32_t>(R * CW * 256);
+  const uint64_t pol = l2_evict_first();
   int ks = ks0 + first, tile = tb;
   tile += ks / KS;
   ks %= KS;
@@ -919,10 +925,58 @@ AIB_DEV void issue_stages(const CUtensorMap* tm8, const CUtensorMap* tme4, uint8
     }
     uint8_t* st = ring + static_cast<size_t>(s) * stage_bytes;
     mbar_arrive_expect_tx(&full[s], stage_bytes);
-    tma_load_3d(st, tm8, &full[s], 0, ks * CW, tile * R);
-    tma_load_3d(st + m8_bytes, tme4, &full[s], 0, ks * CW, tile * R);
+    if (AIB_GEMV_EVICT_FIRST) {
+      tma_load_3d_hint(st, tm8, &full[s], 0, ks * CW, tile * R, pol);
+      tma_load_3d_hint(st + m8_bytes, tme4, &full[s], 0, ks * CW, tile * R, pol);
+    } else {
+      tma_load_3d(st, tm8, &full[s], 0, ks * CW, tile * R);
+      tma_load_3d(st + m8_bytes, tme4, &full[s], 0, ks * CW, tile * R);
+    }
     if (++ks == KS) ks = 0, ++tile;
   }
+}
+
+// Byte offset of the x record (8 bytes: low pair, high pair) for chunk gc, MMA i, lane quad t, column block
+// blk and part sp. Parts 0 and 1 of all (blk, t) form one 128-byte line per (gc, i) and part 2 a 64-byte line
+// in a second region (nch*8*128 bytes further), so each half-warp's 8-byte loads hit 16 distinct bank pairs.
+AIB_DEV int tc_xrec(int nch, int gc, int i, int blk, int t, int sp) {
+  const int gi = gc * 8 + i;
+  return sp < 2 ? gi * 128 + (blk * 2 + sp) * 32 + t * 8 : nch * 1024 + gi * 64 + blk * 32 + t * 8;
+}
+// Exact value of x[col] from its three bf16 parts in the records.
+AIB_DEV float tc_xval(const uint8_t* xr, int nch, int col) {
+  const int gc = col >> 8, cc = col & 255, hf = cc >> 7, c = cc & 127;
+  const int b2 = c >> 6, t2 = (c >> 4) & 3, i2 = (c & 15) >> 1, sh = (c & 1) * 16;
+  float parts[3];
+#pragma unroll
+  for (int s2 = 0; s2 < 3; ++s2) {
+    const uint32_t wv = *reinterpret_cast<const uint32_t*>(xr + tc_xrec(nch, gc, i2, b2, t2, s2) + hf * 4);
+    parts[s2] = bf16_to_f32(static_cast<uint16_t>(wv >> sh));
+  }
+  return (parts[0] + parts[1]) + parts[2];
+}
+
+struct TcXval {  // x[col] of the tensor-core kernel's three-part records
+  const uint8_t* xr;
+  int nch;
+  AIB_DEV float operator()(int col) const { return tc_xval(xr, nch, col); }
+};
+
+// One segment of the finisher: the rows' partial sums (warp order), the buffer's release, the segment's finish.
+template <int MODE>
+AIB_DEV void finish_tc(const float* part, int pw, uint64_t* free_bar, float yold, bool use_yold, int ftile, int fks,
+                       const ExcTab& et, TcXval xval, float* y, int N, int tb, int ks0, int R, int CW, int KS,
+                       int nrows, float* wsp, int* wsc, int maxp, int tiles) {
+  const int lane = threadIdx.x & 31;
+  float v = 0.0f;
+  if (lane < R) {
+    const float* pp = part + lane * pw;
+    v = pp[0];
+    for (int w = 1; w < pw; ++w) v += pp[w];
+  }
+  __syncwarp();
+  if (lane == 0) mbar_arrive(free_bar);
+  finish_segment<MODE>(v, ftile, fks, et, xval, y, N, tb, ks0, R, CW, KS, nrows, wsp, wsc, maxp, tiles, yold, use_yold);
 }
 
 // The finisher warp walks the same stage sequence as the consumers. At the j-th segment end the consumer warps
@@ -930,16 +984,21 @@ AIB_DEV void issue_stages(const CUtensorMap* tm8, const CUtensorMap* tme4, uint8
 // finisher adds each row's pw partials in warp order, releases the buffer (free[j & 1]: the consumers reuse it
 // at segment end j + 2) and then finishes the segment -- exception corrections, y -- off the copy and MMA
 // paths. Two buffers: the consumers wait only when the finisher is two segments behind.
-template <int MODE, typename XF>
+template <int MODE>
 AIB_DEV void finish_segments(const float* pbuf, int pstride, uint64_t* ready, uint64_t* free_, volatile int* abort_flag,
-                             const ExcTab& et, XF xval, float* y, int N, int tb, int ks0, int n_st, int R, int CW,
+                             const ExcTab& et, TcXval xval, float* y, int N, int tb, int ks0, int n_st, int R, int CW,
                              int KS, int nrows, int pw, float* wsp, int* wsc, int maxp, int tiles) {
   const int lane = threadIdx.x & 31;
-  pdl_wait();  // y is read (mode 1) and written after the previous kernel's
+  pdl_wait();  // y is read (modes 1, 2) and written after the previous kernel's
   int ks = ks0, tile = tb, j = 0;
   for (int i = 0; i < n_st; ++i) {
     if (ks == KS - 1 || i == n_st - 1) {
       const int b = j & 1;
+      // a whole segment of mode 1 / 2 adds to y: read y[row] now, ahead of the wait
+      const bool whole = (tile == tb ? ks0 : 0) == 0 && ks == KS - 1;
+      const int row = tile * R + lane;
+      const bool use_yold = (MODE == 1 || MODE == 2) && whole;
+      const float yold = use_yold && lane < R && row < N ? y[row] : 0.0f;
       const uint32_t par = (j >> 1) & 1;
       int ok = 1;
       if (lane == 0) {
@@ -955,15 +1014,8 @@ AIB_DEV void finish_segments(const float* pbuf, int pstride, uint64_t* ready, ui
         if (*abort_flag) ok = 0;
       }
       if (!__shfl_sync(0xffffffffu, ok, 0)) return;
-      float v = 0.0f;
-      if (lane < R) {
-        const float* part = pbuf + b * pstride + lane * pw;
-        v = part[0];
-        for (int w = 1; w < pw; ++w) v += part[w];
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&free_[b]);
-      finish_segment<MODE>(v, tile, ks, et, xval, y, N, tb, ks0, R, CW, KS, nrows, wsp, wsc, maxp, tiles);
+      finish_tc<MODE>(pbuf + b * pstride, pw, &free_[b], yold, use_yold, tile, ks, et, xval, y, N, tb, ks0, R, CW, KS,
+                      nrows, wsp, wsc, maxp, tiles);
       ++j;
     }
     if (++ks == KS) ks = 0, ++tile;
@@ -1226,26 +1278,6 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
 // the column order of parity par, and a row reads its result from the columns of its own parity.
 constexpr int kTcPrologueRecords = 8;  // x records per consumer thread per prologue batch (K <= 16384: one batch)
 
-// Byte offset of the x record (8 bytes: low pair, high pair) for chunk gc, MMA i, lane quad t, column block
-// blk and part sp. Parts 0 and 1 of all (blk, t) form one 128-byte line per (gc, i) and part 2 a 64-byte line
-// in a second region (nch*8*128 bytes further), so each half-warp's 8-byte loads hit 16 distinct bank pairs.
-AIB_DEV int tc_xrec(int nch, int gc, int i, int blk, int t, int sp) {
-  const int gi = gc * 8 + i;
-  return sp < 2 ? gi * 128 + (blk * 2 + sp) * 32 + t * 8 : nch * 1024 + gi * 64 + blk * 32 + t * 8;
-}
-// Exact value of x[col] from its three bf16 parts in the records.
-AIB_DEV float tc_xval(const uint8_t* xr, int nch, int col) {
-  const int gc = col >> 8, cc = col & 255, hf = cc >> 7, c = cc & 127;
-  const int b2 = c >> 6, t2 = (c >> 4) & 3, i2 = (c & 15) >> 1, sh = (c & 1) * 16;
-  float parts[3];
-#pragma unroll
-  for (int s2 = 0; s2 < 3; ++s2) {
-    const uint32_t wv = *reinterpret_cast<const uint32_t*>(xr + tc_xrec(nch, gc, i2, b2, t2, s2) + hf * 4);
-    parts[s2] = bf16_to_f32(static_cast<uint16_t>(wv >> sh));
-  }
-  return (parts[0] + parts[1]) + parts[2];
-}
-
 // NCW consumer warps: 16 with 48 KB stages (R * CW = 128, one CTA per SM), or 8 with 24 KB stages (R * CW = 64,
 // <= 113 KB of shared memory and 288 threads, so two CTAs share an SM: two of the same launch, or the tail of one
 // launch and the head of the next, whose producer then streams its weights while the previous CTA drains).
@@ -1298,12 +1330,18 @@ __global__ void __launch_bounds__(NCW * 32 + 64, (NCW == 16 && SPL == 1) ? 1 : 2
       prefetch_tensormap(&tm8);
       prefetch_tensormap(&tme4);
       const uint32_t m8_bytes = static_cast<uint32_t>(R * CW * 256);
+      const uint64_t pol = l2_evict_first();
       int ks = ks0, tile = tb;
       for (int i = 0; i < first; ++i) {
         uint8_t* st = ring + static_cast<size_t>(i) * kStage;
         mbar_arrive_expect_tx(&full[i], kStage);
-        tma_load_3d(st, &tm8, &full[i], 0, ks * CW, tile * R);
-        tma_load_3d(st + m8_bytes, &tme4, &full[i], 0, ks * CW, tile * R);
+        if (AIB_GEMV_EVICT_FIRST) {
+          tma_load_3d_hint(st, &tm8, &full[i], 0, ks * CW, tile * R, pol);
+          tma_load_3d_hint(st + m8_bytes, &tme4, &full[i], 0, ks * CW, tile * R, pol);
+        } else {
+          tma_load_3d(st, &tm8, &full[i], 0, ks * CW, tile * R);
+          tma_load_3d(st + m8_bytes, &tme4, &full[i], 0, ks * CW, tile * R);
+        }
         if (++ks == KS) ks = 0, ++tile;
       }
     }
@@ -1319,9 +1357,8 @@ __global__ void __launch_bounds__(NCW * 32 + 64, (NCW == 16 && SPL == 1) ? 1 : 2
   pdl_trigger();
 
   if (tid >= kTcConsumers + 32) {  // ---------------- finisher warp
-    auto xval = [&](int col) { return tc_xval(xr, p.nch, col); };
-    finish_segments<MODE>(pbuf, 256, pready, pfree, abort_flag, et, xval, p.y, p.N, tb, ks0, n_st, R, CW, KS, nrows,
-                          PW, p.wsp, p.wsc, p.maxp, p.tiles);
+    finish_segments<MODE>(pbuf, 256, pready, pfree, abort_flag, et, TcXval{xr, p.nch}, p.y, p.N, tb, ks0, n_st, R, CW,
+                          KS, nrows, PW, p.wsp, p.wsc, p.maxp, p.tiles);
     return;
   }
   if (tid >= kTcConsumers) {  // ---------------- producer warp: one thread streams the stages
