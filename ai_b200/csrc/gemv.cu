@@ -760,16 +760,19 @@ struct ExcTab {  // the CTA's exceptions: CSR slice in shared memory (columns + 
 // tile; the lanes add the exception corrections sum_e (v_e - G_e) * x[c_e] over the segment's exceptions (the
 // consumers decode every element, exceptions included, as a finite stand-in G_e -- see exc_garbage) in column
 // order and write y; a segment that is only part of its tile goes through the stream-K workspace. Warp-wide.
-// yold: (modes 1, 2, whole segments) y[row] read ahead of time, used when use_yold.
+// yold: (modes 1, 2, whole segments) y[row] read ahead of time, used when use_yold. have_corr: the segment's
+// correction was computed ahead of time (corr0, the same sum in the same order).
 template <int MODE, typename XF>
 AIB_DEV void finish_segment(float v, int ftile, int fks, const ExcTab& et, XF xval, float* y, int N, int tb, int ks0,
                             int R, int CW, int KS, int nrows, float* wsp, int* wsc, int maxp, int tiles,
-                            float yold = 0.0f, bool use_yold = false) {
+                            float yold = 0.0f, bool use_yold = false, bool have_corr = false, float corr0 = 0.0f) {
   const int lane = threadIdx.x & 31;
   const int seg_lo = ftile == tb ? ks0 : 0;
   const bool whole = seg_lo == 0 && fks == KS - 1;
   const int lr = (ftile - tb) * R + lane, row = ftile * R + lane;
-  if (lane < R && lr < nrows) {  // exception corrections of the segment's columns, in column order
+  if (have_corr) {
+    if (lane < R && lr < nrows) v += corr0;
+  } else if (lane < R && lr < nrows) {  // exception corrections of the segment's columns, in column order
     const int lo = seg_lo * CW * 256, hi = (fks + 1) * CW * 256;
     const int qa = et.rps[lr] - et.e0, qb = et.rps[lr + 1] - et.e0;
     float corr = 0.0f;
@@ -964,9 +967,9 @@ struct TcXval {  // x[col] of the tensor-core kernel's three-part records
 
 // One segment of the finisher: the rows' partial sums (warp order), the buffer's release, the segment's finish.
 template <int MODE>
-AIB_DEV void finish_tc(const float* part, int pw, uint64_t* free_bar, float yold, bool use_yold, int ftile, int fks,
-                       const ExcTab& et, TcXval xval, float* y, int N, int tb, int ks0, int R, int CW, int KS,
-                       int nrows, float* wsp, int* wsc, int maxp, int tiles) {
+AIB_DEV void finish_tc(const float* part, int pw, uint64_t* free_bar, float yold, bool use_yold, bool have_corr,
+                       float corr, int ftile, int fks, const ExcTab& et, TcXval xval, float* y, int N, int tb, int ks0,
+                       int R, int CW, int KS, int nrows, float* wsp, int* wsc, int maxp, int tiles) {
   const int lane = threadIdx.x & 31;
   float v = 0.0f;
   if (lane < R) {
@@ -976,49 +979,135 @@ AIB_DEV void finish_tc(const float* part, int pw, uint64_t* free_bar, float yold
   }
   __syncwarp();
   if (lane == 0) mbar_arrive(free_bar);
-  finish_segment<MODE>(v, ftile, fks, et, xval, y, N, tb, ks0, R, CW, KS, nrows, wsp, wsc, maxp, tiles, yold, use_yold);
+  finish_segment<MODE>(v, ftile, fks, et, xval, y, N, tb, ks0, R, CW, KS, nrows, wsp, wsc, maxp, tiles, yold, use_yold,
+                       have_corr, corr);
 }
 
-// The finisher warp walks the same stage sequence as the consumers. At the j-th segment end the consumer warps
-// have left one partial per (row, warp) in buffer j & 1 (float [R][pw]) and arrived on ready[j & 1]; the
-// finisher adds each row's pw partials in warp order, releases the buffer (free[j & 1]: the consumers reuse it
-// at segment end j + 2) and then finishes the segment -- exception corrections, y -- off the copy and MMA
-// paths. Two buffers: the consumers wait only when the finisher is two segments behind.
+// The finisher warp stages the CTA's slice of the exception CSR (weights only, so before the grid-dependency
+// wait, and off the consumers' path): the row pointers, then each exception's column and correction v - G (G:
+// what the decode makes of the element, from its m8 byte). Every batch issues all its loads (8 per lane) before
+// using any, so it costs one memory round trip. False when the exceptions do not fit (ecap): the finish then
+// reads them from global memory.
+AIB_DEV bool stage_csr_warp(int* rps, int* ecs, float* evs, int ecap, int nrows, int row0, const int32_t* rp,
+                            const int32_t* ec, const float* ev, const uint8_t* m8, int K, int base) {
+  const int lane = threadIdx.x & 31;
+  for (int b0 = 0; b0 <= nrows; b0 += 256) {
+    int v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int i = b0 + lane + 32 * u;
+      v[u] = i <= nrows ? rp[row0 + i] : 0;
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int i = b0 + lane + 32 * u;
+      if (i <= nrows) rps[i] = v[u];
+    }
+  }
+  __syncwarp();
+  const int e0 = rps[0], n_exc = rps[nrows] - e0;
+  if (n_exc > ecap) return false;
+  for (int b0 = 0; b0 < n_exc; b0 += 256) {
+    int col[8], lr[8];
+    float val[8];
+    uint32_t mb[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int q = b0 + lane + 32 * u;
+      col[u] = 0;
+      val[u] = 0.0f;
+      if (q < n_exc) {
+        col[u] = ec[e0 + q];
+        val[u] = ev[e0 + q];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {  // the exception's row: the last one whose CSR range starts at or before q
+      const int q = b0 + lane + 32 * u;
+      int lo = 0, hi = nrows - 1;
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (rps[mid] - e0 <= q)
+          lo = mid;
+        else
+          hi = mid - 1;
+      }
+      lr[u] = lo;
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int q = b0 + lane + 32 * u;
+      mb[u] = q < n_exc ? m8[static_cast<size_t>(row0 + lr[u]) * K + col[u]] : 0u;
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int q = b0 + lane + 32 * u;
+      if (q < n_exc) {
+        ecs[q] = col[u];
+        evs[q] = val[u] - exc_garbage(mb[u], base);
+      }
+    }
+  }
+  __syncwarp();
+  return true;
+}
+
+// The finisher warp walks the consumers' segments (maximal runs of one tile's stages). At the j-th segment end
+// the consumer warps have left one partial per (row, warp) in buffer j & 1 (float [R][pw]) and arrived on
+// ready[j & 1]; the finisher adds each row's pw partials in warp order, releases the buffer (free[j & 1]: the
+// consumers reuse it at segment end j + 2), adds the exception correction and writes y. A whole tile's
+// correction sum_e (v_e - G_e) * x[c_e] and (modes 1, 2) the y it adds to are computed / read before the wait,
+// once the consumers have published the x records (xready), so that only the partial sums and the store follow
+// the consumers' last stage. Two buffers: the consumers wait only when the finisher is two segments behind.
 template <int MODE>
-AIB_DEV void finish_segments(const float* pbuf, int pstride, uint64_t* ready, uint64_t* free_, volatile int* abort_flag,
-                             const ExcTab& et, TcXval xval, float* y, int N, int tb, int ks0, int n_st, int R, int CW,
-                             int KS, int nrows, int pw, float* wsp, int* wsc, int maxp, int tiles) {
+AIB_DEV void finish_segments(const float* pbuf, int pstride, uint64_t* ready, uint64_t* free_, uint64_t* xready,
+                             volatile int* abort_flag, const ExcTab& et, TcXval xval, float* y, int N, int tb, int ks0,
+                             int n_st, int R, int CW, int KS, int nrows, int pw, float* wsp, int* wsc, int maxp,
+                             int tiles) {
   const int lane = threadIdx.x & 31;
   pdl_wait();  // y is read (modes 1, 2) and written after the previous kernel's
-  int ks = ks0, tile = tb, j = 0;
-  for (int i = 0; i < n_st; ++i) {
-    if (ks == KS - 1 || i == n_st - 1) {
-      const int b = j & 1;
-      // a whole segment of mode 1 / 2 adds to y: read y[row] now, ahead of the wait
-      const bool whole = (tile == tb ? ks0 : 0) == 0 && ks == KS - 1;
-      const int row = tile * R + lane;
-      const bool use_yold = (MODE == 1 || MODE == 2) && whole;
-      const float yold = use_yold && lane < R && row < N ? y[row] : 0.0f;
-      const uint32_t par = (j >> 1) & 1;
-      int ok = 1;
-      if (lane == 0) {
-        ok = mbar_try_wait(&ready[b], par);
-        for (uint32_t k = 0, lim = ok ? 0u : spin_limit(); k < lim && !ok; ++k) {
-          ok = mbar_try_wait(&ready[b], par);
-          if (!ok && (k & 63) == 63 && *abort_flag) break;
-        }
-        if (!ok) {
-          if (!*abort_flag) set_status(AIB_DEV_TIMEOUT_FULL);
-          *abort_flag = 1;
-        }
-        if (*abort_flag) ok = 0;
+  // bounded wait on a barrier that lane 0 polls; false (abort raised) when it runs out or another role aborted
+  auto wait_bar = [&](uint64_t* bar, uint32_t par) -> bool {
+    int ok = 1;
+    if (lane == 0) {
+      ok = mbar_try_wait(bar, par);
+      for (uint32_t k = 0, lim = ok ? 0u : spin_limit(); k < lim && !ok; ++k) {
+        ok = mbar_try_wait(bar, par);
+        if (!ok && (k & 63) == 63 && *abort_flag) break;
       }
-      if (!__shfl_sync(0xffffffffu, ok, 0)) return;
-      finish_tc<MODE>(pbuf + b * pstride, pw, &free_[b], yold, use_yold, tile, ks, et, xval, y, N, tb, ks0, R, CW, KS,
-                      nrows, wsp, wsc, maxp, tiles);
-      ++j;
+      if (!ok) {
+        if (!*abort_flag) set_status(AIB_DEV_TIMEOUT_FULL);
+        *abort_flag = 1;
+      }
+      if (*abort_flag) ok = 0;
     }
-    if (++ks == KS) ks = 0, ++tile;
+    return __shfl_sync(0xffffffffu, ok, 0) != 0;
+  };
+  if (!wait_bar(xready, 0)) return;
+  int ks = ks0, tile = tb, j = 0;
+  for (int i = 0; i < n_st;) {
+    const int len = min(KS - ks, n_st - i), fks = ks + len - 1;
+    const bool whole = ks == 0 && fks == KS - 1;
+    const int b = j & 1, lr = (tile - tb) * R + lane, row = tile * R + lane;
+    float corr = 0.0f;
+    if (whole && lane < R && lr < nrows) {  // all of the row's exceptions, in column order
+      const int qa = et.rps[lr] - et.e0, qb = et.rps[lr + 1] - et.e0;
+      for (int q = qa; q < qb; ++q) {
+        const int col = et.staged ? et.ecs[q] : et.ec[et.e0 + q];
+        const float d = et.staged ? et.evs[q]
+                                  : et.ev[et.e0 + q] - exc_garbage(et.m8[static_cast<size_t>(row) * et.K + col], et.base);
+        corr = fmaf(d, xval(col), corr);
+      }
+    }
+    const bool use_yold = (MODE == 1 || MODE == 2) && whole;
+    const float yold = use_yold && lane < R && row < N ? y[row] : 0.0f;
+    if (!wait_bar(&ready[b], (j >> 1) & 1)) return;
+    finish_tc<MODE>(pbuf + b * pstride, pw, &free_[b], yold, use_yold, whole, corr, tile, fks, et, xval, y, N, tb, ks0,
+                    R, CW, KS, nrows, wsp, wsc, maxp, tiles);
+    i += len;
+    ks = 0;
+    ++tile;
+    ++j;
   }
 }
 
@@ -1296,6 +1385,7 @@ __global__ void __launch_bounds__(NCW * 32 + 64, (NCW == 16 && SPL == 1) ? 1 : 2
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + 256);
   uint64_t* pready = reinterpret_cast<uint64_t*>(smem + 384);  // partial buffers: consumers -> finisher
   uint64_t* pfree = pready + 2;                                // finisher -> consumers
+  uint64_t* xready = pready + 4;                               // consumers -> finisher: x records built
   float* rms_red = reinterpret_cast<float*>(smem + 512);
   float* pbuf = reinterpret_cast<float*>(smem + 1024);  // two partial buffers, float [R][PW] each (<= 1 KB)
   uint8_t* xr = smem + p.xs_off;
@@ -1311,9 +1401,8 @@ __global__ void __launch_bounds__(NCW * 32 + 64, (NCW == 16 && SPL == 1) ? 1 : 2
   const int n_st = sh_.n_st;
   const int row0 = sh_.row0;
   const int nrows = sh_.nrows;
-  // The producer thread initialises the barriers and, before the shared prologue below (row pointers and
-  // exception staging: global round trips), issues the ring's first stages, so the weights start streaming at
-  // once; the slots have no previous partials, so both of each stage's arrivals are made here.
+  // The producer thread initialises the barriers and issues the ring's first stages, so the weights start
+  // streaming at once (they do not depend on the previous kernel).
   const int first = AIB_GEMV_EARLY ? min(NS, n_st) : 0;
   if (tid == kTcConsumers) {
     for (int s = 0; s < NS; ++s) {
@@ -1324,6 +1413,7 @@ __global__ void __launch_bounds__(NCW * 32 + 64, (NCW == 16 && SPL == 1) ? 1 : 2
       mbar_init(&pready[b], kTcConsumers / 32);
       mbar_init(&pfree[b], 1);
     }
+    mbar_init(xready, 1);
     *abort_flag = 0;
     fence_mbar_init();
     if (!g_aib_withhold_copies) {
@@ -1346,19 +1436,15 @@ __global__ void __launch_bounds__(NCW * 32 + 64, (NCW == 16 && SPL == 1) ? 1 : 2
       }
     }
   }
-  for (int i = tid; i <= nrows; i += kTcThreads) rps[i] = p.rp[row0 + i];
   __syncthreads();
-  const int e0 = rps[0], n_exc = rps[nrows] - e0;
-  const bool staged = n_exc <= p.ecap;
-  float* evs = reinterpret_cast<float*>(ecs + p.ecap);
-  if (staged) stage_exceptions(ecs, evs, rps, nrows, row0, e0, p.ec, p.ev, p.m8, p.K, p.base, kTcThreads);
-  __syncthreads();
-  const ExcTab et{rps, ecs, evs, staged, e0, row0, p.ec, p.ev, p.m8, p.K, p.base};
   pdl_trigger();
 
-  if (tid >= kTcConsumers + 32) {  // ---------------- finisher warp
-    finish_segments<MODE>(pbuf, 256, pready, pfree, abort_flag, et, TcXval{xr, p.nch}, p.y, p.N, tb, ks0, n_st, R, CW,
-                          KS, nrows, PW, p.wsp, p.wsc, p.maxp, p.tiles);
+  if (tid >= kTcConsumers + 32) {  // ---------------- finisher warp: the CSR slice, then the segments
+    float* evs = reinterpret_cast<float*>(ecs + p.ecap);
+    const bool staged = stage_csr_warp(rps, ecs, evs, p.ecap, nrows, row0, p.rp, p.ec, p.ev, p.m8, p.K, p.base);
+    const ExcTab et{rps, ecs, evs, staged, rps[0], row0, p.ec, p.ev, p.m8, p.K, p.base};
+    finish_segments<MODE>(pbuf, 256, pready, pfree, xready, abort_flag, et, TcXval{xr, p.nch}, p.y, p.N, tb, ks0, n_st,
+                          R, CW, KS, nrows, PW, p.wsp, p.wsc, p.maxp, p.tiles);
     return;
   }
   if (tid >= kTcConsumers) {  // ---------------- producer warp: one thread streams the stages
@@ -1477,6 +1563,7 @@ __global__ void __launch_bounds__(NCW * 32 + 64, (NCW == 16 && SPL == 1) ? 1 : 2
     }
   }
   named_sync(1, kTcConsumers);
+  if (tid == 0) mbar_arrive(xready);  // the finisher reads x records for the exception corrections
 
   const int warp = tid >> 5, g = lane >> 2, t = lane & 3;
   const int half = SPL == 2 ? (warp & 1) : 0, wu = SPL == 2 ? (warp >> 1) : warp;  // wu: the warp's unit
