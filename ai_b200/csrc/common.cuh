@@ -122,6 +122,16 @@ AIB_DEV void tma_load_3d_hint(void* smem_dst, const CUtensorMap* map, uint64_t* 
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "l"(policy)
       : "memory");
 }
+// Flags between CTAs of one grid (GPU scope): a release store after the data it publishes, an acquire load
+// before the data it guards.
+AIB_DEV void st_release_gpu(int* p, int v) {
+  asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+AIB_DEV int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
 AIB_DEV uint64_t l2_evict_first() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));

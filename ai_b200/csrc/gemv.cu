@@ -760,19 +760,14 @@ struct ExcTab {  // the CTA's exceptions: CSR slice in shared memory (columns + 
 // tile; the lanes add the exception corrections sum_e (v_e - G_e) * x[c_e] over the segment's exceptions (the
 // consumers decode every element, exceptions included, as a finite stand-in G_e -- see exc_garbage) in column
 // order and write y; a segment that is only part of its tile goes through the stream-K workspace. Warp-wide.
-// yold: (modes 1, 2, whole segments) y[row] read ahead of time, used when use_yold. have_corr: the segment's
-// correction was computed ahead of time (corr0, the same sum in the same order).
 template <int MODE, typename XF>
 AIB_DEV void finish_segment(float v, int ftile, int fks, const ExcTab& et, XF xval, float* y, int N, int tb, int ks0,
-                            int R, int CW, int KS, int nrows, float* wsp, int* wsc, int maxp, int tiles,
-                            float yold = 0.0f, bool use_yold = false, bool have_corr = false, float corr0 = 0.0f) {
+                            int R, int CW, int KS, int nrows, float* wsp, int* wsc, int maxp, int tiles) {
   const int lane = threadIdx.x & 31;
   const int seg_lo = ftile == tb ? ks0 : 0;
   const bool whole = seg_lo == 0 && fks == KS - 1;
   const int lr = (ftile - tb) * R + lane, row = ftile * R + lane;
-  if (have_corr) {
-    if (lane < R && lr < nrows) v += corr0;
-  } else if (lane < R && lr < nrows) {  // exception corrections of the segment's columns, in column order
+  if (lane < R && lr < nrows) {  // exception corrections of the segment's columns, in column order
     const int lo = seg_lo * CW * 256, hi = (fks + 1) * CW * 256;
     const int qa = et.rps[lr] - et.e0, qb = et.rps[lr + 1] - et.e0;
     float corr = 0.0f;
@@ -794,7 +789,7 @@ AIB_DEV void finish_segment(float v, int ftile, int fks, const ExcTab& et, XF xv
       if (MODE == 0)
         y[row] = v;
       else
-        y[row] = (use_yold ? yold : y[row]) + v;
+        y[row] += v;
     }
     return;
   }
@@ -965,22 +960,36 @@ struct TcXval {  // x[col] of the tensor-core kernel's three-part records
   AIB_DEV float operator()(int col) const { return tc_xval(xr, nch, col); }
 };
 
-// One segment of the finisher: the rows' partial sums (warp order), the buffer's release, the segment's finish.
-template <int MODE>
-AIB_DEV void finish_tc(const float* part, int pw, uint64_t* free_bar, float yold, bool use_yold, bool have_corr,
-                       float corr, int ftile, int fks, const ExcTab& et, TcXval xval, float* y, int N, int tb, int ks0,
-                       int R, int CW, int KS, int nrows, float* wsp, int* wsc, int maxp, int tiles) {
-  const int lane = threadIdx.x & 31;
-  float v = 0.0f;
-  if (lane < R) {
-    const float* pp = part + lane * pw;
-    v = pp[0];
-    for (int w = 1; w < pw; ++w) v += pp[w];
+// Exception correction of tile-local row lr over the columns [lo, hi): sum_e (v_e - G_e) * x[c_e] in column order
+// (the consumers decode every element, exceptions included, as a finite stand-in G_e -- see exc_garbage).
+AIB_DEV float row_correction(const ExcTab& et, TcXval xval, int lr, int row, int lo, int hi) {
+  const int qa = et.rps[lr] - et.e0, qb = et.rps[lr + 1] - et.e0;
+  float corr = 0.0f;
+  for (int q = qa; q < qb; ++q) {
+    const int col = et.staged ? et.ecs[q] : et.ec[et.e0 + q];
+    if (col >= hi) break;
+    if (col < lo) continue;
+    const float d = et.staged ? et.evs[q]
+                              : et.ev[et.e0 + q] - exc_garbage(et.m8[static_cast<size_t>(row) * et.K + col], et.base);
+    corr = fmaf(d, xval(col), corr);
   }
-  __syncwarp();
-  if (lane == 0) mbar_arrive(free_bar);
-  finish_segment<MODE>(v, ftile, fks, et, xval, y, N, tb, ks0, R, CW, KS, nrows, wsp, wsc, maxp, tiles, yold, use_yold,
-                       have_corr, corr);
+  return corr;
+}
+
+// Writes finished row values (lane r < R: row `row`): mode 0 stores, modes 1 / 2 add to y (yold: y[row] read
+// ahead, when use_yold), mode 3 stores silu(gate) * up of the lane pairs (2i, 2i + 1). Warp-wide.
+template <int MODE>
+AIB_DEV void store_rows(float v, float yold, bool use_yold, int row, int R, int N, float* y) {
+  const int lane = threadIdx.x & 31;
+  if (MODE == 3) {
+    const float vu = __shfl_down_sync(0xffffffffu, v, 1);
+    if (lane < R && !(lane & 1) && row + 1 < N) y[row >> 1] = silu_mul(v, vu);
+  } else if (lane < R && row < N) {
+    if (MODE == 0)
+      y[row] = v;
+    else
+      y[row] = (use_yold ? yold : y[row]) + v;
+  }
 }
 
 // The finisher warp stages the CTA's slice of the exception CSR (weights only, so before the grid-dependency
@@ -1056,9 +1065,16 @@ AIB_DEV bool stage_csr_warp(int* rps, int* ecs, float* evs, int ecap, int nrows,
 // the consumer warps have left one partial per (row, warp) in buffer j & 1 (float [R][pw]) and arrived on
 // ready[j & 1]; the finisher adds each row's pw partials in warp order, releases the buffer (free[j & 1]: the
 // consumers reuse it at segment end j + 2), adds the exception correction and writes y. A whole tile's
-// correction sum_e (v_e - G_e) * x[c_e] and (modes 1, 2) the y it adds to are computed / read before the wait,
-// once the consumers have published the x records (xready), so that only the partial sums and the store follow
-// the consumers' last stage. Two buffers: the consumers wait only when the finisher is two segments behind.
+// correction and (modes 1, 2) the y it adds to are computed / read before the wait, once the consumers have
+// published the x records (xready), so that only the partial sums and the store follow the consumers' last
+// stage. Two buffers: the consumers wait only when the finisher is two segments behind.
+//
+// Stream-K (a workspace: the grid splits the tiles * KS stages evenly, so a tile may be split between
+// neighbouring CTAs bf..bl): part pi of a split tile (its CTA's share, exception corrections of its columns
+// included) goes to the workspace slot [tile][pi] with a release flag; CTA bl, which holds the tile's last
+// stage (as the first segment of its range), adds the parts in part order after its other segments -- by then
+// the lower-numbered CTAs, which hold the tile's head in the last segments of their ranges, are finishing too --
+// resets the flags for the next launch and writes y. A CTA only ever waits for lower-numbered CTAs.
 template <int MODE>
 AIB_DEV void finish_segments(const float* pbuf, int pstride, uint64_t* ready, uint64_t* free_, uint64_t* xready,
                              volatile int* abort_flag, const ExcTab& et, TcXval xval, float* y, int N, int tb, int ks0,
@@ -1084,30 +1100,80 @@ AIB_DEV void finish_segments(const float* pbuf, int pstride, uint64_t* ready, ui
     return __shfl_sync(0xffffffffu, ok, 0) != 0;
   };
   if (!wait_bar(xready, 0)) return;
+  const long long nall = static_cast<long long>(tiles) * KS, G = gridDim.x;
+  int def_tile = -1, def_np = 0;  // the split tile this CTA finalizes (at most one: its first segment)
+  float def_v = 0.0f;
   int ks = ks0, tile = tb, j = 0;
   for (int i = 0; i < n_st;) {
     const int len = min(KS - ks, n_st - i), fks = ks + len - 1;
     const bool whole = ks == 0 && fks == KS - 1;
     const int b = j & 1, lr = (tile - tb) * R + lane, row = tile * R + lane;
+    const bool has_row = lane < R && lr < nrows;
     float corr = 0.0f;
-    if (whole && lane < R && lr < nrows) {  // all of the row's exceptions, in column order
-      const int qa = et.rps[lr] - et.e0, qb = et.rps[lr + 1] - et.e0;
-      for (int q = qa; q < qb; ++q) {
-        const int col = et.staged ? et.ecs[q] : et.ec[et.e0 + q];
-        const float d = et.staged ? et.evs[q]
-                                  : et.ev[et.e0 + q] - exc_garbage(et.m8[static_cast<size_t>(row) * et.K + col], et.base);
-        corr = fmaf(d, xval(col), corr);
-      }
-    }
+    if (whole && has_row) corr = row_correction(et, xval, lr, row, 0, KS * CW * 256);
     const bool use_yold = (MODE == 1 || MODE == 2) && whole;
     const float yold = use_yold && lane < R && row < N ? y[row] : 0.0f;
     if (!wait_bar(&ready[b], (j >> 1) & 1)) return;
-    finish_tc<MODE>(pbuf + b * pstride, pw, &free_[b], yold, use_yold, whole, corr, tile, fks, et, xval, y, N, tb, ks0,
-                    R, CW, KS, nrows, wsp, wsc, maxp, tiles);
+    float v = 0.0f;
+    if (lane < R) {
+      const float* pp = pbuf + b * pstride + lane * pw;
+      v = pp[0];
+      for (int w = 1; w < pw; ++w) v += pp[w];
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&free_[b]);
+    if (whole) {
+      if (has_row) v += corr;
+      store_rows<MODE>(v, yold, use_yold, row, R, N, y);
+    } else {
+      if (has_row) v += row_correction(et, xval, lr, row, ks * CW * 256, (fks + 1) * CW * 256);
+      const long long st0 = static_cast<long long>(tile) * KS;
+      const int bf = static_cast<int>(((st0 + 1) * G + nall - 1) / nall - 1);
+      const int bl = static_cast<int>(((st0 + KS) * G + nall - 1) / nall - 1);
+      if (static_cast<int>(blockIdx.x) == bl) {
+        def_tile = tile;
+        def_np = bl - bf + 1;
+        def_v = v;
+      } else {
+        const int pi = static_cast<int>(blockIdx.x) - bf;
+        if (lane < R) wsp[(static_cast<size_t>(tile) * maxp + pi) * R + lane] = v;
+        __threadfence();
+        __syncwarp();
+        if (lane == 0) st_release_gpu(wsc + static_cast<size_t>(tile) * maxp + pi, 1);
+      }
+    }
     i += len;
     ks = 0;
     ++tile;
     ++j;
+  }
+  if (def_tile >= 0) {  // the parts of the split tile whose last stage this CTA held
+    const int* flags = wsc + static_cast<size_t>(def_tile) * maxp;
+    bool ok = true;
+    for (int pi = 0; pi + 1 < def_np && ok; ++pi) {  // all lanes poll (acquire for each lane's reads below)
+      ok = ld_acquire_gpu(flags + pi) == 1;
+      for (uint32_t k = 0, lim = ok ? 0u : spin_limit(); k < lim && !ok; ++k) {
+        ok = ld_acquire_gpu(flags + pi) == 1;
+        if (!ok && (k & 63) == 63 && *abort_flag) break;
+      }
+    }
+    if (!__all_sync(0xffffffffu, ok)) {
+      if (lane == 0) {
+        if (!*abort_flag) set_status(AIB_DEV_TIMEOUT_FULL);
+        *abort_flag = 1;
+      }
+      return;
+    }
+    const float* parts = wsp + static_cast<size_t>(def_tile) * maxp * R;
+    float t = 0.0f;
+    if (lane < R) {
+      t = __ldcg(parts + lane);
+      for (int pi = 1; pi + 1 < def_np; ++pi) t += __ldcg(parts + pi * R + lane);
+      t += def_v;
+    }
+    __syncwarp();
+    for (int pi = lane; pi + 1 < def_np; pi += 32) wsc[static_cast<size_t>(def_tile) * maxp + pi] = 0;  // next launch
+    store_rows<MODE>(t, 0.0f, false, def_tile * R + lane, R, N, y);
   }
 }
 
@@ -1894,17 +1960,20 @@ static int streamk_max_parts(int tiles, int KS, int grid) {
   }
   return mp;
 }
-// Workspace of a wide-stage launch: [tickets: tiles ints, 16-byte padded][partials: tiles x maxp x R floats].
+// Workspace of a wide-stage launch (zero before the first launch; every launch leaves it zero):
+// [ints: tiles x maxp (16-byte padded)][partials: tiles x maxp x R floats]. The tensor-core kernel keeps one
+// ready flag per (tile, part) in the ints, the CUDA-core kernel one ticket per tile (the first `tiles` ints).
 struct StreamK {
   int grid, maxp;
-  size_t bytes;
+  size_t flag_bytes, bytes;
 };
-static StreamK streamk_plan(int tiles, int KS, int R) {
+static StreamK streamk_plan(int tiles, int KS, int R, int max_grid) {
   StreamK k;
   const long long n = static_cast<long long>(tiles) * KS;
-  k.grid = static_cast<int>(std::min<long long>(sm_count(), n));
+  k.grid = static_cast<int>(std::min<long long>(max_grid, n));
   k.maxp = streamk_max_parts(tiles, KS, k.grid);
-  k.bytes = ((static_cast<size_t>(tiles) * 4 + 15) / 16) * 16 + static_cast<size_t>(tiles) * k.maxp * R * 4;
+  k.flag_bytes = ((static_cast<size_t>(tiles) * k.maxp * 4 + 15) / 16) * 16;
+  k.bytes = k.flag_bytes + static_cast<size_t>(tiles) * k.maxp * R * 4;
   return k;
 }
 
@@ -1920,7 +1989,7 @@ static int run_rows(const aib_c12* c, const float* x, float* y, int mode, const 
   const int CW = nch % 16 == 0 ? 16 : (nch % 8 == 0 ? 8 : 4);
   const int R = 128 / CW, KS = nch / CW;
   const int tiles = (c->N + R - 1) / R;
-  const StreamK sk = streamk_plan(tiles, KS, R);
+  const StreamK sk = streamk_plan(tiles, KS, R, sm_count());
   const bool use_sk = ws && ws_bytes >= sk.bytes && !(reinterpret_cast<uintptr_t>(ws) & 15);
   const int grid = use_sk ? sk.grid : std::min(tiles, sm_count());
   const int per = static_cast<int>((static_cast<long long>(tiles) * KS + grid - 1) / grid);
@@ -1939,11 +2008,10 @@ static int run_rows(const aib_c12* c, const float* x, float* y, int mode, const 
   CUtensorMap tm8, tme4;
   int rc = make_maps(c, R, CW, &tm8, &tme4);
   if (rc) return rc;
-  const size_t cnt_bytes = ((static_cast<size_t>(tiles) * 4 + 15) / 16) * 16;
   RowsParams p{static_cast<const uint8_t*>(c->m8), c->rp, c->ec, c->ev, x, y, lnw, eps, c->base, c->N, c->K, nch, R, CW, KS, tiles, NS,
                static_cast<int>(xs_off), static_cast<int>(rps_off), static_cast<int>(ecs_off), ecap,
                static_cast<int>(ring_off), 128u, 8u, 65536u,
-               use_sk ? reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + cnt_bytes) : nullptr,
+               use_sk ? reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + sk.flag_bytes) : nullptr,
                use_sk ? static_cast<int*>(ws) : nullptr, sk.maxp};
   auto go = [&](auto kernel) -> int {
     const int r2 = allow_smem(kernel, smem);
@@ -1982,9 +2050,13 @@ static int run_tc_var(const aib_c12* c, const float* x, float* y, int mode, cons
   if (R * 2 * CW * SPL > 256) return fail(AIB_ENOTSUP, "aib_gemv_c12: partial buffer too small");
   const int tiles = (c->N + R - 1) / R;
   const int max_grid = kPair ? 2 * sm_count() : sm_count();
-  const StreamK sk = streamk_plan(tiles, KS, R);
-  const bool use_sk = !kPair && ws && ws_bytes >= sk.bytes && !(reinterpret_cast<uintptr_t>(ws) & 15);
-  const int grid = use_sk ? sk.grid : std::min(tiles, max_grid);
+  // stream-K (with a workspace) when an even split of the stages shortens the longest CTA's share
+  const StreamK sk = streamk_plan(tiles, KS, R, max_grid);
+  const int whole_grid = std::min(tiles, max_grid);
+  const long long whole_max = static_cast<long long>((tiles + whole_grid - 1) / whole_grid) * KS;
+  const long long sk_max = (static_cast<long long>(tiles) * KS + sk.grid - 1) / sk.grid;
+  const bool use_sk = ws && ws_bytes >= sk.bytes && !(reinterpret_cast<uintptr_t>(ws) & 15) && sk_max < whole_max;
+  const int grid = use_sk ? sk.grid : whole_grid;
   const int per = static_cast<int>((static_cast<long long>(tiles) * KS + grid - 1) / grid);
   const int rows_max = use_sk ? ((per + KS - 1) / KS + 1) * R : ((tiles + grid - 1) / grid) * R;
   // layout: header, two partial buffers, x records (6 bytes per column), row pointers, staged exception
@@ -2005,11 +2077,10 @@ static int run_tc_var(const aib_c12* c, const float* x, float* y, int mode, cons
   CUtensorMap tm8, tme4;
   int rc = make_maps(c, R, CW, &tm8, &tme4);
   if (rc) return rc;
-  const size_t cnt_bytes = ((static_cast<size_t>(tiles) * 4 + 15) / 16) * 16;
   RowsParams p{static_cast<const uint8_t*>(c->m8), c->rp, c->ec, c->ev, x, y, lnw, eps, c->base, c->N, c->K, nch, R, CW, KS, tiles, NS,
                static_cast<int>(xs_off), static_cast<int>(rps_off), static_cast<int>(ecs_off), ecap,
                static_cast<int>(ring_off), 128u, 8u, 65536u,
-               use_sk ? reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + cnt_bytes) : nullptr,
+               use_sk ? reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + sk.flag_bytes) : nullptr,
                use_sk ? static_cast<int*>(ws) : nullptr, sk.maxp};
   auto go = [&](auto kernel) -> int {
     const int r2 = allow_smem(kernel, smem);
@@ -2037,11 +2108,11 @@ static int run_tc(const aib_c12* c, const float* x, float* y, int mode, const ui
     return fail(AIB_ENOTSUP, "aib_gemv_c12: base %d: exceptions need the exact-path kernel", c->base);
   if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(lnw) & 7))
     return fail(AIB_ENOTSUP, "aib_gemv_c12: x / lnw not aligned for vector loads");
-  if (g_variant == 5 && !ws) {
+  if (g_variant == 5) {
     const int rc = run_tc_var<16, 2>(c, x, y, mode, lnw, eps, ws, ws_bytes, s);
     if (rc != AIB_ENOTSUP) return rc;
   }
-  if (g_variant == 3 && !ws) {
+  if (g_variant == 3) {
     const int rc = run_tc_var<8>(c, x, y, mode, lnw, eps, ws, ws_bytes, s);
     if (rc != AIB_ENOTSUP) return rc;
   }
@@ -2140,9 +2211,15 @@ size_t aib_gemv_c12_workspace(const aib_c12* c, int T) {
   if (!c || T != 1 || c->N <= 0 || c->K <= 0 || c->K % 1024) return 0;
   const int nch = c->K / 256;
   size_t need = 0;
-  for (int CW : {nch % 8 == 0 ? 8 : 4, nch % 16 == 0 ? 16 : (nch % 8 == 0 ? 8 : 4)}) {  // both wide kernels
-    const int R = 128 / CW, tiles = (c->N + R - 1) / R;
-    need = std::max(need, gemv::streamk_plan(tiles, nch / CW, R).bytes);
+  const int sms = aib::sm_count();
+  // the wide-stage geometries: tensor-core 48 KB stages (one CTA per SM), tensor-core 24 KB stages (two per
+  // SM), CUDA-core 48 KB stages
+  const int cws[3] = {nch % 8 == 0 ? 8 : 4, 4, nch % 16 == 0 ? 16 : (nch % 8 == 0 ? 8 : 4)};
+  const int rws[3] = {128 / cws[0], 16, 128 / cws[2]};
+  const int grids[3] = {sms, 2 * sms, sms};
+  for (int g = 0; g < 3; ++g) {
+    const int tiles = (c->N + rws[g] - 1) / rws[g];
+    need = std::max(need, gemv::streamk_plan(tiles, nch / cws[g], rws[g], grids[g]).bytes);
   }
   return need;
 }

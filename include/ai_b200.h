@@ -101,10 +101,12 @@ int aib_c12_decode(const aib_c12* c, int first, int last, void* out, int out_dty
  * lnw (bf16 bits [K], may be NULL): RMSNorm prologue of gemvc1_k (wcomp.py:75-86), T == 1 only.
  * x_stride / y_stride: elements between rows of X / Y (ignored for T == 1).
  * ws (optional, T == 1): aib_gemv_c12_workspace(c, 1) bytes, 16-byte aligned and zero-filled once before the
- * first call (it is left zeroed after every call). With it the matrix's (row tile, column group) stages are
- * split evenly over the SMs and a row tile shared by neighbouring CTAs is completed by whichever finishes
- * last, adding the parts in a fixed order (deterministic); without it every CTA takes whole row tiles.
- * Calls that may overlap on the GPU need separate workspaces. */
+ * first call (it is left zeroed after every call). With it, when that shortens the longest CTA's share, the
+ * matrix's (row tile, column group) stages are split evenly over the CTAs and a row tile shared by
+ * neighbouring CTAs is completed by the one holding its last stage, adding the parts in a fixed order
+ * (deterministic); without it every CTA takes whole row tiles. The workspace is touched only after the
+ * previous kernel on the stream has completed, so calls in one stream may share one; calls that may overlap
+ * on the GPU (other streams) need separate workspaces. */
 size_t aib_gemv_c12_workspace(const aib_c12* c, int T);
 /* Kernel choice for T == 1: 0 the tensor-core kernel with 24 KB stages (mma.sync bf16, x split in 3 bf16 parts,
  * K <= 16384), 1 the CUDA-core fp32-FMA kernel with 12 KB stages, 2 the CUDA-core kernel with 48 KB stages,
