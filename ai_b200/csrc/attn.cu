@@ -122,6 +122,7 @@ struct Smem {
   float pw[kWarps][GMAX][kBlk];  // each warp's block probabilities
   float mw[kMaxSplits][GMAX];    // merge weights exp(m_s - M) per split
   float mM[GMAX], mL[GMAX], mc[GMAX], ones[GMAX];
+  long long pos_spec;  // pos as read before the grid dependency resolved (one read for the whole CTA)
   int last;
 };
 
@@ -438,19 +439,23 @@ __global__ void __launch_bounds__(kThreads)
   out += static_cast<size_t>(b) * out_ld;
   uint16_t* kg = kc + static_cast<size_t>(g) * maxt * HD;
   uint16_t* vg = vc + static_cast<size_t>(g) * maxt * HD;
-  // constant inputs before the grid dependency resolves: RoPE frequencies, q / k norm weights, and an L2
-  // hint for this split's K/V rows from a possibly stale pos (any value it reads gives in-bounds rows)
+  // Before the grid dependency resolves: the constant inputs (RoPE frequencies, q / k norm weights) and,
+  // from a speculative read of pos, this split's first K/V rows. The cache rows below pos were written by
+  // the attention of earlier steps, long complete (the kernels in flight at once are the few whose CTAs fit
+  // the SMs together), and no kernel of this step writes them; the rows are re-fetched below if pos turns
+  // out different.
   const float inv_r = threadIdx.x < HD / 2 ? inv[threadIdx.x] : 0.0f;
   for (int d = threadIdx.x; d < HD; d += kThreads) {
     sm.wq[d] = qn[d];
     sm.wk[d] = kn[d];
   }
-  if (threadIdx.x == 0) {
-    const long long ph = *reinterpret_cast<const volatile long long*>(pos_p);
-    const int n = (ph > 0 && ph < maxt) ? static_cast<int>(ph) : 0;
-    const int chunk = (n + S - 1) / S, a = min(n, s * chunk);
-    prefetch_range<HD>(kg, vg, a, min(n, a + chunk));
-  }
+  if (threadIdx.x == 0) sm.pos_spec = *reinterpret_cast<const volatile long long*>(pos_p);
+  __syncthreads();
+  const long long pos_spec = sm.pos_spec;
+  const int n_spec = (pos_spec > 0 && pos_spec < maxt) ? static_cast<int>(pos_spec) : 0;
+  const int chunk_spec = (n_spec + S - 1) / S;
+  const int j0s = min(n_spec, s * chunk_spec), j1s = min(n_spec, j0s + chunk_spec);
+  attend_start<HD>(ring, kg, vg, j0s, j1s);
   pdl_wait();
   // every CTA of this grid is resident by now: the next kernel may launch onto SMs as they free up (it waits
   // for this grid to complete before it reads anything written here)
@@ -469,7 +474,11 @@ __global__ void __launch_bounds__(kThreads)
   const int n = pos_ok ? pos : 0;
   const int chunk = (n + S - 1) / S;
   const int j0 = min(n, s * chunk), j1 = min(n, j0 + chunk);
-  attend_start<HD>(ring, kg, vg, j0, j1);
+  if (j0 != j0s || j1 != j1s) {  // pos moved since the speculative read: drop those rows, fetch the right ones
+    cp_wait<0>();
+    __syncwarp();
+    attend_start<HD>(ring, kg, vg, j0, j1);
+  }
   if (threadIdx.x < HD / 2) {
     const float ang = static_cast<float>(pos) * inv_r;
     sm.cs[threadIdx.x] = cosf(ang);
