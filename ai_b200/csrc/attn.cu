@@ -49,7 +49,7 @@ __host__ __device__ constexpr size_t cmax(size_t a, size_t b) { return a > b ? a
 // Dynamic shared memory: the warps' K/V slots; afterwards reused for the warps' final states
 // [kWarps][GMAX][HD + 2] and by the merge to stage the splits' partials (kMaxSplits x GMAX x (HD + 2) floats).
 template <int HD>
-constexpr size_t ring_bytes() {
+__host__ __device__ constexpr size_t ring_bytes() {
   return cmax(kWarps * slot_bytes<HD>(),
               static_cast<size_t>(kMaxSplits > kWarps ? kMaxSplits : kWarps) * GMAX * (HD + 2) * sizeof(float));
 }
@@ -66,6 +66,17 @@ AIB_DEV void cp_wait() {
 // Hint L2 to fetch [p, p + bytes) (bytes a multiple of 16, p 16-byte aligned).
 AIB_DEV void prefetch_l2(const void* p, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// Distributed shared memory: the generic address of the same shared-memory location in cluster CTA `rank`,
+// and a full cluster barrier (release / acquire: shared-memory writes to peers before it are visible after it).
+AIB_DEV float* cluster_map(float* p, uint32_t rank) {
+  uint64_t r;
+  asm volatile("mapa.u64 %0, %1, %2;" : "=l"(r) : "l"(reinterpret_cast<uint64_t>(p)), "r"(rank));
+  return reinterpret_cast<float*>(r);
+}
+AIB_DEV void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
 // Warp-cooperative copy of `cnt` (<= kBlk) consecutive cache rows into a slot region with row stride STRIDE:
@@ -378,7 +389,8 @@ AIB_DEV void merge_write(Smem<HD>& sm, float* stage, const float* parts, int S, 
                          const float* l0, const float* acc0, float* out) {
   const int nf = S * G * (HD + 2);
   const int n4 = nf / 4;
-  if ((nf & 3) == 0 && (reinterpret_cast<uintptr_t>(parts) & 15) == 0) {
+  if (parts == stage) {  // already in shared memory (cluster merge)
+  } else if ((nf & 3) == 0 && (reinterpret_cast<uintptr_t>(parts) & 15) == 0) {
     // asynchronous 16-byte copies from L2 (every copy in flight at once), then one wait
     for (int i = threadIdx.x; i < n4; i += kThreads) cp16(stage + 4 * i, parts + 4 * i);
     cp_commit();
@@ -426,7 +438,7 @@ __global__ void __launch_bounds__(kThreads)
     rope_attn_kernel(const float* __restrict__ qkv, const uint16_t* __restrict__ qn, const uint16_t* __restrict__ kn,
                      const float* __restrict__ inv, const int64_t* __restrict__ pos_p, uint16_t* kc, uint16_t* vc,
                      float* __restrict__ out, int H, int KV, int maxt, float eps, float scale, float* ws_part,
-                     int* ws_cnt, int qkv_ld, long long kv_bstride, int out_ld) {
+                     int* ws_cnt, int qkv_ld, long long kv_bstride, int out_ld, int clustered) {
   __shared__ Smem<HD> sm;
   extern __shared__ __align__(128) uint8_t ring[];
   const int s = blockIdx.x, S = gridDim.x, g = blockIdx.y, b = blockIdx.z;
@@ -510,6 +522,19 @@ __global__ void __launch_bounds__(kThreads)
     for (int d = lane; d < HD; d += 32) sc += sm.q[h][d] * sm.kcur[d];
     sc = warp_sum(sc);
     if (lane == 0) sm.cur_score[h] = sc * scale;
+  }
+  if (clustered) {
+    // the group's S splits form one cluster: every CTA writes its partial straight into the shared-memory
+    // stage of split 0 (after the ring), one cluster barrier, and split 0 merges them in split order
+    float* stage = reinterpret_cast<float*>(ring + ring_bytes<HD>());
+    attend_range<HD, G>(sm, ring, kg, vg, j0, j1, scale, cluster_map(stage + s * G * (HD + 2), 0));
+    cluster_sync_all();
+    if (s == 0) {
+      if (threadIdx.x < GMAX) sm.ones[threadIdx.x] = 1.0f;  // the current token enters with weight 1
+      __syncthreads();
+      merge_write<HD>(sm, stage, stage, S, G, sm.cur_score, sm.ones, sm.vcur, out + static_cast<size_t>(g) * G * HD);
+    }
+    return;
   }
   float* part = ws_part + (static_cast<size_t>(slot) * S + s) * G * (HD + 2);
   attend_range<HD, G>(sm, ring, kg, vg, j0, j1, scale, part);
@@ -625,6 +650,13 @@ static int splits(int KV, int T, int G, int HD) {
   return std::max(1, std::min(S, fit));
 }
 
+// Cluster sizes tried for the cluster merge (largest first; 16 is the largest B200 schedules). Measured on this
+// pool's B200s: clusters of 16 do not all fit at once (7 of the 8 groups' clusters), and clusters of 8 (64 CTAs)
+// stream K/V slower than the ticket merge's 144 CTAs gain back, so only 16 is tried by default; the debug knob 3
+// sets how many sizes are tried (2: also 8, which the tests use to cover the cluster merge).
+static const int kClusterSizes[2] = {16, 8};
+int g_cluster_sizes = 1;
+
 // Workspace layout: [ticket counters: kMaxSlots ints][partials]. The counters sit at a fixed offset for every
 // T so they are never overwritten by another launch's partials (every launch leaves them at zero).
 constexpr int kMaxSlots = 65536;  // KV * T
@@ -642,14 +674,9 @@ static int check_heads(int H, int KV, int HD) {
   return AIB_OK;
 }
 
-// Launch a kernel template instantiated for the group size G = H / KV (1..GMAX) and head dim HD.
-template <template <int, int> class KSel, typename... Args>
-static int launch_g(int HD, int G, dim3 grid, size_t smem, cudaStream_t s, const char* what, Args... args) {
-  auto go = [&](auto kernel) -> int {
-    const int rc = allow_smem(kernel, smem);
-    if (rc) return rc;
-    return launch(kernel, grid, dim3(kThreads), smem, s, what, args...);
-  };
+// Instantiation for the group size G = H / KV (1..GMAX) and head dim HD.
+template <template <int, int> class KSel, typename Go>
+static int dispatch_g(int HD, int G, const char* what, Go go) {
   switch (HD * 16 + G) {
 #define AIB_ATTN_CASE(hd, g) \
   case hd * 16 + g:          \
@@ -662,6 +689,37 @@ static int launch_g(int HD, int G, dim3 grid, size_t smem, cudaStream_t s, const
     default:
       return fail(AIB_ENOTSUP, "%s: HD=%d G=%d", what, HD, G);
   }
+}
+// Launch a kernel template instantiated for the group size G = H / KV (1..GMAX) and head dim HD.
+template <template <int, int> class KSel, typename... Args>
+static int launch_g(int HD, int G, dim3 grid, size_t smem, cudaStream_t s, const char* what, Args... args) {
+  auto go = [&](auto kernel) -> int {
+    const int rc = allow_smem(kernel, smem);
+    if (rc) return rc;
+    return launch(kernel, grid, dim3(kThreads), smem, s, what, args...);
+  };
+  return dispatch_g<KSel>(HD, G, what, go);
+}
+// Same, for a kernel whose last argument selects the cluster merge: one cluster of cx CTAs (the group's
+// splits) per (group, sequence) -- grid (cx, KV, B) -- for the first cx in `cxs` (descending, <= S) at which
+// the device holds every cluster at once, else the ticket merge over S splits.
+template <template <int, int> class KSel, typename... Args>
+static int launch_g_cluster(int HD, int G, int S, int KV, int B, const int* cxs, int ncx, size_t smem, cudaStream_t s,
+                            const char* what, Args... args) {
+  auto go = [&](auto kernel) -> int {
+    for (int i = 0; i < ncx; ++i) {
+      const int cx = std::min(cxs[i], S);
+      if (cx < 2) break;
+      const size_t smem_cl = smem + static_cast<size_t>(cx) * G * (HD + 2) * sizeof(float);
+      if (allow_smem(kernel, smem_cl) == AIB_OK && clusters_fit(kernel, dim3(kThreads), smem_cl, cx, KV * B))
+        return launch_ex(kernel, dim3(cx, KV, B), dim3(kThreads), smem_cl, s, what, cx, args..., 1);
+      cudaGetLastError();
+    }
+    const int rc = allow_smem(kernel, smem);
+    if (rc) return rc;
+    return launch(kernel, dim3(S, KV, B), dim3(kThreads), smem, s, what, args..., 0);
+  };
+  return dispatch_g<KSel>(HD, G, what, go);
 }
 template <int HD, int G>
 struct RopeAttnSel {
@@ -701,9 +759,10 @@ int aib_rope_attn_decode(const float* qkv, const uint16_t* qn, const uint16_t* k
   int* cnt = static_cast<int*>(ws);
   float* part = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + attn::kCntBytes);
   const size_t smem = HD == 128 ? attn::ring_bytes<128>() : attn::ring_bytes<64>();
-  return attn::launch_g<attn::RopeAttnSel>(HD, H / KV, dim3(S, KV), smem, static_cast<cudaStream_t>(stream),
-                                           "aib_rope_attn_decode", qkv, qn, kn, inv, pos, kc, vc, out, H, KV, maxt,
-                                           eps, scale, part, cnt, (H + 2 * KV) * HD, 0LL, H * HD);
+  return attn::launch_g_cluster<attn::RopeAttnSel>(HD, H / KV, S, KV, 1, attn::kClusterSizes, attn::g_cluster_sizes, smem,
+                                                   static_cast<cudaStream_t>(stream), "aib_rope_attn_decode", qkv, qn,
+                                                   kn, inv, pos, kc, vc, out, H, KV, maxt, eps, scale, part, cnt,
+                                                   (H + 2 * KV) * HD, 0LL, H * HD);
 }
 
 size_t aib_attn_batch_workspace(int H, int KV, int HD, int maxt, int B) {
@@ -731,9 +790,10 @@ int aib_rope_attn_decode_batch(const float* qkv, int qkv_ld, const uint16_t* qn,
   int* cnt = static_cast<int*>(ws);
   float* part = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + attn::kCntBytes);
   const size_t smem = HD == 128 ? attn::ring_bytes<128>() : attn::ring_bytes<64>();
-  return attn::launch_g<attn::RopeAttnSel>(HD, H / KV, dim3(S, KV, B), smem, static_cast<cudaStream_t>(stream),
-                                           "aib_rope_attn_decode_batch", qkv, qn, kn, inv, pos, kc, vc, out, H, KV,
-                                           maxt, eps, scale, part, cnt, qkv_ld, kv_bstride, out_ld);
+  return attn::launch_g_cluster<attn::RopeAttnSel>(HD, H / KV, S, KV, B, attn::kClusterSizes, attn::g_cluster_sizes, smem,
+                                                   static_cast<cudaStream_t>(stream), "aib_rope_attn_decode_batch", qkv,
+                                                   qn, kn, inv, pos, kc, vc, out, H, KV, maxt, eps, scale, part, cnt,
+                                                   qkv_ld, kv_bstride, out_ld);
 }
 
 int aib_qk_rope_cache(const float* qkv, const uint16_t* qn, const uint16_t* kn, const float* inv, const int64_t* pos,

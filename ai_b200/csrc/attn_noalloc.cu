@@ -84,7 +84,7 @@ int aib_rope_attn_decode_noalloc(const float* qkv, const uint16_t* qn, const uin
   const size_t smem = HD == 128 ? attn::ring_bytes<128>() : attn::ring_bytes<64>();
   return attn::launch_g<attn::RopeAttnSel>(HD, H / KV, dim3(S, KV), smem, s, "aib_rope_attn_decode_noalloc", qkv, qn,
                                            kn, inv, pos, kc, vc, out, H, KV, maxt, eps, scale, part, cnt,
-                                           (H + 2 * KV) * HD, 0LL, H * HD);
+                                           (H + 2 * KV) * HD, 0LL, H * HD, 0);
 }
 
 }  // extern "C"

@@ -11,6 +11,9 @@
 #include <utility>
 #include <cuda_runtime.h>
 #include <cuda.h>
+#include <map>
+#include <mutex>
+#include <tuple>
 #include "../../include/ai_b200.h"
 
 #define AIB_DEV __device__ __forceinline__
@@ -227,26 +230,78 @@ int allow_smem(K kernel, size_t bytes) {
   return AIB_OK;
 }
 
-// Launch with the PDL attribute (when enabled) on `stream`.
+// Launch with the PDL attribute (when enabled) on `stream`; cluster_x > 1: thread-block clusters of cluster_x
+// CTAs along x (grid.x a multiple of it).
 template <typename... KArgs, typename... Args>
-int launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, const char* what,
-           Args&&... args) {
+int launch_ex(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, const char* what,
+              int cluster_x, Args&&... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   int na = 0;
   if (pdl_enabled()) {
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    na = 1;
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  if (cluster_x > 1) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = cluster_x;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
   }
   cfg.attrs = attr;
   cfg.numAttrs = na;
   cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
   if (e != cudaSuccess) return fail(AIB_ECUDA, "%s: launch failed: %s", what, cudaGetErrorString(e));
   return AIB_OK;
+}
+template <typename... KArgs, typename... Args>
+int launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, const char* what,
+           Args&&... args) {
+  return launch_ex(kernel, grid, block, smem, stream, what, 1, std::forward<Args>(args)...);
+}
+
+// Whether `need` clusters of cluster_x CTAs of `kernel` (dynamic shared memory `smem`, already allowed) can be
+// resident at once on this device. Cached per (kernel, cluster size, shared memory).
+template <typename... KArgs>
+bool clusters_fit(void (*kernel)(KArgs...), dim3 block, size_t smem, int cluster_x, int need) {
+  static std::mutex mu;
+  static std::map<std::tuple<const void*, int, size_t>, int> cache;
+  const auto key = std::make_tuple(reinterpret_cast<const void*>(kernel), cluster_x, smem);
+  int n = -1;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) n = it->second;
+  }
+  if (n < 0) {
+    n = 0;
+    bool ok = true;
+    if (cluster_x > 8 && cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
+      ok = false;
+    if (ok) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(cluster_x);
+      cfg.blockDim = block;
+      cfg.dynamicSmemBytes = smem;
+      cudaLaunchAttribute a[1];
+      a[0].id = cudaLaunchAttributeClusterDimension;
+      a[0].val.clusterDim.x = cluster_x;
+      a[0].val.clusterDim.y = 1;
+      a[0].val.clusterDim.z = 1;
+      cfg.attrs = a;
+      cfg.numAttrs = 1;
+      if (cudaOccupancyMaxActiveClusters(&n, kernel, &cfg) != cudaSuccess) n = 0;
+    }
+    cudaGetLastError();
+    std::lock_guard<std::mutex> lock(mu);
+    cache[key] = n;
+  }
+  return n >= need;
 }
 }  // namespace aib

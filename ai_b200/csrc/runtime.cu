@@ -7,6 +7,9 @@
 #include "common.cuh"
 
 namespace aib {
+namespace attn {
+extern int g_cluster_sizes;  // attn.cu
+}
 
 static thread_local char t_err[512] = {0};
 static int g_pdl = 1;
@@ -125,6 +128,9 @@ int aib_debug_knob(int knob, int value) {
   } else if (knob == 2) {
     const int v = value ? 1 : 0;
     e = cudaMemcpyToSymbol(aib::g_aib_withhold_copies, &v, sizeof(v));
+  } else if (knob == 3) {
+    if (value < 0 || value > 2) return aib::fail(AIB_EINVAL, "aib_debug_knob(3): value %d not in 0..2", value);
+    aib::attn::g_cluster_sizes = value;
   } else {
     return aib::fail(AIB_EINVAL, "aib_debug_knob: unknown knob %d", knob);
   }

@@ -71,7 +71,10 @@ int aib_status_read(int* out, int clear);
 /* Test knobs of the current device (synchronous; no reference counterpart), so that tests can make a bounded wait
  * run out without any fault: knob 1 = spin limit of every bounded wait (polls; 0 restores the default, ~1e6 times
  * longer than any legitimate wait), knob 2 = 1 makes the wide T = 1 GEMV's producer withhold its copies (its stages
- * never fill, its consumers give up after the spin limit and record AIB_DEV_TIMEOUT_FULL). Not for production. */
+ * never fill, its consumers give up after the spin limit and record AIB_DEV_TIMEOUT_FULL), knob 3 = how many
+ * thread-block cluster sizes (16, then 8 CTAs) the decode attention tries for its cluster merge before the
+ * ticket merge (default 1; 2 lets tests cover the cluster merge on devices that cannot place clusters of 16).
+ * Not for production. */
 int aib_debug_knob(int knob, int value);
 
 /* ---------------------------------------------------------------------------------- 12-bit codec ---- */

@@ -304,9 +304,19 @@ def _attn_case(H, KV, HD, maxt, pos, seed):
     return qkv, qn, kn, kc, vc
 
 
+@pytest.fixture(params=[1, 2], ids=["default", "cluster8"])
+def cluster_sizes(request, lib):
+    """Attention merge: the default choice (cluster of 16 where the device can place one per group, else the
+    ticket merge) and the cluster merge forced down to clusters of 8 CTAs (split partials through distributed
+    shared memory)."""
+    assert lib.aib_debug_knob(3, request.param) == 0
+    yield request.param
+    assert lib.aib_debug_knob(3, 1) == 0
+
+
 @pytest.mark.parametrize("H,KV,HD,pos", [(8, 2, 64, 0), (8, 2, 64, 77), (32, 8, 128, 1), (32, 8, 128, 4100),
                                          (16, 8, 128, 300), (64, 8, 128, 2047)])
-def test_rope_attn_vs_oracle(lib, H, KV, HD, pos):
+def test_rope_attn_vs_oracle(lib, cluster_sizes, H, KV, HD, pos):
     from ai_b200 import tkernels
     maxt = max(128, pos + 1)
     qkv, qn, kn, kc, vc = _attn_case(H, KV, HD, maxt, pos, pos + H)
