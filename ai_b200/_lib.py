@@ -41,7 +41,6 @@ SIGNATURES = {
     "aib_c12_encode_exceptions": (I32, [P, I32, I32, I32, P, P, P, P, P]),
     "aib_c12_decode": (I32, [C.POINTER(C12Desc), I32, I32, P, I32, P]),
     "aib_gemv_c12_workspace": (SZ, [C.POINTER(C12Desc), I32]),
-    "aib_gemv_set_variant": (None, [I32]),
     "aib_head8_tables": (I32, [P, I32, I32, P, P, P, P, P, P]),
     "aib_head8_workspace": (SZ, [I32, I32, I32]),
     "aib_head8_bounds": (I32, [P, I32, I32, P, P, P, P, P, I32, I32, P, I32, P, P, SZ, P]),

@@ -650,12 +650,13 @@ static int splits(int KV, int T, int G, int HD) {
   return std::max(1, std::min(S, fit));
 }
 
-// Cluster sizes tried for the cluster merge (largest first; 16 is the largest B200 schedules). Measured on this
-// pool's B200s: clusters of 16 do not all fit at once (7 of the 8 groups' clusters), and clusters of 8 (64 CTAs)
-// stream K/V slower than the ticket merge's 144 CTAs gain back, so only 16 is tried by default; the debug knob 3
-// sets how many sizes are tried (2: also 8, which the tests use to cover the cluster merge).
+// Cluster sizes tried for the cluster merge (largest first; 16 is the largest B200 schedules). Off by default
+// (g_cluster_sizes = 0: the ticket merge): on this pool's B200s clusters of 16 do not all fit at once (7 of the 8
+// groups' clusters) and clusters of 8 (64 CTAs) stream K/V slower than the ticket merge's 144 CTAs gain back. The
+// debug knob 3 sets how many sizes are tried; the feasibility query it needs is not allowed inside a CUDA graph
+// capture, so a process that turns it on must make its first launch of each shape outside a capture.
 static const int kClusterSizes[2] = {16, 8};
-int g_cluster_sizes = 1;
+int g_cluster_sizes = 0;
 
 // Workspace layout: [ticket counters: kMaxSlots ints][partials]. The counters sit at a fixed offset for every
 // T so they are never overwritten by another launch's partials (every launch leaves them at zero).

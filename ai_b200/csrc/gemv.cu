@@ -145,36 +145,6 @@ AIB_DEV void unit_fast4(const uint4& ml, const uint4& mh, const uint4& ee, const
   }
 }
 
-// Same decode and the same four accumulation chains as unit_fast4, tuned for the integer pipe: the shifts
-// are multiplies by runtime constants (k128 = 128, k8 = 8, k65536 = 65536, passed in by the host so the
-// compiler cannot turn them back into shifts), which issue as IMAD on the FMA pipe instead of competing with
-// the byte permutes and logic ops for the ALU pipe, and the FMAs are packed (fma.rn.f32x2).
-AIB_DEV void unit_fast_imad(const uint4& ml, const uint4& mh, const uint4& ee, const float4* xl, const float4* xh,
-                            uint32_t base7, uint32_t k128, uint32_t k8, uint32_t k65536, float4& a) {
-  const uint32_t E[4] = {ee.x, ee.y, ee.z, ee.w};
-  const uint32_t L[4] = {ml.x, ml.y, ml.z, ml.w};
-  const uint32_t Hh[4] = {mh.x, mh.y, mh.z, mh.w};
-  float2 p0 = make_float2(a.x, a.y), p1 = make_float2(a.z, a.w);
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    const uint32_t x01 = prmt(E[q], 0u, 0x4140u), x23 = prmt(E[q], 0u, 0x4342u);
-    const uint32_t zlo01 = merge_sm_e(prmt(L[q], 0u, 0x9180u), x01 * k128 + base7 - (x01 & 0x00F000F0u) * k128);
-    const uint32_t zlo23 = merge_sm_e(prmt(L[q], 0u, 0xB3A2u), x23 * k128 + base7 - (x23 & 0x00F000F0u) * k128);
-    const uint32_t zhi01 = merge_sm_e(prmt(Hh[q], 0u, 0x9180u), x01 * k8 + base7);
-    const uint32_t zhi23 = merge_sm_e(prmt(Hh[q], 0u, 0xB3A2u), x23 * k8 + base7);
-    p0 = ffma2(make_float2(__uint_as_float(zlo01 * k65536), __uint_as_float(zlo01 & 0xFFFF0000u)),
-               make_float2(xl[q].x, xl[q].y), p0);
-    p1 = ffma2(make_float2(__uint_as_float(zlo23 * k65536), __uint_as_float(zlo23 & 0xFFFF0000u)),
-               make_float2(xl[q].z, xl[q].w), p1);
-    p0 = ffma2(make_float2(__uint_as_float(zhi01 * k65536), __uint_as_float(zhi01 & 0xFFFF0000u)),
-               make_float2(xh[q].x, xh[q].y), p0);
-    p1 = ffma2(make_float2(__uint_as_float(zhi23 * k65536), __uint_as_float(zhi23 & 0xFFFF0000u)),
-               make_float2(xh[q].z, xh[q].w), p1);
-  }
-  a = make_float4(p0.x, p0.y, p1.x, p1.y);
-}
-
-// Element-wise decode with code 15 -> 0 (slow path for units holding exceptions).
 AIB_DEV float dec1(uint32_t m, uint32_t code, uint32_t base) {
   if (code == 15u) return 0.0f;
   return __uint_as_float(((m & 0x80u) << 24) | ((code + base) << 23) | ((m & 0x7Fu) << 16));
@@ -443,307 +413,7 @@ __global__ void __launch_bounds__(kT1Threads, 1)
   }
 }
 
-// ------------------------------------------------------------------------ T = 1 tensor-core kernel
-// Same stream/decode as gemv_t1_kernel, but the packed bf16 pairs produced by the decode are exactly the
-// A-fragment registers of mma.sync.m16n8k16 (bf16 x bf16 -> fp32), so the multiply-accumulate runs on the
-// tensor cores and the fp32 split / FMA instructions disappear. x is stored in shared memory pre-split into
-// three bf16 parts (x = x1 + x2 + x3 exactly; the reference's `_x3`, wcomp.py:130-140) in B-fragment order.
-//
-// Tiles are 16 rows; a stage is 16 rows x 4 chunks (24 KB). The 8 consumer warps form two halves on
-// alternate tiles; warp q of a half takes chunk slot q of each stage and holds rows g and g+8 (g = lane/4)
-// for the lane's 64 columns {32t..32t+31} U {128+32t..128+32t+31} (t = lane%4) of that chunk. MMA i in
-// 0..7 uses the low-half columns 32t+4i..+3, MMA 8+i the high-half ones; the k order inside an MMA is a
-// permutation shared by A and B, so the sum is unchanged. Per tile the 4 warps of a half combine their
-// partial rows in a fixed order.
-constexpr int kMmaStageM8 = 16 * 4 * 256;
-constexpr int kMmaStageE4 = 16 * 4 * 128;
-constexpr int kMmaStage = kMmaStageM8 + kMmaStageE4;  // 24 KB
-constexpr int kMmaHeader = 4096;  // barriers (0..255), abort flag (256), RMS partials (512..), tile partials (1024..3071)
-constexpr int kMmaConsumers = 512;  // 16 warps: 2 halves (alternate tiles) x 4 chunk slots x 2 column halves
-constexpr int kMmaThreads = kMmaConsumers + 32;
-static_assert(kMmaStageM8 == 16 * 4 * 256 && kMmaStageE4 == 16 * 4 * 128, "stage = TMA boxes {256,4,16} + {128,4,16}");
-
-
-// clear the 16-bit halves whose exponent code is 15 (exceptions decode to 0; their value is added apart)
-AIB_DEV uint32_t clear15(uint32_t z, uint32_t codes) {  // codes: low element in bits 0..3, high in 16..19
-  uint32_t m = 0;
-  if ((codes & 0xFu) == 0xFu) m |= 0x0000FFFFu;
-  if (((codes >> 16) & 0xFu) == 0xFu) m |= 0xFFFF0000u;
-  return z & ~m;
-}
-// Byte offset of x's B-fragment piece u (0: split0 b0,b1 + split1 b0,b1; 1: split2 b0,b1) for chunk gc,
-// MMA index i (0..15) and quad lane t. MMA i and i^4 are the two word orders used by even / odd rows, so
-// their records interleave: one 16-byte load of a warp touches 8 distinct 16-byte slots of one 128-byte
-// line -- no bank conflicts.
-AIB_DEV int xrec(int gc, int i, int t, int u) {
-  const int pi = (i & 3) | ((i >> 3) << 2), par = (i >> 2) & 1;
-  return gc * 2048 + pi * 256 + u * 128 + (t * 2 + par) * 16;
-}
-
-// Does the row's CSR slice hold an exception in columns [lo, lo + 32)? (ex_p / ex_col advance monotonically)
-AIB_DEV bool lane_has_exc(const int32_t* ec, int& ex_p, int ex_e, int& ex_col, int lo) {
-  while (ex_col < lo - 256) {  // skip exceptions of earlier chunks (keep this chunk's, any column)
-    ++ex_p;
-    ex_col = ex_p < ex_e ? ec[ex_p] : INT_MAX;
-  }
-  for (int q = ex_p; q < ex_e; ++q) {
-    const int col = (q == ex_p) ? ex_col : ec[q];
-    if (col >= lo + 32) break;
-    if (col >= lo) return true;
-  }
-  return false;
-}
-
-// bf16 pairs of one 4-byte group of a column half (hs = 0: low nibbles / columns c..c+3, 1: high nibbles)
-struct Z2 {
-  uint32_t z01, z23;
-};
-AIB_DEV Z2 decode_half(uint32_t E, uint32_t M, uint32_t base7, int hs, bool exc) {
-  const uint32_t x01 = prmt(E, 0u, 0x4140u), x23 = prmt(E, 0u, 0x4342u);
-  const uint32_t c01 = hs ? (x01 >> 4) & 0x000F000Fu : x01 & 0x000F000Fu;
-  const uint32_t c23 = hs ? (x23 >> 4) & 0x000F000Fu : x23 & 0x000F000Fu;
-  Z2 z;
-  z.z01 = (prmt(M, 0u, 0x9180u) & 0x807F807Fu) | ((c01 << 7) + base7);
-  z.z23 = (prmt(M, 0u, 0xB3A2u) & 0x807F807Fu) | ((c23 << 7) + base7);
-  if (exc) {
-    z.z01 = clear15(z.z01, c01);
-    z.z23 = clear15(z.z23, c23);
-  }
-  return z;
-}
-
-// The CTA's row pointers rp[r0 .. r0+nr] and each row's first exception column, into shared memory.
-// They are weights (never written by an earlier kernel), so this runs before the grid-dependency wait.
-AIB_DEV void load_row_meta(const Params& p, int r0, int nr, int* rps, int* fcs, int nthreads) {
-  for (int i = threadIdx.x; i <= nr; i += nthreads) rps[i] = p.rp[min(r0 + i, p.N)];
-  named_sync(1, nthreads);
-  for (int i = threadIdx.x; i < nr; i += nthreads) fcs[i] = (rps[i] < rps[i + 1]) ? p.ec[rps[i]] : INT_MAX;
-  named_sync(1, nthreads);
-}
-
-template <int MODE, bool RMS>
-__global__ void __launch_bounds__(kMmaThreads, 1)
-    gemv_mma_kernel(const __grid_constant__ CUtensorMap tm8, const __grid_constant__ CUtensorMap tme4, Params p) {
-  extern __shared__ __align__(1024) uint8_t smem[];
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
-  uint64_t* empty = full + 16;  // up to 16 ring slots
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + 256);
-  float* rms_red = reinterpret_cast<float*>(smem + 512);                // [16] RMS partials
-  float* red = reinterpret_cast<float*>(smem + 1024);                   // [2 halves][2 bufs][8 warps][16 rows]
-  uint8_t* xf = smem + kMmaHeader;                                        // x fragments, 2048 B per chunk
-  int* rps = reinterpret_cast<int*>(xf + static_cast<size_t>(p.nch) * 2048);  // row pointers of the CTA's rows
-  int* fcs = rps + p.meta_rows + 1;                                       // first exception column per row
-  uint8_t* ring = smem + p.ring_off;
-
-  const int tid = threadIdx.x;
-  const int tb = static_cast<int>((static_cast<long long>(blockIdx.x) * p.tiles) / gridDim.x);
-  const int te = static_cast<int>((static_cast<long long>(blockIdx.x + 1) * p.tiles) / gridDim.x);
-  const int ntiles = te - tb;
-  if (tid == 0) {
-    for (int s = 0; s < p.NS; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 8);  // the 8 warps of the consuming half
-    }
-    *abort_flag = 0;
-    fence_mbar_init();
-  }
-  __syncthreads();
-  pdl_trigger();
-  if (tid >= kMmaConsumers) {
-    if (tid == kMmaConsumers)
-      produce_pairs(&tm8, &tme4, ring, full, empty, abort_flag, tb, ntiles, p.KS, 16, 4, p.NS, kMmaStage, kMmaStageM8);
-    return;
-  }
-  // row metadata (weights, independent of earlier kernels): load before waiting on them
-  const int r0 = tb * 16, nr = ntiles * 16;
-  load_row_meta(p, r0, nr, rps, fcs, kMmaConsumers);
-  // -------- x prologue: x_eff = [RMS]( MODE 2 ? silu(g)*u : x ), split into 3 bf16 parts, B-fragment order
-  pdl_wait();
-  const int K = p.K;
-  float rs = 1.0f;
-  if (RMS) {
-    float ss = 0.0f;
-    for (int k = tid; k < K; k += kMmaConsumers) {
-      const float v = p.x[k];
-      ss += v * v;
-    }
-    ss = warp_sum(ss);
-    if ((tid & 31) == 0) rms_red[tid >> 5] = ss;
-    named_sync(1, kMmaConsumers);
-    float tot = 0.0f;
-#pragma unroll
-    for (int w = 0; w < kMmaConsumers / 32; ++w) tot += rms_red[w];
-    rs = rsqrtf(tot / static_cast<float>(K) + p.eps);
-  }
-  for (int pr = tid; pr < K / 2; pr += kMmaConsumers) {  // column pair (2pr, 2pr+1)
-    const int k = 2 * pr;
-    float v[2];
-#pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      float x = (MODE == 2) ? silu_mul(p.x[k + e], p.x[K + k + e]) : p.x[k + e];
-      if (RMS) x = bf16_to_f32(p.lnw[k + e]) * (x * rs);
-      v[e] = x;
-    }
-    uint32_t part[3];
-    float r0x = v[0], r1x = v[1];
-#pragma unroll
-    for (int sp = 0; sp < 3; ++sp) {
-      const uint16_t b0 = f32_to_bf16_rne(r0x), b1 = f32_to_bf16_rne(r1x);
-      part[sp] = static_cast<uint32_t>(b0) | (static_cast<uint32_t>(b1) << 16);
-      r0x -= bf16_to_f32(b0);
-      r1x -= bf16_to_f32(b1);
-    }
-    const int gc = k >> 8, kk = k & 255, hf = kk >> 7, kl = kk & 127;
-    const int t = kl >> 5, w = (kl & 31) >> 2, sub = (kl & 3) >> 1;  // sub: b0 (cols +0,+1) or b1 (+2,+3)
-    const int i = hf * 8 + w;
-    uint32_t* u0 = reinterpret_cast<uint32_t*>(xf + xrec(gc, i, t, 0));
-    uint32_t* u1 = reinterpret_cast<uint32_t*>(xf + xrec(gc, i, t, 1));
-    u0[0 + sub] = part[0];  // uint4 0: split0 (b0, b1), split1 (b0, b1)
-    u0[2 + sub] = part[1];
-    u1[0 + sub] = part[2];  // uint4 1: split2 (b0, b1), unused
-  }
-  named_sync(1, kMmaConsumers);
-
-  const int half = tid >> 8, wh = (tid >> 5) & 7, q = wh & 3, hs = wh >> 2;
-  const int lane = tid & 31, g = lane >> 2, t = lane & 3;
-  const uint32_t base7 = (static_cast<uint32_t>(p.base) << 7) | (static_cast<uint32_t>(p.base) << 23);
-  const int my_tiles = half == 0 ? (ntiles + 1) / 2 : ntiles / 2;
-  const bool odd = g & 1;
-  const int o0 = odd ? 16 : 0, o1 = 16 - o0;  // odd rows read their 16-byte halves swapped (bank spread)
-  const int wx = odd ? 4 : 0;                 // ... so their logical word w is physical word w ^ 4
-  const int colbase = hs * 128 + 32 * t;      // the lane's 32 columns inside a chunk
-  bool aborted = false;
-  for (int ti = 0; ti < my_tiles; ++ti) {
-    const int tile = tb + 2 * ti + half;
-    const int lrA = (2 * ti + half) * 16 + g, lrB = lrA + 8;  // rows relative to the CTA's first row
-    const int rowA = r0 + lrA, rowB = r0 + lrB;
-    int exA_p = rps[lrA], exA_e = rps[lrA + 1], exA_col = fcs[lrA];
-    int exB_p = rps[lrB], exB_e = rps[lrB + 1], exB_col = fcs[lrB];
-    float acc[2][3][4];
-#pragma unroll
-    for (int a = 0; a < 2; ++a)
-#pragma unroll
-      for (int b = 0; b < 3; ++b)
-#pragma unroll
-        for (int c = 0; c < 4; ++c) acc[a][b][c] = 0.0f;
-    float exA = 0.0f, exB = 0.0f;
-    for (int ks = 0; ks < p.KS; ++ks) {
-      const int it = 2 * (ti * p.KS + ks) + half;
-      const int s = it % p.NS;
-      // warp-uniform: the MMAs below must run with all 32 lanes converged
-      const bool ok = __all_sync(0xffffffffu, !aborted && wait_full(&full[s], (it / p.NS) & 1, abort_flag));
-      if (!ok) aborted = true;
-      const int gc = ks * 4 + q;
-      if (ok && gc < p.nch) {
-        const uint8_t* st = ring + static_cast<size_t>(s) * kMmaStage;
-        const uint8_t* mA = st + (g * 4 + q) * 256 + colbase;
-        const uint8_t* mB = st + ((g + 8) * 4 + q) * 256 + colbase;
-        const uint8_t* eA = st + kMmaStageM8 + (g * 4 + q) * 128 + 32 * t;
-        const uint8_t* eB = st + kMmaStageM8 + ((g + 8) * 4 + q) * 128 + 32 * t;
-        uint4 MA[2], EA[2], MB[2], EB[2];
-        MA[0] = *reinterpret_cast<const uint4*>(mA + o0);
-        MA[1] = *reinterpret_cast<const uint4*>(mA + o1);
-        EA[0] = *reinterpret_cast<const uint4*>(eA + o0);
-        EA[1] = *reinterpret_cast<const uint4*>(eA + o1);
-        MB[0] = *reinterpret_cast<const uint4*>(mB + o0);
-        MB[1] = *reinterpret_cast<const uint4*>(mB + o1);
-        EB[0] = *reinterpret_cast<const uint4*>(eB + o0);
-        EB[1] = *reinterpret_cast<const uint4*>(eB + o1);
-        const int c0 = gc * 256;
-        const bool xa = (rowA < p.N) && lane_has_exc(p.ec, exA_p, exA_e, exA_col, c0 + colbase);
-        const bool xb = (rowB < p.N) && lane_has_exc(p.ec, exB_p, exB_e, exB_col, c0 + colbase);
-        __syncwarp();  // reconverge after the per-lane CSR walks: the MMAs below are warp-collective
-        const uint32_t* ma = reinterpret_cast<const uint32_t*>(MA);
-        const uint32_t* ea = reinterpret_cast<const uint32_t*>(EA);
-        const uint32_t* mb = reinterpret_cast<const uint32_t*>(MB);
-        const uint32_t* eb = reinterpret_cast<const uint32_t*>(EB);
-#pragma unroll
-        for (int w = 0; w < 8; ++w) {
-          const Z2 za = decode_half(ea[w], ma[w], base7, hs, xa);
-          const Z2 zb = decode_half(eb[w], mb[w], base7, hs, xb);
-          const int i = hs * 8 + (w ^ wx);
-          const uint4 b0 = *reinterpret_cast<const uint4*>(xf + xrec(gc, i, t, 0));
-          const uint2 b1 = *reinterpret_cast<const uint2*>(xf + xrec(gc, i, t, 1));
-          float(*ac)[4] = acc[w & 1];
-          mma_bf16(ac[0], za.z01, zb.z01, za.z23, zb.z23, b0.x, b0.y);
-          mma_bf16(ac[1], za.z01, zb.z01, za.z23, zb.z23, b0.z, b0.w);
-          mma_bf16(ac[2], za.z01, zb.z01, za.z23, zb.z23, b1.x, b1.y);
-        }
-        if (xa || xb) {  // exception values times x, for this lane's columns
-          auto xval = [&](int col) {
-            const int kk = col & 255, hf = kk >> 7, kl = kk & 127;
-            const int i = hf * 8 + ((kl & 31) >> 2), sub = (kl & 3) >> 1, sh = (kl & 1) * 16;
-            const uint32_t* u0 = reinterpret_cast<const uint32_t*>(xf + xrec(col >> 8, i, kl >> 5, 0));
-            const uint32_t* u1 = reinterpret_cast<const uint32_t*>(xf + xrec(col >> 8, i, kl >> 5, 1));
-            const float f1 = bf16_to_f32(static_cast<uint16_t>(u0[0 + sub] >> sh));
-            const float f2 = bf16_to_f32(static_cast<uint16_t>(u0[2 + sub] >> sh));
-            const float f3 = bf16_to_f32(static_cast<uint16_t>(u1[0 + sub] >> sh));
-            return (f1 + f2) + f3;
-          };
-          const int lo = c0 + colbase, hi = lo + 32;
-          if (xa)
-            for (int e = exA_p; e < exA_e; ++e) {
-              const int col = p.ec[e];
-              if (col >= c0 + 256) break;
-              if (col >= lo && col < hi) exA += p.ev[e] * xval(col);
-            }
-          if (xb)
-            for (int e = exB_p; e < exB_e; ++e) {
-              const int col = p.ec[e];
-              if (col >= c0 + 256) break;
-              if (col >= lo && col < hi) exB += p.ev[e] * xval(col);
-            }
-        }
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[s]);
-    }
-    // rows g and g+8: lane (g, t) holds output columns n = 2t (c0, c2) and 2t+1 (c1, c3); column n carries
-    // x in the word order of the lanes with g = n, so an even row is read from an even column, an odd row
-    // from an odd one (all B columns hold the same x).
-    float vA = 0.0f, vB = 0.0f;
-#pragma unroll
-    for (int a = 0; a < 2; ++a)
-#pragma unroll
-      for (int b = 0; b < 3; ++b) {
-        vA += odd ? acc[a][b][1] : acc[a][b][0];
-        vB += odd ? acc[a][b][3] : acc[a][b][2];
-      }
-    exA += __shfl_xor_sync(0xffffffffu, exA, 1);
-    exA += __shfl_xor_sync(0xffffffffu, exA, 2);
-    exB += __shfl_xor_sync(0xffffffffu, exB, 1);
-    exB += __shfl_xor_sync(0xffffffffu, exB, 2);
-    vA += exA;
-    vB += exB;
-    float* rb = red + (half * 2 + (ti & 1)) * 128;
-    if (t == 0) rb[wh * 16 + g] = vA, rb[wh * 16 + g + 8] = vB;
-    named_sync(2 + half, 256);
-    if (wh == 0 && lane < 16 && !aborted) {
-      const int row = tile * 16 + lane;
-      if (row < p.N) {
-        float v = rb[lane];
-#pragma unroll
-        for (int w8 = 1; w8 < 8; ++w8) v += rb[w8 * 16 + lane];
-        if (MODE == 0)
-          p.y[row] = v;
-        else
-          p.y[row] += v;
-      }
-    }
-  }
-}
-
-constexpr int kRowsStage = 128 * 384;  // wide-stage kernels: R * CW * (256 + 128) bytes, R * CW = 128
-
-// ---------------------------------------------------------- producer warp of the wide-stage kernels
-// Streams the CTA's (tile, chunk group) stages through the NS-slot ring. A slot's full barrier completes on
-// two arrivals plus the copied bytes: the first arrival comes with the TMA copies, issued as soon as the slot
-// is free; the second once the slot's bookkeeping is done, which therefore overlaps the copy: when the stage
-// that last used the slot ended a row segment (a whole row tile, or this CTA's share of one), the producer
-// adds the segment's per-warp partials of each of the R rows in a fixed order, adds the exception correction
-// sum_e (v_e - G_e) * x[c_e] over the segment's exceptions (the consumers decode every element, exceptions
-// included, as a finite stand-in G_e -- see exc_garbage) and writes y (stream-K: the tile's parts through
-// the workspace). Meta layout per slot (slot_meta bytes): 128 bytes unused, then float partials[R * pw].
+// ------------------------------------------- the tensor-core wide-stage kernel's exception table
 struct ExcTab {  // the CTA's exceptions: CSR slice in shared memory (columns + corrections) or in global memory
   const int* rps;   // row pointers of the CTA's rows (shared)
   const int* ecs;   // staged columns (shared), valid when staged
@@ -755,142 +425,6 @@ struct ExcTab {  // the CTA's exceptions: CSR slice in shared memory (columns + 
   const uint8_t* m8;
   int K, base;
 };
-// Finishes one row segment of a wide-stage kernel (tile ftile, chunk groups seg_lo..fks, where seg_lo is ks0
-// for the CTA's first tile and 0 otherwise). Lane r < R holds v = the segment's partial sum of row r of the
-// tile; the lanes add the exception corrections sum_e (v_e - G_e) * x[c_e] over the segment's exceptions (the
-// consumers decode every element, exceptions included, as a finite stand-in G_e -- see exc_garbage) in column
-// order and write y; a segment that is only part of its tile goes through the stream-K workspace. Warp-wide.
-template <int MODE, typename XF>
-AIB_DEV void finish_segment(float v, int ftile, int fks, const ExcTab& et, XF xval, float* y, int N, int tb, int ks0,
-                            int R, int CW, int KS, int nrows, float* wsp, int* wsc, int maxp, int tiles) {
-  const int lane = threadIdx.x & 31;
-  const int seg_lo = ftile == tb ? ks0 : 0;
-  const bool whole = seg_lo == 0 && fks == KS - 1;
-  const int lr = (ftile - tb) * R + lane, row = ftile * R + lane;
-  if (lane < R && lr < nrows) {  // exception corrections of the segment's columns, in column order
-    const int lo = seg_lo * CW * 256, hi = (fks + 1) * CW * 256;
-    const int qa = et.rps[lr] - et.e0, qb = et.rps[lr + 1] - et.e0;
-    float corr = 0.0f;
-    for (int q = qa; q < qb; ++q) {
-      const int col = et.staged ? et.ecs[q] : et.ec[et.e0 + q];
-      if (col >= hi) break;
-      if (col < lo) continue;
-      const float d = et.staged ? et.evs[q]
-                                : et.ev[et.e0 + q] - exc_garbage(et.m8[static_cast<size_t>(row) * et.K + col], et.base);
-      corr = fmaf(d, xval(col), corr);
-    }
-    v += corr;
-  }
-  if (whole) {
-    if (MODE == 3) {  // rows (2i, 2i+1) = (gate_i, up_i): y[i] = silu(gate_i) * up_i
-      const float vu = __shfl_down_sync(0xffffffffu, v, 1);
-      if (lane < R && !(lane & 1) && row + 1 < N) y[row >> 1] = silu_mul(v, vu);
-    } else if (lane < R && row < N) {
-      if (MODE == 0)
-        y[row] = v;
-      else
-        y[row] += v;
-    }
-    return;
-  }
-  // stream-K: this CTA holds part `pi` of the tile's stages; the last of its np parts to arrive adds them in
-  // part order (deterministic) and writes y, then clears the ticket
-  const long long nall = static_cast<long long>(tiles) * KS, G = gridDim.x;
-  const long long st0 = static_cast<long long>(ftile) * KS;
-  const int bf = static_cast<int>(((st0 + 1) * G + nall - 1) / nall - 1);
-  const int bl = static_cast<int>(((st0 + KS) * G + nall - 1) / nall - 1);
-  const int pi = static_cast<int>(blockIdx.x) - bf, np = bl - bf + 1;
-  float* slot = wsp + (static_cast<size_t>(ftile) * maxp) * R;
-  if (lane < R) slot[pi * R + lane] = v;
-  __threadfence();
-  __syncwarp();
-  int last = 0;
-  if (lane == 0) last = atomicAdd(&wsc[ftile], 1) == np - 1;
-  last = __shfl_sync(0xffffffffu, last, 0);
-  if (last) {
-    __threadfence();
-    float t = 0.0f;
-    if (lane < R) {
-      t = __ldcg(slot + lane);
-      for (int q = 1; q < np; ++q) t += __ldcg(slot + q * R + lane);
-    }
-    if (MODE == 3) {
-      const float tu = __shfl_down_sync(0xffffffffu, t, 1);
-      if (lane < R && !(lane & 1) && row + 1 < N) y[row >> 1] = silu_mul(t, tu);
-    } else if (lane < R && row < N) {
-      if (MODE == 0)
-        y[row] = t;
-      else
-        y[row] += t;
-    }
-    if (lane == 0) wsc[ftile] = 0;
-  }
-}
-
-template <int MODE, typename XF>
-AIB_DEV void produce_wide(const CUtensorMap* tm8, const CUtensorMap* tme4, uint8_t* ring, uint8_t* meta,
-                          int slot_meta, uint64_t* full, uint64_t* empty, volatile int* abort_flag, const ExcTab& et,
-                          XF xval, float* y, int N, int tb, int ks0, int n_st, int R, int CW, int KS, int NS,
-                          int nrows, int pw, float* wsp, int* wsc, int maxp, int tiles,
-                          uint32_t stage_bytes = kRowsStage, int first = 0) {
-  const int lane = threadIdx.x & 31;
-  if (lane == 0) {
-    prefetch_tensormap(tm8);
-    prefetch_tensormap(tme4);
-  }
-  const uint32_t m8_bytes = static_cast<uint32_t>(R * CW * 256);
-  int s = 0, round = 0, ks = ks0, tile = tb;  // stage i: slot s, ring round i / NS
-  int fks = ks0, ftile = tb;                  // stage i - NS (same slot)
-  for (int i = 0; i < n_st + NS; ++i) {
-    if (i >= NS) {  // the slot's previous stage must be consumed
-      bool ok = true;
-      if (lane == 0) {
-        ok = false;
-        for (uint32_t k = 0, lim = spin_limit(); k < lim && !ok; ++k) {
-          ok = mbar_try_wait(&empty[s], (round - 1) & 1);
-          if (!ok && (k & 63) == 63 && *abort_flag) break;
-        }
-        if (!ok) {
-          if (!*abort_flag) set_status(AIB_DEV_TIMEOUT_EMPTY);
-          *abort_flag = 1;
-        }
-      }
-      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-      if (!ok) {  // never leave with copies in flight (both arrivals of every issued stage were made)
-        if (lane == 0)
-          for (int k = i - NS; k < min(i, n_st); ++k) mbar_wait(&full[k % NS], (k / NS) & 1, AIB_DEV_TIMEOUT_FULL);
-        return;
-      }
-    }
-    uint8_t* sm = meta + s * slot_meta;
-    if (i >= first && i < n_st && lane == 0 && !g_aib_withhold_copies) {  // issue first: the copy is the long pole
-      uint8_t* st = ring + static_cast<size_t>(s) * stage_bytes;
-      mbar_arrive_expect_tx(&full[s], stage_bytes);
-      tma_load_3d(st, tm8, &full[s], 0, ks * CW, tile * R);
-      tma_load_3d(st + m8_bytes, tme4, &full[s], 0, ks * CW, tile * R);
-    }
-    if (i >= NS) {
-      const bool seg_end = fks == KS - 1 || i - NS == n_st - 1;  // consumers left partials in the slot
-      if (seg_end && !*abort_flag) {
-        float v = 0.0f;
-        if (lane < R) {
-          const float* part = reinterpret_cast<const float*>(sm + 128) + lane * pw;
-          v = part[0];
-          for (int w = 1; w < pw; ++w) v += part[w];
-        }
-        finish_segment<MODE>(v, ftile, fks, et, xval, y, N, tb, ks0, R, CW, KS, nrows, wsp, wsc, maxp, tiles);
-      }
-      if (++fks == KS) fks = 0, ++ftile;
-    }
-    __syncwarp();
-    if (i < n_st) {
-      if (lane == 0 && i >= first) mbar_arrive(&full[s]);  // second arrival: the slot's previous partials are read
-      if (++ks == KS) ks = 0, ++tile;
-    }
-    if (++s == NS) s = 0, ++round;
-  }
-}
-
 // ------------------------------------------- producer and finisher warps of the tensor-core wide-stage kernel
 // The producer only streams: one thread issues stage i (two 3-D TMA copies, m8 and e4, no multicast) as soon as
 // its slot's previous stage has been consumed; a slot's full barrier completes on that one arrival plus the
@@ -1177,41 +711,9 @@ AIB_DEV void finish_segments(const float* pbuf, int pstride, uint64_t* ready, ui
   }
 }
 
-// Stage the CTA's exceptions (weights only: before the grid-dependency wait): columns and the corrections
-// v - G they need (G: what the decode makes of the element, from its m8 byte). Threads take rows.
-AIB_DEV void stage_exceptions(int* ecs, float* evs, const int* rps, int nrows, int row0, int e0, const int32_t* ec,
-                              const float* ev, const uint8_t* m8, int K, int base, int nthreads) {
-  for (int lr = threadIdx.x; lr < nrows; lr += nthreads) {
-    const int qa = rps[lr] - e0, qb = rps[lr + 1] - e0;
-    const uint8_t* mrow = m8 + static_cast<size_t>(row0 + lr) * K;
-    for (int q = qa; q < qb; ++q) {
-      const int col = ec[e0 + q];
-      ecs[q] = col;
-      evs[q] = ev[e0 + q] - exc_garbage(mrow[col], base);
-    }
-  }
-}
-
 // --------------------------------------------------------------------- T = 1 wide-stage kernel
-// A TMA copy costs an SM a roughly fixed time whatever its size (measured on B200: 4 KB copies stream at
-// ~1.8 TB/s chip-wide, 16 KB copies at ~6.7 TB/s), so this kernel moves 48 KB per stage in two copies: R rows
-// x CW chunks of m8 (R*CW*256 bytes) and of e4 (half that), with R*CW = 128. Every consumer thread owns one
-// 32-element unit (chunk slot, 16-column group) of two rows of the stage -- rows `pair` and `pair + R/2` of
-// the tile -- so each x vector read from shared memory feeds two rows. The L = 8*CW threads of a row pair
-// cover the stage's row segment.
-//
-// The producer warp does the per-stage bookkeeping so the consumers' loop stays short:
-//  * before issuing a stage it marks, in a per-slot bitmask (one bit per row and unit), the units that hold
-//    an exception (from the CSR: row pointers and, when they fit, the CTA's exception columns, staged in
-//    shared memory before the grid-dependency wait) -- consumers test one bit instead of walking the CSR;
-//  * consumers reduce a finished tile inside each warp and leave one partial per (row, warp) in the slot;
-//    once the slot's empty barrier completes, the producer adds the W = L/32 partials of each row in a fixed
-//    order and writes y. No CTA-wide barrier runs in the main loop.
-constexpr int kRowsConsumers = 512;
-constexpr int kRowsThreads = kRowsConsumers + 32;
-constexpr int kRowsSlotMeta = 256;     // per slot: 32-word exception bitmask + 32 row/warp partials
-constexpr int kRowsHeader = 1024 + 8 * kRowsSlotMeta;  // barriers [0,256), abort 256, RMS partials [512,1024)
-
+// Shared parameters of the wide-stage launches: the matrix, x / y, the stage geometry (R rows x CW chunks per
+// stage, KS stages per row tile, NS ring slots), the shared-memory offsets and the stream-K workspace.
 struct RowsParams {
   const uint8_t* m8;  // the code planes (exception stand-ins are read from m8 when not staged)
   const int32_t* rp;
@@ -1224,7 +726,7 @@ struct RowsParams {
   int base, N, K, nch;
   int R, CW, KS, tiles, NS;
   int xs_off, rps_off, ecs_off, ecap, ring_off;
-  uint32_t k128, k8, k65536;  // 128, 8, 65536 (see unit_fast_imad)
+  uint32_t k128, k8, k65536;  // 128, 8, 65536: decode multipliers passed as values, so they stay on the FMA pipe
   float* wsp;                 // stream-K partials [tiles][maxp][R] (null: whole row tiles per CTA)
   int* wsc;                   // stream-K tickets [tiles], zero between launches
   int maxp;                   // partial slots per tile
@@ -1258,164 +760,6 @@ AIB_DEV WideShare wide_share(const RowsParams& p) {
     w.nrows = min((te - tb) * p.R, p.N - w.row0);
   }
   return w;
-}
-
-template <int MODE, bool RMS>
-__global__ void __launch_bounds__(kRowsThreads, 1)
-    gemv_rows_kernel(const __grid_constant__ CUtensorMap tm8, const __grid_constant__ CUtensorMap tme4, RowsParams p) {
-  extern __shared__ __align__(1024) uint8_t smem[];
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
-  uint64_t* empty = full + 16;
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + 256);
-  float* rms_red = reinterpret_cast<float*>(smem + 512);
-  uint8_t* meta = smem + 1024;  // slot s: uint32 mask[32] at s*256, float part[32] at s*256 + 128
-  float* xs = reinterpret_cast<float*>(smem + p.xs_off);
-  int* rps = reinterpret_cast<int*>(smem + p.rps_off);
-  int* ecs = reinterpret_cast<int*>(smem + p.ecs_off);
-  uint8_t* ring = smem + p.ring_off;
-
-  const int tid = threadIdx.x, lane = tid & 31;
-  const WideShare sh_ = wide_share(p);
-  const int tb = sh_.tb, ks0 = sh_.ks0;
-  const int R = p.R, CW = p.CW, KS = p.KS, NS = p.NS;
-  const int L = 8 * CW, W = L / 32;  // threads / warps per row pair (L = units per row per stage)
-  const int n_st = sh_.n_st;
-  const int row0 = sh_.row0;
-  const int nrows = sh_.nrows;
-  if (tid == 0) {
-    for (int s = 0; s < NS; ++s) {
-      mbar_init(&full[s], 2);  // TMA arrival + bookkeeping arrival
-      mbar_init(&empty[s], kRowsConsumers / 32);
-    }
-    *abort_flag = 0;
-    fence_mbar_init();
-  }
-  // row metadata (weights only, so before the grid-dependency wait), for producer and consumers
-  for (int i = tid; i <= nrows; i += kRowsThreads) rps[i] = p.rp[row0 + i];
-  __syncthreads();
-  const int e0 = rps[0], n_exc = rps[nrows] - e0;
-  const bool staged = n_exc <= p.ecap;
-  float* evs = reinterpret_cast<float*>(ecs + p.ecap);
-  if (staged) stage_exceptions(ecs, evs, rps, nrows, row0, e0, p.ec, p.ev, p.m8, p.K, p.base, kRowsThreads);
-  __syncthreads();
-  const ExcTab et{rps, ecs, evs, staged, e0, row0, p.ec, p.ev, p.m8, p.K, p.base};
-  pdl_trigger();
-
-  if (tid >= kRowsConsumers) {  // ---------------- producer warp
-    auto xval = [&](int col) { return xs[xperm(col)]; };
-    produce_wide<MODE>(&tm8, &tme4, ring, meta, kRowsSlotMeta, full, empty, abort_flag, et, xval, p.y, p.N, tb, ks0,
-                       n_st, R, CW, KS, NS, nrows, W, p.wsp, p.wsc, p.maxp, p.tiles);
-    return;
-  }
-
-  // ---------------- consumers: x prologue (after the grid-dependency wait: x is the previous kernel's output)
-  pdl_wait();
-  const int K = p.K, K4 = K / 4;
-  const float4* __restrict__ xg = reinterpret_cast<const float4*>(p.x);
-  float rs = 1.0f;
-  if (RMS) {
-    float ss = 0.0f;
-    for (int k = tid; k < K4; k += kRowsConsumers) {
-      const float4 v = xg[k];
-      ss += (v.x * v.x + v.y * v.y) + (v.z * v.z + v.w * v.w);
-    }
-    ss = warp_sum(ss);
-    if (lane == 0) rms_red[tid >> 5] = ss;
-    named_sync(1, kRowsConsumers);
-    float tot = 0.0f;
-#pragma unroll
-    for (int w = 0; w < kRowsConsumers / 32; ++w) tot += rms_red[w];
-    rs = rsqrtf(tot / static_cast<float>(K) + p.eps);
-  }
-  for (int k0 = 0; k0 < K4; k0 += 4 * kRowsConsumers) {  // batches of 4 float4 per thread, loads first
-    float4 v[4], u[4];
-    uint2 wl[4];
-#pragma unroll
-    for (int b = 0; b < 4; ++b) {
-      const int k = k0 + b * kRowsConsumers + tid;
-      if (k < K4) {
-        v[b] = xg[k];
-        if (MODE == 2) u[b] = xg[K4 + k];
-        if (RMS) wl[b] = reinterpret_cast<const uint2*>(p.lnw)[k];
-      }
-    }
-#pragma unroll
-    for (int b = 0; b < 4; ++b) {
-      const int k = k0 + b * kRowsConsumers + tid;
-      if (k < K4) {
-        float4 o = v[b];
-        if (MODE == 2)
-          o = make_float4(silu_mul(o.x, u[b].x), silu_mul(o.y, u[b].y), silu_mul(o.z, u[b].z), silu_mul(o.w, u[b].w));
-        if (RMS)
-          o = make_float4(bf16_to_f32(static_cast<uint16_t>(wl[b].x)) * (o.x * rs),
-                          bf16_to_f32(static_cast<uint16_t>(wl[b].x >> 16)) * (o.y * rs),
-                          bf16_to_f32(static_cast<uint16_t>(wl[b].y)) * (o.z * rs),
-                          bf16_to_f32(static_cast<uint16_t>(wl[b].y >> 16)) * (o.w * rs));
-        *reinterpret_cast<float4*>(xs + xperm(4 * k)) = o;
-      }
-    }
-  }
-  named_sync(1, kRowsConsumers);
-
-  const int pair = tid / L, l = tid % L;  // rows pair and pair + R/2 of each tile
-  const int cc = l >> 3, j = l & 7;       // chunk slot and 16-column group of this thread's unit
-  const int wp = l >> 5;                  // warp index inside the pair
-  const uint32_t base7 = (static_cast<uint32_t>(p.base) << 7) | (static_cast<uint32_t>(p.base) << 23);
-  const int ra = pair, rb = pair + R / 2;
-  const uint32_t m8a = static_cast<uint32_t>((ra * CW + cc) * 256 + 16 * j);
-  const uint32_t m8b = static_cast<uint32_t>((rb * CW + cc) * 256 + 16 * j);
-  const uint32_t e4a = static_cast<uint32_t>(R * CW * 256 + (ra * CW + cc) * 128 + 16 * j);
-  const uint32_t e4b = static_cast<uint32_t>(R * CW * 256 + (rb * CW + cc) * 128 + 16 * j);
-  const float4* xs4 = reinterpret_cast<const float4*>(xs);
-
-  bool aborted = false;
-  float4 accA = make_float4(0.0f, 0.0f, 0.0f, 0.0f), accB = accA;
-  int s = 0, ph = 0, ks = ks0, tile = tb;
-  for (int i = 0; i < n_st; ++i) {
-    const bool ok = !aborted && wait_full(&full[s], ph, abort_flag);
-    if (!ok) aborted = true;
-    const int gc = ks * CW + cc;
-    const uint8_t* sm = meta + s * kRowsSlotMeta;
-    if (ok && gc < p.nch) {
-      const uint8_t* st = ring + static_cast<size_t>(s) * kRowsStage;
-      const float4* xb4 = xs4 + gc * 64;
-      float4 xl[4], xh[4];
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        xl[q] = xb4[q * 8 + j];
-        xh[q] = xb4[32 + q * 8 + j];
-      }
-      const uint4 mlA = *reinterpret_cast<const uint4*>(st + m8a);
-      const uint4 mhA = *reinterpret_cast<const uint4*>(st + m8a + 128);
-      const uint4 eeA = *reinterpret_cast<const uint4*>(st + e4a);
-      const uint4 mlB = *reinterpret_cast<const uint4*>(st + m8b);
-      const uint4 mhB = *reinterpret_cast<const uint4*>(st + m8b + 128);
-      const uint4 eeB = *reinterpret_cast<const uint4*>(st + e4b);
-      // exceptions decode to their stand-ins; the producer adds the corrections
-      unit_fast_imad(mlA, mhA, eeA, xl, xh, base7, p.k128, p.k8, p.k65536, accA);
-      unit_fast_imad(mlB, mhB, eeB, xl, xh, base7, p.k128, p.k8, p.k65536, accB);
-    }
-    if (ks == KS - 1 || i == n_st - 1) {  // segment end: reduce inside the warp, one partial per (row, warp)
-      float vA = (accA.x + accA.y) + (accA.z + accA.w);
-      float vB = (accB.x + accB.y) + (accB.z + accB.w);
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        vA += __shfl_xor_sync(0xffffffffu, vA, o);
-        vB += __shfl_xor_sync(0xffffffffu, vB, o);
-      }
-      if (lane == 0) {
-        float* part = reinterpret_cast<float*>(const_cast<uint8_t*>(sm) + 128);
-        part[ra * W + wp] = vA;
-        part[rb * W + wp] = vB;
-      }
-      accA = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-      accB = accA;
-    }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[s]);
-    if (++ks == KS) ks = 0, ++tile;
-    if (++s == NS) s = 0, ph ^= 1;
-  }
 }
 
 // ----------------------------------------------------------- T = 1 wide-stage tensor-core kernel
@@ -1916,39 +1260,6 @@ static int make_maps(const aib_c12* c, int RT, int CW, CUtensorMap* tm8, CUtenso
 constexpr size_t kSmemTarget = 112 * 1024;  // leaves room for a neighbouring kernel's CTA (PDL overlap)
 constexpr size_t kSmemMax = 227 * 1024;
 
-static int run_mma(const aib_c12* c, const float* x, float* y, int mode, const uint16_t* lnw, float eps,
-                   cudaStream_t s) {
-  const int nch = c->K / 256;
-  const int tiles = (c->N + 15) / 16;
-  const int grid = std::min(tiles, sm_count());
-  const int meta_rows = ((tiles + grid - 1) / grid) * 16;
-  CUtensorMap tm8, tme4;
-  int rc = make_maps(c, 16, 4, &tm8, &tme4);
-  if (rc) return rc;
-  const size_t xf_bytes = static_cast<size_t>(nch) * 2048;
-  const size_t meta_bytes = (static_cast<size_t>(meta_rows) * 2 + 1) * 4;
-  const size_t ring_off = ((kMmaHeader + xf_bytes + meta_bytes + 1023) / 1024) * 1024;
-  int NS = static_cast<int>((kSmemMax - ring_off) / kMmaStage);
-  NS = std::min(NS, 8) & ~1;
-  if (NS < 2) return fail(AIB_ENOTSUP, "aib_gemv_c12: K=%d / N=%d too large for the tensor-core kernel", c->K, c->N);
-  const size_t smem = ring_off + static_cast<size_t>(NS) * kMmaStage;
-  Params p{c->rp, c->ec, c->ev, x, y, lnw, eps, c->base, c->N, c->K, nch, 16, 4, (nch + 3) / 4, tiles, NS, 1, 0, 0,
-           c->K, meta_rows, static_cast<int>(ring_off)};
-  auto go = [&](auto kernel) -> int {
-    const int r2 = allow_smem(kernel, smem);
-    if (r2) return r2;
-    return launch(kernel, dim3(grid), dim3(kMmaThreads), smem, s, "aib_gemv_c12(T=1, mma)", tm8, tme4, p);
-  };
-  if (lnw) {
-    if (mode == 0) return go(gemv_mma_kernel<0, true>);
-    if (mode == 1) return go(gemv_mma_kernel<1, true>);
-    return go(gemv_mma_kernel<2, true>);
-  }
-  if (mode == 0) return go(gemv_mma_kernel<0, false>);
-  if (mode == 1) return go(gemv_mma_kernel<1, false>);
-  return go(gemv_mma_kernel<2, false>);
-}
-
 // Stream-K split of `tiles * KS` stages over `grid` CTAs: the most CTAs that share one tile.
 static int streamk_max_parts(int tiles, int KS, int grid) {
   const long long n = static_cast<long long>(tiles) * KS, G = grid;
@@ -1977,64 +1288,11 @@ static StreamK streamk_plan(int tiles, int KS, int R, int max_grid) {
   return k;
 }
 
-// Wide-stage kernel (48 KB TMA stages); ENOTSUP when K is not a multiple of 1024 or x does not fit.
-static int run_rows(const aib_c12* c, const float* x, float* y, int mode, const uint16_t* lnw, float eps, void* ws,
-                    size_t ws_bytes, cudaStream_t s) {
-  const int nch = c->K / 256;
-  if (nch % 4) return fail(AIB_ENOTSUP, "aib_gemv_c12: K=%d is not a multiple of 1024", c->K);
-  if (c->base >= 240)  // the exception stand-in (exponent base + 15) would not be finite
-    return fail(AIB_ENOTSUP, "aib_gemv_c12: base %d: exceptions need the exact-path kernel", c->base);
-  if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(lnw) & 7))
-    return fail(AIB_ENOTSUP, "aib_gemv_c12: x / lnw not aligned for vector loads");
-  const int CW = nch % 16 == 0 ? 16 : (nch % 8 == 0 ? 8 : 4);
-  const int R = 128 / CW, KS = nch / CW;
-  const int tiles = (c->N + R - 1) / R;
-  const StreamK sk = streamk_plan(tiles, KS, R, sm_count());
-  const bool use_sk = ws && ws_bytes >= sk.bytes && !(reinterpret_cast<uintptr_t>(ws) & 15);
-  const int grid = use_sk ? sk.grid : std::min(tiles, sm_count());
-  const int per = static_cast<int>((static_cast<long long>(tiles) * KS + grid - 1) / grid);
-  const int rows_max = use_sk ? ((per + KS - 1) / KS + 1) * R : ((tiles + grid - 1) / grid) * R;
-  const size_t xs_off = kRowsHeader;  // x (fp32, permuted), then row pointers, staged exception columns, ring
-  const size_t rps_off = xs_off + ((static_cast<size_t>(c->K) * 4 + 127) / 128) * 128;
-  const size_t ecs_off = rps_off + ((static_cast<size_t>(rows_max + 1) * 4 + 127) / 128) * 128;
-  const size_t min_ecs = 8192;  // room for at least 1024 staged exceptions (column + correction)
-  const size_t ring_need = ((ecs_off + min_ecs + 1023) / 1024) * 1024;
-  if (ring_need + 2 * static_cast<size_t>(kRowsStage) > kSmemMax)
-    return fail(AIB_ENOTSUP, "aib_gemv_c12: K=%d too large for the wide-stage kernel", c->K);
-  const int NS = std::min(8, static_cast<int>((kSmemMax - ring_need) / kRowsStage));
-  const size_t ring_off = ((kSmemMax - static_cast<size_t>(NS) * kRowsStage) / 1024) * 1024;
-  const int ecap = static_cast<int>((ring_off - ecs_off) / 8);  // column + correction per staged exception
-  const size_t smem = ring_off + static_cast<size_t>(NS) * kRowsStage;
-  CUtensorMap tm8, tme4;
-  int rc = make_maps(c, R, CW, &tm8, &tme4);
-  if (rc) return rc;
-  RowsParams p{static_cast<const uint8_t*>(c->m8), c->rp, c->ec, c->ev, x, y, lnw, eps, c->base, c->N, c->K, nch, R, CW, KS, tiles, NS,
-               static_cast<int>(xs_off), static_cast<int>(rps_off), static_cast<int>(ecs_off), ecap,
-               static_cast<int>(ring_off), 128u, 8u, 65536u,
-               use_sk ? reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + sk.flag_bytes) : nullptr,
-               use_sk ? static_cast<int*>(ws) : nullptr, sk.maxp};
-  auto go = [&](auto kernel) -> int {
-    const int r2 = allow_smem(kernel, smem);
-    if (r2) return r2;
-    return launch(kernel, dim3(grid), dim3(kRowsThreads), smem, s, "aib_gemv_c12(T=1, wide)", tm8, tme4, p);
-  };
-  if (lnw) {
-    if (mode == 0) return go(gemv_rows_kernel<0, true>);
-    if (mode == 1) return go(gemv_rows_kernel<1, true>);
-    if (mode == 3) return go(gemv_rows_kernel<3, true>);
-    return go(gemv_rows_kernel<2, true>);
-  }
-  if (mode == 0) return go(gemv_rows_kernel<0, false>);
-  if (mode == 1) return go(gemv_rows_kernel<1, false>);
-  if (mode == 3) return go(gemv_rows_kernel<3, false>);
-  return go(gemv_rows_kernel<2, false>);
-}
-
-// Wide-stage tensor-core kernel: R = 32 rows x 4 chunks (K a multiple of 1024) or 16 rows x 8 chunks (K a
-// multiple of 2048, finer row tiles); ENOTSUP when x's three-part records do not fit.
-static int g_variant = 3;  // 0: tensor-core 24 KB-stage kernel, 1: CUDA-core 12 KB stages, 2: CUDA-core 48 KB
-                           // stages, 3 (default): tensor-core wide stages, two CTAs per SM where the shape fits,
-                           // 4: tensor-core 48 KB stages, one CTA per SM
+// Kernel choice for T = 1 (test knob 4, aib_debug_knob): 3 (default) the tensor-core wide-stage kernel -- two
+// CTAs per SM with 24 KB stages where the shape fits, else one with 48 KB stages; 4 the one-CTA geometry only;
+// 1 the CUDA-core 12 KB-stage kernel for every shape it takes. Shapes the tensor-core kernel cannot take (K not a
+// multiple of 1024, x records too large for shared memory, base >= 240) always use the CUDA-core kernel.
+int g_variant = 3;
 constexpr size_t kSmemPair = 113 * 1024;  // two CTAs per SM (228 KB per SM, 1 KB reserved per CTA)
 
 template <int NCW, int SPL = 1>
@@ -2108,10 +1366,6 @@ static int run_tc(const aib_c12* c, const float* x, float* y, int mode, const ui
     return fail(AIB_ENOTSUP, "aib_gemv_c12: base %d: exceptions need the exact-path kernel", c->base);
   if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(lnw) & 7))
     return fail(AIB_ENOTSUP, "aib_gemv_c12: x / lnw not aligned for vector loads");
-  if (g_variant == 5) {
-    const int rc = run_tc_var<16, 2>(c, x, y, mode, lnw, eps, ws, ws_bytes, s);
-    if (rc != AIB_ENOTSUP) return rc;
-  }
   if (g_variant == 3) {
     const int rc = run_tc_var<8>(c, x, y, mode, lnw, eps, ws, ws_bytes, s);
     if (rc != AIB_ENOTSUP) return rc;
@@ -2121,24 +1375,15 @@ static int run_tc(const aib_c12* c, const float* x, float* y, int mode, const ui
 
 static int run_t1(const aib_c12* c, const float* x, float* y, int mode, const uint16_t* lnw, float eps, void* ws,
                   size_t ws_bytes, cudaStream_t s) {
-  if (mode == 3) {  // gated output: wide kernels only (their producer pairs the rows)
+  if (mode == 3) {  // gated output: the wide kernel only (its finisher pairs the rows)
     const int rc = run_tc(c, x, y, mode, lnw, eps, ws, ws_bytes, s);
     if (rc != AIB_ENOTSUP) return rc;
-    const int rc2 = run_rows(c, x, y, mode, lnw, eps, ws, ws_bytes, s);
-    if (rc2 != AIB_ENOTSUP) return rc2;
-    return fail(AIB_ENOTSUP, "aib_gemv_c12: mode 3 with T == 1 needs K a multiple of 1024 (K=%d)", c->K);
+    return fail(AIB_ENOTSUP, "aib_gemv_c12: mode 3 with T == 1 needs K a multiple of 1024, base < 240 and x "
+                             "within shared memory (K=%d, base %d)", c->K, c->base);
   }
-  if (g_variant >= 3) {
+  if (g_variant != 1) {
     const int rc = run_tc(c, x, y, mode, lnw, eps, ws, ws_bytes, s);
-    if (rc != AIB_ENOTSUP) return rc;
-  }
-  if (g_variant >= 2) {
-    const int rc = run_rows(c, x, y, mode, lnw, eps, ws, ws_bytes, s);
     if (rc != AIB_ENOTSUP) return rc;  // other shapes use the 12 KB-stage kernel
-  }
-  if (g_variant == 0 && c->K <= 16384) {
-    const int rc = run_mma(c, x, y, mode, lnw, eps, s);
-    if (rc != AIB_ENOTSUP) return rc;  // shapes whose x / row metadata do not fit use the CUDA-core kernel
   }
   const int nch = c->K / 256;
   const Geometry g = pick_geometry(c->N, nch, sm_count());
@@ -2202,10 +1447,6 @@ using namespace aib;
 
 extern "C" {
 
-// Kernel selection for the T = 1 GEMV (tests and A/B timing): 0 = tensor-core kernel with 24 KB stages,
-// 1 = CUDA-core kernel with 12 KB stages, 2 = CUDA-core wide-stage kernel, 3 = tensor-core wide-stage kernel
-// (default). Shapes a kernel cannot take fall back to kernel 2, then 1.
-void aib_gemv_set_variant(int v) { gemv::g_variant = v; }
 
 size_t aib_gemv_c12_workspace(const aib_c12* c, int T) {
   if (!c || T != 1 || c->N <= 0 || c->K <= 0 || c->K % 1024) return 0;

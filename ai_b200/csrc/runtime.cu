@@ -10,6 +10,9 @@ namespace aib {
 namespace attn {
 extern int g_cluster_sizes;  // attn.cu
 }
+namespace gemv {
+extern int g_variant;  // gemv.cu
+}
 
 static thread_local char t_err[512] = {0};
 static int g_pdl = 1;
@@ -131,6 +134,9 @@ int aib_debug_knob(int knob, int value) {
   } else if (knob == 3) {
     if (value < 0 || value > 2) return aib::fail(AIB_EINVAL, "aib_debug_knob(3): value %d not in 0..2", value);
     aib::attn::g_cluster_sizes = value;
+  } else if (knob == 4) {
+    if (value != 1 && value != 3 && value != 4) return aib::fail(AIB_EINVAL, "aib_debug_knob(4): value %d", value);
+    aib::gemv::g_variant = value;
   } else {
     return aib::fail(AIB_EINVAL, "aib_debug_knob: unknown knob %d", knob);
   }

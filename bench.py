@@ -445,7 +445,7 @@ def micro(args):
     build.build()
     torch.cuda.set_device(0)
     if args.gemv_variant is not None:
-        _lib.lib().aib_gemv_set_variant(args.gemv_variant)
+        _lib.call("aib_debug_knob", 4, args.gemv_variant)
     def timed(run, reps):
         """Device time per call: `reps` calls captured in one CUDA graph (no host launch overhead), replayed."""
         for _ in range(3):
@@ -553,8 +553,8 @@ def main():
                                         "gemm1", "exact", "sampler_sweep"],
                     default=None,
                     help="time one kernel alone on a small case (for ncu) instead of the decode benchmark")
-    ap.add_argument("--gemv-variant", type=int, default=None, choices=[0, 1, 2, 3, 4],
-                    help="codec GEMV kernel for --micro: 0 tensor-core 24 KB stages, 1 CUDA-core 12 KB stages, 2 CUDA-core 48 KB stages, 3 tensor-core wide stages with two CTAs per SM where they fit (default), 4 tensor-core 48 KB stages, one CTA per SM")
+    ap.add_argument("--gemv-variant", type=int, default=None, choices=[1, 3, 4],
+                    help="codec GEMV kernel for --micro (test knob 4): 1 CUDA-core 12 KB stages, 3 tensor-core wide stages with two CTAs per SM where they fit (default), 4 tensor-core 48 KB stages, one CTA per SM")
     ap.add_argument("--streamk", action="store_true", help="--micro gemv*: pass the stream-K workspace")
     ap.add_argument("--greedy", action="store_true",
                     help="greedy decoding (the int8 head's exact-candidate pick) instead of the default sampling")

@@ -73,8 +73,10 @@ int aib_status_read(int* out, int clear);
  * longer than any legitimate wait), knob 2 = 1 makes the wide T = 1 GEMV's producer withhold its copies (its stages
  * never fill, its consumers give up after the spin limit and record AIB_DEV_TIMEOUT_FULL), knob 3 = how many
  * thread-block cluster sizes (16, then 8 CTAs) the decode attention tries for its cluster merge before the
- * ticket merge (default 1; 2 lets tests cover the cluster merge on devices that cannot place clusters of 16).
- * Not for production. */
+ * ticket merge (default 0: ticket merge only; its feasibility query is not allowed inside a graph capture),
+ * knob 4 = the T = 1 GEMV kernel: 3 (default) the tensor-core wide-stage kernel, two CTAs per SM where the
+ * shape fits, else one; 4 its one-CTA-per-SM geometry only; 1 the CUDA-core 12 KB-stage kernel (the path for
+ * shapes the tensor-core kernel cannot take). Not for production. */
 int aib_debug_knob(int knob, int value);
 
 /* ---------------------------------------------------------------------------------- 12-bit codec ---- */
@@ -111,12 +113,6 @@ int aib_c12_decode(const aib_c12* c, int first, int last, void* out, int out_dty
  * previous kernel on the stream has completed, so calls in one stream may share one; calls that may overlap
  * on the GPU (other streams) need separate workspaces. */
 size_t aib_gemv_c12_workspace(const aib_c12* c, int T);
-/* Kernel choice for T == 1: 0 the tensor-core kernel with 24 KB stages (mma.sync bf16, x split in 3 bf16 parts,
- * K <= 16384), 1 the CUDA-core fp32-FMA kernel with 12 KB stages, 2 the CUDA-core kernel with 48 KB stages,
- * 3 (default) the tensor-core kernel with 48 KB stages (2 and 3: K a multiple of 1024). Shapes a kernel cannot
- * take fall back to 2, then 1. Same results within fp32 rounding; for tests and A/B timing. No reference
- * counterpart. */
-void aib_gemv_set_variant(int variant);
 int aib_gemv_c12(const aib_c12* c, const float* x, float* y, int T, int x_stride, int y_stride, int mode,
                  const uint16_t* lnw, float eps, void* ws, size_t ws_bytes, void* stream);
 

@@ -128,11 +128,13 @@ GEMV_SHAPES = [(64, 1024, 0, False), (6144, 4096, 0, True), (4096, 4096, 1, Fals
                (64, 16384, 1, False), (200, 8192, 0, True)]  # many CTAs per row tile under stream-K
 
 
-@pytest.fixture(params=[0, 1, 2, 3], ids=["tensorcore", "cudacore", "wide", "widetc"])
+@pytest.fixture(params=[1, 3, 4], ids=["cudacore", "widetc", "widetc1"])
 def variant(request, lib):
-    lib.aib_gemv_set_variant(request.param)
+    """T = 1 GEMV kernel (test knob 4): the CUDA-core 12 KB-stage kernel, the tensor-core wide-stage kernel
+    (default: two CTAs per SM where the shape fits) and its one-CTA-per-SM geometry."""
+    assert lib.aib_debug_knob(4, request.param) == 0
     yield request.param
-    lib.aib_gemv_set_variant(3)  # library default
+    assert lib.aib_debug_knob(4, 3) == 0  # library default
 
 
 @pytest.mark.parametrize("streamk", [False, True], ids=["tiles", "streamk"])
@@ -304,14 +306,13 @@ def _attn_case(H, KV, HD, maxt, pos, seed):
     return qkv, qn, kn, kc, vc
 
 
-@pytest.fixture(params=[1, 2], ids=["default", "cluster8"])
+@pytest.fixture(params=[0, 2], ids=["ticket", "cluster"])
 def cluster_sizes(request, lib):
-    """Attention merge: the default choice (cluster of 16 where the device can place one per group, else the
-    ticket merge) and the cluster merge forced down to clusters of 8 CTAs (split partials through distributed
-    shared memory)."""
+    """Attention merge: the default ticket merge, and the cluster merge (clusters of 16 where the device places
+    one per group, else of 8 CTAs; split partials through distributed shared memory)."""
     assert lib.aib_debug_knob(3, request.param) == 0
     yield request.param
-    assert lib.aib_debug_knob(3, 1) == 0
+    assert lib.aib_debug_knob(3, 0) == 0
 
 
 @pytest.mark.parametrize("H,KV,HD,pos", [(8, 2, 64, 0), (8, 2, 64, 77), (32, 8, 128, 1), (32, 8, 128, 4100),
