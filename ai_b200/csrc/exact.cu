@@ -11,7 +11,7 @@
 //  * Lane per vocabulary row: a warp owns 32 consecutive rows and walks their 256-column chunks in order, so
 //    every lane's sum is sequential with no cross-lane reduction (the reference's order by construction).
 //  * Each warp stages its rows' chunk (32 x 256 bytes of m8 + 32 x 128 bytes of e4) with 16-byte cp.async
-//    copies into a two-slot private ring (the next chunk loads while this one is summed). Rows are stored
+//    copies into a private slot (see AIB_EXACT_SLOTS for why one slot and 16 warps). Rows are stored
 //    with their 16-byte pieces XOR-swizzled by (row & 7), so the lanes' 16-byte reads of 32 different rows
 //    hit every bank group evenly (four wavefronts per LDS.128, the minimum).
 //  * Decode: byte permutes put sign and mantissa of two columns in a bf16 pair, the exponent codes (plus the
@@ -28,10 +28,16 @@
 namespace aib {
 namespace exact {
 
+// Ring slots per warp: 1 (default) -- each warp waits for its chunk, sums it and only then fetches the next,
+// and the shared memory saved doubles the warps per SM (16), which hides the sequential add chains and the
+// copy latency better than double buffering with 8 warps (Qwen3-8B head: 251 vs 275 us); 2 double-buffers.
+#ifndef AIB_EXACT_SLOTS
+#define AIB_EXACT_SLOTS 1
+#endif
 constexpr int kSlotM8 = 32 * 256;
 constexpr int kSlotE4 = 32 * 128;
 constexpr int kSlot = kSlotM8 + kSlotE4;  // 12 KB per ring slot
-constexpr int kMaxWarps = 8;
+constexpr int kMaxWarps = AIB_EXACT_SLOTS == 1 ? 16 : 8;
 
 AIB_DEV void cp_async16(void* dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
@@ -95,7 +101,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) exact_logits_kernel(Args a)
   const int groups = (V + 31) / 32;
   const int gw = gridDim.x * a.nwarps;  // warps in the grid
   const int g0 = blockIdx.x * a.nwarps + warp;
-  uint8_t* ring = smem + static_cast<size_t>(warp) * 2 * kSlot;
+  uint8_t* ring = smem + static_cast<size_t>(warp) * AIB_EXACT_SLOTS * kSlot;
   float* hs = reinterpret_cast<float*>(smem + a.h_off);
   const int n_groups = g0 < groups ? (groups - 1 - g0) / gw + 1 : 0;
   const int n_it = n_groups * nch;
@@ -127,15 +133,21 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) exact_logits_kernel(Args a)
       xc = xp < xe ? a.W.ec[xp] : INT_MAX;
     }
     // prefetch the next chunk (or the next group's first) into the other slot, then wait for this one
+#if AIB_EXACT_SLOTS == 2
     if (it + 1 < n_it) {
       const int gn = (it + 1) / nch, cn = (it + 1) - gn * nch;
       stage_chunk(a, ring + ((it + 1) & 1) * kSlot, (g0 + gn * gw) * 32, cn, lane);
     }
     cp_commit();
     cp_wait1();
+    const int cur = it & 1;
+#else
+    cp_wait0();
+    const int cur = 0;
+#endif
     __syncwarp();
-    const uint8_t* sm8 = ring + (it & 1) * kSlot + r * 256;
-    const uint8_t* se4 = ring + (it & 1) * kSlot + kSlotM8 + r * 128;
+    const uint8_t* sm8 = ring + cur * kSlot + r * 256;
+    const uint8_t* se4 = ring + cur * kSlot + kSlotM8 + r * 128;
 #pragma unroll 1
     for (int hf = 0; hf < 2; ++hf) {
 #pragma unroll 2
@@ -190,7 +202,14 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) exact_logits_kernel(Args a)
         }
       }
     }
-    __syncwarp();  // the slot is refilled two iterations from now
+    __syncwarp();  // the slot is refilled two iterations from now (one, with a single slot: right here)
+#if AIB_EXACT_SLOTS == 1
+    if (it + 1 < n_it) {
+      const int gn = (it + 1) / nch, cn = (it + 1) - gn * nch;
+      stage_chunk(a, ring, (g0 + gn * gw) * 32, cn, lane);
+    }
+    cp_commit();
+#endif
     if (c == nch - 1 && v < V) {
 #pragma unroll
       for (int t = 0; t < TT; ++t)
@@ -205,9 +224,9 @@ static int launch_tt(Args a, cudaStream_t st) {
   const int K = a.W.K;
   const size_t h_bytes = static_cast<size_t>(TT) * K * sizeof(float);
   constexpr size_t kMax = 227 * 1024;
-  if (h_bytes + 2 * kSlot > kMax) return fail(AIB_ENOTSUP, "aib_head_exact_logits: K=%d too large", K);
-  a.nwarps = static_cast<int>(std::min<size_t>(kMaxWarps, (kMax - h_bytes) / (2 * kSlot)));
-  a.h_off = a.nwarps * 2 * kSlot;
+  if (h_bytes + AIB_EXACT_SLOTS * kSlot > kMax) return fail(AIB_ENOTSUP, "aib_head_exact_logits: K=%d too large", K);
+  a.nwarps = static_cast<int>(std::min<size_t>(kMaxWarps, (kMax - h_bytes) / (AIB_EXACT_SLOTS * kSlot)));
+  a.h_off = a.nwarps * AIB_EXACT_SLOTS * kSlot;
   const size_t smem = a.h_off + h_bytes;
   const int rc = allow_smem(exact_logits_kernel<TT>, smem);
   if (rc) return rc;
