@@ -45,6 +45,8 @@ SIGNATURES = {
     "aib_head8_workspace": (SZ, [I32, I32, I32]),
     "aib_head8_bounds": (I32, [P, I32, I32, P, P, P, P, P, I32, I32, P, I32, P, P, SZ, P]),
     "aib_head8_greedy": (I32, [P, I32, I32, C.POINTER(C12Desc), P, I32, P, P, P, SZ, P]),
+    "aib_head8_bounds_topk": (I32, [P, I32, I32, P, P, P, P, P, I32, I32, P, I32, P, I32, P, SZ, P]),
+    "aib_head8_candidate_logits": (I32, [P, I32, I32, C.POINTER(C12Desc), P, I32, P, P, I32, P, SZ, P]),
     "aib_head_exact_logits": (I32, [P, I32, I32, C.POINTER(C12Desc), P, I32, P]),
     "aib_gemv_c12": (I32, [C.POINTER(C12Desc), P, P, I32, I32, I32, I32, P, F32, P, SZ, P]),
     "aib_gemm_c12_workspace": (SZ, [I32, I32, I32]),

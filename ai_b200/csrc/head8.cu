@@ -98,6 +98,7 @@ struct BoundsArgs {
   float* LO;
   float* part;  // [kTokPass][gridDim.x] CTA maxima of a - B
   int* ticket;
+  int kk;       // LO = a lower bound of the kk-th largest exact logit (1: the largest lower bound)
 };
 
 // TT: tokens handled per pass, rounded up to 1, 2, 4 or 8 (loops over t < a.T inside). Each warp walks its
@@ -133,6 +134,7 @@ __global__ void __launch_bounds__(kThreads, 2) bounds_kernel(BoundsArgs a) {
   }
   __syncthreads();
   pdl_trigger();
+  // lo[t]: lane j holds the warp's (j+1)-th largest lower bound a - B so far (descending across lanes)
   float lo[TT], acc[TT];
 #pragma unroll
   for (int t = 0; t < TT; ++t) lo[t] = -INFINITY, acc[t] = 0.0f;
@@ -186,7 +188,9 @@ __global__ void __launch_bounds__(kThreads, 2) bounds_kernel(BoundsArgs a) {
           const float av = s * dot;
           const float b = fminf(c2 * n2s[t], c1 * n1s[t]) + kSlack * am * n1s[t];
           if (lane == 0) a.HI[static_cast<size_t>(t) * a.ldhi + v] = av + b;
-          lo[t] = fmaxf(lo[t], av - b);
+          // insert av - b (the same value in every lane) into the warp's sorted list
+          const float x = av - b, prev = __shfl_up_sync(0xffffffffu, lo[t], 1);
+          if (x > lo[t]) lo[t] = (lane == 0 || x <= prev) ? x : prev;
         }
         acc[t] = 0.0f;
       }
@@ -201,9 +205,13 @@ __global__ void __launch_bounds__(kThreads, 2) bounds_kernel(BoundsArgs a) {
     while (step(qa, qb) && step(qb, qa)) {
     }
   }
-  if (lane == 0)
+  // the warp's kk-th largest lower bound: at most the grid's kk-th largest, so the maximum over the warps is a
+  // lower bound of the kk-th largest exact logit (every warp's kk values are distinct rows)
 #pragma unroll
-    for (int t = 0; t < kTokPass; ++t) wlo[warp][t] = t < TT ? lo[t] : -INFINITY;
+  for (int t = 0; t < kTokPass; ++t) {
+    const float w = t < TT ? __shfl_sync(0xffffffffu, lo[t < TT ? t : 0], a.kk - 1) : -INFINITY;
+    if (lane == 0) wlo[warp][t] = w;
+  }
   __syncthreads();
   if (tid < T) {
     float m = -INFINITY;
@@ -237,15 +245,19 @@ AIB_DEV unsigned long long pick_key(float x, int v) {
   return (static_cast<unsigned long long>(u) << 32) | (0xFFFFFFFFu - static_cast<uint32_t>(v));
 }
 
-// Candidates (t, v) with HI[t, v] >= LO[t], appended as t << 24 | v.
+// Candidates (t, v) with HI[t, v] >= LO[t], appended as t << 24 | v; with `fill`, every other (t, v) gets
+// fill[t * ldf + v] = -inf (the candidates' exact logits are written there afterwards).
 __global__ void __launch_bounds__(kThreads) cand_kernel(const float* __restrict__ HI, int ldhi,
                                                         const float* __restrict__ LO, int T, int V, int* list,
-                                                        int* count) {
+                                                        int* count, float* fill, int ldf) {
   pdl_wait();
   const long long i = static_cast<long long>(blockIdx.x) * kThreads + threadIdx.x;
   if (i < static_cast<long long>(V) * T) {
     const int t = static_cast<int>(i / V), v = static_cast<int>(i % V);
-    if (HI[static_cast<size_t>(t) * ldhi + v] >= LO[t]) list[atomicAdd(count, 1)] = (t << 24) | v;
+    if (HI[static_cast<size_t>(t) * ldhi + v] >= LO[t])
+      list[atomicAdd(count, 1)] = (t << 24) | v;
+    else if (fill)
+      fill[static_cast<size_t>(t) * ldf + v] = -INFINITY;
   }
   pdl_trigger();
 }
@@ -262,6 +274,8 @@ struct GreedyArgs {
   int64_t* out;
   unsigned long long* best;  // [16], zero between calls
   int* ticket;
+  float* logits;  // non-null: write every candidate's exact logit to logits[t * ldl + v] instead of picking
+  int ldl;
 };
 
 // Exact logit of every listed candidate: the warp decodes row v from the codec planes (4 columns per lane
@@ -312,7 +326,10 @@ __global__ void __launch_bounds__(kXWarps * 32) exact_kernel(GreedyArgs a) {
         sum = __fadd_rn(sum, y.z);
         sum = __fadd_rn(sum, y.w);
       }
-      atomicMax(a.best + t, pick_key(sum, v));
+      if (a.logits)
+        a.logits[static_cast<size_t>(t) * a.ldl + v] = sum;
+      else
+        atomicMax(a.best + t, pick_key(sum, v));
     }
     __syncwarp();  // the products are rewritten by the next candidate
   }
@@ -322,7 +339,7 @@ __global__ void __launch_bounds__(kXWarps * 32) exact_kernel(GreedyArgs a) {
   __syncthreads();
   if (last) {
     __threadfence();
-    for (int t = threadIdx.x; t < a.T; t += kXWarps * 32) {
+    for (int t = threadIdx.x; t < a.T && !a.logits; t += kXWarps * 32) {
       const unsigned long long k = atomicExch(a.best + t, 0ull);
       a.out[t] = k ? static_cast<int64_t>(0xFFFFFFFFu - static_cast<uint32_t>(k & 0xFFFFFFFFull)) : -1;
     }
@@ -383,11 +400,11 @@ size_t aib_head8_workspace(int V, int D, int T) {
   return head8::kListOff + static_cast<size_t>(16) * V * sizeof(int);
 }
 
-int aib_head8_bounds(const float* h, int T, int ldh, const int8_t* Q, const float* S, const float* C1,
-                     const float* C2, const float* AM, int V, int D, float* HI, int ldhi, float* LO, void* ws,
-                     size_t ws_bytes, void* stream) {
+int aib_head8_bounds_topk(const float* h, int T, int ldh, const int8_t* Q, const float* S, const float* C1,
+                          const float* C2, const float* AM, int V, int D, float* HI, int ldhi, float* LO, int k,
+                          void* ws, size_t ws_bytes, void* stream) {
   if (!h || !Q || !S || !C1 || !C2 || !AM || !HI || !LO || V <= 0 || D <= 0 || T < 1 || T > 16 || ldh < D ||
-      ldhi < V || V >= (1 << 24))
+      ldhi < V || V >= (1 << 24) || k < 1 || k > 32)
     return fail(AIB_EINVAL, "aib_head8_bounds: bad arguments");
   if (D % 16 || (reinterpret_cast<uintptr_t>(Q) & 15))
     return fail(AIB_EINVAL, "aib_head8_bounds: D must be a multiple of 16 and Q 16-byte aligned (D=%d)", D);
@@ -401,7 +418,8 @@ int aib_head8_bounds(const float* h, int T, int ldh, const int8_t* Q, const floa
     const size_t smem = (static_cast<size_t>(tt) * nch * head8::kChunk + 2 * head8::kTokPass) * sizeof(float);
     head8::BoundsArgs a{h + static_cast<size_t>(t0) * ldh, ldh, tt, Q, S, C1, C2, AM, V, D, nch,
                         HI + static_cast<size_t>(t0) * ldhi, ldhi, LO + t0,
-                        reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + head8::kPartOff), static_cast<int*>(ws)};
+                        reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + head8::kPartOff), static_cast<int*>(ws),
+                        k};
     const int rc = tt == 1   ? head8::launch_bounds_tt<1>(a, smem, s)
                    : tt == 2 ? head8::launch_bounds_tt<2>(a, smem, s)
                    : tt <= 4 ? head8::launch_bounds_tt<4>(a, smem, s)
@@ -411,10 +429,20 @@ int aib_head8_bounds(const float* h, int T, int ldh, const int8_t* Q, const floa
   return AIB_OK;
 }
 
-int aib_head8_greedy(const float* h, int T, int ldh, const aib_c12* W, const float* HI, int ldhi, const float* LO,
-                     int64_t* out, void* ws, size_t ws_bytes, void* stream) {
-  if (!h || !W || !W->m8 || !W->e4 || !W->rp || (W->n_exc > 0 && (!W->ec || !W->ev)) || !HI || !LO || !out ||
-      T < 1 || T > 16 || W->N <= 0 || W->K <= 0 || W->K % 256 || ldh < W->K || ldhi < W->N || W->N >= (1 << 24))
+int aib_head8_bounds(const float* h, int T, int ldh, const int8_t* Q, const float* S, const float* C1,
+                     const float* C2, const float* AM, int V, int D, float* HI, int ldhi, float* LO, void* ws,
+                     size_t ws_bytes, void* stream) {
+  return aib_head8_bounds_topk(h, T, ldh, Q, S, C1, C2, AM, V, D, HI, ldhi, LO, 1, ws, ws_bytes, stream);
+}
+
+// Candidates HI >= LO, then their exact logits: the greedy pick (out) or, with `logits`, the logits row itself
+// (-inf outside the candidates).
+static int head8_candidates(const float* h, int T, int ldh, const aib_c12* W, const float* HI, int ldhi,
+                            const float* LO, int64_t* out, float* logits, int ldl, void* ws, size_t ws_bytes,
+                            void* stream) {
+  if (!h || !W || !W->m8 || !W->e4 || !W->rp || (W->n_exc > 0 && (!W->ec || !W->ev)) || !HI || !LO ||
+      (!out && !logits) || T < 1 || T > 16 || W->N <= 0 || W->K <= 0 || W->K % 256 || ldh < W->K || ldhi < W->N ||
+      W->N >= (1 << 24) || (logits && ldl < W->N))
     return fail(AIB_EINVAL, "aib_head8_greedy: bad arguments");
   if ((ldh & 3) || (reinterpret_cast<uintptr_t>(h) & 15) || (reinterpret_cast<uintptr_t>(W->m8) & 15) ||
       (reinterpret_cast<uintptr_t>(W->e4) & 15))
@@ -432,12 +460,25 @@ int aib_head8_greedy(const float* h, int T, int ldh, const aib_c12* W, const flo
   int* list = reinterpret_cast<int*>(w8 + head8::kListOff);
   const long long n = static_cast<long long>(W->N) * T;
   rc = launch(head8::cand_kernel, dim3(static_cast<int>((n + head8::kThreads - 1) / head8::kThreads)),
-              dim3(head8::kThreads), 0, s, "aib_head8_greedy (candidates)", HI, ldhi, LO, T, W->N, list, count);
+              dim3(head8::kThreads), 0, s, "aib_head8_greedy (candidates)", HI, ldhi, LO, T, W->N, list, count,
+              logits, ldl);
   if (rc) return rc;
   head8::GreedyArgs a{h, ldh, *W, list, count, T, out,
-                      reinterpret_cast<unsigned long long*>(w8 + head8::kBestOff), ticket};
+                      reinterpret_cast<unsigned long long*>(w8 + head8::kBestOff), ticket, logits, ldl};
   const int grid = head8::resident_grid(head8::exact_kernel, head8::kXWarps * 32, smem, 4);
   return launch(head8::exact_kernel, dim3(grid), dim3(head8::kXWarps * 32), smem, s, "aib_head8_greedy", a);
+}
+
+int aib_head8_greedy(const float* h, int T, int ldh, const aib_c12* W, const float* HI, int ldhi, const float* LO,
+                     int64_t* out, void* ws, size_t ws_bytes, void* stream) {
+  if (!out) return fail(AIB_EINVAL, "aib_head8_greedy: out is NULL");
+  return head8_candidates(h, T, ldh, W, HI, ldhi, LO, out, nullptr, 0, ws, ws_bytes, stream);
+}
+
+int aib_head8_candidate_logits(const float* h, int T, int ldh, const aib_c12* W, const float* HI, int ldhi,
+                               const float* LO, float* logits, int ldl, void* ws, size_t ws_bytes, void* stream) {
+  if (!logits) return fail(AIB_EINVAL, "aib_head8_candidate_logits: logits is NULL");
+  return head8_candidates(h, T, ldh, W, HI, ldhi, LO, nullptr, logits, ldl, ws, ws_bytes, stream);
 }
 
 }  // extern "C"

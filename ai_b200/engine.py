@@ -275,7 +275,9 @@ class Engine:
             self.head8.pick(self.hb[r0:T], rows, out=self.out_ids[r0:T])
         else:
             # sampling (or penalties): exact logits of the whole vocabulary, as Head.pick computes them for
-            # sampling (head.py:62-71), then the device sampler
+            # sampling (head.py:62-71), then the device sampler. (Head.topk_logits would restrict top-k sampling
+            # to the int8 bounds' candidates; on the random-init benchmark head the bounds keep nearly every row
+            # and that path measured 4.64 vs 3.36 ms per step, so it is not the engine's default.)
             self._exact(r0, T, rows)
             sampler.sample_into(self.logits[r0:T], self.out_ids[r0:T], prm,
                                 self.u[:rows] if prm.temperature > 0 else None, self.prior if penal else None, None,

@@ -50,13 +50,29 @@ class Head:
             raise ValueError("Head: h rows must be contiguous")
         return h
 
-    def bounds(self, h, T):
-        """HI[:T], LO[:T] for rows h[:T] (on the device, graph-capturable)."""
+    def bounds(self, h, T, k=1):
+        """HI[:T], LO[:T] for rows h[:T] (on the device, graph-capturable). k > 1 (<= 32): LO bounds the k-th
+        largest exact logit from below instead of the largest, so HI >= LO keeps every row of the exact top k."""
         h = self._h(h, T)
-        _lib.call("aib_head8_bounds", ptr(h), T, h.stride(0), ptr(self.Q), ptr(self.S), ptr(self.C1), ptr(self.C2),
-                  ptr(self.AM), self.V, self.D, ptr(self.HI), self.V, ptr(self.LO), ptr(self.ws), self.ws.numel(),
-                  stream_ptr())
+        if not 1 <= k <= 32:
+            raise ValueError("Head.bounds: k must be in 1..32")
+        _lib.call("aib_head8_bounds_topk", ptr(h), T, h.stride(0), ptr(self.Q), ptr(self.S), ptr(self.C1),
+                  ptr(self.C2), ptr(self.AM), self.V, self.D, ptr(self.HI), self.V, ptr(self.LO), int(k), ptr(self.ws),
+                  self.ws.numel(), stream_ptr())
         return self.HI[:T], self.LO[:T]
+
+    def topk_logits(self, h, T, k, out):
+        """out[:T, :V] = exact logits of every row that can be in the top k of h[:T] (the candidates of
+        bounds(h, T, k)) and -inf elsewhere: what a top-k sampler needs, at the cost of the int8 pass plus the
+        candidates' rows instead of the whole 12-bit head."""
+        h = self._h(h, T)
+        if out.dtype != torch.float32 or out.dim() != 2 or out.shape[0] < T or out.shape[1] < self.V or \
+                out.stride(1) != 1:
+            raise ValueError("Head.topk_logits: out must be fp32 [>=T, >=V] with contiguous rows")
+        self.bounds(h, T, k)
+        _lib.call("aib_head8_candidate_logits", ptr(h), T, h.stride(0), C.byref(self._desc), ptr(self.HI), self.V,
+                  ptr(self.LO), ptr(out), out.stride(0), ptr(self.ws), self.ws.numel(), stream_ptr())
+        return out[:T, :self.V]
 
     def pick(self, h, T, temperature=0.0, run_bounds=True, out=None):
         """Greedy ids for rows h[:T]: an int64 device tensor of length T (`out` if given, else a view of an

@@ -150,6 +150,18 @@ int aib_head8_bounds(const float* h, int T, int ldh, const int8_t* Q, const floa
  * order, head.py:19-26); out[t] = the argmax, the smallest id on ties. */
 int aib_head8_greedy(const float* h, int T, int ldh, const aib_c12* W, const float* HI, int ldhi, const float* LO,
                      int64_t* out, void* ws, size_t ws_bytes, void* stream);
+/* Top-k candidates (no reference counterpart; the reference computes exact logits of the whole vocabulary
+ * whenever it samples). aib_head8_bounds_topk: as aib_head8_bounds, but LO[t] = the largest over the kernel's
+ * warps of each warp's k-th largest s_v Q_v.h_t - B (1 <= k <= 32; k = 1 is aib_head8_bounds), a lower bound
+ * of the k-th largest exact logit, so the rows with HI[t, v] >= LO[t] contain every row of the exact top k
+ * (ties included). aib_head8_candidate_logits: logits[t, v] (row stride ldl) = the exact logit (as
+ * aib_head8_greedy computes it) for those rows and -inf for every other row; a sampler that keeps only the
+ * top k then draws exactly what it draws from the full exact logits. */
+int aib_head8_bounds_topk(const float* h, int T, int ldh, const int8_t* Q, const float* S, const float* C1,
+                          const float* C2, const float* AM, int V, int D, float* HI, int ldhi, float* LO, int k,
+                          void* ws, size_t ws_bytes, void* stream);
+int aib_head8_candidate_logits(const float* h, int T, int ldh, const aib_c12* W, const float* HI, int ldhi,
+                               const float* LO, float* logits, int ldl, void* ws, size_t ws_bytes, void* stream);
 /* Exact logits of every vocabulary row for T <= 16 rows of h (fp32 [T, ldh]) from the 12-bit head W [V, D]
  * (replaces the full-vocabulary exact_rows call of Head.pick when sampling, generation/head.py:19-26 and
  * :62-71): out[t, v] (row stride ldo) = sum over d in column order of fp32(w[v,d] * h[t,d]), each product

@@ -601,6 +601,32 @@ def test_head8_greedy_vs_oracle(lib, T, ties, exc):
     assert status_clear() == 0
 
 
+@pytest.mark.parametrize("T,k,ties,exc", [(1, 1, False, False), (1, 20, False, True), (3, 32, True, False),
+                                         (2, 5, True, True)])
+def test_head8_topk_logits_vs_oracle(lib, T, k, ties, exc):
+    """Top-k candidate logits: every row of the exact top k (ties at the k-th value included) is kept with its
+    exact fp32 logit (bit-identical to exact_rows, head.py:19-26), every other row is either kept exactly or set
+    to -inf, and the rows set to -inf are all below the k-th largest exact logit."""
+    from ai_b200.head import Head
+    wb, h, c = _head_case(400 + T + 3 * k + 7 * ties + 11 * exc, 3000, 512, T, ties=ties, exceptions=exc)
+    hd = Head(from_bits(wb), c)
+    H = torch.from_numpy(h).cuda()
+    ex = ohead.exact_logits(wb, h)
+    out = torch.full((T, 3000), float("nan"), device="cuda")
+    for _ in range(2):
+        got = hd.topk_logits(H, T, k, out).cpu().numpy()
+        for t in range(T):
+            kth = np.sort(ex[t])[::-1][k - 1]
+            kept = np.isfinite(got[t])
+            assert not np.isnan(got[t]).any()
+            np.testing.assert_array_equal(got[t][kept], ex[t][kept])
+            assert kept[ex[t] >= kth].all()
+            assert (ex[t][~kept] < kth).all()
+            if not (exc or ties):  # plain random rows: the bounds prune most of the vocabulary
+                assert kept.sum() < 3000
+    assert status_clear() == 0
+
+
 # ------------------------------------------------------------------------------ exact vocabulary logits
 def _exact(c, h, T):
     from ai_b200.head import exact_logits
