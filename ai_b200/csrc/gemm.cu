@@ -56,6 +56,9 @@ struct Params {
   uint32_t tmem_cols;
   int w_off, o_off, o_stage;
   uint32_t k128, k8;
+  int ks, kb_per;  // split-K: blockIdx.z takes k-blocks [z * kb_per, (z + 1) * kb_per) of nkb
+  float* part;     // ks > 1: [tile][split][BM rows][TN] fp32 partial tiles
+  int* tick;       // ks > 1: one arrival counter per (token tile, weight tile), zero before the launch
 };
 
 // ----------------------------------------------------------------------------------- tcgen05 wrappers
@@ -141,7 +144,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* oring = smem + p.o_off;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int m0 = blockIdx.x * p.TN, n0 = blockIdx.y * BM;
-  const int nkb = p.nkb, NW = p.NW, NO = p.NO;
+  const int NW = p.NW, NO = p.NO;
+  const int kb_begin = static_cast<int>(blockIdx.z) * p.kb_per;
+  const int nk = max(0, min(p.nkb, kb_begin + p.kb_per) - kb_begin);  // k-blocks of this split
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < NW; ++s) {
@@ -170,16 +175,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       prefetch_tensormap(&tm8);
       prefetch_tensormap(&tme4);
       int issued = 0;
-      for (int kb = 0; kb < nkb; ++kb) {
-        const int s = kb % NW;
-        if (kb >= NW && !wait_b(&wempty[s], ((kb / NW) - 1) & 1, abort_flag, AIB_DEV_TIMEOUT_EMPTY)) break;
+      for (int i = 0; i < nk; ++i) {
+        const int s = i % NW;
+        if (i >= NW && !wait_b(&wempty[s], ((i / NW) - 1) & 1, abort_flag, AIB_DEV_TIMEOUT_EMPTY)) break;
         if (*abort_flag) break;
         uint8_t* st = wring + s * kWStage;
-        const int kc = kb * BK;
+        const int kc = (kb_begin + i) * BK;
         mbar_arrive_expect_tx(&wfull[s], kWStage);
         tma_load_2d(st, &tm8, &wfull[s], kc, n0);
         tma_load_2d(st + kPlane, &tme4, &wfull[s], (kc >> 8) * 128 + (kc & 127), n0);
-        issued = kb + 1;
+        issued = i + 1;
       }
       if (*abort_flag)  // never leave with copies in flight
         for (int it = (issued > NW ? issued - NW : 0); it < issued; ++it)
@@ -192,15 +197,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       prefetch_tensormap(&tmx);
       int issued = 0;
       const uint32_t bytes = static_cast<uint32_t>(PARTS * p.TN * 128);
-      for (int kb = 0; kb < nkb; ++kb) {
-        const int s = kb % NO;
-        if (kb >= NO && !wait_b(&oempty[s], ((kb / NO) - 1) & 1, abort_flag, AIB_DEV_TIMEOUT_EMPTY)) break;
+      for (int i = 0; i < nk; ++i) {
+        const int s = i % NO;
+        if (i >= NO && !wait_b(&oempty[s], ((i / NO) - 1) & 1, abort_flag, AIB_DEV_TIMEOUT_EMPTY)) break;
         if (*abort_flag) break;
         uint8_t* st = oring + s * p.o_stage + kATile;
         mbar_arrive_expect_tx(&ofull[s], bytes);
 #pragma unroll
-        for (int q = 0; q < PARTS; ++q) tma_load_3d(st + q * p.TN * 128, &tmx, &ofull[s], kb * BK, m0, q);
-        issued = kb + 1;
+        for (int q = 0; q < PARTS; ++q)
+          tma_load_3d(st + q * p.TN * 128, &tmx, &ofull[s], (kb_begin + i) * BK, m0, q);
+        issued = i + 1;
       }
       if (*abort_flag)
         for (int it = (issued > NO ? issued - NO : 0); it < issued; ++it)
@@ -209,9 +215,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     pdl_trigger();
   } else if (warp == 1) {  // ----------------------------------------------- MMA issue
     if (lane == 0) {
-      for (int kb = 0; kb < nkb; ++kb) {
-        const int s = kb % NO;
-        if (!wait_b(&ofull[s], (kb / NO) & 1, abort_flag, AIB_DEV_TIMEOUT_FULL)) break;
+      for (int i = 0; i < nk; ++i) {
+        const int s = i % NO;
+        if (!wait_b(&ofull[s], (i / NO) & 1, abort_flag, AIB_DEV_TIMEOUT_FULL)) break;
         tc_fence_after();
         const uint32_t a0 = smem_u32(oring + s * p.o_stage), b0 = a0 + kATile;
 #pragma unroll
@@ -219,7 +225,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int q = 0; q < PARTS; ++q)
             tc_mma(tmem, sw128_desc(a0 + k * 32), sw128_desc(b0 + q * p.TN * 128 + k * 32), p.idesc,
-                   (kb | k | q) != 0);
+                   (i | k | q) != 0);
         tc_commit(&oempty[s]);
       }
       tc_commit(accfull);  // arrives once every MMA issued above has completed (also after an abort)
@@ -233,6 +239,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (n < p.N) {
       xp = p.rp[n];
       xe = p.rp[n + 1];
+      while (xp < xe && p.ec[xp] < kb_begin * BK) ++xp;  // exceptions of earlier splits
       if (xp < xe) {
         xc = p.ec[xp];
         xv = p.ev[xp];
@@ -242,10 +249,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t k128 = p.k128, k8 = p.k8;
     const int sx = (t >> 1) & 3, ax = t & 7;
     bool aborted = false;
-    for (int kb = 0; kb < nkb; ++kb) {
-      const int sw = kb % NW, so = kb % NO;
-      bool ok = wait_b(&wfull[sw], (kb / NW) & 1, abort_flag, AIB_DEV_TIMEOUT_FULL);
-      if (ok && kb >= NO) ok = wait_b(&oempty[so], ((kb / NO) - 1) & 1, abort_flag, AIB_DEV_TIMEOUT_EMPTY);
+    for (int i = 0; i < nk; ++i) {
+      const int sw = i % NW, so = i % NO;
+      bool ok = wait_b(&wfull[sw], (i / NW) & 1, abort_flag, AIB_DEV_TIMEOUT_FULL);
+      if (ok && i >= NO) ok = wait_b(&oempty[so], ((i / NO) - 1) & 1, abort_flag, AIB_DEV_TIMEOUT_EMPTY);
       if (!__all_sync(0xffffffffu, ok)) {
         aborted = true;
         break;
@@ -253,7 +260,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint8_t* pm = wring + sw * kWStage + t * 64;
       const uint8_t* pe = pm + kPlane;
       uint8_t* pa = oring + so * p.o_stage + t * 128;
-      const int kc = kb * BK;
+      const int kc = (kb_begin + i) * BK;
       const bool hi = (kc & 255) >= 128;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
@@ -293,6 +300,45 @@ __global__ void __launch_bounds__(kThreads, 1)
     pdl_trigger();
     tc_fence_after();
     const int q = warp & 3, row = 32 * q + lane, nn = n0 + row;
+    if (p.ks > 1) {
+      // split-K: this split's partial tile to the workspace; the last split of the tile to arrive adds the
+      // splits in split order (deterministic) and applies the output mode
+      const int tile = static_cast<int>(blockIdx.y * gridDim.x + blockIdx.x), ks = p.ks;
+      float* mine = p.part + ((static_cast<size_t>(tile) * ks + blockIdx.z) * BM + row) * p.TN;
+      for (int c0 = 0; c0 < p.TN; c0 += 16) {
+        uint32_t v[16];
+        tmem_ld16(tmem + (static_cast<uint32_t>(32 * q) << 16) + static_cast<uint32_t>(c0), v);
+        tmem_wait_ld();
+        if (!aborted)
+#pragma unroll
+          for (int j = 0; j < 16; ++j) mine[c0 + j] = __uint_as_float(v[j]);
+      }
+      __threadfence();
+      named_sync(1, 128);  // the four epilogue warps
+      if (threadIdx.x == 96) *reinterpret_cast<volatile int*>(smem + 264) = atomicAdd(&p.tick[tile], 1) == ks - 1;
+      named_sync(1, 128);
+      if (*reinterpret_cast<volatile int*>(smem + 264) && !aborted) {
+        __threadfence();
+        const float* base = p.part + (static_cast<size_t>(tile) * ks * BM + row) * p.TN;
+        for (int c = 0; c < p.TN; ++c) {
+          const int m = m0 + c;
+          if (m >= p.M) break;  // uniform across the warp
+          float val = 0.0f;
+          for (int z = 0; z < ks; ++z) val += __ldcg(base + static_cast<size_t>(z) * BM * p.TN + c);
+          float* yr = p.y + static_cast<size_t>(m) * p.ldy;
+          if (p.ymode == 3) {
+            const float u = __shfl_down_sync(0xffffffffu, val, 1);
+            if (!(lane & 1) && nn < p.N) yr[nn >> 1] = val / (1.0f + expf(-val)) * u;
+          } else if (nn < p.N) {
+            if (p.ymode == 1)
+              yr[nn] += val;
+            else
+              yr[nn] = val;
+          }
+        }
+        if (threadIdx.x == 96) p.tick[tile] = 0;
+      }
+    } else
     for (int c0 = 0; c0 < p.TN; c0 += 16) {
       uint32_t v[16];
       tmem_ld16(tmem + (static_cast<uint32_t>(32 * q) << 16) + static_cast<uint32_t>(c0), v);
@@ -330,9 +376,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 // parts = 1: bf16(xin); parts = 3: x1 = bf16(x), x2 = bf16(x - x1), x3 = bf16(x - x1 - x2), round to nearest.
 __global__ void __launch_bounds__(256) prep_kernel(const float* __restrict__ x, int ldx, int M, int K, int xmode,
                                                    const uint16_t* __restrict__ lnw, float eps, int parts,
-                                                   uint16_t* __restrict__ xp) {
+                                                   uint16_t* __restrict__ xp, int* tick, int ntick) {
   pdl_wait();
   const int m = blockIdx.x;
+  if (m == 0)  // the split-K counters of the GEMM that follows (the previous GEMM is complete by now)
+    for (int i = threadIdx.x; i < ntick; i += 256) tick[i] = 0;
   const float* xr = x + static_cast<size_t>(m) * ldx;
   float rs = 1.0f;
   if (lnw) {
@@ -380,8 +428,30 @@ static uint32_t tmem_cols_for(int TN) {
 
 constexpr size_t kSmemMax = 227 * 1024;
 
+// Split-K for few tokens (M <= 16: one token tile): the weight tiles alone would leave most SMs idle (N = 4096
+// gives 32 tiles), so every tile's K range is split over up to 8 CTAs, at least 4 k-blocks each, about one CTA
+// per SM in total. Workspace past the activation parts: [256-aligned] counters, partial tiles.
+constexpr int kMaxTicks = 1024;
+static int split_k(int M, int N, int K) {
+  if (M > 16) return 1;
+  const int tiles = (N + BM - 1) / BM, nkb = K / BK;
+  int ks = std::max(1, std::min(8, sm_count() / std::max(1, tiles)));
+  ks = std::min(ks, std::max(1, nkb / 4));
+  if (tiles > kMaxTicks) ks = 1;
+  const int per = (nkb + ks - 1) / ks;
+  return (nkb + per - 1) / per;
+}
+static size_t split_bytes(int M) {  // counters + partial tiles (tiles * ks <= SMs; TN = 16)
+  if (M > 16) return 0;
+  return 256 + kMaxTicks * sizeof(int) + static_cast<size_t>(sm_count()) * BM * 16 * sizeof(float);
+}
+static size_t prep_bytes(int M, int K, int parts) {
+  return ((static_cast<size_t>(parts) * M * K * sizeof(uint16_t) + 255) / 256) * 256;
+}
+
 template <int PARTS>
-static int launch_gemm(const aib_c12* W, const uint16_t* xp, int M, float* y, int ldy, int ymode, cudaStream_t s) {
+static int launch_gemm(const aib_c12* W, const uint16_t* xp, int M, float* y, int ldy, int ymode, cudaStream_t s,
+                       int* tick, float* part) {
   const int N = W->N, K = W->K;
   const int TN = pick_tn(M, PARTS);
   const int o_stage = kATile + PARTS * TN * 128;
@@ -431,9 +501,13 @@ static int launch_gemm(const aib_c12* W, const uint16_t* xp, int M, float* y, in
   p.o_stage = o_stage;
   p.k128 = 128u;
   p.k8 = 8u;
+  p.ks = split_k(M, N, K);
+  p.kb_per = (p.nkb + p.ks - 1) / p.ks;
+  p.part = part;
+  p.tick = tick;
   const int rc = allow_smem(gemm_c12_kernel<PARTS>, smem);
   if (rc) return rc;
-  const dim3 grid((M + TN - 1) / TN, (N + BM - 1) / BM);
+  const dim3 grid((M + TN - 1) / TN, (N + BM - 1) / BM, p.ks);
   return launch(gemm_c12_kernel<PARTS>, grid, dim3(kThreads), smem, s, "aib_gemm_c12", tm8, tme4, tmx, p);
 }
 
@@ -446,7 +520,7 @@ extern "C" {
 
 size_t aib_gemm_c12_workspace(int M, int K, int precision) {
   if (M <= 0 || K <= 0 || (precision != 1 && precision != 3)) return 0;
-  return static_cast<size_t>(precision) * M * K * sizeof(uint16_t);
+  return gemm::prep_bytes(M, K, precision) + gemm::split_bytes(M);
 }
 
 int aib_gemm_c12(const aib_c12* W, const float* X, int M, int ldx, int xmode, const uint16_t* lnw, float eps, float* Y,
@@ -469,11 +543,14 @@ int aib_gemm_c12(const aib_c12* W, const float* X, int M, int ldx, int xmode, co
                 aib_gemm_c12_workspace(M, W->K, precision));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   uint16_t* xp = static_cast<uint16_t*>(ws);
+  uint8_t* sk = static_cast<uint8_t*>(ws) + gemm::prep_bytes(M, W->K, precision);
+  int* tick = M <= 16 ? reinterpret_cast<int*>(sk + 256) : nullptr;
+  float* part = M <= 16 ? reinterpret_cast<float*>(sk + 256 + gemm::kMaxTicks * sizeof(int)) : nullptr;
   int rc = launch(gemm::prep_kernel, dim3(M), dim3(256), 0, s, "aib_gemm_c12 (prep)", X, ldx, M, W->K, xmode, lnw,
-                  eps, precision, xp);
+                  eps, precision, xp, tick, tick ? gemm::kMaxTicks : 0);
   if (rc) return rc;
-  return precision == 3 ? gemm::launch_gemm<3>(W, xp, M, Y, ldy, ymode, s)
-                        : gemm::launch_gemm<1>(W, xp, M, Y, ldy, ymode, s);
+  return precision == 3 ? gemm::launch_gemm<3>(W, xp, M, Y, ldy, ymode, s, tick, part)
+                        : gemm::launch_gemm<1>(W, xp, M, Y, ldy, ymode, s, tick, part);
 }
 
 }  // extern "C"

@@ -61,7 +61,27 @@ CASES = [  # (M, N, K, xmode, ymode, rms)
     (128, 256, 512, 0, 0, False), (37, 300, 1024, 0, 1, False), (300, 384, 256, 0, 0, True),
     (200, 256, 1024, 2, 1, False), (64, 512, 768, 0, 3, True), (17, 128, 4096, 0, 0, True),
     (513, 640, 2048, 0, 1, False),
+    # M <= 16: split-K over up to 8 CTAs per weight tile (partials added in split order by the last split)
+    (1, 256, 4096, 0, 1, True), (8, 4096, 4096, 0, 3, True), (16, 1024, 12288, 2, 1, False), (5, 640, 2048, 0, 0, False),
 ]
+
+
+def test_gemm_split_k_deterministic(lib):
+    """Few tokens split K over several CTAs per weight tile: repeated launches give identical bits, and the
+    result equals the same product with one row at a time (each row is its own token tile either way)."""
+    from ai_b200 import wcomp, prefill
+    gen = torch.Generator(device="cuda").manual_seed(5)
+    N, K, M = 4096, 12288, 8
+    c = wcomp.compress((torch.randn(N, K, generator=gen, device="cuda") * 0.02).bfloat16())
+    X = torch.randn(M, K, generator=gen, device="cuda")
+    outs = []
+    for _ in range(3):
+        Y = torch.zeros(M, N, device="cuda")
+        prefill.matrix(X, c, Y, precision=3)
+        outs.append(Y)
+    torch.cuda.synchronize()
+    assert all(torch.equal(outs[0], o) for o in outs[1:])
+    assert status_clear() == 0
 
 
 @pytest.mark.parametrize("precision", [3, 1])
