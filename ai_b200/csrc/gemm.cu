@@ -386,6 +386,7 @@ __global__ void __launch_bounds__(256) prep_kernel(const float* __restrict__ x, 
   if (lnw) {
     __shared__ float red[8];
     float ss = 0.0f;
+#pragma unroll 8  // eight loads in flight per thread (a row is 16-48 KB: one round trip per eight)
     for (int k = threadIdx.x; k < K; k += 256) ss += xr[k] * xr[k];
     ss = warp_sum(ss);
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
@@ -397,6 +398,7 @@ __global__ void __launch_bounds__(256) prep_kernel(const float* __restrict__ x, 
   }
   const size_t plane = static_cast<size_t>(M) * K;
   uint16_t* o = xp + static_cast<size_t>(m) * K;
+#pragma unroll 8
   for (int k = threadIdx.x; k < K; k += 256) {
     float v = xr[k];
     if (xmode == 2) {
