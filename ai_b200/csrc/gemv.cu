@@ -430,9 +430,11 @@ struct ExcTab {  // the CTA's exceptions: CSR slice in shared memory (columns + 
 // its slot's previous stage has been consumed; a slot's full barrier completes on that one arrival plus the
 // copied bytes. Stages below `first` were issued before the CTA's prologue. A wait that runs out raises the
 // abort flag and, before returning, waits (bounded) for the copies still in flight.
+// i0: stages this ring streamed before (earlier phases of a multi-matrix launch); slots and phases follow the
+// launch-wide stage index i0 + i.
 AIB_DEV void issue_stages(const CUtensorMap* tm8, const CUtensorMap* tme4, uint8_t* ring, uint64_t* full,
                           uint64_t* empty, volatile int* abort_flag, int tb, int ks0, int n_st, int first, int R,
-                          int CW, int KS, int NS, uint32_t stage_bytes) {
+                          int CW, int KS, int NS, uint32_t stage_bytes, int i0 = 0) {
   if (g_aib_withhold_copies) return;
   const uint32_t m8_bytes = static_cast<uint32_t>(R * CW * 256);
   const uint64_t pol = l2_evict_first();
@@ -440,9 +442,9 @@ AIB_DEV void issue_stages(const CUtensorMap* tm8, const CUtensorMap* tme4, uint8
   tile += ks / KS;
   ks %= KS;
   for (int i = first; i < n_st; ++i) {
-    const int s = i % NS;
-    if (i >= NS) {
-      const uint32_t par = ((i / NS) - 1) & 1;
+    const int gi = i0 + i, s = gi % NS;
+    if (gi >= NS) {
+      const uint32_t par = ((gi / NS) - 1) & 1;
       bool ok = mbar_try_wait(&empty[s], par);
       for (uint32_t k = 0, lim = ok ? 0u : spin_limit(); k < lim && !ok; ++k) {
         ok = mbar_try_wait(&empty[s], par);
@@ -451,7 +453,7 @@ AIB_DEV void issue_stages(const CUtensorMap* tm8, const CUtensorMap* tme4, uint8
       if (!ok) {
         if (!*abort_flag) set_status(AIB_DEV_TIMEOUT_EMPTY);
         *abort_flag = 1;
-        for (int k = i - NS; k < i; ++k) mbar_wait(&full[k % NS], (k / NS) & 1, AIB_DEV_TIMEOUT_FULL);
+        for (int k = gi - NS; k < gi; ++k) mbar_wait(&full[k % NS], (k / NS) & 1, AIB_DEV_TIMEOUT_FULL);
         return;
       }
     }
@@ -609,11 +611,13 @@ AIB_DEV bool stage_csr_warp(int* rps, int* ecs, float* evs, int ecap, int nrows,
 // stage (as the first segment of its range), adds the parts in part order after its other segments -- by then
 // the lower-numbered CTAs, which hold the tile's head in the last segments of their ranges, are finishing too --
 // resets the flags for the next launch and writes y. A CTA only ever waits for lower-numbered CTAs.
+// j: segment ends finished before (earlier phases; updated), xpar: this phase's xready parity. False when the
+// phase was abandoned (a wait ran out or another role aborted).
 template <int MODE>
-AIB_DEV void finish_segments(const float* pbuf, int pstride, uint64_t* ready, uint64_t* free_, uint64_t* xready,
+AIB_DEV bool finish_segments(const float* pbuf, int pstride, uint64_t* ready, uint64_t* free_, uint64_t* xready,
                              volatile int* abort_flag, const ExcTab& et, TcXval xval, float* y, int N, int tb, int ks0,
                              int n_st, int R, int CW, int KS, int nrows, int pw, float* wsp, int* wsc, int maxp,
-                             int tiles) {
+                             int tiles, int& j, uint32_t xpar = 0) {
   const int lane = threadIdx.x & 31;
   pdl_wait();  // y is read (modes 1, 2) and written after the previous kernel's
   // bounded wait on a barrier that lane 0 polls; false (abort raised) when it runs out or another role aborted
@@ -633,11 +637,11 @@ AIB_DEV void finish_segments(const float* pbuf, int pstride, uint64_t* ready, ui
     }
     return __shfl_sync(0xffffffffu, ok, 0) != 0;
   };
-  if (!wait_bar(xready, 0)) return;
+  if (!wait_bar(xready, xpar)) return false;
   const long long nall = static_cast<long long>(tiles) * KS, G = gridDim.x;
   int def_tile = -1, def_np = 0;  // the split tile this CTA finalizes (at most one: its first segment)
   float def_v = 0.0f;
-  int ks = ks0, tile = tb, j = 0;
+  int ks = ks0, tile = tb;
   for (int i = 0; i < n_st;) {
     const int len = min(KS - ks, n_st - i), fks = ks + len - 1;
     const bool whole = ks == 0 && fks == KS - 1;
@@ -647,7 +651,7 @@ AIB_DEV void finish_segments(const float* pbuf, int pstride, uint64_t* ready, ui
     if (whole && has_row) corr = row_correction(et, xval, lr, row, 0, KS * CW * 256);
     const bool use_yold = (MODE == 1 || MODE == 2) && whole;
     const float yold = use_yold && lane < R && row < N ? y[row] : 0.0f;
-    if (!wait_bar(&ready[b], (j >> 1) & 1)) return;
+    if (!wait_bar(&ready[b], (j >> 1) & 1)) return false;
     float v = 0.0f;
     if (lane < R) {
       const float* pp = pbuf + b * pstride + lane * pw;
@@ -696,7 +700,7 @@ AIB_DEV void finish_segments(const float* pbuf, int pstride, uint64_t* ready, ui
         if (!*abort_flag) set_status(AIB_DEV_TIMEOUT_FULL);
         *abort_flag = 1;
       }
-      return;
+      return false;
     }
     const float* parts = wsp + static_cast<size_t>(def_tile) * maxp * R;
     float t = 0.0f;
@@ -709,6 +713,7 @@ AIB_DEV void finish_segments(const float* pbuf, int pstride, uint64_t* ready, ui
     for (int pi = lane; pi + 1 < def_np; pi += 32) wsc[static_cast<size_t>(def_tile) * maxp + pi] = 0;  // next launch
     store_rows<MODE>(t, 0.0f, false, def_tile * R + lane, R, N, y);
   }
+  return true;
 }
 
 // --------------------------------------------------------------------- T = 1 wide-stage kernel
@@ -783,87 +788,22 @@ constexpr int kTcPrologueRecords = 8;  // x records per consumer thread per prol
 // SPL = 2 splits each (row group, chunk slot, half) unit's eight MMA steps between two warps (four each), so 16
 // consumer warps share a 24 KB stage and two 544-thread CTAs fit an SM: 32 consumer warps per SM to hide the
 // decode's dependency chains.
-template <int MODE, bool RMS, int NCW, int SPL = 1>
-__global__ void __launch_bounds__(NCW * 32 + 64, (NCW == 16 && SPL == 1) ? 1 : 2)
-    gemv_tc_kernel(const __grid_constant__ CUtensorMap tm8, const __grid_constant__ CUtensorMap tme4, RowsParams p) {
+// Consumer warps of the tensor-core wide-stage kernel for one matrix pass ("phase"): the x prologue (three-part
+// B records of xin(x), the RMSNorm folded in; after the grid-dependency wait when wait_pdl), then the stages of
+// the CTA's share `sh`. The ring position (s, ph), the segment-end count jc and the abort state carry over from one
+// phase to the next when several matrices stream through one ring.
+template <int MODE, bool RMS, int NCW, int SPL>
+AIB_DEV void tc_consume(const RowsParams& p, const WideShare& sh_, uint8_t* xr, float* rms_red, uint8_t* ring,
+                        uint64_t* full, uint64_t* empty, float* pbuf, uint64_t* pready, uint64_t* pfree,
+                        uint64_t* xready, volatile int* abort_flag, bool wait_pdl, int& s, int& ph, int& jc,
+                        bool& aborted) {
   constexpr int kTcConsumers = NCW * 32;
-  constexpr int kTcThreads = kTcConsumers + 64;  // + producer warp + finisher warp
-  constexpr int kStage = NCW * 2048 * 3 / 2 / SPL;  // bytes per ring slot: 2048 / SPL weights per consumer warp
-  extern __shared__ __align__(1024) uint8_t smem[];
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
-  uint64_t* empty = full + 16;
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + 256);
-  uint64_t* pready = reinterpret_cast<uint64_t*>(smem + 384);  // partial buffers: consumers -> finisher
-  uint64_t* pfree = pready + 2;                                // finisher -> consumers
-  uint64_t* xready = pready + 4;                               // consumers -> finisher: x records built
-  float* rms_red = reinterpret_cast<float*>(smem + 512);
-  float* pbuf = reinterpret_cast<float*>(smem + 1024);  // two partial buffers, float [R][PW] each (<= 1 KB)
-  uint8_t* xr = smem + p.xs_off;
-  int* rps = reinterpret_cast<int*>(smem + p.rps_off);
-  int* ecs = reinterpret_cast<int*>(smem + p.ecs_off);
-  uint8_t* ring = smem + p.ring_off;
-
+  constexpr int kStage = NCW * 2048 * 3 / 2 / SPL;
   const int tid = threadIdx.x, lane = tid & 31;
-  const WideShare sh_ = wide_share(p);
-  const int tb = sh_.tb, ks0 = sh_.ks0;
+  const int tb = sh_.tb, ks0 = sh_.ks0, n_st = sh_.n_st;
   const int R = p.R, CW = p.CW, KS = p.KS, NS = p.NS;
-  const int PW = 2 * CW * SPL;  // partials per row (warps per row group)
-  const int n_st = sh_.n_st;
-  const int row0 = sh_.row0;
-  const int nrows = sh_.nrows;
-  // The producer thread initialises the barriers and issues the ring's first stages, so the weights start
-  // streaming at once (they do not depend on the previous kernel).
-  const int first = AIB_GEMV_EARLY ? min(NS, n_st) : 0;
-  if (tid == kTcConsumers) {
-    for (int s = 0; s < NS; ++s) {
-      mbar_init(&full[s], 1);  // the TMA arrival (with the stage's bytes)
-      mbar_init(&empty[s], kTcConsumers / 32);
-    }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&pready[b], kTcConsumers / 32);
-      mbar_init(&pfree[b], 1);
-    }
-    mbar_init(xready, 1);
-    *abort_flag = 0;
-    fence_mbar_init();
-    if (!g_aib_withhold_copies) {
-      prefetch_tensormap(&tm8);
-      prefetch_tensormap(&tme4);
-      const uint32_t m8_bytes = static_cast<uint32_t>(R * CW * 256);
-      const uint64_t pol = l2_evict_first();
-      int ks = ks0, tile = tb;
-      for (int i = 0; i < first; ++i) {
-        uint8_t* st = ring + static_cast<size_t>(i) * kStage;
-        mbar_arrive_expect_tx(&full[i], kStage);
-        if (AIB_GEMV_EVICT_FIRST) {
-          tma_load_3d_hint(st, &tm8, &full[i], 0, ks * CW, tile * R, pol);
-          tma_load_3d_hint(st + m8_bytes, &tme4, &full[i], 0, ks * CW, tile * R, pol);
-        } else {
-          tma_load_3d(st, &tm8, &full[i], 0, ks * CW, tile * R);
-          tma_load_3d(st + m8_bytes, &tme4, &full[i], 0, ks * CW, tile * R);
-        }
-        if (++ks == KS) ks = 0, ++tile;
-      }
-    }
-  }
-  __syncthreads();
-  pdl_trigger();
-
-  if (tid >= kTcConsumers + 32) {  // ---------------- finisher warp: the CSR slice, then the segments
-    float* evs = reinterpret_cast<float*>(ecs + p.ecap);
-    const bool staged = stage_csr_warp(rps, ecs, evs, p.ecap, nrows, row0, p.rp, p.ec, p.ev, p.m8, p.K, p.base);
-    const ExcTab et{rps, ecs, evs, staged, rps[0], row0, p.ec, p.ev, p.m8, p.K, p.base};
-    finish_segments<MODE>(pbuf, 256, pready, pfree, xready, abort_flag, et, TcXval{xr, p.nch}, p.y, p.N, tb, ks0, n_st,
-                          R, CW, KS, nrows, PW, p.wsp, p.wsc, p.maxp, p.tiles);
-    return;
-  }
-  if (tid >= kTcConsumers) {  // ---------------- producer warp: one thread streams the stages
-    if (tid == kTcConsumers)
-      issue_stages(&tm8, &tme4, ring, full, empty, abort_flag, tb, ks0, n_st, first, R, CW, KS, NS, kStage);
-    return;
-  }
-
-  // ---------------- consumers: x prologue into the three-part B records
+  const int PW = 2 * CW * SPL;
+  // x prologue into the three-part B records
   // Record pr holds columns (c, c+1) and (128+c, 129+c) of chunk gc = pr / 64 (c = 2 * (pr % 64)). Consumer
   // thread tid owns records tid + 512 j. All of a batch's loads are issued before any is used (one memory
   // round trip per batch; one batch up to K = 16384), the RMS sum reuses the loaded values, and the norm
@@ -880,7 +820,7 @@ __global__ void __launch_bounds__(NCW * 32 + 64, (NCW == 16 && SPL == 1) ? 1 : 2
       lwb[j] = pr < npr ? *reinterpret_cast<const uint32_t*>(p.lnw + k0 + 128) : 0u;
     }
   }
-  pdl_wait();
+  if (wait_pdl) pdl_wait();
   float rs = 1.0f;
   if (RMS && npr > kBatch) {  // several batches: the sum of squares first
     const float4* xg = reinterpret_cast<const float4*>(p.x);
@@ -989,12 +929,11 @@ __global__ void __launch_bounds__(NCW * 32 + 64, (NCW == 16 && SPL == 1) ? 1 : 2
   const uint32_t base7 = (static_cast<uint32_t>(p.base) << 7) | (static_cast<uint32_t>(p.base) << 23);
   const uint32_t k128 = p.k128, k8 = p.k8;
 
-  bool aborted = false;
   constexpr int NACC = AIB_GEMV_ACC;  // independent accumulator chains (MMA i feeds chain i % NACC)
   float acc[NACC][4];
 #pragma unroll
   for (int a = 0; a < NACC; ++a) acc[a][0] = acc[a][1] = acc[a][2] = acc[a][3] = 0.0f;
-  int s = 0, ph = 0, ks = ks0, tile = tb, jc = 0;  // jc: segment ends passed
+  int ks = ks0, tile = tb;
   for (int it = 0; it < n_st; ++it) {
     // warp-uniform: the MMAs below must run with all 32 lanes converged
     const bool ok = __all_sync(0xffffffffu, !aborted && wait_full(&full[s], ph, abort_flag));
@@ -1109,6 +1048,93 @@ __global__ void __launch_bounds__(NCW * 32 + 64, (NCW == 16 && SPL == 1) ? 1 : 2
     if (++ks == KS) ks = 0, ++tile;
     if (++s == NS) s = 0, ph ^= 1;
   }
+}
+
+template <int MODE, bool RMS, int NCW, int SPL = 1>
+__global__ void __launch_bounds__(NCW * 32 + 64, (NCW == 16 && SPL == 1) ? 1 : 2)
+    gemv_tc_kernel(const __grid_constant__ CUtensorMap tm8, const __grid_constant__ CUtensorMap tme4, RowsParams p) {
+  constexpr int kTcConsumers = NCW * 32;
+  constexpr int kTcThreads = kTcConsumers + 64;  // + producer warp + finisher warp
+  constexpr int kStage = NCW * 2048 * 3 / 2 / SPL;  // bytes per ring slot: 2048 / SPL weights per consumer warp
+  extern __shared__ __align__(1024) uint8_t smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* empty = full + 16;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + 256);
+  uint64_t* pready = reinterpret_cast<uint64_t*>(smem + 384);  // partial buffers: consumers -> finisher
+  uint64_t* pfree = pready + 2;                                // finisher -> consumers
+  uint64_t* xready = pready + 4;                               // consumers -> finisher: x records built
+  float* rms_red = reinterpret_cast<float*>(smem + 512);
+  float* pbuf = reinterpret_cast<float*>(smem + 1024);  // two partial buffers, float [R][PW] each (<= 1 KB)
+  uint8_t* xr = smem + p.xs_off;
+  int* rps = reinterpret_cast<int*>(smem + p.rps_off);
+  int* ecs = reinterpret_cast<int*>(smem + p.ecs_off);
+  uint8_t* ring = smem + p.ring_off;
+
+  const int tid = threadIdx.x, lane = tid & 31;
+  const WideShare sh_ = wide_share(p);
+  const int tb = sh_.tb, ks0 = sh_.ks0;
+  const int R = p.R, CW = p.CW, KS = p.KS, NS = p.NS;
+  const int PW = 2 * CW * SPL;  // partials per row (warps per row group)
+  const int n_st = sh_.n_st;
+  const int row0 = sh_.row0;
+  const int nrows = sh_.nrows;
+  // The producer thread initialises the barriers and issues the ring's first stages, so the weights start
+  // streaming at once (they do not depend on the previous kernel).
+  const int first = AIB_GEMV_EARLY ? min(NS, n_st) : 0;
+  if (tid == kTcConsumers) {
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&full[s], 1);  // the TMA arrival (with the stage's bytes)
+      mbar_init(&empty[s], kTcConsumers / 32);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&pready[b], kTcConsumers / 32);
+      mbar_init(&pfree[b], 1);
+    }
+    mbar_init(xready, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    if (!g_aib_withhold_copies) {
+      prefetch_tensormap(&tm8);
+      prefetch_tensormap(&tme4);
+      const uint32_t m8_bytes = static_cast<uint32_t>(R * CW * 256);
+      const uint64_t pol = l2_evict_first();
+      int ks = ks0, tile = tb;
+      for (int i = 0; i < first; ++i) {
+        uint8_t* st = ring + static_cast<size_t>(i) * kStage;
+        mbar_arrive_expect_tx(&full[i], kStage);
+        if (AIB_GEMV_EVICT_FIRST) {
+          tma_load_3d_hint(st, &tm8, &full[i], 0, ks * CW, tile * R, pol);
+          tma_load_3d_hint(st + m8_bytes, &tme4, &full[i], 0, ks * CW, tile * R, pol);
+        } else {
+          tma_load_3d(st, &tm8, &full[i], 0, ks * CW, tile * R);
+          tma_load_3d(st + m8_bytes, &tme4, &full[i], 0, ks * CW, tile * R);
+        }
+        if (++ks == KS) ks = 0, ++tile;
+      }
+    }
+  }
+  __syncthreads();
+  pdl_trigger();
+
+  if (tid >= kTcConsumers + 32) {  // ---------------- finisher warp: the CSR slice, then the segments
+    float* evs = reinterpret_cast<float*>(ecs + p.ecap);
+    const bool staged = stage_csr_warp(rps, ecs, evs, p.ecap, nrows, row0, p.rp, p.ec, p.ev, p.m8, p.K, p.base);
+    const ExcTab et{rps, ecs, evs, staged, rps[0], row0, p.ec, p.ev, p.m8, p.K, p.base};
+    int j = 0;
+    finish_segments<MODE>(pbuf, 256, pready, pfree, xready, abort_flag, et, TcXval{xr, p.nch}, p.y, p.N, tb, ks0, n_st,
+                          R, CW, KS, nrows, PW, p.wsp, p.wsc, p.maxp, p.tiles, j);
+    return;
+  }
+  if (tid >= kTcConsumers) {  // ---------------- producer warp: one thread streams the stages
+    if (tid == kTcConsumers)
+      issue_stages(&tm8, &tme4, ring, full, empty, abort_flag, tb, ks0, n_st, first, R, CW, KS, NS, kStage);
+    return;
+  }
+
+  int s_ = 0, ph_ = 0, jc_ = 0;
+  bool aborted_ = false;
+  tc_consume<MODE, RMS, NCW, SPL>(p, sh_, xr, rms_red, ring, full, empty, pbuf, pready, pfree, xready, abort_flag, true,
+                                  s_, ph_, jc_, aborted_);
 }
 
 // ------------------------------------------------------------------------------- batched kernel
