@@ -181,6 +181,18 @@ AIB_DEV uint16_t f32_to_bf16_rne(float f) {
   u += 0x7FFFu + ((u >> 16) & 1u);
   return static_cast<uint16_t>(u >> 16);
 }
+// The same rounding as one conversion instruction (cvt.rn, subnormals kept; a NaN becomes the hardware's
+// canonical NaN): two floats packed as bf16x2 (lo in bits 0-15), or one.
+AIB_DEV uint32_t bf16x2_rn(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+AIB_DEV uint16_t bf16_rn(float f) {
+  uint16_t r;
+  asm("cvt.rn.bf16.f32 %0, %1;" : "=h"(r) : "f"(f));
+  return r;
+}
 
 AIB_DEV float warp_sum(float v) {
 #pragma unroll

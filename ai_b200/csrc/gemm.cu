@@ -407,7 +407,7 @@ __global__ void __launch_bounds__(256) prep_kernel(const float* __restrict__ x, 
     }
     if (lnw) v = bf16_to_f32(lnw[k]) * (v * rs);
     for (int q = 0; q < parts; ++q) {
-      const uint16_t b = f32_to_bf16_rne(v);
+      const uint16_t b = bf16_rn(v);
       o[q * plane + k] = b;
       v -= bf16_to_f32(b);
     }

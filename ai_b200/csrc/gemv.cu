@@ -430,12 +430,18 @@ struct ExcTab {  // the CTA's exceptions: CSR slice in shared memory (columns + 
 // its slot's previous stage has been consumed; a slot's full barrier completes on that one arrival plus the
 // copied bytes. Stages below `first` were issued before the CTA's prologue. A wait that runs out raises the
 // abort flag and, before returning, waits (bounded) for the copies still in flight.
-// i0: stages this ring streamed before (earlier phases of a multi-matrix launch); slots and phases follow the
-// launch-wide stage index i0 + i.
-AIB_DEV void issue_stages(const CUtensorMap* tm8, const CUtensorMap* tme4, uint8_t* ring, uint64_t* full,
+// Bounded wait until the copies into the last min(NS, n) issued stages (launch-wide indices < n) have landed, so
+// no copy is in flight into shared memory when the CTA exits after an abort.
+AIB_DEV void drain_ring(uint64_t* full, int n, int NS) {
+  for (int k = max(0, n - NS); k < n; ++k) mbar_wait(&full[k % NS], (k / NS) & 1, AIB_DEV_TIMEOUT_FULL);
+}
+
+// i0: stages this ring streamed before (slots and phases follow the stage index i0 + i). Stops issuing when any
+// role has raised the abort flag, and then waits for the copies in flight. False when aborted.
+AIB_DEV bool issue_stages(const CUtensorMap* tm8, const CUtensorMap* tme4, uint8_t* ring, uint64_t* full,
                           uint64_t* empty, volatile int* abort_flag, int tb, int ks0, int n_st, int first, int R,
                           int CW, int KS, int NS, uint32_t stage_bytes, int i0 = 0) {
-  if (g_aib_withhold_copies) return;
+  if (g_aib_withhold_copies) return true;
   const uint32_t m8_bytes = static_cast<uint32_t>(R * CW * 256);
   const uint64_t pol = l2_evict_first();
   int ks = ks0 + first, tile = tb;
@@ -443,19 +449,23 @@ AIB_DEV void issue_stages(const CUtensorMap* tm8, const CUtensorMap* tme4, uint8
   ks %= KS;
   for (int i = first; i < n_st; ++i) {
     const int gi = i0 + i, s = gi % NS;
+    bool ok = true;
     if (gi >= NS) {
       const uint32_t par = ((gi / NS) - 1) & 1;
-      bool ok = mbar_try_wait(&empty[s], par);
+      ok = mbar_try_wait(&empty[s], par);
       for (uint32_t k = 0, lim = ok ? 0u : spin_limit(); k < lim && !ok; ++k) {
         ok = mbar_try_wait(&empty[s], par);
         if (!ok && (k & 63) == 63 && *abort_flag) break;
       }
-      if (!ok) {
-        if (!*abort_flag) set_status(AIB_DEV_TIMEOUT_EMPTY);
-        *abort_flag = 1;
-        for (int k = gi - NS; k < gi; ++k) mbar_wait(&full[k % NS], (k / NS) & 1, AIB_DEV_TIMEOUT_FULL);
-        return;
-      }
+      if (!ok && !*abort_flag) set_status(AIB_DEV_TIMEOUT_EMPTY);
+    }
+    // checked after the wait: aborted consumers release slots without waiting for their copies, so a slot freed
+    // after an abort may still be filling and must not be reused
+    if (ok && *abort_flag) ok = false;
+    if (!ok) {
+      *abort_flag = 1;
+      drain_ring(full, gi, NS);
+      return false;
     }
     uint8_t* st = ring + static_cast<size_t>(s) * stage_bytes;
     mbar_arrive_expect_tx(&full[s], stage_bytes);
@@ -468,6 +478,7 @@ AIB_DEV void issue_stages(const CUtensorMap* tm8, const CUtensorMap* tme4, uint8
     }
     if (++ks == KS) ks = 0, ++tile;
   }
+  return true;
 }
 
 // Byte offset of the x record (8 bytes: low pair, high pair) for chunk gc, MMA i, lane quad t, column block
@@ -754,7 +765,7 @@ AIB_DEV WideShare wide_share(const RowsParams& p) {
     w.ks0 = static_cast<int>(g0 % p.KS);
     const int tl = w.n_st > 0 ? static_cast<int>((g1 - 1) / p.KS) : w.tb;
     w.row0 = w.tb * p.R;
-    w.nrows = min((tl - w.tb + 1) * p.R, p.N - w.row0);
+    w.nrows = max(0, min((tl - w.tb + 1) * p.R, p.N - w.row0));
   } else {
     const int tb = static_cast<int>(b * p.tiles / G), te = static_cast<int>((b + 1) * p.tiles / G);
     w.g0 = tb * p.KS;
@@ -762,7 +773,7 @@ AIB_DEV WideShare wide_share(const RowsParams& p) {
     w.tb = tb;
     w.ks0 = 0;
     w.row0 = tb * p.R;
-    w.nrows = min((te - tb) * p.R, p.N - w.row0);
+    w.nrows = max(0, min((te - tb) * p.R, p.N - w.row0));
   }
   return w;
 }
@@ -894,17 +905,15 @@ AIB_DEV void tc_consume(const RowsParams& p, const WideShare& sh_, uint8_t* xr, 
         v[2] = __uint_as_float(wb << 16) * (v[2] * rs);
         v[3] = __uint_as_float(wb & 0xFFFF0000u) * (v[3] * rs);
       }
-      uint32_t w[3][2];
+      uint32_t w[3][2];  // parts: one conversion instruction per pair (this loop bounds the prologue)
 #pragma unroll
       for (int sp = 0; sp < 3; ++sp) {
-        uint16_t bq[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          bq[e] = f32_to_bf16_rne(v[e]);
-          v[e] -= bf16_to_f32(bq[e]);
-        }
-        w[sp][0] = static_cast<uint32_t>(bq[0]) | (static_cast<uint32_t>(bq[1]) << 16);
-        w[sp][1] = static_cast<uint32_t>(bq[2]) | (static_cast<uint32_t>(bq[3]) << 16);
+        w[sp][0] = bf16x2_rn(v[0], v[1]);
+        w[sp][1] = bf16x2_rn(v[2], v[3]);
+        v[0] -= __uint_as_float(w[sp][0] << 16);
+        v[1] -= __uint_as_float(w[sp][0] & 0xFFFF0000u);
+        v[2] -= __uint_as_float(w[sp][1] << 16);
+        v[3] -= __uint_as_float(w[sp][1] & 0xFFFF0000u);
       }
       const int blk = c >> 6, t = (c >> 4) & 3, i = (c & 15) >> 1;
 #pragma unroll
@@ -1126,8 +1135,12 @@ __global__ void __launch_bounds__(NCW * 32 + 64, (NCW == 16 && SPL == 1) ? 1 : 2
     return;
   }
   if (tid >= kTcConsumers) {  // ---------------- producer warp: one thread streams the stages
-    if (tid == kTcConsumers)
-      issue_stages(&tm8, &tme4, ring, full, empty, abort_flag, tb, ks0, n_st, first, R, CW, KS, NS, kStage);
+    // after the last copy, wait for the ring's copies to land: the CTA must not exit with copies in flight if
+    // another role aborts and the consumers stop waiting for the stages
+    if (tid == kTcConsumers &&
+        issue_stages(&tm8, &tme4, ring, full, empty, abort_flag, tb, ks0, n_st, first, R, CW, KS, NS, kStage) &&
+        !g_aib_withhold_copies)
+      drain_ring(full, n_st, NS);
     return;
   }
 
