@@ -488,6 +488,13 @@ AIB_DEV int tc_xrec(int nch, int gc, int i, int blk, int t, int sp) {
   const int gi = gc * 8 + i;
   return sp < 2 ? gi * 128 + (blk * 2 + sp) * 32 + t * 8 : nch * 1024 + gi * 64 + blk * 32 + t * 8;
 }
+// Column (chunk * 256 + c, c < 128; the record also holds c + 1, 128 + c, 129 + c) of prologue record pr. Within a
+// chunk's 64 records the order is (i, blk, t) from slow to fast, so the 16 lanes of a half-warp building
+// consecutive records store to 16 distinct 8-byte slots of the record lines (no shared-memory bank conflicts).
+AIB_DEV int tc_rec_col(int pr) {
+  const int l6 = pr & 63;
+  return (pr >> 6) * 256 + ((l6 >> 2) & 1) * 64 + (l6 & 3) * 16 + (l6 >> 3) * 2;
+}
 // Exact value of x[col] from its three bf16 parts in the records.
 AIB_DEV float tc_xval(const uint8_t* xr, int nch, int col) {
   const int gc = col >> 8, cc = col & 255, hf = cc >> 7, c = cc & 127;
@@ -791,7 +798,11 @@ AIB_DEV WideShare wide_share(const RowsParams& p) {
 // 128 + 2i, 129 + 2i of that range. Even and odd rows of the warp use different column blocks, which keeps
 // the 16-byte shared loads of a quarter-warp on distinct banks; B column n = 2*sp + par carries x part sp in
 // the column order of parity par, and a row reads its result from the columns of its own parity.
-constexpr int kTcPrologueRecords = 8;  // x records per consumer thread per prologue batch (K <= 16384: one batch)
+#ifndef AIB_REC_UNROLL
+#define AIB_REC_UNROLL 8
+#endif
+constexpr int kTcPrologueRecords = 8;
+constexpr int kRecUnroll = AIB_REC_UNROLL;  // x records per consumer thread per prologue batch (K <= 16384: one batch)
 
 // NCW consumer warps: 16 with 48 KB stages (R * CW = 128, one CTA per SM), or 8 with 24 KB stages (R * CW = 64,
 // <= 113 KB of shared memory and 288 threads, so two CTAs share an SM: two of the same launch, or the tail of one
@@ -815,7 +826,7 @@ AIB_DEV void tc_consume(const RowsParams& p, const WideShare& sh_, uint8_t* xr, 
   const int R = p.R, CW = p.CW, KS = p.KS, NS = p.NS;
   const int PW = 2 * CW * SPL;
   // x prologue into the three-part B records
-  // Record pr holds columns (c, c+1) and (128+c, 129+c) of chunk gc = pr / 64 (c = 2 * (pr % 64)). Consumer
+  // Record pr holds columns (c, c+1) and (128+c, 129+c) of chunk gc = pr / 64 (c from tc_rec_col). Consumer
   // thread tid owns records tid + 512 j. All of a batch's loads are issued before any is used (one memory
   // round trip per batch; one batch up to K = 16384), the RMS sum reuses the loaded values, and the norm
   // weights -- constant inputs -- are read before the grid dependency resolves.
@@ -826,7 +837,7 @@ AIB_DEV void tc_consume(const RowsParams& p, const WideShare& sh_, uint8_t* xr, 
 #pragma unroll
     for (int j = 0; j < kTcPrologueRecords; ++j) {
       const int pr = tid + j * kTcConsumers;
-      const int k0 = (pr >> 6) * 256 + (pr & 63) * 2;
+      const int k0 = tc_rec_col(pr);
       lwa[j] = pr < npr ? *reinterpret_cast<const uint32_t*>(p.lnw + k0) : 0u;
       lwb[j] = pr < npr ? *reinterpret_cast<const uint32_t*>(p.lnw + k0 + 128) : 0u;
     }
@@ -853,7 +864,7 @@ AIB_DEV void tc_consume(const RowsParams& p, const WideShare& sh_, uint8_t* xr, 
 #pragma unroll
     for (int j = 0; j < kTcPrologueRecords; ++j) {
       const int pr = b0 + tid + j * kTcConsumers;
-      const int k0 = (pr >> 6) * 256 + (pr & 63) * 2;
+      const int k0 = tc_rec_col(pr);
       float2 lo = make_float2(0.0f, 0.0f), hi = lo;
       if (pr < npr) {
         lo = *reinterpret_cast<const float2*>(p.x + k0);
@@ -865,7 +876,7 @@ AIB_DEV void tc_consume(const RowsParams& p, const WideShare& sh_, uint8_t* xr, 
 #pragma unroll
       for (int j = 0; j < kTcPrologueRecords; ++j) {
         const int pr = b0 + tid + j * kTcConsumers;
-        const int k0 = (pr >> 6) * 256 + (pr & 63) * 2;
+        const int k0 = tc_rec_col(pr);
         if (pr < npr) {
           const float2 lo = *reinterpret_cast<const float2*>(p.x + K + k0);
           const float2 hi = *reinterpret_cast<const float2*>(p.x + K + k0 + 128);
@@ -887,11 +898,11 @@ AIB_DEV void tc_consume(const RowsParams& p, const WideShare& sh_, uint8_t* xr, 
       for (int w = 0; w < kTcConsumers / 32; ++w) tot += rms_red[w];
       rs = rsqrtf(tot / static_cast<float>(K) + p.eps);
     }
-#pragma unroll
+#pragma unroll kRecUnroll
     for (int j = 0; j < kTcPrologueRecords; ++j) {
       const int pr = b0 + tid + j * kTcConsumers;
       if (pr >= npr) continue;
-      const int gc = pr >> 6, c = (pr & 63) * 2;
+      const int gc = pr >> 6, c = tc_rec_col(pr) & 255;
       float v[4] = {xv[j].x, xv[j].y, xv[j].z, xv[j].w};
       if (RMS) {
         uint32_t wa = lwa[j], wb = lwb[j];
@@ -916,9 +927,13 @@ AIB_DEV void tc_consume(const RowsParams& p, const WideShare& sh_, uint8_t* xr, 
         v[3] -= __uint_as_float(w[sp][1] & 0xFFFF0000u);
       }
       const int blk = c >> 6, t = (c >> 4) & 3, i = (c & 15) >> 1;
-#pragma unroll
-      for (int sp = 0; sp < 3; ++sp)
-        *reinterpret_cast<uint2*>(xr + tc_xrec(p.nch, gc, i, blk, t, sp)) = make_uint2(w[sp][0], w[sp][1]);
+      // parts 0 and 1 share a 128-byte line per (chunk, i): lanes of odd i store part 1 first, so each store
+      // instruction of a half-warp covers 16 distinct bank pairs
+      const int o0 = tc_xrec(p.nch, gc, i, blk, t, 0), sw = i & 1;
+      *reinterpret_cast<uint2*>(xr + o0 + sw * 32) = sw ? make_uint2(w[1][0], w[1][1]) : make_uint2(w[0][0], w[0][1]);
+      *reinterpret_cast<uint2*>(xr + o0 + (sw ^ 1) * 32) =
+          sw ? make_uint2(w[0][0], w[0][1]) : make_uint2(w[1][0], w[1][1]);
+      *reinterpret_cast<uint2*>(xr + tc_xrec(p.nch, gc, i, blk, t, 2)) = make_uint2(w[2][0], w[2][1]);
     }
   }
   named_sync(1, kTcConsumers);
