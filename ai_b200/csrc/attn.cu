@@ -133,6 +133,8 @@ struct Smem {
   float pw[kWarps][GMAX][kBlk];  // each warp's block probabilities
   float mw[kMaxSplits][GMAX];    // merge weights exp(m_s - M) per split
   float mM[GMAX], mL[GMAX], mc[GMAX], ones[GMAX];
+  float cwt[kWarps][GMAX];  // the warps' weights exp(m_w - M) in the CTA's combine
+  float cM[GMAX];
   long long pos_spec;  // pos as read before the grid dependency resolved (one read for the whole CTA)
   int last;
 };
@@ -174,19 +176,13 @@ AIB_DEV void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, 
                : "r"(addr));
 }
 // x = p0 + p1 + p2 in bf16 parts (round to nearest even at each step): fp32-faithful products on bf16 MMAs
-AIB_DEV void split3(float x, uint16_t* p) {
-  p[0] = f32_to_bf16_rne(x);
-  x -= bf16_to_f32(p[0]);
-  p[1] = f32_to_bf16_rne(x);
-  x -= bf16_to_f32(p[1]);
-  p[2] = f32_to_bf16_rne(x);
-}
 AIB_DEV void split3_pair(float lo, float hi, uint32_t* w) {  // w[part] = (hi part << 16) | lo part
-  uint16_t a[3], b[3];
-  split3(lo, a);
-  split3(hi, b);
 #pragma unroll
-  for (int k = 0; k < 3; ++k) w[k] = static_cast<uint32_t>(a[k]) | (static_cast<uint32_t>(b[k]) << 16);
+  for (int k = 0; k < 3; ++k) {  // the same roundings, one conversion instruction per pair
+    w[k] = bf16x2_rn(lo, hi);
+    lo -= __uint_as_float(w[k] << 16);
+    hi -= __uint_as_float(w[k] & 0xFFFF0000u);
+  }
 }
 
 // Attention of the G query heads in sm.q over cache rows [j0, j1) of one group, on the tensor cores. Warp w
@@ -355,25 +351,29 @@ AIB_DEV void attend_range(Smem<HD>& sm, uint8_t* ring, const uint16_t* kc, const
     }
   }
   __syncthreads();
-  // combine the warps in order
+  // combine the warps in order: the weights exp(m_w - M) once per (warp, head) (0 for a warp without
+  // positions), then fixed-order weighted sums
+  if (threadIdx.x < G * kWarps) {
+    const int h = threadIdx.x / kWarps, w = threadIdx.x % kWarps;
+    float M = -INFINITY;
+    for (int w2 = 0; w2 < kWarps; ++w2) M = fmaxf(M, wst[(w2 * GMAX + h) * (HD + 2) + HD]);
+    const float mw = wst[(w * GMAX + h) * (HD + 2) + HD];
+    sm.cwt[w][h] = (M == -INFINITY || mw == -INFINITY) ? 0.0f : expf(mw - M);
+    if (w == 0) sm.cM[h] = M;
+  }
+  __syncthreads();
   for (int idx = threadIdx.x; idx < G * HD; idx += kThreads) {
     const int h = idx / HD, d = idx % HD;
-    float M = -INFINITY;
-    for (int w = 0; w < kWarps; ++w) M = fmaxf(M, wst[(w * GMAX + h) * (HD + 2) + HD]);
-    float L = 0.0f, A = 0.0f;
-    if (M != -INFINITY) {
-      for (int w = 0; w < kWarps; ++w) {
-        const float* src = wst + (w * GMAX + h) * (HD + 2);
-        if (src[HD] == -INFINITY) continue;
-        const float f = expf(src[HD] - M);
-        L += src[HD + 1] * f;
-        A += src[d] * f;
-      }
-    }
+    float A = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) A += wst[(w * GMAX + h) * (HD + 2) + d] * sm.cwt[w][h];
     float* ph = part + static_cast<size_t>(h) * (HD + 2);
     ph[d] = A;
     if (d == 0) {
-      ph[HD] = M;
+      float L = 0.0f;
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) L += wst[(w * GMAX + h) * (HD + 2) + HD + 1] * sm.cwt[w][h];
+      ph[HD] = sm.cM[h];
       ph[HD + 1] = L;
     }
   }
