@@ -624,13 +624,14 @@ AIB_DEV bool stage_csr_warp(int* rps, int* ecs, float* evs, int ecap, int nrows,
 // stage. Two buffers: the consumers wait only when the finisher is two segments behind.
 //
 // Stream-K (a workspace: the grid splits the tiles * KS stages evenly, so a tile may be split between
-// neighbouring CTAs bf..bl): part pi of a split tile (its CTA's share, exception corrections of its columns
-// included) goes to the workspace slot [tile][pi] with a release flag; CTA bl, which holds the tile's last
-// stage (as the first segment of its range), adds the parts in part order after its other segments -- by then
-// the lower-numbered CTAs, which hold the tile's head in the last segments of their ranges, are finishing too --
-// resets the flags for the next launch and writes y. A CTA only ever waits for lower-numbered CTAs.
-// j: segment ends finished before (earlier phases; updated), xpar: this phase's xready parity. False when the
-// phase was abandoned (a wait ran out or another role aborted).
+// neighbouring CTAs bf..bl): CTA bf holds the tile's head as the last segment of its range and finishes the tile;
+// each other part (CTAs bf+1..bl: the tile is the first segment of their ranges, so they publish it early) goes,
+// exception corrections of its columns included, to the workspace slot [tile][b - bf - 1] with a release flag.
+// CTA bf reads those parts while its own last stages are still in flight (they are normally published by then),
+// adds them after its own part in CTA order (deterministic), resets the flags for the next launch and writes y.
+// A CTA only ever waits for higher-numbered CTAs, and only for work they do first.
+// j: segment ends finished before (updated), xpar: the xready parity. False when the work was abandoned (a wait
+// ran out or another role aborted).
 template <int MODE>
 AIB_DEV bool finish_segments(const float* pbuf, int pstride, uint64_t* ready, uint64_t* free_, uint64_t* xready,
                              volatile int* abort_flag, const ExcTab& et, TcXval xval, float* y, int N, int tb, int ks0,
@@ -657,79 +658,69 @@ AIB_DEV bool finish_segments(const float* pbuf, int pstride, uint64_t* ready, ui
   };
   if (!wait_bar(xready, xpar)) return false;
   const long long nall = static_cast<long long>(tiles) * KS, G = gridDim.x;
-  int def_tile = -1, def_np = 0;  // the split tile this CTA finalizes (at most one: its first segment)
-  float def_v = 0.0f;
+  const int b = static_cast<int>(blockIdx.x);
   int ks = ks0, tile = tb;
   for (int i = 0; i < n_st;) {
     const int len = min(KS - ks, n_st - i), fks = ks + len - 1;
     const bool whole = ks == 0 && fks == KS - 1;
-    const int b = j & 1, lr = (tile - tb) * R + lane, row = tile * R + lane;
+    const int pb = j & 1, lr = (tile - tb) * R + lane, row = tile * R + lane;
     const bool has_row = lane < R && lr < nrows;
     float corr = 0.0f;
-    if (whole && has_row) corr = row_correction(et, xval, lr, row, 0, KS * CW * 256);
-    const bool use_yold = (MODE == 1 || MODE == 2) && whole;
-    const float yold = use_yold && lane < R && row < N ? y[row] : 0.0f;
-    if (!wait_bar(&ready[b], (j >> 1) & 1)) return false;
+    if (has_row) corr = row_correction(et, xval, lr, row, ks * CW * 256, (fks + 1) * CW * 256);
+    const bool use_yold = (MODE == 1 || MODE == 2) && (whole || ks == 0);
+    const float yold = use_yold && lane < R && row < N ? __ldcg(y + row) : 0.0f;
+    // a split tile's head (ks == 0): this CTA finishes it; the other parts are read before its own partial
+    float other = 0.0f;
+    if (!whole && ks == 0) {
+      const long long st0 = static_cast<long long>(tile) * KS;
+      const int np = static_cast<int>(((st0 + KS) * G + nall - 1) / nall - 1) - b;  // parts of CTAs b+1..bl
+      const int* flags = wsc + static_cast<size_t>(tile) * maxp;
+      bool ok = true;
+      for (int pi = 0; pi < np && ok; ++pi) {  // all lanes poll (acquire for each lane's reads below)
+        ok = ld_acquire_gpu(flags + pi) == 1;
+        for (uint32_t k = 0, lim = ok ? 0u : spin_limit(); k < lim && !ok; ++k) {
+          ok = ld_acquire_gpu(flags + pi) == 1;
+          if (!ok && (k & 63) == 63 && *abort_flag) break;
+        }
+      }
+      if (!__all_sync(0xffffffffu, ok)) {
+        if (lane == 0) {
+          if (!*abort_flag) set_status(AIB_DEV_TIMEOUT_FULL);
+          *abort_flag = 1;
+        }
+        return false;
+      }
+      const float* parts = wsp + static_cast<size_t>(tile) * maxp * R;
+      if (lane < R)
+        for (int pi = 0; pi < np; ++pi) other += __ldcg(parts + pi * R + lane);
+      __syncwarp();
+      for (int pi = lane; pi < np; pi += 32) wsc[static_cast<size_t>(tile) * maxp + pi] = 0;  // next launch
+    }
+    if (!wait_bar(&ready[pb], (j >> 1) & 1)) return false;
     float v = 0.0f;
     if (lane < R) {
-      const float* pp = pbuf + b * pstride + lane * pw;
+      const float* pp = pbuf + pb * pstride + lane * pw;
       v = pp[0];
       for (int w = 1; w < pw; ++w) v += pp[w];
     }
     __syncwarp();
-    if (lane == 0) mbar_arrive(&free_[b]);
-    if (whole) {
-      if (has_row) v += corr;
-      store_rows<MODE>(v, yold, use_yold, row, R, N, y);
-    } else {
-      if (has_row) v += row_correction(et, xval, lr, row, ks * CW * 256, (fks + 1) * CW * 256);
+    if (lane == 0) mbar_arrive(&free_[pb]);
+    if (has_row) v += corr;
+    if (whole || ks == 0) {
+      store_rows<MODE>(v + other, yold, use_yold, row, R, N, y);
+    } else {  // a later part of a tile whose head a lower-numbered CTA holds
       const long long st0 = static_cast<long long>(tile) * KS;
       const int bf = static_cast<int>(((st0 + 1) * G + nall - 1) / nall - 1);
-      const int bl = static_cast<int>(((st0 + KS) * G + nall - 1) / nall - 1);
-      if (static_cast<int>(blockIdx.x) == bl) {
-        def_tile = tile;
-        def_np = bl - bf + 1;
-        def_v = v;
-      } else {
-        const int pi = static_cast<int>(blockIdx.x) - bf;
-        if (lane < R) wsp[(static_cast<size_t>(tile) * maxp + pi) * R + lane] = v;
-        __threadfence();
-        __syncwarp();
-        if (lane == 0) st_release_gpu(wsc + static_cast<size_t>(tile) * maxp + pi, 1);
-      }
+      const int pi = b - bf - 1;
+      if (lane < R) wsp[(static_cast<size_t>(tile) * maxp + pi) * R + lane] = v;
+      __threadfence();
+      __syncwarp();
+      if (lane == 0) st_release_gpu(wsc + static_cast<size_t>(tile) * maxp + pi, 1);
     }
     i += len;
     ks = 0;
     ++tile;
     ++j;
-  }
-  if (def_tile >= 0) {  // the parts of the split tile whose last stage this CTA held
-    const int* flags = wsc + static_cast<size_t>(def_tile) * maxp;
-    bool ok = true;
-    for (int pi = 0; pi + 1 < def_np && ok; ++pi) {  // all lanes poll (acquire for each lane's reads below)
-      ok = ld_acquire_gpu(flags + pi) == 1;
-      for (uint32_t k = 0, lim = ok ? 0u : spin_limit(); k < lim && !ok; ++k) {
-        ok = ld_acquire_gpu(flags + pi) == 1;
-        if (!ok && (k & 63) == 63 && *abort_flag) break;
-      }
-    }
-    if (!__all_sync(0xffffffffu, ok)) {
-      if (lane == 0) {
-        if (!*abort_flag) set_status(AIB_DEV_TIMEOUT_FULL);
-        *abort_flag = 1;
-      }
-      return false;
-    }
-    const float* parts = wsp + static_cast<size_t>(def_tile) * maxp * R;
-    float t = 0.0f;
-    if (lane < R) {
-      t = __ldcg(parts + lane);
-      for (int pi = 1; pi + 1 < def_np; ++pi) t += __ldcg(parts + pi * R + lane);
-      t += def_v;
-    }
-    __syncwarp();
-    for (int pi = lane; pi + 1 < def_np; pi += 32) wsc[static_cast<size_t>(def_tile) * maxp + pi] = 0;  // next launch
-    store_rows<MODE>(t, 0.0f, false, def_tile * R + lane, R, N, y);
   }
   return true;
 }

@@ -21,6 +21,7 @@ pick run through the whole-prompt prefill (`ai_b200.prefill`: tcgen05 codec GEMM
 the reference's blocked path, core/engine.py:446-487); others run in 16-token batched chunks (the reference's
 legacy path, core/engine.py:471-480).
 """
+import gc
 import os
 import time
 
@@ -31,6 +32,13 @@ from .head import Head as Head8, exact_logits
 from . import _lib, wcomp, tkernels, sampler, codecfile, prefill
 from ._lib import ptr, stream_ptr
 from .model import CONFIGS, Ckpt, RandomWeights, Qwen3Config, check_tp, shard_layer
+
+
+def _collect_before_capture():
+    """Collect unreachable Python objects before a CUDA-graph capture. torch no longer does this by default, and a
+    collection that runs during the capture and frees an object holding CUDA resources (a dropped engine's graphs,
+    for instance) makes a call that invalidates the capture."""
+    gc.collect()
 
 MATS = ("qkv", "o", "gu", "down")
 MAXB = 16
@@ -158,6 +166,9 @@ class Engine:
         self.tws = prefill.workspace(MAXB, max(int(c["K"]) for c in self.W[0].values()), 3, dev)  # T <= 16 passes
         wsz = max(_lib.lib().aib_attn_workspace(H, KV, HD, maxt, t) for t in range(1, MAXB + 1))
         self.ws = torch.zeros(wsz, dtype=torch.uint8, device=dev)
+        # stream-K workspace of the gate/up GEMV (the one matrix whose whole-tile split leaves a long tail: 1536
+        # row tiles over 296 CTAs); the other matrices run whole row tiles (measured faster for them)
+        self.gws = wcomp.gemv_workspace([w["gu"] for w in self.W], dev)
         self.use_graphs = graphs
         self.graphs = {}
         self._setup_allreduce()
@@ -232,7 +243,7 @@ class Engine:
                 wcomp.gemvc1(self.attb[0], W["o"], x, self._add)
                 self._reduce(self.xb[:1])
                 if self.gated:
-                    wcomp.gemvc1(x, W["gu"], self.gub[0], 3, lnw=s["ln2"], eps=self.eps)
+                    wcomp.gemvc1(x, W["gu"], self.gub[0], 3, lnw=s["ln2"], eps=self.eps, ws=self.gws)
                     wcomp.gemvc1(self.gub[0], W["down"], x, self._add)
                 else:
                     wcomp.gemvc1(x, W["gu"], self.gub[0], 0, lnw=s["ln2"], eps=self.eps)
@@ -327,6 +338,7 @@ class Engine:
             # First use of this shape: run the step eagerly (it is the real step; one-time library setup such
             # as shared-memory attributes happens outside capture), then capture it for later replays.
             self._step(T, prm, rows, penal)
+            _collect_before_capture()
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g, capture_error_mode="thread_local"):
                 self._step(T, prm, rows, penal)
@@ -630,6 +642,7 @@ class Batch:
         g = self.graphs.get(key)
         if g is None:
             self._step(prm)
+            _collect_before_capture()
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g, capture_error_mode="thread_local"):
                 self._step(prm)

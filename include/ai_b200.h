@@ -108,7 +108,7 @@ int aib_c12_decode(const aib_c12* c, int first, int last, void* out, int out_dty
  * ws (optional, T == 1): aib_gemv_c12_workspace(c, 1) bytes, 16-byte aligned and zero-filled once before the
  * first call (it is left zeroed after every call). With it, when that shortens the longest CTA's share, the
  * matrix's (row tile, column group) stages are split evenly over the CTAs and a row tile shared by
- * neighbouring CTAs is completed by the one holding its last stage, adding the parts in a fixed order
+ * neighbouring CTAs is completed by the one holding its first stage, adding the parts in a fixed order
  * (deterministic); without it every CTA takes whole row tiles. The workspace is touched only after the
  * previous kernel on the stream has completed, so calls in one stream may share one; calls that may overlap
  * on the GPU (other streams) need separate workspaces. */
