@@ -163,8 +163,10 @@ def gemv_roofline(eng, peak, reps=20):
     from ai_b200.head import exact_logits
     W, s = eng.W[0], eng.small[0]
     gu_mode, down_mode = (3, 1) if eng.gated else (0, 2)  # the engine's own modes
-    launches = [(W["qkv"], eng.xb[0], eng.qkvb[0], 0, s["ln1"]), (W["o"], eng.attb[0], eng.xb[1], 1, None),
-                (W["gu"], eng.xb[0], eng.gub[0], gu_mode, s["ln2"]), (W["down"], eng.gub[0], eng.xb[1], down_mode, None)]
+    gws = eng.gws if eng.gated else None  # gate/up with the engine's stream-K workspace
+    launches = [(W["qkv"], eng.xb[0], eng.qkvb[0], 0, s["ln1"], None), (W["o"], eng.attb[0], eng.xb[1], 1, None, None),
+                (W["gu"], eng.xb[0], eng.gub[0], gu_mode, s["ln2"], gws),
+                (W["down"], eng.gub[0], eng.xb[1], down_mode, None, None)]
     eng.xb[:2].normal_()
     eng.attb[0].normal_()
     eng.gub[0].normal_()
@@ -172,8 +174,8 @@ def gemv_roofline(eng, peak, reps=20):
     st = torch.cuda.current_stream()
 
     def run_layer():
-        for c, x, y, m, lnw in launches:
-            wcomp.gemvc1(x, c, y, m, lnw=lnw, eps=eng.eps)
+        for c, x, y, m, lnw, ws in launches:
+            wcomp.gemvc1(x, c, y, m, lnw=lnw, eps=eng.eps, ws=ws)
 
     def timed(fn):
         for _ in range(3):
