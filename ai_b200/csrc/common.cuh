@@ -26,9 +26,10 @@ __device__ int g_aib_status = 0;
 
 AIB_DEV void set_status(int code) { atomicCAS(&g_aib_status, 0, code); }
 
-// spin limit for bounded waits: each try_wait suspends for at most kSuspendNs (1 us), so this bounds a wait to
-// about a second while being ~1e5x longer than any legitimate wait in these kernels.
-constexpr uint32_t kSpinLimit = 1u << 20;
+// spin limit for bounded waits: 4M tries of a try_wait that suspends up to the hardware's limit -- tens of
+// milliseconds to a few seconds in all, far longer than any legitimate wait in these kernels (the longest is a
+// launch's early CTAs waiting out a millisecond-long previous kernel).
+constexpr uint32_t kSpinLimit = 1u << 22;
 // Test knobs (aib_debug_knob): a smaller spin limit, so a test can make a wait run out in milliseconds, and a
 // switch under which the wide GEMV's producer issues no copies (its stages never fill). Zero = off.
 __device__ uint32_t g_aib_spin_override = 0;
@@ -59,10 +60,11 @@ AIB_DEV void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
 AIB_DEV void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
-// A waiting thread is suspended (it takes no issue slots) until the phase completes or kSuspendNs elapses; a
-// spin-loop of these therefore sleeps instead of competing with the working warps for issue.
+// A waiting thread may be suspended (taking no issue slots) until the phase completes or a time limit elapses:
+// kSuspendNs when non-zero, else the hardware's own limit. The hardware's limit measured 0.5 % faster on the
+// decode step than a 1 us hint (313.2 vs 314.8 tok/s).
 #ifndef AIB_SUSPEND_NS
-#define AIB_SUSPEND_NS 1000
+#define AIB_SUSPEND_NS 0
 #endif
 constexpr uint32_t kSuspendNs = AIB_SUSPEND_NS;
 AIB_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {

@@ -69,8 +69,8 @@ void aib_set_pdl(int enabled);
 /* Device status word of the current device: copies it to *out (synchronous) and, if clear != 0, resets it. */
 int aib_status_read(int* out, int clear);
 /* Test knobs of the current device (synchronous; no reference counterpart), so that tests can make a bounded wait
- * run out without any fault: knob 1 = spin limit of every bounded wait (polls; 0 restores the default, ~1e6 times
- * longer than any legitimate wait), knob 2 = 1 makes the wide T = 1 GEMV's producer withhold its copies (its stages
+ * run out without any fault: knob 1 = spin limit of every bounded wait (polls; 0 restores the default, 2^22 polls,
+ * far longer than any legitimate wait), knob 2 = 1 makes the wide T = 1 GEMV's producer withhold its copies (its stages
  * never fill, its consumers give up after the spin limit and record AIB_DEV_TIMEOUT_FULL), knob 3 = how many
  * thread-block cluster sizes (16, then 8 CTAs) the decode attention tries for its cluster merge before the
  * ticket merge (default 0: ticket merge only; its feasibility query is not allowed inside a graph capture),
